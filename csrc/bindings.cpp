@@ -1,0 +1,382 @@
+// torch bindings of the sm_100a kernels (module sglang_omni_b200._C).
+// Every entry validates device, dtype, contiguity and shape, then forwards raw
+// pointers and the current CUDA stream to the launchers in omni_kernels.h.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "omni_kernels.h"
+
+namespace {
+
+#define OMNI_CHECK_CUDA(t) TORCH_CHECK((t).is_cuda(), #t " must be a CUDA tensor")
+#define OMNI_CHECK_BF16(t) TORCH_CHECK((t).scalar_type() == at::kBFloat16, #t " must be bfloat16")
+#define OMNI_CHECK_CONTIG(t) TORCH_CHECK((t).is_contiguous(), #t " must be contiguous")
+
+void check_launch(cudaError_t e, const char* what) {
+  TORCH_CHECK(e == cudaSuccess, what, " failed: ", cudaGetErrorString(e));
+}
+
+int* status_ptr(const c10::optional<torch::Tensor>& status) {
+  if (!status.has_value()) return nullptr;
+  TORCH_CHECK(status->scalar_type() == at::kInt && status->is_cuda(), "status must be a CUDA int32 tensor");
+  return status->data_ptr<int>();
+}
+
+// out[r, m] = act(b[r] . a[g*a_rows + m]) (+ bias) (+ residual)
+void gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& out, const c10::optional<torch::Tensor>& offsets,
+          int64_t m_out, bool gated, const c10::optional<torch::Tensor>& bias,
+          const c10::optional<torch::Tensor>& residual, int64_t act, int64_t expected_rows,
+          const c10::optional<torch::Tensor>& status, int64_t max_ctas) {
+  OMNI_CHECK_CUDA(a);
+  OMNI_CHECK_CUDA(b);
+  OMNI_CHECK_CUDA(out);
+  OMNI_CHECK_BF16(a);
+  OMNI_CHECK_BF16(b);
+  OMNI_CHECK_CONTIG(a);
+  OMNI_CHECK_CONTIG(b);
+  TORCH_CHECK(out.stride(-1) == 1, "out must have a contiguous last dim");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 || out.scalar_type() == at::kFloat, "out must be bf16 or fp32");
+  const int64_t k = b.size(-1);
+  TORCH_CHECK(a.size(-1) == k, "K mismatch: a ", a.sizes(), " b ", b.sizes());
+  const int64_t rows = b.numel() / k;
+  int groups = 1;
+  int64_t a_rows;
+  const int* off = nullptr;
+  if (a.dim() == 3) {
+    groups = static_cast<int>(a.size(0));
+    a_rows = a.size(1);
+  } else {
+    TORCH_CHECK(a.dim() == 2, "a must be 2-D or 3-D");
+    a_rows = a.size(0);
+  }
+  if (offsets.has_value()) {
+    TORCH_CHECK(offsets->scalar_type() == at::kInt && offsets->is_cuda() && offsets->numel() == groups + 1,
+                "offsets must be CUDA int32 [groups+1]");
+    off = offsets->data_ptr<int>();
+  } else {
+    TORCH_CHECK(groups == 1, "grouped GEMM needs offsets");
+  }
+  TORCH_CHECK(gated ? a_rows == 2 * m_out : a_rows >= m_out, "weight rows do not match m_out");
+  TORCH_CHECK(out.numel() / out.size(-1) == rows && out.size(-1) >= m_out, "out shape mismatch");
+  const at::cuda::CUDAGuard guard(b.device());
+  omni::GemmArgs args{};
+  args.a = a.data_ptr();
+  args.b = b.data_ptr();
+  args.out = out.data_ptr();
+  args.ldo = out.dim() >= 2 ? out.stride(-2) : out.size(-1);
+  args.out_f32 = out.scalar_type() == at::kFloat;
+  if (bias.has_value()) {
+    OMNI_CHECK_BF16(*bias);
+    TORCH_CHECK(bias->numel() == static_cast<int64_t>(groups) * m_out, "bias size mismatch");
+    args.bias = bias->data_ptr();
+  }
+  if (residual.has_value()) {
+    OMNI_CHECK_BF16(*residual);
+    TORCH_CHECK(residual->stride(-1) == 1 && residual->numel() / residual->size(-1) == rows, "residual shape");
+    args.residual = residual->data_ptr();
+    args.ldr = residual->dim() >= 2 ? residual->stride(-2) : residual->size(-1);
+  }
+  args.m_out = static_cast<int>(m_out);
+  args.a_rows = static_cast<int>(a_rows);
+  args.k = static_cast<int>(k);
+  args.groups = groups;
+  args.offsets = off;
+  args.rows = static_cast<int>(rows);
+  args.expected_rows_per_group = static_cast<int>(expected_rows);
+  args.gated = gated ? 1 : 0;
+  args.act = static_cast<int>(act);
+  args.status = status_ptr(status);
+  args.max_ctas = static_cast<int>(max_ctas);
+  check_launch(omni::gemm_bf16(args, at::cuda::getCurrentCUDAStream()), "gemm_bf16");
+}
+
+void rmsnorm(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& y,
+             const c10::optional<torch::Tensor>& residual, double eps) {
+  OMNI_CHECK_CUDA(x);
+  OMNI_CHECK_BF16(x);
+  OMNI_CHECK_BF16(w);
+  OMNI_CHECK_BF16(y);
+  const int64_t hidden = x.size(-1);
+  TORCH_CHECK(w.numel() == hidden && x.stride(-1) == 1 && y.stride(-1) == 1, "rmsnorm shapes");
+  const int64_t rows = x.numel() / hidden;
+  const int64_t ld_x = x.dim() >= 2 ? x.stride(-2) : hidden;
+  const int64_t ld_y = y.dim() >= 2 ? y.stride(-2) : hidden;
+  void* res = nullptr;
+  if (residual.has_value()) {
+    OMNI_CHECK_BF16(*residual);
+    OMNI_CHECK_CONTIG(*residual);
+    TORCH_CHECK(residual->numel() == rows * hidden, "residual shape");
+    res = residual->data_ptr();
+  }
+  const at::cuda::CUDAGuard guard(x.device());
+  check_launch(omni::rmsnorm_bf16(x.data_ptr(), w.data_ptr(), y.data_ptr(), res, static_cast<int>(rows),
+                                  static_cast<int>(hidden), ld_x, ld_y, static_cast<float>(eps),
+                                  at::cuda::getCurrentCUDAStream()),
+               "rmsnorm_bf16");
+}
+
+void layernorm(const torch::Tensor& x, const torch::Tensor& w, const c10::optional<torch::Tensor>& b, torch::Tensor& y,
+               double eps) {
+  OMNI_CHECK_CUDA(x);
+  OMNI_CHECK_BF16(x);
+  OMNI_CHECK_CONTIG(x);
+  OMNI_CHECK_CONTIG(y);
+  const int64_t hidden = x.size(-1);
+  const at::cuda::CUDAGuard guard(x.device());
+  check_launch(omni::layernorm_bf16(x.data_ptr(), w.data_ptr(), b.has_value() ? b->data_ptr() : nullptr,
+                                    y.data_ptr(), static_cast<int>(x.numel() / hidden), static_cast<int>(hidden),
+                                    static_cast<float>(eps), at::cuda::getCurrentCUDAStream()),
+               "layernorm_bf16");
+}
+
+
+template <class T>
+const T* opt_ptr(const c10::optional<torch::Tensor>& t) {
+  return t.has_value() ? static_cast<const T*>(t->data_ptr()) : nullptr;
+}
+template <class T>
+T* opt_mut(const c10::optional<torch::Tensor>& t) {
+  return t.has_value() ? static_cast<T*>(t->data_ptr()) : nullptr;
+}
+
+void attention_prefill(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, torch::Tensor& out,
+                       const c10::optional<torch::Tensor>& block_table, const torch::Tensor& cu_q,
+                       const torch::Tensor& kv_lens, const c10::optional<torch::Tensor>& cu_kv,
+                       const torch::Tensor& tile_req, const torch::Tensor& tile_tok0, int64_t hq, int64_t hkv,
+                       int64_t head_dim, double scale, bool causal) {
+  OMNI_CHECK_CUDA(q);
+  OMNI_CHECK_BF16(q);
+  OMNI_CHECK_BF16(k);
+  OMNI_CHECK_BF16(v);
+  OMNI_CHECK_BF16(out);
+  TORCH_CHECK(q.stride(-1) == 1 && out.stride(-1) == 1, "rows must be contiguous");
+  const at::cuda::CUDAGuard guard(q.device());
+  omni::AttnPrefillArgs a{};
+  a.q = q.data_ptr();
+  a.q_stride = q.stride(0);
+  a.k = k.data_ptr();
+  a.v = v.data_ptr();
+  a.kv_stride = block_table.has_value() ? 0 : k.stride(0);
+  if (block_table.has_value()) {
+    a.block_table = block_table->data_ptr<int>();
+    a.bt_stride = static_cast<int>(block_table->stride(0));
+  }
+  a.cu_q = cu_q.data_ptr<int>();
+  a.kv_lens = kv_lens.data_ptr<int>();
+  a.cu_kv = cu_kv.has_value() ? cu_kv->data_ptr<int>() : nullptr;
+  TORCH_CHECK(block_table.has_value() || cu_kv.has_value(), "contiguous K/V needs cu_kv");
+  a.tile_req = tile_req.data_ptr<int>();
+  a.tile_tok0 = tile_tok0.data_ptr<int>();
+  a.num_tiles = static_cast<int>(tile_req.numel());
+  a.hq = static_cast<int>(hq);
+  a.hkv = static_cast<int>(hkv);
+  a.head_dim = static_cast<int>(head_dim);
+  a.scale = static_cast<float>(scale);
+  a.causal = causal ? 1 : 0;
+  a.out = out.data_ptr();
+  a.out_stride = out.stride(0);
+  check_launch(omni::attention_prefill(a, at::cuda::getCurrentCUDAStream()), "attention_prefill");
+}
+
+void attention_decode(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, torch::Tensor& out,
+                      const torch::Tensor& block_table, const torch::Tensor& kv_lens, int64_t hq, int64_t hkv,
+                      int64_t head_dim, double scale, int64_t keys_per_split, int64_t max_splits,
+                      torch::Tensor& part_o, torch::Tensor& part_lse) {
+  OMNI_CHECK_CUDA(q);
+  OMNI_CHECK_BF16(q);
+  TORCH_CHECK(q.stride(-1) == 1 && out.stride(-1) == 1, "rows must be contiguous");
+  const int64_t batch = kv_lens.numel();
+  TORCH_CHECK(part_o.numel() >= batch * hq * max_splits * head_dim && part_lse.numel() >= batch * hq * max_splits,
+              "decode scratch too small");
+  const at::cuda::CUDAGuard guard(q.device());
+  omni::AttnDecodeArgs a{};
+  a.q = q.data_ptr();
+  a.q_stride = q.stride(0);
+  a.k = k.data_ptr();
+  a.v = v.data_ptr();
+  a.block_table = block_table.data_ptr<int>();
+  a.bt_stride = static_cast<int>(block_table.stride(0));
+  a.kv_lens = kv_lens.data_ptr<int>();
+  a.batch = static_cast<int>(batch);
+  a.hq = static_cast<int>(hq);
+  a.hkv = static_cast<int>(hkv);
+  a.head_dim = static_cast<int>(head_dim);
+  a.scale = static_cast<float>(scale);
+  a.keys_per_split = static_cast<int>(keys_per_split);
+  a.max_splits = static_cast<int>(max_splits);
+  a.out = out.data_ptr();
+  a.out_stride = out.stride(0);
+  a.part_o = part_o.data_ptr<float>();
+  a.part_lse = part_lse.data_ptr<float>();
+  check_launch(omni::attention_decode(a, at::cuda::getCurrentCUDAStream()), "attention_decode");
+}
+
+void qkv_rope_store(torch::Tensor& qkv, int64_t hq, int64_t hkv, int64_t head_dim,
+                    const c10::optional<torch::Tensor>& q_norm, const c10::optional<torch::Tensor>& k_norm, double eps,
+                    const torch::Tensor& positions, const std::vector<int64_t>& section, bool interleaved,
+                    const torch::Tensor& cos_tab, const torch::Tensor& sin_tab, int64_t rot_dim, bool neox,
+                    const c10::optional<torch::Tensor>& slot_mapping, const c10::optional<torch::Tensor>& k_cache,
+                    const c10::optional<torch::Tensor>& v_cache) {
+  OMNI_CHECK_CUDA(qkv);
+  OMNI_CHECK_BF16(qkv);
+  TORCH_CHECK(qkv.stride(-1) == 1, "qkv rows must be contiguous");
+  TORCH_CHECK(positions.scalar_type() == at::kInt && positions.is_contiguous(), "positions int32");
+  TORCH_CHECK(cos_tab.scalar_type() == at::kFloat && sin_tab.scalar_type() == at::kFloat, "fp32 rope tables");
+  TORCH_CHECK(rot_dim == 0 || !neox || (rot_dim / 2) % 32 == 0, "neox rotation needs rot_dim/2 % 32 == 0");
+  const at::cuda::CUDAGuard guard(qkv.device());
+  omni::RopeStoreArgs a{};
+  a.qkv = qkv.data_ptr();
+  a.qkv_stride = qkv.stride(0);
+  a.tokens = static_cast<int>(qkv.size(0));
+  a.hq = static_cast<int>(hq);
+  a.hkv = static_cast<int>(hkv);
+  a.head_dim = static_cast<int>(head_dim);
+  a.q_norm = q_norm.has_value() ? q_norm->data_ptr() : nullptr;
+  a.k_norm = k_norm.has_value() ? k_norm->data_ptr() : nullptr;
+  a.eps = static_cast<float>(eps);
+  a.positions = positions.data_ptr<int>();
+  a.pos_rows = positions.dim() == 2 ? static_cast<int>(positions.size(0)) : 1;
+  for (int i = 0; i < 3; ++i) a.section[i] = i < static_cast<int>(section.size()) ? static_cast<int>(section[i]) : 0;
+  a.interleaved = interleaved ? 1 : 0;
+  a.cos_tab = cos_tab.data_ptr<float>();
+  a.sin_tab = sin_tab.data_ptr<float>();
+  a.rot_dim = static_cast<int>(rot_dim);
+  a.neox = neox ? 1 : 0;
+  a.slot_mapping = slot_mapping.has_value() ? slot_mapping->data_ptr<int>() : nullptr;
+  a.k_cache = k_cache.has_value() ? k_cache->data_ptr() : nullptr;
+  a.v_cache = v_cache.has_value() ? v_cache->data_ptr() : nullptr;
+  check_launch(omni::qkv_rope_store(a, at::cuda::getCurrentCUDAStream()), "qkv_rope_store");
+}
+
+void moe_route(const torch::Tensor& logits, int64_t topk, int64_t mode, const c10::optional<torch::Tensor>& bias,
+               int64_t n_group, int64_t topk_group, bool renormalize, double scaling, torch::Tensor& topk_ids,
+               torch::Tensor& topk_w, const c10::optional<torch::Tensor>& counts,
+               const c10::optional<torch::Tensor>& cursor, const c10::optional<torch::Tensor>& offsets,
+               const c10::optional<torch::Tensor>& inv_perm, const c10::optional<torch::Tensor>& x,
+               const c10::optional<torch::Tensor>& x_perm) {
+  OMNI_CHECK_CUDA(logits);
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.stride(-1) == 1, "router logits must be fp32");
+  const at::cuda::CUDAGuard guard(logits.device());
+  omni::MoeRouteArgs a{};
+  a.logits = logits.data_ptr<float>();
+  a.logits_stride = logits.stride(0);
+  a.tokens = static_cast<int>(logits.size(0));
+  a.experts = static_cast<int>(logits.size(1));
+  a.topk = static_cast<int>(topk);
+  a.mode = static_cast<int>(mode);
+  a.bias = opt_ptr<float>(bias);
+  a.n_group = static_cast<int>(n_group);
+  a.topk_group = static_cast<int>(topk_group);
+  a.renormalize = renormalize ? 1 : 0;
+  a.scaling = static_cast<float>(scaling);
+  a.topk_ids = topk_ids.data_ptr<int>();
+  a.topk_w = topk_w.data_ptr<float>();
+  a.counts = opt_mut<int>(counts);
+  a.cursor = opt_mut<int>(cursor);
+  a.offsets = opt_mut<int>(offsets);
+  a.inv_perm = opt_mut<int>(inv_perm);
+  if (a.counts) TORCH_CHECK(a.cursor && a.offsets && a.inv_perm, "permutation outputs required");
+  if (x.has_value()) {
+    OMNI_CHECK_BF16(*x);
+    TORCH_CHECK(x_perm.has_value() && x->is_contiguous() && x->size(-1) % 8 == 0, "x / x_perm");
+    a.x = x->data_ptr();
+    a.x_perm = x_perm->data_ptr();
+    a.hidden = static_cast<int>(x->size(-1));
+  }
+  check_launch(omni::moe_route(a, at::cuda::getCurrentCUDAStream()), "moe_route");
+}
+
+void moe_combine(const torch::Tensor& y_perm, const torch::Tensor& inv_perm, const torch::Tensor& topk_w,
+                 torch::Tensor& out, const c10::optional<torch::Tensor>& shared,
+                 const c10::optional<torch::Tensor>& shared_gate) {
+  OMNI_CHECK_CUDA(y_perm);
+  OMNI_CHECK_BF16(y_perm);
+  OMNI_CHECK_CONTIG(out);
+  const at::cuda::CUDAGuard guard(y_perm.device());
+  omni::MoeCombineArgs a{};
+  a.y_perm = y_perm.data_ptr();
+  a.inv_perm = inv_perm.data_ptr<int>();
+  a.topk_w = topk_w.data_ptr<float>();
+  a.tokens = static_cast<int>(out.size(0));
+  a.topk = static_cast<int>(topk_w.size(1));
+  a.hidden = static_cast<int>(out.size(1));
+  a.shared = shared.has_value() ? shared->data_ptr() : nullptr;
+  if (shared_gate.has_value()) {
+    TORCH_CHECK(shared_gate->scalar_type() == at::kFloat, "shared gate fp32");
+    a.shared_gate = shared_gate->data_ptr<float>();
+    a.shared_gate_stride = static_cast<int>(shared_gate->dim() >= 2 ? shared_gate->stride(0) : 1);
+  }
+  a.out = out.data_ptr();
+  check_launch(omni::moe_combine(a, at::cuda::getCurrentCUDAStream()), "moe_combine");
+}
+
+void embed(const torch::Tensor& ids, const torch::Tensor& table, torch::Tensor& out,
+           const c10::optional<torch::Tensor>& mm_index, const c10::optional<torch::Tensor>& mm_embeds) {
+  OMNI_CHECK_CUDA(ids);
+  TORCH_CHECK(ids.scalar_type() == at::kInt, "ids int32");
+  OMNI_CHECK_BF16(table);
+  OMNI_CHECK_CONTIG(table);
+  OMNI_CHECK_CONTIG(out);
+  const at::cuda::CUDAGuard guard(ids.device());
+  omni::EmbedArgs a{};
+  a.ids = ids.data_ptr<int>();
+  a.table = table.data_ptr();
+  a.mm_index = mm_index.has_value() ? mm_index->data_ptr<int>() : nullptr;
+  a.mm_embeds = mm_embeds.has_value() ? mm_embeds->data_ptr() : nullptr;
+  a.out = out.data_ptr();
+  a.tokens = static_cast<int>(ids.numel());
+  a.hidden = static_cast<int>(table.size(1));
+  check_launch(omni::embed(a, at::cuda::getCurrentCUDAStream()), "embed");
+}
+
+void sample(torch::Tensor& logits, torch::Tensor& out_tokens, const c10::optional<torch::Tensor>& temperature,
+            const c10::optional<torch::Tensor>& top_k, const c10::optional<torch::Tensor>& top_p,
+            const c10::optional<torch::Tensor>& min_p, const c10::optional<torch::Tensor>& rep_penalty,
+            const c10::optional<torch::Tensor>& seen, int64_t suppress_lo, int64_t suppress_hi,
+            int64_t suppress_keep, const c10::optional<torch::Tensor>& seeds,
+            const c10::optional<torch::Tensor>& step) {
+  OMNI_CHECK_CUDA(logits);
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.stride(-1) == 1, "logits fp32");
+  const at::cuda::CUDAGuard guard(logits.device());
+  omni::SampleArgs a{};
+  a.logits = logits.data_ptr<float>();
+  a.logits_stride = logits.stride(0);
+  a.rows = static_cast<int>(logits.size(0));
+  a.vocab = static_cast<int>(logits.size(1));
+  a.temperature = opt_ptr<float>(temperature);
+  a.top_k = opt_ptr<int>(top_k);
+  a.top_p = opt_ptr<float>(top_p);
+  a.min_p = opt_ptr<float>(min_p);
+  a.rep_penalty = opt_ptr<float>(rep_penalty);
+  if (seen.has_value()) {
+    TORCH_CHECK(seen->scalar_type() == at::kByte, "seen must be uint8");
+    a.seen = seen->data_ptr<uint8_t>();
+    a.seen_stride = seen->stride(0);
+  }
+  a.suppress_lo = static_cast<int>(suppress_lo);
+  a.suppress_hi = static_cast<int>(suppress_hi);
+  a.suppress_keep = static_cast<int>(suppress_keep);
+  a.seeds = seeds.has_value() ? seeds->data_ptr<int64_t>() : nullptr;
+  a.step = opt_ptr<int>(step);
+  a.out_tokens = out_tokens.data_ptr<int>();
+  check_launch(omni::sample(a, at::cuda::getCurrentCUDAStream()), "sample");
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "sm_100a kernels of sglang_omni_b200";
+  m.def("gemm", &gemm, "tcgen05 GEMM (dense / grouped / gated)", py::arg("a"), py::arg("b"), py::arg("out"),
+        py::arg("offsets"), py::arg("m_out"), py::arg("gated"), py::arg("bias"), py::arg("residual"), py::arg("act"),
+        py::arg("expected_rows"), py::arg("status"), py::arg("max_ctas") = 0);
+  m.def("rmsnorm", &rmsnorm, "RMSNorm (+ fused residual add)");
+  m.def("layernorm", &layernorm, "LayerNorm");
+  m.def("attention_prefill", &attention_prefill, "paged / varlen GQA prefill attention");
+  m.def("attention_decode", &attention_decode, "paged split-KV GQA decode attention");
+  m.def("qkv_rope_store", &qkv_rope_store, "QK RMSNorm + (M-)RoPE + paged KV store");
+  m.def("moe_route", &moe_route, "MoE top-k routing + permutation + gather");
+  m.def("moe_combine", &moe_combine, "MoE top-k weighted combine (+ shared expert)");
+  m.def("embed", &embed, "embedding gather with multimodal overwrite");
+  m.def("sample", &sample, "fused logits processing + sampling");
+}

@@ -1,0 +1,606 @@
+// Memory-bound fused ops of the decoder step:
+//   * qkv_rope_store: per-head QK RMSNorm + (M-)RoPE on q and k in place, and
+//     the paged KV-cache write of k and v (one warp per token-head);
+//   * moe_topk / moe_scatter / moe_combine: router top-k (softmax or sigmoid
+//     group-limited), expert histogram + offsets, permutation + row gather,
+//     and the top-k weighted combine (+ optional gated shared expert);
+//   * embed: token-embedding gather with multimodal row overwrite;
+//   * sample: greedy / temperature / top-k / top-p / min-p sampling with
+//     repetition penalty, one CTA per row.
+//
+// Reference counterparts: sgl_kernel fused_qk_norm_rope and SGLang
+// MRotaryEmbedding (sglang_omni/models/qwen3_omni/thinker.py:262-323), TopK +
+// FusedMoE routing (thinker.py:395-412, ming_omni/thinker.py:370-462), the
+// omni embedding injection (engines/omni/runtime/sglang_ar.py:548-701) and the
+// sampling path (engines/omni/runtime/sglang_ar.py:882-1032).
+#include <cuda_bf16.h>
+#include <float.h>
+#include <stdint.h>
+
+#include "omni_kernels.h"
+
+namespace omni {
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, d));
+  return v;
+}
+__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16(x)); }
+
+// ---------------------------------------------------------------------------
+// QK norm + RoPE + KV store
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int mrope_section(int j, const int* sec, int interleaved) {
+  if (interleaved) {
+    if ((j % 3) == 1 && j < 3 * sec[1]) return 1;
+    if ((j % 3) == 2 && j < 3 * sec[2]) return 2;
+    return 0;
+  }
+  if (j < sec[0]) return 0;
+  if (j < sec[0] + sec[1]) return 1;
+  return 2;
+}
+
+template <int D>
+__global__ void qkv_rope_store_kernel(RopeStoreArgs a) {
+  constexpr int PER = D / 32;  // elements per lane
+  const int warp_global = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int heads = a.hq + 2 * a.hkv;
+  const int tok = warp_global / heads;
+  const int head = warp_global - tok * heads;
+  if (tok >= a.tokens) return;
+  __nv_bfloat16* row = static_cast<__nv_bfloat16*>(a.qkv) + static_cast<int64_t>(tok) * a.qkv_stride + head * D;
+  const bool is_q = head < a.hq;
+  const bool is_k = !is_q && head < a.hq + a.hkv;
+  const bool is_v = !is_q && !is_k;
+  // Lane owns elements e = lane + 32 * i (i < PER).  For neox rotation the
+  // partner of e is e +- rot/2; we load the whole row into registers via
+  // shared-free shuffles by owning both halves: element index mapping below.
+  float x[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) x[i] = __bfloat162float(row[lane + 32 * i]);
+  if (!is_v) {
+    const __nv_bfloat16* nw = is_q ? static_cast<const __nv_bfloat16*>(a.q_norm)
+                                   : static_cast<const __nv_bfloat16*>(a.k_norm);
+    if (nw != nullptr) {
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) ss += x[i] * x[i];
+      ss = warp_sum(ss);
+      const float rstd = rsqrtf(ss / D + a.eps);
+#pragma unroll
+      for (int i = 0; i < PER; ++i) x[i] = bf16r(bf16r(x[i] * rstd) * __bfloat162float(nw[lane + 32 * i]));
+    }
+    if (a.rot_dim > 0) {
+      const int half = a.rot_dim / 2;
+      int pos3[3];
+      if (a.pos_rows == 3) {
+        pos3[0] = a.positions[tok];
+        pos3[1] = a.positions[a.tokens + tok];
+        pos3[2] = a.positions[2 * a.tokens + tok];
+      } else {
+        pos3[0] = pos3[1] = pos3[2] = a.positions[tok];
+      }
+      float y[PER];
+      // Partner of element e = lane + 32 i: neox (half % 32 == 0) -> same lane,
+      // register i +- half/32; interleaved pairs -> lane ^ 1, same register.
+      const int hs = half >> 5;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const int e = lane + 32 * i;
+        float pv;
+        if (a.neox) {
+          const int pi = e < half ? i + hs : i - hs;
+          pv = 0.f;
+#pragma unroll
+          for (int ii = 0; ii < PER; ++ii)
+            if (ii == pi) pv = x[ii];
+        } else {
+          pv = __shfl_xor_sync(0xffffffffu, x[i], 1);
+        }
+        y[i] = x[i];
+        if (e < a.rot_dim) {
+          const int j = a.neox ? (e < half ? e : e - half) : (e >> 1);
+          const float sign = a.neox ? (e < half ? -1.f : 1.f) : ((e & 1) ? 1.f : -1.f);
+          const int s = a.pos_rows == 3 ? mrope_section(j, a.section, a.interleaved) : 0;
+          const int pos = pos3[s];
+          const float c = a.cos_tab[static_cast<int64_t>(pos) * half + j];
+          const float sn = a.sin_tab[static_cast<int64_t>(pos) * half + j];
+          y[i] = x[i] * c + sign * pv * sn;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < PER; ++i) x[i] = y[i];
+    }
+  }
+  // write back q / k in place, k / v into the cache
+  if (!is_v) {
+#pragma unroll
+    for (int i = 0; i < PER; ++i) row[lane + 32 * i] = __float2bfloat16(x[i]);
+  }
+  if (!is_q && a.slot_mapping != nullptr) {
+    const int slot = a.slot_mapping[tok];
+    if (slot >= 0) {
+      const int h = is_k ? head - a.hq : head - a.hq - a.hkv;
+      const int page = slot >> 6, off = slot & 63;
+      __nv_bfloat16* cache = static_cast<__nv_bfloat16*>(is_k ? a.k_cache : a.v_cache);
+      __nv_bfloat16* dst = cache + ((static_cast<int64_t>(page) * a.hkv + h) * 64 + off) * D;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) dst[lane + 32 * i] = __float2bfloat16(x[i]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// MoE routing
+// ---------------------------------------------------------------------------
+// One warp per token.  E <= 512 (E/32 values per lane).
+template <int PER>
+__global__ void moe_topk_kernel(MoeRouteArgs a) {
+  const int tok = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (tok >= a.tokens) return;
+  const float* lg = a.logits + static_cast<int64_t>(tok) * a.logits_stride;
+  float sc[PER];    // selection score
+  float wt[PER];    // weight score
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int e = lane + 32 * i;
+    sc[i] = e < a.experts ? lg[e] : -INFINITY;
+  }
+  if (a.mode == 0) {
+    // softmax over experts
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) m = fmaxf(m, sc[i]);
+    m = warp_max(m);
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      wt[i] = (lane + 32 * i) < a.experts ? __expf(sc[i] - m) : 0.f;
+      s += wt[i];
+    }
+    s = warp_sum(s);
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      wt[i] /= s;
+      sc[i] = (lane + 32 * i) < a.experts ? wt[i] : -INFINITY;
+    }
+  } else {
+    // sigmoid scores; selection adds the expert bias; group-limited choice
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int e = lane + 32 * i;
+      if (e < a.experts) {
+        wt[i] = 1.f / (1.f + __expf(-sc[i]));
+        sc[i] = wt[i] + (a.bias ? a.bias[e] : 0.f);
+      } else {
+        wt[i] = 0.f;
+      }
+    }
+    if (a.n_group > 1) {
+      // experts of group gi are e in [gi*gs, (gi+1)*gs); with gs == 32 a group is
+      // one register index across the warp.
+      const int gs = a.experts / a.n_group;
+      float gscore[PER];
+#pragma unroll
+      for (int i = 0; i < PER; ++i) gscore[i] = -INFINITY;
+      for (int gi = 0; gi < a.n_group; ++gi) {
+        // top-2 sum inside group gi
+        float best1 = -INFINITY, best2 = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < PER; ++i) {
+          const int e = lane + 32 * i;
+          if (e / gs == gi) {
+            const float v = sc[i];
+            if (v > best1) { best2 = best1; best1 = v; } else if (v > best2) { best2 = v; }
+          }
+        }
+        // warp-level top-2 merge
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) {
+          const float o1 = __shfl_xor_sync(0xffffffffu, best1, d);
+          const float o2 = __shfl_xor_sync(0xffffffffu, best2, d);
+          const float n1 = fmaxf(best1, o1);
+          const float n2 = fmaxf(fminf(best1, o1), fmaxf(best2, o2));
+          best1 = n1;
+          best2 = n2;
+        }
+        const float gsc = best1 + best2;
+#pragma unroll
+        for (int i = 0; i < PER; ++i)
+          if ((lane + 32 * i) / gs == gi) gscore[i] = gsc;
+      }
+      // keep the topk_group best groups: a group is dropped when at least
+      // topk_group groups score strictly higher (ties keep lower index first).
+      for (int gi = 0; gi < a.n_group; ++gi) {
+        float my = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < PER; ++i)
+          if ((lane + 32 * i) / gs == gi) my = gscore[i];
+        my = warp_max(my);
+        int better = 0;
+        for (int gj = 0; gj < a.n_group; ++gj) {
+          float other = -INFINITY;
+#pragma unroll
+          for (int i = 0; i < PER; ++i)
+            if ((lane + 32 * i) / gs == gj) other = gscore[i];
+          other = warp_max(other);
+          if (other > my || (other == my && gj < gi)) ++better;
+        }
+        if (better >= a.topk_group) {
+#pragma unroll
+          for (int i = 0; i < PER; ++i)
+            if ((lane + 32 * i) / gs == gi) sc[i] = -INFINITY;
+        }
+      }
+    }
+  }
+  // top-k by repeated warp argmax (lowest index wins ties)
+  float wsum = 0.f;
+  int my_ids[16];
+  float my_w[16];
+  for (int k = 0; k < a.topk; ++k) {
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int e = lane + 32 * i;
+      if (sc[i] > best || (sc[i] == best && e < bi)) {
+        best = sc[i];
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, d);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, d);
+      if (ob > best || (ob == best && oi < bi)) {
+        best = ob;
+        bi = oi;
+      }
+    }
+    // owner lane fetches the weight and removes the expert
+    float w = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      if (lane + 32 * i == bi) {
+        w = wt[i];
+        sc[i] = -INFINITY;
+      }
+    }
+    w = warp_sum(w);  // only the owner contributed
+    my_ids[k] = bi;
+    my_w[k] = w;
+    wsum += w;
+  }
+  const float scale = (a.renormalize ? 1.f / wsum : 1.f) * a.scaling;
+  if (lane < a.topk) {
+    float w = 0.f;
+    int id = 0;
+    for (int k = 0; k < a.topk; ++k)
+      if (k == lane) {
+        w = my_w[k];
+        id = my_ids[k];
+      }
+    a.topk_ids[tok * a.topk + lane] = id;
+    a.topk_w[tok * a.topk + lane] = w * scale;
+    if (a.counts) atomicAdd(&a.counts[id], 1);
+  }
+}
+
+// Offsets (exclusive scan of counts, computed by every CTA) + permutation + row gather.
+__global__ void moe_scatter_kernel(MoeRouteArgs a) {
+  extern __shared__ int s_off[];
+  for (int e = threadIdx.x; e < a.experts; e += blockDim.x) s_off[e] = a.counts[e];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int e = 0; e < a.experts; ++e) {
+      const int c = s_off[e];
+      s_off[e] = acc;
+      acc += c;
+    }
+    s_off[a.experts] = acc;
+  }
+  __syncthreads();
+  if (blockIdx.x == 0)
+    for (int e = threadIdx.x; e <= a.experts; e += blockDim.x) a.offsets[e] = s_off[e];
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  for (int tok = blockIdx.x * warps + (threadIdx.x >> 5); tok < a.tokens; tok += gridDim.x * warps) {
+    for (int k = 0; k < a.topk; ++k) {
+      int pos = 0;
+      if (lane == 0) {
+        const int e = a.topk_ids[tok * a.topk + k];
+        pos = s_off[e] + atomicAdd(&a.cursor[e], 1);
+        a.inv_perm[tok * a.topk + k] = pos;
+      }
+      pos = __shfl_sync(0xffffffffu, pos, 0);
+      if (a.x != nullptr) {
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.x) +
+                                                          static_cast<int64_t>(tok) * a.hidden);
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.x_perm) + static_cast<int64_t>(pos) * a.hidden);
+        for (int v = lane; v < a.hidden / 8; v += 32) dst[v] = src[v];
+      }
+    }
+  }
+}
+
+// out[t] = sum_k w[t,k] * y[inv[t,k]] (+ sigmoid(gate[t]) * shared[t])
+__global__ void moe_combine_kernel(MoeCombineArgs a) {
+  const int tok = blockIdx.x;
+  const __nv_bfloat16* y = static_cast<const __nv_bfloat16*>(a.y_perm);
+  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) + static_cast<int64_t>(tok) * a.hidden;
+  float sg = 0.f;
+  if (a.shared != nullptr) sg = a.shared_gate ? 1.f / (1.f + __expf(-a.shared_gate[tok * a.shared_gate_stride])) : 1.f;
+  for (int v = threadIdx.x; v < a.hidden / 2; v += blockDim.x) {
+    float2 acc = make_float2(0.f, 0.f);
+    for (int k = 0; k < a.topk; ++k) {
+      const int pos = a.inv_perm[tok * a.topk + k];
+      const float w = a.topk_w[tok * a.topk + k];
+      const float2 f = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(y + static_cast<int64_t>(pos) * a.hidden)[v]);
+      acc.x += w * f.x;
+      acc.y += w * f.y;
+    }
+    if (a.shared != nullptr) {
+      const float2 f = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(
+          static_cast<const __nv_bfloat16*>(a.shared) + static_cast<int64_t>(tok) * a.hidden)[v]);
+      acc.x += sg * f.x;
+      acc.y += sg * f.y;
+    }
+    reinterpret_cast<__nv_bfloat162*>(out)[v] = __floats2bfloat162_rn(acc.x, acc.y);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Embedding gather with multimodal overwrite
+// ---------------------------------------------------------------------------
+__global__ void embed_kernel(EmbedArgs a) {
+  const int tok = blockIdx.x;
+  const int mm = a.mm_index ? a.mm_index[tok] : -1;
+  const uint4* src;
+  if (mm >= 0) {
+    src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.mm_embeds) + static_cast<int64_t>(mm) * a.hidden);
+  } else {
+    const int id = a.ids[tok];
+    src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.table) + static_cast<int64_t>(id) * a.hidden);
+  }
+  uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + static_cast<int64_t>(tok) * a.hidden);
+  for (int v = threadIdx.x; v < a.hidden / 8; v += blockDim.x) dst[v] = src[v];
+}
+
+// ---------------------------------------------------------------------------
+// Sampling: one CTA (1024 threads) per row.
+// ---------------------------------------------------------------------------
+// SplitMix64 finaliser (Steele, Lea & Flood, OOPSLA 2014) as a counter-based hash.
+__device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+__device__ __forceinline__ float uniform01(uint64_t seed, uint64_t ctr) {
+  const uint64_t h = splitmix64(seed ^ splitmix64(ctr));
+  return (static_cast<float>(h >> 40) + 0.5f) * (1.0f / 16777216.0f);  // (0, 1)
+}
+__device__ __forceinline__ uint32_t f2key(float f) {
+  const uint32_t b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float key2f(uint32_t k) {
+  const uint32_t b = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+  return __uint_as_float(b);
+}
+
+template <class Op>
+__device__ __forceinline__ float block_reduce(float v, float* sred, Op op, float init) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, d));
+  __syncthreads();
+  if (lane == 0) sred[warp] = v;
+  __syncthreads();
+  v = (threadIdx.x < (blockDim.x >> 5)) ? sred[threadIdx.x] : init;
+  if (warp == 0) {
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, d));
+    if (lane == 0) sred[32] = v;
+  }
+  __syncthreads();
+  return sred[32];
+}
+
+struct MaxOp { __device__ float operator()(float a, float b) const { return fmaxf(a, b); } };
+struct SumOp { __device__ float operator()(float a, float b) const { return a + b; } };
+
+__global__ void __launch_bounds__(1024) sample_kernel(SampleArgs a) {
+  __shared__ float sred[33];
+  __shared__ unsigned int hist[256];
+  __shared__ uint32_t s_prefix;
+  __shared__ int s_kleft;
+  __shared__ unsigned long long s_best;
+  const int row = blockIdx.x;
+  float* lg = a.logits + static_cast<int64_t>(row) * a.logits_stride;
+  const int V = a.vocab;
+  const float temp = a.temperature ? a.temperature[row] : 0.f;
+  const float rep = a.rep_penalty ? a.rep_penalty[row] : 1.f;
+  const uint8_t* seen = a.seen ? a.seen + static_cast<int64_t>(row) * a.seen_stride : nullptr;
+
+  // 1) logits processing in place: suppression ranges, repetition penalty, temperature
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    float x = lg[i];
+    if (a.suppress_lo >= 0 && i >= a.suppress_lo && i < a.suppress_hi && i != a.suppress_keep) x = -INFINITY;
+    if (seen && rep != 1.f && seen[i]) x = x > 0.f ? x / rep : x * rep;
+    if (temp > 0.f) x = x / temp;
+    lg[i] = x;
+  }
+  __syncthreads();
+  // greedy
+  if (!(temp > 0.f)) {
+    unsigned long long best = 0ull;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+      const unsigned long long key = (static_cast<unsigned long long>(f2key(lg[i])) << 32) | (0xffffffffu - i);
+      best = key > best ? key : best;
+    }
+    if (threadIdx.x == 0) s_best = 0ull;
+    __syncthreads();
+    atomicMax(&s_best, best);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const int tok = static_cast<int>(0xffffffffu - static_cast<uint32_t>(s_best & 0xffffffffull));
+      a.out_tokens[row] = tok;
+      if (a.seen) a.seen[static_cast<int64_t>(row) * a.seen_stride + tok] = 1;
+    }
+    return;
+  }
+  float m = -INFINITY;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) m = fmaxf(m, lg[i]);
+  m = block_reduce(m, sred, MaxOp(), -INFINITY);
+  // 2) top-k threshold by 4-pass radix select on order-preserving keys
+  float thr = -INFINITY;
+  const int topk = a.top_k ? a.top_k[row] : 0;
+  if (topk > 0 && topk < V) {
+    if (threadIdx.x == 0) {
+      s_prefix = 0u;
+      s_kleft = topk;
+    }
+    for (int pass = 0; pass < 4; ++pass) {
+      const int shift = 24 - 8 * pass;
+      const uint32_t mask_hi = pass == 0 ? 0u : (0xffffffffu << (32 - 8 * pass));
+      for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0u;
+      __syncthreads();
+      const uint32_t pref = s_prefix;
+      for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        const uint32_t k = f2key(lg[i]);
+        if ((k & mask_hi) == pref) atomicAdd(&hist[(k >> shift) & 255u], 1u);
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        int left = s_kleft;
+        int bin = 255;
+        for (; bin > 0; --bin) {
+          const int c = static_cast<int>(hist[bin]);
+          if (c >= left) break;
+          left -= c;
+        }
+        s_kleft = left;
+        s_prefix = pref | (static_cast<uint32_t>(bin) << shift);
+      }
+      __syncthreads();
+    }
+    thr = key2f(s_prefix);
+  }
+  // 3) min-p threshold
+  const float minp = a.min_p ? a.min_p[row] : 0.f;
+  if (minp > 0.f) thr = fmaxf(thr, m + logf(minp));
+  // 4) top-p threshold: largest v with sum_{x >= v} e^(x-m) >= p * Z (binary search)
+  const float topp = a.top_p ? a.top_p[row] : 1.f;
+  if (topp < 1.f) {
+    float z = 0.f;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+      const float x = lg[i];
+      if (x >= thr) z += __expf(x - m);
+    }
+    z = block_reduce(z, sred, SumOp(), 0.f);
+    float lo = thr == -INFINITY ? m - 80.f : thr, hi = m;
+    for (int it = 0; it < 24; ++it) {
+      const float mid = 0.5f * (lo + hi);
+      float s = 0.f;
+      for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        const float x = lg[i];
+        if (x >= mid && x >= thr) s += __expf(x - m);
+      }
+      s = block_reduce(s, sred, SumOp(), 0.f);
+      if (s >= topp * z) lo = mid; else hi = mid;
+    }
+    thr = fmaxf(thr, lo);
+  }
+  // 5) Gumbel-max over the kept set
+  const uint64_t seed = a.seeds ? static_cast<uint64_t>(a.seeds[row]) : 0x1234ull;
+  const uint64_t step = a.step ? static_cast<uint64_t>(a.step[row]) : 0ull;
+  unsigned long long best = 0ull;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float x = lg[i];
+    if (x >= thr && x > -INFINITY) {
+      const float u = uniform01(seed + 0x9E37ull * step, static_cast<uint64_t>(i));
+      const float gmb = -logf(-logf(u));
+      const unsigned long long key = (static_cast<unsigned long long>(f2key(x + gmb)) << 32) | (0xffffffffu - i);
+      best = key > best ? key : best;
+    }
+  }
+  if (threadIdx.x == 0) s_best = 0ull;
+  __syncthreads();
+  atomicMax(&s_best, best);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int tok = static_cast<int>(0xffffffffu - static_cast<uint32_t>(s_best & 0xffffffffull));
+    if (s_best == 0ull) tok = 0;
+    a.out_tokens[row] = tok;
+    if (a.seen) a.seen[static_cast<int64_t>(row) * a.seen_stride + tok] = 1;
+  }
+}
+
+}  // namespace
+
+cudaError_t qkv_rope_store(const RopeStoreArgs& a, cudaStream_t stream) {
+  if (a.tokens == 0) return cudaSuccess;
+  const long warps = static_cast<long>(a.tokens) * (a.hq + 2 * a.hkv);
+  const int threads = 256;
+  const long grid = (warps + 7) / 8;
+  switch (a.head_dim) {
+    case 64: qkv_rope_store_kernel<64><<<grid, threads, 0, stream>>>(a); break;
+    case 128: qkv_rope_store_kernel<128><<<grid, threads, 0, stream>>>(a); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t moe_route(const MoeRouteArgs& a, cudaStream_t stream) {
+  if (a.tokens == 0) return cudaSuccess;
+  if (a.experts > 512 || a.topk > 16 || a.topk < 1) return cudaErrorInvalidValue;
+  if (a.counts) {
+    cudaMemsetAsync(a.counts, 0, sizeof(int) * a.experts, stream);
+    cudaMemsetAsync(a.cursor, 0, sizeof(int) * a.experts, stream);
+  }
+  const int grid = (a.tokens + 7) / 8;
+  const int per = (a.experts + 31) / 32;
+  if (per <= 4) moe_topk_kernel<4><<<grid, 256, 0, stream>>>(a);
+  else if (per <= 8) moe_topk_kernel<8><<<grid, 256, 0, stream>>>(a);
+  else moe_topk_kernel<16><<<grid, 256, 0, stream>>>(a);
+  if (a.counts) {
+    int sgrid = (a.tokens + 7) / 8;
+    if (sgrid > 1024) sgrid = 1024;
+    moe_scatter_kernel<<<sgrid, 256, sizeof(int) * (a.experts + 1), stream>>>(a);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t moe_combine(const MoeCombineArgs& a, cudaStream_t stream) {
+  if (a.tokens == 0) return cudaSuccess;
+  moe_combine_kernel<<<a.tokens, 256, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t embed(const EmbedArgs& a, cudaStream_t stream) {
+  if (a.tokens == 0) return cudaSuccess;
+  if (a.hidden % 8 != 0) return cudaErrorInvalidValue;
+  embed_kernel<<<a.tokens, 128, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t sample(const SampleArgs& a, cudaStream_t stream) {
+  if (a.rows == 0) return cudaSuccess;
+  sample_kernel<<<a.rows, 1024, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace omni

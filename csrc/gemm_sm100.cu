@@ -1,0 +1,412 @@
+// Persistent tcgen05 GEMM for every projection of the serving path: dense
+// linear layers, the MoE grouped expert GEMMs (w13 with SiLU*up fused, w2),
+// the LM head (fp32 logits) and the encoders' linear layers (bias + GELU).
+//
+// Layout choice ("weights as A"): the weight matrix feeds the M=128 side of the
+// UMMA and the token rows feed N (16..256).  Decode batches therefore keep the
+// tensor core's M dimension full, and one kernel covers decode (few tokens per
+// expert) and prefill (thousands of tokens) by picking the token tile BN.
+//
+// Warp roles (6 warps, one CTA per SM, persistent over tiles):
+//   warp 0     TMA producer (one elected lane), 128B-swizzled K-major tiles
+//   warp 1     TMEM allocator + MMA issuer (one elected lane)
+//   warps 2-5  epilogue: tcgen05.ld -> activation/bias/residual -> global store
+// Accumulators are double buffered in TMEM so the epilogue of tile i overlaps
+// the MMAs of tile i+1.
+//
+// Reference counterparts: SGLang QKVParallelLinear / RowParallelLinear /
+// FusedMoE as used by sglang_omni/models/qwen3_omni/thinker.py:192-213,402-412
+// and the talker's native MoE (sglang_omni/models/qwen3_omni/talker.py:242-247).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "omni_kernels.h"
+#include "sm100.cuh"
+
+namespace omni {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kThreads = 192;
+constexpr int kMaxGroups = 512;
+
+struct DevParams {
+  void* out;
+  int64_t ldo;
+  const __nv_bfloat16* bias;
+  const __nv_bfloat16* residual;
+  int64_t ldr;
+  const int* offsets;
+  int rows;
+  int m_out;
+  int a_rows;
+  int k;
+  int groups;
+  int out_f32;
+  int act;
+  int* status;
+};
+
+template <int BN, bool GATED>
+struct Cfg {
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes * (GATED ? 2 : 1) + kBBytes;
+  static constexpr int kAccCols = BN * (GATED ? 2 : 1);
+  static constexpr int kTmemCols = (2 * kAccCols) <= 32    ? 32
+                                   : (2 * kAccCols) <= 64  ? 64
+                                   : (2 * kAccCols) <= 128 ? 128
+                                   : (2 * kAccCols) <= 256 ? 256
+                                                           : 512;
+  static constexpr int kStagesRaw = (200 * 1024) / kStageBytes;
+  static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
+  // tiles + 1 KB alignment slack + barriers and the group tables (4 KB + 2 * (kMaxGroups + 1) ints)
+  static constexpr int kAuxBytes = 1024 + 8 * (kMaxGroups + 1) + 512;
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kAuxBytes;
+  static_assert(2 * kAccCols <= 512, "accumulators exceed TMEM");
+  static_assert(kBBytes % 1024 == 0, "B tile must keep 1024-byte alignment");
+};
+
+template <int BN>
+__device__ __forceinline__ void decode_tile(int t, const int* prefix, const int* offs, int groups, int& g, int& mt,
+                                            int& nt) {
+  int lo = 0, hi = groups - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (prefix[mid] <= t) lo = mid; else hi = mid - 1;
+  }
+  g = lo;
+  const int local = t - prefix[g];
+  const int rows = offs[g + 1] - offs[g];
+  const int ntiles = (rows + BN - 1) / BN;
+  mt = local / ntiles;
+  nt = local - mt * ntiles;
+}
+
+template <int BN, bool GATED>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                     const DevParams p) {
+  using C = Cfg<BN, GATED>;
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte aligned base for the swizzled tiles.
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
+  uint8_t* aux = smem + C::kStages * C::kStageBytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(aux);
+  uint64_t* empty_bar = full_bar + C::kStages;
+  uint64_t* tfull_bar = empty_bar + C::kStages;   // [2]
+  uint64_t* tempty_bar = tfull_bar + 2;           // [2]
+  uint64_t* drain_bar = tempty_bar + 2;           // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* total_tiles_s = const_cast<int*>(reinterpret_cast<volatile int*>(tmem_slot + 2));
+  int* offs_s = reinterpret_cast<int*>(aux + 512);
+  int* prefix_s = offs_s + (kMaxGroups + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int groups = p.groups;
+  const int m_tiles = (p.m_out + kBM - 1) / kBM;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 128);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  // Group row offsets and tile prefix sums (warp 2).
+  if (warp == 2) {
+    int carry = 0;
+    for (int base = 0; base < groups; base += 32) {
+      const int g = base + lane;
+      int rows = 0;
+      if (g < groups) {
+        const int o0 = p.offsets ? p.offsets[g] : 0;
+        const int o1 = p.offsets ? p.offsets[g + 1] : p.rows;
+        offs_s[g] = o0;
+        if (g == groups - 1) offs_s[groups] = o1;
+        rows = o1 - o0;
+      }
+      const int tiles = (g < groups) ? m_tiles * ((rows + BN - 1) / BN) : 0;
+      int incl = tiles;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) incl += v;
+      }
+      if (g < groups) prefix_s[g] = carry + incl - tiles;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) {
+      prefix_s[groups] = carry;
+      *total_tiles_s = carry;
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  const uint32_t tmem_base = *tmem_slot;
+  const int total_tiles = *total_tiles_s;
+  const int num_kb = (p.k + kBK - 1) / kBK;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      long issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        int g, mt, nt;
+        decode_tile<BN>(t, prefix_s, offs_s, groups, g, mt, nt);
+        const int a_row = g * p.a_rows + mt * kBM;
+        const int b_row = offs_s[g] + nt * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, p.status)) { ok = false; break; }
+          uint8_t* sa = smem + stage * C::kStageBytes;
+          uint8_t* sb = sa + C::kABytes * (GATED ? 2 : 1);
+          mbar_arrive_expect_tx(&full_bar[stage], C::kStageBytes);
+          tma_load_2d(sa, &tmap_a, &full_bar[stage], kb * kBK, a_row);
+          if (GATED) tma_load_2d(sa + C::kABytes, &tmap_a, &full_bar[stage], kb * kBK, a_row + p.m_out);
+          tma_load_2d(sb, &tmap_b, &full_bar[stage], kb * kBK, b_row);
+          ++issued;
+          if (++stage == C::kStages) { stage = 0; phase ^= 1; }
+        }
+      }
+      // Drain: wait (bounded) for the loads this thread issued last on every stage.
+      const long first = issued > C::kStages ? issued - C::kStages : 0;
+      for (long i = first; i < issued; ++i) {
+        const int s = static_cast<int>(i % C::kStages);
+        const uint32_t ph = static_cast<uint32_t>((i / C::kStages) & 1);
+        mbar_wait(&full_bar[s], ph, nullptr, p.status);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc = umma_idesc_bf16_f32(kBM, BN);
+    int stage = 0;
+    uint32_t phase = 0;
+    int local = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, abort_flag, p.status)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * C::kAccCols;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.status)) { ok = false; break; }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t sa = smem_u32(smem + stage * C::kStageBytes);
+          const uint32_t sb = sa + C::kABytes * (GATED ? 2 : 1);
+          const uint64_t adesc = umma_desc_sw128(sa);
+          const uint64_t bdesc = umma_desc_sw128(sb);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            // +32 bytes per 16-element K step inside the 128-byte swizzle atom (>>4 => +2).
+            const uint32_t accum = (kb > 0 || kk > 0) ? 1u : 0u;
+            umma_f16_ss(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, accum);
+            if (GATED) {
+              const uint64_t adesc_up = umma_desc_sw128(sa + C::kABytes);
+              umma_f16_ss(d_tmem + BN, adesc_up + 2 * kk, bdesc + 2 * kk, idesc, accum);
+            }
+          }
+          umma_commit(&empty_bar[stage]);
+        }
+        __syncwarp();
+        if (++stage == C::kStages) { stage = 0; phase ^= 1; }
+      }
+      if (!ok) break;
+      if (lane == 0) umma_commit(&tfull_bar[acc]);
+      __syncwarp();
+    }
+    // Drain every MMA this thread issued before TMEM is released.
+    if (lane == 0) {
+      umma_commit(drain_bar);
+      mbar_wait(drain_bar, 0, nullptr, p.status);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int lane_base = 32 * (warp & 3);
+    int local = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
+      int g, mt, nt;
+      decode_tile<BN>(t, prefix_s, offs_s, groups, g, mt, nt);
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, p.status)) break;
+      tc_fence_after();
+      const int m = mt * kBM + lane_base + lane;
+      const int row0 = offs_s[g] + nt * BN;
+      const int row_end = offs_s[g + 1];
+      const bool m_ok = m < p.m_out;
+      float bias_v = 0.f;
+      if (p.bias != nullptr && m_ok) bias_v = __bfloat162float(p.bias[static_cast<int64_t>(g) * p.m_out + m]);
+      const uint32_t t_base = tmem_base + (static_cast<uint32_t>(lane_base) << 16) + acc * C::kAccCols;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        uint32_t r[16];
+        uint32_t u[16];
+        tmem_ld_32x32b_x16(t_base + c, r);
+        if (GATED) tmem_ld_32x32b_x16(t_base + BN + c, u);
+        tmem_ld_wait();
+        if (m_ok) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int row = row0 + c + j;
+            if (row < row_end) {
+              float v = __uint_as_float(r[j]);
+              if (GATED) {
+                v = silu_f(v) * __uint_as_float(u[j]);
+              } else {
+                v += bias_v;
+                if (p.act == kActGeluTanh) v = gelu_tanh_f(v);
+                else if (p.act == kActGeluErf) v = gelu_erf_f(v);
+                else if (p.act == kActSilu) v = silu_f(v);
+              }
+              if (p.residual != nullptr) v += __bfloat162float(p.residual[static_cast<int64_t>(row) * p.ldr + m]);
+              if (p.out_f32) {
+                static_cast<float*>(p.out)[static_cast<int64_t>(row) * p.ldo + m] = v;
+              } else {
+                static_cast<__nv_bfloat16*>(p.out)[static_cast<int64_t>(row) * p.ldo + m] = __float2bfloat16(v);
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty_bar[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map [rows, cols] (cols contiguous), box [box_rows, 64], 128-byte swizzle.
+bool make_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t row_stride_elems,
+                  uint32_t box_rows) {
+  auto fn = get_encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {row_stride_elems * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int num_sms() {
+  static int n = 0;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  });
+  return n;
+}
+
+template <int BN, bool GATED>
+cudaError_t launch(const GemmArgs& a, cudaStream_t stream) {
+  using C = Cfg<BN, GATED>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_bf16_kernel<BN, GATED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  CUtensorMap ta, tb;
+  if (!make_tmap_2d(&ta, a.a, static_cast<uint64_t>(a.groups) * a.a_rows, a.k, a.k, kBM)) return cudaErrorInvalidValue;
+  if (!make_tmap_2d(&tb, a.b, a.rows > 0 ? a.rows : 1, a.k, a.k, BN)) return cudaErrorInvalidValue;
+  DevParams p;
+  p.out = a.out;
+  p.ldo = a.ldo;
+  p.bias = static_cast<const __nv_bfloat16*>(a.bias);
+  p.residual = static_cast<const __nv_bfloat16*>(a.residual);
+  p.ldr = a.ldr;
+  p.offsets = a.offsets;
+  p.rows = a.rows;
+  p.m_out = a.m_out;
+  p.a_rows = a.a_rows;
+  p.k = a.k;
+  p.groups = a.groups;
+  p.out_f32 = a.out_f32;
+  p.act = a.act;
+  p.status = a.status;
+  const int m_tiles = (a.m_out + kBM - 1) / kBM;
+  // Upper bound of the tile count: every group may add one partial token tile.
+  const long row_tiles = (a.offsets ? (static_cast<long>(a.rows) + BN - 1) / BN + a.groups : (a.rows + BN - 1) / BN);
+  const long bound = static_cast<long>(m_tiles) * (row_tiles > 0 ? row_tiles : 1);
+  int grid = a.max_ctas > 0 ? a.max_ctas : num_sms();
+  if (bound < grid) grid = static_cast<int>(bound);
+  if (grid < 1) grid = 1;
+  gemm_bf16_kernel<BN, GATED><<<grid, kThreads, C::kSmemBytes, stream>>>(ta, tb, p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
+  if (a.groups < 1 || a.groups > kMaxGroups || a.k <= 0 || a.m_out <= 0) return cudaErrorInvalidValue;
+  if (a.k % 8 != 0) return cudaErrorInvalidValue;  // 16-byte row stride for TMA
+  if (a.rows == 0) return cudaSuccess;
+  int hint = a.expected_rows_per_group > 0 ? a.expected_rows_per_group : a.rows;
+  if (a.gated) {
+    if (hint <= 16) return launch<16, true>(a, stream);
+    if (hint <= 32) return launch<32, true>(a, stream);
+    if (hint <= 64) return launch<64, true>(a, stream);
+    return launch<128, true>(a, stream);
+  }
+  if (hint <= 16) return launch<16, false>(a, stream);
+  if (hint <= 32) return launch<32, false>(a, stream);
+  if (hint <= 64) return launch<64, false>(a, stream);
+  if (hint <= 128) return launch<128, false>(a, stream);
+  return launch<256, false>(a, stream);
+}
+
+}  // namespace omni

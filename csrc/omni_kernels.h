@@ -1,0 +1,179 @@
+// Host-side launchers of the sm_100a kernels.  The .cu files implement them
+// against raw device pointers (no torch headers, so they compile fast); the
+// torch bindings in bindings.cpp validate tensors and forward here.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace omni {
+
+// ---------------------------------------------------------------- GEMM (tcgen05)
+// out[r, m] = act( sum_k B[r, k] * A[g * a_rows + m, k] ) (+ bias[g, m]) (+ residual[r, m])
+// for every row r of group g (rows offsets[g] .. offsets[g+1]) and m < m_out.
+// A holds the weights ([groups * a_rows, k] bf16, K contiguous); B holds the
+// activations ([rows, k] bf16).  With gated=1 a_rows = 2 * m_out: the first
+// m_out rows of each group are the gate projection, the next m_out the up
+// projection, and the epilogue emits silu(gate) * up.
+enum GemmAct : int { kActNone = 0, kActGeluTanh = 1, kActGeluErf = 2, kActSilu = 3 };
+
+struct GemmArgs {
+  const void* a;          // weights, bf16
+  const void* b;          // activations, bf16
+  void* out;              // bf16 or fp32
+  int64_t ldo;            // out row stride in elements
+  int out_f32;
+  const void* bias;       // bf16 [groups, m_out] or nullptr
+  const void* residual;   // bf16, row stride ldr, or nullptr
+  int64_t ldr;
+  int m_out;
+  int a_rows;             // weight rows per group
+  int k;
+  int groups;
+  const int* offsets;     // device int32 [groups + 1], or nullptr for one dense group
+  int rows;               // total rows of B (for the tensor map and dense mode)
+  int expected_rows_per_group;  // host hint used to pick the token tile
+  int gated;
+  int act;
+  int* status;            // device int32 status word (may be nullptr)
+  int max_ctas;           // 0 = one CTA per SM
+};
+cudaError_t gemm_bf16(const GemmArgs& args, cudaStream_t stream);
+
+// ---------------------------------------------------------------- normalisation
+// y = rmsnorm(x (+ residual)) * w ; when residual != nullptr the sum is also
+// written back into residual (fused residual add).
+cudaError_t rmsnorm_bf16(const void* x, const void* w, void* y, void* residual, int rows, int hidden,
+                         int64_t ld_x, int64_t ld_y, float eps, cudaStream_t stream);
+// Per-head RMSNorm over the last dim (head_dim) of a [rows, heads, head_dim] view.
+cudaError_t layernorm_bf16(const void* x, const void* w, const void* b, void* y, int rows, int hidden, float eps,
+                           cudaStream_t stream);
+
+
+// ---------------------------------------------------------------- attention
+// Paged KV cache of one layer: [pages, hkv, 64, head_dim] bf16 (page size 64).
+struct AttnPrefillArgs {
+  const void* q;          // [tokens, hq, D] rows of stride q_stride
+  int64_t q_stride;
+  const void* k;          // paged cache, or contiguous [kv_tokens, hkv, D] rows of stride kv_stride
+  const void* v;
+  int64_t kv_stride;
+  const int* block_table; // [B, bt_stride] page ids, nullptr => contiguous K/V
+  int bt_stride;
+  const int* cu_q;        // [B + 1]
+  const int* kv_lens;     // [B] keys visible to each request (including this chunk)
+  const int* cu_kv;       // contiguous mode: [B + 1] first key row of each request
+  const int* tile_req;    // [num_tiles] request of each 64-row query tile
+  const int* tile_tok0;   // [num_tiles] first query token (within the request) of the tile
+  int num_tiles;
+  int hq, hkv, head_dim;
+  float scale;
+  int causal;
+  void* out;              // [tokens, hq, D] rows of stride out_stride
+  int64_t out_stride;
+};
+cudaError_t attention_prefill(const AttnPrefillArgs& a, cudaStream_t stream);
+
+struct AttnDecodeArgs {
+  const void* q;          // [B, hq, D] rows of stride q_stride
+  int64_t q_stride;
+  const void* k;
+  const void* v;
+  const int* block_table;
+  int bt_stride;
+  const int* kv_lens;
+  int batch, hq, hkv, head_dim;
+  float scale;
+  int keys_per_split;     // multiple of 64
+  int max_splits;         // grid.x; splits beyond a request's length exit at once
+  void* out;
+  int64_t out_stride;
+  float* part_o;          // scratch [B, hq, max_splits, D] fp32
+  float* part_lse;        // scratch [B, hq, max_splits] fp32
+};
+cudaError_t attention_decode(const AttnDecodeArgs& a, cudaStream_t stream);
+
+// ---------------------------------------------------------------- fused decoder-step ops
+struct RopeStoreArgs {
+  void* qkv;               // [tokens, (hq + 2 hkv) * D], q and k rotated in place
+  int64_t qkv_stride;
+  int tokens, hq, hkv, head_dim;
+  const void* q_norm;      // [D] bf16 or nullptr
+  const void* k_norm;
+  float eps;
+  const int* positions;    // [pos_rows, tokens]
+  int pos_rows;            // 1 (plain RoPE) or 3 (M-RoPE t/h/w)
+  int section[3];          // M-RoPE frequency sections (pairs)
+  int interleaved;         // M-RoPE interleaved (THWTHW...) layout
+  const float* cos_tab;    // [max_pos, rot_dim / 2]
+  const float* sin_tab;
+  int rot_dim;             // rotated dims (<= D); 0 disables RoPE
+  int neox;                // 1: rotate halves, 0: rotate adjacent pairs
+  const int* slot_mapping; // [tokens] page * 64 + offset, -1 skips; nullptr => no cache write
+  void* k_cache;
+  void* v_cache;
+};
+cudaError_t qkv_rope_store(const RopeStoreArgs& a, cudaStream_t stream);
+
+struct MoeRouteArgs {
+  const float* logits;     // [tokens, experts] router logits (fp32)
+  int64_t logits_stride;
+  int tokens, experts, topk;
+  int mode;                // 0 softmax top-k; 1 sigmoid + bias, group-limited
+  const float* bias;       // [experts] selection bias (mode 1) or nullptr
+  int n_group, topk_group;
+  int renormalize;
+  float scaling;
+  int* topk_ids;           // [tokens, topk]
+  float* topk_w;           // [tokens, topk]
+  int* counts;             // scratch [experts]; nullptr => routing only
+  int* cursor;             // scratch [experts]
+  int* offsets;            // [experts + 1]
+  int* inv_perm;           // [tokens, topk] row of each (token, k) in the permuted layout
+  const void* x;           // [tokens, hidden] bf16 rows to gather (or nullptr)
+  void* x_perm;            // [tokens * topk, hidden]
+  int hidden;
+};
+cudaError_t moe_route(const MoeRouteArgs& a, cudaStream_t stream);
+
+struct MoeCombineArgs {
+  const void* y_perm;      // [tokens * topk, hidden]
+  const int* inv_perm;
+  const float* topk_w;
+  int tokens, topk, hidden;
+  const void* shared;      // [tokens, hidden] shared-expert output or nullptr
+  const float* shared_gate;// [tokens] gate logits (sigmoid applied) or nullptr (=1)
+  int shared_gate_stride;
+  void* out;               // [tokens, hidden]
+};
+cudaError_t moe_combine(const MoeCombineArgs& a, cudaStream_t stream);
+
+struct EmbedArgs {
+  const int* ids;
+  const void* table;       // [vocab, hidden]
+  const int* mm_index;     // [tokens] row of mm_embeds or -1 (nullptr => none)
+  const void* mm_embeds;
+  void* out;
+  int tokens, hidden;
+};
+cudaError_t embed(const EmbedArgs& a, cudaStream_t stream);
+
+struct SampleArgs {
+  float* logits;           // [rows, vocab] fp32, processed in place
+  int64_t logits_stride;
+  int rows, vocab;
+  const float* temperature;  // [rows] (0 => greedy) or nullptr (all greedy)
+  const int* top_k;          // [rows] (<= 0 disables)
+  const float* top_p;        // [rows]
+  const float* min_p;        // [rows]
+  const float* rep_penalty;  // [rows]
+  uint8_t* seen;             // [rows, seen_stride] token-seen mask (penalty + update)
+  int64_t seen_stride;
+  int suppress_lo, suppress_hi, suppress_keep;  // [lo, hi) masked except keep; lo < 0 disables
+  const int64_t* seeds;      // [rows]
+  const int* step;           // [rows] decode step (RNG counter)
+  int* out_tokens;           // [rows]
+};
+cudaError_t sample(const SampleArgs& a, cudaStream_t stream);
+
+}  // namespace omni

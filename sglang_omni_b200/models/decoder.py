@@ -1,0 +1,259 @@
+"""Decoder-only transformer shared by every autoregressive stage.
+
+One implementation covers:
+  * the Qwen3-Omni thinker (MoE 128x top-8, QK-norm, interleaved M-RoPE),
+  * the Qwen3-Omni talker (MoE top-6 + sigmoid-gated shared expert),
+  * the Qwen3-Omni code predictor (dense SwiGLU),
+  * the S2-Pro slow AR (dense, non-neox RoPE, tied embeddings),
+  * Ming's BailingMoeV2 LLM (sigmoid group-limited routing, partial RoPE,
+    first-k dense layers, shared expert).
+
+All hot ops go through ``sglang_omni_b200.ops`` (sm_100a kernels on CUDA,
+PyTorch restatements on CPU).  Fused weight layouts: ``qkv`` = [q; k; v],
+``w13`` = [gate; up] per expert, so the SiLU*up multiply happens inside the
+GEMM epilogue.
+
+Reference counterparts: Qwen3OmniMoeThinkerTextModel / DecoderLayer /
+Attention / SparseMoeBlock (sglang_omni/models/qwen3_omni/thinker.py:140-706),
+the talker text model (sglang_omni/models/qwen3_omni/talker.py:177-400), the
+S2-Pro SGLang text model (sglang_omni/models/fishaudio_s2_pro/sglang_model.py:53-380)
+and BailingMoeV2 (sglang_omni/models/ming_omni/thinker.py:155-826).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+from torch import nn
+
+from .. import ops
+from ..ops.attention import DecodeWorkspace
+from ..ops.moe import MoEWorkspace
+
+
+@dataclass
+class DecoderConfig:
+    vocab_size: int = 151936
+    hidden_size: int = 2048
+    num_layers: int = 48
+    num_heads: int = 32
+    num_kv_heads: int = 4
+    head_dim: int = 128
+    intermediate_size: int = 0          # dense SwiGLU width (dense layers)
+    num_experts: int = 0
+    topk: int = 0
+    moe_intermediate_size: int = 0
+    shared_expert_intermediate_size: int = 0
+    shared_expert_gate: bool = True     # sigmoid gate on the shared expert (Qwen3 talker)
+    norm_topk_prob: bool = True
+    router_mode: int = 0                # 0 softmax top-k, 1 sigmoid + bias group-limited
+    n_group: int = 1
+    topk_group: int = 1
+    routed_scaling_factor: float = 1.0
+    first_k_dense: int = 0
+    mlp_only_layers: tuple = ()
+    rms_norm_eps: float = 1e-6
+    rope_theta: float = 1e6
+    rope_neox: bool = True
+    rotary_dim: int | None = None
+    mrope_section: list | None = None   # e.g. [24, 20, 20]
+    mrope_interleaved: bool = True
+    qk_norm: bool = True
+    tie_word_embeddings: bool = False
+    max_position: int = 65536
+    dtype: torch.dtype = torch.bfloat16
+    name: str = "decoder"
+
+    def is_moe_layer(self, i: int) -> bool:
+        return self.num_experts > 0 and i >= self.first_k_dense and i not in self.mlp_only_layers
+
+    @property
+    def q_size(self):
+        return self.num_heads * self.head_dim
+
+    @property
+    def kv_size(self):
+        return self.num_kv_heads * self.head_dim
+
+    def param_count(self) -> int:
+        H = self.hidden_size
+        n = 2 * self.vocab_size * H if not self.tie_word_embeddings else self.vocab_size * H
+        for i in range(self.num_layers):
+            n += H * (self.q_size + 2 * self.kv_size) + self.q_size * H + 2 * H
+            if self.is_moe_layer(i):
+                n += self.num_experts * (3 * H * self.moe_intermediate_size) + self.num_experts * H
+                if self.shared_expert_intermediate_size:
+                    n += 3 * H * self.shared_expert_intermediate_size + H
+            else:
+                n += 3 * H * self.intermediate_size
+        return n
+
+
+@dataclass
+class ForwardBatch:
+    """Device-side description of one engine step (prefill chunk or decode)."""
+
+    is_decode: bool
+    positions: torch.Tensor                 # int32 [3, T] (M-RoPE) or [T]
+    slot_mapping: torch.Tensor | None       # int32 [T]
+    kv_lens: torch.Tensor                   # int32 [B]
+    block_table: torch.Tensor               # int32 [B, max_pages]
+    input_ids: torch.Tensor | None = None   # int32 [T]
+    input_embeds: torch.Tensor | None = None
+    cu_q: torch.Tensor | None = None        # prefill: int32 [B + 1]
+    tile_req: torch.Tensor | None = None
+    tile_tok0: torch.Tensor | None = None
+    logits_indices: torch.Tensor | None = None  # rows whose logits are needed
+    mm_index: torch.Tensor | None = None    # int32 [T] row of mm_embeds or -1
+    mm_embeds: torch.Tensor | None = None
+    deepstack: list | None = None           # [(positions int64 [n], embeds [n, H])] for layers 0..
+    capture_layers: tuple = ()
+    captured: dict = field(default_factory=dict)
+
+
+class DecoderLM(nn.Module):
+    """Weights as plain parameters in fused layouts; forward is op-by-op on the kernels."""
+
+    def __init__(self, cfg: DecoderConfig, device="cpu"):
+        super().__init__()
+        self.cfg = cfg
+        H, dt = cfg.hidden_size, cfg.dtype
+        P = lambda *shape: nn.Parameter(torch.empty(*shape, dtype=dt, device=device), requires_grad=False)  # noqa: E731
+        self.embed = P(cfg.vocab_size, H)
+        self.layers = nn.ModuleList()
+        for i in range(cfg.num_layers):
+            L = nn.Module()
+            L.ln1 = P(H)
+            L.qkv = P(cfg.q_size + 2 * cfg.kv_size, H)
+            L.o = P(H, cfg.q_size)
+            L.ln2 = P(H)
+            if cfg.qk_norm:
+                L.q_norm = P(cfg.head_dim)
+                L.k_norm = P(cfg.head_dim)
+            if cfg.is_moe_layer(i):
+                E, I = cfg.num_experts, cfg.moe_intermediate_size
+                L.router = P(E, H)
+                L.w13 = P(E, 2 * I, H)
+                L.w2 = P(E, H, I)
+                if cfg.router_mode == 1:
+                    L.router_bias = nn.Parameter(torch.zeros(E, dtype=torch.float32, device=device),
+                                                 requires_grad=False)
+                if cfg.shared_expert_intermediate_size:
+                    Is = cfg.shared_expert_intermediate_size
+                    L.s13 = P(2 * Is, H)
+                    L.s2 = P(H, Is)
+                    if cfg.shared_expert_gate:
+                        L.sgate = P(1, H)
+            else:
+                L.mlp13 = P(2 * cfg.intermediate_size, H)
+                L.mlp2 = P(H, cfg.intermediate_size)
+            self.layers.append(L)
+        self.final_norm = P(H)
+        self.lm_head = None if cfg.tie_word_embeddings else P(cfg.vocab_size, H)
+        rot = cfg.rotary_dim or cfg.head_dim
+        cos, sin = ops.rope_tables(rot, cfg.rope_theta, cfg.max_position, device)
+        self.register_buffer("cos_tab", cos, persistent=False)
+        self.register_buffer("sin_tab", sin, persistent=False)
+        self._moe_ws: MoEWorkspace | None = None
+        self._dec_ws: DecodeWorkspace | None = None
+
+    # ------------------------------------------------------------------ init
+    @torch.no_grad()
+    def random_init_(self, seed: int = 0, std: float = 0.02):
+        """N(0, std) for matrices, ones for norm weights; deterministic per parameter."""
+        dev = self.embed.device
+        for idx, (name, p) in enumerate(self.named_parameters()):
+            if p.dim() == 1 and ("ln" in name or "norm" in name):
+                p.fill_(1.0)
+            elif name.endswith("router_bias"):
+                p.zero_()
+            else:
+                g = torch.Generator(device=dev).manual_seed(seed * 100003 + idx)
+                p.normal_(0.0, std, generator=g)
+        return self
+
+    @property
+    def head_weight(self):
+        return self.embed if self.lm_head is None else self.lm_head
+
+    # ------------------------------------------------------------------ workspaces
+    def ensure_workspaces(self, max_tokens: int, max_batch: int, max_context: int):
+        cfg, dev = self.cfg, self.embed.device
+        if cfg.num_experts and (self._moe_ws is None or self._moe_ws.max_tokens < max_tokens):
+            self._moe_ws = MoEWorkspace(max_tokens, cfg.num_experts, cfg.topk, cfg.hidden_size,
+                                        cfg.moe_intermediate_size, dev, cfg.dtype)
+        if dev.type == "cuda":
+            ws = self._dec_ws
+            need_splits = max(1, (max_context + 255) // 256)
+            if ws is None or ws.max_splits < need_splits or ws.part_lse.numel() < max_batch * cfg.num_heads * need_splits:
+                self._dec_ws = DecodeWorkspace(max_batch, cfg.num_heads, cfg.head_dim, max_context, dev)
+
+    # ------------------------------------------------------------------ forward
+    def _mlp(self, L, x, i):
+        cfg = self.cfg
+        if cfg.is_moe_layer(i):
+            shared_out = shared_gate = None
+            if cfg.shared_expert_intermediate_size:
+                shared_out = ops.linear(ops.linear(x, L.s13, gated=True), L.s2)
+                if cfg.shared_expert_gate:
+                    shared_gate = ops.linear(x, L.sgate, out_dtype=torch.float32)
+            ws = self._moe_ws
+            if ws is None or ws.max_tokens < x.shape[0]:
+                self.ensure_workspaces(x.shape[0], 1, 64)
+                ws = self._moe_ws
+            return ops.fused_moe(x, L.router, L.w13, L.w2, cfg.topk, ws, renormalize=cfg.norm_topk_prob,
+                                 mode=cfg.router_mode, bias=getattr(L, "router_bias", None), n_group=cfg.n_group,
+                                 topk_group=cfg.topk_group, scaling=cfg.routed_scaling_factor,
+                                 shared_out=shared_out, shared_gate=shared_gate)
+        return ops.linear(ops.linear(x, L.mlp13, gated=True), L.mlp2)
+
+    def forward(self, fb: ForwardBatch, kv_cache: torch.Tensor) -> torch.Tensor:
+        """Returns final-normed hidden states of ``fb.logits_indices`` rows (all rows if None).
+
+        kv_cache: [layers, 2, pages, Hkv, 64, D].
+        """
+        cfg = self.cfg
+        if fb.input_embeds is not None:
+            x = fb.input_embeds
+        else:
+            x = ops.embed(fb.input_ids, self.embed, fb.mm_index, fb.mm_embeds)
+        T = x.shape[0]
+        res = x.clone() if fb.input_embeds is not None else x
+        h = None
+        rot = cfg.rotary_dim or cfg.head_dim
+        scale = 1.0 / math.sqrt(cfg.head_dim)
+        for i, L in enumerate(self.layers):
+            if h is None:
+                normed = ops.rms_norm(res, L.ln1, cfg.rms_norm_eps)
+            else:
+                normed = ops.rms_norm(h, L.ln1, cfg.rms_norm_eps, residual=res)
+            if i in fb.capture_layers:
+                fb.captured[i] = res.clone()
+            qkv = ops.linear(normed, L.qkv)
+            ops.qkv_rope_store(qkv, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, fb.positions, self.cos_tab,
+                               self.sin_tab, rot, getattr(L, "q_norm", None), getattr(L, "k_norm", None),
+                               cfg.rms_norm_eps, cfg.rope_neox, cfg.mrope_section, cfg.mrope_interleaved,
+                               fb.slot_mapping, kv_cache[i, 0], kv_cache[i, 1])
+            if fb.is_decode:
+                attn = ops.decode_attention(qkv, kv_cache[i, 0], kv_cache[i, 1], fb.block_table, fb.kv_lens,
+                                            cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, self._dec_ws, scale)
+            else:
+                attn = ops.prefill_attention(qkv, kv_cache[i, 0], kv_cache[i, 1], fb.block_table, fb.cu_q,
+                                             fb.kv_lens, fb.tile_req, fb.tile_tok0, cfg.num_heads,
+                                             cfg.num_kv_heads, cfg.head_dim, scale)
+            o = ops.linear(attn, L.o)
+            normed2 = ops.rms_norm(o, L.ln2, cfg.rms_norm_eps, residual=res)
+            h = self._mlp(L, normed2, i)
+            if fb.deepstack is not None and i < len(fb.deepstack) and fb.deepstack[i] is not None:
+                pos, emb = fb.deepstack[i]
+                h.index_add_(0, pos, emb.to(h.dtype))
+        if cfg.num_layers in fb.capture_layers:
+            fb.captured[cfg.num_layers] = (res + h).clone()
+        if fb.logits_indices is not None:
+            sel = fb.logits_indices.long()
+            return ops.rms_norm(h[sel], self.final_norm, cfg.rms_norm_eps, residual=res[sel].clone())
+        return ops.rms_norm(h, self.final_norm, cfg.rms_norm_eps, residual=res)
+
+    def logits(self, hidden: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        return ops.linear(hidden, self.head_weight, out=out, out_dtype=torch.float32)

@@ -1,0 +1,159 @@
+"""Paged GQA attention (csrc/attention.cu) and the KV-cache layout helpers.
+
+KV cache of one layer: ``[pages, Hkv, 64, D]`` bf16 (page size 64); a request
+owns a row of page ids in ``block_table``; token slot = page * 64 + offset.
+
+Reference counterparts: SGLang RadixAttention backends (FlashInfer / FA3) as
+used by sglang_omni/models/qwen3_omni/thinker.py:236-243, and the encoders'
+non-causal SDPA (transformers qwen3_omni_moe audio / vision towers).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+from ._ext import ext
+
+PAGE = 64
+
+
+def prefill_tiles(q_lens: list[int], group: int) -> tuple[list[int], list[int]]:
+    """64-row query tiles of the GQA-packed prefill kernel: (request, first token) per tile."""
+    tpt = max(1, 64 // group)
+    req, tok0 = [], []
+    for b, n in enumerate(q_lens):
+        for t in range(0, n, tpt):
+            req.append(b)
+            tok0.append(t)
+    return req, tok0
+
+
+def _sdpa_ref(q, k, v, causal, q_offset, scale):
+    """q [Tq, Hq, D], k/v [Tk, Hkv, D] -> [Tq, Hq, D] in fp32."""
+    hq, hkv = q.shape[1], k.shape[1]
+    g = hq // hkv
+    k = k.float().repeat_interleave(g, dim=1)
+    v = v.float().repeat_interleave(g, dim=1)
+    s = torch.einsum("qhd,khd->hqk", q.float(), k) * scale
+    if causal:
+        tq, tk = q.shape[0], k.shape[0]
+        qi = torch.arange(tq, device=q.device)[:, None] + q_offset
+        ki = torch.arange(tk, device=q.device)[None, :]
+        s = s.masked_fill((ki > qi)[None], float("-inf"))
+    p = torch.softmax(s, dim=-1)
+    return torch.einsum("hqk,khd->qhd", p, v)
+
+
+def gather_kv_ref(cache: torch.Tensor, pages: list[int] | torch.Tensor, n: int) -> torch.Tensor:
+    """[n, Hkv, D] keys (or values) of one request from a paged cache [pages, Hkv, 64, D]."""
+    pages = torch.as_tensor(pages, dtype=torch.long, device=cache.device)
+    need = (n + PAGE - 1) // PAGE
+    blk = cache[pages[:need]]  # [need, Hkv, 64, D]
+    return blk.permute(0, 2, 1, 3).reshape(need * PAGE, cache.shape[1], cache.shape[3])[:n]
+
+
+def paged_attention_ref(q, k_cache, v_cache, block_table, cu_q, kv_lens, scale, causal=True):
+    cu = cu_q.tolist()
+    kl = kv_lens.tolist()
+    out = torch.empty(q.shape, dtype=torch.float32, device=q.device)
+    for b in range(len(kl)):
+        a, e = cu[b], cu[b + 1]
+        if e <= a:
+            continue
+        k = gather_kv_ref(k_cache, block_table[b], kl[b])
+        v = gather_kv_ref(v_cache, block_table[b], kl[b])
+        out[a:e] = _sdpa_ref(q[a:e], k, v, causal, kl[b] - (e - a), scale)
+    return out
+
+
+def varlen_attention_ref(q, k, v, cu_seqlens, scale, causal=False):
+    cu = cu_seqlens.tolist()
+    out = torch.empty(q.shape, dtype=torch.float32, device=q.device)
+    for b in range(len(cu) - 1):
+        a, e = cu[b], cu[b + 1]
+        if e > a:
+            out[a:e] = _sdpa_ref(q[a:e], k[a:e], v[a:e], causal, 0, scale)
+    return out
+
+
+def prefill_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table: torch.Tensor,
+                      cu_q: torch.Tensor, kv_lens: torch.Tensor, tile_req: torch.Tensor, tile_tok0: torch.Tensor,
+                      num_heads: int, num_kv_heads: int, head_dim: int, scale: float | None = None,
+                      out: torch.Tensor | None = None, causal: bool = True) -> torch.Tensor:
+    """Causal prefill over the paged cache. q: [T, Hq * D] rows (any row stride)."""
+    scale = scale if scale is not None else 1.0 / math.sqrt(head_dim)
+    q3 = q.view(q.shape[0], -1) if q.dim() == 2 else q
+    if out is None:
+        out = torch.empty(q.shape[0], num_heads * head_dim, dtype=q.dtype, device=q.device)
+    if not q.is_cuda:
+        ref = paged_attention_ref(q3.reshape(q.shape[0], -1)[:, : num_heads * head_dim].view(-1, num_heads, head_dim),
+                                  k_cache, v_cache, block_table, cu_q, kv_lens, scale, causal)
+        out.copy_(ref.reshape(out.shape))
+        return out
+    ext().attention_prefill(q3, k_cache, v_cache, out, block_table, cu_q, kv_lens, None, tile_req, tile_tok0,
+                            num_heads, num_kv_heads, head_dim, scale, causal)
+    return out
+
+
+def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens: torch.Tensor,
+                     num_heads: int, num_kv_heads: int, head_dim: int, scale: float | None = None,
+                     causal: bool = False, out: torch.Tensor | None = None, q_lens: list[int] | None = None,
+                     tiles: tuple[torch.Tensor, torch.Tensor] | None = None) -> torch.Tensor:
+    """Ragged (block-diagonal) attention over contiguous q/k/v rows (encoders)."""
+    scale = scale if scale is not None else 1.0 / math.sqrt(head_dim)
+    T = q.shape[0]
+    if out is None:
+        out = torch.empty(T, num_heads * head_dim, dtype=q.dtype, device=q.device)
+    if not q.is_cuda:
+        ref = varlen_attention_ref(q.reshape(T, num_heads, head_dim), k.reshape(T, num_kv_heads, head_dim),
+                                   v.reshape(T, num_kv_heads, head_dim), cu_seqlens, scale, causal)
+        out.copy_(ref.reshape(out.shape))
+        return out
+    if tiles is None:
+        if q_lens is None:
+            cu = cu_seqlens.tolist()
+            q_lens = [cu[i + 1] - cu[i] for i in range(len(cu) - 1)]
+        req, tok0 = prefill_tiles(q_lens, num_heads // num_kv_heads)
+        tiles = (torch.tensor(req, dtype=torch.int32, device=q.device),
+                 torch.tensor(tok0, dtype=torch.int32, device=q.device))
+    lens = cu_seqlens[1:] - cu_seqlens[:-1]
+    ext().attention_prefill(q, k, v, out, None, cu_seqlens, lens.to(torch.int32), cu_seqlens, tiles[0], tiles[1],
+                            num_heads, num_kv_heads, head_dim, scale, causal)
+    return out
+
+
+class DecodeWorkspace:
+    """Split-KV scratch of the decode kernel, sized for a max batch / context."""
+
+    def __init__(self, max_batch: int, num_heads: int, head_dim: int, max_context: int, device,
+                 keys_per_split: int = 256):
+        self.keys_per_split = keys_per_split
+        self.max_splits = max(1, (max_context + keys_per_split - 1) // keys_per_split)
+        self.part_o = torch.empty(max_batch * num_heads * self.max_splits * head_dim, dtype=torch.float32,
+                                  device=device)
+        self.part_lse = torch.empty(max_batch * num_heads * self.max_splits, dtype=torch.float32, device=device)
+
+
+def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table: torch.Tensor,
+                     kv_lens: torch.Tensor, num_heads: int, num_kv_heads: int, head_dim: int,
+                     workspace: DecodeWorkspace | None = None, scale: float | None = None,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+    """One query token per request. q: [B, >= Hq * D] rows."""
+    scale = scale if scale is not None else 1.0 / math.sqrt(head_dim)
+    B = kv_lens.shape[0]
+    if out is None:
+        out = torch.empty(B, num_heads * head_dim, dtype=q.dtype, device=q.device)
+    if not q.is_cuda:
+        cu = torch.arange(B + 1, dtype=torch.int32)
+        ref = paged_attention_ref(q.reshape(B, -1)[:, : num_heads * head_dim].view(B, num_heads, head_dim),
+                                  k_cache, v_cache, block_table, cu, kv_lens, scale, True)
+        out.copy_(ref.reshape(out.shape))
+        return out
+    if workspace is None:
+        max_ctx = int(kv_lens.max().item())
+        workspace = DecodeWorkspace(B, num_heads, head_dim, max_ctx, q.device)
+    ext().attention_decode(q, k_cache, v_cache, out, block_table, kv_lens, num_heads, num_kv_heads, head_dim, scale,
+                           workspace.keys_per_split, workspace.max_splits, workspace.part_o, workspace.part_lse)
+    return out

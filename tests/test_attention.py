@@ -1,0 +1,92 @@
+"""Paged prefill / decode and varlen attention kernels vs an fp32 oracle."""
+import math
+
+import pytest
+import torch
+
+from sglang_omni_b200.ops import attention as A
+
+
+def _make_cache(kv_lens, hkv, d, device, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    pages_needed = [(n + 63) // 64 for n in kv_lens]
+    total = sum(pages_needed) + 3
+    perm = torch.randperm(total, generator=g).tolist()
+    k = (torch.randn(total, hkv, 64, d, generator=g) * 0.5).bfloat16()
+    v = torch.randn(total, hkv, 64, d, generator=g).bfloat16()
+    maxp = max(pages_needed)
+    bt = torch.zeros(len(kv_lens), maxp, dtype=torch.int32)
+    i = 0
+    for b, n in enumerate(pages_needed):
+        bt[b, :n] = torch.tensor(perm[i:i + n])
+        i += n
+    return k.to(device), v.to(device), bt.to(device)
+
+
+def test_prefill_tiles():
+    req, tok0 = A.prefill_tiles([10, 0, 17], 8)
+    assert req == [0, 0, 1 + 1, 2, 2] or req == [0, 0, 2, 2, 2]
+    assert len(req) == len(tok0)
+
+
+def test_paged_ref_matches_dense_sdpa():
+    torch.manual_seed(0)
+    kv_lens = [70]
+    k, v, bt = _make_cache(kv_lens, 2, 16, "cpu")
+    q = torch.randn(5, 4, 16)
+    cu = torch.tensor([0, 5], dtype=torch.int32)
+    out = A.paged_attention_ref(q, k, v, bt, cu, torch.tensor(kv_lens), 0.25, True)
+    kk = A.gather_kv_ref(k, bt[0], 70).float().repeat_interleave(2, 1)
+    vv = A.gather_kv_ref(v, bt[0], 70).float().repeat_interleave(2, 1)
+    qq = q.permute(1, 0, 2)[None]
+    mask = torch.ones(5, 70, dtype=torch.bool).tril(65)
+    ref = torch.nn.functional.scaled_dot_product_attention(qq, kk.permute(1, 0, 2)[None], vv.permute(1, 0, 2)[None],
+                                                           attn_mask=mask, scale=0.25)
+    torch.testing.assert_close(out, ref[0].permute(1, 0, 2), atol=1e-4, rtol=1e-4)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("hq,hkv", [(32, 4), (16, 2), (32, 8), (16, 8)])
+@pytest.mark.parametrize("q_lens,kv_extra", [([1, 7, 64, 130], [0, 5, 0, 100]), ([300], [0]), ([9, 1], [200, 1000])])
+def test_prefill_paged(hq, hkv, q_lens, kv_extra):
+    d = 128
+    kv_lens = [q + e for q, e in zip(q_lens, kv_extra)]
+    k, v, bt = _make_cache(kv_lens, hkv, d, "cuda")
+    T = sum(q_lens)
+    q = (torch.randn(T, hq * d, device="cuda") * 0.5).bfloat16()
+    cu = torch.tensor([0] + list(torch.tensor(q_lens).cumsum(0).tolist()), dtype=torch.int32, device="cuda")
+    kl = torch.tensor(kv_lens, dtype=torch.int32, device="cuda")
+    req, tok0 = A.prefill_tiles(q_lens, hq // hkv)
+    tr = torch.tensor(req, dtype=torch.int32, device="cuda")
+    tt = torch.tensor(tok0, dtype=torch.int32, device="cuda")
+    out = A.prefill_attention(q, k, v, bt, cu, kl, tr, tt, hq, hkv, d)
+    ref = A.paged_attention_ref(q.view(T, hq, d), k, v, bt, cu, kl, 1 / math.sqrt(d), True)
+    torch.testing.assert_close(out.float().view(T, hq, d), ref, atol=2e-2, rtol=2e-2)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("hq,hkv,d", [(32, 4, 128), (16, 2, 128), (32, 8, 128), (16, 8, 128), (8, 8, 64)])
+@pytest.mark.parametrize("kv_lens", [[1, 63, 64, 65, 1000], [3000, 17]])
+def test_decode_paged(hq, hkv, d, kv_lens):
+    k, v, bt = _make_cache(kv_lens, hkv, d, "cuda", seed=3)
+    B = len(kv_lens)
+    q = torch.randn(B, hq * d, device="cuda").bfloat16()
+    kl = torch.tensor(kv_lens, dtype=torch.int32, device="cuda")
+    ws = A.DecodeWorkspace(B, hq, d, max(kv_lens), "cuda", keys_per_split=256)
+    out = A.decode_attention(q, k, v, bt, kl, hq, hkv, d, ws)
+    cu = torch.arange(B + 1, dtype=torch.int32, device="cuda")
+    ref = A.paged_attention_ref(q.view(B, hq, d), k, v, bt, cu, kl, 1 / math.sqrt(d), True)
+    torch.testing.assert_close(out.float().view(B, hq, d), ref, atol=2e-2, rtol=2e-2)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("h,d", [(20, 64), (16, 80), (16, 128)])
+def test_varlen_noncausal(h, d):
+    lens = [5, 100, 33, 200]
+    T = sum(lens)
+    cu = torch.tensor([0] + torch.tensor(lens).cumsum(0).tolist(), dtype=torch.int32, device="cuda")
+    qkv = (torch.randn(T, 3, h, d, device="cuda") * 0.5).bfloat16()
+    q, k, v = qkv[:, 0].reshape(T, h * d), qkv[:, 1].reshape(T, h * d), qkv[:, 2].reshape(T, h * d)
+    out = A.varlen_attention(q.contiguous(), k.contiguous(), v.contiguous(), cu, h, h, d)
+    ref = A.varlen_attention_ref(qkv[:, 0], qkv[:, 1], qkv[:, 2], cu, 1 / math.sqrt(d), False)
+    torch.testing.assert_close(out.float().view(T, h, d), ref, atol=2e-2, rtol=2e-2)
