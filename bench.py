@@ -1,0 +1,230 @@
+"""Headline benchmark: Qwen3-Omni-30B-A3B thinker serving, text in / text out.
+
+Workload (per GPU): 64 concurrent requests, 1024 random prompt ids each, 256
+greedy output tokens (EOS ignored), bf16, random-init weights of the full
+48-layer / 128-expert architecture.  One "step" is one complete serving
+round of that workload through the paged engine (chunked prefill of 64K
+tokens, then 256 CUDA-graph decode steps at batch 64).
+
+Multi-GPU (torchrun, one process per GPU): every rank serves its own 64
+requests with a full replica (data parallel, weak scaling); the reported value
+is the whole-job output tok/s = sum of tokens / max over ranks of the
+device-timed duration.
+
+``--impl reference`` runs the unmodified reference from baseline/_ref through
+its own public API, or prints an ``unavailable`` line when it cannot run.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--requests", type=int, default=64)
+    ap.add_argument("--prompt-len", type=int, default=1024)
+    ap.add_argument("--output-len", type=int, default=256)
+    ap.add_argument("--layers", type=int, default=48, help="only for quick local checks; the headline uses 48")
+    ap.add_argument("--max-prefill-tokens", type=int, default=8192)
+    return ap.parse_args()
+
+
+class ClockSampler:
+    """Samples nvidia-smi SM clocks and throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+                parts = [p.strip() for p in out.stdout.strip().split(",")]
+                if len(parts) >= 9:
+                    self.samples.append(parts)
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons}
+
+
+def reference_arm(args):
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    why = None
+    if not os.path.isdir(os.path.join(ref, "sglang_omni")):
+        why = "reference not installed under baseline/_ref"
+    else:
+        try:
+            import importlib.util
+            if importlib.util.find_spec("sglang") is None:
+                why = ("the reference serves the thinker through sglang==0.5.8 (ModelRunner, sgl_kernel, flashinfer), "
+                       "which is not in this image or its offline wheelhouse; the sglang_omni package itself "
+                       "installed with --no-deps")
+        except Exception as exc:  # pragma: no cover
+            why = f"probe failed: {exc}"
+    if why is not None:
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps({"impl": "reference", "unavailable": why}))
+        return
+    raise SystemExit("reference arm: sglang present but the runner is not wired")  # pragma: no cover
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+    sys.path.insert(0, ROOT)
+    import torch
+    import torch.distributed as dist
+
+    from sglang_omni_b200.engines.ar import AREngine, ARRequest, KVPool
+    from sglang_omni_b200.models.decoder import DecoderLM
+    from sglang_omni_b200.models.qwen3_omni.hf_config import thinker_text_config
+    from sglang_omni_b200.ops import _ext
+    from sglang_omni_b200.sampling_params import SamplingParams
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=600))
+    _ext.ext()  # fail loudly without the kernels
+
+    cfg = thinker_text_config(num_layers=args.layers)
+    model = DecoderLM(cfg, device=dev).random_init_(seed=0)
+    max_ctx = ((args.prompt_len + args.output_len + 63) // 64) * 64
+    pages_needed = args.requests * (max_ctx // 64) + 64
+    pool = KVPool(cfg.num_layers, cfg.num_kv_heads, cfg.head_dim, pages_needed + 1, dev)
+    eng = AREngine(model, pool, max_batch=args.requests, max_prefill_tokens=args.max_prefill_tokens,
+                   max_context=max_ctx, use_graphs=True, overlap=True)
+    g = torch.Generator().manual_seed(1234 + rank)
+    prompts = torch.randint(0, cfg.vocab_size, (args.requests, args.prompt_len), generator=g, dtype=torch.int32)
+    prompts_pinned = prompts.pin_memory()
+    sp = SamplingParams(temperature=0.0, ignore_eos=True)
+
+    def round_(tag):
+        host = prompts_pinned.tolist()
+        reqs = [ARRequest(rid=f"{tag}-{rank}-{i}", prompt_ids=host[i], sampling=sp, max_new_tokens=args.output_len)
+                for i in range(args.requests)]
+        eng.generate(reqs)
+        return reqs
+
+    for w in range(args.warmup):
+        round_(f"w{w}")
+    torch.cuda.synchronize()
+    _ext.check_status(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    with ClockSampler(local) as clk:
+        start.record()
+        out_tokens = 0
+        ttfts = []
+        for s in range(args.steps):
+            reqs = round_(f"s{s}")
+            out_tokens += sum(len(r.output_ids) for r in reqs)
+            ttfts += [r.first_token_time - r.arrival for r in reqs]
+        end.record()
+        torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    _ext.check_status(dev)
+    ms = start.elapsed_time(end)
+    t = torch.tensor([ms, float(out_tokens), wall], dtype=torch.float64, device=dev)
+    if world > 1:
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = t.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        ms_max, tokens_total, wall_max = float(mx[0]), float(sm[1]), float(mx[2])
+    else:
+        ms_max, tokens_total, wall_max = ms, float(out_tokens), wall
+    value = tokens_total / (ms_max / 1e3)
+    e2e = tokens_total / wall_max
+    if rank == 0:
+        line = {
+            "metric": "output tok/s + p50 time-to-first-audio-chunk, Qwen3-Omni-30B-A3B, 1/2/4/8 B200",
+            "value": round(value, 2),
+            "unit": "output tokens/s (whole job)",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_max / args.steps, 3),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic: uniform random prompt ids, random-init N(0,0.02) weights of the full architecture",
+            "config": {
+                "model": f"Qwen3-Omni-30B-A3B thinker ({cfg.num_layers} layers, 128 experts top-8, hidden 2048)",
+                "global_batch": args.requests * world,
+                "seq_len": args.prompt_len,
+                "output_len": args.output_len,
+                "parallelism": f"dp{world}" if world > 1 else "tp1",
+                "step": "one serving round: 64 requests x (1024 prompt -> 256 greedy tokens) per GPU",
+                "l2": "inputs larger than L2 (61 GB of weights streamed per decode step)",
+                "ttft_p50_ms": round(1e3 * statistics.median(ttfts), 2),
+                "ttfa_p50_ms": None,
+            },
+            "e2e": {"value": round(e2e, 2), "unit": "output tokens/s, host wall clock through AREngine.generate",
+                    "h2d_bytes_per_step": int(args.requests * args.prompt_len * 4),
+                    "d2h_bytes_per_step": int(args.requests * args.output_len * 4)},
+            "gpu_launches": None,
+            "clocks": clk.summary(),
+            "impl": "ours",
+        }
+        print(json.dumps(line))
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -335,7 +335,8 @@ void sample(torch::Tensor& logits, torch::Tensor& out_tokens, const c10::optiona
             const c10::optional<torch::Tensor>& min_p, const c10::optional<torch::Tensor>& rep_penalty,
             const c10::optional<torch::Tensor>& seen, int64_t suppress_lo, int64_t suppress_hi,
             int64_t suppress_keep, const c10::optional<torch::Tensor>& seeds,
-            const c10::optional<torch::Tensor>& step) {
+            const c10::optional<torch::Tensor>& step, const c10::optional<torch::Tensor>& row_slot,
+            const c10::optional<torch::Tensor>& slot_tokens) {
   OMNI_CHECK_CUDA(logits);
   TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.stride(-1) == 1, "logits fp32");
   const at::cuda::CUDAGuard guard(logits.device());
@@ -358,8 +359,10 @@ void sample(torch::Tensor& logits, torch::Tensor& out_tokens, const c10::optiona
   a.suppress_hi = static_cast<int>(suppress_hi);
   a.suppress_keep = static_cast<int>(suppress_keep);
   a.seeds = seeds.has_value() ? seeds->data_ptr<int64_t>() : nullptr;
-  a.step = opt_ptr<int>(step);
+  a.step = opt_mut<int>(step);
   a.out_tokens = out_tokens.data_ptr<int>();
+  a.row_slot = opt_ptr<int>(row_slot);
+  a.slot_tokens = opt_mut<int>(slot_tokens);
   check_launch(omni::sample(a, at::cuda::getCurrentCUDAStream()), "sample");
 }
 

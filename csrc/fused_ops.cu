@@ -429,11 +429,12 @@ __global__ void __launch_bounds__(1024) sample_kernel(SampleArgs a) {
   __shared__ int s_kleft;
   __shared__ unsigned long long s_best;
   const int row = blockIdx.x;
+  const int sr = a.row_slot ? a.row_slot[row] : row;  // state row
   float* lg = a.logits + static_cast<int64_t>(row) * a.logits_stride;
   const int V = a.vocab;
-  const float temp = a.temperature ? a.temperature[row] : 0.f;
-  const float rep = a.rep_penalty ? a.rep_penalty[row] : 1.f;
-  const uint8_t* seen = a.seen ? a.seen + static_cast<int64_t>(row) * a.seen_stride : nullptr;
+  const float temp = a.temperature ? a.temperature[sr] : 0.f;
+  const float rep = a.rep_penalty ? a.rep_penalty[sr] : 1.f;
+  const uint8_t* seen = a.seen ? a.seen + static_cast<int64_t>(sr) * a.seen_stride : nullptr;
 
   // 1) logits processing in place: suppression ranges, repetition penalty, temperature
   for (int i = threadIdx.x; i < V; i += blockDim.x) {
@@ -458,7 +459,9 @@ __global__ void __launch_bounds__(1024) sample_kernel(SampleArgs a) {
     if (threadIdx.x == 0) {
       const int tok = static_cast<int>(0xffffffffu - static_cast<uint32_t>(s_best & 0xffffffffull));
       a.out_tokens[row] = tok;
-      if (a.seen) a.seen[static_cast<int64_t>(row) * a.seen_stride + tok] = 1;
+      if (a.slot_tokens) a.slot_tokens[sr] = tok;
+      if (a.step) a.step[sr] += 1;
+      if (a.seen) a.seen[static_cast<int64_t>(sr) * a.seen_stride + tok] = 1;
     }
     return;
   }
@@ -467,7 +470,7 @@ __global__ void __launch_bounds__(1024) sample_kernel(SampleArgs a) {
   m = block_reduce(m, sred, MaxOp(), -INFINITY);
   // 2) top-k threshold by 4-pass radix select on order-preserving keys
   float thr = -INFINITY;
-  const int topk = a.top_k ? a.top_k[row] : 0;
+  const int topk = a.top_k ? a.top_k[sr] : 0;
   if (topk > 0 && topk < V) {
     if (threadIdx.x == 0) {
       s_prefix = 0u;
@@ -500,10 +503,10 @@ __global__ void __launch_bounds__(1024) sample_kernel(SampleArgs a) {
     thr = key2f(s_prefix);
   }
   // 3) min-p threshold
-  const float minp = a.min_p ? a.min_p[row] : 0.f;
+  const float minp = a.min_p ? a.min_p[sr] : 0.f;
   if (minp > 0.f) thr = fmaxf(thr, m + logf(minp));
   // 4) top-p threshold: largest v with sum_{x >= v} e^(x-m) >= p * Z (binary search)
-  const float topp = a.top_p ? a.top_p[row] : 1.f;
+  const float topp = a.top_p ? a.top_p[sr] : 1.f;
   if (topp < 1.f) {
     float z = 0.f;
     for (int i = threadIdx.x; i < V; i += blockDim.x) {
@@ -525,8 +528,8 @@ __global__ void __launch_bounds__(1024) sample_kernel(SampleArgs a) {
     thr = fmaxf(thr, lo);
   }
   // 5) Gumbel-max over the kept set
-  const uint64_t seed = a.seeds ? static_cast<uint64_t>(a.seeds[row]) : 0x1234ull;
-  const uint64_t step = a.step ? static_cast<uint64_t>(a.step[row]) : 0ull;
+  const uint64_t seed = a.seeds ? static_cast<uint64_t>(a.seeds[sr]) : 0x1234ull;
+  const uint64_t step = a.step ? static_cast<uint64_t>(a.step[sr]) : 0ull;
   unsigned long long best = 0ull;
   for (int i = threadIdx.x; i < V; i += blockDim.x) {
     const float x = lg[i];
@@ -545,7 +548,9 @@ __global__ void __launch_bounds__(1024) sample_kernel(SampleArgs a) {
     int tok = static_cast<int>(0xffffffffu - static_cast<uint32_t>(s_best & 0xffffffffull));
     if (s_best == 0ull) tok = 0;
     a.out_tokens[row] = tok;
-    if (a.seen) a.seen[static_cast<int64_t>(row) * a.seen_stride + tok] = 1;
+    if (a.slot_tokens) a.slot_tokens[sr] = tok;
+    if (a.step) a.step[sr] += 1;
+    if (a.seen) a.seen[static_cast<int64_t>(sr) * a.seen_stride + tok] = 1;
   }
 }
 

@@ -171,8 +171,12 @@ struct SampleArgs {
   int64_t seen_stride;
   int suppress_lo, suppress_hi, suppress_keep;  // [lo, hi) masked except keep; lo < 0 disables
   const int64_t* seeds;      // [rows]
-  const int* step;           // [rows] decode step (RNG counter)
+  int* step;                 // [rows] decode step (RNG counter), incremented after the draw
   int* out_tokens;           // [rows]
+  const int* row_slot;       // optional [rows]: per-row state lives at index row_slot[row]
+                             // of temperature / top_k / top_p / min_p / rep_penalty / seen /
+                             // seeds / step, and the token is also written to slot_tokens[slot]
+  int* slot_tokens;
 };
 cudaError_t sample(const SampleArgs& a, cudaStream_t stream);
 

@@ -16,7 +16,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0a")
 os.environ.setdefault("MAX_JOBS", str(max(1, min(16, os.cpu_count() or 4))))
 
-from torch.utils.cpp_extension import BuildExtension, CppExtension, CUDAExtension  # noqa: E402
+from torch.utils.cpp_extension import BuildExtension, CUDAExtension  # noqa: E402
 
 CUDA_FLAGS = [
     "-gencode=arch=compute_100a,code=sm_100a",
@@ -42,12 +42,17 @@ ext_modules = [
     ),
 ]
 if runtime_sources:
+    # plain pybind11 module: no torch / CUDA linkage, importable on CPU-only hosts
+    from pybind11.setup_helpers import Pybind11Extension
+
     ext_modules.append(
-        CppExtension(
-            name="sglang_omni_b200._runtime",
+        Pybind11Extension(
+            "sglang_omni_b200._runtime",
             sources=runtime_sources,
             include_dirs=[os.path.join(ROOT, "csrc", "runtime")],
-            extra_compile_args=["-O3", "-std=c++17"],
+            extra_compile_args=["-O3"],
+            cxx_std=17,
+            extra_link_args=["-lrt"],
         )
     )
 

@@ -79,12 +79,35 @@ def sample_ref(logits, st: SamplingTensors, suppress=(-1, -1, -1), generator=Non
     return out
 
 
+def _gather_state(st: SamplingTensors, idx: torch.Tensor) -> SamplingTensors:
+    g = lambda t: None if t is None else t[idx]  # noqa: E731
+    return SamplingTensors(g(st.temperature), g(st.top_k), g(st.top_p), g(st.min_p), g(st.rep_penalty), g(st.seen),
+                           g(st.seeds), g(st.step))
+
+
 def sample(logits: torch.Tensor, st: SamplingTensors | None = None, suppress=(-1, -1, -1),
-           out: torch.Tensor | None = None) -> torch.Tensor:
-    """Returns int32 token ids [rows]. Modifies `logits` in place on the GPU path."""
+           out: torch.Tensor | None = None, row_slot: torch.Tensor | None = None,
+           slot_tokens: torch.Tensor | None = None) -> torch.Tensor:
+    """Returns int32 token ids [rows]. Modifies `logits` in place on the GPU path.
+
+    With ``row_slot`` the per-request state arrays of ``st`` are indexed by
+    slot (row r uses state row_slot[r]); the drawn token is also stored at
+    ``slot_tokens[row_slot[r]]`` and the slot's step counter advances.
+    """
     st = st or SamplingTensors()
     if not logits.is_cuda:
-        r = sample_ref(logits, st, suppress)
+        if row_slot is not None:
+            idx = row_slot.long()
+            sub = _gather_state(st, idx)
+            r = sample_ref(logits, sub, suppress)
+            if st.seen is not None:
+                st.seen[idx] = sub.seen
+            if st.step is not None:
+                st.step[idx] += 1
+            if slot_tokens is not None:
+                slot_tokens[idx] = r
+        else:
+            r = sample_ref(logits, st, suppress)
         if out is not None:
             out.copy_(r)
             return out
@@ -93,5 +116,5 @@ def sample(logits: torch.Tensor, st: SamplingTensors | None = None, suppress=(-1
         out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
     lo, hi, keep = suppress
     ext().sample(logits, out, st.temperature, st.top_k, st.top_p, st.min_p, st.rep_penalty, st.seen, lo, hi, keep,
-                 st.seeds, st.step)
+                 st.seeds, st.step, row_slot, slot_tokens)
     return out
