@@ -612,3 +612,85 @@ cudaError_t attention_decode(const AttnDecodeArgs& a, cudaStream_t stream) {
 }
 
 }  // namespace omni
+
+// ===========================================================================
+// Allocation-free decode attention (C ABI).  See omni_noalloc.h.
+// ===========================================================================
+#include <cstdio>
+#include <mutex>
+
+#include "omni_noalloc.h"
+
+namespace {
+
+// Split-KV scratch of the allocation-free entry point: partial outputs
+// followed by partial log-sum-exps.  It lives in the module's static device
+// memory, so every GPU that loads this library holds these 16.25 MiB until the
+// process exits.  In host code `g_noalloc_decode_scratch` names a host-side
+// stand-in, not the device array: its device address comes from
+// cudaGetSymbolAddress below.
+constexpr long long kNoAllocPartFloats = OMNI_NOALLOC_DECODE_PART_FLOATS;
+constexpr long long kNoAllocLseFloats = OMNI_NOALLOC_DECODE_LSE_FLOATS;
+static __device__ __align__(256) float g_noalloc_decode_scratch[kNoAllocPartFloats + kNoAllocLseFloats];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::once_flag g_noalloc_once[kNoAllocMaxDevices];
+float* g_noalloc_ptr[kNoAllocMaxDevices];
+cudaError_t g_noalloc_err[kNoAllocMaxDevices];
+
+// Device address of the scratch array on the current device, resolved once per
+// device with that device current.
+cudaError_t noalloc_scratch(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return cudaErrorInvalidDevice;
+  std::call_once(g_noalloc_once[dev], [dev] {
+    void* p = nullptr;
+    g_noalloc_err[dev] = cudaGetSymbolAddress(&p, g_noalloc_decode_scratch);
+    g_noalloc_ptr[dev] = g_noalloc_err[dev] == cudaSuccess ? static_cast<float*>(p) : nullptr;
+  });
+  if (g_noalloc_err[dev] != cudaSuccess) return g_noalloc_err[dev];
+  *out = g_noalloc_ptr[dev];
+  return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) int omni_attention_decode_noalloc(
+    const void* q, long long q_stride, const void* k_cache, const void* v_cache, const int* block_table,
+    int bt_stride, const int* kv_lens, int batch, int num_heads, int num_kv_heads, int head_dim, float scale,
+    int keys_per_split, int max_splits, void* out, long long out_stride, void* stream) {
+  const long long slots = static_cast<long long>(batch) * num_heads * max_splits;
+  if (batch < 0 || max_splits < 1 || slots * head_dim > kNoAllocPartFloats || slots > kNoAllocLseFloats) {
+    std::fprintf(stderr,
+                 "omni_attention_decode_noalloc: batch %d x heads %d x splits %d x head_dim %d needs %lld partial "
+                 "floats and %lld LSE floats; the static scratch holds %lld and %lld\n",
+                 batch, num_heads, max_splits, head_dim, slots * head_dim, slots, kNoAllocPartFloats,
+                 kNoAllocLseFloats);
+    return OMNI_NOALLOC_ERR_TOO_LARGE;
+  }
+  float* scratch = nullptr;
+  cudaError_t e = noalloc_scratch(&scratch);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  omni::AttnDecodeArgs a{};
+  a.q = q;
+  a.q_stride = q_stride;
+  a.k = k_cache;
+  a.v = v_cache;
+  a.block_table = block_table;
+  a.bt_stride = bt_stride;
+  a.kv_lens = kv_lens;
+  a.batch = batch;
+  a.hq = num_heads;
+  a.hkv = num_kv_heads;
+  a.head_dim = head_dim;
+  a.scale = scale;
+  a.keys_per_split = keys_per_split;
+  a.max_splits = max_splits;
+  a.out = out;
+  a.out_stride = out_stride;
+  a.part_o = scratch;
+  a.part_lse = scratch + kNoAllocPartFloats;
+  return static_cast<int>(omni::attention_decode(a, static_cast<cudaStream_t>(stream)));
+}
