@@ -27,7 +27,8 @@ int* status_ptr(const c10::optional<torch::Tensor>& status) {
 void gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& out, const c10::optional<torch::Tensor>& offsets,
           int64_t m_out, bool gated, const c10::optional<torch::Tensor>& bias,
           const c10::optional<torch::Tensor>& residual, int64_t act, int64_t expected_rows,
-          const c10::optional<torch::Tensor>& status, int64_t max_ctas) {
+          const c10::optional<torch::Tensor>& status, int64_t max_ctas,
+          const c10::optional<torch::Tensor>& splitk_ws, const c10::optional<torch::Tensor>& splitk_counters) {
   OMNI_CHECK_CUDA(a);
   OMNI_CHECK_CUDA(b);
   OMNI_CHECK_CUDA(out);
@@ -88,6 +89,14 @@ void gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& out, co
   args.act = static_cast<int>(act);
   args.status = status_ptr(status);
   args.max_ctas = static_cast<int>(max_ctas);
+  if (splitk_ws.has_value() && splitk_counters.has_value()) {
+    TORCH_CHECK(splitk_ws->scalar_type() == at::kFloat && splitk_counters->scalar_type() == at::kInt,
+                "split-K scratch must be fp32 / int32");
+    args.splitk_ws = splitk_ws->data_ptr<float>();
+    args.splitk_ws_floats = splitk_ws->numel();
+    args.splitk_counters = splitk_counters->data_ptr<int>();
+    args.splitk_counter_slots = static_cast<int>(splitk_counters->numel());
+  }
   check_launch(omni::gemm_bf16(args, at::cuda::getCurrentCUDAStream()), "gemm_bf16");
 }
 
@@ -372,7 +381,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels of sglang_omni_b200";
   m.def("gemm", &gemm, "tcgen05 GEMM (dense / grouped / gated)", py::arg("a"), py::arg("b"), py::arg("out"),
         py::arg("offsets"), py::arg("m_out"), py::arg("gated"), py::arg("bias"), py::arg("residual"), py::arg("act"),
-        py::arg("expected_rows"), py::arg("status"), py::arg("max_ctas") = 0);
+        py::arg("expected_rows"), py::arg("status"), py::arg("max_ctas") = 0, py::arg("splitk_ws") = py::none(),
+        py::arg("splitk_counters") = py::none());
   m.def("rmsnorm", &rmsnorm, "RMSNorm (+ fused residual add)");
   m.def("layernorm", &layernorm, "LayerNorm");
   m.def("attention_prefill", &attention_prefill, "paged / varlen GQA prefill attention");

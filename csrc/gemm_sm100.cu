@@ -48,6 +48,9 @@ struct DevParams {
   int out_f32;
   int act;
   int* status;
+  int k_splits;          // > 1: split-K over K blocks with an fp32 workspace
+  float* ws;             // [rows, m_out] fp32, zero between calls (self-cleaning)
+  int* counters;         // [tiles] arrival counters, zero between calls
 };
 
 template <int BN, bool GATED>
@@ -166,6 +169,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
   const int total_tiles = *total_tiles_s;
   const int num_kb = (p.k + kBK - 1) / kBK;
+  const int ks = p.k_splits > 1 ? p.k_splits : 1;
+  const int kb_per = (num_kb + ks - 1) / ks;
+  const int total_work = total_tiles * ks;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -174,12 +180,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       long issued = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+      for (int w = blockIdx.x; w < total_work && ok; w += gridDim.x) {
+        const int t = w / ks, split = w - t * ks;
         int g, mt, nt;
         decode_tile<BN>(t, prefix_s, offs_s, groups, g, mt, nt);
         const int a_row = g * p.a_rows + mt * kBM;
         const int b_row = offs_s[g] + nt * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        const int kb0 = split * kb_per, kb1 = min(num_kb, kb0 + kb_per);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, p.status)) { ok = false; break; }
           uint8_t* sa = smem + stage * C::kStageBytes;
           uint8_t* sb = sa + C::kABytes * (GATED ? 2 : 1);
@@ -206,13 +214,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t phase = 0;
     int local = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++local) {
+    for (int w = blockIdx.x; w < total_work && ok; w += gridDim.x, ++local) {
+      const int split = w % ks;
+      const int kb0 = split * kb_per, kb1 = min(num_kb, kb0 + kb_per);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, abort_flag, p.status)) { ok = false; break; }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + acc * C::kAccCols;
-      for (int kb = 0; kb < num_kb; ++kb) {
+      for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.status)) { ok = false; break; }
         tc_fence_after();
         if (lane == 0) {
@@ -223,7 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
             // +32 bytes per 16-element K step inside the 128-byte swizzle atom (>>4 => +2).
-            const uint32_t accum = (kb > 0 || kk > 0) ? 1u : 0u;
+            const uint32_t accum = (kb > kb0 || kk > 0) ? 1u : 0u;
             umma_f16_ss(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, accum);
             if (GATED) {
               const uint64_t adesc_up = umma_desc_sw128(sa + C::kABytes);
@@ -249,7 +259,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int lane_base = 32 * (warp & 3);
     int local = 0;
-    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
+    for (int w = blockIdx.x; w < total_work; w += gridDim.x, ++local) {
+      const int t = w / ks;
       int g, mt, nt;
       decode_tile<BN>(t, prefix_s, offs_s, groups, g, mt, nt);
       const int acc = local & 1;
@@ -270,7 +281,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_32x32b_x16(t_base + c, r);
         if (GATED) tmem_ld_32x32b_x16(t_base + BN + c, u);
         tmem_ld_wait();
-        if (m_ok) {
+        if (ks > 1) {
+          // split-K partial: accumulate the raw (pre-epilogue) sums in fp32
+          if (m_ok) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int row = row0 + c + j;
+              if (row < row_end) {
+                atomicAdd(&p.ws[static_cast<int64_t>(row) * p.m_out + m], __uint_as_float(r[j]));
+              }
+            }
+          }
+        } else if (m_ok) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int row = row0 + c + j;
@@ -296,6 +318,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(&tempty_bar[acc]);
+      if (ks > 1) {
+        // The last split to arrive finalises the tile: epilogue from the fp32
+        // sums, then zeroes its workspace rows and counter for the next call.
+        __shared__ int s_last;
+        __threadfence();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (threadIdx.x == 64) s_last = (atomicAdd(&p.counters[t], 1) == ks - 1);
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (s_last) {
+          __threadfence();
+          if (m_ok) {
+            for (int row = row0; row < min(row_end, row0 + BN); ++row) {
+              float* wp = &p.ws[static_cast<int64_t>(row) * p.m_out + m];
+              float v = __ldcg(wp) + bias_v;
+              *wp = 0.f;
+              if (p.act == kActGeluTanh) v = gelu_tanh_f(v);
+              else if (p.act == kActGeluErf) v = gelu_erf_f(v);
+              else if (p.act == kActSilu) v = silu_f(v);
+              if (p.residual != nullptr) v += __bfloat162float(p.residual[static_cast<int64_t>(row) * p.ldr + m]);
+              if (p.out_f32) {
+                static_cast<float*>(p.out)[static_cast<int64_t>(row) * p.ldo + m] = v;
+              } else {
+                static_cast<__nv_bfloat16*>(p.out)[static_cast<int64_t>(row) * p.ldo + m] = __float2bfloat16(v);
+              }
+            }
+          }
+          if (threadIdx.x == 64) p.counters[t] = 0;
+        }
+      }
     }
   }
 
@@ -378,10 +429,32 @@ cudaError_t launch(const GemmArgs& a, cudaStream_t stream) {
   p.out_f32 = a.out_f32;
   p.act = a.act;
   p.status = a.status;
+  p.k_splits = 1;
+  p.ws = nullptr;
+  p.counters = nullptr;
   const int m_tiles = (a.m_out + kBM - 1) / kBM;
+  const int num_kb = (a.k + kBK - 1) / kBK;
+  // Split-K for dense GEMMs that would leave most SMs idle (decode projections).
+  if (!GATED && a.offsets == nullptr && a.splitk_ws != nullptr && a.splitk_counters != nullptr) {
+    const long tiles = static_cast<long>(m_tiles) * ((a.rows + BN - 1) / BN);
+    const int sms = num_sms();
+    if (tiles * 2 <= sms && num_kb >= 4 && static_cast<long>(a.rows) * a.m_out <= a.splitk_ws_floats &&
+        tiles <= a.splitk_counter_slots) {
+      int ksp = static_cast<int>((sms + tiles - 1) / tiles);
+      if (ksp > num_kb / 2) ksp = num_kb / 2;
+      if (ksp > 16) ksp = 16;
+      if (ksp > 1) {
+        const int per = (num_kb + ksp - 1) / ksp;
+        ksp = (num_kb + per - 1) / per;  // no empty splits
+        p.k_splits = ksp;
+        p.ws = a.splitk_ws;
+        p.counters = a.splitk_counters;
+      }
+    }
+  }
   // Upper bound of the tile count: every group may add one partial token tile.
   const long row_tiles = (a.offsets ? (static_cast<long>(a.rows) + BN - 1) / BN + a.groups : (a.rows + BN - 1) / BN);
-  const long bound = static_cast<long>(m_tiles) * (row_tiles > 0 ? row_tiles : 1);
+  const long bound = static_cast<long>(m_tiles) * (row_tiles > 0 ? row_tiles : 1) * p.k_splits;
   int grid = a.max_ctas > 0 ? a.max_ctas : num_sms();
   if (bound < grid) grid = static_cast<int>(bound);
   if (grid < 1) grid = 1;

@@ -1,0 +1,169 @@
+"""Pipeline configuration schema.
+
+Field names, defaults and validation follow the reference
+(sglang_omni/config/schema.py:11-222) so YAML written for it loads here:
+unique stage names, entry stage defined, aggregated sources and stream_to
+targets exist, fused groups adjacent and in order.  Additions: relay backends
+``inproc`` / ``cuda_ipc`` / ``auto`` (in-process when every stage shares the
+process, shm otherwise) and per-stage parallel layout in executor args.
+"""
+from __future__ import annotations
+
+from typing import Any, Literal
+
+from pydantic import BaseModel, ConfigDict, Field
+
+
+class ExecutorConfig(BaseModel):
+    model_config = ConfigDict(extra="forbid")
+    factory: str
+    args: dict[str, Any] = Field(default_factory=dict)
+
+
+class InputHandlerConfig(BaseModel):
+    model_config = ConfigDict(extra="forbid")
+    type: Literal["direct", "aggregated"] = "direct"
+    sources: list[str] | None = None
+    merge_fn: str | None = None
+
+
+class RelayConfig(BaseModel):
+    model_config = ConfigDict(extra="forbid")
+    slot_size_mb: int = 512
+    credits: int = 2
+    rank: int | None = None
+    world_size: int | None = None
+    device: str = "cpu"
+
+
+class StreamTargetConfig(BaseModel):
+    model_config = ConfigDict(extra="forbid")
+    to_stage: str
+    bootstrap: bool = True
+
+
+class StageConfig(BaseModel):
+    model_config = ConfigDict(extra="forbid")
+    name: str
+    executor: ExecutorConfig
+    get_next: str
+    input_handler: InputHandlerConfig = Field(default_factory=InputHandlerConfig)
+    relay: RelayConfig = Field(default_factory=RelayConfig)
+    num_workers: int = 1
+    stream_to: list[StreamTargetConfig] = Field(default_factory=list)
+
+
+class EndpointsConfig(BaseModel):
+    model_config = ConfigDict(extra="forbid")
+    scheme: Literal["ipc", "tcp"] = "ipc"
+    base_path: str = "/tmp/sglang_omni_b200"
+    base_port: int = 16000
+
+
+class PipelineConfig(BaseModel):
+    model_config = ConfigDict(extra="forbid")
+
+    model_path: str
+    entry_stage: str
+    stages: list[StageConfig]
+    name: str = "model"
+    terminal_stages: list[str] = Field(default_factory=list)
+    relay_backend: Literal["auto", "inproc", "shm", "nccl", "cuda_ipc", "nixl", "mooncake"] = "auto"
+    fused_stages: list[list[str]] = Field(default_factory=list)
+    endpoints: EndpointsConfig = Field(default_factory=EndpointsConfig)
+    gpu_placement: dict[str, int] = Field(default_factory=dict)
+    completion_endpoint: str | None = None
+    abort_endpoint: str | None = None
+    config_cls: str | None = None
+
+    def model_post_init(self, __context: Any = None) -> None:
+        self._validate_general()
+        self._validate_fusion()
+        if self.config_cls is None or self.config_cls == "PipelineConfig":
+            self.config_cls = self.__class__.__name__
+
+    @staticmethod
+    def from_dict(data: dict[str, Any]) -> "PipelineConfig":
+        return PipelineConfig(**data)
+
+    def stage(self, name: str) -> StageConfig:
+        for s in self.stages:
+            if s.name == name:
+                return s
+        raise KeyError(name)
+
+    def _validate_general(self) -> None:
+        if not self.model_path:
+            raise ValueError("model_path is required")
+        names = [s.name for s in self.stages]
+        if not names:
+            raise ValueError("pipeline must define at least one stage")
+        if len(names) != len(set(names)):
+            raise ValueError("stage names must be unique")
+        if self.entry_stage not in names:
+            raise ValueError(f"entry_stage {self.entry_stage!r} is not defined")
+        for s in self.stages:
+            if s.num_workers < 1:
+                raise ValueError(f"stage {s.name!r} needs at least one worker")
+            if not s.executor.factory:
+                raise ValueError(f"stage {s.name!r} missing executor factory")
+            if not s.get_next:
+                raise ValueError(f"stage {s.name!r} missing get_next")
+            if s.input_handler.type == "aggregated":
+                unknown = set(s.input_handler.sources or []) - set(names)
+                if unknown:
+                    raise ValueError(f"stage {s.name!r} has unknown sources: {sorted(unknown)}")
+            for st in s.stream_to:
+                if st.to_stage not in names:
+                    raise ValueError(f"stage {s.name!r} stream_to references unknown stage {st.to_stage!r}")
+        for t in self.terminal_stages:
+            if t not in names:
+                raise ValueError(f"terminal stage {t!r} is not defined")
+
+    def _validate_fusion(self) -> None:
+        if not self.fused_stages:
+            return
+        idx = {s.name: i for i, s in enumerate(self.stages)}
+        seen: set[str] = set()
+        for group in self.fused_stages:
+            if len(group) < 2:
+                raise ValueError("fused_stages groups need at least 2 stage names")
+            for n in group:
+                if n not in idx:
+                    raise ValueError(f"fused stage {n!r} is not defined")
+                if n in seen:
+                    raise ValueError(f"stage {n!r} appears in multiple fused groups")
+                seen.add(n)
+            ii = [idx[n] for n in group]
+            if ii != sorted(ii):
+                raise ValueError(f"fused group is out of order: {group}")
+            if ii != list(range(ii[0], ii[0] + len(ii))):
+                raise ValueError(f"stages in the fused group are not adjacent: {group}")
+
+    def apply_fusion(self) -> tuple[list[StageConfig], dict[str, str], str]:
+        """Collapses each fused group into one stage named after its last member."""
+        by_name = {s.name: s for s in self.stages}
+        name_map = {n: n for n in by_name}
+        group_by_last: dict[str, list[str]] = {}
+        for g in self.fused_stages or []:
+            group_by_last[g[-1]] = g
+            for n in g:
+                name_map[n] = g[-1]
+        out: list[StageConfig] = []
+        for s in self.stages:
+            if name_map[s.name] != s.name:
+                continue
+            if s.name in group_by_last:
+                g = group_by_last[s.name]
+                first = by_name[g[0]]
+                out.append(StageConfig(
+                    name=s.name,
+                    executor=ExecutorConfig(
+                        factory="sglang_omni_b200.config.compiler.build_fused_executor",
+                        args={"executors": [{"factory": by_name[n].executor.factory, "args": by_name[n].executor.args}
+                                            for n in g], "names": list(g)}),
+                    get_next=s.get_next, input_handler=first.input_handler, relay=first.relay,
+                    num_workers=first.num_workers, stream_to=first.stream_to))
+            else:
+                out.append(s)
+        return out, name_map, name_map[self.entry_stage]

@@ -1,0 +1,50 @@
+"""asyncio adapter of the threaded paged engine to the executor-side engine
+contract: ``await generate(rid, ARRequest, on_chunk, stream_fn)`` returns the
+finished request; ``on_chunk((token, info))`` fires per generated token on
+the event loop; ``abort(rid)``."""
+from __future__ import annotations
+
+import asyncio
+
+from .engine import AREngine, ThreadedAREngine
+from .request import ARRequest
+
+
+class PagedAREngineAdapter:
+    def __init__(self, engine: AREngine):
+        self.threaded = ThreadedAREngine(engine)
+        self._started = False
+
+    @property
+    def engine(self) -> AREngine:
+        return self.threaded.engine
+
+    def start(self):
+        if not self._started:
+            self.threaded.start()
+            self._started = True
+
+    def stop(self):
+        if self._started:
+            self.threaded.stop()
+            self._started = False
+
+    async def generate(self, rid: str, req: ARRequest, on_chunk=None, stream_fn=None) -> ARRequest:
+        self.start()
+        if self.threaded.error is not None:
+            raise RuntimeError(f"AR engine failed: {self.threaded.error}")
+        req.rid = rid
+        fut, q = self.threaded.submit(req, stream=on_chunk is not None)
+        if q is not None:
+            while True:
+                item = await q.get()
+                if item is None:
+                    break
+                on_chunk(item)
+        r = await fut
+        if r.finish_reason and r.finish_reason.startswith("error"):
+            raise RuntimeError(r.finish_reason)
+        return r
+
+    def abort(self, rid: str):
+        self.threaded.abort(rid)

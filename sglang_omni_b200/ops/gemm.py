@@ -15,6 +15,24 @@ import torch.nn.functional as F
 
 from ._ext import ext, status_word
 
+# Per-device split-K scratch of the dense GEMM (fp32 partial sums + per-tile
+# arrival counters).  The kernel leaves both zeroed after every call, so one
+# buffer serves every dense GEMM issued on the device's (single) compute
+# stream, including inside captured CUDA graphs.
+_SPLITK_FLOATS = 8 * 1024 * 1024
+_SPLITK_COUNTERS = 65536
+_splitk: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
+
+
+def splitk_scratch(device: torch.device):
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    sc = _splitk.get(idx)
+    if sc is None:
+        sc = (torch.zeros(_SPLITK_FLOATS, dtype=torch.float32, device=device),
+              torch.zeros(_SPLITK_COUNTERS, dtype=torch.int32, device=device))
+        _splitk[idx] = sc
+    return sc
+
 ACT_NONE, ACT_GELU_TANH, ACT_GELU_ERF, ACT_SILU = 0, 1, 2, 3
 _ACTS = {None: ACT_NONE, "none": ACT_NONE, "gelu_tanh": ACT_GELU_TANH, "gelu_pytorch_tanh": ACT_GELU_TANH,
          "gelu": ACT_GELU_ERF, "gelu_erf": ACT_GELU_ERF, "silu": ACT_SILU}
@@ -68,7 +86,8 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias=None, residual=None, act=None,
         out = torch.empty(*x.shape[:-1], n, dtype=out_dtype or torch.bfloat16, device=x.device)
     x2 = x if x.is_contiguous() else x.contiguous()
     rows = x2.numel() // x2.shape[-1]
-    ext().gemm(w, x2, out, None, n, gated, bias, residual, act_code(act), rows, status_word(x.device))
+    ws, ctr = splitk_scratch(x.device)
+    ext().gemm(w, x2, out, None, n, gated, bias, residual, act_code(act), rows, status_word(x.device), 0, ws, ctr)
     return out
 
 
