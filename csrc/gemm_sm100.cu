@@ -282,14 +282,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (GATED) tmem_ld_32x32b_x16(t_base + BN + c, u);
         tmem_ld_wait();
         if (ks > 1) {
-          // split-K partial: accumulate the raw (pre-epilogue) sums in fp32
+          // split-K partial: raw fp32 sums of this K range, reduced by splitk_reduce_kernel
           if (m_ok) {
+            float* wsp = p.ws + (static_cast<int64_t>(w % ks) * p.rows) * p.m_out + m;
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               const int row = row0 + c + j;
-              if (row < row_end) {
-                atomicAdd(&p.ws[static_cast<int64_t>(row) * p.m_out + m], __uint_as_float(r[j]));
-              }
+              if (row < row_end) wsp[static_cast<int64_t>(row) * p.m_out] = __uint_as_float(r[j]);
             }
           }
         } else if (m_ok) {
@@ -318,35 +317,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(&tempty_bar[acc]);
-      if (ks > 1) {
-        // The last split to arrive finalises the tile: epilogue from the fp32
-        // sums, then zeroes its workspace rows and counter for the next call.
-        __shared__ int s_last;
-        __threadfence();
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (threadIdx.x == 64) s_last = (atomicAdd(&p.counters[t], 1) == ks - 1);
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (s_last) {
-          __threadfence();
-          if (m_ok) {
-            for (int row = row0; row < min(row_end, row0 + BN); ++row) {
-              float* wp = &p.ws[static_cast<int64_t>(row) * p.m_out + m];
-              float v = __ldcg(wp) + bias_v;
-              *wp = 0.f;
-              if (p.act == kActGeluTanh) v = gelu_tanh_f(v);
-              else if (p.act == kActGeluErf) v = gelu_erf_f(v);
-              else if (p.act == kActSilu) v = silu_f(v);
-              if (p.residual != nullptr) v += __bfloat162float(p.residual[static_cast<int64_t>(row) * p.ldr + m]);
-              if (p.out_f32) {
-                static_cast<float*>(p.out)[static_cast<int64_t>(row) * p.ldo + m] = v;
-              } else {
-                static_cast<__nv_bfloat16*>(p.out)[static_cast<int64_t>(row) * p.ldo + m] = __float2bfloat16(v);
-              }
-            }
-          }
-          if (threadIdx.x == 64) p.counters[t] = 0;
-        }
-      }
     }
   }
 
@@ -355,6 +325,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// Sums the split-K partials [ks][rows][m_out] and applies the epilogue.
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int ks, int rows, int m_out, void* out,
+                                     int64_t ldo, int out_f32, const __nv_bfloat16* __restrict__ bias,
+                                     const __nv_bfloat16* __restrict__ residual, int64_t ldr, int act) {
+  const int64_t n = static_cast<int64_t>(rows) * m_out;
+  const int64_t plane = n;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int row = static_cast<int>(i / m_out);
+    const int m = static_cast<int>(i - static_cast<int64_t>(row) * m_out);
+    float v = 0.f;
+    for (int s = 0; s < ks; ++s) v += __ldg(ws + s * plane + i);
+    if (bias != nullptr) v += __bfloat162float(bias[m]);
+    if (act == kActGeluTanh) v = gelu_tanh_f(v);
+    else if (act == kActGeluErf) v = gelu_erf_f(v);
+    else if (act == kActSilu) v = silu_f(v);
+    if (residual != nullptr) v += __bfloat162float(residual[static_cast<int64_t>(row) * ldr + m]);
+    if (out_f32) static_cast<float*>(out)[static_cast<int64_t>(row) * ldo + m] = v;
+    else static_cast<__nv_bfloat16*>(out)[static_cast<int64_t>(row) * ldo + m] = __float2bfloat16(v);
   }
 }
 
@@ -438,17 +430,17 @@ cudaError_t launch(const GemmArgs& a, cudaStream_t stream) {
   if (!GATED && a.offsets == nullptr && a.splitk_ws != nullptr && a.splitk_counters != nullptr) {
     const long tiles = static_cast<long>(m_tiles) * ((a.rows + BN - 1) / BN);
     const int sms = num_sms();
-    if (tiles * 2 <= sms && num_kb >= 4 && static_cast<long>(a.rows) * a.m_out <= a.splitk_ws_floats &&
-        tiles <= a.splitk_counter_slots) {
+    if (tiles * 2 <= sms && num_kb >= 4) {
       int ksp = static_cast<int>((sms + tiles - 1) / tiles);
       if (ksp > num_kb / 2) ksp = num_kb / 2;
       if (ksp > 16) ksp = 16;
       if (ksp > 1) {
         const int per = (num_kb + ksp - 1) / ksp;
         ksp = (num_kb + per - 1) / per;  // no empty splits
-        p.k_splits = ksp;
-        p.ws = a.splitk_ws;
-        p.counters = a.splitk_counters;
+        if (static_cast<long long>(ksp) * a.rows * a.m_out <= a.splitk_ws_floats) {
+          p.k_splits = ksp;
+          p.ws = a.splitk_ws;
+        }
       }
     }
   }
@@ -459,6 +451,13 @@ cudaError_t launch(const GemmArgs& a, cudaStream_t stream) {
   if (bound < grid) grid = static_cast<int>(bound);
   if (grid < 1) grid = 1;
   gemm_bf16_kernel<BN, GATED><<<grid, kThreads, C::kSmemBytes, stream>>>(ta, tb, p);
+  if (p.k_splits > 1) {
+    const long long n = static_cast<long long>(a.rows) * a.m_out;
+    int rgrid = static_cast<int>((n + 255) / 256);
+    if (rgrid > 4 * num_sms()) rgrid = 4 * num_sms();
+    splitk_reduce_kernel<<<rgrid, 256, 0, stream>>>(p.ws, p.k_splits, a.rows, a.m_out, a.out, a.ldo, a.out_f32,
+                                                    p.bias, p.residual, a.ldr, a.act);
+  }
   return cudaGetLastError();
 }
 

@@ -37,12 +37,12 @@ struct GemmArgs {
   int act;
   int* status;            // device int32 status word (may be nullptr)
   int max_ctas;           // 0 = one CTA per SM
-  // Optional split-K scratch for dense, non-gated GEMMs with few output tiles.
-  // Must be zero before the first use; every call leaves it zero again.
-  // Calls that share it must not overlap on the GPU.
-  float* splitk_ws;       // fp32, >= rows * m_out elements to be used
+  // Optional split-K scratch for dense, non-gated GEMMs with few output tiles:
+  // fp32 partials [k_splits][rows][m_out], reduced by a second kernel.  Calls
+  // that share it must not overlap on the GPU.
+  float* splitk_ws;
   long long splitk_ws_floats;
-  int* splitk_counters;   // int32 per output tile
+  int* splitk_counters;   // unused (kept for ABI stability of GemmArgs)
   int splitk_counter_slots;
 };
 cudaError_t gemm_bf16(const GemmArgs& args, cudaStream_t stream);

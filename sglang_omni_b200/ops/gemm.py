@@ -15,12 +15,12 @@ import torch.nn.functional as F
 
 from ._ext import ext, status_word
 
-# Per-device split-K scratch of the dense GEMM (fp32 partial sums + per-tile
-# arrival counters).  The kernel leaves both zeroed after every call, so one
-# buffer serves every dense GEMM issued on the device's (single) compute
-# stream, including inside captured CUDA graphs.
+# Per-device split-K scratch of the dense GEMM: fp32 partial sums
+# [splits][rows][m_out], reduced by a second kernel.  One buffer serves every
+# dense GEMM issued on the device's (single) compute stream, including inside
+# captured CUDA graphs; GEMMs needing more fall back to no split.
 _SPLITK_FLOATS = 8 * 1024 * 1024
-_SPLITK_COUNTERS = 65536
+_SPLITK_COUNTERS = 16
 _splitk: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
 
 

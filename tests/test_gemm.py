@@ -88,8 +88,8 @@ def test_grouped(gated, groups, avg):
 @pytest.mark.gpu
 @pytest.mark.parametrize("rows,n,k", [(64, 5120, 2048), (64, 128, 2048), (7, 2048, 4096), (200, 256, 1024)])
 def test_splitk_dense_repeated(rows, n, k):
-    """Small-tile GEMMs take the split-K path; the self-cleaning workspace must give
-    identical results on back-to-back calls (bias + residual in the finaliser)."""
+    """Small-tile GEMMs take the split-K path (partials + reduce kernel); back-to-back
+    calls must agree (bias + residual applied in the reduction)."""
     torch.manual_seed(rows + n)
     x = torch.randn(rows, k, device="cuda").bfloat16()
     w = (torch.randn(n, k, device="cuda") * 0.02).bfloat16()
@@ -100,6 +100,3 @@ def test_splitk_dense_repeated(rows, n, k):
     y2 = L.linear(x, w, bias=b, residual=r)
     _close(y1, ref)
     _close(y2, ref)
-    ws, ctr = L.splitk_scratch(x.device)
-    torch.cuda.synchronize()
-    assert int(ctr.abs().sum()) == 0 and float(ws[: rows * n].abs().sum()) == 0.0
