@@ -107,6 +107,7 @@ struct PrefillParams {
   int causal;
   __nv_bfloat16* out;
   int64_t out_stride;
+  int window;
 };
 
 template <int D>
@@ -156,6 +157,8 @@ __global__ void __launch_bounds__(128) prefill_kernel(const PrefillParams p) {
   const int last_tok = min(q_len, tok0 + tokens_per_tile) - 1;
   const int key_end = p.causal ? min(kv_len, pos_base + last_tok + 1) : kv_len;
   const int ntiles = (key_end + kPage - 1) / kPage;
+  // sliding window: keys below (first query pos - window + 1) are never visible
+  const int first_tile = p.window > 0 ? max(0, pos_base + tok0 - p.window + 1) / kPage : 0;
 
   float o[NJ][4];
 #pragma unroll
@@ -182,8 +185,8 @@ __global__ void __launch_bounds__(128) prefill_kernel(const PrefillParams p) {
     cp_async_commit();
   };
 
-  if (ntiles > 0) issue(0, 0);
-  for (int it = 0; it < ntiles; ++it) {
+  if (ntiles > first_tile) issue(first_tile, first_tile & 1);
+  for (int it = first_tile; it < ntiles; ++it) {
     const int buf = it & 1;
     if (it + 1 < ntiles) {
       issue(it + 1, buf ^ 1);
@@ -219,8 +222,10 @@ __global__ void __launch_bounds__(128) prefill_kernel(const PrefillParams p) {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int key = k0 + n * 8 + 2 * t + e;
-        const bool okA = validA && key < kv_len && (!p.causal || key <= posA);
-        const bool okB = validB && key < kv_len && (!p.causal || key <= posB);
+        const bool okA = validA && key < kv_len && (!p.causal || key <= posA) &&
+                         (p.window <= 0 || key > posA - p.window);
+        const bool okB = validB && key < kv_len && (!p.causal || key <= posB) &&
+                         (p.window <= 0 || key > posB - p.window);
         s[n][e] = okA ? s[n][e] * p.scale_log2 : -INFINITY;
         s[n][2 + e] = okB ? s[n][2 + e] * p.scale_log2 : -INFINITY;
         mxA = fmaxf(mxA, s[n][e]);
@@ -576,6 +581,7 @@ cudaError_t attention_prefill(const AttnPrefillArgs& a, cudaStream_t stream) {
   p.causal = a.causal;
   p.out = static_cast<__nv_bfloat16*>(a.out);
   p.out_stride = a.out_stride;
+  p.window = a.window;
   switch (a.head_dim) {
     case 64: return launch_prefill<64>(p, a.num_tiles, stream);
     case 80: return launch_prefill<80>(p, a.num_tiles, stream);

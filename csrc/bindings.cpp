@@ -153,7 +153,7 @@ void attention_prefill(const torch::Tensor& q, const torch::Tensor& k, const tor
                        const c10::optional<torch::Tensor>& block_table, const torch::Tensor& cu_q,
                        const torch::Tensor& kv_lens, const c10::optional<torch::Tensor>& cu_kv,
                        const torch::Tensor& tile_req, const torch::Tensor& tile_tok0, int64_t hq, int64_t hkv,
-                       int64_t head_dim, double scale, bool causal) {
+                       int64_t head_dim, double scale, bool causal, int64_t window) {
   OMNI_CHECK_CUDA(q);
   OMNI_CHECK_BF16(q);
   OMNI_CHECK_BF16(k);
@@ -185,6 +185,7 @@ void attention_prefill(const torch::Tensor& q, const torch::Tensor& k, const tor
   a.causal = causal ? 1 : 0;
   a.out = out.data_ptr();
   a.out_stride = out.stride(0);
+  a.window = static_cast<int>(window);
   check_launch(omni::attention_prefill(a, at::cuda::getCurrentCUDAStream()), "attention_prefill");
 }
 
@@ -375,6 +376,79 @@ void sample(torch::Tensor& logits, torch::Tensor& out_tokens, const c10::optiona
   check_launch(omni::sample(a, at::cuda::getCurrentCUDAStream()), "sample");
 }
 
+void snake(const torch::Tensor& x, const torch::Tensor& alpha, const c10::optional<torch::Tensor>& beta,
+           torch::Tensor& y, bool log_scale) {
+  OMNI_CHECK_CUDA(x);
+  OMNI_CHECK_BF16(x);
+  OMNI_CHECK_CONTIG(x);
+  OMNI_CHECK_CONTIG(y);
+  TORCH_CHECK(alpha.scalar_type() == at::kFloat, "alpha fp32");
+  const at::cuda::CUDAGuard guard(x.device());
+  check_launch(omni::snake(x.data_ptr(), alpha.data_ptr<float>(), opt_ptr<float>(beta), y.data_ptr(), x.numel(),
+                           static_cast<int>(x.size(-1)), log_scale ? 1 : 0, at::cuda::getCurrentCUDAStream()),
+               "snake");
+}
+
+void conv1d_im2col(const torch::Tensor& x, torch::Tensor& out, int64_t K, int64_t dil, int64_t stride,
+                   int64_t pad_left) {
+  OMNI_CHECK_CUDA(x);
+  OMNI_CHECK_BF16(x);
+  OMNI_CHECK_CONTIG(x);
+  TORCH_CHECK(x.dim() == 3 && out.dim() == 3 && out.stride(-1) == 1, "x [B, T, C], out [B, T_out, >= K*C]");
+  const at::cuda::CUDAGuard guard(x.device());
+  check_launch(omni::conv1d_im2col(x.data_ptr(), out.data_ptr(), static_cast<int>(x.size(0)),
+                                   static_cast<int>(x.size(1)), static_cast<int>(out.size(1)),
+                                   static_cast<int>(x.size(2)), static_cast<int>(K), static_cast<int>(dil),
+                                   static_cast<int>(stride), static_cast<int>(pad_left),
+                                   static_cast<int>(out.stride(1)), at::cuda::getCurrentCUDAStream()),
+               "conv1d_im2col");
+}
+
+void conv_transpose_ola(const torch::Tensor& y, const c10::optional<torch::Tensor>& bias, torch::Tensor& out,
+                        int64_t s) {
+  OMNI_CHECK_CUDA(y);
+  OMNI_CHECK_BF16(y);
+  OMNI_CHECK_CONTIG(y);
+  OMNI_CHECK_CONTIG(out);
+  TORCH_CHECK(y.dim() == 3, "y [B, T, 2s*C]");
+  const int64_t C = out.size(-1);
+  TORCH_CHECK(y.size(2) == 2 * s * C, "y width must be 2*s*C");
+  const at::cuda::CUDAGuard guard(y.device());
+  check_launch(omni::conv_transpose_ola(y.data_ptr(), bias.has_value() ? bias->data_ptr() : nullptr,
+                                        out.data_ptr(), static_cast<int>(y.size(0)), static_cast<int>(y.size(1)),
+                                        static_cast<int>(s), static_cast<int>(C), at::cuda::getCurrentCUDAStream()),
+               "conv_transpose_ola");
+}
+
+void dwconv1d_causal(const torch::Tensor& x, const torch::Tensor& w, const c10::optional<torch::Tensor>& bias,
+                     torch::Tensor& out) {
+  OMNI_CHECK_CUDA(x);
+  OMNI_CHECK_BF16(x);
+  OMNI_CHECK_CONTIG(x);
+  TORCH_CHECK(w.scalar_type() == at::kFloat && w.is_contiguous(), "w fp32 [C, K]");
+  const at::cuda::CUDAGuard guard(x.device());
+  check_launch(omni::dwconv1d_causal(x.data_ptr(), w.data_ptr<float>(), opt_ptr<float>(bias), out.data_ptr(),
+                                     static_cast<int>(x.size(0)), static_cast<int>(x.size(1)),
+                                     static_cast<int>(x.size(2)), static_cast<int>(w.size(1)),
+                                     at::cuda::getCurrentCUDAStream()),
+               "dwconv1d_causal");
+}
+
+void conv2d_im2col(const torch::Tensor& x, torch::Tensor& out, int64_t kh, int64_t kw, int64_t stride, int64_t pad) {
+  OMNI_CHECK_CUDA(x);
+  OMNI_CHECK_BF16(x);
+  OMNI_CHECK_CONTIG(x);
+  TORCH_CHECK(x.dim() == 4 && out.dim() == 4, "x [N, H, W, C], out [N, Ho, Wo, >= kh*kw*C]");
+  const at::cuda::CUDAGuard guard(x.device());
+  check_launch(omni::conv2d_im2col(x.data_ptr(), out.data_ptr(), static_cast<int>(x.size(0)),
+                                   static_cast<int>(x.size(1)), static_cast<int>(x.size(2)),
+                                   static_cast<int>(x.size(3)), static_cast<int>(out.size(1)),
+                                   static_cast<int>(out.size(2)), static_cast<int>(kh), static_cast<int>(kw),
+                                   static_cast<int>(stride), static_cast<int>(pad), static_cast<int>(out.stride(2)),
+                                   at::cuda::getCurrentCUDAStream()),
+               "conv2d_im2col");
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -392,4 +466,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine", &moe_combine, "MoE top-k weighted combine (+ shared expert)");
   m.def("embed", &embed, "embedding gather with multimodal overwrite");
   m.def("sample", &sample, "fused logits processing + sampling");
+  m.def("snake", &snake, "Snake / SnakeBeta activation (channels-last)");
+  m.def("conv1d_im2col", &conv1d_im2col, "causal dilated conv1d im2col rows");
+  m.def("conv_transpose_ola", &conv_transpose_ola, "transposed-conv overlap-add + bias + causal trim");
+  m.def("dwconv1d_causal", &dwconv1d_causal, "depthwise causal conv1d");
+  m.def("conv2d_im2col", &conv2d_im2col, "2-D conv im2col rows (kh, kw, c)");
 }

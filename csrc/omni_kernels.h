@@ -78,6 +78,7 @@ struct AttnPrefillArgs {
   int causal;
   void* out;              // [tokens, hq, D] rows of stride out_stride
   int64_t out_stride;
+  int window;             // > 0: causal sliding window (a query sees its last `window` keys)
 };
 cudaError_t attention_prefill(const AttnPrefillArgs& a, cudaStream_t stream);
 
@@ -186,5 +187,17 @@ struct SampleArgs {
   int* slot_tokens;
 };
 cudaError_t sample(const SampleArgs& a, cudaStream_t stream);
+
+// ---------------------------------------------------------------- audio / vocoder ops (channels-last)
+cudaError_t snake(const void* x, const float* alpha, const float* beta, void* y, int64_t n, int C, int log_scale,
+                  cudaStream_t stream);
+cudaError_t conv1d_im2col(const void* x, void* out, int B, int T_in, int T_out, int C, int K, int dil, int stride,
+                          int pad_left, int out_row_stride, cudaStream_t stream);
+cudaError_t conv_transpose_ola(const void* y, const void* bias, void* out, int B, int T, int s, int C,
+                               cudaStream_t stream);
+cudaError_t dwconv1d_causal(const void* x, const float* w, const float* bias, void* out, int B, int T, int C, int K,
+                            cudaStream_t stream);
+cudaError_t conv2d_im2col(const void* x, void* out, int N, int H, int W, int C, int Ho, int Wo, int kh, int kw,
+                          int stride, int pad, int K_stride, cudaStream_t stream);
 
 }  // namespace omni

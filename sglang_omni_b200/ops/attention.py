@@ -30,8 +30,8 @@ def prefill_tiles(q_lens: list[int], group: int) -> tuple[list[int], list[int]]:
     return req, tok0
 
 
-def _sdpa_ref(q, k, v, causal, q_offset, scale):
-    """q [Tq, Hq, D], k/v [Tk, Hkv, D] -> [Tq, Hq, D] in fp32."""
+def _sdpa_ref(q, k, v, causal, q_offset, scale, window=0):
+    """q [Tq, Hq, D], k/v [Tk, Hkv, D] -> [Tq, Hq, D] in fp32 (window > 0: causal sliding window)."""
     hq, hkv = q.shape[1], k.shape[1]
     g = hq // hkv
     k = k.float().repeat_interleave(g, dim=1)
@@ -42,6 +42,8 @@ def _sdpa_ref(q, k, v, causal, q_offset, scale):
         qi = torch.arange(tq, device=q.device)[:, None] + q_offset
         ki = torch.arange(tk, device=q.device)[None, :]
         s = s.masked_fill((ki > qi)[None], float("-inf"))
+        if window > 0:
+            s = s.masked_fill((ki <= qi - window)[None], float("-inf"))
     p = torch.softmax(s, dim=-1)
     return torch.einsum("hqk,khd->qhd", p, v)
 
@@ -68,13 +70,13 @@ def paged_attention_ref(q, k_cache, v_cache, block_table, cu_q, kv_lens, scale, 
     return out
 
 
-def varlen_attention_ref(q, k, v, cu_seqlens, scale, causal=False):
+def varlen_attention_ref(q, k, v, cu_seqlens, scale, causal=False, window=0):
     cu = cu_seqlens.tolist()
     out = torch.empty(q.shape, dtype=torch.float32, device=q.device)
     for b in range(len(cu) - 1):
         a, e = cu[b], cu[b + 1]
         if e > a:
-            out[a:e] = _sdpa_ref(q[a:e], k[a:e], v[a:e], causal, 0, scale)
+            out[a:e] = _sdpa_ref(q[a:e], k[a:e], v[a:e], causal, 0, scale, window)
     return out
 
 
@@ -93,22 +95,24 @@ def prefill_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Ten
         out.copy_(ref.reshape(out.shape))
         return out
     ext().attention_prefill(q3, k_cache, v_cache, out, block_table, cu_q, kv_lens, None, tile_req, tile_tok0,
-                            num_heads, num_kv_heads, head_dim, scale, causal)
+                            num_heads, num_kv_heads, head_dim, scale, causal, 0)
     return out
 
 
 def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens: torch.Tensor,
                      num_heads: int, num_kv_heads: int, head_dim: int, scale: float | None = None,
                      causal: bool = False, out: torch.Tensor | None = None, q_lens: list[int] | None = None,
-                     tiles: tuple[torch.Tensor, torch.Tensor] | None = None) -> torch.Tensor:
-    """Ragged (block-diagonal) attention over contiguous q/k/v rows (encoders)."""
+                     tiles: tuple[torch.Tensor, torch.Tensor] | None = None, window: int = 0) -> torch.Tensor:
+    """Ragged (block-diagonal) attention over contiguous q/k/v rows (encoders, vocoder transformers).
+
+    ``window`` > 0 (with causal) limits every query to its last ``window`` keys."""
     scale = scale if scale is not None else 1.0 / math.sqrt(head_dim)
     T = q.shape[0]
     if out is None:
         out = torch.empty(T, num_heads * head_dim, dtype=q.dtype, device=q.device)
     if not q.is_cuda:
         ref = varlen_attention_ref(q.reshape(T, num_heads, head_dim), k.reshape(T, num_kv_heads, head_dim),
-                                   v.reshape(T, num_kv_heads, head_dim), cu_seqlens, scale, causal)
+                                   v.reshape(T, num_kv_heads, head_dim), cu_seqlens, scale, causal, window)
         out.copy_(ref.reshape(out.shape))
         return out
     if tiles is None:
@@ -120,7 +124,7 @@ def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqle
                  torch.tensor(tok0, dtype=torch.int32, device=q.device))
     lens = cu_seqlens[1:] - cu_seqlens[:-1]
     ext().attention_prefill(q, k, v, out, None, cu_seqlens, lens.to(torch.int32), cu_seqlens, tiles[0], tiles[1],
-                            num_heads, num_kv_heads, head_dim, scale, causal)
+                            num_heads, num_kv_heads, head_dim, scale, causal, window)
     return out
 
 
