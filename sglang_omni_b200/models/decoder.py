@@ -152,7 +152,7 @@ class DecoderLM(nn.Module):
         self.final_norm = P(H)
         self.lm_head = None if cfg.tie_word_embeddings else P(cfg.vocab_size, H)
         rot = cfg.rotary_dim or cfg.head_dim
-        cos, sin = ops.rope_tables(rot, cfg.rope_theta, cfg.max_position, device)
+        cos, sin = ops.rope_tables(rot, cfg.rope_theta, cfg.max_position, device, round_bf16=cfg.dtype == torch.bfloat16)
         self.register_buffer("cos_tab", cos, persistent=False)
         self.register_buffer("sin_tab", sin, persistent=False)
         self._moe_ws: MoEWorkspace | None = None
