@@ -59,3 +59,13 @@ def test_prefill_layout():
     # system segment skipped, user segment 5 tokens, assistant part 9 rows
     assert pre.shape[0] == 5 + 9
     assert trail.shape[0] == 1  # response tokens after the first
+
+
+@pytest.mark.gpu
+def test_batched_streams_match_single_gpu_graphs():
+    t, emb = tiny(torch.bfloat16, "cuda")
+    both = _gen(t, emb, ["a", "b"], 6, device="cuda")
+    alone_a = _gen(t, emb, ["a"], 6, device="cuda")
+    assert len(both["a"]) == 7
+    # greedy + per-row independent kernels: batching must not change a stream's codes
+    assert both["a"] == alone_a["a"]
