@@ -26,6 +26,7 @@ class ARRequest:
     deepstack: list | None = None                  # per layer [L_vis, H] embeds, with ds_positions
     ds_positions: torch.Tensor | None = None
     capture_layers: tuple = ()                     # hidden states to emit per generated token
+    capture_prompt_layer: int | None = None        # keep this layer's prompt rows in extra['prompt_hidden']
     on_token: Callable[["ARRequest", int, dict], None] | None = None
     extra: dict[str, Any] = field(default_factory=dict)
     # engine state

@@ -199,7 +199,8 @@ class ARModelRunner:
                         ps.append(p[sel] - s + o)
                         es.append(r.deepstack[li][sel.nonzero().squeeze(1)])
                 deepstack.append((torch.cat(ps).to(dev), torch.cat(es).to(dev)) if ps else None)
-        capture = tuple(sorted({c for r, _, _ in chunks for c in r.capture_layers}))
+        capture = tuple(sorted({c for r, _, _ in chunks for c in r.capture_layers} |
+                               {r.capture_prompt_layer for r, _, _ in chunks if r.capture_prompt_layer is not None}))
         fb = ForwardBatch(
             is_decode=False, positions=as_dev(pos), slot_mapping=as_dev(slots), kv_lens=as_dev(kv_lens),
             block_table=as_dev(bt), input_ids=as_dev(ids) if input_embeds is None else None,
@@ -211,6 +212,10 @@ class ARModelRunner:
         if not logits_rows:
             fb.logits_indices = torch.zeros(1, dtype=torch.int32, device=dev)
         hidden = self.model(fb, self.pool.kv)
+        for b, (r, s, e) in enumerate(chunks):
+            if r.capture_prompt_layer is not None and r.capture_prompt_layer in fb.captured:
+                rows = fb.captured[r.capture_prompt_layer][cu[b]:cu[b + 1]]
+                r.extra.setdefault("prompt_hidden", []).append(rows)
         captured = {}
         if capture and logits_rows:
             sel = fb.logits_indices.long()

@@ -53,12 +53,12 @@ class ResultQueueMixin:
     """Completion-order result delivery shared by the concrete executors."""
 
     def _init_results(self):
-        self._done: asyncio.Queue | None = None
+        self._result_q: asyncio.Queue | None = None
 
     def _results(self) -> asyncio.Queue:
-        if getattr(self, "_done", None) is None:
-            self._done = asyncio.Queue()
-        return self._done
+        if getattr(self, "_result_q", None) is None:
+            self._result_q = asyncio.Queue()
+        return self._result_q
 
     async def get_result(self) -> StagePayload:
         item = await self._results().get()

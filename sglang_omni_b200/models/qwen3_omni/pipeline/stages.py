@@ -1,0 +1,533 @@
+"""Stage factories of the Qwen3-Omni pipelines.
+
+preprocessing  (CPU)  chat layout with audio / image placeholders, M-RoPE positions
+audio_encoder  (GPU)  batched log-mel + audio tower (generic step engine, LRU cache)
+image_encoder  (GPU)  vision tower (skips requests without images)
+mm_aggregate          fan-in -> thinker input
+thinker        (GPU)  paged AR engine; text deltas to the client; in speech mode
+                      every token (and the prompt's accept-layer states) is
+                      streamed to talker_ar
+decode                terminal text result
+talker_ar      (GPU)  SpeechGenerator: talker + code predictor for all streams
+                      in lock step, code frames streamed to code2wav
+code2wav       (GPU)  streaming vocoder, audio chunks to the client
+
+Reference counterpart: sglang_omni/models/qwen3_omni/pipeline/stages.py:56-675
+and the streaming executors in sglang_omni/models/qwen3_omni/components/.
+"""
+from __future__ import annotations
+
+import asyncio
+import base64
+import io
+import logging
+import threading
+import time
+from collections import deque
+from typing import Any
+
+import numpy as np
+import torch
+
+from ....client.audio import decode_wav
+from ....engines.ar import AREngine, ARRequest, KVPool
+from ....engines.ar.adapter import PagedAREngineAdapter
+from ....engines.omni.factory import create_encoder_engine
+from ....engines.omni.runtime.encoder import EncoderRequestData
+from ....executors import EngineExecutor, PreprocessingExecutor
+from ....executors.interface import Executor, ResultQueueMixin
+from ....executors.preprocessing_executor import StageError
+from ....ops.mel import LogMel
+from ....proto import StagePayload
+from ...common.ar_stage import sampling_for
+from ...common.tokenizer import IncrementalDetokenizer, load_tokenizer
+from .. import loader
+from ..engine_io import build_prompt, mrope_positions
+from ..hf_config import THINKER_EOS_IDS
+from ..talker import SpeechGenerator, build_talker_prefill
+from ..code2wav import StreamingCode2Wav
+
+log = logging.getLogger(__name__)
+SAMPLE_RATE_IN = 16000
+SAMPLE_RATE_OUT = 24000
+
+
+def _speech_requested(params: dict) -> bool:
+    mods = params.get("output_modalities") or []
+    return "audio" in mods or params.get("task") == "tts"
+
+
+# ----------------------------------------------------------------------------- preprocessing
+def _load_audio(item: Any) -> torch.Tensor:
+    """Waveform at 16 kHz from an array / list / {"array", "sampling_rate"} / wav path / base64 wav."""
+    sr = SAMPLE_RATE_IN
+    if isinstance(item, dict):
+        sr = int(item.get("sampling_rate", SAMPLE_RATE_IN))
+        item = item.get("array", item.get("data", item.get("path")))
+    if isinstance(item, str):
+        if item.startswith("data:"):
+            item = item.split(",", 1)[1]
+        try:
+            raw = base64.b64decode(item, validate=True)
+        except Exception:
+            with open(item, "rb") as f:
+                raw = f.read()
+        x, sr = decode_wav(raw)
+        item = x
+    x = torch.as_tensor(np.asarray(item, dtype=np.float32)).reshape(-1)
+    if sr != SAMPLE_RATE_IN:
+        n = int(round(x.numel() * SAMPLE_RATE_IN / sr))
+        x = torch.nn.functional.interpolate(x[None, None], size=n, mode="linear", align_corners=False)[0, 0]
+    return x
+
+
+def create_preprocessing_executor(model_path: str = "", overrides: dict | None = None):
+    tok = load_tokenizer(model_path)
+    n_window = 50
+
+    def audio_tokens(n_samples: int) -> int:
+        from ..audio_encoder import cnn_out_len
+
+        frames = n_samples // 160
+        cs = 2 * n_window
+        full, rem = divmod(frames, cs)
+        return full * cnn_out_len(cs) + (cnn_out_len(rem) if rem else 0)
+
+    def preprocess(payload: StagePayload) -> StagePayload:
+        inp = payload.request.inputs if isinstance(payload.request.inputs, dict) else {}
+        waves = [_load_audio(a) for a in (inp.get("audios") or [])]
+        counts = [audio_tokens(w.numel()) for w in waves]
+        if inp.get("prompt_token_ids") is not None and not waves:
+            ids = list(inp["prompt_token_ids"])
+            p = torch.arange(len(ids), dtype=torch.int32)
+            pos, delta, spans = torch.stack([p, p, p]), 0, []
+        else:
+            lay = build_prompt(tok, inp.get("messages"), inp.get("prompt"), counts)
+            ids = lay.ids
+            pos, delta = mrope_positions(lay)
+            spans = lay.audio_spans
+        data = {"prompt_token_ids": ids, "audio_waveforms": waves, "audio_spans": spans,
+                "mrope_positions": pos, "mrope_delta": delta,
+                "speech": _speech_requested(payload.request.params or {})}
+        return StagePayload(payload.request_id, payload.request, data)
+
+    return PreprocessingExecutor(preprocess)
+
+
+# ----------------------------------------------------------------------------- encoders
+def create_audio_encoder_executor(model_path: str = "", device: str = "cuda:0", max_batch_size: int = 32,
+                                  overrides: dict | None = None):
+    dev = torch.device(device)
+    enc = loader.get_audio_encoder(model_path, dev, overrides)
+    mel = LogMel(enc.cfg.num_mel_bins, dev)
+
+    def encode(inputs: dict) -> list:
+        per_req = inputs["waves"]
+        flat = [w for ws in per_req for w in ws]
+        mels = [mel(w.to(dev)) for w in flat]
+        outs = enc(mels) if mels else []
+        res, i = [], 0
+        for ws in per_req:
+            res.append({"audio_embeds": outs[i:i + len(ws)]})
+            i += len(ws)
+        return res
+
+    engine = create_encoder_engine(encode, max_batch_size=max_batch_size, device=dev, cache_size=0)
+
+    def request_builder(payload: StagePayload):
+        waves = (payload.data or {}).get("audio_waveforms") or []
+        return EncoderRequestData(inputs={"waves": waves}, skip=not waves)
+
+    def result_builder(payload: StagePayload, out):
+        if not isinstance(out, dict):  # skipped request (no audio)
+            out = {"audio_embeds": None}
+        return StagePayload(payload.request_id, payload.request, out)
+
+    return EngineExecutor(engine, request_builder, result_builder)
+
+
+def create_image_encoder_executor(model_path: str = "", device: str = "cuda:0", max_batch_size: int = 32,
+                                  overrides: dict | None = None):
+    def run(payload: StagePayload) -> StagePayload:
+        images = (payload.data or {}).get("images") or []
+        if not images:
+            return StagePayload(payload.request_id, payload.request, {"image_embeds": None})
+        from ..vision_encoder import encode_images
+
+        return StagePayload(payload.request_id, payload.request,
+                            encode_images(model_path, torch.device(device), images, overrides))
+
+    return PreprocessingExecutor(run)
+
+
+def create_aggregate_executor(**_):
+    return PreprocessingExecutor(lambda p: p)
+
+
+# ----------------------------------------------------------------------------- thinker
+def create_thinker_executor(model_path: str = "", device: str = "cuda:0", max_batch: int = 64,
+                            max_context: int = 4096, max_prefill_tokens: int = 8192, speech_target: str | None = None,
+                            accept_hidden_layer: int = 24, overrides: dict | None = None, use_graphs: bool = True):
+    dev = torch.device(device)
+    model = loader.get_thinker(model_path, dev, overrides)
+    tok = load_tokenizer(model_path, model.cfg.vocab_size)
+    cfg = model.cfg
+    pages = max_batch * ((max_context + 63) // 64) + 8
+    pool = KVPool(cfg.num_layers, cfg.num_kv_heads, cfg.head_dim, pages, dev, cfg.dtype)
+    engine = AREngine(model, pool, max_batch=max_batch, max_prefill_tokens=max_prefill_tokens,
+                      max_context=max_context, use_graphs=use_graphs and dev.type == "cuda",
+                      eos_token_ids=THINKER_EOS_IDS)
+    adapter = PagedAREngineAdapter(engine)
+    detoks: dict[str, IncrementalDetokenizer] = {}
+    accept = min(accept_hidden_layer, cfg.num_layers)
+
+    ex = EngineExecutor(adapter, None, None, None)
+
+    def request_builder(payload: StagePayload) -> ARRequest:
+        d = payload.data
+        sp = sampling_for(payload, "thinker")
+        ids = list(d["prompt_token_ids"])
+        req = ARRequest(rid=payload.request_id, prompt_ids=ids, sampling=sp,
+                        max_new_tokens=sp.max_new_tokens or 256)
+        req.mrope_positions = d.get("mrope_positions")
+        req.mrope_delta = int(d.get("mrope_delta") or 0)
+        aud = d.get("audio_embeds")
+        spans = d.get("audio_spans") or []
+        if aud:
+            mm_index = torch.full((len(ids),), -1, dtype=torch.int32)
+            base = 0
+            for (a, b), emb in zip(spans, aud):
+                n = min(b - a, emb.shape[0])
+                mm_index[a:a + n] = torch.arange(base, base + n, dtype=torch.int32)
+                base += emb.shape[0]
+            req.mm_index = mm_index
+            req.mm_embeds = torch.cat(list(aud), 0)
+        speech = bool(d.get("speech")) and speech_target is not None
+        if speech:
+            req.capture_prompt_layer = accept if aud else None
+            sent = {"first": True}
+
+            def on_token(r, token, info, _rid=payload.request_id, _sent=sent, _spans=spans):
+                msg = {"token_id": int(token)}
+                if _sent["first"]:
+                    _sent["first"] = False
+                    ph = r.extra.get("prompt_hidden")
+                    if ph:
+                        full = torch.cat(ph, 0)
+                        mask = torch.zeros(full.shape[0], dtype=torch.bool)
+                        for a, b in _spans:
+                            mask[a:b] = True
+                        msg["mm_mask"] = mask
+                        msg["mm_hidden"] = full[mask.to(full.device)]
+                if ex._stream_fn is not None:
+                    ex._stream_fn(_rid, msg, speech_target)
+
+            req.on_token = on_token
+        detoks[payload.request_id] = IncrementalDetokenizer(tok)
+        return req
+
+    def stream_builder(payload: StagePayload, chunk):
+        token, _ = chunk
+        d = detoks.get(payload.request_id)
+        text = d.push(token) if d is not None else ""
+        return {"modality": "text", "token_ids": [int(token)], "text": text}
+
+    def result_builder(payload: StagePayload, r: ARRequest) -> StagePayload:
+        detoks.pop(payload.request_id, None)
+        text = tok.decode(r.output_ids, skip_special_tokens=True)
+        data = {"token_ids": list(r.output_ids), "text": text, "finish_reason": r.finish_reason,
+                "usage": {"prompt_tokens": len(r.prompt_ids), "completion_tokens": len(r.output_ids),
+                          "total_tokens": len(r.prompt_ids) + len(r.output_ids)},
+                "ttft_s": (r.first_token_time - r.arrival) if r.first_token_time else None}
+        return StagePayload(payload.request_id, payload.request, data)
+
+    ex.request_builder = request_builder
+    ex.stream_builder = stream_builder
+    ex.result_builder = result_builder
+    ex.ar_engine = engine
+    return ex
+
+
+def create_decode_executor(**_):
+    def run(payload: StagePayload) -> StagePayload:
+        d = dict(payload.data or {})
+        meta = payload.request.metadata or {}
+        if "usage" in d and meta.get("engine_time_s") is not None:
+            d["usage"] = dict(d["usage"], engine_time_s=meta["engine_time_s"])
+        return StagePayload(payload.request_id, payload.request, d)
+
+    return PreprocessingExecutor(run)
+
+
+# ----------------------------------------------------------------------------- talker (+ code predictor)
+class TalkerStreamingExecutor(ResultQueueMixin, Executor):
+    """Runs the SpeechGenerator on its own thread; inbound thinker tokens come
+    through the stage mailbox, code frames go to ``code_target``."""
+
+    def __init__(self, model_path: str, device: str, max_streams: int = 64, code_target: str = "code2wav",
+                 overrides: dict | None = None, max_frames: int = 4096, use_graphs: bool = True,
+                 tail_frames: int = 50):
+        super().__init__()
+        dev = torch.device(device)
+        self.device = dev
+        self.talker = loader.get_talker(model_path, dev, overrides)
+        self.embed = loader.thinker_embedding(model_path, dev, overrides)
+        self.gen = SpeechGenerator(self.talker, self.embed, max_streams=max_streams,
+                                   use_graphs=use_graphs and dev.type == "cuda", tail_frames=tail_frames)
+        self.code_target = code_target
+        self.max_frames = max_frames
+        self._cv = threading.Condition()
+        self._new: deque = deque()        # (rid, prompt_ids, speaker)
+        self._tokens: dict[str, list] = {}
+        self._first: dict[str, dict] = {}
+        self._done: set[str] = set()
+        self._aborted: set[str] = set()
+        self._pending: dict[str, dict] = {}
+        self._thread: threading.Thread | None = None
+        self._loop: asyncio.AbstractEventLoop | None = None
+        self._stop = False
+        self.error: BaseException | None = None
+
+    async def start(self):
+        self._loop = asyncio.get_running_loop()
+        if self._thread is None:
+            self._thread = threading.Thread(target=self._run, name="talker", daemon=True)
+            self._thread.start()
+
+    async def stop(self):
+        with self._cv:
+            self._stop = True
+            self._cv.notify_all()
+
+    async def add_request(self, payload: StagePayload) -> None:
+        rid = payload.request_id
+        d = payload.data or {}
+        meta = payload.request.metadata or {}
+        speaker = (meta.get("audio") or {}).get("voice") or meta.get("voice")
+        self._pending[rid] = {"payload": payload, "t0": time.perf_counter()}
+        with self._cv:
+            self._tokens[rid] = []
+            self._new.append((rid, list(d.get("prompt_token_ids") or []), speaker))
+            self._cv.notify_all()
+        asyncio.ensure_future(self._pump(rid))
+
+    async def _pump(self, rid: str):
+        """Moves thinker chunks from the mailbox to the generator thread."""
+        try:
+            while True:
+                item = await self._mailbox.get(rid)
+                if item is None:
+                    break
+                with self._cv:
+                    data = item.data
+                    if "mm_hidden" in data:
+                        self._first[rid] = {"mm_mask": data["mm_mask"], "mm_hidden": data["mm_hidden"]}
+                    self._tokens.setdefault(rid, []).append(int(data["token_id"]))
+                    self._cv.notify_all()
+        except Exception as exc:  # thinker stream error
+            self._finish(rid, error=str(exc))
+            return
+        with self._cv:
+            self._done.add(rid)
+            self._cv.notify_all()
+
+    def _finish(self, rid: str, error: str | None = None, frames: int = 0):
+        info = self._pending.pop(rid, None)
+        if info is None:
+            return
+        p = info["payload"]
+        if error is not None:
+            item = StageError(rid, error)
+        else:
+            item = StagePayload(rid, p.request, {"num_frames": frames})
+        self._loop.call_soon_threadsafe(self._results().put_nowait, item)
+
+    async def abort(self, request_id: str) -> None:
+        with self._cv:
+            self._aborted.add(request_id)
+            self._cv.notify_all()
+
+    # ---------------------------------------------------------------- generator thread
+    def _run(self):
+        try:
+            with torch.inference_mode():
+                self._loop_body()
+        except BaseException as exc:
+            log.exception("talker thread failed")
+            self.error = exc
+            for rid in list(self._pending):
+                self._finish(rid, error=f"talker failed: {exc}")
+
+    def _emit(self, streams, codes: torch.Tensor):
+        host = codes.cpu().tolist()
+        eos = self.talker.special.codec_eos
+        for s, c in zip(streams, host):
+            if c[0] == eos or s.frames >= s.max_frames:
+                s.finished = True
+                self._stream_fn(s.rid, {"codes": [], "eos": True}, self.code_target)
+                self._finish(s.rid, frames=s.frames)
+                self.gen.remove(s.rid)
+            else:
+                self._stream_fn(s.rid, {"codes": c}, self.code_target)
+
+    def _loop_body(self):
+        gen = self.gen
+        while True:
+            with self._cv:
+                while not self._stop and not self._has_work():
+                    self._cv.wait(timeout=0.5)
+                if self._stop:
+                    return
+                aborted, self._aborted = self._aborted, set()
+                new_ready = []
+                keep = deque()
+                while self._new:
+                    rid, ids, spk = self._new.popleft()
+                    if rid in aborted:
+                        continue
+                    if self._tokens.get(rid):
+                        new_ready.append((rid, ids, spk, self._tokens[rid][:1], self._first.pop(rid, None)))
+                        self._tokens[rid] = self._tokens[rid][1:]
+                    else:
+                        keep.append((rid, ids, spk))
+                self._new = keep
+                pending_tokens = {rid: self._tokens[rid] for rid in list(self._tokens) if self._tokens[rid]
+                                  and rid in gen.streams}
+                for rid in pending_tokens:
+                    self._tokens[rid] = []
+                done = {rid for rid in self._done if rid in gen.streams}
+                self._done -= done
+            for rid in aborted:
+                if rid in gen.streams:
+                    gen.remove(rid)
+                self._pending.pop(rid, None)
+            # new streams: build the HF-parity prefill and run it batched
+            new_streams = []
+            for rid, ids, spk, first, mm in new_ready:
+                pre, trail, pad_e, eos_e = build_talker_prefill(
+                    self.talker, self.embed, ids, first, None if mm is None else mm["mm_mask"],
+                    None if mm is None else self._scatter_mm(mm, len(ids)), spk)
+                done_now = rid in self._done
+                new_streams.append(gen.add_stream(rid, pre, trail, pad_e, eos_e, thinker_done=done_now,
+                                                  max_frames=self.max_frames))
+            if new_streams:
+                self._emit(new_streams, gen.prefill(new_streams))
+            # trailing text from newly arrived thinker tokens (one batched projection)
+            if pending_tokens:
+                rids = list(pending_tokens)
+                flat = [t for r in rids for t in pending_tokens[r]]
+                proj = self.talker.project_text(self.embed[torch.tensor(flat, device=self.device)])
+                o = 0
+                for r in rids:
+                    n = len(pending_tokens[r])
+                    gen.push_trailing(r, proj[o:o + n], done=False)
+                    o += n
+            for rid in done:
+                gen.push_trailing(rid, None, done=True)
+            ready = [s for s in gen.ready_streams() if len(self._pending) and s.rid in self._pending]
+            if ready:
+                self._emit(ready, gen.step(ready))
+
+    def _scatter_mm(self, mm, L):
+        full = torch.zeros(L, mm["mm_hidden"].shape[-1], dtype=mm["mm_hidden"].dtype, device=self.device)
+        mask = mm["mm_mask"][:L]
+        full[mask.to(self.device)] = mm["mm_hidden"].to(self.device)[: int(mask.sum())]
+        return full
+
+    def _has_work(self) -> bool:
+        if self._aborted or self._done:
+            return True
+        if any(self._tokens.get(rid) for rid, *_ in self._new):
+            return True
+        if any(self._tokens.get(rid) for rid in self.gen.streams):
+            return True
+        return bool(self.gen.ready_streams())
+
+
+def create_talker_executor(model_path: str = "", device: str = "cuda:0", max_streams: int = 64,
+                           overrides: dict | None = None, use_graphs: bool = True, tail_frames: int = 50,
+                           max_frames: int = 4096):
+    return TalkerStreamingExecutor(model_path, device, max_streams, overrides=overrides, use_graphs=use_graphs,
+                                   tail_frames=tail_frames, max_frames=max_frames)
+
+
+# ----------------------------------------------------------------------------- code2wav
+class Code2WavStreamingExecutor(ResultQueueMixin, Executor):
+    """Incremental vocoding of every active stream; emits float32 PCM chunks
+    (12.5 Hz frames -> 24 kHz) to the client as they are produced."""
+
+    def __init__(self, model_path: str, device: str, chunk: int = 10, left_context: int = 25,
+                 first_chunk: int | None = None, overrides: dict | None = None):
+        super().__init__()
+        dev = torch.device(device)
+        self.model = loader.get_code2wav(model_path, dev, overrides)
+        self.sc = StreamingCode2Wav(self.model, chunk, left_context, first_chunk)
+        self._streams: dict[str, asyncio.Queue] = {}
+        self._audio: dict[str, list] = {}
+        self._lock = asyncio.Lock()
+
+    async def add_request(self, payload: StagePayload) -> None:
+        rid = payload.request_id
+        self._streams[rid] = asyncio.Queue()
+        self._audio[rid] = []
+        asyncio.ensure_future(self._run(payload))
+
+    def stream(self, request_id: str):
+        q = self._streams.get(request_id)
+        if q is None:
+            return None
+
+        async def gen():
+            while True:
+                item = await q.get()
+                if item is None:
+                    return
+                yield item
+
+        return gen()
+
+    async def _decode(self, rid: str, final: bool):
+        async with self._lock:  # one vocoder forward at a time on this GPU
+            out = await asyncio.to_thread(self.sc.decode_ready, [rid], final)
+        for r, wav in out.items():
+            a = wav.float().cpu().numpy()
+            self._audio[r].append(a)
+            q = self._streams.get(r)
+            if q is not None:
+                q.put_nowait({"modality": "audio", "audio_waveform": a, "sample_rate": SAMPLE_RATE_OUT,
+                              "t": time.perf_counter()})
+
+    async def _run(self, payload: StagePayload):
+        rid = payload.request_id
+        try:
+            while True:
+                item = await self._mailbox.get(rid)
+                if item is None or item.data.get("eos"):
+                    break
+                self.sc.add_codes(rid, torch.tensor(item.data["codes"], dtype=torch.long))
+                if self.sc.ready(rid):
+                    await self._decode(rid, final=False)
+            await self._decode(rid, final=True)
+            audio = np.concatenate(self._audio.pop(rid)) if self._audio.get(rid) else np.zeros(0, np.float32)
+            self._results().put_nowait(StagePayload(rid, payload.request,
+                                                    {"audio_waveform": audio, "sample_rate": SAMPLE_RATE_OUT}))
+        except asyncio.CancelledError:
+            raise
+        except Exception as exc:
+            self._results().put_nowait(StageError(rid, f"code2wav: {exc}"))
+        finally:
+            self.sc.close(rid)
+            q = self._streams.pop(rid, None)
+            if q is not None:
+                q.put_nowait(None)
+
+    async def abort(self, request_id: str) -> None:
+        self.sc.close(request_id)
+        q = self._streams.pop(request_id, None)
+        if q is not None:
+            q.put_nowait(None)
+
+
+def create_code2wav_executor(model_path: str = "", device: str = "cuda:0", chunk: int = 10,
+                             left_context: int = 25, first_chunk: int | None = None, overrides: dict | None = None):
+    return Code2WavStreamingExecutor(model_path, device, chunk, left_context, first_chunk, overrides)

@@ -184,7 +184,8 @@ class SpeechGenerator:
 
     def __init__(self, talker: Qwen3OmniTalker, thinker_embed: torch.Tensor, max_streams: int = 64,
                  max_context: int = 2048, max_trailing: int = 1024, use_graphs: bool = True,
-                 talker_sampling=(0.9, 50, 1.0, 1.05), cp_sampling=(1.0, 50, 0.8), seed: int = 0):
+                 talker_sampling=(0.9, 50, 1.0, 1.05), cp_sampling=(1.0, 50, 0.8), seed: int = 0,
+                 tail_frames: int = 50):
         self.talker = talker
         self.thinker_embed = thinker_embed
         tc, cc = talker.lm.cfg, talker.cp.cfg
@@ -207,6 +208,9 @@ class SpeechGenerator:
         self.trail_idx = torch.zeros(S, dtype=torch.long, device=dev)
         self.pad_embed = torch.zeros(H, dtype=tc.dtype, device=dev)
         self.max_trailing = max_trailing
+        # after the thinker finished and its text is consumed, a stream that
+        # has not produced the codec EOS stops after tail_frames more frames
+        self.tail_frames = tail_frames
         # sampling state (talker: rows = slots; CP: rows = slots, 15 groups share it)
         t, k, p, rep = talker_sampling
         self.t_st = SamplingTensors(torch.full((S,), t, device=dev), torch.full((S,), k, dtype=torch.int32, device=dev),
@@ -270,6 +274,7 @@ class SpeechGenerator:
             if st.trailing_len < self.max_trailing:
                 self.trail[st.slot, st.trailing_len] = self._eos_embed
                 st.trailing_len += 1
+            st.max_frames = min(st.max_frames, st.trailing_len + self.tail_frames)
 
     def remove(self, rid: str) -> None:
         st = self.streams.pop(rid, None)

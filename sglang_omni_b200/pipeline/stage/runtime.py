@@ -18,8 +18,8 @@ import asyncio
 import logging
 import os
 
-from ...proto import (AbortMessage, DataReadyMessage, ProfilerStartMessage, ProfilerStopMessage, ShutdownMessage,
-                      SubmitMessage)
+from ...proto import (AbortMessage, CompleteMessage, DataReadyMessage, ProfilerStartMessage, ProfilerStopMessage,
+                      ShutdownMessage, SubmitMessage)
 from ..control_plane import StageControlPlane
 from ..worker.data_plane import DataPlaneAdapter
 from .input import DirectInput, InputHandler
@@ -77,8 +77,15 @@ class Stage:
                     break
                 try:
                     await self._handle_message(msg)
-                except Exception:
+                except Exception as exc:
                     log.exception("stage %s failed to handle %s", self.name, type(msg).__name__)
+                    rid = getattr(msg, "request_id", None)
+                    if rid is not None:  # fail only this request (fail-fast at the coordinator)
+                        try:
+                            await self.cp.send_to_coordinator(CompleteMessage(
+                                rid, self.name, False, None, f"{self.name}: {type(exc).__name__}: {exc}"))
+                        except Exception:
+                            log.exception("could not report the failure of %s", rid)
         finally:
             for t in self._tasks:
                 t.cancel()

@@ -94,6 +94,7 @@ class Worker:
                     fut.set_exception(exc)
                 else:
                     log.exception("executor error without a request id in stage %s", self.stage_name)
+                    await asyncio.sleep(0.1)
 
     # ------------------------------------------------------------------ streaming
     def _stream_fn(self, request_id: str, data: Any, target_stage: str | None = None, metadata: dict | None = None):
