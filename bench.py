@@ -39,7 +39,64 @@ def parse():
     ap.add_argument("--output-len", type=int, default=256)
     ap.add_argument("--layers", type=int, default=48, help="only for quick local checks; the headline uses 48")
     ap.add_argument("--max-prefill-tokens", type=int, default=8192)
+    ap.add_argument("--speech", type=int, default=1, help="also measure p50 time-to-first-audio-chunk (speech pipeline)")
+    ap.add_argument("--speech-streams", type=int, default=32)
+    ap.add_argument("--speech-tokens", type=int, default=256)
+    ap.add_argument("--speech-audio-s", type=float, default=10.0)
     return ap.parse_args()
+
+
+def speech_phase(args, dev, rank):
+    """Qwen3-Omni speech-in / speech-out through the public Client API: N
+    concurrent streams of Gaussian-noise audio (sigma 0.1, 16 kHz) -> audio
+    tower -> thinker -> talker + code predictor -> streaming Code2Wav.
+    Returns (p50 time-to-first-audio-chunk ms, text tok/s, frames/s, bytes in)."""
+    import asyncio
+
+    import numpy as np
+
+    from sglang_omni_b200.client import Client, GenerateRequest, SamplingParams
+    from sglang_omni_b200.config import PipelineRunner, compile_pipeline
+    from sglang_omni_b200.models.qwen3_omni.config import Qwen3OmniSpeechPipelineConfig, text_stages
+
+    cfg = Qwen3OmniSpeechPipelineConfig(model_path="random", stages=text_stages(
+        device=str(dev), max_batch=args.speech_streams, max_context=2048, speech=True, tail_frames=50))
+    rng = np.random.default_rng(7 + rank)
+    n = int(16000 * args.speech_audio_s)
+    audios = [(rng.standard_normal(n) * 0.1).astype(np.float32) for _ in range(args.speech_streams)]
+
+    async def run():
+        coord, stages = compile_pipeline(cfg)
+        async with PipelineRunner(coord, stages):
+            client = Client(coord)
+
+            async def one(i, tag):
+                t0 = time.perf_counter()
+                req = GenerateRequest(prompt="Describe the audio.", audios=[audios[i]],
+                                      max_tokens=args.speech_tokens,
+                                      sampling=SamplingParams(temperature=0.0, ignore_eos=True),
+                                      output_modalities=["text", "audio"], stream=True,
+                                      request_id=f"{tag}-{rank}-{i}")
+                first_audio, ntok, frames = None, 0, 0
+                async for ch in client.generate(req):
+                    if ch.finish_reason is not None:
+                        continue
+                    if ch.modality == "audio":
+                        if first_audio is None:
+                            first_audio = time.perf_counter() - t0
+                        frames += 1
+                    elif ch.token_ids:
+                        ntok += len(ch.token_ids)
+                return first_audio, ntok
+
+            await asyncio.gather(*[one(i, "sw") for i in range(min(4, args.speech_streams))])
+            t0 = time.perf_counter()
+            res = await asyncio.gather(*[one(i, "s") for i in range(args.speech_streams)])
+            wall = time.perf_counter() - t0
+            ttfa = sorted(r[0] for r in res if r[0] is not None)
+            return (1e3 * statistics.median(ttfa) if ttfa else None, sum(r[1] for r in res) / wall, n * 4)
+
+    return asyncio.run(run())
 
 
 class ClockSampler:
@@ -134,8 +191,10 @@ def main():
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=600))
     _ext.ext()  # fail loudly without the kernels
 
+    from sglang_omni_b200.models.qwen3_omni import loader
+
     cfg = thinker_text_config(num_layers=args.layers)
-    model = DecoderLM(cfg, device=dev).random_init_(seed=0)
+    model = loader.get_thinker("random", dev, {"thinker": {"num_layers": args.layers}} if args.layers != 48 else None)
     max_ctx = ((args.prompt_len + args.output_len + 63) // 64) * 64
     pages_needed = args.requests * (max_ctx // 64) + 64
     pool = KVPool(cfg.num_layers, cfg.num_kv_heads, cfg.head_dim, pages_needed + 1, dev)
@@ -189,6 +248,15 @@ def main():
         ms_max, tokens_total, wall_max = ms, float(out_tokens), wall
     value = tokens_total / (ms_max / 1e3)
     e2e = tokens_total / wall_max
+    ttfa_ms = speech_tok_s = None
+    if args.speech and args.layers == 48:
+        del eng, pool
+        torch.cuda.empty_cache()
+        ttfa_ms, speech_tok_s, _ = speech_phase(args, dev, rank)
+        if world > 1:
+            tt = torch.tensor([ttfa_ms or 0.0], dtype=torch.float64, device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            ttfa_ms = float(tt[0])
     if rank == 0:
         line = {
             "metric": "output tok/s + p50 time-to-first-audio-chunk, Qwen3-Omni-30B-A3B, 1/2/4/8 B200",
@@ -212,8 +280,15 @@ def main():
                 "step": "one serving round: 64 requests x (1024 prompt -> 256 greedy tokens) per GPU",
                 "l2": "inputs larger than L2 (61 GB of weights streamed per decode step)",
                 "ttft_p50_ms": round(1e3 * statistics.median(ttfts), 2),
-                "ttfa_p50_ms": None,
+                "ttfa_p50_ms": None if ttfa_ms is None else round(ttfa_ms, 2),
+                "speech": None if ttfa_ms is None else {
+                    "streams_per_gpu": args.speech_streams, "audio_in_s": args.speech_audio_s,
+                    "text_tokens": args.speech_tokens, "chunk_frames": 10, "frame_hz": 12.5,
+                    "text_tok_s_per_gpu": round(speech_tok_s, 2),
+                    "timing": "host wall clock from Client.generate to the first audio SSE chunk (p50 over streams), "
+                              "max over ranks"},
             },
+            "ttfa_p50_ms": None if ttfa_ms is None else round(ttfa_ms, 2),
             "e2e": {"value": round(e2e, 2), "unit": "output tokens/s, host wall clock through AREngine.generate",
                     "h2d_bytes_per_step": int(args.requests * args.prompt_len * 4),
                     "d2h_bytes_per_step": int(args.requests * args.output_len * 4)},

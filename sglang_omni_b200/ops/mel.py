@@ -65,10 +65,13 @@ class LogMel:
             k = torch.arange(N_FFT // 2 + 1, dtype=torch.float64)
             ang = 2 * math.pi * k[:, None] * n[None, :] / N_FFT
             win = torch.hann_window(N_FFT, periodic=True, dtype=torch.float64)
-            basis = torch.cat([torch.cos(ang) * win, -torch.sin(ang) * win], 0)  # [402, 400]
-            self.basis = torch.zeros(512, 400, dtype=torch.float64)
-            self.basis[:402] = basis
-            self.basis = self.basis.to(self.device, torch.bfloat16)
+            basis = torch.zeros(512, 400, dtype=torch.float64)
+            basis[:402] = torch.cat([torch.cos(ang) * win, -torch.sin(ang) * win], 0)  # [402, 400]
+            # bf16 hi/lo split of the basis: with the input split the same way one
+            # GEMM over K = [x_hi | x_hi | x_lo] . [b_hi | b_lo | b_hi] keeps ~16-bit accuracy
+            b_hi = basis.to(torch.bfloat16)
+            b_lo = (basis - b_hi.double()).to(torch.bfloat16)
+            self.basis = torch.cat([b_hi, b_lo, b_hi], 1).to(self.device)  # [512, 1200]
             fb = torch.zeros(n_mels, 208, dtype=torch.float32)
             fb[:, :201] = self.filters.cpu()
             self.fb = fb.to(self.device, torch.bfloat16)
@@ -85,7 +88,10 @@ class LogMel:
             frames = x.unfold(0, N_FFT, HOP)[:-1]  # [T, 400]
             # scale into bf16 range well away from underflow, undo after squaring
             scale = float(frames.abs().max().clamp_min(1e-8))
-            spec = linear((frames / scale).to(torch.bfloat16).contiguous(), self.basis, out_dtype=torch.float32)
+            f = frames / scale
+            f_hi = f.to(torch.bfloat16)
+            f_lo = (f - f_hi.float()).to(torch.bfloat16)
+            spec = linear(torch.cat([f_hi, f_hi, f_lo], 1).contiguous(), self.basis, out_dtype=torch.float32)
             re, im = spec[:, :201], spec[:, 201:402]
             power = (re * re + im * im) * (scale * scale)  # [T, 201]
             p = torch.zeros(power.shape[0], 208, dtype=torch.float32, device=self.device)
