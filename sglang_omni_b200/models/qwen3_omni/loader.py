@@ -130,6 +130,25 @@ def get_audio_encoder(model_path: str, device, overrides: dict | None = None) ->
         return m
 
 
+def get_vision_encoder(model_path: str, device, overrides: dict | None = None):
+    from .vision_encoder import Qwen3OmniVisionEncoder, VisionConfig
+
+    k = _key(model_path, "vision", device, overrides)
+    with _LOCK:
+        if k in _CACHE:
+            return _CACHE[k]
+        cfg = VisionConfig()
+        cfg.out_hidden_size = _apply(_cfgs(model_path)["thinker"], (overrides or {}).get("thinker")).hidden_size
+        _apply(cfg, (overrides or {}).get("vision"))
+        m = Qwen3OmniVisionEncoder(cfg, device)
+        if has_checkpoint(model_path):
+            m.load_hf_state_dict(load_by_prefix(model_path, "thinker.visual."))
+        else:
+            m.random_init_(seed=SEEDS["vision"])
+        _CACHE[k] = m
+        return m
+
+
 def get_code2wav(model_path: str, device, overrides: dict | None = None) -> Code2Wav:
     k = _key(model_path, "code2wav", device, overrides)
     with _LOCK:

@@ -58,6 +58,29 @@ def _speech_requested(params: dict) -> bool:
 
 
 # ----------------------------------------------------------------------------- preprocessing
+def _load_image(item: Any) -> np.ndarray:
+    """uint8 RGB [H, W, 3] from an array / nested list / PIL image / path / base64 (PNG/JPEG via PIL)."""
+    if isinstance(item, dict):
+        item = item.get("url") or item.get("image") or item.get("data")
+    if isinstance(item, str):
+        from PIL import Image
+
+        if item.startswith("data:"):
+            item = item.split(",", 1)[1]
+        try:
+            raw = base64.b64decode(item, validate=True)
+            img = Image.open(io.BytesIO(raw))
+        except Exception:
+            img = Image.open(item)
+        item = np.asarray(img.convert("RGB"))
+    arr = np.asarray(item)
+    if arr.dtype != np.uint8:
+        arr = np.clip(arr, 0, 255).astype(np.uint8)
+    if arr.ndim == 2:
+        arr = np.repeat(arr[..., None], 3, -1)
+    return arr
+
+
 def _load_audio(item: Any) -> torch.Tensor:
     """Waveform at 16 kHz from an array / list / {"array", "sampling_rate"} / wav path / base64 wav."""
     sr = SAMPLE_RATE_IN
@@ -93,20 +116,35 @@ def create_preprocessing_executor(model_path: str = "", overrides: dict | None =
         full, rem = divmod(frames, cs)
         return full * cnn_out_len(cs) + (cnn_out_len(rem) if rem else 0)
 
+    from ..vision_encoder import VisionConfig
+
+    vcfg = VisionConfig()
+    unit = vcfg.patch_size * vcfg.spatial_merge_size
+
     def preprocess(payload: StagePayload) -> StagePayload:
         inp = payload.request.inputs if isinstance(payload.request.inputs, dict) else {}
         waves = [_load_audio(a) for a in (inp.get("audios") or [])]
         counts = [audio_tokens(w.numel()) for w in waves]
-        if inp.get("prompt_token_ids") is not None and not waves:
+        images = [_load_image(im) for im in (inp.get("images") or [])]
+        grids = []
+        for im in images:
+            th = max(unit, round(im.shape[0] / unit) * unit)
+            tw = max(unit, round(im.shape[1] / unit) * unit)
+            grids.append((1, th // unit, tw // unit))
+        if inp.get("prompt_token_ids") is not None and not waves and not images:
             ids = list(inp["prompt_token_ids"])
             p = torch.arange(len(ids), dtype=torch.int32)
             pos, delta, spans = torch.stack([p, p, p]), 0, []
         else:
-            lay = build_prompt(tok, inp.get("messages"), inp.get("prompt"), counts)
+            lay = build_prompt(tok, inp.get("messages"), inp.get("prompt"), counts, image_grids=grids)
             ids = lay.ids
             pos, delta = mrope_positions(lay)
             spans = lay.audio_spans
+            image_spans = lay.image_spans
+        if inp.get("prompt_token_ids") is not None and not waves and not images:
+            image_spans = []
         data = {"prompt_token_ids": ids, "audio_waveforms": waves, "audio_spans": spans,
+                "images": images, "image_spans": image_spans,
                 "mrope_positions": pos, "mrope_delta": delta,
                 "speech": _speech_requested(payload.request.params or {})}
         return StagePayload(payload.request_id, payload.request, data)
@@ -191,17 +229,25 @@ def create_thinker_executor(model_path: str = "", device: str = "cuda:0", max_ba
                         max_new_tokens=sp.max_new_tokens or 256)
         req.mrope_positions = d.get("mrope_positions")
         req.mrope_delta = int(d.get("mrope_delta") or 0)
-        aud = d.get("audio_embeds")
+        aud = d.get("audio_embeds") or []
         spans = d.get("audio_spans") or []
-        if aud:
+        img = d.get("image_embeds") or []
+        img_spans = d.get("image_spans") or []
+        if aud or img:
             mm_index = torch.full((len(ids),), -1, dtype=torch.int32)
-            base = 0
-            for (a, b), emb in zip(spans, aud):
+            base, mats = 0, []
+            for (a, b), emb in list(zip(spans, aud)) + list(zip(img_spans, img)):
                 n = min(b - a, emb.shape[0])
                 mm_index[a:a + n] = torch.arange(base, base + n, dtype=torch.int32)
                 base += emb.shape[0]
+                mats.append(emb)
             req.mm_index = mm_index
-            req.mm_embeds = torch.cat(list(aud), 0)
+            req.mm_embeds = torch.cat(mats, 0)
+        ds = d.get("deepstack")
+        if ds and img_spans:
+            pos = torch.cat([torch.arange(a, b) for a, b in img_spans])
+            req.deepstack = [torch.cat(list(layer), 0) for layer in ds]
+            req.ds_positions = pos
         speech = bool(d.get("speech")) and speech_target is not None
         if speech:
             req.capture_prompt_layer = accept if aud else None

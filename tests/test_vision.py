@@ -1,0 +1,65 @@
+"""Vision tower against transformers' Qwen3OmniMoeVisionEncoder on CPU."""
+import numpy as np
+import pytest
+import torch
+
+from sglang_omni_b200.models.qwen3_omni.vision_encoder import Qwen3OmniVisionEncoder, VisionConfig, image_to_patches
+
+hf = pytest.importorskip("transformers.models.qwen3_omni_moe.modeling_qwen3_omni_moe")
+hfc = pytest.importorskip("transformers.models.qwen3_omni_moe.configuration_qwen3_omni_moe")
+
+
+def tiny():
+    cfg = hfc.Qwen3OmniMoeVisionEncoderConfig(depth=3, hidden_size=64, intermediate_size=96, num_heads=4,
+                                              patch_size=4, spatial_merge_size=2, temporal_patch_size=2,
+                                              out_hidden_size=40, num_position_embeddings=64,
+                                              deepstack_visual_indexes=[0, 2])
+    cfg._attn_implementation = "eager"
+    torch.manual_seed(0)
+    m = hf.Qwen3OmniMoeVisionEncoder(cfg).eval()
+    with torch.no_grad():
+        for n, p in m.named_parameters():
+            p.copy_(torch.randn_like(p) * (0.1 if p.dim() > 1 else 0.02) + (1.0 if ("norm" in n or "ln" in n)
+                                                                             and n.endswith("weight") else 0.0))
+    ours = Qwen3OmniVisionEncoder(VisionConfig(depth=3, hidden_size=64, intermediate_size=96, num_heads=4,
+                                               patch_size=4, out_hidden_size=40, num_position_embeddings=64,
+                                               deepstack_visual_indexes=[0, 2], dtype=torch.float32))
+    ours.load_hf_state_dict(m.state_dict())
+    return m, ours
+
+
+def test_vision_matches_hf_cpu():
+    m, ours = tiny()
+    rng = np.random.default_rng(0)
+    imgs = [rng.integers(0, 256, (16, 24, 3), dtype=np.uint8), rng.integers(0, 256, (8, 8, 3), dtype=np.uint8)]
+    patches, grids = zip(*[image_to_patches(im, ours.cfg) for im in imgs])
+    px = torch.cat(patches, 0)
+    grid = torch.tensor(grids)
+    with torch.no_grad():
+        ref = m(px, grid_thw=grid)
+        out, ds = ours(px, list(grids))
+    ref_main = ref.pooler_output if getattr(ref, "pooler_output", None) is not None else ref.last_hidden_state
+    ref_ds = ref.deepstack_features
+    assert out.shape == ref_main.shape
+    assert (out - ref_main).abs().max() / ref_main.abs().max() < 1e-3
+    for a, b in zip(ds, ref_ds):
+        assert (a - b).abs().max() / b.abs().max() < 1e-3
+
+
+@pytest.mark.gpu
+def test_vision_gpu_matches_cpu_head_dim_72():
+    """head_dim 72 (the real tower's) runs as 80 in the attention kernel."""
+    cfg = dict(depth=2, hidden_size=288, intermediate_size=512, num_heads=4, out_hidden_size=256,
+               deepstack_visual_indexes=[0])
+    cpu = Qwen3OmniVisionEncoder(VisionConfig(**cfg, dtype=torch.float32)).random_init_(seed=2, std=0.05)
+    gpu = Qwen3OmniVisionEncoder(VisionConfig(**cfg), device="cuda")
+    with torch.no_grad():
+        for (n, a), (_, b) in zip(cpu.named_parameters(), gpu.named_parameters()):
+            b.copy_(a.to(b.dtype))
+    rng = np.random.default_rng(1)
+    img = rng.integers(0, 256, (128, 96, 3), dtype=np.uint8)
+    px, grid = image_to_patches(img, cpu.cfg)
+    ref, ref_ds = cpu(px, [grid])
+    out, ds = gpu(px, [grid])
+    assert (out.float().cpu() - ref).abs().max() / ref.abs().max() < 0.05
+    assert (ds[0].float().cpu() - ref_ds[0]).abs().max() / ref_ds[0].abs().max() < 0.05
