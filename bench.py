@@ -43,6 +43,8 @@ def parse():
     ap.add_argument("--speech-streams", type=int, default=32)
     ap.add_argument("--speech-tokens", type=int, default=256)
     ap.add_argument("--speech-audio-s", type=float, default=10.0)
+    ap.add_argument("--count-launches", type=int, default=1, help="count kernel launches in one extra untimed round")
+    ap.add_argument("--thinker", type=int, default=1, help="run the thinker serving phase (headline value)")
     return ap.parse_args()
 
 
@@ -143,6 +145,27 @@ class ClockSampler:
                 "reasons": reasons}
 
 
+def count_launches(fn):
+    """Kernel launches of one call of ``fn``, counted from CUPTI kernel records
+    (CUDA-graph replays included) in a separate, untimed pass.  Returns
+    (launches of this repository's kernels, all kernel launches)."""
+    import torch
+    from torch.autograd import DeviceType
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    ours = total = 0
+    for e in prof.events():
+        if e.device_type != DeviceType.CUDA or "memcpy" in e.name.lower() or "memset" in e.name.lower():
+            continue
+        total += 1
+        if "omni::" in e.name:
+            ours += 1
+    return ours, total
+
+
 def reference_arm(args):
     ref = os.path.join(ROOT, "baseline", "_ref")
     why = None
@@ -192,6 +215,15 @@ def main():
     _ext.ext()  # fail loudly without the kernels
 
     from sglang_omni_b200.models.qwen3_omni import loader
+
+    if not args.thinker:  # speech phase alone (a quick check; no headline value)
+        ttfa_ms, speech_tok_s, _ = speech_phase(args, dev, rank)
+        if rank == 0:
+            print(json.dumps({"metric": "p50 time-to-first-audio-chunk", "ttfa_p50_ms": ttfa_ms,
+                              "speech_text_tok_s": speech_tok_s, "streams": args.speech_streams, "impl": "ours"}))
+        if world > 1:
+            dist.destroy_process_group()
+        return
 
     cfg = thinker_text_config(num_layers=args.layers)
     model = loader.get_thinker("random", dev, {"thinker": {"num_layers": args.layers}} if args.layers != 48 else None)
@@ -248,6 +280,10 @@ def main():
         ms_max, tokens_total, wall_max = ms, float(out_tokens), wall
     value = tokens_total / (ms_max / 1e3)
     e2e = tokens_total / wall_max
+    launches = None
+    if args.count_launches:
+        ours, total = count_launches(lambda: round_("count"))
+        launches = {"ours_per_step": ours, "all_per_step": total}
     ttfa_ms = speech_tok_s = None
     if args.speech and args.layers == 48:
         del eng, pool
@@ -292,7 +328,10 @@ def main():
             "e2e": {"value": round(e2e, 2), "unit": "output tokens/s, host wall clock through AREngine.generate",
                     "h2d_bytes_per_step": int(args.requests * args.prompt_len * 4),
                     "d2h_bytes_per_step": int(args.requests * args.output_len * 4)},
-            "gpu_launches": None,
+            "gpu_launches": None if launches is None else launches["ours_per_step"] * args.steps,
+            "gpu_launches_detail": None if launches is None else dict(
+                launches, how="CUPTI kernel records of one extra untimed round (graph replays included); "
+                              "ours = kernels of the omni:: namespace in sglang_omni_b200/_C"),
             "clocks": clk.summary(),
             "impl": "ours",
         }

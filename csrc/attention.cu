@@ -304,6 +304,15 @@ __global__ void __launch_bounds__(128) prefill_kernel(const PrefillParams p) {
 // Split-KV decode: grid (splits, Hkv, B); the G heads of a KV head are the rows
 // of one 16-row MMA tile; each warp takes 16 keys of every 64-key tile.
 // ---------------------------------------------------------------------------
+// Keys per split for one request: the configured split size, widened (in
+// whole pages) when the context would need more than max_splits splits, so a
+// request never writes or reads partials past its max_splits slots.
+__device__ __forceinline__ int split_keys(int kv_len, int keys_per_split, int max_splits) {
+  const int need = (kv_len + max_splits - 1) / max_splits;
+  const int need_pages = (need + kPage - 1) / kPage * kPage;
+  return need_pages > keys_per_split ? need_pages : keys_per_split;
+}
+
 struct DecodeParams {
   const __nv_bfloat16* q;
   int64_t q_stride;
@@ -334,10 +343,11 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int G = p.hq / p.hkv;
   const int kv_len = p.kv_lens[b];
-  const int k_begin = split * p.keys_per_split;
+  const int kps = split_keys(kv_len, p.keys_per_split, p.max_splits);
+  const int k_begin = split * kps;
   if (k_begin >= kv_len) return;
-  const int k_end = min(kv_len, k_begin + p.keys_per_split);
-  const int nsplit = (kv_len + p.keys_per_split - 1) / p.keys_per_split;
+  const int k_end = min(kv_len, k_begin + kps);
+  const int nsplit = (kv_len + kps - 1) / kps;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const bool validA = g < G, validB = g + 8 < G;
@@ -506,7 +516,8 @@ template <int D>
 __global__ void decode_combine_kernel(const DecodeParams p) {
   const int head = blockIdx.x, b = blockIdx.y;
   const int kv_len = p.kv_lens[b];
-  const int nsplit = (kv_len + p.keys_per_split - 1) / p.keys_per_split;
+  const int kps = split_keys(kv_len, p.keys_per_split, p.max_splits);
+  const int nsplit = (kv_len + kps - 1) / kps;
   if (nsplit <= 1) return;
   const int64_t slot0 = (static_cast<int64_t>(b) * p.hq + head) * p.max_splits;
   float M = -INFINITY;

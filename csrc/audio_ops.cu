@@ -65,9 +65,11 @@ __global__ void conv1d_im2col_kernel(const __nv_bfloat16* __restrict__ x, __nv_b
 
 // y: [B, T, 2s, C] rows of the GEMM x @ W(c_in -> (j, c_out)); out: [B, (T-1)*s, C]
 // out[u] = y[u/s + 1, u%s] + y[u/s, u%s + s] + bias
+// Output sample u is sample f = u + shift of the full transposed conv
+// (length (T + 1) * s): full[f] = y[f / s][f % s] + y[f / s - 1][f % s + s].
 __global__ void conv_transpose_ola_kernel(const __nv_bfloat16* __restrict__ y, const __nv_bfloat16* __restrict__ bias,
-                                          __nv_bfloat16* __restrict__ out, int B, int T, int s, int C) {
-  const int T_out = (T - 1) * s;
+                                          __nv_bfloat16* __restrict__ out, int B, int T, int s, int C, int T_out,
+                                          int shift) {
   const int64_t total = static_cast<int64_t>(B) * T_out * C;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -75,11 +77,13 @@ __global__ void conv_transpose_ola_kernel(const __nv_bfloat16* __restrict__ y, c
     const int64_t bu = i / C;
     const int u = static_cast<int>(bu % T_out);
     const int b = static_cast<int>(bu / T_out);
-    const int t = u / s, j = u - (u / s) * s;
+    const int f = u + shift;
+    const int t = f / s, j = f - t * s;
     const int64_t base = static_cast<int64_t>(b) * T;
-    const float a0 = __bfloat162float(y[((base + t + 1) * (2 * s) + j) * C + c]);
-    const float a1 = __bfloat162float(y[((base + t) * (2 * s) + j + s) * C + c]);
-    out[i] = __float2bfloat16(a0 + a1 + (bias ? __bfloat162float(bias[c]) : 0.f));
+    float v = bias ? __bfloat162float(bias[c]) : 0.f;
+    if (t < T) v += __bfloat162float(y[((base + t) * (2 * s) + j) * C + c]);
+    if (t >= 1 && t - 1 < T) v += __bfloat162float(y[((base + t - 1) * (2 * s) + j + s) * C + c]);
+    out[i] = __float2bfloat16(v);
   }
 }
 
@@ -154,13 +158,14 @@ cudaError_t conv1d_im2col(const void* x, void* out, int B, int T_in, int T_out, 
   return cudaGetLastError();
 }
 
-cudaError_t conv_transpose_ola(const void* y, const void* bias, void* out, int B, int T, int s, int C,
-                               cudaStream_t stream) {
-  const int64_t n = static_cast<int64_t>(B) * (T - 1) * s * C;
+cudaError_t conv_transpose_ola(const void* y, const void* bias, void* out, int B, int T, int s, int C, int T_out,
+                               int shift, cudaStream_t stream) {
+  if (shift < 0 || T_out + shift > (T + 1) * s) return cudaErrorInvalidValue;
+  const int64_t n = static_cast<int64_t>(B) * T_out * C;
   if (n <= 0) return cudaSuccess;
   conv_transpose_ola_kernel<<<grid_for(n), 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(y),
                                                              static_cast<const __nv_bfloat16*>(bias),
-                                                             static_cast<__nv_bfloat16*>(out), B, T, s, C);
+                                                             static_cast<__nv_bfloat16*>(out), B, T, s, C, T_out, shift);
   return cudaGetLastError();
 }
 

@@ -233,7 +233,7 @@ void qkv_rope_store(torch::Tensor& qkv, int64_t hq, int64_t hkv, int64_t head_di
   TORCH_CHECK(qkv.stride(-1) == 1, "qkv rows must be contiguous");
   TORCH_CHECK(positions.scalar_type() == at::kInt && positions.is_contiguous(), "positions int32");
   TORCH_CHECK(cos_tab.scalar_type() == at::kFloat && sin_tab.scalar_type() == at::kFloat, "fp32 rope tables");
-  TORCH_CHECK(rot_dim == 0 || !neox || (rot_dim / 2) % 32 == 0, "neox rotation needs rot_dim/2 % 32 == 0");
+  TORCH_CHECK(rot_dim % 2 == 0 && rot_dim <= head_dim, "rot_dim must be even and <= head_dim");
   const at::cuda::CUDAGuard guard(qkv.device());
   omni::RopeStoreArgs a{};
   a.qkv = qkv.data_ptr();
@@ -340,6 +340,44 @@ void embed(const torch::Tensor& ids, const torch::Tensor& table, torch::Tensor& 
   check_launch(omni::embed(a, at::cuda::getCurrentCUDAStream()), "embed");
 }
 
+void vq_embed(const c10::optional<torch::Tensor>& ids, const c10::optional<torch::Tensor>& slot,
+              const c10::optional<torch::Tensor>& slot_tokens, const torch::Tensor& table,
+              const torch::Tensor& codebooks, const torch::Tensor& codes, const c10::optional<torch::Tensor>& code_row,
+              int64_t sem_lo, int64_t sem_hi, int64_t cb_size, double scale, torch::Tensor& out) {
+  OMNI_CHECK_BF16(table);
+  OMNI_CHECK_BF16(codebooks);
+  OMNI_CHECK_BF16(out);
+  OMNI_CHECK_CONTIG(table);
+  OMNI_CHECK_CONTIG(codebooks);
+  OMNI_CHECK_CONTIG(out);
+  TORCH_CHECK(codes.scalar_type() == at::kInt && codes.dim() == 2 && codes.stride(1) == 1, "codes int32 [rows, ncb]");
+  TORCH_CHECK(ids.has_value() != slot.has_value(), "give ids or slot");
+  TORCH_CHECK(!slot.has_value() || slot_tokens.has_value(), "slot needs slot_tokens");
+  const int64_t tokens = ids.has_value() ? ids->numel() : slot->numel();
+  TORCH_CHECK(out.size(0) >= tokens && out.size(1) == table.size(1) && codebooks.size(1) == table.size(1),
+              "vq_embed shapes");
+  TORCH_CHECK(codebooks.size(0) >= codes.size(1) * cb_size, "codebook table too small");
+  const at::cuda::CUDAGuard guard(table.device());
+  omni::VqEmbedArgs a{};
+  a.ids = ids.has_value() ? ids->data_ptr<int>() : nullptr;
+  a.slot = slot.has_value() ? slot->data_ptr<int>() : nullptr;
+  a.slot_tokens = slot_tokens.has_value() ? slot_tokens->data_ptr<int>() : nullptr;
+  a.table = table.data_ptr();
+  a.codebooks = codebooks.data_ptr();
+  a.codes = codes.data_ptr<int>();
+  a.codes_stride = static_cast<int>(codes.stride(0));
+  a.code_row = code_row.has_value() ? code_row->data_ptr<int>() : nullptr;
+  a.sem_lo = static_cast<int>(sem_lo);
+  a.sem_hi = static_cast<int>(sem_hi);
+  a.ncb = static_cast<int>(codes.size(1));
+  a.cb_size = static_cast<int>(cb_size);
+  a.scale = static_cast<float>(scale);
+  a.out = out.data_ptr();
+  a.tokens = static_cast<int>(tokens);
+  a.hidden = static_cast<int>(table.size(1));
+  check_launch(omni::vq_embed(a, at::cuda::getCurrentCUDAStream()), "vq_embed");
+}
+
 void sample(torch::Tensor& logits, torch::Tensor& out_tokens, const c10::optional<torch::Tensor>& temperature,
             const c10::optional<torch::Tensor>& top_k, const c10::optional<torch::Tensor>& top_p,
             const c10::optional<torch::Tensor>& min_p, const c10::optional<torch::Tensor>& rep_penalty,
@@ -405,7 +443,7 @@ void conv1d_im2col(const torch::Tensor& x, torch::Tensor& out, int64_t K, int64_
 }
 
 void conv_transpose_ola(const torch::Tensor& y, const c10::optional<torch::Tensor>& bias, torch::Tensor& out,
-                        int64_t s) {
+                        int64_t s, int64_t shift) {
   OMNI_CHECK_CUDA(y);
   OMNI_CHECK_BF16(y);
   OMNI_CHECK_CONTIG(y);
@@ -416,7 +454,8 @@ void conv_transpose_ola(const torch::Tensor& y, const c10::optional<torch::Tenso
   const at::cuda::CUDAGuard guard(y.device());
   check_launch(omni::conv_transpose_ola(y.data_ptr(), bias.has_value() ? bias->data_ptr() : nullptr,
                                         out.data_ptr(), static_cast<int>(y.size(0)), static_cast<int>(y.size(1)),
-                                        static_cast<int>(s), static_cast<int>(C), at::cuda::getCurrentCUDAStream()),
+                                        static_cast<int>(s), static_cast<int>(C), static_cast<int>(out.size(1)),
+                                        static_cast<int>(shift), at::cuda::getCurrentCUDAStream()),
                "conv_transpose_ola");
 }
 
@@ -465,6 +504,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_route", &moe_route, "MoE top-k routing + permutation + gather");
   m.def("moe_combine", &moe_combine, "MoE top-k weighted combine (+ shared expert)");
   m.def("embed", &embed, "embedding gather with multimodal overwrite");
+  m.def("vq_embed", &vq_embed, "dual-AR input embedding with the scaled VQ codebook sum");
   m.def("sample", &sample, "fused logits processing + sampling");
   m.def("snake", &snake, "Snake / SnakeBeta activation (channels-last)");
   m.def("conv1d_im2col", &conv1d_im2col, "causal dilated conv1d im2col rows");

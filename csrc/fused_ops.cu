@@ -49,8 +49,9 @@ __device__ __forceinline__ int mrope_section(int j, const int* sec, int interlea
 }
 
 template <int D>
-__global__ void qkv_rope_store_kernel(RopeStoreArgs a) {
+__global__ void __launch_bounds__(256) qkv_rope_store_kernel(RopeStoreArgs a) {
   constexpr int PER = D / 32;  // elements per lane
+  __shared__ float rope_row[8 * D];  // one row per warp (neox with half % 32 != 0)
   const int warp_global = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   const int heads = a.hq + 2 * a.hkv;
@@ -90,14 +91,24 @@ __global__ void qkv_rope_store_kernel(RopeStoreArgs a) {
         pos3[0] = pos3[1] = pos3[2] = a.positions[tok];
       }
       float y[PER];
-      // Partner of element e = lane + 32 i: neox (half % 32 == 0) -> same lane,
-      // register i +- half/32; interleaved pairs -> lane ^ 1, same register.
+      // Partner of element e = lane + 32 i: neox with half % 32 == 0 -> same
+      // lane, register i +- half/32; neox otherwise -> through this warp's
+      // shared-memory copy of the row; interleaved pairs -> lane ^ 1.
       const int hs = half >> 5;
+      const bool neox_smem = a.neox && (half & 31) != 0;
+      float* srow = rope_row + (threadIdx.x >> 5) * D;
+      if (neox_smem) {
+#pragma unroll
+        for (int i = 0; i < PER; ++i) srow[lane + 32 * i] = x[i];
+        __syncwarp();
+      }
 #pragma unroll
       for (int i = 0; i < PER; ++i) {
         const int e = lane + 32 * i;
         float pv;
-        if (a.neox) {
+        if (neox_smem) {
+          pv = e < a.rot_dim ? srow[e < half ? e + half : e - half] : 0.f;
+        } else if (a.neox) {
           const int pi = e < half ? i + hs : i - hs;
           pv = 0.f;
 #pragma unroll
@@ -379,6 +390,65 @@ __global__ void embed_kernel(EmbedArgs a) {
 }
 
 // ---------------------------------------------------------------------------
+// Dual-AR input embedding with the VQ codebook sum (one CTA per token)
+// ---------------------------------------------------------------------------
+__global__ void vq_embed_kernel(VqEmbedArgs a) {
+  const int t = blockIdx.x;
+  const int s = a.slot ? a.slot[t] : -1;
+  const int id = a.slot ? a.slot_tokens[s] : a.ids[t];
+  int r;
+  bool vq;
+  if (a.code_row) {
+    r = a.code_row[t];
+    vq = r >= 0;
+  } else {
+    r = a.slot ? s : t;
+    vq = id >= a.sem_lo && id <= a.sem_hi;
+  }
+  const __nv_bfloat16* e = static_cast<const __nv_bfloat16*>(a.table) + static_cast<int64_t>(id) * a.hidden;
+  __nv_bfloat16* o = static_cast<__nv_bfloat16*>(a.out) + static_cast<int64_t>(t) * a.hidden;
+  const int nvec = a.hidden >> 3;
+  if (!vq) {
+    for (int v = threadIdx.x; v < nvec; v += blockDim.x)
+      reinterpret_cast<uint4*>(o)[v] = reinterpret_cast<const uint4*>(e)[v];
+    return;
+  }
+  __shared__ int rows[32];
+  if (threadIdx.x < a.ncb) {
+    int c = a.codes[static_cast<int64_t>(r) * a.codes_stride + threadIdx.x];
+    c = c < 0 ? 0 : (c >= a.cb_size ? a.cb_size - 1 : c);
+    rows[threadIdx.x] = threadIdx.x * a.cb_size + c;
+  }
+  __syncthreads();
+  const __nv_bfloat16* cb = static_cast<const __nv_bfloat16*>(a.codebooks);
+  for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int c = 0; c < a.ncb; ++c) {
+      const uint4 u = reinterpret_cast<const uint4*>(cb + static_cast<int64_t>(rows[c]) * a.hidden)[v];
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(h[j]);
+        acc[2 * j] += f.x;
+        acc[2 * j + 1] += f.y;
+      }
+    }
+    const uint4 ue = reinterpret_cast<const uint4*>(e)[v];
+    const __nv_bfloat162* he = reinterpret_cast<const __nv_bfloat162*>(&ue);
+    uint4 uo;
+    __nv_bfloat162* ho = reinterpret_cast<__nv_bfloat162*>(&uo);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(he[j]);
+      const float x0 = bf16r(bf16r(f.x + bf16r(acc[2 * j])) * a.scale);
+      const float x1 = bf16r(bf16r(f.y + bf16r(acc[2 * j + 1])) * a.scale);
+      ho[j] = __floats2bfloat162_rn(x0, x1);
+    }
+    reinterpret_cast<uint4*>(o)[v] = uo;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Sampling: one CTA (1024 threads) per row.
 // ---------------------------------------------------------------------------
 // SplitMix64 finaliser (Steele, Lea & Flood, OOPSLA 2014) as a counter-based hash.
@@ -562,7 +632,9 @@ cudaError_t qkv_rope_store(const RopeStoreArgs& a, cudaStream_t stream) {
   const int threads = 256;
   const long grid = (warps + 7) / 8;
   switch (a.head_dim) {
+    case 32: qkv_rope_store_kernel<32><<<grid, threads, 0, stream>>>(a); break;
     case 64: qkv_rope_store_kernel<64><<<grid, threads, 0, stream>>>(a); break;
+    case 96: qkv_rope_store_kernel<96><<<grid, threads, 0, stream>>>(a); break;
     case 128: qkv_rope_store_kernel<128><<<grid, threads, 0, stream>>>(a); break;
     default: return cudaErrorInvalidValue;
   }
@@ -592,6 +664,13 @@ cudaError_t moe_route(const MoeRouteArgs& a, cudaStream_t stream) {
 cudaError_t moe_combine(const MoeCombineArgs& a, cudaStream_t stream) {
   if (a.tokens == 0) return cudaSuccess;
   moe_combine_kernel<<<a.tokens, 256, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t vq_embed(const VqEmbedArgs& a, cudaStream_t stream) {
+  if (a.tokens == 0) return cudaSuccess;
+  if (a.hidden % 8 != 0 || a.ncb > 32 || a.ncb < 1) return cudaErrorInvalidValue;
+  vq_embed_kernel<<<a.tokens, 128, 0, stream>>>(a);
   return cudaGetLastError();
 }
 

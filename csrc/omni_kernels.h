@@ -166,6 +166,28 @@ struct EmbedArgs {
 };
 cudaError_t embed(const EmbedArgs& a, cudaStream_t stream);
 
+// Dual-AR (S2-Pro) input embedding: token embedding plus, at VQ positions, the
+// sum of one codebook embedding per codebook, scaled:
+//   out[t] = vq(t) ? bf16(bf16(E[id] + bf16(sum_c CB[c * cb_size + code_c])) * scale) : E[id]
+// Token id: slot_tokens[slot[t]] when slot != nullptr, else ids[t].
+// Code row r: code_row[t] when code_row != nullptr (r < 0: no VQ), else slot[t] or t;
+// without code_row, vq(t) holds for ids in [sem_lo, sem_hi].
+struct VqEmbedArgs {
+  const int* ids;
+  const int* slot;
+  const int* slot_tokens;
+  const void* table;       // [vocab, hidden] bf16
+  const void* codebooks;   // [ncb * cb_size, hidden] bf16
+  const int* codes;        // [rows, codes_stride] int32
+  int codes_stride;
+  const int* code_row;
+  int sem_lo, sem_hi, ncb, cb_size;
+  float scale;
+  void* out;
+  int tokens, hidden;
+};
+cudaError_t vq_embed(const VqEmbedArgs& a, cudaStream_t stream);
+
 struct SampleArgs {
   float* logits;           // [rows, vocab] fp32, processed in place
   int64_t logits_stride;
@@ -193,8 +215,8 @@ cudaError_t snake(const void* x, const float* alpha, const float* beta, void* y,
                   cudaStream_t stream);
 cudaError_t conv1d_im2col(const void* x, void* out, int B, int T_in, int T_out, int C, int K, int dil, int stride,
                           int pad_left, int out_row_stride, cudaStream_t stream);
-cudaError_t conv_transpose_ola(const void* y, const void* bias, void* out, int B, int T, int s, int C,
-                               cudaStream_t stream);
+cudaError_t conv_transpose_ola(const void* y, const void* bias, void* out, int B, int T, int s, int C, int T_out,
+                               int shift, cudaStream_t stream);
 cudaError_t dwconv1d_causal(const void* x, const float* w, const float* bias, void* out, int B, int T, int C, int K,
                             cudaStream_t stream);
 cudaError_t conv2d_im2col(const void* x, void* out, int N, int H, int W, int C, int Ho, int Wo, int kh, int kw,

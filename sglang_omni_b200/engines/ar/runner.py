@@ -19,6 +19,9 @@ import torch
 from ...models.decoder import DecoderLM, ForwardBatch
 from ...ops import prefill_tiles
 from ...ops.sampling import SamplingTensors, sample
+from ...environ import environ
+from ...utils.cuda_graph import capture_graph
+from ...utils.staging import PinnedRing
 from .kv_pool import KVPool
 from .request import ARRequest
 
@@ -65,14 +68,14 @@ class ARModelRunner:
         if not self.buckets or self.buckets[-1] < max_batch:
             self.buckets.append(max_batch)
         packed = 6 * max_batch + max_batch * self.max_pages
-        self.meta_host = torch.zeros(packed, dtype=torch.int32, pin_memory=self.is_cuda)
+        self.meta_ring = PinnedRing(packed, torch.int32, 2, self.is_cuda)
         self.meta_dev = torch.zeros(packed, dtype=torch.int32, device=dev)
         # two pinned token buffers: with overlap scheduling step N+1 is launched before step N is read
         self._tok_host = [torch.zeros(max(max_batch, 1024), dtype=torch.int32, pin_memory=self.is_cuda)
                           for _ in range(2)]
         self._tok_flip = 0
         self.builder = _rt.DecodeMetaBuilder(max_batch, self.max_pages) if _rt is not None else None
-        self.use_graphs = use_graphs and self.is_cuda
+        self.use_graphs = use_graphs and self.is_cuda and environ.OMNI_USE_CUDA_GRAPHS.get()
         self.graphs: dict[int, tuple] = {}
         self.capture_hidden = False
         self.hidden_out: dict[int, torch.Tensor] = {}
@@ -273,7 +276,7 @@ class ARModelRunner:
     def _fill_meta(self, reqs: list[ARRequest], PB: int):
         B = len(reqs)
         P = self.max_pages
-        host = self.meta_host.numpy()
+        host = self.meta_ring.next().numpy()
         kl = np.fromiter((r.num_cached for r in reqs), dtype=np.int64, count=B)
         md = np.fromiter((r.mrope_delta for r in reqs), dtype=np.int64, count=B)
         sl = np.fromiter((r.slot for r in reqs), dtype=np.int64, count=B)
@@ -294,30 +297,19 @@ class ARModelRunner:
             for i, r in enumerate(reqs):
                 host[6 * PB + i * P:6 * PB + i * P + len(r.pages)] = r.pages
         n = 6 * PB + PB * P
-        self.meta_dev[:n].copy_(self.meta_host[:n], non_blocking=True)
+        self.meta_ring.upload(self.meta_dev, n)
 
     @torch.no_grad()
     def capture(self, PB: int):
         if not self.use_graphs or PB in self.graphs:
             return
         # dummy-but-valid metadata: every row is padding (empty context, no cache write)
-        host = self.meta_host.numpy()
+        host = self.meta_ring.next().numpy()
         n = 6 * PB + PB * self.max_pages
         host[:n] = 0
         host[PB:2 * PB] = -1
-        self.meta_dev[:n].copy_(self.meta_host[:n])
-        s = torch.cuda.Stream()
-        s.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(s):
-            for _ in range(2):
-                self._decode_body(PB)
-        torch.cuda.current_stream().wait_stream(s)
-        torch.cuda.synchronize()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            out = self._decode_body(PB)
-        torch.cuda.synchronize()
-        self.graphs[PB] = (g, out)
+        self.meta_ring.upload(self.meta_dev, n, blocking=True)
+        self.graphs[PB] = capture_graph(lambda: self._decode_body(PB))
 
     @torch.no_grad()
     def decode(self, reqs: list[ARRequest]):

@@ -157,6 +157,7 @@ class DecoderLM(nn.Module):
         self.register_buffer("sin_tab", sin, persistent=False)
         self._moe_ws: MoEWorkspace | None = None
         self._dec_ws: DecodeWorkspace | None = None
+        self._retired_ws: list = []
 
     # ------------------------------------------------------------------ init
     @torch.no_grad()
@@ -179,14 +180,22 @@ class DecoderLM(nn.Module):
 
     # ------------------------------------------------------------------ workspaces
     def ensure_workspaces(self, max_tokens: int, max_batch: int, max_context: int):
+        """Grow the MoE / decode scratch to cover these sizes.
+
+        A replaced workspace is kept alive (``_retired_ws``): CUDA graphs that
+        were captured with it still read and write its memory on replay."""
         cfg, dev = self.cfg, self.embed.device
         if cfg.num_experts and (self._moe_ws is None or self._moe_ws.max_tokens < max_tokens):
+            if self._moe_ws is not None:
+                self._retired_ws.append(self._moe_ws)
             self._moe_ws = MoEWorkspace(max_tokens, cfg.num_experts, cfg.topk, cfg.hidden_size,
                                         cfg.moe_intermediate_size, dev, cfg.dtype)
         if dev.type == "cuda":
             ws = self._dec_ws
             need_splits = max(1, (max_context + 255) // 256)
             if ws is None or ws.max_splits < need_splits or ws.part_lse.numel() < max_batch * cfg.num_heads * need_splits:
+                if ws is not None:
+                    self._retired_ws.append(ws)
                 self._dec_ws = DecodeWorkspace(max_batch, cfg.num_heads, cfg.head_dim, max_context, dev)
 
     # ------------------------------------------------------------------ forward
@@ -198,14 +207,25 @@ class DecoderLM(nn.Module):
                 shared_out = ops.linear(ops.linear(x, L.s13, gated=True), L.s2)
                 if cfg.shared_expert_gate:
                     shared_gate = ops.linear(x, L.sgate, out_dtype=torch.float32)
+            if self._moe_ws is None:
+                self.ensure_workspaces(max(x.shape[0], 4096), 1, 64)
             ws = self._moe_ws
-            if ws is None or ws.max_tokens < x.shape[0]:
-                self.ensure_workspaces(x.shape[0], 1, 64)
-                ws = self._moe_ws
-            return ops.fused_moe(x, L.router, L.w13, L.w2, cfg.topk, ws, renormalize=cfg.norm_topk_prob,
-                                 mode=cfg.router_mode, bias=getattr(L, "router_bias", None), n_group=cfg.n_group,
-                                 topk_group=cfg.topk_group, scaling=cfg.routed_scaling_factor,
-                                 shared_out=shared_out, shared_gate=shared_gate)
+            T, step = x.shape[0], ws.max_tokens
+            if T <= step:
+                return ops.fused_moe(x, L.router, L.w13, L.w2, cfg.topk, ws, renormalize=cfg.norm_topk_prob,
+                                     mode=cfg.router_mode, bias=getattr(L, "router_bias", None), n_group=cfg.n_group,
+                                     topk_group=cfg.topk_group, scaling=cfg.routed_scaling_factor,
+                                     shared_out=shared_out, shared_gate=shared_gate)
+            # more tokens than the (graph-captured) workspace holds: run in chunks
+            out = torch.empty_like(x)
+            for a in range(0, T, step):
+                b = min(T, a + step)
+                ops.fused_moe(x[a:b], L.router, L.w13, L.w2, cfg.topk, ws, renormalize=cfg.norm_topk_prob,
+                              mode=cfg.router_mode, bias=getattr(L, "router_bias", None), n_group=cfg.n_group,
+                              topk_group=cfg.topk_group, scaling=cfg.routed_scaling_factor, out=out[a:b],
+                              shared_out=None if shared_out is None else shared_out[a:b],
+                              shared_gate=None if shared_gate is None else shared_gate[a:b])
+            return out
         return ops.linear(ops.linear(x, L.mlp13, gated=True), L.mlp2)
 
     def forward(self, fb: ForwardBatch, kv_cache: torch.Tensor) -> torch.Tensor:

@@ -35,6 +35,9 @@ from torch import nn
 from ... import ops
 from ...engines.ar.kv_pool import KVPool
 from ...ops.sampling import SamplingTensors, sample
+from ...environ import environ
+from ...utils.cuda_graph import capture_graph
+from ...utils.staging import PinnedRing
 from ..decoder import DecoderConfig, DecoderLM, ForwardBatch
 from .hf_config import code_predictor_config, talker_text_config
 
@@ -230,15 +233,14 @@ class SpeechGenerator:
         self.suppress = (tc.vocab_size - 1024, tc.vocab_size, self.sp.codec_eos)
         self.streams: dict[str, SpeechStream] = {}
         self.free_slots = list(range(S - 1, 0, -1))
-        self.use_graphs = use_graphs and dev.type == "cuda"
+        self.use_graphs = use_graphs and dev.type == "cuda" and environ.OMNI_USE_CUDA_GRAPHS.get()
         self.graphs: dict[int, tuple] = {}
         self.buckets = [b for b in (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128) if b <= max_streams]
         if self.buckets[-1] < max_streams:
             self.buckets.append(max_streams)
         PB = max_streams
-        self.meta_host = torch.zeros(6 * PB + PB * self.max_pages, dtype=torch.int32,
-                                     pin_memory=dev.type == "cuda")
-        self.meta_dev = torch.zeros_like(self.meta_host, device=dev)
+        self.meta_ring = PinnedRing(6 * PB + PB * self.max_pages, torch.int32, 2, dev.type == "cuda")
+        self.meta_dev = torch.zeros(6 * PB + PB * self.max_pages, dtype=torch.int32, device=dev)
         self.codes_out = torch.zeros(S, self.G, dtype=torch.int32, device=dev)
         try:
             from ... import _runtime as rt
@@ -250,6 +252,8 @@ class SpeechGenerator:
     def add_stream(self, rid: str, prefill_embeds: torch.Tensor, trailing: torch.Tensor, pad_e, eos_e,
                    thinker_done: bool = False, max_frames: int = 4096) -> SpeechStream:
         slot = self.free_slots.pop()
+        # the KV of prefill + one position per frame must fit the slot's pages
+        max_frames = max(1, min(max_frames, self.max_pages * 64 - prefill_embeds.shape[0]))
         st = SpeechStream(rid, slot, max_frames=max_frames)
         self.streams[rid] = st
         self.pad_embed.copy_(pad_e)
@@ -389,14 +393,14 @@ class SpeechGenerator:
         return self._talker_tail(hidden, slots, cp_bt, cp_base)
 
     def _fill_meta(self, streams, PB):
-        host = self.meta_host.numpy()
+        host = self.meta_ring.next().numpy()
         B = len(streams)
         kl = np.fromiter((s.num_cached for s in streams), dtype=np.int64, count=B)
         md = np.zeros(B, dtype=np.int64)
         sl = np.fromiter((s.slot for s in streams), dtype=np.int64, count=B)
         self.builder.build(host, [s.pages for s in streams], kl, md, sl, self.pool.allocator_native(), PB)
         n = 6 * PB + PB * self.max_pages
-        self.meta_dev[:n].copy_(self.meta_host[:n], non_blocking=True)
+        self.meta_ring.upload(self.meta_dev, n)
 
     @torch.no_grad()
     def step(self, streams: list[SpeechStream]):
@@ -418,24 +422,14 @@ class SpeechGenerator:
         return codes[:B]
 
     def _capture(self, PB):
-        host = self.meta_host.numpy()
+        host = self.meta_ring.next().numpy()
         n = 6 * PB + PB * self.max_pages
         host[:n] = 0
         host[PB:2 * PB] = -1
-        self.meta_dev[:n].copy_(self.meta_host[:n])
+        self.meta_ring.upload(self.meta_dev, n, blocking=True)
         saved = (self.feedback.clone(), self.trail_idx.clone(), self.codes_out.clone(), self.t_st.step.clone(),
                  self.c_st.step.clone(), self.t_st.seen[0].clone())
-        s = torch.cuda.Stream()
-        s.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(s):
-            for _ in range(2):
-                self._step_body(PB)
-        torch.cuda.current_stream().wait_stream(s)
-        torch.cuda.synchronize()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            codes = self._step_body(PB)
-        torch.cuda.synchronize()
+        g, codes = capture_graph(lambda: self._step_body(PB))
         # padding rows only touched slot 0; restore the state rows they may have changed
         self.feedback.copy_(saved[0])
         self.trail_idx.copy_(saved[1])

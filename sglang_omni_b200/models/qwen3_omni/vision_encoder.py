@@ -155,8 +155,9 @@ class Qwen3OmniVisionEncoder(nn.Module):
         ms = cfg.spatial_merge_size
         outs = []
         for t, h, w in grids:
-            hi = torch.linspace(0, side - 1, h)
-            wi = torch.linspace(0, side - 1, w)
+            dev = self.pos_embed.device
+            hi = torch.linspace(0, side - 1, h, device=dev)
+            wi = torch.linspace(0, side - 1, w, device=dev)
             h0, w0 = hi.long(), wi.long()
             h1, w1 = (h0 + 1).clamp(max=side - 1), (w0 + 1).clamp(max=side - 1)
             dh, dw = hi - h0, wi - w0

@@ -14,6 +14,7 @@ import math
 import torch
 import torch.nn.functional as F
 
+from . import _check
 from ._ext import ext
 
 PAGE = 64
@@ -94,6 +95,9 @@ def prefill_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Ten
                                   k_cache, v_cache, block_table, cu_q, kv_lens, scale, causal)
         out.copy_(ref.reshape(out.shape))
         return out
+    if _check.enabled():
+        _check.check_paged("attention_prefill", block_table, kv_lens, k_cache.shape[0], cu_q, q.shape[0])
+        _check.check_tiles("attention_prefill", tile_req, tile_tok0, cu_q)
     ext().attention_prefill(q3, k_cache, v_cache, out, block_table, cu_q, kv_lens, None, tile_req, tile_tok0,
                             num_heads, num_kv_heads, head_dim, scale, causal, 0)
     return out
@@ -123,6 +127,11 @@ def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqle
         tiles = (torch.tensor(req, dtype=torch.int32, device=q.device),
                  torch.tensor(tok0, dtype=torch.int32, device=q.device))
     lens = cu_seqlens[1:] - cu_seqlens[:-1]
+    if _check.enabled():
+        _check.check_range("varlen_attention", "cu_seqlens", cu_seqlens, 0, T + 1)
+        if bool((lens < 0).any()):
+            raise _check.LaunchCheckError("varlen_attention: cu_seqlens not monotone")
+        _check.check_tiles("varlen_attention", tiles[0], tiles[1], cu_seqlens)
     ext().attention_prefill(q, k, v, out, None, cu_seqlens, lens.to(torch.int32), cu_seqlens, tiles[0], tiles[1],
                             num_heads, num_kv_heads, head_dim, scale, causal, window)
     return out
@@ -158,6 +167,8 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     if workspace is None:
         max_ctx = int(kv_lens.max().item())
         workspace = DecodeWorkspace(B, num_heads, head_dim, max_ctx, q.device)
+    if _check.enabled():
+        _check.check_paged("attention_decode", block_table, kv_lens, k_cache.shape[0])
     ext().attention_decode(q, k_cache, v_cache, out, block_table, kv_lens, num_heads, num_kv_heads, head_dim, scale,
                            workspace.keys_per_split, workspace.max_splits, workspace.part_o, workspace.part_lse)
     return out

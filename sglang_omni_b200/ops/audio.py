@@ -62,20 +62,27 @@ def causal_conv1d(x: torch.Tensor, w2d: torch.Tensor, bias: torch.Tensor | None,
     return linear(cols, w2d, bias=bias, residual=residual)
 
 
-def conv_transpose1d(x: torch.Tensor, w_t: torch.Tensor, bias: torch.Tensor | None, stride: int) -> torch.Tensor:
-    """Causal transposed conv with kernel 2*stride (HF CausalTransConvNet) -> [B, (T-1)*stride, Cout].
+def conv_transpose1d(x: torch.Tensor, w_t: torch.Tensor, bias: torch.Tensor | None, stride: int,
+                     trim_left: int | None = None, t_out: int | None = None) -> torch.Tensor:
+    """Transposed conv with kernel 2*stride, trimmed: output sample u is sample u + trim_left of
+    the full (T + 1) * stride result.
 
+    Defaults (trim ``stride`` on both sides -> [B, (T-1)*stride, Cout]) match the Code2Wav
+    CausalTransConvNet; DAC's causal variant keeps the left edge (trim_left=0, t_out=T*stride).
     w_t: [(2s)*Cout, Cin] = the ConvTranspose1d weight [Cin, Cout, 2s] permuted to ((j, o), c)."""
     B, T, C = x.shape
     Cout = w_t.shape[0] // (2 * stride)
+    shift = stride if trim_left is None else trim_left
+    if t_out is None:
+        t_out = (T - 1) * stride if trim_left is None else (T + 1) * stride - shift
     if not x.is_cuda:
         w = w_t.float().view(2 * stride, Cout, C).permute(2, 1, 0)  # [Cin, Cout, 2s]
         y = F.conv_transpose1d(x.float().transpose(1, 2), w, None if bias is None else bias.float(), stride=stride)
-        y = y[..., stride: y.shape[-1] - stride]
+        y = y[..., shift: shift + t_out]
         return y.transpose(1, 2).to(x.dtype).contiguous()
     cols = linear(x.contiguous(), w_t)  # [B, T, 2s*Cout]
-    out = torch.empty(B, (T - 1) * stride, Cout, dtype=x.dtype, device=x.device)
-    ext().conv_transpose_ola(cols, bias, out, stride)
+    out = torch.empty(B, t_out, Cout, dtype=x.dtype, device=x.device)
+    ext().conv_transpose_ola(cols, bias, out, stride, shift)
     return out
 
 

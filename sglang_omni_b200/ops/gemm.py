@@ -13,6 +13,7 @@ from __future__ import annotations
 import torch
 import torch.nn.functional as F
 
+from . import _check
 from ._ext import ext, status_word
 
 # Per-device split-K scratch of the dense GEMM: fp32 partial sums
@@ -124,5 +125,7 @@ def grouped_linear(x: torch.Tensor, w: torch.Tensor, offsets: torch.Tensor, gate
         out = torch.empty(x.shape[0], m_out, dtype=torch.bfloat16, device=x.device)
     if expected_rows is None:
         expected_rows = max(1, x.shape[0] // max(1, w.shape[0]))
+    if _check.enabled():
+        _check.check_offsets("grouped_linear", offsets, x.shape[0])
     ext().gemm(w, x, out, offsets, m_out, gated, None, None, ACT_NONE, expected_rows, status_word(x.device))
     return out

@@ -10,6 +10,7 @@ from __future__ import annotations
 
 import torch
 
+from . import _check
 from ._ext import ext
 
 
@@ -104,6 +105,10 @@ def qkv_rope_store(qkv: torch.Tensor, num_heads: int, num_kv_heads: int, head_di
     if not qkv.is_cuda:
         return qkv_rope_store_ref(qkv, num_heads, num_kv_heads, head_dim, q_norm, k_norm, eps, positions, cos_tab,
                                   sin_tab, rot, neox, mrope_section, interleaved, slot_mapping, k_cache, v_cache)
+    if _check.enabled():
+        _check.check_range("qkv_rope_store", "positions", positions, 0, cos_tab.shape[0])
+        if slot_mapping is not None and k_cache is not None:
+            _check.check_range("qkv_rope_store", "slot_mapping", slot_mapping, 0, k_cache.shape[0] * 64, allow=-1)
     ext().qkv_rope_store(qkv, num_heads, num_kv_heads, head_dim, q_norm, k_norm, eps, positions,
                          list(mrope_section or [0, 0, 0]), interleaved, cos_tab, sin_tab, rot, neox, slot_mapping,
                          k_cache, v_cache)

@@ -15,6 +15,7 @@ from dataclasses import dataclass
 
 import torch
 
+from . import _check
 from ._ext import ext
 
 
@@ -115,6 +116,12 @@ def sample(logits: torch.Tensor, st: SamplingTensors | None = None, suppress=(-1
     if out is None:
         out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
     lo, hi, keep = suppress
+    if _check.enabled() and row_slot is not None:
+        arrs = [t for t in (st.temperature, st.top_k, st.seeds, st.step) if t is not None]
+        if arrs:
+            _check.check_range("sample", "row_slot", row_slot, 0, min(t.shape[0] for t in arrs))
+        if slot_tokens is not None:
+            _check.check_range("sample", "row_slot", row_slot, 0, slot_tokens.shape[0])
     ext().sample(logits, out, st.temperature, st.top_k, st.top_p, st.min_p, st.rep_penalty, st.seen, lo, hi, keep,
                  st.seeds, st.step, row_slot, slot_tokens)
     return out

@@ -80,6 +80,22 @@ def test_decode_paged(hq, hkv, d, kv_lens):
 
 
 @pytest.mark.gpu
+def test_decode_context_longer_than_workspace():
+    """Contexts above max_splits * keys_per_split widen the split instead of overrunning the scratch."""
+    kv_lens = [3000, 700, 5]
+    hq, hkv, d = 16, 2, 128
+    k, v, bt = _make_cache(kv_lens, hkv, d, "cuda", seed=5)
+    B = len(kv_lens)
+    q = torch.randn(B, hq * d, device="cuda").bfloat16()
+    kl = torch.tensor(kv_lens, dtype=torch.int32, device="cuda")
+    ws = A.DecodeWorkspace(B, hq, d, 512, "cuda", keys_per_split=256)  # 2 splits
+    out = A.decode_attention(q, k, v, bt, kl, hq, hkv, d, ws)
+    cu = torch.arange(B + 1, dtype=torch.int32, device="cuda")
+    ref = A.paged_attention_ref(q.view(B, hq, d), k, v, bt, cu, kl, 1 / math.sqrt(d), True)
+    torch.testing.assert_close(out.float().view(B, hq, d), ref, atol=2e-2, rtol=2e-2)
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("h,d", [(20, 64), (16, 80), (16, 128)])
 def test_varlen_noncausal(h, d):
     lens = [5, 100, 33, 200]

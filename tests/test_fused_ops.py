@@ -29,16 +29,17 @@ def test_route_ref_topk():
 @pytest.mark.gpu
 @pytest.mark.parametrize("mrope", [False, True])
 @pytest.mark.parametrize("neox", [True, False])
-def test_qkv_rope_store(mrope, neox):
+@pytest.mark.parametrize("d", [128, 32, 96])
+def test_qkv_rope_store(mrope, neox, d):
     torch.manual_seed(0)
-    T, hq, hkv, d = 37, 32, 4, 128
+    T, hq, hkv = 37, 32, 4
     qkv = torch.randn(T, (hq + 2 * hkv) * d, device="cuda").bfloat16()
     qn = (1 + 0.1 * torch.randn(d, device="cuda")).bfloat16()
     kn = (1 + 0.1 * torch.randn(d, device="cuda")).bfloat16()
     cos, sin = R.rope_tables(d, 1e6, 4096, "cuda")
     if mrope:
         pos = torch.randint(0, 4000, (3, T), dtype=torch.int32, device="cuda")
-        sec = [24, 20, 20]
+        sec = [24, 20, 20] if d == 128 else [d // 2 - 2 * (d // 8), d // 8, d // 8]
     else:
         pos = torch.randint(0, 4000, (T,), dtype=torch.int32, device="cuda")
         sec = None

@@ -13,10 +13,10 @@ def tiny(dtype=torch.float32, device="cpu"):
                              codec_pad=254, codec_bos=255, speakers={"a": 240}, default_speaker="a",
                              tts_pad=90, tts_bos=91, tts_eos=92, im_start=93, im_end=94, system=95, user=96,
                              assistant=97, newline=98, num_code_groups=4)
-    tc = DecoderConfig(vocab_size=256, hidden_size=64, num_layers=2, num_heads=4, num_kv_heads=2, head_dim=32,
+    tc = DecoderConfig(vocab_size=256, hidden_size=64, num_layers=2, num_heads=4, num_kv_heads=2, head_dim=64,
                        intermediate_size=96, num_experts=8, topk=2, moe_intermediate_size=32,
-                       shared_expert_intermediate_size=64, rope_theta=1e4, mrope_section=[6, 5, 5], dtype=dtype)
-    cc = DecoderConfig(vocab_size=64, hidden_size=64, num_layers=2, num_heads=4, num_kv_heads=2, head_dim=32,
+                       shared_expert_intermediate_size=64, rope_theta=1e4, mrope_section=[12, 10, 10], dtype=dtype)
+    cc = DecoderConfig(vocab_size=64, hidden_size=64, num_layers=2, num_heads=4, num_kv_heads=2, head_dim=64,
                        intermediate_size=96, rope_theta=1e4, max_position=64, dtype=dtype)
     t = Qwen3OmniTalker(tc, cc, thinker_hidden=48, special=sp, device=device).random_init_(seed=1, std=0.2)
     emb = (torch.randn(100, 48, generator=torch.Generator().manual_seed(2)) * 0.5).to(dtype).to(device)
