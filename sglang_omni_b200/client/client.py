@@ -73,7 +73,7 @@ class Client:
         sampling = req.sampling.to_dict()
         if req.max_tokens is not None:
             sampling["max_new_tokens"] = req.max_tokens
-        params: dict[str, Any] = {"sampling": sampling}
+        params: dict[str, Any] = {"sampling": sampling, "stream": bool(req.stream)}
         if req.stage_sampling:
             params["stage_sampling"] = {k: (v.to_dict() if hasattr(v, "to_dict") else dict(v))
                                         for k, v in req.stage_sampling.items()}

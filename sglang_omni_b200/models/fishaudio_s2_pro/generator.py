@@ -129,8 +129,9 @@ class DualARGenerator:
         self.cb_st.top_p[slot] = float(top_p)
         self.cb_st.step[slot] = 0
         if seed is not None:
-            self.sem_st.seeds[slot] = int(seed)
-            self.cb_st.seeds[slot] = int(seed) * 31 + 7
+            m = (1 << 62) - 1
+            self.sem_st.seeds[slot] = int(seed) & m
+            self.cb_st.seeds[slot] = (int(seed) * 31 + 7) & m
         return st
 
     def remove(self, rid: str) -> None:

@@ -42,7 +42,8 @@ _SPECIAL_RE = re.compile(r"(<\|[^<>|]+\|>)")
 
 
 class FishFallbackTokenizer:
-    """UTF-8 bytes at [3, 259); specials from 151643; speakers 0..22; semantic tokens from 151678."""
+    """UTF-8 bytes at [3, 259); specials from 151643 (or lower, for small test vocabularies);
+    speakers 0..22; then the contiguous semantic tokens (from 151678 at full size)."""
 
     SPECIAL_BASE = 151643
     NUM_SPEAKERS = 23
@@ -51,7 +52,9 @@ class FishFallbackTokenizer:
         self.vocab_size = vocab_size
         self.offset = offset
         self._tok2id: dict[str, int] = {}
-        nid = self.SPECIAL_BASE
+        nid = min(self.SPECIAL_BASE, vocab_size - codebook_size - len(_SPECIALS) - self.NUM_SPEAKERS)
+        if nid < offset + 256:
+            raise ValueError("vocabulary too small for bytes, special and semantic tokens")
         for s in _SPECIALS:
             self._tok2id[s] = nid
             nid += 1
@@ -107,12 +110,12 @@ class FishFallbackTokenizer:
         return "".join(out)
 
 
-def load_s2pro_tokenizer(model_path: str | None):
+def load_s2pro_tokenizer(model_path: str | None, vocab_size: int = 155776, codebook_size: int = 4096):
     if model_path and os.path.isdir(model_path) and os.path.exists(os.path.join(model_path, "tokenizer.json")):
         from transformers import PreTrainedTokenizerFast
 
         return PreTrainedTokenizerFast.from_pretrained(model_path)
-    return FishFallbackTokenizer()
+    return FishFallbackTokenizer(vocab_size, codebook_size)
 
 
 @dataclass
