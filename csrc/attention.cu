@@ -89,6 +89,11 @@ __device__ __forceinline__ void load_tile(__nv_bfloat16* dst, RowFn src_row, int
 // ---------------------------------------------------------------------------
 // Prefill / varlen attention.  One CTA = 64 packed rows of one KV head.
 // ---------------------------------------------------------------------------
+// A block-table entry outside the cache reads the reserved padding page 0.
+__device__ __forceinline__ int checked_page(int page, int num_pages) {
+  return (num_pages > 0 && static_cast<unsigned>(page) >= static_cast<unsigned>(num_pages)) ? 0 : page;
+}
+
 struct PrefillParams {
   const __nv_bfloat16* q;
   int64_t q_stride;  // elements between tokens
@@ -108,6 +113,7 @@ struct PrefillParams {
   __nv_bfloat16* out;
   int64_t out_stride;
   int window;
+  int num_pages;
 };
 
 template <int D>
@@ -170,7 +176,7 @@ __global__ void __launch_bounds__(128) prefill_kernel(const PrefillParams p) {
     const int k0 = it * kPage;
     const int nvalid = min(kPage, kv_len - k0);
     if (p.block_table) {
-      const int page = p.block_table[static_cast<int64_t>(b) * p.bt_stride + it];
+      const int page = checked_page(p.block_table[static_cast<int64_t>(b) * p.bt_stride + it], p.num_pages);
       const int64_t base = (static_cast<int64_t>(page) * p.hkv + h) * kPage * D;
       load_tile<D>(sk + buf * T::kElems, [&](int r) { return p.k + base + static_cast<int64_t>(r) * D; }, nvalid);
       load_tile<D>(sv + buf * T::kElems, [&](int r) { return p.v + base + static_cast<int64_t>(r) * D; }, nvalid);
@@ -329,7 +335,9 @@ struct DecodeParams {
   int64_t out_stride;
   float* part_o;    // [B, Hq, max_splits, D]
   float* part_lse;  // [B, Hq, max_splits]
+  int num_pages;
 };
+
 
 template <int D>
 __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
@@ -345,6 +353,15 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
   const int kv_len = p.kv_lens[b];
   const int kps = split_keys(kv_len, p.keys_per_split, p.max_splits);
   const int k_begin = split * kps;
+  if (kv_len <= 0) {
+    // empty context (a padding row of a batch bucket): defined zero output, so
+    // later layers never see uninitialised memory
+    if (split == 0) {
+      for (int i = threadIdx.x; i < G * D; i += blockDim.x)
+        p.out[static_cast<int64_t>(b) * p.out_stride + (h * G) * D + i] = __float2bfloat16(0.f);
+    }
+    return;
+  }
   if (k_begin >= kv_len) return;
   const int k_end = min(kv_len, k_begin + kps);
   const int nsplit = (kv_len + kps - 1) / kps;
@@ -374,7 +391,7 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
   auto issue = [&](int i, int buf) {
     const int it = first_tile + i;
     const int nvalid = min(kPage, k_end - it * kPage);
-    const int page = p.block_table[static_cast<int64_t>(b) * p.bt_stride + it];
+    const int page = checked_page(p.block_table[static_cast<int64_t>(b) * p.bt_stride + it], p.num_pages);
     const int64_t base = (static_cast<int64_t>(page) * p.hkv + h) * kPage * D;
     load_tile<D>(sk + buf * T::kElems, [&](int r) { return p.k + base + static_cast<int64_t>(r) * D; }, nvalid);
     load_tile<D>(sv + buf * T::kElems, [&](int r) { return p.v + base + static_cast<int64_t>(r) * D; }, nvalid);
@@ -593,6 +610,7 @@ cudaError_t attention_prefill(const AttnPrefillArgs& a, cudaStream_t stream) {
   p.out = static_cast<__nv_bfloat16*>(a.out);
   p.out_stride = a.out_stride;
   p.window = a.window;
+  p.num_pages = a.num_pages;
   switch (a.head_dim) {
     case 64: return launch_prefill<64>(p, a.num_tiles, stream);
     case 80: return launch_prefill<80>(p, a.num_tiles, stream);
@@ -621,6 +639,7 @@ cudaError_t attention_decode(const AttnDecodeArgs& a, cudaStream_t stream) {
   p.out_stride = a.out_stride;
   p.part_o = a.part_o;
   p.part_lse = a.part_lse;
+  p.num_pages = a.num_pages;
   switch (a.head_dim) {
     case 64: return launch_decode<64>(p, a.batch, stream);
     case 128: return launch_decode<128>(p, a.batch, stream);

@@ -186,6 +186,7 @@ void attention_prefill(const torch::Tensor& q, const torch::Tensor& k, const tor
   a.out = out.data_ptr();
   a.out_stride = out.stride(0);
   a.window = static_cast<int>(window);
+  a.num_pages = block_table.has_value() ? static_cast<int>(k.size(0)) : 0;
   check_launch(omni::attention_prefill(a, at::cuda::getCurrentCUDAStream()), "attention_prefill");
 }
 
@@ -219,6 +220,7 @@ void attention_decode(const torch::Tensor& q, const torch::Tensor& k, const torc
   a.out_stride = out.stride(0);
   a.part_o = part_o.data_ptr<float>();
   a.part_lse = part_lse.data_ptr<float>();
+  a.num_pages = static_cast<int>(k.size(0));
   check_launch(omni::attention_decode(a, at::cuda::getCurrentCUDAStream()), "attention_decode");
 }
 
@@ -256,6 +258,7 @@ void qkv_rope_store(torch::Tensor& qkv, int64_t hq, int64_t hkv, int64_t head_di
   a.slot_mapping = slot_mapping.has_value() ? slot_mapping->data_ptr<int>() : nullptr;
   a.k_cache = k_cache.has_value() ? k_cache->data_ptr() : nullptr;
   a.v_cache = v_cache.has_value() ? v_cache->data_ptr() : nullptr;
+  a.num_slots = k_cache.has_value() ? k_cache->size(0) * 64 : 0;
   check_launch(omni::qkv_rope_store(a, at::cuda::getCurrentCUDAStream()), "qkv_rope_store");
 }
 
@@ -337,6 +340,7 @@ void embed(const torch::Tensor& ids, const torch::Tensor& table, torch::Tensor& 
   a.out = out.data_ptr();
   a.tokens = static_cast<int>(ids.numel());
   a.hidden = static_cast<int>(table.size(1));
+  a.vocab = static_cast<int>(table.size(0));
   check_launch(omni::embed(a, at::cuda::getCurrentCUDAStream()), "embed");
 }
 
@@ -375,6 +379,7 @@ void vq_embed(const c10::optional<torch::Tensor>& ids, const c10::optional<torch
   a.out = out.data_ptr();
   a.tokens = static_cast<int>(tokens);
   a.hidden = static_cast<int>(table.size(1));
+  a.vocab = static_cast<int>(table.size(0));
   check_launch(omni::vq_embed(a, at::cuda::getCurrentCUDAStream()), "vq_embed");
 }
 

@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(256) qkv_rope_store_kernel(RopeStoreArgs a) {
   }
   if (!is_q && a.slot_mapping != nullptr) {
     const int slot = a.slot_mapping[tok];
-    if (slot >= 0) {
+    if (slot >= 0 && (a.num_slots == 0 || slot < a.num_slots)) {
       const int h = is_k ? head - a.hq : head - a.hq - a.hkv;
       const int page = slot >> 6, off = slot & 63;
       __nv_bfloat16* cache = static_cast<__nv_bfloat16*>(is_k ? a.k_cache : a.v_cache);
@@ -165,7 +165,8 @@ __global__ void moe_topk_kernel(MoeRouteArgs a) {
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
     const int e = lane + 32 * i;
-    sc[i] = e < a.experts ? lg[e] : -INFINITY;
+    const float v = e < a.experts ? lg[e] : -INFINITY;
+    sc[i] = v == v ? v : -INFINITY;  // a NaN logit never wins a selection
   }
   if (a.mode == 0) {
     // softmax over experts
@@ -265,7 +266,7 @@ __global__ void moe_topk_kernel(MoeRouteArgs a) {
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
       const int e = lane + 32 * i;
-      if (sc[i] > best || (sc[i] == best && e < bi)) {
+      if (e < a.experts && (sc[i] > best || (sc[i] == best && e < bi))) {
         best = sc[i];
         bi = e;
       }
@@ -279,6 +280,7 @@ __global__ void moe_topk_kernel(MoeRouteArgs a) {
         bi = oi;
       }
     }
+    if (bi >= a.experts) bi = 0;  // no finite score left: route to expert 0 (ids stay in range)
     // owner lane fetches the weight and removes the expert
     float w = 0.f;
 #pragma unroll
@@ -382,7 +384,8 @@ __global__ void embed_kernel(EmbedArgs a) {
   if (mm >= 0) {
     src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.mm_embeds) + static_cast<int64_t>(mm) * a.hidden);
   } else {
-    const int id = a.ids[tok];
+    int id = a.ids[tok];
+    if (a.vocab > 0) id = id < 0 ? 0 : (id >= a.vocab ? a.vocab - 1 : id);
     src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.table) + static_cast<int64_t>(id) * a.hidden);
   }
   uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + static_cast<int64_t>(tok) * a.hidden);
@@ -395,7 +398,8 @@ __global__ void embed_kernel(EmbedArgs a) {
 __global__ void vq_embed_kernel(VqEmbedArgs a) {
   const int t = blockIdx.x;
   const int s = a.slot ? a.slot[t] : -1;
-  const int id = a.slot ? a.slot_tokens[s] : a.ids[t];
+  int id = a.slot ? a.slot_tokens[s] : a.ids[t];
+  if (a.vocab > 0) id = id < 0 ? 0 : (id >= a.vocab ? a.vocab - 1 : id);
   int r;
   bool vq;
   if (a.code_row) {

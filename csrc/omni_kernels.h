@@ -79,6 +79,8 @@ struct AttnPrefillArgs {
   void* out;              // [tokens, hq, D] rows of stride out_stride
   int64_t out_stride;
   int window;             // > 0: causal sliding window (a query sees its last `window` keys)
+  int num_pages;          // paged mode: pages in the cache; block-table entries outside [0, num_pages)
+                          // read page 0 (the reserved padding page). 0 = unchecked
 };
 cudaError_t attention_prefill(const AttnPrefillArgs& a, cudaStream_t stream);
 
@@ -98,6 +100,7 @@ struct AttnDecodeArgs {
   int64_t out_stride;
   float* part_o;          // scratch [B, hq, max_splits, D] fp32
   float* part_lse;        // scratch [B, hq, max_splits] fp32
+  int num_pages;          // as in AttnPrefillArgs (0 = unchecked)
 };
 cudaError_t attention_decode(const AttnDecodeArgs& a, cudaStream_t stream);
 
@@ -120,6 +123,7 @@ struct RopeStoreArgs {
   const int* slot_mapping; // [tokens] page * 64 + offset, -1 skips; nullptr => no cache write
   void* k_cache;
   void* v_cache;
+  int64_t num_slots;       // cache slots (pages * 64); stores at slots >= num_slots are skipped. 0 = unchecked
 };
 cudaError_t qkv_rope_store(const RopeStoreArgs& a, cudaStream_t stream);
 
@@ -163,6 +167,7 @@ struct EmbedArgs {
   const void* mm_embeds;
   void* out;
   int tokens, hidden;
+  int vocab;               // rows of table; ids are clamped into [0, vocab) (0 = unchecked)
 };
 cudaError_t embed(const EmbedArgs& a, cudaStream_t stream);
 
@@ -185,6 +190,7 @@ struct VqEmbedArgs {
   float scale;
   void* out;
   int tokens, hidden;
+  int vocab;               // rows of table (ids clamped into range; 0 = unchecked)
 };
 cudaError_t vq_embed(const VqEmbedArgs& a, cudaStream_t stream);
 

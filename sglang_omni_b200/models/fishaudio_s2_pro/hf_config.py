@@ -7,8 +7,9 @@ sglang_omni/models/fishaudio_s2_pro/sglang_model.py:163-181).
 Fast AR (audio decoder): 4 layers predicting codebooks 1..9 after the
 semantic token, codebook vocab 4096, 10 codebooks
 (FishQwen3AudioDecoder, .../text2semantic/modeling.py:919-1010).  The fast
-AR's width is read from the checkpoint's config.json when one is present;
-the random-init default uses the text width (so ``project_in`` is identity).
+AR's shape is read from the checkpoint's config.json when one is present;
+the random-init default is 4 layers x 1024 (16 x 64 heads, SwiGLU 3072), so
+``project_in`` maps the 2560-wide slow hidden state to 1024.
 """
 from __future__ import annotations
 
@@ -31,8 +32,8 @@ def slow_config(**over) -> DecoderConfig:
 
 
 def fast_config(**over) -> DecoderConfig:
-    c = DecoderConfig(vocab_size=4096, hidden_size=2560, num_layers=4, num_heads=32, num_kv_heads=8, head_dim=128,
-                      intermediate_size=9728, rms_norm_eps=1e-6, rope_theta=1e6, rope_neox=False, qk_norm=True,
+    c = DecoderConfig(vocab_size=4096, hidden_size=1024, num_layers=4, num_heads=16, num_kv_heads=8, head_dim=64,
+                      intermediate_size=3072, rms_norm_eps=1e-6, rope_theta=1e6, rope_neox=False, qk_norm=True,
                       tie_word_embeddings=False, max_position=16, name="s2pro_fast_ar")
     for k, v in over.items():
         setattr(c, k, v)
