@@ -44,6 +44,9 @@ def parse():
     ap.add_argument("--speech-tokens", type=int, default=256)
     ap.add_argument("--speech-audio-s", type=float, default=10.0)
     ap.add_argument("--count-launches", type=int, default=1, help="count kernel launches in one extra untimed round")
+    ap.add_argument("--s2pro", type=int, default=1, help="also measure the S2-Pro streaming TTS phase")
+    ap.add_argument("--s2pro-streams", type=int, default=64)
+    ap.add_argument("--s2pro-audio-s", type=float, default=15.0)
     ap.add_argument("--thinker", type=int, default=1, help="run the thinker serving phase (headline value)")
     return ap.parse_args()
 
@@ -97,6 +100,67 @@ def speech_phase(args, dev, rank):
             wall = time.perf_counter() - t0
             ttfa = sorted(r[0] for r in res if r[0] is not None)
             return (1e3 * statistics.median(ttfa) if ttfa else None, sum(r[1] for r in res) / wall, n * 4)
+
+    return asyncio.run(run())
+
+
+def s2pro_phase(args, dev, rank):
+    """S2-Pro-style streaming dual-AR TTS through the public Client API: N concurrent
+    streams, ~200-token random text prompts, 28-layer slow AR (2560 wide), 4-layer
+    fast AR (1024 wide, 10 codebooks x 4096), DAC decoder to 44.1 kHz, 15 s of audio
+    per stream (EOS ignored).  Returns (p50 TTFA ms, mean real-time factor, audio s/s)."""
+    import asyncio
+    import random
+
+    import numpy as np
+
+    from sglang_omni_b200.client import Client, GenerateRequest, SamplingParams
+    from sglang_omni_b200.config import PipelineRunner, compile_pipeline
+    from sglang_omni_b200.models.fishaudio_s2_pro.config import S2ProPipelineConfig, s2pro_stages
+
+    frames = int(round(args.s2pro_audio_s * 44100 / 2048))
+    cfg = S2ProPipelineConfig(model_path="random", stages=s2pro_stages(
+        overrides={"slow": {"num_layers": 28}}, device=str(dev), max_new_tokens=frames,
+        max_streams=args.s2pro_streams, max_context=1024))
+    rnd = random.Random(11 + rank)
+    words = ["alpha", "bravo", "charlie", "delta", "echo", "foxtrot", "golf", "hotel", "india", "juliet"]
+
+    def text():  # ~200 byte-level ids with the fallback tokenizer
+        t = ""
+        while len(t) < 200:
+            t += rnd.choice(words) + " "
+        return t[:200]
+
+    async def run():
+        coord, stages = compile_pipeline(cfg)
+        async with PipelineRunner(coord, stages):
+            client = Client(coord)
+
+            async def one(i, tag):
+                t0 = time.perf_counter()
+                req = GenerateRequest(prompt=text(), sampling=SamplingParams(temperature=0.8, top_p=0.8, top_k=30,
+                                                                              ignore_eos=True),
+                                      max_tokens=frames, output_modalities=["audio"], task="tts", stream=True,
+                                      request_id=f"{tag}-{rank}-{i}")
+                first, samples = None, 0
+                async for ch in client.generate(req):
+                    if ch.finish_reason is not None:
+                        continue
+                    if ch.modality == "audio" and ch.audio_data is not None:
+                        if first is None:
+                            first = time.perf_counter() - t0
+                        samples += np.asarray(ch.audio_data).size
+                return first, samples / 44100.0, time.perf_counter() - t0
+
+            await asyncio.gather(*[one(i, "tw") for i in range(min(4, args.s2pro_streams))])
+            t0 = time.perf_counter()
+            res = await asyncio.gather(*[one(i, "t") for i in range(args.s2pro_streams)])
+            wall = time.perf_counter() - t0
+            ttfa = sorted(r[0] for r in res if r[0] is not None)
+            rtf = [r[2] / r[1] for r in res if r[1] > 0]
+            audio = sum(r[1] for r in res)
+            return (1e3 * statistics.median(ttfa) if ttfa else None, statistics.mean(rtf) if rtf else None,
+                    audio / wall)
 
     return asyncio.run(run())
 
@@ -216,11 +280,16 @@ def main():
 
     from sglang_omni_b200.models.qwen3_omni import loader
 
-    if not args.thinker:  # speech phase alone (a quick check; no headline value)
-        ttfa_ms, speech_tok_s, _ = speech_phase(args, dev, rank)
+    if not args.thinker:  # speech / TTS phases alone (a quick check; no headline value)
+        line = {"metric": "p50 time-to-first-audio-chunk", "impl": "ours"}
+        if args.speech:
+            ttfa_ms, speech_tok_s, _ = speech_phase(args, dev, rank)
+            line.update(ttfa_p50_ms=ttfa_ms, speech_text_tok_s=speech_tok_s, streams=args.speech_streams)
+        if args.s2pro:
+            a, b, c = s2pro_phase(args, dev, rank)
+            line.update(s2pro_ttfa_p50_ms=a, s2pro_rtf=b, s2pro_audio_s_per_s=c, s2pro_streams=args.s2pro_streams)
         if rank == 0:
-            print(json.dumps({"metric": "p50 time-to-first-audio-chunk", "ttfa_p50_ms": ttfa_ms,
-                              "speech_text_tok_s": speech_tok_s, "streams": args.speech_streams, "impl": "ours"}))
+            print(json.dumps(line))
         if world > 1:
             dist.destroy_process_group()
         return
@@ -293,6 +362,23 @@ def main():
             tt = torch.tensor([ttfa_ms or 0.0], dtype=torch.float64, device=dev)
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             ttfa_ms = float(tt[0])
+    s2 = None
+    if args.s2pro and args.layers == 48:
+        a, b, c = s2pro_phase(args, dev, rank)
+        t = torch.tensor([a or 0.0, b or 0.0, c or 0.0], dtype=torch.float64, device=dev)
+        if world > 1:
+            mx = t.clone()
+            dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+            sm = t.clone()
+            dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+            a, b, c = float(mx[0]), float(mx[1]), float(sm[2])
+        s2 = {"streams_per_gpu": args.s2pro_streams, "audio_s_per_stream": args.s2pro_audio_s,
+              "ttfa_p50_ms": None if a is None else round(a, 2), "rtf_mean": None if b is None else round(b, 4),
+              "audio_seconds_per_second": None if c is None else round(c, 2),
+              "model": "S2-Pro-style dual AR: slow 28 x 2560 (32/8 heads), fast 4 x 1024, 10 codebooks x 4096, "
+                       "DAC decoder 44.1 kHz; random init",
+              "timing": "host wall clock through Client.generate (stream=True): first audio chunk p50; "
+                        "RTF = request wall time / audio seconds; max over ranks"}
     if rank == 0:
         line = {
             "metric": "output tok/s + p50 time-to-first-audio-chunk, Qwen3-Omni-30B-A3B, 1/2/4/8 B200",
@@ -325,6 +411,7 @@ def main():
                               "max over ranks"},
             },
             "ttfa_p50_ms": None if ttfa_ms is None else round(ttfa_ms, 2),
+            "s2pro_tts": s2,
             "e2e": {"value": round(e2e, 2), "unit": "output tokens/s, host wall clock through AREngine.generate",
                     "h2d_bytes_per_step": int(args.requests * args.prompt_len * 4),
                     "d2h_bytes_per_step": int(args.requests * args.output_len * 4)},

@@ -101,7 +101,7 @@ def create_preprocessing_executor(model_path: str = "", overrides: dict | None =
         prompt = builder.build(text, refs or None, speaker=spk if isinstance(spk, int) else 0)
         sp = dict(SPEECH_DEFAULTS)
         samp = params.get("sampling") or {}
-        for k in ("temperature", "top_p", "top_k", "repetition_penalty", "seed"):
+        for k in ("temperature", "top_p", "top_k", "repetition_penalty", "seed", "ignore_eos"):
             if samp.get(k) is not None:
                 sp[k] = samp[k]
         data = {
@@ -266,7 +266,7 @@ class S2ProTTSExecutor(ResultQueueMixin, Executor):
         im_end = self.model.cfg.im_end_id
         for s, c in zip(streams, host):
             info = self._pending.get(s.rid)
-            if c[0] == im_end:
+            if c[0] == im_end and not (info is not None and info["payload"].data.get("ignore_eos")):
                 s.finished = True
             else:
                 self._codes.setdefault(s.rid, []).append(c)
