@@ -4,6 +4,8 @@ start the coordinator and every stage, run until one of them fails
 from __future__ import annotations
 
 import asyncio
+import os
+import sys
 import logging
 
 from ..pipeline.coordinator import Coordinator
@@ -19,6 +21,12 @@ class PipelineRunner:
         self._tasks: list[asyncio.Task] = []
 
     async def start(self):
+        # Engine threads of GPU stages share this interpreter with the event loop
+        # that routes every stage message; a short GIL switch interval keeps the
+        # loop responsive while they run Python between kernel launches.
+        iv = float(os.environ.get("OMNI_GIL_SWITCH_INTERVAL_S", "0.0005"))
+        if 0 < iv < sys.getswitchinterval():
+            sys.setswitchinterval(iv)
         await self.coordinator.start()
         for s in self.stages:
             await s.start()

@@ -289,6 +289,7 @@ class ThreadedAREngine:
     def _run(self):
         eng = self.engine
         try:
+            eng.runner.capture_all()  # every decode bucket, before the first request (not on its latency path)
             while True:
                 with self._cv:
                     while not self._inbox and not eng.has_work() and not self._stop:

@@ -299,6 +299,12 @@ class ARModelRunner:
         n = 6 * PB + PB * P
         self.meta_ring.upload(self.meta_dev, n)
 
+    def capture_all(self):
+        """Captures the decode graph of every batch bucket up front."""
+        if self.use_graphs:
+            for PB in self.buckets:
+                self.capture(PB)
+
     @torch.no_grad()
     def capture(self, PB: int):
         if not self.use_graphs or PB in self.graphs:

@@ -276,6 +276,13 @@ class DualARGenerator:
         n = 6 * PB + PB * self.max_pages
         self.meta_ring.upload(self.meta_dev, n)
 
+    def capture_all(self):
+        """Captures the frame-step graph of every batch bucket up front."""
+        if self.use_graphs:
+            for PB in self.buckets:
+                if PB not in self.graphs:
+                    self._capture(PB)
+
     def _capture(self, PB: int):
         host = self.meta_ring.next().numpy()
         n = 6 * PB + PB * self.max_pages

@@ -230,6 +230,7 @@ class S2ProTTSExecutor(ResultQueueMixin, Executor):
     def _run(self):
         try:
             with torch.inference_mode():
+                self.gen.capture_all()
                 self._loop_body()
         except BaseException as exc:  # the engine thread died: fail every request it holds
             log.exception("s2pro engine thread failed")

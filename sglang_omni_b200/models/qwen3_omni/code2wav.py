@@ -285,16 +285,20 @@ class StreamingCode2Wav:
         return pending >= need or (final and pending > 0)
 
     @torch.no_grad()
-    def decode_ready(self, rids: list[str], final: bool = False) -> dict[str, torch.Tensor]:
-        """Returns {rid: float32 waveform of the new frames} for every ready stream."""
+    def decode_ready(self, rids: list[str], final: bool = False, finals=None) -> dict[str, torch.Tensor]:
+        """Returns {rid: float32 waveform of the new frames} for every ready stream.
+
+        ``final`` (all streams) or ``finals`` (a set of stream ids) flush the streams
+        whose last frame has arrived."""
         up = self.model.cfg.total_upsample
         groups: dict[tuple[int, int], list[tuple[str, torch.Tensor]]] = {}
         for rid in rids:
-            if not self.ready(rid, final):
+            fin = final or (finals is not None and rid in finals)
+            if not self.ready(rid, fin):
                 continue
             st = self.streams[rid]
             pending = len(st.codes) - st.emitted_frames
-            if final:
+            if fin:
                 end = len(st.codes)
             elif st.emitted_frames == 0:
                 end = self.first_chunk + (pending - self.first_chunk) // self.chunk * self.chunk

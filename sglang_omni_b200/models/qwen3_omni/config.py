@@ -23,7 +23,9 @@ _S = "sglang_omni_b200.models.qwen3_omni.pipeline.stages"
 _N = "sglang_omni_b200.models.qwen3_omni.pipeline.next_stage"
 
 
-def text_stages(overrides=None, device="cuda:0", max_batch=64, max_context=4096, speech=False, tail_frames=50):
+def text_stages(overrides=None, device="cuda:0", max_batch=64, max_context=4096, speech=False, tail_frames=50,
+                first_chunk=4):
+    """``first_chunk``: frames of the first Code2Wav chunk (later chunks are 10 frames of 80 ms)."""
     ov = {"overrides": overrides} if overrides else {}
     thinker_args = {"device": device, "max_batch": max_batch, "max_context": max_context, **ov}
     if speech:
@@ -58,7 +60,8 @@ def text_stages(overrides=None, device="cuda:0", max_batch=64, max_context=4096,
                         get_next=f"{_N}.talker_next",
                         stream_to=[StreamTargetConfig(to_stage="code2wav", bootstrap=True)]),
             StageConfig(name="code2wav", executor=ExecutorConfig(factory=f"{_S}.create_code2wav_executor",
-                                                                  args={"device": device, **ov}),
+                                                                  args={"device": device, "first_chunk": first_chunk,
+                                                                        **ov}),
                         get_next=f"{_N}.code2wav_next"),
         ]
     return stages

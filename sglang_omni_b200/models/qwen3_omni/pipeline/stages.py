@@ -397,6 +397,7 @@ class TalkerStreamingExecutor(ResultQueueMixin, Executor):
     def _run(self):
         try:
             with torch.inference_mode():
+                self.gen.capture_all()
                 self._loop_body()
         except BaseException as exc:
             log.exception("talker thread failed")
@@ -500,7 +501,11 @@ def create_talker_executor(model_path: str = "", device: str = "cuda:0", max_str
 # ----------------------------------------------------------------------------- code2wav
 class Code2WavStreamingExecutor(ResultQueueMixin, Executor):
     """Incremental vocoding of every active stream; emits float32 PCM chunks
-    (12.5 Hz frames -> 24 kHz) to the client as they are produced."""
+    (12.5 Hz frames -> 24 kHz) to the client as they are produced.
+
+    One decoder loop serves all streams: whenever frames arrive it decodes every
+    stream that has a chunk ready in one batched forward per window length
+    (instead of one forward per stream), off the event loop."""
 
     def __init__(self, model_path: str, device: str, chunk: int = 10, left_context: int = 25,
                  first_chunk: int | None = None, overrides: dict | None = None):
@@ -510,12 +515,20 @@ class Code2WavStreamingExecutor(ResultQueueMixin, Executor):
         self.sc = StreamingCode2Wav(self.model, chunk, left_context, first_chunk)
         self._streams: dict[str, asyncio.Queue] = {}
         self._audio: dict[str, list] = {}
-        self._lock = asyncio.Lock()
+        self._finals: set[str] = set()
+        self._flushed: dict[str, asyncio.Future] = {}
+        self._wake: asyncio.Event | None = None
+        self._loop_task: asyncio.Task | None = None
 
     async def add_request(self, payload: StagePayload) -> None:
         rid = payload.request_id
+        if self._wake is None:
+            self._wake = asyncio.Event()
+        if self._loop_task is None or self._loop_task.done():
+            self._loop_task = asyncio.ensure_future(self._decoder_loop())
         self._streams[rid] = asyncio.Queue()
         self._audio[rid] = []
+        self._flushed[rid] = asyncio.get_running_loop().create_future()
         asyncio.ensure_future(self._run(payload))
 
     def stream(self, request_id: str):
@@ -532,16 +545,39 @@ class Code2WavStreamingExecutor(ResultQueueMixin, Executor):
 
         return gen()
 
-    async def _decode(self, rid: str, final: bool):
-        async with self._lock:  # one vocoder forward at a time on this GPU
-            out = await asyncio.to_thread(self.sc.decode_ready, [rid], final)
-        for r, wav in out.items():
-            a = wav.float().cpu().numpy()
-            self._audio[r].append(a)
-            q = self._streams.get(r)
-            if q is not None:
-                q.put_nowait({"modality": "audio", "audio_waveform": a, "sample_rate": SAMPLE_RATE_OUT,
-                              "t": time.perf_counter()})
+    async def _decoder_loop(self):
+        while True:
+            await self._wake.wait()
+            self._wake.clear()
+            live = [r for r in self._streams if r in self.sc.streams]
+            finals = {r for r in live if r in self._finals}
+            ready = [r for r in live if self.sc.ready(r, r in finals)]
+            if ready:
+                try:
+                    out = await asyncio.to_thread(self.sc.decode_ready, ready, False, finals)
+                except Exception as exc:  # fail the streams of this batch only
+                    log.exception("code2wav batch failed")
+                    for r in ready:
+                        f = self._flushed.get(r)
+                        if f is not None and not f.done():
+                            f.set_exception(exc)
+                    continue
+                now = time.perf_counter()
+                for r, wav in out.items():
+                    a = wav.float().cpu().numpy()
+                    if r in self._audio:
+                        self._audio[r].append(a)
+                    q = self._streams.get(r)
+                    if q is not None:
+                        q.put_nowait({"modality": "audio", "audio_waveform": a, "sample_rate": SAMPLE_RATE_OUT,
+                                      "t": now})
+            for r in finals:
+                if not self.sc.ready(r, True):
+                    f = self._flushed.get(r)
+                    if f is not None and not f.done():
+                        f.set_result(True)
+            if any(self.sc.ready(r, r in self._finals) for r in self._streams if r in self.sc.streams):
+                self._wake.set()
 
     async def _run(self, payload: StagePayload):
         rid = payload.request_id
@@ -552,8 +588,12 @@ class Code2WavStreamingExecutor(ResultQueueMixin, Executor):
                     break
                 self.sc.add_codes(rid, torch.tensor(item.data["codes"], dtype=torch.long))
                 if self.sc.ready(rid):
-                    await self._decode(rid, final=False)
-            await self._decode(rid, final=True)
+                    self._wake.set()
+            if rid not in self.sc.streams:  # no frame at all
+                self.sc.add_codes(rid, torch.zeros(0, self.model.cfg.num_quantizers, dtype=torch.long))
+            self._finals.add(rid)
+            self._wake.set()
+            await self._flushed[rid]
             audio = np.concatenate(self._audio.pop(rid)) if self._audio.get(rid) else np.zeros(0, np.float32)
             self._results().put_nowait(StagePayload(rid, payload.request,
                                                     {"audio_waveform": audio, "sample_rate": SAMPLE_RATE_OUT}))
@@ -562,16 +602,22 @@ class Code2WavStreamingExecutor(ResultQueueMixin, Executor):
         except Exception as exc:
             self._results().put_nowait(StageError(rid, f"code2wav: {exc}"))
         finally:
-            self.sc.close(rid)
-            q = self._streams.pop(rid, None)
-            if q is not None:
-                q.put_nowait(None)
+            self._cleanup(rid)
 
-    async def abort(self, request_id: str) -> None:
-        self.sc.close(request_id)
-        q = self._streams.pop(request_id, None)
+    def _cleanup(self, rid: str):
+        self.sc.close(rid)
+        self._finals.discard(rid)
+        self._flushed.pop(rid, None)
+        self._audio.pop(rid, None)
+        q = self._streams.pop(rid, None)
         if q is not None:
             q.put_nowait(None)
+
+    async def abort(self, request_id: str) -> None:
+        f = self._flushed.get(request_id)
+        if f is not None and not f.done():
+            f.cancel()
+        self._cleanup(request_id)
 
 
 def create_code2wav_executor(model_path: str = "", device: str = "cuda:0", chunk: int = 10,

@@ -421,6 +421,13 @@ class SpeechGenerator:
             s.frames += 1
         return codes[:B]
 
+    def capture_all(self):
+        """Captures the frame-step graph of every batch bucket up front."""
+        if self.use_graphs:
+            for PB in self.buckets:
+                if PB not in self.graphs:
+                    self._capture(PB)
+
     def _capture(self, PB):
         host = self.meta_ring.next().numpy()
         n = 6 * PB + PB * self.max_pages
