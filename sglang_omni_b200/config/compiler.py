@@ -35,10 +35,16 @@ class Endpoints:
     abort: str
 
 
-def allocate_endpoints(cfg: PipelineConfig, stage_names: list[str], run_id: str | None = None) -> Endpoints:
+def allocate_endpoints(cfg: PipelineConfig, stage_names: list[str], run_id: str | None = None,
+                       multiprocess: bool = True) -> Endpoints:
     run_id = run_id or uuid.uuid4().hex[:10]
     ep = cfg.endpoints
-    if ep.scheme == "ipc":
+    scheme = ep.scheme if ep.scheme != "auto" else ("ipc" if multiprocess else "local")
+    if scheme == "local":
+        stages = {n: f"local://{run_id}/{n}" for n in stage_names}
+        completion = f"local://{run_id}/_completion"
+        abort = f"local://{run_id}/_abort"
+    elif scheme == "ipc":
         base = os.path.join(ep.base_path, run_id)
         os.makedirs(base, exist_ok=True)
         stages = {n: f"ipc://{base}/{n}.sock" for n in stage_names}
@@ -134,7 +140,7 @@ def compile_pipeline(cfg: PipelineConfig, run_id: str | None = None) -> tuple[Co
     """Single-process build: every stage in this process (zero-copy in-process relay by default)."""
     stages_cfg, name_map, entry = cfg.apply_fusion()
     names = [s.name for s in stages_cfg]
-    endpoints = allocate_endpoints(cfg, names, run_id)
+    endpoints = allocate_endpoints(cfg, names, run_id, multiprocess=False)
     terminals = [name_map.get(t, t) for t in cfg.terminal_stages]
     coordinator = Coordinator(endpoints.completion, endpoints.abort, entry, terminals)
     receivers = {name_map.get(t.to_stage, t.to_stage) for s in stages_cfg for t in s.stream_to}

@@ -55,7 +55,7 @@ class StageConfig(BaseModel):
 
 class EndpointsConfig(BaseModel):
     model_config = ConfigDict(extra="forbid")
-    scheme: Literal["ipc", "tcp"] = "ipc"
+    scheme: Literal["auto", "ipc", "tcp", "local"] = "auto"  # auto: local in one process, else ipc
     base_path: str = "/tmp/sglang_omni_b200"
     base_port: int = 16000
 

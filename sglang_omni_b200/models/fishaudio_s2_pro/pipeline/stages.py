@@ -12,8 +12,10 @@ Streaming differs in where the work runs: the reference re-decodes every code
 so far on the CPU after 5 and then every 100 tokens; here a vocoder thread
 decodes on the GPU after ``stream_stride`` frames and then every
 ``stream_followup_stride`` frames, over a window of at most
-``stream_context`` earlier frames (the decoder is causal; its transformer
-attends 128 frames back per layer).
+``stream_context`` earlier frames (the decoder is causal; its convolutions
+see a few frames back and its transformer up to 128 frames per layer, so a
+48-frame context reproduces the full decode closely at a fraction of the cost).
+Ready windows of all streams are decoded together, one forward per window shape.
 """
 from __future__ import annotations
 
@@ -127,7 +129,7 @@ class S2ProTTSExecutor(ResultQueueMixin, Executor):
 
     def __init__(self, model_path: str = "", device: str = "cuda:0", max_streams: int = 64, max_context: int = 4096,
                  max_new_tokens: int = 2048, overrides: dict | None = None, use_graphs: bool = True,
-                 stream_stride: int = 5, stream_followup_stride: int = 20, stream_context: int = 128,
+                 stream_stride: int = 5, stream_followup_stride: int = 20, stream_context: int = 48,
                  max_prefill_tokens: int = 8192):
         super().__init__()
         dev = torch.device(device)
@@ -317,41 +319,68 @@ class S2ProTTSExecutor(ResultQueueMixin, Executor):
                 self._emit(ready, gen.step(ready))
 
     def _vocoder_loop(self):
-        """Decodes stream windows; one job at a time on this GPU."""
-        hop = None
+        """Decodes the stream windows of every stream with a chunk ready, batched:
+        one decoder forward per (window length, context) group."""
         while True:
-            job = self._voc_q.get()
-            if job is None:
-                return
-            rid, codes, info, final = job
+            jobs = [self._voc_q.get()]
+            while True:
+                try:
+                    jobs.append(self._voc_q.get_nowait())
+                except queue.Empty:
+                    break
+            stop = any(j is None for j in jobs)
+            latest: dict[str, tuple] = {}
+            finals: set[str] = set()
+            for j in jobs:
+                if j is None:
+                    continue
+                rid, codes, info, final = j
+                if rid not in latest or len(codes) >= len(latest[rid][0]):
+                    latest[rid] = (codes, info)
+                if final:
+                    finals.add(rid)
             try:
-                if self._decoder is None:
-                    self._decoder = loader.get_decoder(self.model_path, self.device, self.overrides)
-                dec = self._decoder
-                hop = hop or dec.cfg.hop
-                n = len(codes)
-                done = info["emitted"] // hop
-                if n > done:
-                    start = max(0, done - self.stream_context)
-                    window = torch.tensor(codes[start:n], dtype=torch.int64, device=self.device)[:, 1:]
-                    with torch.inference_mode():
-                        wav = dec.decode(window.t()[None])[0]
-                    a = wav[(done - start) * hop:].float().cpu().numpy()
-                    info["emitted"] = n * hop
-                    q = self._streams.get(rid)
-                    if q is not None and a.size:
-                        self._post(q.put_nowait, {"modality": "audio", "audio_waveform": a,
-                                                  "sample_rate": dec.cfg.sample_rate, "t": time.perf_counter()})
+                self._decode_batch(latest)
             except Exception:
-                log.exception("stream vocoding of %s failed", rid)
-            if final:
+                log.exception("stream vocoding failed")
+            for rid in finals:
                 self._close_stream(rid)
+            if stop:
+                return
+
+    def _decode_batch(self, latest: dict[str, tuple]):
+        if not latest:
+            return
+        if self._decoder is None:
+            self._decoder = loader.get_decoder(self.model_path, self.device, self.overrides)
+        dec = self._decoder
+        hop = dec.cfg.hop
+        groups: dict[tuple[int, int], list] = {}
+        for rid, (codes, info) in latest.items():
+            n = len(codes)
+            done = info["emitted"] // hop
+            if n <= done:
+                continue
+            start = max(0, done - self.stream_context)
+            groups.setdefault((n - start, done - start), []).append((rid, codes[start:n], info, n))
+        for (_, ctx), items in groups.items():
+            win = torch.tensor([c for _, c, _, _ in items], dtype=torch.int64)[:, :, 1:]   # [B, W, ncb]
+            with torch.inference_mode():
+                wav = dec.decode(win.permute(0, 2, 1).contiguous().to(self.device))
+            wav = wav[:, ctx * hop:].float().cpu().numpy()
+            now = time.perf_counter()
+            for (rid, _, info, n), a in zip(items, wav):
+                info["emitted"] = n * hop
+                q = self._streams.get(rid)
+                if q is not None and a.size:
+                    self._post(q.put_nowait, {"modality": "audio", "audio_waveform": a,
+                                              "sample_rate": dec.cfg.sample_rate, "t": now})
 
 
 def create_tts_engine_executor(model_path: str = "", device: str = "cuda:0", max_new_tokens: int = 2048,
                                max_streams: int = 64, max_context: int = 4096, overrides: dict | None = None,
                                use_graphs: bool = True, stream_stride: int = 5, stream_followup_stride: int = 20,
-                               stream_context: int = 128, top_k: int | None = None):
+                               stream_context: int = 48, top_k: int | None = None):
     """Same factory arguments as the reference (device, max_new_tokens, stream strides)."""
     return S2ProTTSExecutor(model_path, device, max_streams, max_context, max_new_tokens, overrides, use_graphs,
                             stream_stride, stream_followup_stride, stream_context)

@@ -6,6 +6,11 @@ Topology (same as sglang_omni/pipeline/control_plane.py:59-443):
   * stages PUSH completions and stream chunks to the coordinator's PULL;
   * the coordinator PUBlishes aborts, every stage SUBscribes.
 Messages are msgpack dicts (see proto.messages); tensors never travel here.
+
+Endpoints ``local://...`` (single-process pipelines) skip ZMQ and msgpack: a
+PUSH/PULL pair is one asyncio queue of message objects and PUB/SUB a list of
+queues, all owned by the process's event loop.  Per-token stream chunks
+between stages and to the coordinator then cost one queue operation each.
 """
 from __future__ import annotations
 
@@ -38,6 +43,85 @@ class ControlPlaneContext:
         if cls._ctx is None or cls._ctx.closed:
             cls._ctx = zmq.asyncio.Context.instance()
         return cls._ctx
+
+
+LOCAL_PREFIX = "local://"
+_LOCAL_QUEUES: dict[str, asyncio.Queue] = {}
+_LOCAL_SUBS: dict[str, list[asyncio.Queue]] = {}
+
+
+def _local_queue(endpoint: str) -> asyncio.Queue:
+    q = _LOCAL_QUEUES.get(endpoint)
+    if q is None:
+        q = _LOCAL_QUEUES[endpoint] = asyncio.Queue()
+    return q
+
+
+class _LocalPush:
+    def __init__(self, endpoint: str):
+        self.endpoint = endpoint
+
+    async def send(self, msg) -> None:
+        _local_queue(self.endpoint).put_nowait(msg)
+
+    def close(self):
+        pass
+
+
+class _LocalPull:
+    def __init__(self, endpoint: str):
+        self.endpoint = endpoint
+        _LOCAL_QUEUES[endpoint] = _LOCAL_QUEUES.get(endpoint) or asyncio.Queue()
+
+    async def recv(self):
+        return await _local_queue(self.endpoint).get()
+
+    def close(self):
+        _LOCAL_QUEUES.pop(self.endpoint, None)
+
+
+class _LocalPub:
+    def __init__(self, endpoint: str):
+        self.endpoint = endpoint
+        _LOCAL_SUBS.setdefault(endpoint, [])
+
+    async def publish(self, msg) -> None:
+        for q in _LOCAL_SUBS.get(self.endpoint, []):
+            q.put_nowait(msg)
+
+    def close(self):
+        _LOCAL_SUBS.pop(self.endpoint, None)
+
+
+class _LocalSub:
+    def __init__(self, endpoint: str):
+        self.endpoint = endpoint
+        self.q: asyncio.Queue = asyncio.Queue()
+        _LOCAL_SUBS.setdefault(endpoint, []).append(self.q)
+
+    async def recv(self):
+        return await self.q.get()
+
+    def close(self):
+        subs = _LOCAL_SUBS.get(self.endpoint)
+        if subs and self.q in subs:
+            subs.remove(self.q)
+
+
+def _push(endpoint: str, bind: bool = False):
+    return _LocalPush(endpoint) if endpoint.startswith(LOCAL_PREFIX) else PushSocket(endpoint, bind)
+
+
+def _pull(endpoint: str):
+    return _LocalPull(endpoint) if endpoint.startswith(LOCAL_PREFIX) else PullSocket(endpoint, bind=True)
+
+
+def _pub(endpoint: str):
+    return _LocalPub(endpoint) if endpoint.startswith(LOCAL_PREFIX) else PubSocket(endpoint)
+
+
+def _sub(endpoint: str):
+    return _LocalSub(endpoint) if endpoint.startswith(LOCAL_PREFIX) else SubSocket(endpoint)
 
 
 class _Sock:
@@ -102,9 +186,9 @@ class StageControlPlane:
         self._peers: dict[str, PushSocket] = {}
 
     def start(self):
-        self._pull = PullSocket(self.recv_endpoint, bind=True)
-        self._to_coord = PushSocket(self.coordinator_endpoint)
-        self._sub = SubSocket(self.abort_endpoint)
+        self._pull = _pull(self.recv_endpoint)
+        self._to_coord = _push(self.coordinator_endpoint)
+        self._sub = _sub(self.abort_endpoint)
 
     async def recv(self):
         return await self._pull.recv()
@@ -115,7 +199,7 @@ class StageControlPlane:
     async def send_to_stage(self, endpoint: str, msg) -> None:
         s = self._peers.get(endpoint)
         if s is None:
-            s = self._peers[endpoint] = PushSocket(endpoint)
+            s = self._peers[endpoint] = _push(endpoint)
         await s.send(msg)
 
     async def send_to_coordinator(self, msg) -> None:
@@ -137,14 +221,14 @@ class CoordinatorControlPlane:
         self._stages: dict[str, PushSocket] = {}
 
     async def start(self):
-        self._pull = PullSocket(self.completion_endpoint, bind=True)
-        self._pub = PubSocket(self.abort_endpoint)
+        self._pull = _pull(self.completion_endpoint)
+        self._pub = _pub(self.abort_endpoint)
         await asyncio.sleep(0.05)  # let subscribers connect before the first publish
 
     async def send_to_stage(self, endpoint: str, msg) -> None:
         s = self._stages.get(endpoint)
         if s is None:
-            s = self._stages[endpoint] = PushSocket(endpoint)
+            s = self._stages[endpoint] = _push(endpoint)
         await s.send(msg)
 
     async def recv(self):
