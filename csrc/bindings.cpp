@@ -1,6 +1,9 @@
 // torch bindings of the sm_100a kernels (module sglang_omni_b200._C).
 // Every entry validates device, dtype, contiguity and shape, then forwards raw
 // pointers and the current CUDA stream to the launchers in omni_kernels.h.
+#include <cstring>
+#include <string>
+
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
@@ -383,6 +386,105 @@ void vq_embed(const c10::optional<torch::Tensor>& ids, const c10::optional<torch
   check_launch(omni::vq_embed(a, at::cuda::getCurrentCUDAStream()), "vq_embed");
 }
 
+// ---- symmetric memory through CUDA IPC (one cudaMalloc per rank, mapped by peers)
+int64_t ipc_alloc(int64_t bytes) {
+  void* p = nullptr;
+  check_launch(cudaMalloc(&p, static_cast<size_t>(bytes)), "cudaMalloc");
+  check_launch(cudaMemset(p, 0, static_cast<size_t>(bytes)), "cudaMemset");
+  return reinterpret_cast<int64_t>(p);
+}
+void ipc_free(int64_t ptr) { check_launch(cudaFree(reinterpret_cast<void*>(ptr)), "cudaFree"); }
+py::bytes ipc_handle(int64_t ptr) {
+  cudaIpcMemHandle_t h;
+  check_launch(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(ptr)), "cudaIpcGetMemHandle");
+  return py::bytes(reinterpret_cast<const char*>(&h), sizeof(h));
+}
+int64_t ipc_open(const py::bytes& handle) {
+  std::string s = handle;
+  TORCH_CHECK(s.size() == sizeof(cudaIpcMemHandle_t), "bad IPC handle size");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, s.data(), sizeof(h));
+  void* p = nullptr;
+  check_launch(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+  return reinterpret_cast<int64_t>(p);
+}
+void ipc_close(int64_t ptr) { check_launch(cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr)), "cudaIpcCloseMemHandle"); }
+torch::Tensor tensor_at(int64_t ptr, const std::vector<int64_t>& shape, c10::ScalarType dtype, int64_t device) {
+  return at::from_blob(reinterpret_cast<void*>(ptr), shape,
+                       at::TensorOptions().dtype(dtype).device(at::kCUDA, static_cast<c10::DeviceIndex>(device)));
+}
+
+// ---- expert-parallel exchange
+omni::EpArgs ep_args(const torch::Tensor& topk_ids, const torch::Tensor& peer_base, const std::vector<int64_t>& offs,
+                     int64_t rank, int64_t world, int64_t experts, int64_t hidden, int64_t cap_rows,
+                     int64_t max_slots, torch::Tensor& cursor, torch::Tensor& local_offsets, torch::Tensor& total_rows,
+                     torch::Tensor& epoch, const c10::optional<torch::Tensor>& status, double timeout_s) {
+  TORCH_CHECK(topk_ids.scalar_type() == at::kInt && topk_ids.dim() == 2 && topk_ids.is_contiguous(), "topk_ids");
+  TORCH_CHECK(peer_base.scalar_type() == at::kLong && peer_base.numel() == world, "peer_base int64 [world]");
+  TORCH_CHECK(offs.size() == 5, "five region offsets");
+  TORCH_CHECK(experts % world == 0 && hidden % 8 == 0, "experts % world, hidden % 8");
+  omni::EpArgs a{};
+  a.rank = static_cast<int>(rank);
+  a.world = static_cast<int>(world);
+  a.experts = static_cast<int>(experts);
+  a.local_experts = static_cast<int>(experts / world);
+  a.topk = static_cast<int>(topk_ids.size(1));
+  a.hidden = static_cast<int>(hidden);
+  a.tokens = static_cast<int>(topk_ids.size(0));
+  a.topk_ids = topk_ids.data_ptr<int>();
+  a.peer_base = peer_base.data_ptr<int64_t>();
+  a.off_counts = offs[0];
+  a.off_flags = offs[1];
+  a.off_recv_x = offs[2];
+  a.off_recv_meta = offs[3];
+  a.off_comb = offs[4];
+  a.cap_rows = static_cast<int>(cap_rows);
+  a.max_slots = static_cast<int>(max_slots);
+  a.cursor = cursor.data_ptr<int>();
+  a.local_offsets = local_offsets.data_ptr<int>();
+  a.total_rows = total_rows.data_ptr<int>();
+  a.epoch = reinterpret_cast<uint32_t*>(epoch.data_ptr<int>());
+  a.status = status_ptr(status);
+  a.timeout_ns = static_cast<uint64_t>(timeout_s * 1e9);
+  return a;
+}
+
+void ep_counts(const torch::Tensor& topk_ids, const torch::Tensor& peer_base, const std::vector<int64_t>& offs,
+               int64_t rank, int64_t world, int64_t experts, int64_t hidden, int64_t cap_rows, int64_t max_slots,
+               torch::Tensor& cursor, torch::Tensor& local_offsets, torch::Tensor& total_rows, torch::Tensor& epoch,
+               const c10::optional<torch::Tensor>& status, double timeout_s) {
+  const at::cuda::CUDAGuard guard(topk_ids.device());
+  auto a = ep_args(topk_ids, peer_base, offs, rank, world, experts, hidden, cap_rows, max_slots, cursor, local_offsets,
+                   total_rows, epoch, status, timeout_s);
+  check_launch(omni::ep_counts(a, at::cuda::getCurrentCUDAStream()), "ep_counts");
+}
+
+void ep_dispatch(const torch::Tensor& x, const torch::Tensor& topk_ids, const torch::Tensor& peer_base,
+                 const std::vector<int64_t>& offs, int64_t rank, int64_t world, int64_t experts, int64_t cap_rows,
+                 int64_t max_slots, torch::Tensor& cursor, torch::Tensor& local_offsets, torch::Tensor& total_rows,
+                 torch::Tensor& epoch, const c10::optional<torch::Tensor>& status, double timeout_s) {
+  OMNI_CHECK_BF16(x);
+  OMNI_CHECK_CONTIG(x);
+  TORCH_CHECK(x.size(0) == topk_ids.size(0), "x rows != topk_ids rows");
+  const at::cuda::CUDAGuard guard(x.device());
+  auto a = ep_args(topk_ids, peer_base, offs, rank, world, experts, x.size(1), cap_rows, max_slots, cursor,
+                   local_offsets, total_rows, epoch, status, timeout_s);
+  a.x = x.data_ptr();
+  check_launch(omni::ep_dispatch(a, at::cuda::getCurrentCUDAStream()), "ep_dispatch");
+}
+
+void ep_combine(const torch::Tensor& y, const torch::Tensor& topk_ids, const torch::Tensor& peer_base,
+                const std::vector<int64_t>& offs, int64_t rank, int64_t world, int64_t experts, int64_t cap_rows,
+                int64_t max_slots, torch::Tensor& cursor, torch::Tensor& local_offsets, torch::Tensor& total_rows,
+                torch::Tensor& epoch, const c10::optional<torch::Tensor>& status, double timeout_s) {
+  OMNI_CHECK_BF16(y);
+  TORCH_CHECK(y.stride(-1) == 1, "y rows");
+  const at::cuda::CUDAGuard guard(y.device());
+  auto a = ep_args(topk_ids, peer_base, offs, rank, world, experts, y.size(1), cap_rows, max_slots, cursor,
+                   local_offsets, total_rows, epoch, status, timeout_s);
+  check_launch(omni::ep_combine(a, y.data_ptr(), y.stride(0), at::cuda::getCurrentCUDAStream()), "ep_combine");
+}
+
 void sample(torch::Tensor& logits, torch::Tensor& out_tokens, const c10::optional<torch::Tensor>& temperature,
             const c10::optional<torch::Tensor>& top_k, const c10::optional<torch::Tensor>& top_p,
             const c10::optional<torch::Tensor>& min_p, const c10::optional<torch::Tensor>& rep_penalty,
@@ -510,6 +612,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine", &moe_combine, "MoE top-k weighted combine (+ shared expert)");
   m.def("embed", &embed, "embedding gather with multimodal overwrite");
   m.def("vq_embed", &vq_embed, "dual-AR input embedding with the scaled VQ codebook sum");
+  m.def("ipc_alloc", &ipc_alloc, "cudaMalloc + zero, returns the device address");
+  m.def("ipc_free", &ipc_free, "cudaFree");
+  m.def("ipc_handle", &ipc_handle, "CUDA IPC handle of an ipc_alloc buffer");
+  m.def("ipc_open", &ipc_open, "maps a peer's IPC handle, returns its address in this process");
+  m.def("ipc_close", &ipc_close, "unmaps a peer buffer");
+  m.def("tensor_at", &tensor_at, "non-owning CUDA tensor over a device address");
+  m.def("ep_counts", &ep_counts, "expert-parallel: exchange per-expert counts, derive offsets");
+  m.def("ep_dispatch", &ep_dispatch, "expert-parallel: rows to their experts' ranks (expert-major) + barrier");
+  m.def("ep_combine", &ep_combine, "expert-parallel: expert outputs back to their source slots + barrier");
   m.def("sample", &sample, "fused logits processing + sampling");
   m.def("snake", &snake, "Snake / SnakeBeta activation (channels-last)");
   m.def("conv1d_im2col", &conv1d_im2col, "causal dilated conv1d im2col rows");

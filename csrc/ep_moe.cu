@@ -30,8 +30,7 @@
 // The epoch of a layer is a device counter bumped by ep_counts, so the same
 // launches can be captured once in a CUDA graph and replayed.  Every wait is
 // bounded (%globaltimer); a wait that runs out writes status 2 and returns.
-// No TMA and no multicast: peer memory is only touched by plain vector loads
-// and stores.
+// No TMA here: peer memory is only touched by plain vector loads and stores.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -72,6 +71,7 @@ __device__ void wait_flags(const EpArgs& a, int phase, uint32_t epoch) {
     }
   }
   __syncthreads();
+  __threadfence_system();  // every thread's later reads of peer-written data follow the acquire
 }
 
 __device__ void signal_peers(const EpArgs& a, int phase, uint32_t epoch) {

@@ -228,4 +228,24 @@ cudaError_t dwconv1d_causal(const void* x, const float* w, const float* bias, vo
 cudaError_t conv2d_im2col(const void* x, void* out, int N, int H, int W, int C, int Ho, int Wo, int kh, int kw,
                           int stride, int pad, int K_stride, cudaStream_t stream);
 
+// Expert-parallel MoE exchange over peer memory (csrc/ep_moe.cu).
+struct EpArgs {
+  int rank, world, experts, local_experts, topk, hidden;
+  int tokens;                  // local tokens of this call
+  const int* topk_ids;         // [tokens, topk]
+  const void* x;               // [tokens, hidden] bf16 (dispatch)
+  const int64_t* peer_base;    // [world] base address of every rank's symmetric buffer (this process's mapping)
+  int64_t off_counts, off_flags, off_recv_x, off_recv_meta, off_comb;
+  int cap_rows, max_slots;
+  int* cursor;                 // [experts] scratch
+  int* local_offsets;          // [local_experts + 1] group offsets of the received rows
+  int* total_rows;             // [1]
+  uint32_t* epoch;             // [1] layer counter, bumped by ep_counts
+  int* status;
+  uint64_t timeout_ns;
+};
+cudaError_t ep_counts(const EpArgs& a, cudaStream_t stream);
+cudaError_t ep_dispatch(const EpArgs& a, cudaStream_t stream);
+cudaError_t ep_combine(const EpArgs& a, const void* y, int64_t y_stride, cudaStream_t stream);
+
 }  // namespace omni

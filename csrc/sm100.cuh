@@ -1,6 +1,6 @@
 // sm_100a building blocks shared by the hand-written kernels: mbarrier
-// pipelines with bounded waits, TMA tile loads (local memory only, never the
-// cluster-multicast form), tcgen05 MMA / TMEM management and the UMMA shared
+// pipelines with bounded waits, TMA tile loads (this GPU's own memory, one
+// destination CTA per load), tcgen05 MMA / TMEM management and the UMMA shared
 // memory / instruction descriptors.
 //
 // Every spin-wait in this file is bounded by a wall-clock limit read from
