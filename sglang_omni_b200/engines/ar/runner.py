@@ -21,6 +21,7 @@ from ...ops import prefill_tiles
 from ...ops.sampling import SamplingTensors, sample
 from ...environ import environ
 from ...utils.cuda_graph import capture_graph
+from ...utils.hostdev import h2d
 from ...utils.staging import PinnedRing
 from .kv_pool import KVPool
 from .request import ARRequest
@@ -101,8 +102,8 @@ class ARModelRunner:
         if self.seen is not None:
             self.seen[s].zero_()
             if req.prompt_ids and sp.repetition_penalty != 1.0:
-                ids = torch.tensor([i for i in req.prompt_ids if 0 <= i < self.cfg.vocab_size], dtype=torch.long)
-                self.seen[s, ids.to(self.device)] = 1
+                ids = [i for i in req.prompt_ids if 0 <= i < self.cfg.vocab_size]
+                self.seen[s, h2d(ids, self.device, torch.long)] = 1
 
     def release_slot(self, req: ARRequest):
         if req.slot > 0:
@@ -151,7 +152,7 @@ class ARModelRunner:
             bt[b, :len(r.pages)] = r.pages[:max_pages]
             if any_embeds:
                 if r.input_embeds is not None:
-                    embeds.append(r.input_embeds[s:e].to(dev, non_blocking=True))
+                    embeds.append(h2d(r.input_embeds[s:e], dev))
                 else:
                     embeds.append(None)
             if r.mm_index is not None:
@@ -164,12 +165,12 @@ class ARModelRunner:
                 sample_reqs.append(r)
             off += n
         req_t, tok0_t = prefill_tiles(q_lens, self.cfg.num_heads // self.cfg.num_kv_heads)
-        as_dev = lambda a: torch.from_numpy(a).to(dev, non_blocking=True)  # noqa: E731
+        as_dev = lambda a: h2d(a, dev)  # noqa: E731
         if any_embeds:
             parts = []
             for (r, s, e), emb in zip(chunks, embeds):
                 if emb is None:
-                    ids_d = torch.from_numpy(ids[cu[len(parts)]:cu[len(parts)] + (e - s)]).to(dev)
+                    ids_d = h2d(ids[cu[len(parts)]:cu[len(parts)] + (e - s)], dev)
                     emb = self.model.embed[ids_d.long()]
                 parts.append(emb.to(self.cfg.dtype))
             input_embeds = torch.cat(parts, 0)
@@ -186,7 +187,7 @@ class ARModelRunner:
                 mats.append(emb)
                 base += emb.shape[0]
             mm_index = as_dev(mm_index_np)
-            mm_embeds = torch.cat([m.to(dev, non_blocking=True) for m in mats], 0).to(self.cfg.dtype)
+            mm_embeds = torch.cat([h2d(m, dev) for m in mats], 0).to(self.cfg.dtype)
         deepstack = None
         if ds_items:
             nl = max(len(r.deepstack) for *_, r in ds_items)
@@ -201,14 +202,14 @@ class ARModelRunner:
                     if bool(sel.any()):
                         ps.append(p[sel] - s + o)
                         es.append(r.deepstack[li][sel.nonzero().squeeze(1)])
-                deepstack.append((torch.cat(ps).to(dev), torch.cat(es).to(dev)) if ps else None)
+                deepstack.append((h2d(torch.cat(ps), dev), h2d(torch.cat(es), dev)) if ps else None)
         capture = tuple(sorted({c for r, _, _ in chunks for c in r.capture_layers} |
                                {r.capture_prompt_layer for r, _, _ in chunks if r.capture_prompt_layer is not None}))
         fb = ForwardBatch(
             is_decode=False, positions=as_dev(pos), slot_mapping=as_dev(slots), kv_lens=as_dev(kv_lens),
             block_table=as_dev(bt), input_ids=as_dev(ids) if input_embeds is None else None,
-            input_embeds=input_embeds, cu_q=as_dev(cu), tile_req=torch.tensor(req_t, dtype=torch.int32).to(dev),
-            tile_tok0=torch.tensor(tok0_t, dtype=torch.int32).to(dev),
+            input_embeds=input_embeds, cu_q=as_dev(cu), tile_req=h2d(req_t, dev, torch.int32),
+            tile_tok0=h2d(tok0_t, dev, torch.int32),
             logits_indices=as_dev(np.asarray(logits_rows, dtype=np.int32)) if logits_rows else None,
             mm_index=mm_index, mm_embeds=mm_embeds, deepstack=deepstack, capture_layers=capture,
         )
@@ -228,7 +229,7 @@ class ARModelRunner:
         if not logits_rows:
             return None
         logits = self.model.logits(hidden)
-        row_slot = torch.tensor([r.slot for r in sample_reqs], dtype=torch.int32).to(dev, non_blocking=True)
+        row_slot = h2d([r.slot for r in sample_reqs], dev, torch.int32)
         toks = sample(logits, self.st, self.suppress, row_slot=row_slot, slot_tokens=self.slot_tokens)
         n = len(sample_reqs)
         host = self._next_tok_host()[:n]

@@ -33,6 +33,7 @@ from ...engines.ar.kv_pool import KVPool
 from ...environ import environ
 from ...ops.sampling import SamplingTensors, sample
 from ...utils.cuda_graph import capture_graph
+from ...utils.hostdev import h2d
 from ...utils.staging import PinnedRing
 from ..decoder import ForwardBatch
 from .model import S2ProDualAR
@@ -211,16 +212,16 @@ class DualARGenerator:
             base += s.vq_codes.shape[0]
         code_rows = torch.cat(rows)
         all_codes = torch.cat(codes, 0) if base else torch.zeros(1, self.ncb, dtype=torch.int32)
-        d = lambda a: torch.from_numpy(a).to(dev)  # noqa: E731
-        x = ops.vq_embed(sl.embed, m.codebook_embeddings, all_codes.to(dev), cfg.codebook_size, cfg.vq_scale,
-                         cfg.semantic_begin_id, cfg.semantic_end_id, ids=d(ids), code_row=code_rows.to(dev))
+        d = lambda a: h2d(a, dev)  # noqa: E731
+        x = ops.vq_embed(sl.embed, m.codebook_embeddings, d(all_codes), cfg.codebook_size, cfg.vq_scale,
+                         cfg.semantic_begin_id, cfg.semantic_end_id, ids=d(ids), code_row=d(code_rows))
         req, tok0 = ops.prefill_tiles(lens, sl.cfg.num_heads // sl.cfg.num_kv_heads)
         fb = ForwardBatch(is_decode=False, positions=d(pos), slot_mapping=d(slot_map),
-                          kv_lens=torch.tensor(lens, dtype=torch.int32, device=dev), block_table=d(bt),
-                          input_embeds=x, cu_q=d(cu), tile_req=torch.tensor(req, dtype=torch.int32, device=dev),
-                          tile_tok0=torch.tensor(tok0, dtype=torch.int32, device=dev), logits_indices=d(cu[1:] - 1))
+                          kv_lens=h2d(lens, dev, torch.int32), block_table=d(bt),
+                          input_embeds=x, cu_q=d(cu), tile_req=h2d(req, dev, torch.int32),
+                          tile_tok0=h2d(tok0, dev, torch.int32), logits_indices=d(cu[1:] - 1))
         hidden = sl(fb, self.pool.kv)
-        slots = torch.tensor([s.slot for s in streams], dtype=torch.int32, device=dev)
+        slots = h2d([s.slot for s in streams], dev, torch.int32)
         out = self._tail(hidden, slots)
         for s, n in zip(streams, lens):
             s.num_cached = n

@@ -39,6 +39,7 @@ from ....executors.interface import Executor, ResultQueueMixin
 from ....executors.preprocessing_executor import StageError
 from ....ops.mel import LogMel
 from ....proto import StagePayload
+from ....utils.hostdev import h2d
 from ...common.ar_stage import sampling_for
 from ...common.tokenizer import IncrementalDetokenizer, load_tokenizer
 from .. import loader
@@ -463,7 +464,7 @@ class TalkerStreamingExecutor(ResultQueueMixin, Executor):
             if pending_tokens:
                 rids = list(pending_tokens)
                 flat = [t for r in rids for t in pending_tokens[r]]
-                proj = self.talker.project_text(self.embed[torch.tensor(flat, device=self.device)])
+                proj = self.talker.project_text(self.embed[h2d(flat, self.device, torch.long)])
                 o = 0
                 for r in rids:
                     n = len(pending_tokens[r])
@@ -476,9 +477,12 @@ class TalkerStreamingExecutor(ResultQueueMixin, Executor):
                 self._emit(ready, gen.step(ready))
 
     def _scatter_mm(self, mm, L):
-        full = torch.zeros(L, mm["mm_hidden"].shape[-1], dtype=mm["mm_hidden"].dtype, device=self.device)
+        hid = mm["mm_hidden"]
+        full = torch.zeros(L, hid.shape[-1], dtype=hid.dtype, device=self.device)
         mask = mm["mm_mask"][:L]
-        full[mask.to(self.device)] = mm["mm_hidden"].to(self.device)[: int(mask.sum())]
+        sel = (mask.cpu() if mask.is_cuda else mask).nonzero().view(-1)   # host-side: no device sync
+        if sel.numel():
+            full.index_copy_(0, h2d(sel, self.device), hid.to(self.device)[: sel.numel()])
         return full
 
     def _has_work(self) -> bool:

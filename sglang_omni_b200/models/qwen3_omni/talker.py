@@ -37,6 +37,7 @@ from ...engines.ar.kv_pool import KVPool
 from ...ops.sampling import SamplingTensors, sample
 from ...environ import environ
 from ...utils.cuda_graph import capture_graph
+from ...utils.hostdev import h2d
 from ...utils.staging import PinnedRing
 from ..decoder import DecoderConfig, DecoderLM, ForwardBatch
 from .hf_config import code_predictor_config, talker_text_config
@@ -139,26 +140,27 @@ def build_talker_prefill(talker: Qwen3OmniTalker, thinker_embed: torch.Tensor, p
     ids = list(prompt_ids)
     segs = segment_chat_template(ids, sp)
     parts = []
-    pad_e, bos_e, eos_e = (talker.project_text(thinker_embed[torch.tensor([t], device=dev)])
-                           for t in (sp.tts_pad, sp.tts_bos, sp.tts_eos))
+    pad_e, bos_e, eos_e = talker.project_text(thinker_embed[h2d([sp.tts_pad, sp.tts_bos, sp.tts_eos], dev,
+                                                                 torch.long)]).split(1, 0)
+    mm_cpu = None if mm_mask is None else mm_mask.cpu() if mm_mask.is_cuda else mm_mask
     for role, s, e in segs:
         if role != "user":
             continue
-        tok = torch.tensor(ids[s:e], device=dev)
-        emb = talker.project_text(thinker_embed[tok])
-        if mm_mask is not None and mm_hidden is not None:
-            m = mm_mask[s:e].to(dev)
-            if bool(m.any()):
-                emb[m] = talker.project_hidden(mm_hidden[s:e][m].to(dev)).to(emb.dtype)
+        emb = talker.project_text(thinker_embed[h2d(ids[s:e], dev, torch.long)])
+        if mm_cpu is not None and mm_hidden is not None:
+            sel = mm_cpu[s:e].nonzero().view(-1)           # host-side: no device sync
+            if sel.numel():
+                rows = mm_hidden[s:e].index_select(0, h2d(sel, mm_hidden.device))
+                emb.index_copy_(0, h2d(sel, dev), talker.project_hidden(rows.to(dev)).to(emb.dtype))
         parts.append(emb)
     # assistant part: the template tokens "<|im_start|>assistant\n" then the response
     asst = [sp.im_start, sp.assistant, sp.newline] + list(first_tokens)
-    proj = talker.project_text(thinker_embed[torch.tensor(asst, device=dev)])
+    proj = talker.project_text(thinker_embed[h2d(asst, dev, torch.long)])
     fourth = proj[3:4] if proj.shape[0] > 3 else torch.zeros_like(proj[:1])
     text_side = torch.cat([proj[:3], pad_e.expand(4, -1), bos_e, fourth], 0)
     spk = sp.speakers.get((speaker or sp.default_speaker).lower(), next(iter(sp.speakers.values())))
-    codec_ids = torch.tensor([sp.codec_nothink, sp.codec_think_bos, sp.codec_think_eos, spk, sp.codec_pad,
-                              sp.codec_bos], device=dev)
+    codec_ids = h2d([sp.codec_nothink, sp.codec_think_bos, sp.codec_think_eos, spk, sp.codec_pad, sp.codec_bos],
+                    dev, torch.long)
     codec_side = torch.cat([torch.zeros(3, proj.shape[1], dtype=proj.dtype, device=dev),
                             talker.codec_embed(codec_ids).to(proj.dtype)], 0)
     parts.append(text_side + codec_side)
@@ -349,15 +351,14 @@ class SpeechGenerator:
         for i, s in enumerate(streams):
             bt[i, :len(s.pages)] = s.pages
         req, tok0 = ops.prefill_tiles(lens, tl.cfg.num_heads // tl.cfg.num_kv_heads)
-        d = lambda a: torch.from_numpy(a).to(dev)  # noqa: E731
+        d = lambda a: h2d(a, dev)  # noqa: E731
         fb = ForwardBatch(is_decode=False, positions=d(np.stack([pos] * 3)), slot_mapping=d(slot_map),
-                          kv_lens=torch.tensor(lens, dtype=torch.int32, device=dev), block_table=d(bt),
+                          kv_lens=h2d(lens, dev, torch.int32), block_table=d(bt),
                           input_embeds=torch.cat(embeds, 0).to(tl.cfg.dtype), cu_q=d(cu),
-                          tile_req=torch.tensor(req, dtype=torch.int32, device=dev),
-                          tile_tok0=torch.tensor(tok0, dtype=torch.int32, device=dev),
+                          tile_req=h2d(req, dev, torch.int32), tile_tok0=h2d(tok0, dev, torch.int32),
                           logits_indices=d(cu[1:] - 1))
         hidden = tl(fb, self.pool.kv)
-        slots = torch.tensor([s.slot for s in streams], dtype=torch.int32, device=dev)
+        slots = h2d([s.slot for s in streams], dev, torch.int32)
         cp_bt = (slots + 1).view(-1, 1).to(torch.int32)
         cp_base = (slots + 1) * 64
         codes = self._talker_tail(hidden, slots, cp_bt, cp_base)
