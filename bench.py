@@ -48,6 +48,9 @@ def parse():
     ap.add_argument("--s2pro-streams", type=int, default=64)
     ap.add_argument("--s2pro-audio-s", type=float, default=15.0)
     ap.add_argument("--thinker", type=int, default=1, help="run the thinker serving phase (headline value)")
+    ap.add_argument("--ep", type=int, default=1,
+                    help="N>1: experts sharded over the GPUs (expert parallel MoE over NVLink, data-parallel "
+                         "attention); 0: one full replica per GPU")
     return ap.parse_args()
 
 
@@ -295,7 +298,17 @@ def main():
         return
 
     cfg = thinker_text_config(num_layers=args.layers)
-    model = loader.get_thinker("random", dev, {"thinker": {"num_layers": args.layers}} if args.layers != 48 else None)
+    ep = None
+    if world > 1 and args.ep:
+        from sglang_omni_b200.models.decoder import DecoderLM as _DLM
+        from sglang_omni_b200.parallel import EPMoE
+
+        ep = EPMoE(cfg.num_experts, cfg.topk, cfg.hidden_size, cfg.moe_intermediate_size,
+                   max_tokens=max(args.max_prefill_tokens, args.requests), device=dev)
+        model = _DLM(cfg, dev, ep=ep).random_init_(seed=loader.SEEDS["thinker"])
+    else:
+        model = loader.get_thinker("random", dev,
+                                   {"thinker": {"num_layers": args.layers}} if args.layers != 48 else None)
     max_ctx = ((args.prompt_len + args.output_len + 63) // 64) * 64
     pages_needed = args.requests * (max_ctx // 64) + 64
     pool = KVPool(cfg.num_layers, cfg.num_kv_heads, cfg.head_dim, pages_needed + 1, dev)
@@ -398,7 +411,8 @@ def main():
                 "global_batch": args.requests * world,
                 "seq_len": args.prompt_len,
                 "output_len": args.output_len,
-                "parallelism": f"dp{world}" if world > 1 else "tp1",
+                "parallelism": (f"ep{world} (experts sharded, peer-memory dispatch/combine) + dp{world} attention"
+                                if ep is not None else f"dp{world}" if world > 1 else "tp1"),
                 "step": "one serving round: 64 requests x (1024 prompt -> 256 greedy tokens) per GPU",
                 "l2": "inputs larger than L2 (61 GB of weights streamed per decode step)",
                 "ttft_p50_ms": round(1e3 * statistics.median(ttfts), 2),
@@ -424,6 +438,12 @@ def main():
         }
         print(json.dumps(line))
     if world > 1:
+        if ep is not None:
+            eng = pool = model = None  # release the decode graphs that reference the exchange buffers
+            import gc
+
+            gc.collect()
+            ep.close()
         dist.destroy_process_group()
 
 

@@ -115,9 +115,14 @@ class ForwardBatch:
 class DecoderLM(nn.Module):
     """Weights as plain parameters in fused layouts; forward is op-by-op on the kernels."""
 
-    def __init__(self, cfg: DecoderConfig, device="cpu"):
+    def __init__(self, cfg: DecoderConfig, device="cpu", ep=None):
+        """``ep``: an ``parallel.EPMoE`` exchange; this rank then holds experts
+        [ep.rank * El, (ep.rank + 1) * El) and the MoE layers run expert-parallel."""
         super().__init__()
         self.cfg = cfg
+        self.ep = ep
+        self.num_local_experts = cfg.num_experts if ep is None else ep.local_experts
+        self.expert0 = 0 if ep is None else ep.rank * self.num_local_experts
         H, dt = cfg.hidden_size, cfg.dtype
         P = lambda *shape: nn.Parameter(torch.empty(*shape, dtype=dt, device=device), requires_grad=False)  # noqa: E731
         self.embed = P(cfg.vocab_size, H)
@@ -134,8 +139,8 @@ class DecoderLM(nn.Module):
             if cfg.is_moe_layer(i):
                 E, I = cfg.num_experts, cfg.moe_intermediate_size
                 L.router = P(E, H)
-                L.w13 = P(E, 2 * I, H)
-                L.w2 = P(E, H, I)
+                L.w13 = P(self.num_local_experts, 2 * I, H)
+                L.w2 = P(self.num_local_experts, H, I)
                 if cfg.router_mode == 1:
                     L.router_bias = nn.Parameter(torch.zeros(E, dtype=torch.float32, device=device),
                                                  requires_grad=False)
@@ -162,13 +167,19 @@ class DecoderLM(nn.Module):
     # ------------------------------------------------------------------ init
     @torch.no_grad()
     def random_init_(self, seed: int = 0, std: float = 0.02):
-        """N(0, std) for matrices, ones for norm weights; deterministic per parameter."""
+        """N(0, std) for matrices, ones for norm weights; deterministic per parameter
+        (per expert for expert weights, so an expert-parallel rank draws exactly its
+        slice of the full model)."""
         dev = self.embed.device
         for idx, (name, p) in enumerate(self.named_parameters()):
             if p.dim() == 1 and ("ln" in name or "norm" in name):
                 p.fill_(1.0)
             elif name.endswith("router_bias"):
                 p.zero_()
+            elif name.endswith((".w13", ".w2")):
+                for j in range(p.shape[0]):
+                    g = torch.Generator(device=dev).manual_seed((seed * 100003 + idx) * 1009 + self.expert0 + j)
+                    p[j].normal_(0.0, std, generator=g)
             else:
                 g = torch.Generator(device=dev).manual_seed(seed * 100003 + idx)
                 p.normal_(0.0, std, generator=g)
@@ -185,7 +196,7 @@ class DecoderLM(nn.Module):
         A replaced workspace is kept alive (``_retired_ws``): CUDA graphs that
         were captured with it still read and write its memory on replay."""
         cfg, dev = self.cfg, self.embed.device
-        if cfg.num_experts and (self._moe_ws is None or self._moe_ws.max_tokens < max_tokens):
+        if cfg.num_experts and self.ep is None and (self._moe_ws is None or self._moe_ws.max_tokens < max_tokens):
             if self._moe_ws is not None:
                 self._retired_ws.append(self._moe_ws)
             self._moe_ws = MoEWorkspace(max_tokens, cfg.num_experts, cfg.topk, cfg.hidden_size,
@@ -207,6 +218,12 @@ class DecoderLM(nn.Module):
                 shared_out = ops.linear(ops.linear(x, L.s13, gated=True), L.s2)
                 if cfg.shared_expert_gate:
                     shared_gate = ops.linear(x, L.sgate, out_dtype=torch.float32)
+            if self.ep is not None:
+                return self.ep.forward(x, L.router, L.w13, L.w2, renormalize=cfg.norm_topk_prob,
+                                       mode=cfg.router_mode, bias=getattr(L, "router_bias", None),
+                                       n_group=cfg.n_group, topk_group=cfg.topk_group,
+                                       scaling=cfg.routed_scaling_factor, shared_out=shared_out,
+                                       shared_gate=shared_gate)
             if self._moe_ws is None:
                 self.ensure_workspaces(max(x.shape[0], 4096), 1, 64)
             ws = self._moe_ws

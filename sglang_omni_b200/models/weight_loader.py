@@ -78,14 +78,15 @@ def load_decoder_from_hf(model: DecoderLM, sd: dict[str, torch.Tensor], model_pr
         if cfg.is_moe_layer(i):
             cp(L.router, g(p + "mlp.gate.weight"))
             stacked = model_prefix + p + "mlp.experts.gate_up_proj"
+            e0, El = getattr(model, "expert0", 0), L.w13.shape[0]   # this rank's experts (expert parallel)
             if stacked in sd:
-                cp(L.w13, sd[stacked])
-                cp(L.w2, g(p + "mlp.experts.down_proj"))
+                cp(L.w13, sd[stacked][e0:e0 + El])
+                cp(L.w2, g(p + "mlp.experts.down_proj")[e0:e0 + El])
             else:
-                for e in range(cfg.num_experts):
-                    q = p + f"mlp.experts.{e}."
-                    L.w13[e].copy_(torch.cat([g(q + "gate_proj.weight"), g(q + "up_proj.weight")], 0).to(L.w13.dtype))
-                    L.w2[e].copy_(g(q + "down_proj.weight").to(L.w2.dtype))
+                for j in range(El):
+                    q = p + f"mlp.experts.{e0 + j}."
+                    L.w13[j].copy_(torch.cat([g(q + "gate_proj.weight"), g(q + "up_proj.weight")], 0).to(L.w13.dtype))
+                    L.w2[j].copy_(g(q + "down_proj.weight").to(L.w2.dtype))
             if hasattr(L, "router_bias") and model_prefix + p + "mlp.gate.e_score_correction_bias" in sd:
                 cp(L.router_bias, g(p + "mlp.gate.e_score_correction_bias"))
             if cfg.shared_expert_intermediate_size:
