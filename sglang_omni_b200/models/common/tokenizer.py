@@ -75,3 +75,54 @@ class IncrementalDetokenizer:
         delta = text[self.emitted:]
         self.emitted = len(text)
         return delta
+
+
+class SpecialsByteTokenizer(ByteTokenizer):
+    """ByteTokenizer that also maps a fixed list of special-token strings to ids
+    ``base, base + 1, ...`` (for random-init deployments of models whose prompts
+    are built from special tokens)."""
+
+    def __init__(self, specials: list[str], vocab_size: int, base: int | None = None, eos: str | None = None):
+        super().__init__(vocab_size)
+        import re
+
+        base = base if base is not None else vocab_size - len(specials) - 1
+        if base < self.offset + 256:
+            raise ValueError("vocabulary too small for bytes and special tokens")
+        self._tok2id = {s: base + i for i, s in enumerate(specials)}
+        self._id2tok = {v: k for k, v in self._tok2id.items()}
+        self._re = re.compile("(" + "|".join(re.escape(s) for s in sorted(specials, key=len, reverse=True)) + ")")
+        if eos is not None:
+            self.eos_token_id = self._tok2id[eos]
+
+    def convert_tokens_to_ids(self, token):
+        if isinstance(token, (list, tuple)):
+            return [self.convert_tokens_to_ids(t) for t in token]
+        return self._tok2id[token]
+
+    def encode(self, text: str, add_special_tokens: bool = False) -> list[int]:
+        ids: list[int] = []
+        for piece in self._re.split(text):
+            if not piece:
+                continue
+            if piece in self._tok2id:
+                ids.append(self._tok2id[piece])
+            else:
+                ids.extend(super().encode(piece))
+        return ids
+
+    def decode(self, ids, skip_special_tokens: bool = True) -> str:
+        out, run = [], []
+        for i in ids:
+            i = int(i)
+            if i in self._id2tok:
+                if run:
+                    out.append(super().decode(run))
+                    run = []
+                if not skip_special_tokens:
+                    out.append(self._id2tok[i])
+            else:
+                run.append(i)
+        if run:
+            out.append(super().decode(run))
+        return "".join(out)

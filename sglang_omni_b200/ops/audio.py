@@ -33,10 +33,12 @@ def snake(x: torch.Tensor, alpha: torch.Tensor, beta: torch.Tensor | None = None
 
 def causal_conv1d(x: torch.Tensor, w2d: torch.Tensor, bias: torch.Tensor | None, kernel: int, dilation: int = 1,
                   stride: int = 1, pad_left: int | None = None, t_out: int | None = None,
-                  residual: torch.Tensor | None = None) -> torch.Tensor:
+                  residual: torch.Tensor | None = None, act=None) -> torch.Tensor:
     """x [B, T, Cin]; w2d [Cout, K*Cin] in (tap, channel) order -> [B, T_out, Cout].
 
-    Default padding is causal: (K-1)*dil - (stride-1) on the left (HF CausalConvNet)."""
+    Default padding is causal: (K-1)*dil - (stride-1) on the left (HF CausalConvNet); positions
+    past the input on either side read zeros, so ``pad_left`` + ``t_out`` also express symmetric
+    padding.  ``act`` ("gelu" / "silu") runs in the GEMM epilogue."""
     B, T, C = x.shape
     eff = (kernel - 1) * dilation + 1
     if pad_left is None:
@@ -51,6 +53,10 @@ def causal_conv1d(x: torch.Tensor, w2d: torch.Tensor, bias: torch.Tensor | None,
         w = w2d.float().view(w2d.shape[0], kernel, C).permute(0, 2, 1)
         y = F.conv1d(xp, w, None if bias is None else bias.float(), stride=stride, dilation=dilation)
         y = y.transpose(1, 2)[:, :t_out]
+        if act == "gelu":
+            y = F.gelu(y)
+        elif act == "silu":
+            y = F.silu(y)
         if residual is not None:
             y = y + residual.float()
         return y.to(x.dtype)
@@ -59,7 +65,7 @@ def causal_conv1d(x: torch.Tensor, w2d: torch.Tensor, bias: torch.Tensor | None,
     else:
         cols = torch.empty(B, t_out, kernel * C, dtype=x.dtype, device=x.device)
         ext().conv1d_im2col(x.contiguous(), cols, kernel, dilation, stride, pad_left)
-    return linear(cols, w2d, bias=bias, residual=residual)
+    return linear(cols, w2d, bias=bias, residual=residual, act=act)
 
 
 def conv_transpose1d(x: torch.Tensor, w_t: torch.Tensor, bias: torch.Tensor | None, stride: int,
