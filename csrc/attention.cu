@@ -336,6 +336,7 @@ struct DecodeParams {
   float* part_o;    // [B, Hq, max_splits, D]
   float* part_lse;  // [B, Hq, max_splits]
   int num_pages;
+  int* counters;    // [B, Hkv] zeros: split arrivals (nullptr: separate combine launch)
 };
 
 
@@ -527,6 +528,34 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
       if (d == 0) p.part_lse[slot] = L > 0.f ? sub + log2f(L) : -INFINITY;
     }
   }
+  if (nsplit == 1 || p.counters == nullptr) return;
+  // The last split of (request, KV head) to finish merges all splits: no second launch.
+  __shared__ int s_last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int* c = p.counters + static_cast<int64_t>(b) * p.hkv + h;
+    const int done = atomicAdd(c, 1) + 1;
+    s_last = done == nsplit;
+    if (s_last) *c = 0;  // ready for the next launch (graph replays reuse the counters)
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
+    const int r = idx / D, d = idx - r * D;
+    const int64_t slot0 = (static_cast<int64_t>(b) * p.hq + h * G + r) * p.max_splits;
+    float M = -INFINITY;
+    for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, __ldcg(p.part_lse + slot0 + sp));
+    const float sub = M == -INFINITY ? 0.f : M;
+    float L = 0.f, acc = 0.f;
+    for (int sp = 0; sp < nsplit; ++sp) {
+      const float f = exp2f(__ldcg(p.part_lse + slot0 + sp) - sub);
+      L += f;
+      acc += f * __ldcg(p.part_o + (slot0 + sp) * D + d);
+    }
+    p.out[static_cast<int64_t>(b) * p.out_stride + (h * G + r) * D + d] = __float2bfloat16(L > 0.f ? acc / L : 0.f);
+  }
 }
 
 template <int D>
@@ -578,7 +607,7 @@ cudaError_t launch_decode(const DecodeParams& p, int batch, cudaStream_t stream)
   }
   dim3 grid(p.max_splits, p.hkv, batch);
   decode_kernel<D><<<grid, 128, smem, stream>>>(p);
-  if (p.max_splits > 1) {
+  if (p.max_splits > 1 && p.counters == nullptr) {
     dim3 g2(p.hq, batch);
     decode_combine_kernel<D><<<g2, D, 0, stream>>>(p);
   }
@@ -640,6 +669,7 @@ cudaError_t attention_decode(const AttnDecodeArgs& a, cudaStream_t stream) {
   p.part_o = a.part_o;
   p.part_lse = a.part_lse;
   p.num_pages = a.num_pages;
+  p.counters = a.counters;
   switch (a.head_dim) {
     case 64: return launch_decode<64>(p, a.batch, stream);
     case 128: return launch_decode<128>(p, a.batch, stream);

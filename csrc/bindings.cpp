@@ -196,7 +196,8 @@ void attention_prefill(const torch::Tensor& q, const torch::Tensor& k, const tor
 void attention_decode(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, torch::Tensor& out,
                       const torch::Tensor& block_table, const torch::Tensor& kv_lens, int64_t hq, int64_t hkv,
                       int64_t head_dim, double scale, int64_t keys_per_split, int64_t max_splits,
-                      torch::Tensor& part_o, torch::Tensor& part_lse) {
+                      torch::Tensor& part_o, torch::Tensor& part_lse,
+                      const c10::optional<torch::Tensor>& counters) {
   OMNI_CHECK_CUDA(q);
   OMNI_CHECK_BF16(q);
   TORCH_CHECK(q.stride(-1) == 1 && out.stride(-1) == 1, "rows must be contiguous");
@@ -224,6 +225,10 @@ void attention_decode(const torch::Tensor& q, const torch::Tensor& k, const torc
   a.part_o = part_o.data_ptr<float>();
   a.part_lse = part_lse.data_ptr<float>();
   a.num_pages = static_cast<int>(k.size(0));
+  if (counters.has_value()) {
+    TORCH_CHECK(counters->scalar_type() == at::kInt && counters->numel() >= batch * hkv, "split counters int32 [B, hkv]");
+    a.counters = counters->data_ptr<int>();
+  }
   check_launch(omni::attention_decode(a, at::cuda::getCurrentCUDAStream()), "attention_decode");
 }
 

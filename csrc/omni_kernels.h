@@ -101,6 +101,7 @@ struct AttnDecodeArgs {
   float* part_o;          // scratch [B, hq, max_splits, D] fp32
   float* part_lse;        // scratch [B, hq, max_splits] fp32
   int num_pages;          // as in AttnPrefillArgs (0 = unchecked)
+  int* counters;          // [B, hkv] int32 zeros: the last split merges (nullptr: separate combine launch)
 };
 cudaError_t attention_decode(const AttnDecodeArgs& a, cudaStream_t stream);
 

@@ -24,6 +24,7 @@ from collections import deque
 
 import torch
 
+from ...utils.hostdev import own_stream
 from .kv_pool import KVPool
 from .request import ARRequest
 from .runner import ARModelRunner
@@ -288,6 +289,9 @@ class ThreadedAREngine:
 
     def _run(self):
         eng = self.engine
+        stream = own_stream(eng.runner.device) if eng.runner.is_cuda else None
+        if stream is not None:
+            torch.cuda.set_stream(stream)  # this thread's work queues behind nobody else's
         try:
             eng.runner.capture_all()  # every decode bucket, before the first request (not on its latency path)
             while True:

@@ -21,7 +21,7 @@ from ...ops import prefill_tiles
 from ...ops.sampling import SamplingTensors, sample
 from ...environ import environ
 from ...utils.cuda_graph import capture_graph
-from ...utils.hostdev import h2d
+from ...utils.hostdev import adopt, h2d
 from ...utils.staging import PinnedRing
 from .kv_pool import KVPool
 from .request import ARRequest
@@ -152,7 +152,7 @@ class ARModelRunner:
             bt[b, :len(r.pages)] = r.pages[:max_pages]
             if any_embeds:
                 if r.input_embeds is not None:
-                    embeds.append(h2d(r.input_embeds[s:e], dev))
+                    embeds.append(h2d(adopt(r.input_embeds)[s:e], dev))
                 else:
                     embeds.append(None)
             if r.mm_index is not None:
@@ -187,7 +187,7 @@ class ARModelRunner:
                 mats.append(emb)
                 base += emb.shape[0]
             mm_index = as_dev(mm_index_np)
-            mm_embeds = torch.cat([h2d(m, dev) for m in mats], 0).to(self.cfg.dtype)
+            mm_embeds = torch.cat([h2d(adopt(m), dev) for m in mats], 0).to(self.cfg.dtype)
         deepstack = None
         if ds_items:
             nl = max(len(r.deepstack) for *_, r in ds_items)

@@ -12,6 +12,8 @@ import asyncio
 import logging
 from typing import Any
 
+import torch
+
 from ..base import Engine
 from .types import RequestOutput, SchedulerOutput
 
@@ -70,9 +72,9 @@ class OmniEngine(Engine):
         reqs_all = list(sched_out.requests)
         if sched_out.requests:
             if self.run_in_thread:
-                res = await asyncio.to_thread(self.model_runner.execute, sched_out)
+                res = await asyncio.to_thread(_execute_synced, self.model_runner, sched_out)
             else:
-                res = self.model_runner.execute(sched_out)
+                res = _execute_synced(self.model_runner, sched_out)
             outputs.update(res.outputs)
             if self.cache is not None:
                 for r in sched_out.requests:
@@ -101,3 +103,12 @@ class OmniEngine(Engine):
             except Exception as exc:
                 log.exception("engine step failed")
                 self.scheduler.fail(sched_out, exc)
+
+
+def _execute_synced(runner, sched_out):
+    """Runs one batch and waits for its GPU work: its output tensors go to other
+    stages, whose threads run on their own streams."""
+    res = runner.execute(sched_out)
+    if torch.cuda.is_available() and torch.cuda.is_initialized():
+        torch.cuda.current_stream().synchronize()
+    return res

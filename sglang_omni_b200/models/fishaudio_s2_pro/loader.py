@@ -30,6 +30,14 @@ def _key(model_path, name, device, overrides):
     return (model_path, name, str(device), json.dumps(overrides or {}, sort_keys=True, default=str))
 
 
+def _ready(obj):
+    """Components are built once and then used from several threads, each on its own
+    CUDA stream: finish their initialisation before anyone can see them."""
+    if torch.cuda.is_available() and torch.cuda.is_initialized():
+        torch.cuda.synchronize()
+    return obj
+
+
 def _apply(obj, over: dict | None):
     for k, v in (over or {}).items():
         setattr(obj, k, v)
@@ -71,6 +79,7 @@ def get_model(model_path: str, device, overrides: dict | None = None) -> S2ProDu
         m.load_state_dict_fish(load_by_prefix(model_path, ""))
     else:
         m.random_init_(seed=SEEDS["model"])
+    _ready(m)
     with _LOCK:
         _CACHE.setdefault(k, m)
         return _CACHE[k]
@@ -103,6 +112,7 @@ def get_decoder(model_path: str, device, overrides: dict | None = None) -> DACDe
         if k in _CACHE:
             return _CACHE[k]
     dec = DACDecoder(dac_config(overrides), device).load_state_dict_dac(get_codec_state(model_path, overrides))
+    _ready(dec)
     with _LOCK:
         _CACHE.setdefault(k, dec)
         return _CACHE[k]
@@ -114,6 +124,7 @@ def get_encoder(model_path: str, device, overrides: dict | None = None) -> DACEn
         if k in _CACHE:
             return _CACHE[k]
     enc = DACEncoder(get_codec_state(model_path, overrides), dac_config(overrides), device)
+    _ready(enc)
     with _LOCK:
         _CACHE.setdefault(k, enc)
         return _CACHE[k]

@@ -33,6 +33,7 @@ from ....executors import PreprocessingExecutor
 from ....executors.interface import Executor, ResultQueueMixin
 from ....executors.preprocessing_executor import StageError
 from ....proto import StagePayload
+from ....utils.hostdev import own_stream
 from .. import loader
 from ..generator import DualARGenerator, stream_seed
 from ..tokenizer import Reference, S2ProPromptBuilder
@@ -230,6 +231,9 @@ class S2ProTTSExecutor(ResultQueueMixin, Executor):
             self._post(q.put_nowait, None)
 
     def _run(self):
+        stream = own_stream(self.device)
+        if stream is not None:
+            torch.cuda.set_stream(stream)
         try:
             with torch.inference_mode():
                 self.gen.capture_all()
@@ -321,6 +325,9 @@ class S2ProTTSExecutor(ResultQueueMixin, Executor):
     def _vocoder_loop(self):
         """Decodes the stream windows of every stream with a chunk ready, batched:
         one decoder forward per (window length, context) group."""
+        stream = own_stream(self.device)
+        if stream is not None:
+            torch.cuda.set_stream(stream)  # chunks do not wait behind generation steps
         while True:
             jobs = [self._voc_q.get()]
             while True:

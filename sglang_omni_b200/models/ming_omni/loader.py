@@ -30,6 +30,14 @@ def _key(model_path, name, device, overrides):
     return (model_path, name, str(device), json.dumps(overrides or {}, sort_keys=True, default=str))
 
 
+def _ready(obj):
+    """Components are built once and then used from several threads, each on its own
+    CUDA stream: finish their initialisation before anyone can see them."""
+    if torch.cuda.is_available() and torch.cuda.is_initialized():
+        torch.cuda.synchronize()
+    return obj
+
+
 def _cfgs(model_path, overrides):
     c = configs_from_hf(model_path) if has_checkpoint(model_path) else {"llm": llm_config(), "whisper": WhisperConfig()}
     for k, v in ((overrides or {}).get("llm") or {}).items():
@@ -63,6 +71,7 @@ def get_llm(model_path: str, device, overrides: dict | None = None, ep=None) -> 
         load_bailing(m, load_by_prefix(model_path, "model."))
     else:
         m.random_init_(seed=SEEDS["llm"])
+    _ready(m)
     with _LOCK:
         _CACHE.setdefault(k, m)
         return _CACHE[k]
@@ -81,6 +90,7 @@ def get_audio_encoder(model_path: str, device, overrides: dict | None = None) ->
         enc.load_hf_state_dict(sd)
     else:
         enc.random_init_(seed=SEEDS["audio"])
+    _ready(enc)
     with _LOCK:
         _CACHE.setdefault(k, enc)
         return _CACHE[k]

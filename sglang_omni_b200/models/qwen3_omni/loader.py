@@ -32,6 +32,14 @@ def _key(model_path, name, device, overrides):
     return (model_path, name, str(device), json.dumps(overrides or {}, sort_keys=True, default=str))
 
 
+def _ready(obj):
+    """Components are built once and then used from several threads, each on its own
+    CUDA stream: finish their initialisation before anyone can see them."""
+    if torch.cuda.is_available() and torch.cuda.is_initialized():
+        torch.cuda.synchronize()
+    return obj
+
+
 def _cfgs(model_path):
     if has_checkpoint(model_path):
         return configs_from_hf(model_path)
@@ -57,6 +65,7 @@ def get_thinker(model_path: str, device, overrides: dict | None = None) -> Decod
             load_decoder_from_hf(m, sd, "model.", "lm_head.weight")
         else:
             m.random_init_(seed=SEEDS["thinker"])
+        _ready(m)
         _CACHE[k] = m
         return m
 
@@ -108,6 +117,7 @@ def get_talker(model_path: str, device, overrides: dict | None = None) -> Qwen3O
                     t.cp_embeds[gidx].copy_(cp[f"model.codec_embedding.{gidx}.weight"].to(t.cp_embeds.dtype))
         else:
             t.random_init_(seed=SEEDS["talker"])
+        _ready(t)
         _CACHE[k] = t
         return t
 
@@ -126,6 +136,7 @@ def get_audio_encoder(model_path: str, device, overrides: dict | None = None) ->
             m.load_hf_state_dict(load_by_prefix(model_path, "thinker.audio_tower."))
         else:
             m.random_init_(seed=SEEDS["audio"])
+        _ready(m)
         _CACHE[k] = m
         return m
 
@@ -145,6 +156,7 @@ def get_vision_encoder(model_path: str, device, overrides: dict | None = None):
             m.load_hf_state_dict(load_by_prefix(model_path, "thinker.visual."))
         else:
             m.random_init_(seed=SEEDS["vision"])
+        _ready(m)
         _CACHE[k] = m
         return m
 
@@ -160,5 +172,6 @@ def get_code2wav(model_path: str, device, overrides: dict | None = None) -> Code
             m.load_hf_state_dict(load_by_prefix(model_path, "code2wav."))
         else:
             m.random_init_(seed=SEEDS["code2wav"])
+        _ready(m)
         _CACHE[k] = m
         return m

@@ -39,7 +39,7 @@ from ....executors.interface import Executor, ResultQueueMixin
 from ....executors.preprocessing_executor import StageError
 from ....ops.mel import LogMel
 from ....proto import StagePayload
-from ....utils.hostdev import h2d
+from ....utils.hostdev import adopt, h2d, own_stream
 from ...common.ar_stage import sampling_for
 from ...common.tokenizer import IncrementalDetokenizer, load_tokenizer
 from .. import loader
@@ -193,8 +193,10 @@ def create_image_encoder_executor(model_path: str = "", device: str = "cuda:0", 
             return StagePayload(payload.request_id, payload.request, {"image_embeds": None})
         from ..vision_encoder import encode_images
 
-        return StagePayload(payload.request_id, payload.request,
-                            encode_images(model_path, torch.device(device), images, overrides))
+        out = encode_images(model_path, torch.device(device), images, overrides)
+        if torch.device(device).type == "cuda":
+            torch.cuda.current_stream().synchronize()  # the thinker reads these on its own stream
+        return StagePayload(payload.request_id, payload.request, out)
 
     return PreprocessingExecutor(run)
 
@@ -263,12 +265,14 @@ def create_thinker_executor(model_path: str = "", device: str = "cuda:0", max_ba
                     _sent["first"] = False
                     ph = r.extra.get("prompt_hidden")
                     if ph:
-                        full = torch.cat(ph, 0)
-                        mask = torch.zeros(full.shape[0], dtype=torch.bool)
+                        # the prefill rows are complete (this runs after the first token's event);
+                        # the talker gathers the multimodal rows on its own stream
+                        n = sum(t.shape[0] for t in ph)
+                        mask = torch.zeros(n, dtype=torch.bool)
                         for a, b in _spans:
                             mask[a:b] = True
                         msg["mm_mask"] = mask
-                        msg["mm_hidden"] = full[mask.to(full.device)]
+                        msg["mm_hidden_parts"] = list(ph)
                 if ex._stream_fn is not None:
                     ex._stream_fn(_rid, msg, speech_target)
 
@@ -370,8 +374,8 @@ class TalkerStreamingExecutor(ResultQueueMixin, Executor):
                     break
                 with self._cv:
                     data = item.data
-                    if "mm_hidden" in data:
-                        self._first[rid] = {"mm_mask": data["mm_mask"], "mm_hidden": data["mm_hidden"]}
+                    if "mm_hidden_parts" in data:
+                        self._first[rid] = {"mm_mask": data["mm_mask"], "parts": data["mm_hidden_parts"]}
                     self._tokens.setdefault(rid, []).append(int(data["token_id"]))
                     self._cv.notify_all()
         except Exception as exc:  # thinker stream error
@@ -399,6 +403,9 @@ class TalkerStreamingExecutor(ResultQueueMixin, Executor):
 
     # ---------------------------------------------------------------- generator thread
     def _run(self):
+        stream = own_stream(self.device)
+        if stream is not None:
+            torch.cuda.set_stream(stream)  # frames wait only for talker work, not for queued thinker steps
         try:
             with torch.inference_mode():
                 self.gen.capture_all()
@@ -456,7 +463,7 @@ class TalkerStreamingExecutor(ResultQueueMixin, Executor):
             new_streams = []
             for rid, ids, spk, first, mm in new_ready:
                 pre, trail, pad_e, eos_e = build_talker_prefill(
-                    self.talker, self.embed, ids, first, None if mm is None else mm["mm_mask"],
+                    self.talker, self.embed, ids, first, None if mm is None else mm["mm_mask"][:len(ids)],
                     None if mm is None else self._scatter_mm(mm, len(ids)), spk)
                 done_now = rid in self._done
                 new_streams.append(gen.add_stream(rid, pre, trail, pad_e, eos_e, thinker_done=done_now,
@@ -480,12 +487,13 @@ class TalkerStreamingExecutor(ResultQueueMixin, Executor):
                 self._emit(ready, gen.step(ready))
 
     def _scatter_mm(self, mm, L):
-        hid = mm["mm_hidden"]
+        parts = [adopt(t) for t in mm["parts"]]          # produced on the thinker's stream
+        hid = torch.cat(parts, 0) if len(parts) > 1 else parts[0]
         full = torch.zeros(L, hid.shape[-1], dtype=hid.dtype, device=self.device)
         mask = mm["mm_mask"][:L]
         sel = (mask.cpu() if mask.is_cuda else mask).nonzero().view(-1)   # host-side: no device sync
         if sel.numel():
-            full.index_copy_(0, h2d(sel, self.device), hid.to(self.device)[: sel.numel()])
+            full.index_copy_(0, h2d(sel, self.device), hid.to(self.device).index_select(0, h2d(sel, hid.device)))
         return full
 
     def _has_work(self) -> bool:

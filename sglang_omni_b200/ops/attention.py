@@ -147,6 +147,8 @@ class DecodeWorkspace:
         self.part_o = torch.empty(max_batch * num_heads * self.max_splits * head_dim, dtype=torch.float32,
                                   device=device)
         self.part_lse = torch.empty(max_batch * num_heads * self.max_splits, dtype=torch.float32, device=device)
+        # split arrival counters: the last split of a (request, KV head) merges in the same launch
+        self.counters = torch.zeros(max_batch * num_heads, dtype=torch.int32, device=device)
 
 
 def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table: torch.Tensor,
@@ -170,5 +172,6 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     if _check.enabled():
         _check.check_paged("attention_decode", block_table, kv_lens, k_cache.shape[0])
     ext().attention_decode(q, k_cache, v_cache, out, block_table, kv_lens, num_heads, num_kv_heads, head_dim, scale,
-                           workspace.keys_per_split, workspace.max_splits, workspace.part_o, workspace.part_lse)
+                           workspace.keys_per_split, workspace.max_splits, workspace.part_o, workspace.part_lse,
+                           getattr(workspace, "counters", None))
     return out

@@ -33,3 +33,23 @@ def h2d(data, device, dtype=None) -> torch.Tensor:
     if t.numel() == 0:
         return torch.empty(t.shape, dtype=t.dtype, device=device)
     return t.contiguous().pin_memory().to(device, non_blocking=True)
+
+
+def own_stream(device) -> "torch.cuda.Stream | None":
+    """A dedicated stream for one engine thread (None on CPU).  Engines of one
+    process then only wait for their own queued work when they synchronise."""
+    device = torch.device(device)
+    if device.type != "cuda":
+        return None
+    return torch.cuda.Stream(device=device)
+
+
+def adopt(t: torch.Tensor) -> torch.Tensor:
+    """Marks a device tensor produced on another thread's stream as used on the
+    current stream, so the allocator does not hand its memory back to the
+    producer stream while this stream's queued work still reads it.  The data
+    itself must already be complete (its producer synchronised, or the value
+    is known to be finished through a host-side signal)."""
+    if isinstance(t, torch.Tensor) and t.is_cuda:
+        t.record_stream(torch.cuda.current_stream(t.device))
+    return t
