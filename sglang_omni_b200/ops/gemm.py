@@ -17,21 +17,24 @@ from . import _check
 from ._ext import ext, status_word
 
 # Per-device split-K scratch of the dense GEMM: fp32 partial sums
-# [splits][rows][m_out], reduced by a second kernel.  One buffer serves every
-# dense GEMM issued on the device's (single) compute stream, including inside
-# captured CUDA graphs; GEMMs needing more fall back to no split.
+# [splits][rows][m_out], reduced by a second kernel.  One buffer per CUDA
+# stream: GEMMs of one stream are ordered, those of different engine threads'
+# streams may run concurrently.  A graph captured on a stream keeps using that
+# stream's buffer on replay (the capture streams are per thread, see
+# utils.cuda_graph).  GEMMs needing more than the buffer fall back to no split.
 _SPLITK_FLOATS = 8 * 1024 * 1024
 _SPLITK_COUNTERS = 16
-_splitk: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
+_splitk: dict[tuple[int, int], tuple[torch.Tensor, torch.Tensor]] = {}
 
 
 def splitk_scratch(device: torch.device):
     idx = device.index if device.index is not None else torch.cuda.current_device()
-    sc = _splitk.get(idx)
+    key = (idx, torch.cuda.current_stream(idx).cuda_stream)
+    sc = _splitk.get(key)
     if sc is None:
         sc = (torch.zeros(_SPLITK_FLOATS, dtype=torch.float32, device=device),
               torch.zeros(_SPLITK_COUNTERS, dtype=torch.int32, device=device))
-        _splitk[idx] = sc
+        _splitk[key] = sc
     return sc
 
 ACT_NONE, ACT_GELU_TANH, ACT_GELU_ERF, ACT_SILU = 0, 1, 2, 3

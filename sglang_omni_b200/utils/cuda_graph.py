@@ -13,9 +13,21 @@ process's work on that stream.
 """
 from __future__ import annotations
 
+import threading
 from typing import Any, Callable
 
 import torch
+
+
+_tls = threading.local()
+
+
+def _capture_stream() -> torch.cuda.Stream:
+    """One capture stream per thread (graphs captured by a thread share its per-stream scratch)."""
+    s = getattr(_tls, "stream", None)
+    if s is None or s.device != torch.device("cuda", torch.cuda.current_device()):
+        s = _tls.stream = torch.cuda.Stream()
+    return s
 
 
 def capture_graph(body: Callable[[], Any], warmup: int = 2, pool=None) -> tuple[torch.cuda.CUDAGraph, Any]:
@@ -29,7 +41,11 @@ def capture_graph(body: Callable[[], Any], warmup: int = 2, pool=None) -> tuple[
     # the work other threads keep queueing on that stream
     for _ in range(warmup):
         body()
-    side = torch.cuda.Stream()
+    side = _capture_stream()
+    with torch.cuda.stream(side):  # the stream's split-K scratch must exist before the capture starts
+        from ..ops.gemm import splitk_scratch
+
+        splitk_scratch(torch.device("cuda", torch.cuda.current_device()))
     side.wait_stream(cur)
     side.synchronize()
     g = torch.cuda.CUDAGraph()
