@@ -99,6 +99,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
   uint8_t* aux = smem + C::kStages * C::kStageBytes;
+  __shared__ int s_last;  // split-K: this CTA finalises the tile
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(aux);
   uint64_t* empty_bar = full_bar + C::kStages;
   uint64_t* tfull_bar = empty_bar + C::kStages;   // [2]
@@ -317,6 +318,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(&tempty_bar[acc]);
+      if (ks > 1 && p.counters != nullptr) {
+        // The last split of this tile to arrive sums the partials and runs the epilogue:
+        // no second launch.  Counters reset themselves for the next call / graph replay.
+        __threadfence();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (threadIdx.x == 64) {
+          const int prev = atomicAdd(&p.counters[t], 1);
+          s_last = prev == ks - 1;
+          if (s_last) p.counters[t] = 0;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (s_last) {
+          __threadfence();
+          if (m_ok) {
+            const int64_t plane = static_cast<int64_t>(p.rows) * p.m_out;
+            for (int row = row0; row < row_end && row < row0 + BN; ++row) {
+              const float* src = p.ws + static_cast<int64_t>(row) * p.m_out + m;
+              float v = 0.f;
+              for (int s = 0; s < ks; ++s) v += __ldcg(src + s * plane);
+              v += bias_v;
+              if (p.act == kActGeluTanh) v = gelu_tanh_f(v);
+              else if (p.act == kActGeluErf) v = gelu_erf_f(v);
+              else if (p.act == kActSilu) v = silu_f(v);
+              if (p.residual != nullptr) v += __bfloat162float(p.residual[static_cast<int64_t>(row) * p.ldr + m]);
+              if (p.out_f32) static_cast<float*>(p.out)[static_cast<int64_t>(row) * p.ldo + m] = v;
+              else static_cast<__nv_bfloat16*>(p.out)[static_cast<int64_t>(row) * p.ldo + m] = __float2bfloat16(v);
+            }
+          }
+        }
+      }
     }
   }
 
@@ -440,6 +471,8 @@ cudaError_t launch(const GemmArgs& a, cudaStream_t stream) {
         if (static_cast<long long>(ksp) * a.rows * a.m_out <= a.splitk_ws_floats) {
           p.k_splits = ksp;
           p.ws = a.splitk_ws;
+          // tiles within the counter slots: the last split finalises in-kernel (no reduce launch)
+          if (tiles <= a.splitk_counter_slots) p.counters = a.splitk_counters;
         }
       }
     }
@@ -451,7 +484,7 @@ cudaError_t launch(const GemmArgs& a, cudaStream_t stream) {
   if (bound < grid) grid = static_cast<int>(bound);
   if (grid < 1) grid = 1;
   gemm_bf16_kernel<BN, GATED><<<grid, kThreads, C::kSmemBytes, stream>>>(ta, tb, p);
-  if (p.k_splits > 1) {
+  if (p.k_splits > 1 && p.counters == nullptr) {
     const long long n = static_cast<long long>(a.rows) * a.m_out;
     int rgrid = static_cast<int>((n + 255) / 256);
     if (rgrid > 4 * num_sms()) rgrid = 4 * num_sms();

@@ -23,7 +23,7 @@ from ._ext import ext, status_word
 # stream's buffer on replay (the capture streams are per thread, see
 # utils.cuda_graph).  GEMMs needing more than the buffer fall back to no split.
 _SPLITK_FLOATS = 8 * 1024 * 1024
-_SPLITK_COUNTERS = 16
+_SPLITK_COUNTERS = 1024   # per-tile arrival counters of the in-kernel split-K finalisation
 _splitk: dict[tuple[int, int], tuple[torch.Tensor, torch.Tensor]] = {}
 
 
