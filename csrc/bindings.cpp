@@ -298,6 +298,8 @@ void moe_route(const torch::Tensor& logits, int64_t topk, int64_t mode, const c1
   a.offsets = opt_mut<int>(offsets);
   a.inv_perm = opt_mut<int>(inv_perm);
   if (a.counts) TORCH_CHECK(a.cursor && a.offsets && a.inv_perm, "permutation outputs required");
+  // a cursor with one extra slot (a done counter) makes the scatter leave counts / cursor zeroed itself
+  a.self_clean = a.counts && cursor->numel() > a.experts ? 1 : 0;
   if (x.has_value()) {
     OMNI_CHECK_BF16(*x);
     TORCH_CHECK(x_perm.has_value() && x->is_contiguous() && x->size(-1) % 8 == 0, "x / x_perm");

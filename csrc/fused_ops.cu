@@ -346,6 +346,21 @@ __global__ void moe_scatter_kernel(MoeRouteArgs a) {
       }
     }
   }
+  if (a.self_clean) {
+    // the last CTA to finish leaves counts / cursor zeroed for the next call (no memset launches)
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      if (atomicAdd(&a.cursor[a.experts], 1) + 1 == static_cast<int>(gridDim.x)) {
+        for (int e = 0; e < a.experts; ++e) {
+          a.counts[e] = 0;
+          a.cursor[e] = 0;
+        }
+        a.cursor[a.experts] = 0;
+        __threadfence();
+      }
+    }
+  }
 }
 
 // out[t] = sum_k w[t,k] * y[inv[t,k]] (+ sigmoid(gate[t]) * shared[t])
@@ -648,7 +663,7 @@ cudaError_t qkv_rope_store(const RopeStoreArgs& a, cudaStream_t stream) {
 cudaError_t moe_route(const MoeRouteArgs& a, cudaStream_t stream) {
   if (a.tokens == 0) return cudaSuccess;
   if (a.experts > 512 || a.topk > 16 || a.topk < 1) return cudaErrorInvalidValue;
-  if (a.counts) {
+  if (a.counts && !a.self_clean) {
     cudaMemsetAsync(a.counts, 0, sizeof(int) * a.experts, stream);
     cudaMemsetAsync(a.cursor, 0, sizeof(int) * a.experts, stream);
   }

@@ -133,10 +133,80 @@ __global__ void layernorm_kernel(const __nv_bfloat16* __restrict__ x, const __nv
 
 }  // namespace
 
+// One CTA per row (few rows: decode batches); each thread owns VPT 16-byte vectors.
+template <int VPT>
+__global__ void rmsnorm_row_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+                                   __nv_bfloat16* __restrict__ y, __nv_bfloat16* __restrict__ res, int hidden,
+                                   int64_t ld_x, int64_t ld_y, float eps) {
+  __shared__ float red[32];
+  const int row = blockIdx.x;
+  const int nvec = hidden >> 3;
+  const bf16x8* xr = reinterpret_cast<const bf16x8*>(x + row * ld_x);
+  bf16x8* rr = res ? reinterpret_cast<bf16x8*>(res + static_cast<int64_t>(row) * hidden) : nullptr;
+  float vals[VPT][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int v = threadIdx.x + blockDim.x * i;
+    if (v < nvec) {
+      unpack(xr[v], vals[i]);
+      if (rr) {
+        float r[8];
+        unpack(rr[v], r);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) vals[i][j] += r[j];
+        bf16x8 s = pack(vals[i]);
+        rr[v] = s;
+        unpack(s, vals[i]);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += vals[i][j] * vals[i][j];
+    }
+  }
+  ss = warp_sum(ss);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  if (warp == 0) {
+    float t = lane < (blockDim.x >> 5) ? red[lane] : 0.f;
+    t = warp_sum(t);
+    if (lane == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float rstd = rsqrtf(red[0] / static_cast<float>(hidden) + eps);
+  const bf16x8* wr = reinterpret_cast<const bf16x8*>(w);
+  bf16x8* yr = reinterpret_cast<bf16x8*>(y + row * ld_y);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int v = threadIdx.x + blockDim.x * i;
+    if (v < nvec) {
+      float wf[8], o[8];
+      unpack(wr[v], wf);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = __bfloat162float(__float2bfloat16(vals[i][j] * rstd)) * wf[j];
+      yr[v] = pack(o);
+    }
+  }
+}
+
 cudaError_t rmsnorm_bf16(const void* x, const void* w, void* y, void* residual, int rows, int hidden, int64_t ld_x,
                          int64_t ld_y, float eps, cudaStream_t stream) {
   if (hidden % 8 != 0 || hidden > 8 * 32 * 32) return cudaErrorInvalidValue;
   if (rows == 0) return cudaSuccess;
+  if (rows <= 512) {  // few rows: a CTA per row keeps many SMs busy (a warp per row would use rows / 8 SMs)
+    const int nvec = hidden / 8;
+    int threads = nvec <= 256 ? ((nvec + 31) / 32) * 32 : 256;
+    const int vpt = (nvec + threads - 1) / threads;
+    auto xp = static_cast<const __nv_bfloat16*>(x);
+    auto wp = static_cast<const __nv_bfloat16*>(w);
+    auto yp = static_cast<__nv_bfloat16*>(y);
+    auto rp = static_cast<__nv_bfloat16*>(residual);
+    if (vpt <= 1) rmsnorm_row_kernel<1><<<rows, threads, 0, stream>>>(xp, wp, yp, rp, hidden, ld_x, ld_y, eps);
+    else if (vpt <= 2) rmsnorm_row_kernel<2><<<rows, threads, 0, stream>>>(xp, wp, yp, rp, hidden, ld_x, ld_y, eps);
+    else if (vpt <= 4) rmsnorm_row_kernel<4><<<rows, threads, 0, stream>>>(xp, wp, yp, rp, hidden, ld_x, ld_y, eps);
+    else rmsnorm_row_kernel<8><<<rows, threads, 0, stream>>>(xp, wp, yp, rp, hidden, ld_x, ld_y, eps);
+    return cudaGetLastError();
+  }
   const int threads = 256;
   const int grid = (rows + 7) / 8;
   auto xp = static_cast<const __nv_bfloat16*>(x);

@@ -146,6 +146,7 @@ struct MoeRouteArgs {
   const void* x;           // [tokens, hidden] bf16 rows to gather (or nullptr)
   void* x_perm;            // [tokens * topk, hidden]
   int hidden;
+  int self_clean;          // cursor has experts + 1 entries: the last scatter CTA re-zeroes counts / cursor
 };
 cudaError_t moe_route(const MoeRouteArgs& a, cudaStream_t stream);
 

@@ -79,7 +79,8 @@ class MoEWorkspace:
         self.topk_ids = torch.empty(max_tokens, topk, dtype=torch.int32, device=device)
         self.topk_w = torch.empty(max_tokens, topk, dtype=torch.float32, device=device)
         self.counts = torch.zeros(experts, dtype=torch.int32, device=device)
-        self.cursor = torch.zeros(experts, dtype=torch.int32, device=device)
+        # experts + 1: the last slot is the scatter's done counter; the kernel re-zeroes counts / cursor
+        self.cursor = torch.zeros(experts + 1, dtype=torch.int32, device=device)
         self.offsets = torch.zeros(experts + 1, dtype=torch.int32, device=device)
         self.inv_perm = torch.empty(max_tokens, topk, dtype=torch.int32, device=device)
         self.x_perm = torch.empty(rows, hidden, dtype=dtype, device=device)
