@@ -311,26 +311,45 @@ void moe_route(const torch::Tensor& logits, int64_t topk, int64_t mode, const c1
 }
 
 void moe_combine(const torch::Tensor& y_perm, const torch::Tensor& inv_perm, const torch::Tensor& topk_w,
-                 torch::Tensor& out, const c10::optional<torch::Tensor>& shared,
-                 const c10::optional<torch::Tensor>& shared_gate) {
+                 const c10::optional<torch::Tensor>& out, const c10::optional<torch::Tensor>& shared,
+                 const c10::optional<torch::Tensor>& shared_gate, const c10::optional<torch::Tensor>& residual,
+                 const c10::optional<torch::Tensor>& norm_w, const c10::optional<torch::Tensor>& normed, double eps) {
   OMNI_CHECK_CUDA(y_perm);
   OMNI_CHECK_BF16(y_perm);
-  OMNI_CHECK_CONTIG(out);
+  OMNI_CHECK_CONTIG(y_perm);
+  TORCH_CHECK(topk_w.dim() == 2 && topk_w.is_contiguous() && inv_perm.is_contiguous(), "topk weights / inverse permutation");
+  TORCH_CHECK(out.has_value() || residual.has_value(), "moe_combine needs an output");
   const at::cuda::CUDAGuard guard(y_perm.device());
   omni::MoeCombineArgs a{};
   a.y_perm = y_perm.data_ptr();
   a.inv_perm = inv_perm.data_ptr<int>();
   a.topk_w = topk_w.data_ptr<float>();
-  a.tokens = static_cast<int>(out.size(0));
+  a.tokens = static_cast<int>(topk_w.size(0));
   a.topk = static_cast<int>(topk_w.size(1));
-  a.hidden = static_cast<int>(out.size(1));
-  a.shared = shared.has_value() ? shared->data_ptr() : nullptr;
+  a.hidden = static_cast<int>(y_perm.size(1));
+  TORCH_CHECK(inv_perm.numel() == static_cast<int64_t>(a.tokens) * a.topk, "inverse permutation size");
+  auto rows_of = [&](const torch::Tensor& t, const char* what) {
+    OMNI_CHECK_BF16(t);
+    TORCH_CHECK(t.is_contiguous() && t.dim() == 2 && t.size(0) == a.tokens && t.size(1) == a.hidden, what,
+                " must be a contiguous [tokens, hidden] tensor");
+    return t.data_ptr();
+  };
+  if (shared.has_value()) a.shared = rows_of(*shared, "shared expert output");
   if (shared_gate.has_value()) {
     TORCH_CHECK(shared_gate->scalar_type() == at::kFloat, "shared gate fp32");
     a.shared_gate = shared_gate->data_ptr<float>();
     a.shared_gate_stride = static_cast<int>(shared_gate->dim() >= 2 ? shared_gate->stride(0) : 1);
   }
-  a.out = out.data_ptr();
+  if (out.has_value()) a.out = rows_of(*out, "out");
+  if (residual.has_value()) {
+    TORCH_CHECK(norm_w.has_value() && normed.has_value(), "fused norm needs its weight and output");
+    a.residual = rows_of(*residual, "residual");
+    a.normed = rows_of(*normed, "normed");
+    OMNI_CHECK_BF16(*norm_w);
+    TORCH_CHECK(norm_w->numel() == a.hidden && norm_w->is_contiguous(), "norm weight");
+    a.norm_w = norm_w->data_ptr();
+    a.eps = static_cast<float>(eps);
+  }
   check_launch(omni::moe_combine(a, at::cuda::getCurrentCUDAStream()), "moe_combine");
 }
 
@@ -616,7 +635,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_decode", &attention_decode, "paged split-KV GQA decode attention");
   m.def("qkv_rope_store", &qkv_rope_store, "QK RMSNorm + (M-)RoPE + paged KV store");
   m.def("moe_route", &moe_route, "MoE top-k routing + permutation + gather");
-  m.def("moe_combine", &moe_combine, "MoE top-k weighted combine (+ shared expert)");
+  m.def("moe_combine", &moe_combine, "MoE top-k weighted combine (+ shared expert), optionally fused with the "
+        "next block's residual add + RMSNorm", py::arg("y_perm"), py::arg("inv_perm"), py::arg("topk_w"),
+        py::arg("out"), py::arg("shared") = py::none(), py::arg("shared_gate") = py::none(),
+        py::arg("residual") = py::none(), py::arg("norm_w") = py::none(), py::arg("normed") = py::none(),
+        py::arg("eps") = 1e-6);
   m.def("embed", &embed, "embedding gather with multimodal overwrite");
   m.def("vq_embed", &vq_embed, "dual-AR input embedding with the scaled VQ codebook sum");
   m.def("ipc_alloc", &ipc_alloc, "cudaMalloc + zero, returns the device address");

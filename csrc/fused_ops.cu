@@ -22,6 +22,24 @@
 namespace omni {
 namespace {
 
+__device__ __forceinline__ void unpack8(const uint4& p, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&p);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint4 p;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&p);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+  return p;
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int d = 16; d > 0; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
@@ -363,29 +381,83 @@ __global__ void moe_scatter_kernel(MoeRouteArgs a) {
   }
 }
 
-// out[t] = sum_k w[t,k] * y[inv[t,k]] (+ sigmoid(gate[t]) * shared[t])
-__global__ void moe_combine_kernel(MoeCombineArgs a) {
+// out[t] = sum_k w[t,k] * y[inv[t,k]] (+ sigmoid(gate[t]) * shared[t]), rounded to bf16.
+// With a residual: residual[t] = bf16(residual[t] + out[t]) and normed[t] = w * rmsnorm(residual[t])
+// (the next block's fused add + RMSNorm, same rounding points as rmsnorm_kernel).
+// One CTA of 256 threads per token, VPT 16-byte vectors per thread.
+template <int VPT>
+__global__ void __launch_bounds__(256) moe_combine_kernel(MoeCombineArgs a) {
+  __shared__ int s_pos[16];
+  __shared__ float s_w[16];
+  __shared__ float red[8];
   const int tok = blockIdx.x;
-  const __nv_bfloat16* y = static_cast<const __nv_bfloat16*>(a.y_perm);
-  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) + static_cast<int64_t>(tok) * a.hidden;
+  if (threadIdx.x < a.topk) {
+    s_pos[threadIdx.x] = a.inv_perm[tok * a.topk + threadIdx.x];
+    s_w[threadIdx.x] = a.topk_w[tok * a.topk + threadIdx.x];
+  }
+  __syncthreads();
+  const int nvec = a.hidden >> 3;
+  const uint4* y = static_cast<const uint4*>(a.y_perm);
   float sg = 0.f;
   if (a.shared != nullptr) sg = a.shared_gate ? 1.f / (1.f + __expf(-a.shared_gate[tok * a.shared_gate_stride])) : 1.f;
-  for (int v = threadIdx.x; v < a.hidden / 2; v += blockDim.x) {
-    float2 acc = make_float2(0.f, 0.f);
+  float vals[VPT][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int v = threadIdx.x + 256 * i;
+    if (v >= nvec) continue;
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
     for (int k = 0; k < a.topk; ++k) {
-      const int pos = a.inv_perm[tok * a.topk + k];
-      const float w = a.topk_w[tok * a.topk + k];
-      const float2 f = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(y + static_cast<int64_t>(pos) * a.hidden)[v]);
-      acc.x += w * f.x;
-      acc.y += w * f.y;
+      float f[8];
+      unpack8(__ldg(y + static_cast<int64_t>(s_pos[k]) * nvec + v), f);
+      const float w = s_w[k];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += w * f[j];
     }
     if (a.shared != nullptr) {
-      const float2 f = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(
-          static_cast<const __nv_bfloat16*>(a.shared) + static_cast<int64_t>(tok) * a.hidden)[v]);
-      acc.x += sg * f.x;
-      acc.y += sg * f.y;
+      float f[8];
+      unpack8(static_cast<const uint4*>(a.shared)[static_cast<int64_t>(tok) * nvec + v], f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += sg * f[j];
     }
-    reinterpret_cast<__nv_bfloat162*>(out)[v] = __floats2bfloat162_rn(acc.x, acc.y);
+    uint4 h = pack8(acc);
+    if (a.out != nullptr) static_cast<uint4*>(a.out)[static_cast<int64_t>(tok) * nvec + v] = h;
+    if (a.residual != nullptr) {
+      uint4* rr = static_cast<uint4*>(a.residual) + static_cast<int64_t>(tok) * nvec + v;
+      float r[8];
+      unpack8(h, acc);
+      unpack8(*rr, r);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += r[j];
+      const uint4 s = pack8(acc);
+      *rr = s;
+      unpack8(s, vals[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += vals[i][j] * vals[i][j];
+    }
+  }
+  if (a.residual == nullptr) return;
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, d);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) tot += red[w];
+  const float rstd = rsqrtf(tot / static_cast<float>(a.hidden) + a.eps);
+  const uint4* wr = static_cast<const uint4*>(a.norm_w);
+  uint4* yr = static_cast<uint4*>(a.normed) + static_cast<int64_t>(tok) * nvec;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int v = threadIdx.x + 256 * i;
+    if (v >= nvec) continue;
+    float wf[8], o[8];
+    unpack8(wr[v], wf);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = __bfloat162float(__float2bfloat16(vals[i][j] * rstd)) * wf[j];
+    yr[v] = pack8(o);
   }
 }
 
@@ -682,7 +754,12 @@ cudaError_t moe_route(const MoeRouteArgs& a, cudaStream_t stream) {
 
 cudaError_t moe_combine(const MoeCombineArgs& a, cudaStream_t stream) {
   if (a.tokens == 0) return cudaSuccess;
-  moe_combine_kernel<<<a.tokens, 256, 0, stream>>>(a);
+  const int nvec = a.hidden / 8;
+  if (a.hidden % 8 != 0 || a.topk > 16 || nvec > 256 * 4) return cudaErrorInvalidValue;
+  if (a.residual != nullptr && (a.norm_w == nullptr || a.normed == nullptr)) return cudaErrorInvalidValue;
+  if (nvec <= 256) moe_combine_kernel<1><<<a.tokens, 256, 0, stream>>>(a);
+  else if (nvec <= 512) moe_combine_kernel<2><<<a.tokens, 256, 0, stream>>>(a);
+  else moe_combine_kernel<4><<<a.tokens, 256, 0, stream>>>(a);
   return cudaGetLastError();
 }
 

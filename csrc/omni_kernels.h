@@ -158,7 +158,12 @@ struct MoeCombineArgs {
   const void* shared;      // [tokens, hidden] shared-expert output or nullptr
   const float* shared_gate;// [tokens] gate logits (sigmoid applied) or nullptr (=1)
   int shared_gate_stride;
-  void* out;               // [tokens, hidden]
+  void* out;               // [tokens, hidden] (may be nullptr when the residual / norm outputs are used)
+  // optional fused "add + RMSNorm" of the next block: residual += out (bf16), normed = w * rmsnorm(residual)
+  void* residual;          // [tokens, hidden] or nullptr
+  const void* norm_w;      // [hidden]
+  void* normed;            // [tokens, hidden]
+  float eps;
 };
 cudaError_t moe_combine(const MoeCombineArgs& a, cudaStream_t stream);
 

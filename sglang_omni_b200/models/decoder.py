@@ -210,7 +210,9 @@ class DecoderLM(nn.Module):
                 self._dec_ws = DecodeWorkspace(max_batch, cfg.num_heads, cfg.head_dim, max_context, dev)
 
     # ------------------------------------------------------------------ forward
-    def _mlp(self, L, x, i):
+    def _mlp(self, L, x, i, norm=None):
+        """MLP of layer i.  ``norm = (residual, next_weight, eps)`` (MoE layers only): the
+        combine also does the next block's residual add + RMSNorm and returns its output."""
         cfg = self.cfg
         if cfg.is_moe_layer(i):
             shared_out = shared_gate = None
@@ -223,7 +225,7 @@ class DecoderLM(nn.Module):
                                        mode=cfg.router_mode, bias=getattr(L, "router_bias", None),
                                        n_group=cfg.n_group, topk_group=cfg.topk_group,
                                        scaling=cfg.routed_scaling_factor, shared_out=shared_out,
-                                       shared_gate=shared_gate)
+                                       shared_gate=shared_gate, norm=norm)
             if self._moe_ws is None:
                 self.ensure_workspaces(max(x.shape[0], 4096), 1, 64)
             ws = self._moe_ws
@@ -232,7 +234,7 @@ class DecoderLM(nn.Module):
                 return ops.fused_moe(x, L.router, L.w13, L.w2, cfg.topk, ws, renormalize=cfg.norm_topk_prob,
                                      mode=cfg.router_mode, bias=getattr(L, "router_bias", None), n_group=cfg.n_group,
                                      topk_group=cfg.topk_group, scaling=cfg.routed_scaling_factor,
-                                     shared_out=shared_out, shared_gate=shared_gate)
+                                     shared_out=shared_out, shared_gate=shared_gate, norm=norm)
             # more tokens than the (graph-captured) workspace holds: run in chunks
             out = torch.empty_like(x)
             for a in range(0, T, step):
@@ -241,7 +243,8 @@ class DecoderLM(nn.Module):
                               mode=cfg.router_mode, bias=getattr(L, "router_bias", None), n_group=cfg.n_group,
                               topk_group=cfg.topk_group, scaling=cfg.routed_scaling_factor, out=out[a:b],
                               shared_out=None if shared_out is None else shared_out[a:b],
-                              shared_gate=None if shared_gate is None else shared_gate[a:b])
+                              shared_gate=None if shared_gate is None else shared_gate[a:b],
+                              norm=None if norm is None else (norm[0][a:b], norm[1], norm[2]))
             return out
         return ops.linear(ops.linear(x, L.mlp13, gated=True), L.mlp2)
 
@@ -258,10 +261,14 @@ class DecoderLM(nn.Module):
         T = x.shape[0]
         res = x.clone() if fb.input_embeds is not None else x
         h = None
+        fused_next = None    # this layer's input norm, already done by the previous MoE combine
         rot = cfg.rotary_dim or cfg.head_dim
         scale = 1.0 / math.sqrt(cfg.head_dim)
+        nl = len(self.layers)
         for i, L in enumerate(self.layers):
-            if h is None:
+            if fused_next is not None:
+                normed, fused_next = fused_next, None
+            elif h is None:
                 normed = ops.rms_norm(res, L.ln1, cfg.rms_norm_eps)
             else:
                 normed = ops.rms_norm(h, L.ln1, cfg.rms_norm_eps, residual=res)
@@ -281,8 +288,12 @@ class DecoderLM(nn.Module):
                                              cfg.num_kv_heads, cfg.head_dim, scale)
             o = ops.linear(attn, L.o)
             normed2 = ops.rms_norm(o, L.ln2, cfg.rms_norm_eps, residual=res)
+            has_ds = fb.deepstack is not None and i < len(fb.deepstack) and fb.deepstack[i] is not None
+            if i + 1 < nl and cfg.is_moe_layer(i) and not has_ds:
+                fused_next = self._mlp(L, normed2, i, norm=(res, self.layers[i + 1].ln1, cfg.rms_norm_eps))
+                continue
             h = self._mlp(L, normed2, i)
-            if fb.deepstack is not None and i < len(fb.deepstack) and fb.deepstack[i] is not None:
+            if has_ds:
                 pos, emb = fb.deepstack[i]
                 h.index_add_(0, pos, emb.to(h.dtype))
         if cfg.num_layers in fb.capture_layers:

@@ -18,6 +18,7 @@ import torch.nn.functional as F
 
 from ._ext import ext
 from .gemm import grouped_linear, linear
+from .norm import rms_norm
 
 
 def route_ref(logits, topk, mode=0, bias=None, n_group=1, topk_group=1, renormalize=True, scaling=1.0):
@@ -108,17 +109,23 @@ def route(logits: torch.Tensor, topk: int, mode: int = 0, bias=None, n_group: in
 def fused_moe(x: torch.Tensor, w_router: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor, topk: int,
               ws: MoEWorkspace, renormalize: bool = True, out: torch.Tensor | None = None, mode: int = 0,
               bias=None, n_group: int = 1, topk_group: int = 1, scaling: float = 1.0,
-              shared_out: torch.Tensor | None = None, shared_gate: torch.Tensor | None = None) -> torch.Tensor:
-    """Routed expert MLP on the sm_100a kernels: [T, H] -> [T, H]."""
+              shared_out: torch.Tensor | None = None, shared_gate: torch.Tensor | None = None,
+              norm: tuple | None = None) -> torch.Tensor:
+    """Routed expert MLP on the sm_100a kernels: [T, H] -> [T, H].
+
+    ``norm = (residual, weight, eps)`` fuses the next block's add + RMSNorm into
+    the combine: residual += moe(x) in place and the normalised rows are returned.
+    """
     T, H = x.shape
     E = w13.shape[0]
     if not x.is_cuda:
-        shared = None
         y = moe_ref(x, w_router, w13, w2, topk, renormalize, None, mode, bias, n_group, topk_group, scaling)
         if shared_out is not None:
             g = torch.sigmoid(shared_gate.float()) if shared_gate is not None else 1.0
             y = y + g * shared_out.float()
         y = y.to(x.dtype)
+        if norm is not None:
+            return rms_norm(y, norm[1], norm[2], residual=norm[0], out=out)
         if out is not None:
             out.copy_(y)
             return out
@@ -132,5 +139,9 @@ def fused_moe(x: torch.Tensor, w_router: torch.Tensor, w13: torch.Tensor, w2: to
     grouped_linear(ws.h_perm[:rows], w2, ws.offsets, gated=False, out=ws.y_perm[:rows], expected_rows=exp_rows)
     if out is None:
         out = torch.empty_like(x)
-    ext().moe_combine(ws.y_perm[:rows], ws.inv_perm[:T], ws.topk_w[:T], out, shared_out, shared_gate)
+    if norm is not None:
+        ext().moe_combine(ws.y_perm[:rows], ws.inv_perm[:T], ws.topk_w[:T], None, shared_out, shared_gate,
+                          norm[0], norm[1], out, norm[2])
+    else:
+        ext().moe_combine(ws.y_perm[:rows], ws.inv_perm[:T], ws.topk_w[:T], out, shared_out, shared_gate)
     return out

@@ -72,8 +72,12 @@ class EPMoE:
     def forward(self, x: torch.Tensor, w_router: torch.Tensor, w13_local: torch.Tensor, w2_local: torch.Tensor,
                 renormalize: bool = True, mode: int = 0, bias=None, n_group: int = 1, topk_group: int = 1,
                 scaling: float = 1.0, shared_out: torch.Tensor | None = None,
-                shared_gate: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
-        """x [T, H] (this rank's tokens) -> [T, H]; w13_local / w2_local hold this rank's experts."""
+                shared_gate: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                norm: tuple | None = None) -> torch.Tensor:
+        """x [T, H] (this rank's tokens) -> [T, H]; w13_local / w2_local hold this rank's experts.
+
+        ``norm = (residual, weight, eps)``: residual += result in place and the
+        RMS-normalised rows are returned (the next block's fused add + norm)."""
         T = x.shape[0]
         assert T <= self.max_tokens, f"{T} tokens > EP buffer capacity {self.max_tokens}"
         st = status_word(x.device)
@@ -98,7 +102,11 @@ class EPMoE:
         if out is None:
             out = torch.empty_like(x)
         n = T * self.topk
-        e.moe_combine(self.comb[:n], self.slots[:n].view(T, self.topk), w, out, shared_out, shared_gate)
+        if norm is not None:
+            e.moe_combine(self.comb[:n], self.slots[:n].view(T, self.topk), w, None, shared_out, shared_gate,
+                          norm[0], norm[1], out, norm[2])
+        else:
+            e.moe_combine(self.comb[:n], self.slots[:n].view(T, self.topk), w, out, shared_out, shared_gate)
         return out
 
     def close(self):

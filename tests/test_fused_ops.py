@@ -95,6 +95,55 @@ def test_moe_shared_expert_combine():
 
 
 @pytest.mark.gpu
+def test_moe_routing_scratch_reused_across_calls():
+    """The scatter re-zeroes its own histogram: back-to-back calls of different sizes on
+    one workspace must each see fresh counts (no memset between them)."""
+    E, k, H, I = 64, 4, 128, 64
+    g = torch.Generator(device="cuda").manual_seed(3)
+    wr = (torch.randn(E, H, device="cuda", generator=g) * 0.1).bfloat16()
+    w13 = (torch.randn(E, 2 * I, H, device="cuda", generator=g) * 0.05).bfloat16()
+    w2 = (torch.randn(E, H, I, device="cuda", generator=g) * 0.05).bfloat16()
+    ws = M.MoEWorkspace(96, E, k, H, I, "cuda")
+    for T in (96, 3, 57, 96, 1):
+        x = torch.randn(T, H, device="cuda", generator=g).bfloat16()
+        y = M.fused_moe(x, wr, w13, w2, k, ws)
+        ref = M.moe_ref(x, wr, w13, w2, k)
+        assert ((y.float() - ref).abs().max() / ref.abs().max()) < 3e-2, T
+        assert int(ws.offsets[E]) == T * k
+        assert int(ws.counts.abs().sum()) == 0 and int(ws.cursor.abs().sum()) == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("H,shared", [(2048, False), (4096, True), (1024, False)])
+def test_moe_combine_fused_add_rmsnorm(H, shared):
+    """combine + residual add + RMSNorm in one launch == unfused combine, then rms_norm(residual=...)."""
+    from sglang_omni_b200.ops import norm as N
+
+    torch.manual_seed(H)
+    T, E, k, I = 33, 32, 8, 64
+    x = torch.randn(T, H, device="cuda").bfloat16()
+    wr = (torch.randn(E, H, device="cuda") * 0.05).bfloat16()
+    w13 = (torch.randn(E, 2 * I, H, device="cuda") * 0.05).bfloat16()
+    w2 = (torch.randn(E, H, I, device="cuda") * 0.05).bfloat16()
+    so = torch.randn(T, H, device="cuda").bfloat16() if shared else None
+    sg = torch.randn(T, 1, device="cuda") if shared else None
+    nw = (1 + 0.1 * torch.randn(H, device="cuda")).bfloat16()
+    res0 = torch.randn(T, H, device="cuda").bfloat16()
+    ws = M.MoEWorkspace(T, E, k, H, I, "cuda")
+    h = M.fused_moe(x, wr, w13, w2, k, ws, shared_out=so, shared_gate=sg)
+    res_a = res0.clone()
+    want = N.rms_norm(h, nw, 1e-6, residual=res_a)
+    res_b = res0.clone()
+    got = M.fused_moe(x, wr, w13, w2, k, ws, shared_out=so, shared_gate=sg, norm=(res_b, nw, 1e-6))
+    torch.testing.assert_close(res_b, res_a, atol=0, rtol=0)
+    torch.testing.assert_close(got, want, atol=1e-2, rtol=1e-2)
+    # and against fp32
+    r32 = res0.float() + h.float()
+    ref = N.rms_norm_ref(r32, nw.float(), 1e-6)
+    assert float((got.float() - ref).abs().max()) < 0.05
+
+
+@pytest.mark.gpu
 def test_group_limited_sigmoid_routing():
     torch.manual_seed(7)
     T, E = 40, 256
