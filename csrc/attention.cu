@@ -542,19 +542,61 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
-    const int r = idx / D, d = idx - r * D;
-    const int64_t slot0 = (static_cast<int64_t>(b) * p.hq + h * G + r) * p.max_splits;
+  // Merge weights per (head, split) in shared memory (the K/V buffers are free now):
+  // w[r][sp] = 2^(lse - max) / sum, so the output is a plain weighted sum of partials.
+  float* wsm = reinterpret_cast<float*>(smem_raw);  // [G][nsplit]
+  const int64_t slot_h = (static_cast<int64_t>(b) * p.hq + h * G) * p.max_splits;
+  for (int i = threadIdx.x; i < G * nsplit; i += blockDim.x) {
+    const int r = i / nsplit, sp = i - r * nsplit;
+    wsm[i] = __ldcg(p.part_lse + slot_h + static_cast<int64_t>(r) * p.max_splits + sp);
+  }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    float* w = wsm + threadIdx.x * nsplit;
     float M = -INFINITY;
-    for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, __ldcg(p.part_lse + slot0 + sp));
+    for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, w[sp]);
     const float sub = M == -INFINITY ? 0.f : M;
-    float L = 0.f, acc = 0.f;
+    float L = 0.f;
     for (int sp = 0; sp < nsplit; ++sp) {
-      const float f = exp2f(__ldcg(p.part_lse + slot0 + sp) - sub);
-      L += f;
-      acc += f * __ldcg(p.part_o + (slot0 + sp) * D + d);
+      w[sp] = exp2f(w[sp] - sub);
+      L += w[sp];
     }
-    p.out[static_cast<int64_t>(b) * p.out_stride + (h * G + r) * D + d] = __float2bfloat16(L > 0.f ? acc / L : 0.f);
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    for (int sp = 0; sp < nsplit; ++sp) w[sp] *= inv;
+  }
+  __syncthreads();
+  // 16-byte partial loads, four splits per round per item
+  constexpr int V = D / 4;
+  for (int it = threadIdx.x; it < G * V; it += blockDim.x) {
+    const int r = it / V, d4 = it - r * V;
+    const float4* src = reinterpret_cast<const float4*>(p.part_o + (slot_h + static_cast<int64_t>(r) * p.max_splits) * D) + d4;
+    const float* w = wsm + r * nsplit;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    int sp = 0;
+    for (; sp + 4 <= nsplit; sp += 4) {
+      float4 x[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) x[u] = __ldcg(src + static_cast<int64_t>(sp + u) * V);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float wu = w[sp + u];
+        acc.x += wu * x[u].x;
+        acc.y += wu * x[u].y;
+        acc.z += wu * x[u].z;
+        acc.w += wu * x[u].w;
+      }
+    }
+    for (; sp < nsplit; ++sp) {
+      const float4 x = __ldcg(src + static_cast<int64_t>(sp) * V);
+      const float wu = w[sp];
+      acc.x += wu * x.x;
+      acc.y += wu * x.y;
+      acc.z += wu * x.z;
+      acc.w += wu * x.w;
+    }
+    __nv_bfloat16* o = p.out + static_cast<int64_t>(b) * p.out_stride + (h * G + r) * D + 4 * d4;
+    *reinterpret_cast<uint32_t*>(o) = pack_bf16(acc.x, acc.y);
+    *reinterpret_cast<uint32_t*>(o + 2) = pack_bf16(acc.z, acc.w);
   }
 }
 

@@ -331,37 +331,44 @@ __global__ void moe_topk_kernel(MoeRouteArgs a) {
 // Offsets (exclusive scan of counts, computed by every CTA) + permutation + row gather.
 __global__ void moe_scatter_kernel(MoeRouteArgs a) {
   extern __shared__ int s_off[];
-  for (int e = threadIdx.x; e < a.experts; e += blockDim.x) s_off[e] = a.counts[e];
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int acc = 0;
-    for (int e = 0; e < a.experts; ++e) {
-      const int c = s_off[e];
-      s_off[e] = acc;
-      acc += c;
+  // exclusive scan of the expert histogram by warp 0 (32 experts per round)
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    int carry = 0;
+    for (int base = 0; base < a.experts; base += 32) {
+      const int e = base + lane;
+      const int c = e < a.experts ? a.counts[e] : 0;
+      int incl = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+      }
+      if (e < a.experts) s_off[e] = carry + incl - c;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
     }
-    s_off[a.experts] = acc;
+    if (lane == 0) s_off[a.experts] = carry;
   }
   __syncthreads();
   if (blockIdx.x == 0)
     for (int e = threadIdx.x; e <= a.experts; e += blockDim.x) a.offsets[e] = s_off[e];
   const int warps = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
-  for (int tok = blockIdx.x * warps + (threadIdx.x >> 5); tok < a.tokens; tok += gridDim.x * warps) {
-    for (int k = 0; k < a.topk; ++k) {
-      int pos = 0;
-      if (lane == 0) {
-        const int e = a.topk_ids[tok * a.topk + k];
-        pos = s_off[e] + atomicAdd(&a.cursor[e], 1);
-        a.inv_perm[tok * a.topk + k] = pos;
-      }
-      pos = __shfl_sync(0xffffffffu, pos, 0);
-      if (a.x != nullptr) {
-        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.x) +
-                                                          static_cast<int64_t>(tok) * a.hidden);
-        uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.x_perm) + static_cast<int64_t>(pos) * a.hidden);
-        for (int v = lane; v < a.hidden / 8; v += 32) dst[v] = src[v];
-      }
+  const int n = a.tokens * a.topk;
+  // one warp per (token, k) pair
+  for (int i = blockIdx.x * warps + (threadIdx.x >> 5); i < n; i += gridDim.x * warps) {
+    int pos = 0;
+    if (lane == 0) {
+      const int e = a.topk_ids[i];
+      pos = s_off[e] + atomicAdd(&a.cursor[e], 1);
+      a.inv_perm[i] = pos;
+    }
+    pos = __shfl_sync(0xffffffffu, pos, 0);
+    if (a.x != nullptr) {
+      const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.x) +
+                                                        static_cast<int64_t>(i / a.topk) * a.hidden);
+      uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.x_perm) + static_cast<int64_t>(pos) * a.hidden);
+      for (int v = lane; v < a.hidden / 8; v += 32) dst[v] = src[v];
     }
   }
   if (a.self_clean) {
@@ -745,8 +752,8 @@ cudaError_t moe_route(const MoeRouteArgs& a, cudaStream_t stream) {
   else if (per <= 8) moe_topk_kernel<8><<<grid, 256, 0, stream>>>(a);
   else moe_topk_kernel<16><<<grid, 256, 0, stream>>>(a);
   if (a.counts) {
-    int sgrid = (a.tokens + 7) / 8;
-    if (sgrid > 1024) sgrid = 1024;
+    int sgrid = (a.tokens * a.topk + 7) / 8;   // one warp per (token, k)
+    if (sgrid > 148 * 8) sgrid = 148 * 8;
     moe_scatter_kernel<<<sgrid, 256, sizeof(int) * (a.experts + 1), stream>>>(a);
   }
   return cudaGetLastError();

@@ -49,9 +49,22 @@ struct DevParams {
   int act;
   int* status;
   int k_splits;          // > 1: split-K over K blocks with an fp32 workspace
-  float* ws;             // [rows, m_out] fp32, zero between calls (self-cleaning)
+  float* ws;             // [tiles][128][BN] fp32 partial sums, zero between calls (the finaliser re-zeroes)
   int* counters;         // [tiles] arrival counters, zero between calls
 };
+
+// Vector fp32 reduction into global memory (sm_90+): fire-and-forget, no return value.
+__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+__device__ __forceinline__ float epilogue_act(float v, int act) {
+  if (act == kActGeluTanh) return gelu_tanh_f(v);
+  if (act == kActGeluErf) return gelu_erf_f(v);
+  if (act == kActSilu) return silu_f(v);
+  return v;
+}
 
 template <int BN, bool GATED>
 struct Cfg {
@@ -283,15 +296,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (GATED) tmem_ld_32x32b_x16(t_base + BN + c, u);
         tmem_ld_wait();
         if (ks > 1) {
-          // split-K partial: raw fp32 sums of this K range, reduced by splitk_reduce_kernel
-          if (m_ok) {
-            float* wsp = p.ws + (static_cast<int64_t>(w % ks) * p.rows) * p.m_out + m;
+          // split-K partial: added into the tile's fp32 plane [t][128][BN] (thread = one A row,
+          // 16 consecutive tokens = four 16-byte vector reductions)
+          float* wsp = p.ws + (static_cast<int64_t>(t) * kBM + lane_base + lane) * BN + c;
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int row = row0 + c + j;
-              if (row < row_end) wsp[static_cast<int64_t>(row) * p.m_out] = __uint_as_float(r[j]);
-            }
-          }
+          for (int j = 0; j < 16; j += 4)
+            red_add_v4(wsp + j, __uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                       __uint_as_float(r[j + 3]));
         } else if (m_ok) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
@@ -331,19 +342,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (s_last) {
           __threadfence();
-          if (m_ok) {
-            const int64_t plane = static_cast<int64_t>(p.rows) * p.m_out;
-            for (int row = row0; row < row_end && row < row0 + BN; ++row) {
-              const float* src = p.ws + static_cast<int64_t>(row) * p.m_out + m;
-              float v = 0.f;
-              for (int s = 0; s < ks; ++s) v += __ldcg(src + s * plane);
-              v += bias_v;
-              if (p.act == kActGeluTanh) v = gelu_tanh_f(v);
-              else if (p.act == kActGeluErf) v = gelu_erf_f(v);
-              else if (p.act == kActSilu) v = silu_f(v);
-              if (p.residual != nullptr) v += __bfloat162float(p.residual[static_cast<int64_t>(row) * p.ldr + m]);
-              if (p.out_f32) static_cast<float*>(p.out)[static_cast<int64_t>(row) * p.ldo + m] = v;
-              else static_cast<__nv_bfloat16*>(p.out)[static_cast<int64_t>(row) * p.ldo + m] = __float2bfloat16(v);
+          // up to 32 tokens per round (eight 16-byte loads in flight per thread), then re-zero the plane
+          constexpr int kChunk = BN < 32 ? BN : 32;
+          float* wsp = p.ws + (static_cast<int64_t>(t) * kBM + lane_base + lane) * BN;
+#pragma unroll 1
+          for (int c = 0; c < BN; c += kChunk) {
+            float4 v4[kChunk / 4];
+#pragma unroll
+            for (int q = 0; q < kChunk / 4; ++q) v4[q] = __ldcg(reinterpret_cast<const float4*>(wsp + c) + q);
+#pragma unroll
+            for (int q = 0; q < kChunk / 4; ++q)
+              __stcg(reinterpret_cast<float4*>(wsp + c) + q, make_float4(0.f, 0.f, 0.f, 0.f));
+            if (m_ok) {
+              const float* vf = reinterpret_cast<const float*>(v4);
+#pragma unroll
+              for (int j = 0; j < kChunk; ++j) {
+                const int row = row0 + c + j;
+                if (row < row_end) {
+                  float v = epilogue_act(vf[j] + bias_v, p.act);
+                  if (p.residual != nullptr) v += __bfloat162float(p.residual[static_cast<int64_t>(row) * p.ldr + m]);
+                  if (p.out_f32) static_cast<float*>(p.out)[static_cast<int64_t>(row) * p.ldo + m] = v;
+                  else static_cast<__nv_bfloat16*>(p.out)[static_cast<int64_t>(row) * p.ldo + m] = __float2bfloat16(v);
+                }
+              }
             }
           }
         }
@@ -359,22 +380,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Sums the split-K partials [ks][rows][m_out] and applies the epilogue.
-__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int ks, int rows, int m_out, void* out,
+// Fallback finaliser (more tiles than arrival counters): reads the fp32 plane
+// [tiles][128][BN], re-zeroes it and applies the epilogue.
+__global__ void splitk_reduce_kernel(float* __restrict__ ws, int bn, int n_tiles, int rows, int m_out, void* out,
                                      int64_t ldo, int out_f32, const __nv_bfloat16* __restrict__ bias,
                                      const __nv_bfloat16* __restrict__ residual, int64_t ldr, int act) {
   const int64_t n = static_cast<int64_t>(rows) * m_out;
-  const int64_t plane = n;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int row = static_cast<int>(i / m_out);
     const int m = static_cast<int>(i - static_cast<int64_t>(row) * m_out);
-    float v = 0.f;
-    for (int s = 0; s < ks; ++s) v += __ldg(ws + s * plane + i);
+    const int t = (m / kBM) * n_tiles + row / bn;
+    float* src = ws + (static_cast<int64_t>(t) * kBM + m % kBM) * bn + row % bn;
+    float v = __ldcg(src);
+    __stcg(src, 0.f);
     if (bias != nullptr) v += __bfloat162float(bias[m]);
-    if (act == kActGeluTanh) v = gelu_tanh_f(v);
-    else if (act == kActGeluErf) v = gelu_erf_f(v);
-    else if (act == kActSilu) v = silu_f(v);
+    v = epilogue_act(v, act);
     if (residual != nullptr) v += __bfloat162float(residual[static_cast<int64_t>(row) * ldr + m]);
     if (out_f32) static_cast<float*>(out)[static_cast<int64_t>(row) * ldo + m] = v;
     else static_cast<__nv_bfloat16*>(out)[static_cast<int64_t>(row) * ldo + m] = __float2bfloat16(v);
@@ -462,13 +483,15 @@ cudaError_t launch(const GemmArgs& a, cudaStream_t stream) {
     const long tiles = static_cast<long>(m_tiles) * ((a.rows + BN - 1) / BN);
     const int sms = num_sms();
     if (tiles * 2 <= sms && num_kb >= 4) {
-      int ksp = static_cast<int>((sms + tiles - 1) / tiles);
+      // one wave: tiles * splits <= SMs (a partial second wave doubles the time)
+      int ksp = static_cast<int>(sms / tiles);
       if (ksp > num_kb / 2) ksp = num_kb / 2;
       if (ksp > 16) ksp = 16;
       if (ksp > 1) {
         const int per = (num_kb + ksp - 1) / ksp;
         ksp = (num_kb + per - 1) / per;  // no empty splits
-        if (static_cast<long long>(ksp) * a.rows * a.m_out <= a.splitk_ws_floats) {
+        const long long plane = static_cast<long long>(m_tiles) * kBM * ((a.rows + BN - 1) / BN) * BN;
+        if (plane <= a.splitk_ws_floats) {
           p.k_splits = ksp;
           p.ws = a.splitk_ws;
           // tiles within the counter slots: the last split finalises in-kernel (no reduce launch)
@@ -488,8 +511,8 @@ cudaError_t launch(const GemmArgs& a, cudaStream_t stream) {
     const long long n = static_cast<long long>(a.rows) * a.m_out;
     int rgrid = static_cast<int>((n + 255) / 256);
     if (rgrid > 4 * num_sms()) rgrid = 4 * num_sms();
-    splitk_reduce_kernel<<<rgrid, 256, 0, stream>>>(p.ws, p.k_splits, a.rows, a.m_out, a.out, a.ldo, a.out_f32,
-                                                    p.bias, p.residual, a.ldr, a.act);
+    splitk_reduce_kernel<<<rgrid, 256, 0, stream>>>(p.ws, BN, (a.rows + BN - 1) / BN, a.rows, a.m_out, a.out, a.ldo,
+                                                    a.out_f32, p.bias, p.residual, a.ldr, a.act);
   }
   return cudaGetLastError();
 }
