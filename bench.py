@@ -51,6 +51,10 @@ def parse():
     ap.add_argument("--ep", type=int, default=1,
                     help="N>1: experts sharded over the GPUs (expert parallel MoE over NVLink, data-parallel "
                          "attention); 0: one full replica per GPU")
+    ap.add_argument("--tp", type=int, default=0,
+                    help="N>1: tensor-parallel thinker instead (heads, experts and MLP slices split; fused "
+                         "owner-scatter GEMM epilogues + reduce/RMSNorm/all-gather kernel); every rank serves the "
+                         "same --requests (strong scaling)")
     return ap.parse_args()
 
 
@@ -298,8 +302,14 @@ def main():
         return
 
     cfg = thinker_text_config(num_layers=args.layers)
-    ep = None
-    if world > 1 and args.ep:
+    ep = tp = None
+    if world > 1 and args.tp:
+        from sglang_omni_b200.models.decoder import DecoderLM as _DLM
+        from sglang_omni_b200.parallel import TPGroup
+
+        tp = TPGroup(cfg.hidden_size, max(args.max_prefill_tokens, args.requests), dev)
+        model = _DLM(cfg, dev, tp=tp).random_init_(seed=loader.SEEDS["thinker"])
+    elif world > 1 and args.ep:
         from sglang_omni_b200.models.decoder import DecoderLM as _DLM
         from sglang_omni_b200.parallel import EPMoE
 
@@ -311,10 +321,10 @@ def main():
                                    {"thinker": {"num_layers": args.layers}} if args.layers != 48 else None)
     max_ctx = ((args.prompt_len + args.output_len + 63) // 64) * 64
     pages_needed = args.requests * (max_ctx // 64) + 64
-    pool = KVPool(cfg.num_layers, cfg.num_kv_heads, cfg.head_dim, pages_needed + 1, dev)
+    pool = KVPool(cfg.num_layers, model.cfg.num_kv_heads, cfg.head_dim, pages_needed + 1, dev)
     eng = AREngine(model, pool, max_batch=args.requests, max_prefill_tokens=args.max_prefill_tokens,
                    max_context=max_ctx, use_graphs=True, overlap=True)
-    g = torch.Generator().manual_seed(1234 + rank)
+    g = torch.Generator().manual_seed(1234 + (0 if tp is not None else rank))  # TP ranks serve the same requests
     prompts = torch.randint(0, cfg.vocab_size, (args.requests, args.prompt_len), generator=g, dtype=torch.int32)
     prompts_pinned = prompts.pin_memory()
     sp = SamplingParams(temperature=0.0, ignore_eos=True)
@@ -358,6 +368,8 @@ def main():
         sm = t.clone()
         dist.all_reduce(sm, op=dist.ReduceOp.SUM)
         ms_max, tokens_total, wall_max = float(mx[0]), float(sm[1]), float(mx[2])
+        if tp is not None:  # every TP rank generated the same tokens: count them once
+            tokens_total /= world
     else:
         ms_max, tokens_total, wall_max = ms, float(out_tokens), wall
     value = tokens_total / (ms_max / 1e3)
@@ -402,18 +414,22 @@ def main():
             "warmup": args.warmup,
             "ms_per_step": round(ms_max / args.steps, 3),
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong" if tp is not None else "weak",
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic: uniform random prompt ids, random-init N(0,0.02) weights of the full architecture",
             "config": {
                 "model": f"Qwen3-Omni-30B-A3B thinker ({cfg.num_layers} layers, 128 experts top-8, hidden 2048)",
-                "global_batch": args.requests * world,
+                "global_batch": args.requests if tp is not None else args.requests * world,
                 "seq_len": args.prompt_len,
                 "output_len": args.output_len,
                 "parallelism": (f"ep{world} (experts sharded, peer-memory dispatch/combine) + dp{world} attention"
-                                if ep is not None else f"dp{world}" if world > 1 else "tp1"),
-                "step": "one serving round: 64 requests x (1024 prompt -> 256 greedy tokens) per GPU",
+                                if ep is not None else
+                                f"tp{world} (heads / experts split, fused owner-scatter epilogues + peer-memory "
+                                f"reduce/RMSNorm/all-gather)" if tp is not None else
+                                f"dp{world}" if world > 1 else "tp1"),
+                "step": (f"one serving round: {args.requests} requests x ({args.prompt_len} prompt -> "
+                         f"{args.output_len} greedy tokens) " + ("over the TP group" if tp is not None else "per GPU")),
                 "l2": "inputs larger than L2 (61 GB of weights streamed per decode step)",
                 "ttft_p50_ms": round(1e3 * statistics.median(ttfts), 2),
                 "ttfa_p50_ms": None if ttfa_ms is None else round(ttfa_ms, 2),
@@ -438,12 +454,12 @@ def main():
         }
         print(json.dumps(line))
     if world > 1:
-        if ep is not None:
+        if ep is not None or tp is not None:
             eng = pool = model = None  # release the decode graphs that reference the exchange buffers
             import gc
 
             gc.collect()
-            ep.close()
+            (ep or tp).close()
         dist.destroy_process_group()
 
 

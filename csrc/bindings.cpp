@@ -31,7 +31,9 @@ void gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& out, co
           int64_t m_out, bool gated, const c10::optional<torch::Tensor>& bias,
           const c10::optional<torch::Tensor>& residual, int64_t act, int64_t expected_rows,
           const c10::optional<torch::Tensor>& status, int64_t max_ctas,
-          const c10::optional<torch::Tensor>& splitk_ws, const c10::optional<torch::Tensor>& splitk_counters) {
+          const c10::optional<torch::Tensor>& splitk_ws, const c10::optional<torch::Tensor>& splitk_counters,
+          const c10::optional<torch::Tensor>& peer_out, int64_t rows_per, const c10::optional<torch::Tensor>& wait_flags,
+          const c10::optional<torch::Tensor>& wait_seq, double wait_timeout_s) {
   OMNI_CHECK_CUDA(a);
   OMNI_CHECK_CUDA(b);
   OMNI_CHECK_CUDA(out);
@@ -99,6 +101,21 @@ void gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& out, co
     args.splitk_ws_floats = splitk_ws->numel();
     args.splitk_counters = splitk_counters->data_ptr<int>();
     args.splitk_counter_slots = static_cast<int>(splitk_counters->numel());
+  }
+  if (peer_out.has_value()) {
+    TORCH_CHECK(peer_out->scalar_type() == at::kLong && peer_out->is_cuda() && !args.out_f32 && rows_per > 0,
+                "owner scatter: int64 device pointer table, bf16 output, rows_per > 0");
+    TORCH_CHECK((rows + rows_per - 1) / rows_per <= peer_out->numel(), "owner scatter: more owners than pointers");
+    args.peer_out = reinterpret_cast<const unsigned long long*>(peer_out->data_ptr<int64_t>());
+    args.rows_per = static_cast<int>(rows_per);
+  }
+  if (wait_flags.has_value()) {
+    TORCH_CHECK(wait_seq.has_value() && wait_flags->scalar_type() == at::kInt && wait_seq->scalar_type() == at::kInt,
+                "wait flags / sequence must be int32");
+    args.wait_flags = reinterpret_cast<const unsigned int*>(wait_flags->data_ptr<int>());
+    args.wait_seq = reinterpret_cast<const unsigned int*>(wait_seq->data_ptr<int>());
+    args.wait_count = static_cast<int>(wait_flags->numel());
+    args.wait_timeout_ns = static_cast<long long>(wait_timeout_s * 1e9);
   }
   check_launch(omni::gemm_bf16(args, at::cuda::getCurrentCUDAStream()), "gemm_bf16");
 }
@@ -275,7 +292,7 @@ void moe_route(const torch::Tensor& logits, int64_t topk, int64_t mode, const c1
                torch::Tensor& topk_w, const c10::optional<torch::Tensor>& counts,
                const c10::optional<torch::Tensor>& cursor, const c10::optional<torch::Tensor>& offsets,
                const c10::optional<torch::Tensor>& inv_perm, const c10::optional<torch::Tensor>& x,
-               const c10::optional<torch::Tensor>& x_perm) {
+               const c10::optional<torch::Tensor>& x_perm, int64_t local_e0, int64_t local_el) {
   OMNI_CHECK_CUDA(logits);
   TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.stride(-1) == 1, "router logits must be fp32");
   const at::cuda::CUDAGuard guard(logits.device());
@@ -307,18 +324,23 @@ void moe_route(const torch::Tensor& logits, int64_t topk, int64_t mode, const c1
     a.x_perm = x_perm->data_ptr();
     a.hidden = static_cast<int>(x->size(-1));
   }
+  TORCH_CHECK(local_el >= 0 && local_e0 >= 0 && local_e0 + local_el <= a.experts, "local expert range");
+  a.local_e0 = static_cast<int>(local_e0);
+  a.local_el = static_cast<int>(local_el);
   check_launch(omni::moe_route(a, at::cuda::getCurrentCUDAStream()), "moe_route");
 }
 
 void moe_combine(const torch::Tensor& y_perm, const torch::Tensor& inv_perm, const torch::Tensor& topk_w,
                  const c10::optional<torch::Tensor>& out, const c10::optional<torch::Tensor>& shared,
                  const c10::optional<torch::Tensor>& shared_gate, const c10::optional<torch::Tensor>& residual,
-                 const c10::optional<torch::Tensor>& norm_w, const c10::optional<torch::Tensor>& normed, double eps) {
+                 const c10::optional<torch::Tensor>& norm_w, const c10::optional<torch::Tensor>& normed, double eps,
+                 const c10::optional<torch::Tensor>& local_offsets, const c10::optional<torch::Tensor>& peer_out,
+                 int64_t rows_per) {
   OMNI_CHECK_CUDA(y_perm);
   OMNI_CHECK_BF16(y_perm);
   OMNI_CHECK_CONTIG(y_perm);
   TORCH_CHECK(topk_w.dim() == 2 && topk_w.is_contiguous() && inv_perm.is_contiguous(), "topk weights / inverse permutation");
-  TORCH_CHECK(out.has_value() || residual.has_value(), "moe_combine needs an output");
+  TORCH_CHECK(out.has_value() || residual.has_value() || peer_out.has_value(), "moe_combine needs an output");
   const at::cuda::CUDAGuard guard(y_perm.device());
   omni::MoeCombineArgs a{};
   a.y_perm = y_perm.data_ptr();
@@ -349,6 +371,20 @@ void moe_combine(const torch::Tensor& y_perm, const torch::Tensor& inv_perm, con
     TORCH_CHECK(norm_w->numel() == a.hidden && norm_w->is_contiguous(), "norm weight");
     a.norm_w = norm_w->data_ptr();
     a.eps = static_cast<float>(eps);
+  }
+  if (local_offsets.has_value()) {
+    TORCH_CHECK(local_offsets->scalar_type() == at::kInt && local_offsets->is_contiguous() && local_offsets->numel() >= 2,
+                "local expert offsets");
+    a.local_offsets = local_offsets->data_ptr<int>();
+    a.local_experts = static_cast<int>(local_offsets->numel() - 1);
+  }
+  if (peer_out.has_value()) {
+    TORCH_CHECK(peer_out->scalar_type() == at::kLong && rows_per > 0 && !residual.has_value(),
+                "owner scatter: int64 pointer table, rows_per > 0, no fused norm");
+    TORCH_CHECK((a.tokens + rows_per - 1) / rows_per <= peer_out->numel(), "owner scatter: more owners than pointers");
+    a.peer_out = reinterpret_cast<const unsigned long long*>(peer_out->data_ptr<int64_t>());
+    a.rows_per = static_cast<int>(rows_per);
+    a.out = nullptr;
   }
   check_launch(omni::moe_combine(a, at::cuda::getCurrentCUDAStream()), "moe_combine");
 }
@@ -473,6 +509,61 @@ omni::EpArgs ep_args(const torch::Tensor& topk_ids, const torch::Tensor& peer_ba
   a.status = status_ptr(status);
   a.timeout_ns = static_cast<uint64_t>(timeout_s * 1e9);
   return a;
+}
+
+// Tensor-parallel reduce point: ptrs = int64 [4, world] device table of the
+// part / gath / gres / flags region bases of every rank (gres row 0 = none).
+omni::TpReduceArgs tp_args(const torch::Tensor& ptrs, int64_t rank, int64_t world, int64_t tokens, int64_t hidden,
+                           int64_t rows_per, int64_t max_tokens, bool gather_residual, torch::Tensor& seq,
+                           torch::Tensor& counter, const c10::optional<torch::Tensor>& status, double timeout_s) {
+  TORCH_CHECK(ptrs.scalar_type() == at::kLong && ptrs.is_cuda() && ptrs.is_contiguous() && ptrs.dim() == 2 &&
+                  ptrs.size(0) == 4 && ptrs.size(1) == world,
+              "pointer table must be int64 [4, world] on the device");
+  TORCH_CHECK(seq.scalar_type() == at::kInt && counter.scalar_type() == at::kInt, "seq / counter int32");
+  TORCH_CHECK(rank >= 0 && rank < world && tokens <= max_tokens && rows_per > 0, "tp reduce geometry");
+  omni::TpReduceArgs a{};
+  const auto* p = reinterpret_cast<const unsigned long long*>(ptrs.data_ptr<int64_t>());
+  a.peer_part = p;
+  a.peer_gath = p + world;
+  a.peer_gres = gather_residual ? p + 2 * world : nullptr;
+  a.peer_flags = p + 3 * world;
+  a.rank = static_cast<int>(rank);
+  a.world = static_cast<int>(world);
+  a.tokens = static_cast<int>(tokens);
+  a.hidden = static_cast<int>(hidden);
+  a.rows_per = static_cast<int>(rows_per);
+  a.max_tokens = static_cast<int>(max_tokens);
+  a.seq = reinterpret_cast<unsigned int*>(seq.data_ptr<int>());
+  a.counter = counter.data_ptr<int>();
+  a.status = status_ptr(status);
+  a.timeout_ns = static_cast<long long>(timeout_s * 1e9);
+  return a;
+}
+
+void tp_reduce_norm(const torch::Tensor& ptrs, int64_t rank, int64_t world, int64_t tokens, int64_t rows_per,
+                    int64_t max_tokens, torch::Tensor& residual, const torch::Tensor& norm_w, double eps,
+                    bool gather_residual, torch::Tensor& seq, torch::Tensor& counter,
+                    const c10::optional<torch::Tensor>& status, double timeout_s) {
+  OMNI_CHECK_CUDA(residual);
+  OMNI_CHECK_BF16(residual);
+  OMNI_CHECK_CONTIG(residual);
+  OMNI_CHECK_BF16(norm_w);
+  TORCH_CHECK(residual.dim() == 2 && residual.size(0) >= tokens && norm_w.numel() == residual.size(1),
+              "residual [tokens, H] / norm weight [H]");
+  const at::cuda::CUDAGuard guard(residual.device());
+  auto a = tp_args(ptrs, rank, world, tokens, residual.size(1), rows_per, max_tokens, gather_residual, seq, counter,
+                   status, timeout_s);
+  a.residual = residual.data_ptr();
+  a.norm_w = norm_w.data_ptr();
+  a.eps = static_cast<float>(eps);
+  check_launch(omni::tp_reduce_norm(a, at::cuda::getCurrentCUDAStream()), "tp_reduce_norm");
+}
+
+void tp_wait(const torch::Tensor& ptrs, int64_t rank, int64_t world, torch::Tensor& seq, torch::Tensor& counter,
+             const c10::optional<torch::Tensor>& status, double timeout_s) {
+  const at::cuda::CUDAGuard guard(ptrs.device());
+  auto a = tp_args(ptrs, rank, world, 0, 8, 1, 0, false, seq, counter, status, timeout_s);
+  check_launch(omni::tp_wait(a, at::cuda::getCurrentCUDAStream()), "tp_wait");
 }
 
 void ep_counts(const torch::Tensor& topk_ids, const torch::Tensor& peer_base, const std::vector<int64_t>& offs,
@@ -628,18 +719,24 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "tcgen05 GEMM (dense / grouped / gated)", py::arg("a"), py::arg("b"), py::arg("out"),
         py::arg("offsets"), py::arg("m_out"), py::arg("gated"), py::arg("bias"), py::arg("residual"), py::arg("act"),
         py::arg("expected_rows"), py::arg("status"), py::arg("max_ctas") = 0, py::arg("splitk_ws") = py::none(),
-        py::arg("splitk_counters") = py::none());
+        py::arg("splitk_counters") = py::none(), py::arg("peer_out") = py::none(), py::arg("rows_per") = 0,
+        py::arg("wait_flags") = py::none(), py::arg("wait_seq") = py::none(), py::arg("wait_timeout_s") = 2.0);
   m.def("rmsnorm", &rmsnorm, "RMSNorm (+ fused residual add)");
   m.def("layernorm", &layernorm, "LayerNorm");
   m.def("attention_prefill", &attention_prefill, "paged / varlen GQA prefill attention");
   m.def("attention_decode", &attention_decode, "paged split-KV GQA decode attention");
   m.def("qkv_rope_store", &qkv_rope_store, "QK RMSNorm + (M-)RoPE + paged KV store");
-  m.def("moe_route", &moe_route, "MoE top-k routing + permutation + gather");
+  m.def("moe_route", &moe_route, "MoE top-k routing + permutation + gather", py::arg("logits"), py::arg("topk"),
+        py::arg("mode"), py::arg("bias"), py::arg("n_group"), py::arg("topk_group"), py::arg("renormalize"),
+        py::arg("scaling"), py::arg("topk_ids"), py::arg("topk_w"), py::arg("counts"), py::arg("cursor"),
+        py::arg("offsets"), py::arg("inv_perm"), py::arg("x"), py::arg("x_perm"), py::arg("local_e0") = 0,
+        py::arg("local_el") = 0);
   m.def("moe_combine", &moe_combine, "MoE top-k weighted combine (+ shared expert), optionally fused with the "
         "next block's residual add + RMSNorm", py::arg("y_perm"), py::arg("inv_perm"), py::arg("topk_w"),
         py::arg("out"), py::arg("shared") = py::none(), py::arg("shared_gate") = py::none(),
         py::arg("residual") = py::none(), py::arg("norm_w") = py::none(), py::arg("normed") = py::none(),
-        py::arg("eps") = 1e-6);
+        py::arg("eps") = 1e-6, py::arg("local_offsets") = py::none(), py::arg("peer_out") = py::none(),
+        py::arg("rows_per") = 0);
   m.def("embed", &embed, "embedding gather with multimodal overwrite");
   m.def("vq_embed", &vq_embed, "dual-AR input embedding with the scaled VQ codebook sum");
   m.def("ipc_alloc", &ipc_alloc, "cudaMalloc + zero, returns the device address");
@@ -648,6 +745,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_open", &ipc_open, "maps a peer's IPC handle, returns its address in this process");
   m.def("ipc_close", &ipc_close, "unmaps a peer buffer");
   m.def("tensor_at", &tensor_at, "non-owning CUDA tensor over a device address");
+  m.def("tp_reduce_norm", &tp_reduce_norm, "tensor-parallel reduce-scatter + residual + RMSNorm + all-gather "
+        "over peer memory");
+  m.def("tp_wait", &tp_wait, "tensor-parallel: wait until every rank's gathered rows have landed");
   m.def("ep_counts", &ep_counts, "expert-parallel: exchange per-expert counts, derive offsets");
   m.def("ep_dispatch", &ep_dispatch, "expert-parallel: rows to their experts' ranks (expert-major) + barrier");
   m.def("ep_combine", &ep_combine, "expert-parallel: expert outputs back to their source slots + barrier");

@@ -364,7 +364,12 @@ __global__ void moe_scatter_kernel(MoeRouteArgs a) {
       a.inv_perm[i] = pos;
     }
     pos = __shfl_sync(0xffffffffu, pos, 0);
-    if (a.x != nullptr) {
+    bool copy = a.x != nullptr;
+    if (copy && a.local_el > 0) {  // tensor-parallel MoE: only this rank's experts are computed
+      const int e = a.topk_ids[i];
+      copy = e >= a.local_e0 && e < a.local_e0 + a.local_el;
+    }
+    if (copy) {
       const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.x) +
                                                         static_cast<int64_t>(i / a.topk) * a.hidden);
       uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.x_perm) + static_cast<int64_t>(pos) * a.hidden);
@@ -399,7 +404,9 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(MoeCombineArgs a) {
   __shared__ float red[8];
   const int tok = blockIdx.x;
   if (threadIdx.x < a.topk) {
-    s_pos[threadIdx.x] = a.inv_perm[tok * a.topk + threadIdx.x];
+    int pos = a.inv_perm[tok * a.topk + threadIdx.x];
+    if (a.local_offsets != nullptr && (pos < a.local_offsets[0] || pos >= a.local_offsets[a.local_experts])) pos = -1;
+    s_pos[threadIdx.x] = pos;
     s_w[threadIdx.x] = a.topk_w[tok * a.topk + threadIdx.x];
   }
   __syncthreads();
@@ -417,6 +424,7 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(MoeCombineArgs a) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[j] = 0.f;
     for (int k = 0; k < a.topk; ++k) {
+      if (s_pos[k] < 0) continue;  // another rank's expert (tensor-parallel MoE)
       float f[8];
       unpack8(__ldg(y + static_cast<int64_t>(s_pos[k]) * nvec + v), f);
       const float w = s_w[k];
@@ -430,7 +438,10 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(MoeCombineArgs a) {
       for (int j = 0; j < 8; ++j) acc[j] += sg * f[j];
     }
     uint4 h = pack8(acc);
-    if (a.out != nullptr) static_cast<uint4*>(a.out)[static_cast<int64_t>(tok) * nvec + v] = h;
+    if (a.peer_out != nullptr)
+      reinterpret_cast<uint4*>(a.peer_out[tok / a.rows_per])[static_cast<int64_t>(tok) * nvec + v] = h;
+    else if (a.out != nullptr)
+      static_cast<uint4*>(a.out)[static_cast<int64_t>(tok) * nvec + v] = h;
     if (a.residual != nullptr) {
       uint4* rr = static_cast<uint4*>(a.residual) + static_cast<int64_t>(tok) * nvec + v;
       float r[8];

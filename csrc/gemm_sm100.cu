@@ -51,7 +51,19 @@ struct DevParams {
   int k_splits;          // > 1: split-K over K blocks with an fp32 workspace
   float* ws;             // [tiles][128][BN] fp32 partial sums, zero between calls (the finaliser re-zeroes)
   int* counters;         // [tiles] arrival counters, zero between calls
+  const unsigned long long* peer_out;  // owner scatter: row r -> peer_out[r / rows_per] + r * ldo
+  int rows_per;
+  const unsigned int* wait_flags;      // wait before the first load: wait_flags[i] == *wait_seq
+  const unsigned int* wait_seq;
+  int wait_count;
+  long long wait_timeout_ns;
 };
+
+__device__ __forceinline__ __nv_bfloat16* out_row_bf16(const DevParams& p, int row) {
+  if (p.peer_out != nullptr)
+    return reinterpret_cast<__nv_bfloat16*>(p.peer_out[row / p.rows_per]) + static_cast<int64_t>(row) * p.ldo;
+  return static_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.ldo;
+}
 
 // Vector fp32 reduction into global memory (sm_90+): fire-and-forget, no return value.
 __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
@@ -190,6 +202,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
+      if (p.wait_count > 0) {
+        // the activations are gathered from the other ranks: wait (bounded) until all have landed
+        const uint32_t target = *reinterpret_cast<const volatile uint32_t*>(p.wait_seq);
+        const uint64_t t0 = globaltimer_ns();
+        for (int i = 0; i < p.wait_count; ++i) {
+          uint32_t v;
+          do {
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p.wait_flags + i) : "memory");
+            if (v == target) break;
+            if (globaltimer_ns() - t0 > static_cast<uint64_t>(p.wait_timeout_ns)) {
+              if (p.status) atomicExch(p.status, kStatusPeerTimeout);
+              break;
+            }
+          } while (true);
+        }
+      }
       int stage = 0;
       uint32_t phase = 0;
       long issued = 0;
@@ -321,7 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (p.out_f32) {
                 static_cast<float*>(p.out)[static_cast<int64_t>(row) * p.ldo + m] = v;
               } else {
-                static_cast<__nv_bfloat16*>(p.out)[static_cast<int64_t>(row) * p.ldo + m] = __float2bfloat16(v);
+                out_row_bf16(p, row)[m] = __float2bfloat16(v);
               }
             }
           }
@@ -362,7 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                   float v = epilogue_act(vf[j] + bias_v, p.act);
                   if (p.residual != nullptr) v += __bfloat162float(p.residual[static_cast<int64_t>(row) * p.ldr + m]);
                   if (p.out_f32) static_cast<float*>(p.out)[static_cast<int64_t>(row) * p.ldo + m] = v;
-                  else static_cast<__nv_bfloat16*>(p.out)[static_cast<int64_t>(row) * p.ldo + m] = __float2bfloat16(v);
+                  else out_row_bf16(p, row)[m] = __float2bfloat16(v);
                 }
               }
             }
@@ -476,6 +504,12 @@ cudaError_t launch(const GemmArgs& a, cudaStream_t stream) {
   p.k_splits = 1;
   p.ws = nullptr;
   p.counters = nullptr;
+  p.peer_out = a.peer_out;
+  p.rows_per = a.rows_per > 0 ? a.rows_per : 1;
+  p.wait_flags = a.wait_flags;
+  p.wait_seq = a.wait_seq;
+  p.wait_count = a.wait_flags != nullptr && a.wait_seq != nullptr ? a.wait_count : 0;
+  p.wait_timeout_ns = a.wait_timeout_ns;
   const int m_tiles = (a.m_out + kBM - 1) / kBM;
   const int num_kb = (a.k + kBK - 1) / kBK;
   // Split-K for dense GEMMs that would leave most SMs idle (decode projections).
@@ -496,6 +530,10 @@ cudaError_t launch(const GemmArgs& a, cudaStream_t stream) {
           p.ws = a.splitk_ws;
           // tiles within the counter slots: the last split finalises in-kernel (no reduce launch)
           if (tiles <= a.splitk_counter_slots) p.counters = a.splitk_counters;
+          if (p.counters == nullptr && a.peer_out != nullptr) {  // the fallback reduce writes locally only
+            p.k_splits = 1;
+            p.ws = nullptr;
+          }
         }
       }
     }

@@ -38,12 +38,24 @@ struct GemmArgs {
   int* status;            // device int32 status word (may be nullptr)
   int max_ctas;           // 0 = one CTA per SM
   // Optional split-K scratch for dense, non-gated GEMMs with few output tiles:
-  // fp32 partials [k_splits][rows][m_out], reduced by a second kernel.  Calls
-  // that share it must not overlap on the GPU.
+  // one fp32 plane [tiles][128][token tile] that the splits add into and the
+  // last split of each tile (per-tile arrival counters) reads back, re-zeroes
+  // and finalises.  Calls that share it must not overlap on the GPU.
   float* splitk_ws;
   long long splitk_ws_floats;
-  int* splitk_counters;   // unused (kept for ABI stability of GemmArgs)
+  int* splitk_counters;
   int splitk_counter_slots;
+  // Optional owner scatter (tensor parallel): bf16 output row r is stored at
+  // peer_out[r / rows_per] + r * ldo, i.e. straight into the memory of the
+  // rank that owns token r (over NVLink for the other ranks).
+  const unsigned long long* peer_out;   // device [world]
+  int rows_per;
+  // Optional wait before the first TMA load: flags[i] == *wait_seq for i < wait_count
+  // (the all-gather of this GEMM's activations has landed).  Bounded by wait_timeout_ns.
+  const unsigned int* wait_flags;
+  const unsigned int* wait_seq;
+  int wait_count;
+  long long wait_timeout_ns;
 };
 cudaError_t gemm_bf16(const GemmArgs& args, cudaStream_t stream);
 
@@ -147,6 +159,7 @@ struct MoeRouteArgs {
   void* x_perm;            // [tokens * topk, hidden]
   int hidden;
   int self_clean;          // cursor has experts + 1 entries: the last scatter CTA re-zeroes counts / cursor
+  int local_e0, local_el;  // local_el > 0: copy x rows only for experts [e0, e0 + El) (tensor-parallel MoE)
 };
 cudaError_t moe_route(const MoeRouteArgs& a, cudaStream_t stream);
 
@@ -164,6 +177,13 @@ struct MoeCombineArgs {
   const void* norm_w;      // [hidden]
   void* normed;            // [tokens, hidden]
   float eps;
+  // tensor-parallel MoE: only positions of this rank's experts count (offsets of
+  // experts e0 .. e0 + El, pointer already advanced to e0), and row t is stored at
+  // peer_out[t / rows_per] + t * hidden (the owner's partial-sum slot)
+  const int* local_offsets;
+  int local_experts;
+  const unsigned long long* peer_out;
+  int rows_per;
 };
 cudaError_t moe_combine(const MoeCombineArgs& a, cudaStream_t stream);
 
@@ -254,5 +274,23 @@ struct EpArgs {
 cudaError_t ep_counts(const EpArgs& a, cudaStream_t stream);
 cudaError_t ep_dispatch(const EpArgs& a, cudaStream_t stream);
 cudaError_t ep_combine(const EpArgs& a, const void* y, int64_t y_stride, cudaStream_t stream);
+
+// ---------------------------------------------------------------- tensor parallel
+struct TpReduceArgs {
+  const unsigned long long* peer_part;   // [world] each rank's part region bf16 [world][max_tokens][H]
+  const unsigned long long* peer_gath;   // [world] each rank's gath region bf16 [max_tokens][H]
+  const unsigned long long* peer_gres;   // [world] each rank's gres region, or nullptr (no residual gather)
+  const unsigned long long* peer_flags;  // [world] each rank's flags u32 [2][world]
+  int rank, world, tokens, hidden, rows_per, max_tokens;
+  void* residual;          // local bf16 [tokens, H]: owned rows read and updated
+  const void* norm_w;      // bf16 [H]
+  float eps;
+  unsigned int* seq;       // local sequence counter (device)
+  int* counter;            // local CTA arrival counter, zero between calls
+  int* status;
+  long long timeout_ns;
+};
+cudaError_t tp_reduce_norm(const TpReduceArgs& a, cudaStream_t stream);
+cudaError_t tp_wait(const TpReduceArgs& a, cudaStream_t stream);
 
 }  // namespace omni

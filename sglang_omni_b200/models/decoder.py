@@ -21,6 +21,7 @@ and BailingMoeV2 (sglang_omni/models/ming_omni/thinker.py:155-826).
 """
 from __future__ import annotations
 
+import dataclasses
 import math
 from dataclasses import dataclass, field
 
@@ -115,14 +116,36 @@ class ForwardBatch:
 class DecoderLM(nn.Module):
     """Weights as plain parameters in fused layouts; forward is op-by-op on the kernels."""
 
-    def __init__(self, cfg: DecoderConfig, device="cpu", ep=None):
+    def __init__(self, cfg: DecoderConfig, device="cpu", ep=None, tp=None):
         """``ep``: an ``parallel.EPMoE`` exchange; this rank then holds experts
-        [ep.rank * El, (ep.rank + 1) * El) and the MoE layers run expert-parallel."""
+        [ep.rank * El, (ep.rank + 1) * El) and the MoE layers run expert-parallel.
+
+        ``tp``: a ``parallel.TPGroup``; this rank then holds its query / KV heads
+        (``self.cfg`` describes the local attention: local head counts), the
+        matching o_proj columns, experts [rank * E / world, ...) and slices of the
+        shared-expert / dense MLP intermediate; every rank runs every token and the
+        reduce points are the fused peer-memory kernels of ``parallel.tp``."""
         super().__init__()
+        assert ep is None or tp is None, "expert parallel and tensor parallel are separate layouts"
+        self.full_cfg = cfg
+        self.tp = tp
+        self._tp_split = None
+        if tp is not None:
+            from ..parallel.tp import head_split
+
+            qh, kvh = head_split(cfg.num_heads, cfg.num_kv_heads, tp.rank, tp.world)
+            self._tp_split = (qh, kvh)
+            assert cfg.num_experts % tp.world == 0 or not cfg.num_experts
+            for w in (cfg.intermediate_size, cfg.shared_expert_intermediate_size):
+                assert w % tp.world == 0, "MLP widths must divide over the TP group"
+            cfg = dataclasses.replace(cfg, num_heads=len(qh), num_kv_heads=len(kvh),
+                                      intermediate_size=cfg.intermediate_size // tp.world,
+                                      shared_expert_intermediate_size=cfg.shared_expert_intermediate_size // tp.world)
         self.cfg = cfg
         self.ep = ep
-        self.num_local_experts = cfg.num_experts if ep is None else ep.local_experts
-        self.expert0 = 0 if ep is None else ep.rank * self.num_local_experts
+        par = ep if ep is not None else tp
+        self.num_local_experts = cfg.num_experts if par is None else cfg.num_experts // par.world
+        self.expert0 = 0 if par is None else par.rank * self.num_local_experts
         H, dt = cfg.hidden_size, cfg.dtype
         P = lambda *shape: nn.Parameter(torch.empty(*shape, dtype=dt, device=device), requires_grad=False)  # noqa: E731
         self.embed = P(cfg.vocab_size, H)
@@ -182,8 +205,48 @@ class DecoderLM(nn.Module):
                     p[j].normal_(0.0, std, generator=g)
             else:
                 g = torch.Generator(device=dev).manual_seed(seed * 100003 + idx)
-                p.normal_(0.0, std, generator=g)
+                kind = name.rsplit(".", 1)[-1]
+                full = self.full_shape(kind, p)
+                if full is None:
+                    p.normal_(0.0, std, generator=g)
+                else:   # tensor parallel: draw the unsharded tensor, keep this rank's slice
+                    t = torch.empty(full, dtype=p.dtype, device=dev).normal_(0.0, std, generator=g)
+                    p.copy_(self.shard(kind, t))
         return self
+
+    # ------------------------------------------------------------------ tensor-parallel slices
+    _TP_KINDS = ("qkv", "o", "s13", "s2", "mlp13", "mlp2")
+
+    def full_shape(self, kind: str, p: torch.Tensor):
+        """Unsharded shape of a tensor-parallel parameter (None if not sharded)."""
+        if self.tp is None or kind not in self._TP_KINDS:
+            return None
+        f, H, D = self.full_cfg, self.full_cfg.hidden_size, self.full_cfg.head_dim
+        return {"qkv": (f.q_size + 2 * f.kv_size, H), "o": (H, f.q_size),
+                "s13": (2 * f.shared_expert_intermediate_size, H), "s2": (H, f.shared_expert_intermediate_size),
+                "mlp13": (2 * f.intermediate_size, H), "mlp2": (H, f.intermediate_size)}[kind]
+
+    def shard(self, kind: str, full: torch.Tensor) -> torch.Tensor:
+        """This rank's slice of an unsharded tensor (identity without TP): QKV rows of
+        the local heads, o_proj columns, gate/up rows and down columns of the MLPs."""
+        if self.tp is None or kind not in self._TP_KINDS:
+            return full
+        f, D = self.full_cfg, self.full_cfg.head_dim
+        qh, kvh = self._tp_split
+        r, w = self.tp.rank, self.tp.world
+        if kind == "qkv":
+            q = full[qh.start * D:qh.stop * D]
+            k = full[f.q_size + kvh.start * D:f.q_size + kvh.stop * D]
+            v = full[f.q_size + f.kv_size + kvh.start * D:f.q_size + f.kv_size + kvh.stop * D]
+            return torch.cat([q, k, v], 0)
+        if kind == "o":
+            return full[:, qh.start * D:qh.stop * D]
+        if kind in ("s13", "mlp13"):
+            i = full.shape[0] // 2
+            n = i // w
+            return torch.cat([full[r * n:(r + 1) * n], full[i + r * n:i + (r + 1) * n]], 0)
+        n = full.shape[1] // w
+        return full[:, r * n:(r + 1) * n]
 
     @property
     def head_weight(self):
@@ -260,6 +323,8 @@ class DecoderLM(nn.Module):
             x = ops.embed(fb.input_ids, self.embed, fb.mm_index, fb.mm_embeds)
         T = x.shape[0]
         res = x.clone() if fb.input_embeds is not None else x
+        if self.tp is not None:
+            return self._forward_tp(fb, kv_cache, res)
         h = None
         fused_next = None    # this layer's input norm, already done by the previous MoE combine
         rot = cfg.rotary_dim or cfg.head_dim
@@ -302,6 +367,74 @@ class DecoderLM(nn.Module):
             sel = fb.logits_indices.long()
             return ops.rms_norm(h[sel], self.final_norm, cfg.rms_norm_eps, residual=res[sel].clone())
         return ops.rms_norm(h, self.final_norm, cfg.rms_norm_eps, residual=res)
+
+    def _attention(self, L, i, normed, fb, kv_cache, wait=None):
+        cfg = self.cfg
+        qkv = ops.linear(normed, L.qkv, wait=wait)
+        ops.qkv_rope_store(qkv, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, fb.positions, self.cos_tab,
+                           self.sin_tab, cfg.rotary_dim or cfg.head_dim, getattr(L, "q_norm", None),
+                           getattr(L, "k_norm", None), cfg.rms_norm_eps, cfg.rope_neox, cfg.mrope_section,
+                           cfg.mrope_interleaved, fb.slot_mapping, kv_cache[i, 0], kv_cache[i, 1])
+        scale = 1.0 / math.sqrt(cfg.head_dim)
+        if fb.is_decode:
+            return ops.decode_attention(qkv, kv_cache[i, 0], kv_cache[i, 1], fb.block_table, fb.kv_lens,
+                                        cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, self._dec_ws, scale)
+        return ops.prefill_attention(qkv, kv_cache[i, 0], kv_cache[i, 1], fb.block_table, fb.cu_q, fb.kv_lens,
+                                     fb.tile_req, fb.tile_tok0, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, scale)
+
+    def _forward_tp(self, fb: ForwardBatch, kv_cache: torch.Tensor, res: torch.Tensor) -> torch.Tensor:
+        """Tensor-parallel forward: local heads / experts / MLP slices, every reduce point
+        one fused kernel (owner scatter in the producer, reduce + residual + RMSNorm +
+        all-gather in ``tp.reduce_norm``), the consumer GEMMs wait on the gather flags."""
+        cfg, tp = self.cfg, self.tp
+        T = res.shape[0]
+        eps = cfg.rms_norm_eps
+        nl = len(self.layers)
+        if not res.is_cuda:
+            raise RuntimeError("tensor parallelism runs on CUDA devices only")
+        if fb.deepstack is not None and any(d is not None for d in fb.deepstack):
+            raise NotImplementedError("deepstack injection under tensor parallelism")
+        scatter = tp.scatter(T)
+        normed, wait = ops.rms_norm(res, self.layers[0].ln1, eps), None
+        if 0 in fb.capture_layers:
+            fb.captured[0] = res.clone()
+        for i, L in enumerate(self.layers):
+            attn = self._attention(L, i, normed, fb, kv_cache, wait)
+            ops.linear(attn, L.o, out=tp.part_local[:T], scatter=scatter)
+            normed2 = tp.reduce_norm(res, L.ln2, eps, T)
+            self._mlp_tp(L, normed2, i, T, scatter)
+            last = i + 1 == nl
+            cap = (i + 1) in fb.capture_layers
+            normed = tp.reduce_norm(res, self.final_norm if last else self.layers[i + 1].ln1, eps, T,
+                                    gather_residual=cap)
+            wait = tp.wait
+            if cap:
+                tp.wait_gather()
+                fb.captured[i + 1] = tp.gres[:T].clone()
+        tp.wait_gather()
+        if fb.logits_indices is not None:
+            return normed[fb.logits_indices.long()]
+        return normed.clone()
+
+    def _mlp_tp(self, L, x, i, T, scatter):
+        """MLP of layer i on the gathered rows ``x``; writes this rank's partial rows to their owners."""
+        cfg, tp = self.cfg, self.tp
+        if not cfg.is_moe_layer(i):
+            ops.linear(ops.linear(x, L.mlp13, gated=True, wait=tp.wait), L.mlp2, out=tp.part_local[:T],
+                       scatter=scatter)
+            return
+        if self._moe_ws is None or self._moe_ws.max_tokens < T:
+            self.ensure_workspaces(max(T, 4096), 1, 64)
+        ws = self._moe_ws
+        shared_out = shared_gate = None
+        if cfg.shared_expert_intermediate_size:
+            shared_out = ops.linear(ops.linear(x, L.s13, gated=True, wait=tp.wait), L.s2)
+            if cfg.shared_expert_gate:
+                shared_gate = ops.linear(x, L.sgate, out_dtype=torch.float32, wait=tp.wait)
+        ops.tp_moe(x, L.router, L.w13, L.w2, cfg.topk, ws, self.expert0, tp, scatter,
+                   renormalize=cfg.norm_topk_prob, mode=cfg.router_mode, bias=getattr(L, "router_bias", None),
+                   n_group=cfg.n_group, topk_group=cfg.topk_group, scaling=cfg.routed_scaling_factor,
+                   shared_out=shared_out, shared_gate=shared_gate)
 
     def logits(self, hidden: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         return ops.linear(hidden, self.head_weight, out=out, out_dtype=torch.float32)

@@ -58,9 +58,10 @@ def load_by_prefix(model_path: str, prefix: str) -> dict[str, torch.Tensor]:
 def load_decoder_from_hf(model: DecoderLM, sd: dict[str, torch.Tensor], model_prefix: str = "model.",
                          lm_head_key: str | None = "lm_head.weight", embed_key: str = "embed_tokens.weight") -> None:
     """Fills a DecoderLM from HF-named tensors (prefix of the text model already stripped)."""
-    cfg = model.cfg
+    cfg = model.full_cfg if hasattr(model, "full_cfg") else model.cfg
     g = lambda k: sd[model_prefix + k]  # noqa: E731
     cp = lambda dst, src: dst.copy_(src.to(dst.dtype))  # noqa: E731
+    sh = getattr(model, "shard", lambda kind, t: t)   # tensor parallel: this rank's slice
     if model_prefix + embed_key in sd:
         cp(model.embed, g(embed_key))
     for i, L in enumerate(model.layers):
@@ -68,10 +69,10 @@ def load_decoder_from_hf(model: DecoderLM, sd: dict[str, torch.Tensor], model_pr
         cp(L.ln1, g(p + "input_layernorm.weight"))
         cp(L.ln2, g(p + "post_attention_layernorm.weight"))
         if model_prefix + p + "self_attn.qkv_proj.weight" in sd:
-            cp(L.qkv, g(p + "self_attn.qkv_proj.weight"))
+            cp(L.qkv, sh("qkv", g(p + "self_attn.qkv_proj.weight")))
         else:
-            cp(L.qkv, torch.cat([g(p + f"self_attn.{n}_proj.weight") for n in "qkv"], 0))
-        cp(L.o, g(p + "self_attn.o_proj.weight"))
+            cp(L.qkv, sh("qkv", torch.cat([g(p + f"self_attn.{n}_proj.weight") for n in "qkv"], 0)))
+        cp(L.o, sh("o", g(p + "self_attn.o_proj.weight")))
         if cfg.qk_norm:
             cp(L.q_norm, g(p + "self_attn.q_norm.weight"))
             cp(L.k_norm, g(p + "self_attn.k_norm.weight"))
@@ -91,13 +92,13 @@ def load_decoder_from_hf(model: DecoderLM, sd: dict[str, torch.Tensor], model_pr
                 cp(L.router_bias, g(p + "mlp.gate.e_score_correction_bias"))
             if cfg.shared_expert_intermediate_size:
                 s = p + "mlp.shared_expert."
-                cp(L.s13, torch.cat([g(s + "gate_proj.weight"), g(s + "up_proj.weight")], 0))
-                cp(L.s2, g(s + "down_proj.weight"))
+                cp(L.s13, sh("s13", torch.cat([g(s + "gate_proj.weight"), g(s + "up_proj.weight")], 0)))
+                cp(L.s2, sh("s2", g(s + "down_proj.weight")))
                 if cfg.shared_expert_gate:
                     cp(L.sgate, g(p + "mlp.shared_expert_gate.weight"))
         else:
-            cp(L.mlp13, torch.cat([g(p + "mlp.gate_proj.weight"), g(p + "mlp.up_proj.weight")], 0))
-            cp(L.mlp2, g(p + "mlp.down_proj.weight"))
+            cp(L.mlp13, sh("mlp13", torch.cat([g(p + "mlp.gate_proj.weight"), g(p + "mlp.up_proj.weight")], 0)))
+            cp(L.mlp2, sh("mlp2", g(p + "mlp.down_proj.weight")))
     cp(model.final_norm, g("norm.weight"))
     if model.lm_head is not None and lm_head_key is not None and lm_head_key in sd:
         cp(model.lm_head, sd[lm_head_key])

@@ -2,13 +2,13 @@
 from .attention import DecodeWorkspace, decode_attention, prefill_attention, prefill_tiles, varlen_attention
 from .embedding import embed, vq_embed
 from .gemm import grouped_linear, linear
-from .moe import MoEWorkspace, fused_moe, route
+from .moe import MoEWorkspace, fused_moe, route, tp_moe
 from .norm import layer_norm, rms_norm
 from .rope import qkv_rope_store, rope_tables
 from .sampling import SamplingTensors, sample
 
 __all__ = [
     "DecodeWorkspace", "decode_attention", "prefill_attention", "prefill_tiles", "varlen_attention", "embed", "vq_embed",
-    "grouped_linear", "linear", "MoEWorkspace", "fused_moe", "route", "layer_norm", "rms_norm", "qkv_rope_store",
+    "grouped_linear", "linear", "MoEWorkspace", "fused_moe", "route", "tp_moe", "layer_norm", "rms_norm", "qkv_rope_store",
     "rope_tables", "SamplingTensors", "sample",
 ]

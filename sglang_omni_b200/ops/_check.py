@@ -101,5 +101,6 @@ def check_range(op: str, name: str, t: torch.Tensor, lo: int, hi: int, allow: in
 
 def check_offsets(op: str, offsets: torch.Tensor, rows: int):
     o = _h(offsets)
-    if int(o[0]) != 0 or bool((o[1:] < o[:-1]).any()) or int(o[-1]) > rows:
+    # a sub-range of experts (tensor-parallel MoE) starts past row 0
+    if int(o[0]) < 0 or bool((o[1:] < o[:-1]).any()) or int(o[-1]) > rows:
         _fail(op, f"group offsets not monotone within [0, {rows}]: first {o.tolist()[:6]} last {int(o[-1])}")

@@ -74,10 +74,14 @@ def linear_ref(x, w, bias=None, residual=None, act=None, out_dtype=None, gated=F
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, bias=None, residual=None, act=None, out=None,
-           out_dtype=None, gated: bool = False) -> torch.Tensor:
+           out_dtype=None, gated: bool = False, scatter=None, wait=None) -> torch.Tensor:
     """Y[..., N] = act(X[..., K] @ W[N, K]^T + bias) + residual.
 
     With ``gated`` W stacks [gate; up] ([2N, K]) and Y = silu(X W_gate^T) * (X W_up^T).
+    Tensor parallel (CUDA only): ``scatter = (peer_ptrs, rows_per)`` stores output
+    row r into the owner rank's buffer ``peer_ptrs[r // rows_per] + r * N`` instead of
+    ``out``; ``wait = (flags, seq, timeout_s)`` holds the first operand load until
+    every flag equals ``seq`` (the gathered activations have arrived).
     """
     if not x.is_cuda:
         y = linear_ref(x, w, bias, residual, act, out_dtype, gated)
@@ -91,7 +95,10 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias=None, residual=None, act=None,
     x2 = x if x.is_contiguous() else x.contiguous()
     rows = x2.numel() // x2.shape[-1]
     ws, ctr = splitk_scratch(x.device)
-    ext().gemm(w, x2, out, None, n, gated, bias, residual, act_code(act), rows, status_word(x.device), 0, ws, ctr)
+    peer, rows_per = scatter if scatter is not None else (None, 0)
+    wf, wseq, wt = wait if wait is not None else (None, None, 2.0)
+    ext().gemm(w, x2, out, None, n, gated, bias, residual, act_code(act), rows, status_word(x.device), 0, ws, ctr,
+               peer, rows_per, wf, wseq, wt)
     return out
 
 

@@ -145,3 +145,29 @@ def fused_moe(x: torch.Tensor, w_router: torch.Tensor, w13: torch.Tensor, w2: to
     else:
         ext().moe_combine(ws.y_perm[:rows], ws.inv_perm[:T], ws.topk_w[:T], out, shared_out, shared_gate)
     return out
+
+
+def tp_moe(x: torch.Tensor, w_router: torch.Tensor, w13_local: torch.Tensor, w2_local: torch.Tensor, topk: int,
+           ws: MoEWorkspace, expert0: int, tp, scatter, renormalize: bool = True, mode: int = 0, bias=None,
+           n_group: int = 1, topk_group: int = 1, scaling: float = 1.0, shared_out: torch.Tensor | None = None,
+           shared_gate: torch.Tensor | None = None) -> None:
+    """Tensor-parallel MoE: every rank routes every token (identical routing on all
+    ranks), computes only its experts [expert0, expert0 + El) and the combine stores
+    each token's partial sum (local experts + this rank's shared-expert slice) into
+    the owner's partial slot (``scatter``) for ``tp.reduce_norm``.  ``x`` is the
+    gathered activations; the router GEMM waits for them."""
+    T = x.shape[0]
+    El = w13_local.shape[0]
+    E = ws.offsets.numel() - 1
+    logits = ws.logits[:T]
+    linear(x, w_router, out=logits, wait=tp.wait)
+    rows = T * topk
+    ext().moe_route(logits, topk, mode, bias, n_group, topk_group, renormalize, scaling, ws.topk_ids[:T],
+                    ws.topk_w[:T], ws.counts, ws.cursor, ws.offsets, ws.inv_perm[:T], x, ws.x_perm[:rows],
+                    expert0, El)
+    loc = ws.offsets[expert0:expert0 + El + 1]
+    exp_rows = max(1, rows // E)
+    grouped_linear(ws.x_perm[:rows], w13_local, loc, gated=True, out=ws.h_perm[:rows], expected_rows=exp_rows)
+    grouped_linear(ws.h_perm[:rows], w2_local, loc, gated=False, out=ws.y_perm[:rows], expected_rows=exp_rows)
+    ext().moe_combine(ws.y_perm[:rows], ws.inv_perm[:T], ws.topk_w[:T], None, shared_out, shared_gate,
+                      None, None, None, 1e-6, loc, scatter[0], scatter[1])

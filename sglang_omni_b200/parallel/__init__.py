@@ -3,5 +3,6 @@ buffers and the expert-parallel MoE exchange."""
 from .dist import ParallelState, init_distributed
 from .ep_moe import EPMoE
 from .symm import SymmetricBuffer
+from .tp import TPGroup, head_split
 
-__all__ = ["ParallelState", "init_distributed", "SymmetricBuffer", "EPMoE"]
+__all__ = ["ParallelState", "init_distributed", "SymmetricBuffer", "EPMoE", "TPGroup", "head_split"]

@@ -1,0 +1,171 @@
+"""Tensor parallelism over peer memory on 2 GPUs (one process per GPU): the
+sharded decoder (local heads, local experts / MLP slices, fused owner-scatter
+epilogues + reduce/RMSNorm/all-gather kernel) must match the unsharded model of
+the same weights, for a prefill and for engine decode steps (eager and CUDA
+graphs).  Host-side pieces (head split, weight slices) also run on the CPU."""
+import os
+import socket
+
+import pytest
+import torch
+
+from sglang_omni_b200.models.decoder import DecoderConfig, DecoderLM
+
+
+def _cfg(moe: bool, **kw):
+    c = DecoderConfig(vocab_size=512, hidden_size=256, num_layers=3, num_heads=8, num_kv_heads=2, head_dim=64,
+                      intermediate_size=512, num_experts=16 if moe else 0, topk=4 if moe else 0,
+                      moe_intermediate_size=128, shared_expert_intermediate_size=128 if moe else 0,
+                      rope_theta=10000.0, mrope_section=[12, 10, 10], qk_norm=True, max_position=4096,
+                      dtype=torch.bfloat16)
+    for k, v in kw.items():
+        setattr(c, k, v)
+    return c
+
+
+def test_head_split_gqa_groups():
+    from sglang_omni_b200.parallel.tp import head_split
+
+    for world in (1, 2, 4, 8):
+        qs, kvs = [], []
+        for r in range(world):
+            q, kv = head_split(32, 4, r, world)
+            qs += list(q)
+            kvs.append(list(kv))
+            assert all(h // 8 in kv for h in q)
+        assert qs == list(range(32))
+    assert head_split(32, 4, 5, 8)[1] == range(2, 3)
+
+
+class _FakeTP:
+    def __init__(self, rank, world):
+        self.rank, self.world = rank, world
+
+
+def test_shards_reassemble_cpu():
+    """Concatenating every rank's slices gives back the unsharded tensors."""
+    from sglang_omni_b200.parallel.tp import head_split
+
+    cfg = _cfg(True, dtype=torch.float32)
+    full = DecoderLM(cfg).random_init_(seed=3)
+    world = 2
+    parts = [DecoderLM(cfg, tp=_FakeTP(r, world)).random_init_(seed=3) for r in range(world)]
+    L0 = full.layers[1]
+    D, qs, kvs = cfg.head_dim, cfg.q_size, cfg.kv_size
+    for r, m in enumerate(parts):
+        q, kv = head_split(cfg.num_heads, cfg.num_kv_heads, r, world)
+        P = m.layers[1]
+        assert torch.equal(P.qkv[:len(q) * D], L0.qkv[q.start * D:q.stop * D])
+        assert torch.equal(P.qkv[len(q) * D:len(q) * D + len(kv) * D], L0.qkv[qs + kv.start * D:qs + kv.stop * D])
+        assert torch.equal(P.o, L0.o[:, q.start * D:q.stop * D])
+        El = cfg.num_experts // world
+        assert torch.equal(P.w13, L0.w13[r * El:(r + 1) * El])
+        Is = cfg.shared_expert_intermediate_size // world
+        assert torch.equal(P.s13[:Is], L0.s13[r * Is:(r + 1) * Is])
+        assert torch.equal(P.s2, L0.s2[:, r * Is:(r + 1) * Is])
+        assert torch.equal(P.router, L0.router) and torch.equal(m.embed, full.embed)
+        assert m.cfg.num_heads == cfg.num_heads // world and m.cfg.num_kv_heads == 1
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    try:
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=60))
+        from sglang_omni_b200.engines.ar import AREngine, ARRequest, KVPool
+        from sglang_omni_b200.ops._ext import check_status
+        from sglang_omni_b200.parallel import TPGroup
+        from sglang_omni_b200.sampling_params import SamplingParams
+        from test_ar_engine import full_logits
+
+        errs = {}
+        for moe in (True, False):
+            cfg = _cfg(moe)
+            ref = DecoderLM(cfg, device=dev).random_init_(seed=11, std=0.05)
+            tp = TPGroup(cfg.hidden_size, 512, dev)
+            m = DecoderLM(cfg, device=dev, tp=tp).random_init_(seed=11, std=0.05)
+            toks = torch.randint(0, cfg.vocab_size, (150,), generator=torch.Generator().manual_seed(5)).tolist()
+            a = full_logits(ref, toks, dev)
+            b = full_logits(m, toks, dev)
+            torch.cuda.synchronize()
+            check_status(dev)
+            errs[f"prefill_moe{moe}"] = float((a - b).norm() / a.norm())
+            # engine: greedy decode, graphs on / off, identical requests on both ranks
+            for graphs in (False, True):
+                pool = KVPool(m.cfg.num_layers, m.cfg.num_kv_heads, m.cfg.head_dim, 128, dev, m.cfg.dtype)
+                eng = AREngine(m, pool, max_batch=4, max_prefill_tokens=128, max_context=512, use_graphs=graphs)
+                g = torch.Generator().manual_seed(7)
+                reqs = [ARRequest(rid=f"r{i}", prompt_ids=torch.randint(0, cfg.vocab_size, (20 + 13 * i,),
+                                                                       generator=g).tolist(),
+                                  sampling=SamplingParams(temperature=0.0, ignore_eos=True), max_new_tokens=12)
+                        for i in range(5)]
+                eng.generate(reqs)
+                torch.cuda.synchronize()
+                check_status(dev)
+                worst = 0.0
+                for r in reqs:
+                    lg = full_logits(ref, list(r.prompt_ids) + r.output_ids, dev)
+                    for i, tok in enumerate(r.output_ids):
+                        row = lg[len(r.prompt_ids) - 1 + i]
+                        worst = max(worst, float(row.max() - row[tok]))
+                errs[f"greedy_gap_moe{moe}_graphs{graphs}"] = worst
+                # both ranks produced the same tokens
+                mine = torch.tensor([t for r in reqs for t in r.output_ids], device=dev)
+                other = mine.clone()
+                dist.broadcast(other, 0)
+                errs[f"rank_mismatch_moe{moe}_graphs{graphs}"] = float((mine != other).sum())
+                eng = pool = None
+            m = None
+            import gc
+
+            gc.collect()
+            torch.cuda.synchronize()
+            tp.close()
+        dist.destroy_process_group()
+        q.put((rank, errs, None))
+    except Exception:  # report instead of hanging the parent
+        import traceback
+
+        q.put((rank, None, traceback.format_exc()))
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp_matches_unsharded():
+    import sys
+
+    import torch.multiprocessing as mp
+
+    sys.path.insert(0, os.path.dirname(__file__))
+    world = 2
+    ctx = mp.get_context("spawn")
+    qu = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, qu)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [qu.get(timeout=600) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, errs, tb in res:
+        assert tb is None, tb
+        for k, v in errs.items():
+            if k.startswith("prefill"):
+                assert v < 0.03, (rank, k, v)
+            elif k.startswith("greedy"):
+                assert v < 0.2, (rank, k, v)
+            else:
+                assert v == 0, (rank, k, v)
