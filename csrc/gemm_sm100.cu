@@ -49,7 +49,7 @@ struct DevParams {
   int act;
   int* status;
   int k_splits;          // > 1: split-K over K blocks with an fp32 workspace
-  float* ws;             // [tiles][128][BN] fp32 partial sums, zero between calls (the finaliser re-zeroes)
+  float* ws;             // [splits][tiles][128][BN] fp32 partial sums (each split owns its plane)
   int* counters;         // [tiles] arrival counters, zero between calls
   const unsigned long long* peer_out;  // owner scatter: row r -> peer_out[r / rows_per] + r * ldo
   int rows_per;
@@ -63,12 +63,6 @@ __device__ __forceinline__ __nv_bfloat16* out_row_bf16(const DevParams& p, int r
   if (p.peer_out != nullptr)
     return reinterpret_cast<__nv_bfloat16*>(p.peer_out[row / p.rows_per]) + static_cast<int64_t>(row) * p.ldo;
   return static_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.ldo;
-}
-
-// Vector fp32 reduction into global memory (sm_90+): fire-and-forget, no return value.
-__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
-               : "memory");
 }
 
 __device__ __forceinline__ float epilogue_act(float v, int act) {
@@ -324,13 +318,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (GATED) tmem_ld_32x32b_x16(t_base + BN + c, u);
         tmem_ld_wait();
         if (ks > 1) {
-          // split-K partial: added into the tile's fp32 plane [t][128][BN] (thread = one A row,
-          // 16 consecutive tokens = four 16-byte vector reductions)
-          float* wsp = p.ws + (static_cast<int64_t>(t) * kBM + lane_base + lane) * BN + c;
+          // split-K partial into this split's plane [split][t][128][BN] (thread = one A row,
+          // 16 consecutive tokens = four 16-byte stores); summed in split order by the finaliser,
+          // so the result does not depend on which split arrives first
+          float4* wsp = reinterpret_cast<float4*>(
+              p.ws + ((static_cast<int64_t>(w - t * ks) * total_tiles + t) * kBM + lane_base + lane) * BN + c);
 #pragma unroll
           for (int j = 0; j < 16; j += 4)
-            red_add_v4(wsp + j, __uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
-                       __uint_as_float(r[j + 3]));
+            __stcg(wsp + j / 4, make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                            __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3])));
         } else if (m_ok) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
@@ -370,17 +366,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (s_last) {
           __threadfence();
-          // up to 32 tokens per round (eight 16-byte loads in flight per thread), then re-zero the plane
-          constexpr int kChunk = BN < 32 ? BN : 32;
-          float* wsp = p.ws + (static_cast<int64_t>(t) * kBM + lane_base + lane) * BN;
+          // sum the split planes in split order, two splits per round (up to 32 16-byte loads in flight)
+          constexpr int kChunk = BN < 64 ? BN : 64;
+          const int64_t plane4 = static_cast<int64_t>(total_tiles) * kBM * BN / 4;
+          const float4* wsp = reinterpret_cast<const float4*>(p.ws + (static_cast<int64_t>(t) * kBM + lane_base + lane) * BN);
 #pragma unroll 1
           for (int c = 0; c < BN; c += kChunk) {
             float4 v4[kChunk / 4];
 #pragma unroll
-            for (int q = 0; q < kChunk / 4; ++q) v4[q] = __ldcg(reinterpret_cast<const float4*>(wsp + c) + q);
+            for (int q = 0; q < kChunk / 4; ++q) v4[q] = __ldcg(wsp + c / 4 + q);
+#pragma unroll 1
+            for (int sp = 1; sp < ks; sp += 2) {
+              float4 x0[kChunk / 4], x1[kChunk / 4];
+              const bool two = sp + 1 < ks;
 #pragma unroll
-            for (int q = 0; q < kChunk / 4; ++q)
-              __stcg(reinterpret_cast<float4*>(wsp + c) + q, make_float4(0.f, 0.f, 0.f, 0.f));
+              for (int q = 0; q < kChunk / 4; ++q) {
+                x0[q] = __ldcg(wsp + sp * plane4 + c / 4 + q);
+                x1[q] = two ? __ldcg(wsp + (sp + 1) * plane4 + c / 4 + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+              }
+#pragma unroll
+              for (int q = 0; q < kChunk / 4; ++q) {
+                v4[q].x = (v4[q].x + x0[q].x) + x1[q].x;
+                v4[q].y = (v4[q].y + x0[q].y) + x1[q].y;
+                v4[q].z = (v4[q].z + x0[q].z) + x1[q].z;
+                v4[q].w = (v4[q].w + x0[q].w) + x1[q].w;
+              }
+            }
             if (m_ok) {
               const float* vf = reinterpret_cast<const float*>(v4);
 #pragma unroll
@@ -408,20 +419,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Fallback finaliser (more tiles than arrival counters): reads the fp32 plane
-// [tiles][128][BN], re-zeroes it and applies the epilogue.
-__global__ void splitk_reduce_kernel(float* __restrict__ ws, int bn, int n_tiles, int rows, int m_out, void* out,
-                                     int64_t ldo, int out_f32, const __nv_bfloat16* __restrict__ bias,
+// Fallback finaliser (more tiles than arrival counters): sums the split planes
+// [splits][tiles][128][BN] in split order and applies the epilogue.
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int ks, int bn, int n_tiles, int total_tiles,
+                                     int rows, int m_out, void* out, int64_t ldo, int out_f32,
+                                     const __nv_bfloat16* __restrict__ bias,
                                      const __nv_bfloat16* __restrict__ residual, int64_t ldr, int act) {
   const int64_t n = static_cast<int64_t>(rows) * m_out;
+  const int64_t plane = static_cast<int64_t>(total_tiles) * kBM * bn;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int row = static_cast<int>(i / m_out);
     const int m = static_cast<int>(i - static_cast<int64_t>(row) * m_out);
     const int t = (m / kBM) * n_tiles + row / bn;
-    float* src = ws + (static_cast<int64_t>(t) * kBM + m % kBM) * bn + row % bn;
-    float v = __ldcg(src);
-    __stcg(src, 0.f);
+    const float* src = ws + (static_cast<int64_t>(t) * kBM + m % kBM) * bn + row % bn;
+    float v = 0.f;
+    for (int s = 0; s < ks; ++s) v += __ldcg(src + s * plane);
     if (bias != nullptr) v += __bfloat162float(bias[m]);
     v = epilogue_act(v, act);
     if (residual != nullptr) v += __bfloat162float(residual[static_cast<int64_t>(row) * ldr + m]);
@@ -520,12 +533,12 @@ cudaError_t launch(const GemmArgs& a, cudaStream_t stream) {
       // one wave: tiles * splits <= SMs (a partial second wave doubles the time)
       int ksp = static_cast<int>(sms / tiles);
       if (ksp > num_kb / 2) ksp = num_kb / 2;
-      if (ksp > 16) ksp = 16;
+      if (ksp > 8) ksp = 8;   // the finaliser reads every split: keep its rounds few
       if (ksp > 1) {
         const int per = (num_kb + ksp - 1) / ksp;
         ksp = (num_kb + per - 1) / per;  // no empty splits
         const long long plane = static_cast<long long>(m_tiles) * kBM * ((a.rows + BN - 1) / BN) * BN;
-        if (plane <= a.splitk_ws_floats) {
+        if (plane * ksp <= a.splitk_ws_floats) {
           p.k_splits = ksp;
           p.ws = a.splitk_ws;
           // tiles within the counter slots: the last split finalises in-kernel (no reduce launch)
@@ -549,8 +562,9 @@ cudaError_t launch(const GemmArgs& a, cudaStream_t stream) {
     const long long n = static_cast<long long>(a.rows) * a.m_out;
     int rgrid = static_cast<int>((n + 255) / 256);
     if (rgrid > 4 * num_sms()) rgrid = 4 * num_sms();
-    splitk_reduce_kernel<<<rgrid, 256, 0, stream>>>(p.ws, BN, (a.rows + BN - 1) / BN, a.rows, a.m_out, a.out, a.ldo,
-                                                    a.out_f32, p.bias, p.residual, a.ldr, a.act);
+    const int n_tiles = (a.rows + BN - 1) / BN;
+    splitk_reduce_kernel<<<rgrid, 256, 0, stream>>>(p.ws, p.k_splits, BN, n_tiles, m_tiles * n_tiles, a.rows, a.m_out,
+                                                    a.out, a.ldo, a.out_f32, p.bias, p.residual, a.ldr, a.act);
   }
   return cudaGetLastError();
 }
