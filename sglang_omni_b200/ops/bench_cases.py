@@ -1,7 +1,7 @@
 """Small standalone kernel workloads for profiling (one kernel family per case,
 three launches, a few GB on the device at most):
 
-    python -m sglang_omni_b200.ops.bench_cases {moe_w13|dense_prefill|decode_attn}
+    python -m sglang_omni_b200.ops.bench_cases {moe_w13|dense_prefill|decode_attn|decode_dense|time}
 
 Used to produce the ncu summaries of the hot kernels.
 """
@@ -44,10 +44,68 @@ def run(case: str) -> None:
         ws = A.DecodeWorkspace(B, hq, d, ctx, "cuda")
         for _ in range(3):
             A.decode_attention(q, k, v, bt, kl, hq, hkv, d, ws)
+    elif case == "decode_dense":
+        # thinker decode projections at batch 64: QKV, o_proj, router (fp32 logits); split-K path
+        x = torch.randn(64, 2048, device="cuda").bfloat16()
+        xo = torch.randn(64, 4096, device="cuda").bfloat16()
+        wq = (torch.randn(5120, 2048, device="cuda") * 0.02).bfloat16()
+        wo = (torch.randn(2048, 4096, device="cuda") * 0.02).bfloat16()
+        wr = (torch.randn(128, 2048, device="cuda") * 0.02).bfloat16()
+        for _ in range(3):
+            L.linear(x, wq)
+            L.linear(xo, wo)
+            L.linear(x, wr, out_dtype=torch.float32)
+    elif case == "time":
+        _time_cases()
+        return
     else:
         raise SystemExit(f"unknown case {case!r}")
     torch.cuda.synchronize()
     print("ok", case)
+
+
+def _time_cases() -> None:
+    """CUDA-event times of the decode-step kernels in isolation (L2 flushed between iterations)."""
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+
+    def t(fn, n=20):
+        for _ in range(3):
+            fn()
+        tot = 0.0
+        for _ in range(n):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            tot += a.elapsed_time(b)
+        return tot / n * 1e3
+
+    x = torch.randn(64, 2048, device="cuda").bfloat16()
+    xo = torch.randn(64, 4096, device="cuda").bfloat16()
+    wq = (torch.randn(5120, 2048, device="cuda") * 0.02).bfloat16()
+    wo = (torch.randn(2048, 4096, device="cuda") * 0.02).bfloat16()
+    wr = (torch.randn(128, 2048, device="cuda") * 0.02).bfloat16()
+    wl = (torch.randn(151936, 2048, device="cuda") * 0.02).bfloat16()
+    res = {
+        "qkv 5120x2048 T64": (t(lambda: L.linear(x, wq)), wq.numel() * 2),
+        "o_proj 2048x4096 T64": (t(lambda: L.linear(xo, wo)), wo.numel() * 2),
+        "router 128x2048 T64 fp32": (t(lambda: L.linear(x, wr, out_dtype=torch.float32)), wr.numel() * 2),
+        "lm_head 151936x2048 T64 fp32": (t(lambda: L.linear(x, wl, out_dtype=torch.float32)), wl.numel() * 2),
+    }
+    B, hq, hkv, d, ctx = 64, 32, 4, 128, 1152
+    pages = (ctx + 63) // 64
+    k = torch.randn(B * pages + 1, hkv, 64, d, device="cuda").bfloat16()
+    v = torch.randn_like(k)
+    bt = torch.arange(B * pages, dtype=torch.int32, device="cuda").view(B, pages)
+    kl = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
+    q = torch.randn(B, hq * d, device="cuda").bfloat16()
+    ws = A.DecodeWorkspace(B, hq, d, ctx, "cuda")
+    res["decode_attn B64 ctx1152"] = (t(lambda: A.decode_attention(q, k, v, bt, kl, hq, hkv, d, ws)),
+                                      2 * B * ctx * hkv * d * 2)
+    for name, (us, nbytes) in res.items():
+        print(f"{name:32s} {us:8.2f} us  {nbytes / us / 1e3:7.1f} GB/s")
 
 
 if __name__ == "__main__":
