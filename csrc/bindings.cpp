@@ -94,13 +94,15 @@ void gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& out, co
   args.act = static_cast<int>(act);
   args.status = status_ptr(status);
   args.max_ctas = static_cast<int>(max_ctas);
-  if (splitk_ws.has_value() && splitk_counters.has_value()) {
-    TORCH_CHECK(splitk_ws->scalar_type() == at::kFloat && splitk_counters->scalar_type() == at::kInt,
-                "split-K scratch must be fp32 / int32");
+  if (splitk_ws.has_value()) {
+    TORCH_CHECK(splitk_ws->scalar_type() == at::kFloat, "split-K scratch must be fp32");
     args.splitk_ws = splitk_ws->data_ptr<float>();
     args.splitk_ws_floats = splitk_ws->numel();
-    args.splitk_counters = splitk_counters->data_ptr<int>();
-    args.splitk_counter_slots = static_cast<int>(splitk_counters->numel());
+    if (splitk_counters.has_value()) {  // without counters a second kernel finalises the splits
+      TORCH_CHECK(splitk_counters->scalar_type() == at::kInt, "split-K counters must be int32");
+      args.splitk_counters = splitk_counters->data_ptr<int>();
+      args.splitk_counter_slots = static_cast<int>(splitk_counters->numel());
+    }
   }
   if (peer_out.has_value()) {
     TORCH_CHECK(peer_out->scalar_type() == at::kLong && peer_out->is_cuda() && !args.out_f32 && rows_per > 0,

@@ -526,7 +526,7 @@ cudaError_t launch(const GemmArgs& a, cudaStream_t stream) {
   const int m_tiles = (a.m_out + kBM - 1) / kBM;
   const int num_kb = (a.k + kBK - 1) / kBK;
   // Split-K for dense GEMMs that would leave most SMs idle (decode projections).
-  if (!GATED && a.offsets == nullptr && a.splitk_ws != nullptr && a.splitk_counters != nullptr) {
+  if (!GATED && a.offsets == nullptr && a.splitk_ws != nullptr) {
     const long tiles = static_cast<long>(m_tiles) * ((a.rows + BN - 1) / BN);
     const int sms = num_sms();
     if (tiles * 2 <= sms && num_kb >= 4) {
@@ -542,7 +542,7 @@ cudaError_t launch(const GemmArgs& a, cudaStream_t stream) {
           p.k_splits = ksp;
           p.ws = a.splitk_ws;
           // tiles within the counter slots: the last split finalises in-kernel (no reduce launch)
-          if (tiles <= a.splitk_counter_slots) p.counters = a.splitk_counters;
+          if (a.splitk_counters != nullptr && tiles <= a.splitk_counter_slots) p.counters = a.splitk_counters;
           if (p.counters == nullptr && a.peer_out != nullptr) {  // the fallback reduce writes locally only
             p.k_splits = 1;
             p.ws = nullptr;

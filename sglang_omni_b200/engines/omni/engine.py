@@ -21,13 +21,29 @@ log = logging.getLogger(__name__)
 
 
 class OmniEngine(Engine):
-    def __init__(self, scheduler, model_runner, cache_manager=None, run_in_thread: bool = True):
+    def __init__(self, scheduler, model_runner, cache_manager=None, run_in_thread: bool = True,
+                 stream_priority: int | None = None, poll_s: float = 0.0):
+        """``stream_priority``: run steps on a dedicated CUDA stream of this priority
+        (lower = served first by the block scheduler; encoders on the time-to-first-
+        audio path use the highest).  ``poll_s``: sleep between polls while the
+        planner holds requests back (a batching window)."""
         self.scheduler = scheduler
         self.model_runner = model_runner
         self.cache = cache_manager
         self.run_in_thread = run_in_thread
+        self.stream_priority = stream_priority
+        self.poll_s = poll_s
+        self._stream = None
         self._task: asyncio.Task | None = None
         self._wake: asyncio.Event | None = None
+
+    def _engine_stream(self):
+        if self.stream_priority is None or self._stream is not None:
+            return self._stream
+        dev = torch.device(getattr(self.model_runner, "device", "cpu"))
+        if dev.type == "cuda":
+            self._stream = torch.cuda.Stream(device=dev, priority=self.stream_priority)
+        return self._stream
 
     async def start(self):
         if self._task is None:
@@ -71,10 +87,11 @@ class OmniEngine(Engine):
         outputs: dict[str, RequestOutput] = dict(hits)
         reqs_all = list(sched_out.requests)
         if sched_out.requests:
+            stream = self._engine_stream()
             if self.run_in_thread:
-                res = await asyncio.to_thread(_execute_synced, self.model_runner, sched_out)
+                res = await asyncio.to_thread(_execute_synced, self.model_runner, sched_out, stream)
             else:
-                res = _execute_synced(self.model_runner, sched_out)
+                res = _execute_synced(self.model_runner, sched_out, stream)
             outputs.update(res.outputs)
             if self.cache is not None:
                 for r in sched_out.requests:
@@ -94,7 +111,7 @@ class OmniEngine(Engine):
                 if not self.scheduler.has_work():
                     await self._wake.wait()
                 else:
-                    await asyncio.sleep(0)
+                    await asyncio.sleep(self.poll_s)
                 continue
             try:
                 await self._step(sched_out)
@@ -105,9 +122,14 @@ class OmniEngine(Engine):
                 self.scheduler.fail(sched_out, exc)
 
 
-def _execute_synced(runner, sched_out):
+def _execute_synced(runner, sched_out, stream=None):
     """Runs one batch and waits for its GPU work: its output tensors go to other
     stages, whose threads run on their own streams."""
+    if stream is not None:
+        with torch.cuda.stream(stream):
+            res = runner.execute(sched_out)
+        stream.synchronize()
+        return res
     res = runner.execute(sched_out)
     if torch.cuda.is_available() and torch.cuda.is_initialized():
         torch.cuda.current_stream().synchronize()

@@ -2,6 +2,8 @@
 engines over the generic step engine, AR engines over the paged engine."""
 from __future__ import annotations
 
+import torch
+
 from .engine import OmniEngine
 from .model_runner import ModelRunner
 from .runtime.cache import SimpleCacheManager
@@ -10,11 +12,19 @@ from .runtime.encoder import EncoderBatchPlanner, EncoderInputPreparer, EncoderM
 from .scheduler import Scheduler
 
 
-def create_encoder_engine(encode_fn, max_batch_size: int = 32, device="cpu", cache_size: int = 64) -> OmniEngine:
-    sched = Scheduler(EncoderBatchPlanner(max_batch_size), SimpleResourceManager(max_batch_size * 4),
+def create_encoder_engine(encode_fn, max_batch_size: int = 32, device="cpu", cache_size: int = 64,
+                          gather_window_s: float = 0.008, high_priority: bool = True) -> OmniEngine:
+    """Encoders sit on the time-to-first-token/audio path: a short gathering window
+    batches a burst of arrivals, and their steps run on a high-priority stream so
+    they are not queued behind other stages' decode work on the same GPU."""
+    sched = Scheduler(EncoderBatchPlanner(max_batch_size, gather_window_s), SimpleResourceManager(max_batch_size * 4),
                       SinglePassIterationController())
     runner = ModelRunner(EncoderModelWrapper(encode_fn), EncoderInputPreparer(), EncoderOutputProcessor(), device)
-    return OmniEngine(sched, runner, SimpleCacheManager(cache_size) if cache_size else None)
+    prio = None
+    if high_priority and torch.device(device).type == "cuda" and torch.cuda.is_available():
+        prio = -1   # lower = higher priority; clamped by PyTorch to the device's range
+    return OmniEngine(sched, runner, SimpleCacheManager(cache_size) if cache_size else None,
+                      stream_priority=prio, poll_s=0.001)
 
 
 def create_ar_engine(model, **kw):

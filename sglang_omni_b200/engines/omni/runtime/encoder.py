@@ -5,6 +5,7 @@ model; outputs are split back per request by the recorded row counts
 (sglang_omni/engines/omni/runtime/encoder.py:19-526)."""
 from __future__ import annotations
 
+import time
 from dataclasses import dataclass, field
 from typing import Any
 
@@ -24,10 +25,24 @@ class EncoderRequestData:
 
 
 class EncoderBatchPlanner:
-    def __init__(self, max_batch_size: int = 32):
+    """Up to ``max_batch_size`` waiting requests per step.  With ``gather_window_s``
+    a partial batch waits until its oldest request has waited that long, so a
+    burst of arrivals (requests leaving preprocessing a few ms apart) is encoded
+    as one batch instead of a small batch followed by a large one."""
+
+    def __init__(self, max_batch_size: int = 32, gather_window_s: float = 0.0):
         self.max_batch_size = max_batch_size
+        self.gather_window_s = gather_window_s
+        self._seen: dict[str, float] = {}
 
     def select_requests(self, waiting, running, resources):
+        if self.gather_window_s > 0 and 0 < len(waiting) < self.max_batch_size:
+            now = time.monotonic()
+            first = min(self._seen.setdefault(r.request_id, now) for r in waiting)
+            if now - first < self.gather_window_s:
+                return []
+        for r in waiting[: self.max_batch_size]:
+            self._seen.pop(r.request_id, None)
         out = []
         for r in waiting:
             if len(out) >= self.max_batch_size or not resources.can_allocate(r):

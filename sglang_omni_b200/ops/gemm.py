@@ -10,6 +10,8 @@ sglang_omni/models/qwen3_omni/thinker.py:192-213,402-412.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.nn.functional as F
 
@@ -24,6 +26,7 @@ from ._ext import ext, status_word
 # utils.cuda_graph).  GEMMs needing more than the buffer fall back to no split.
 _SPLITK_FLOATS = 8 * 1024 * 1024
 _SPLITK_COUNTERS = 1024   # per-tile arrival counters of the in-kernel split-K finalisation
+_SPLITK_MODE = int(os.environ.get("OMNI_SPLITK", "2"))  # 2 in-kernel finalise, 1 reduce kernel, 0 off
 _splitk: dict[tuple[int, int], tuple[torch.Tensor, torch.Tensor]] = {}
 
 
@@ -95,6 +98,10 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias=None, residual=None, act=None,
     x2 = x if x.is_contiguous() else x.contiguous()
     rows = x2.numel() // x2.shape[-1]
     ws, ctr = splitk_scratch(x.device)
+    if _SPLITK_MODE != 2:   # 0: no split-K, 1: split-K finalised by a second kernel
+        ctr = None
+        if _SPLITK_MODE == 0:
+            ws = None
     peer, rows_per = scatter if scatter is not None else (None, 0)
     wf, wseq, wt = wait if wait is not None else (None, None, 2.0)
     ext().gemm(w, x2, out, None, n, gated, bias, residual, act_code(act), rows, status_word(x.device), 0, ws, ctr,
