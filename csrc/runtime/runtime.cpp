@@ -7,11 +7,18 @@
 //                     rows, request slots) into a caller-provided pinned buffer,
 //                     allocating a page whenever a request crosses a page edge;
 //  * ShmRing        - single-producer / single-consumer byte ring in POSIX
-//                     shared memory used by the CPU relay between stage processes.
+//                     shared memory used by the CPU relay between stage processes;
+//  * PrefixCache    - page-granular radix tree of cached KV prefixes: each node is
+//                     one full 64-token page, shared by every request whose prompt
+//                     starts with the same token blocks (same namespace), locked
+//                     while a request uses it and evicted leaf-first in LRU order
+//                     when the page allocator runs dry.
 //
 // Reference counterparts: SGLang's token-to-KV pool and ScheduleBatch metadata
 // (used through sglang_omni/engines/ar/sglang_backend/scheduler/*.py) and the
-// POSIX SHM relay (sglang_omni/relay/shm.py:18-169).
+// POSIX SHM relay (sglang_omni/relay/shm.py:18-169); SGLang's RadixCache as the
+// engines create it (sglang_omni/engines/ar/sglang_backend/scheduler/cache.py:9-30,
+// cache_unfinished_req at sglang_omni/engines/omni/runtime/sglang_ar.py:205).
 #include <fcntl.h>
 #include <pybind11/numpy.h>
 #include <pybind11/pybind11.h>
@@ -20,8 +27,11 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstring>
+#include <queue>
+#include <unordered_map>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -198,8 +208,221 @@ class ShmRing {
   uint8_t* base_ = nullptr;
 };
 
+// Radix tree over page-sized token blocks.  The key of a node is
+// (parent node, namespace, the block's token ids); a lookup hashes the key and
+// compares the stored ids, so hash collisions never alias two prefixes.
+// A request that matched a prefix holds one reference on every node of its
+// path (ancestors of a referenced node are therefore always referenced), and
+// a node is evictable once it has no reference and no child.
+class PrefixCache {
+ public:
+  explicit PrefixCache(int block) : block_(block) {
+    if (block <= 0) throw std::invalid_argument("block must be positive");
+    nodes_.push_back(Node{});  // node 0: root (never evicted, holds no page)
+  }
+
+  int block() const { return block_; }
+  int cached_pages() const { return live_; }
+  int evictable_pages() const {
+    int n = 0;
+    for (size_t i = 1; i < nodes_.size(); ++i)
+      if (nodes_[i].alive && nodes_[i].ref == 0) ++n;
+    return n;
+  }
+  uint64_t hits() const { return hit_blocks_; }
+
+  // Longest cached run of full blocks at the start of `tokens` (at most
+  // max_blocks blocks).  Takes a reference on every matched node and returns
+  // (node ids, page ids) in order.
+  py::tuple match(uint64_t ns, py::array_t<int32_t, py::array::c_style> tokens, int max_blocks) {
+    auto t = tokens.unchecked<1>();
+    const int nblk = std::min<int>(max_blocks, static_cast<int>(t.shape(0)) / block_);
+    std::vector<int> path, pages;
+    int cur = 0;
+    const uint64_t now = ++clock_;
+    for (int b = 0; b < nblk; ++b) {
+      const int32_t* blk = t.data(b * block_);
+      const int child = find(cur, ns, blk);
+      if (child < 0) break;
+      path.push_back(child);
+      pages.push_back(nodes_[child].page);
+      cur = child;
+    }
+    for (int n : path) {
+      nodes_[n].ref += 1;
+      nodes_[n].last = now;
+    }
+    hit_blocks_ += path.size();
+    return py::make_tuple(path, pages);
+  }
+
+  // Inserts the full blocks of `tokens` whose KV lives in `pages` (the request's
+  // page list, block i in pages[i]); the first locked.size() blocks are the
+  // nodes the request matched.  Releases the request's references and returns
+  // the pages the caller must free: pages of blocks that another request has
+  // cached in the meantime.  Pages that became tree nodes are owned by the cache.
+  std::vector<int> insert_release(uint64_t ns, py::array_t<int32_t, py::array::c_style> tokens,
+                                  const std::vector<int>& pages, const std::vector<int>& locked) {
+    auto t = tokens.unchecked<1>();
+    const int nblk = std::min<int>(static_cast<int>(t.shape(0)) / block_, static_cast<int>(pages.size()));
+    if (static_cast<int>(locked.size()) > nblk) throw std::invalid_argument("more locked nodes than blocks");
+    std::vector<int> dup;
+    const uint64_t now = ++clock_;
+    int cur = 0;
+    for (int b = 0; b < nblk; ++b) {
+      if (b < static_cast<int>(locked.size())) {
+        cur = locked[b];
+        check_node(cur);
+        if (nodes_[cur].page != pages[b]) throw std::invalid_argument("locked node does not own the request's page");
+        continue;
+      }
+      const int32_t* blk = t.data(b * block_);
+      const int child = find(cur, ns, blk);
+      if (child >= 0) {  // cached by another request: keep the tree's copy
+        dup.push_back(pages[b]);
+        nodes_[child].last = now;
+        cur = child;
+        continue;
+      }
+      cur = add(cur, ns, blk, pages[b], now);
+    }
+    release(locked);
+    return dup;
+  }
+
+  // Drops the request's references without inserting anything.
+  void release(const std::vector<int>& locked) {
+    for (int n : locked) {
+      check_node(n);
+      if (nodes_[n].ref <= 0) throw std::runtime_error("prefix node released more often than matched");
+      nodes_[n].ref -= 1;
+    }
+  }
+
+  // Evicts up to n unreferenced leaves, least recently used first (a parent
+  // that becomes an unreferenced leaf joins the queue); returns their pages.
+  std::vector<int> evict(int n) {
+    using Item = std::pair<uint64_t, int>;
+    std::priority_queue<Item, std::vector<Item>, std::greater<Item>> q;
+    for (size_t i = 1; i < nodes_.size(); ++i) {
+      const Node& x = nodes_[i];
+      if (x.alive && x.ref == 0 && x.children == 0) q.push({x.last, static_cast<int>(i)});
+    }
+    std::vector<int> out;
+    while (static_cast<int>(out.size()) < n && !q.empty()) {
+      const int id = q.top().second;
+      q.pop();
+      Node& x = nodes_[id];
+      if (!x.alive || x.ref != 0 || x.children != 0) continue;
+      out.push_back(x.page);
+      const int parent = x.parent;
+      remove(id);
+      if (parent > 0) {
+        const Node& p = nodes_[parent];
+        if (p.alive && p.ref == 0 && p.children == 0) q.push({p.last, parent});
+      }
+    }
+    return out;
+  }
+
+  // Evicts every unreferenced node; returns their pages.
+  std::vector<int> clear() { return evict(static_cast<int>(nodes_.size())); }
+
+ private:
+  struct Node {
+    int parent = -1;
+    int page = -1;
+    int ref = 0;
+    int children = 0;
+    uint64_t ns = 0;
+    uint64_t key = 0;
+    uint64_t last = 0;
+    bool alive = true;
+    std::vector<int32_t> toks;
+  };
+
+  uint64_t key_of(int parent, uint64_t ns, const int32_t* blk) const {
+    // FNV-1a over the parent id, the namespace and the block's token ids.
+    uint64_t h = 1469598103934665603ull;
+    auto mix = [&h](uint64_t v) {
+      for (int i = 0; i < 8; ++i) {
+        h ^= (v >> (8 * i)) & 0xffu;
+        h *= 1099511628211ull;
+      }
+    };
+    mix(static_cast<uint64_t>(parent));
+    mix(ns);
+    for (int i = 0; i < block_; ++i) mix(static_cast<uint32_t>(blk[i]));
+    return h;
+  }
+
+  int find(int parent, uint64_t ns, const int32_t* blk) const {
+    auto it = index_.find(key_of(parent, ns, blk));
+    if (it == index_.end()) return -1;
+    for (int id : it->second) {
+      const Node& x = nodes_[id];
+      if (x.alive && x.parent == parent && x.ns == ns &&
+          std::equal(x.toks.begin(), x.toks.end(), blk))
+        return id;
+    }
+    return -1;
+  }
+
+  int add(int parent, uint64_t ns, const int32_t* blk, int page, uint64_t now) {
+    int id;
+    if (!free_ids_.empty()) {
+      id = free_ids_.back();
+      free_ids_.pop_back();
+    } else {
+      id = static_cast<int>(nodes_.size());
+      nodes_.push_back(Node{});
+    }
+    Node& x = nodes_[id];
+    x = Node{};
+    x.parent = parent;
+    x.page = page;
+    x.ns = ns;
+    x.key = key_of(parent, ns, blk);
+    x.last = now;
+    x.toks.assign(blk, blk + block_);
+    index_[x.key].push_back(id);
+    nodes_[parent].children += 1;
+    live_ += 1;
+    return id;
+  }
+
+  void remove(int id) {
+    Node& x = nodes_[id];
+    auto it = index_.find(x.key);
+    if (it != index_.end()) {
+      auto& v = it->second;
+      v.erase(std::remove(v.begin(), v.end(), id), v.end());
+      if (v.empty()) index_.erase(it);
+    }
+    nodes_[x.parent].children -= 1;
+    x.alive = false;
+    x.toks.clear();
+    x.toks.shrink_to_fit();
+    free_ids_.push_back(id);
+    live_ -= 1;
+  }
+
+  void check_node(int id) const {
+    if (id <= 0 || id >= static_cast<int>(nodes_.size()) || !nodes_[id].alive)
+      throw std::out_of_range("bad prefix node id");
+  }
+
+  int block_;
+  int live_ = 0;
+  uint64_t clock_ = 0;
+  uint64_t hit_blocks_ = 0;
+  std::vector<Node> nodes_;
+  std::vector<int> free_ids_;
+  std::unordered_map<uint64_t, std::vector<int>> index_;
+};
+
 PYBIND11_MODULE(_runtime, m) {
-  m.doc() = "host runtime of sglang_omni_b200 (page allocator, decode metadata, shm ring)";
+  m.doc() = "host runtime of sglang_omni_b200 (page allocator, decode metadata, shm ring, prefix cache)";
   py::class_<PageAllocator>(m, "PageAllocator")
       .def(py::init<int, int>(), py::arg("num_pages"), py::arg("reserved") = 1)
       .def("num_free", &PageAllocator::num_free)
@@ -218,4 +441,16 @@ PYBIND11_MODULE(_runtime, m) {
       .def("readable", &ShmRing::readable)
       .def("put", &ShmRing::put)
       .def("get", &ShmRing::get);
+  py::class_<PrefixCache>(m, "PrefixCache")
+      .def(py::init<int>(), py::arg("block") = 64)
+      .def("block", &PrefixCache::block)
+      .def("cached_pages", &PrefixCache::cached_pages)
+      .def("evictable_pages", &PrefixCache::evictable_pages)
+      .def("hits", &PrefixCache::hits)
+      .def("match", &PrefixCache::match, py::arg("ns"), py::arg("tokens"), py::arg("max_blocks"))
+      .def("insert_release", &PrefixCache::insert_release, py::arg("ns"), py::arg("tokens"), py::arg("pages"),
+           py::arg("locked"))
+      .def("release", &PrefixCache::release)
+      .def("evict", &PrefixCache::evict)
+      .def("clear", &PrefixCache::clear);
 }

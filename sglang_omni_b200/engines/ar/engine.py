@@ -2,6 +2,15 @@
 retraction, overlap scheduling (the host plans and launches step N+1 before
 it reads step N's tokens), CUDA-graph decode.
 
+With ``prefix_cache=True`` finished requests leave their full KV pages in a
+page-granular radix tree (``KVPool.enable_prefix_cache``); a later request
+whose token prompt starts with the same pages skips their prefill.  Only
+requests whose KV is a function of their token ids alone take part (no
+embedding overrides, multimodal rows, deep-stack inputs, shifted M-RoPE
+positions or captured prompt hidden states); ``extra["prefix_key"]`` puts a
+request into a namespace of its own (e.g. one per LoRA or speaker) and
+``extra["no_prefix_cache"]`` opts it out.
+
 ``AREngine.step()`` is the synchronous core used by benchmarks and tests;
 ``ThreadedAREngine`` runs the same loop on a dedicated thread and exposes the
 engine contract used by the pipeline executors (add_request / stream /
@@ -12,7 +21,8 @@ Reference counterparts: OmniEngine normal / overlap step loop
 selection and post-step filtering (sglang_omni/engines/omni/runtime/sglang_ar.py:40-300),
 PrefillManager / DecodeManager retraction
 (sglang_omni/engines/ar/sglang_backend/scheduler/prefill.py:13-80,
-sglang_omni/engines/ar/sglang_backend/scheduler/decode.py:14-78).
+sglang_omni/engines/ar/sglang_backend/scheduler/decode.py:14-78), radix tree
+cache (sglang_omni/engines/ar/sglang_backend/scheduler/cache.py:9-30).
 """
 from __future__ import annotations
 
@@ -22,10 +32,11 @@ import threading
 import time
 from collections import deque
 
+import numpy as np
 import torch
 
 from ...utils.hostdev import own_stream
-from .kv_pool import KVPool
+from .kv_pool import PAGE, KVPool
 from .request import ARRequest
 from .runner import ARModelRunner
 
@@ -35,8 +46,10 @@ log = logging.getLogger(__name__)
 class AREngine:
     def __init__(self, model, pool: KVPool, max_batch: int = 64, max_prefill_tokens: int = 8192,
                  max_context: int = 8192, use_graphs: bool = True, overlap: bool = True, eos_token_ids=(),
-                 suppress=(-1, -1, -1), track_seen: bool = False, max_slots: int | None = None):
+                 suppress=(-1, -1, -1), track_seen: bool = False, max_slots: int | None = None,
+                 prefix_cache: bool = False):
         self.pool = pool
+        self.prefix_cache = pool.enable_prefix_cache() if prefix_cache else pool.prefix_cache
         self.max_batch = max_batch
         self.max_prefill_tokens = max_prefill_tokens
         self.max_context = max_context
@@ -53,6 +66,7 @@ class AREngine:
         self._finished_buf: list[ARRequest] = []
         self.num_steps = 0
         self.num_retractions = 0
+        self.num_prefix_hit_tokens = 0
 
     # ------------------------------------------------------------------ API
     def add_request(self, req: ARRequest):
@@ -76,6 +90,56 @@ class AREngine:
     def has_work(self) -> bool:
         return bool(self.waiting or self.prefilling or self.running or self.pending)
 
+    # ------------------------------------------------------------------ prefix cache
+    @staticmethod
+    def _cacheable(r: ARRequest) -> bool:
+        if (r.input_embeds is not None or r.mm_index is not None or r.deepstack is not None
+                or r.capture_prompt_layer is not None or r.extra.get("no_prefix_cache")):
+            return False
+        if r.mrope_positions is not None:  # text-only layouts have plain positions and no delta
+            n = r.mrope_positions.shape[1]
+            return r.mrope_delta == 0 and n > 0 and int(r.mrope_positions[0, n - 1]) == n - 1
+        return True
+
+    @staticmethod
+    def _namespace(r: ARRequest) -> int:
+        key = r.extra.get("prefix_key")
+        return 0 if key is None else hash(key) & 0xFFFFFFFFFFFFFFFF
+
+    def _match_prefix(self, r: ARRequest):
+        """Reuses the cached full pages at the start of r's prompt; at least the
+        last prompt token is always recomputed (its logits start the decode)."""
+        max_blocks = (r.prompt_len - 1) // PAGE
+        if max_blocks <= 0:
+            return
+        seq = np.asarray(r.prefill_ids(0, max_blocks * PAGE), dtype=np.int32)
+        nodes, pages = self.prefix_cache.match(self._namespace(r), seq, max_blocks)
+        if nodes:
+            r.prefix_nodes = list(nodes)
+            r.pages = list(pages)
+            r.num_cached = len(pages) * PAGE
+            r.cached_tokens = max(r.cached_tokens, r.num_cached)
+            self.num_prefix_hit_tokens += r.num_cached
+
+    def _release_kv(self, r: ARRequest, keep: bool):
+        """Returns r's pages: with ``keep`` its full pages join the prefix cache
+        (their KV is final: every position < num_cached has been written, in
+        stream order before any later reader), the rest go back to the pool."""
+        pc = self.prefix_cache
+        if pc is None:
+            self.pool.free(r.pages)
+        elif keep and self._cacheable(r):
+            seq_len = min(r.num_cached, len(r.prompt_ids) + len(r.output_ids))
+            nblk = min(seq_len // PAGE, len(r.pages))
+            seq = np.asarray((list(r.prompt_ids) + list(r.output_ids))[:nblk * PAGE], dtype=np.int32)
+            dup = pc.insert_release(self._namespace(r), seq, list(r.pages[:nblk]), r.prefix_nodes)
+            self.pool.free(list(dup) + list(r.pages[nblk:]))
+        else:
+            pc.release(r.prefix_nodes)
+            self.pool.free(r.pages[len(r.prefix_nodes):])
+        r.pages = []
+        r.prefix_nodes = []
+
     # ------------------------------------------------------------------ scheduling
     def _tokens_in_flight(self, r: ARRequest) -> int:
         return r.folded + (1 if r.prefill_done else 0) + r.scheduled_decodes
@@ -91,6 +155,8 @@ class AREngine:
             new = r.slot < 0
             if new and active >= self.max_batch:
                 break
+            if new and self.prefix_cache is not None and r.num_cached == 0 and not r.pages and self._cacheable(r):
+                self._match_prefix(r)
             remaining = r.prompt_len - r.num_cached
             n = min(remaining, budget)
             if n <= 0:
@@ -128,8 +194,7 @@ class AREngine:
             return False
         victim = max(self.running, key=lambda r: r.arrival)
         self.running.remove(victim)
-        self.pool.free(victim.pages)
-        victim.pages = []
+        self._release_kv(victim, keep=True)  # its re-prefill can match its own pages if they survive
         # recompute later: the generated tokens are re-prefilled after the prompt
         victim.folded = len(victim.output_ids)
         victim.num_cached = 0
@@ -144,7 +209,7 @@ class AREngine:
                  if not r.finished and self._tokens_in_flight(r) < r.max_new_tokens][: self.max_batch]
         while batch:
             need = sum(1 for r in batch if r.num_cached % 64 == 0 and r.num_cached // 64 >= len(r.pages))
-            if self.pool.can_alloc(need):
+            if self.pool.ensure_free(need):  # the decode metadata builder allocates from the free list
                 break
             if not self._retract_one():
                 raise RuntimeError("KV pool exhausted and nothing to retract")
@@ -209,8 +274,7 @@ class AREngine:
                 lst.remove(r)
         if r in self.waiting:
             self.waiting.remove(r)
-        self.pool.free(r.pages)
-        r.pages = []
+        self._release_kv(r, keep=not r.aborted)
         self.runner.release_slot(r)
 
     def run_until_idle(self, max_steps: int = 10_000_000) -> None:

@@ -4,6 +4,12 @@ Page 0 is reserved as the padding page of CUDA-graph decode buckets.
 The allocator is the native ``_runtime.PageAllocator`` when built, else a
 Python free list with the same interface.
 
+With ``enable_prefix_cache()`` the pool also keeps a page-granular radix
+tree of finished requests' KV (``_runtime.PrefixCache``): a new request whose
+prompt starts with cached full pages reuses them instead of recomputing
+them, and cached pages that no request references are evicted (LRU, leaves
+first) whenever an allocation would otherwise fail.
+
 Reference counterpart: SGLang's token-to-KV pool behind
 sglang_omni/engines/ar/sglang_backend/model_worker.py (mem_fraction_static
 sizing, sglang_omni/engines/ar/sglang_backend/server_args_builder.py:10-35).
@@ -56,6 +62,14 @@ class KVPool:
         self.num_pages = num_pages
         self.kv = torch.zeros(num_layers, 2, num_pages, num_kv_heads, PAGE, head_dim, dtype=dtype, device=self.device)
         self._alloc = _rt.PageAllocator(num_pages, 1) if _rt is not None else _PyAllocator(num_pages, 1)
+        self.prefix_cache = None
+
+    def enable_prefix_cache(self):
+        if _rt is None:
+            raise RuntimeError("the prefix cache needs the native _runtime extension")
+        if self.prefix_cache is None:
+            self.prefix_cache = _rt.PrefixCache(PAGE)
+        return self.prefix_cache
 
     @classmethod
     def for_memory(cls, num_layers, num_kv_heads, head_dim, bytes_budget: int, device, dtype=torch.bfloat16,
@@ -74,9 +88,21 @@ class KVPool:
         return self._alloc.num_free()
 
     def can_alloc(self, n: int) -> bool:
+        if self._alloc.can_alloc(n):
+            return True
+        pc = self.prefix_cache
+        return pc is not None and self._alloc.num_free() + pc.evictable_pages() >= n
+
+    def ensure_free(self, n: int) -> bool:
+        """Makes at least n pages free in the allocator itself (evicting cached
+        prefixes if needed), for callers that allocate through it directly."""
+        short = n - self._alloc.num_free()
+        if short > 0 and self.prefix_cache is not None:
+            self._alloc.free(self.prefix_cache.evict(short))
         return self._alloc.can_alloc(n)
 
     def alloc(self, n: int) -> list[int]:
+        self.ensure_free(n)
         return list(self._alloc.alloc(n))
 
     def free(self, pages: list[int]):

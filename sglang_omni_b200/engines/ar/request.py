@@ -42,6 +42,8 @@ class ARRequest:
     finish_time: float | None = None
     scheduled_decodes: int = 0   # decode steps launched since the last (re)prefill
     folded: int = 0              # generated tokens re-prefilled after a KV retraction
+    prefix_nodes: list = field(default_factory=list)  # prefix-cache nodes this request holds (pages[:n])
+    cached_tokens: int = 0       # prompt tokens served from the prefix cache
 
     @property
     def prompt_len(self) -> int:

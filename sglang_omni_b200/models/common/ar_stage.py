@@ -40,14 +40,14 @@ def prompt_ids_of(data: Any) -> list[int]:
 
 def create_ar_executor(model, stage_name: str, tokenizer, max_batch: int = 64, max_context: int = 4096,
                        max_prefill_tokens: int = 8192, kv_pages: int | None = None, use_graphs: bool = True,
-                       eos_token_ids=(), default_max_new_tokens: int = 128) -> EngineExecutor:
+                       eos_token_ids=(), default_max_new_tokens: int = 128, prefix_cache: bool = True) -> EngineExecutor:
     cfg = model.cfg
     dev = model.embed.device
     pages = kv_pages or (max_batch * ((max_context + 63) // 64) + 8)
     pool = KVPool(cfg.num_layers, cfg.num_kv_heads, cfg.head_dim, pages, dev, cfg.dtype)
     engine = AREngine(model, pool, max_batch=max_batch, max_prefill_tokens=max_prefill_tokens,
                       max_context=max_context, use_graphs=use_graphs and dev.type == "cuda",
-                      eos_token_ids=eos_token_ids)
+                      eos_token_ids=eos_token_ids, prefix_cache=prefix_cache)
     adapter = PagedAREngineAdapter(engine)
     detoks: dict[str, IncrementalDetokenizer] = {}
 

@@ -209,7 +209,7 @@ def create_aggregate_executor(**_):
 def create_thinker_executor(model_path: str = "", device: str = "cuda:0", max_batch: int = 64,
                             max_context: int = 4096, max_prefill_tokens: int = 8192, speech_target: str | None = None,
                             accept_hidden_layer: int = 24, overrides: dict | None = None, use_graphs: bool = True,
-                            model=None, tokenizer=None, eos_token_ids=THINKER_EOS_IDS):
+                            model=None, tokenizer=None, eos_token_ids=THINKER_EOS_IDS, prefix_cache: bool = True):
     """The thinker stage over the paged engine; ``model`` / ``tokenizer`` / ``eos_token_ids``
     let another omni model (same request layout: prompt ids + audio / image spans) reuse it."""
     dev = torch.device(device)
@@ -220,7 +220,7 @@ def create_thinker_executor(model_path: str = "", device: str = "cuda:0", max_ba
     pool = KVPool(cfg.num_layers, cfg.num_kv_heads, cfg.head_dim, pages, dev, cfg.dtype)
     engine = AREngine(model, pool, max_batch=max_batch, max_prefill_tokens=max_prefill_tokens,
                       max_context=max_context, use_graphs=use_graphs and dev.type == "cuda",
-                      eos_token_ids=eos_token_ids)
+                      eos_token_ids=eos_token_ids, prefix_cache=prefix_cache)
     adapter = PagedAREngineAdapter(engine)
     detoks: dict[str, IncrementalDetokenizer] = {}
     accept = min(accept_hidden_layer, cfg.num_layers)
