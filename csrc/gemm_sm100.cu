@@ -49,7 +49,9 @@ struct DevParams {
   int act;
   int* status;
   int k_splits;          // > 1: split-K over K blocks with an fp32 workspace
-  float* ws;             // [splits][tiles][128][BN] fp32 partial sums (each split owns its plane)
+  float* ws;             // [splits][tiles][BN][128] fp32 partial sums (each split owns its plane;
+                         // token-major inside a tile, so stores and the finaliser's reads coalesce)
+  int vec4;              // outputs / bias / residual allow 4-wide vector access (split-K finaliser)
   int* counters;         // [tiles] arrival counters, zero between calls
   const unsigned long long* peer_out;  // owner scatter: row r -> peer_out[r / rows_per] + r * ldo
   int rows_per;
@@ -65,11 +67,60 @@ __device__ __forceinline__ __nv_bfloat16* out_row_bf16(const DevParams& p, int r
   return static_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.ldo;
 }
 
-__device__ __forceinline__ float epilogue_act(float v, int act) {
+// The activations live out of line: inlined into every unrolled epilogue store
+// they made the kernel's code large enough that instruction fetch, not memory,
+// bounded the small decode GEMMs.
+__device__ __noinline__ float act_apply(float v, int act) {
   if (act == kActGeluTanh) return gelu_tanh_f(v);
   if (act == kActGeluErf) return gelu_erf_f(v);
   if (act == kActSilu) return silu_f(v);
   return v;
+}
+
+__device__ __forceinline__ float epilogue_act(float v, int act) { return act == kActNone ? v : act_apply(v, act); }
+
+// Split-K finaliser store of four consecutive outputs (m .. m+3) of one token row:
+// bias, activation, residual, bf16 / fp32 store (8 / 16-byte vectors when p.vec4).
+__device__ __noinline__ void store_out4(const __nv_bfloat16* __restrict__ bias, const __nv_bfloat16* __restrict__ residual,
+                                        int64_t ldr, void* out_row, int out_f32, int act, int m, int m_out, int vec4,
+                                        int64_t row, float4 v4) {
+  float v[4] = {v4.x, v4.y, v4.z, v4.w};
+  if (vec4 && m + 3 < m_out) {
+    if (bias != nullptr) {
+      const uint2 b = *reinterpret_cast<const uint2*>(bias + m);
+      const __nv_bfloat162 b01 = *reinterpret_cast<const __nv_bfloat162*>(&b.x);
+      const __nv_bfloat162 b23 = *reinterpret_cast<const __nv_bfloat162*>(&b.y);
+      v[0] += __low2float(b01); v[1] += __high2float(b01); v[2] += __low2float(b23); v[3] += __high2float(b23);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = epilogue_act(v[j], act);
+    if (residual != nullptr) {
+      const uint2 r = *reinterpret_cast<const uint2*>(residual + row * ldr + m);
+      const __nv_bfloat162 r01 = *reinterpret_cast<const __nv_bfloat162*>(&r.x);
+      const __nv_bfloat162 r23 = *reinterpret_cast<const __nv_bfloat162*>(&r.y);
+      v[0] += __low2float(r01); v[1] += __high2float(r01); v[2] += __low2float(r23); v[3] += __high2float(r23);
+    }
+    if (out_f32) {
+      *reinterpret_cast<float4*>(static_cast<float*>(out_row) + m) = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+      const __nv_bfloat162 o01 = __floats2bfloat162_rn(v[0], v[1]);
+      const __nv_bfloat162 o23 = __floats2bfloat162_rn(v[2], v[3]);
+      uint2 o;
+      o.x = *reinterpret_cast<const uint32_t*>(&o01);
+      o.y = *reinterpret_cast<const uint32_t*>(&o23);
+      *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(out_row) + m) = o;
+    }
+    return;
+  }
+  for (int j = 0; j < 4; ++j) {
+    if (m + j >= m_out) break;
+    float x = v[j];
+    if (bias != nullptr) x += __bfloat162float(bias[m + j]);
+    x = epilogue_act(x, act);
+    if (residual != nullptr) x += __bfloat162float(residual[row * ldr + m + j]);
+    if (out_f32) static_cast<float*>(out_row)[m + j] = x;
+    else static_cast<__nv_bfloat16*>(out_row)[m + j] = __float2bfloat16(x);
+  }
 }
 
 template <int BN, bool GATED>
@@ -318,15 +369,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (GATED) tmem_ld_32x32b_x16(t_base + BN + c, u);
         tmem_ld_wait();
         if (ks > 1) {
-          // split-K partial into this split's plane [split][t][128][BN] (thread = one A row,
-          // 16 consecutive tokens = four 16-byte stores); summed in split order by the finaliser,
-          // so the result does not depend on which split arrives first
-          float4* wsp = reinterpret_cast<float4*>(
-              p.ws + ((static_cast<int64_t>(w - t * ks) * total_tiles + t) * kBM + lane_base + lane) * BN + c);
+          // split-K partial into this split's plane [split][t][BN][128] (thread = one A row; for
+          // each token a warp stores 32 consecutive floats); summed in split order by the
+          // finaliser, so the result does not depend on which split arrives first
+          float* wsp = p.ws + ((static_cast<int64_t>(w - t * ks) * total_tiles + t) * BN + c) * kBM + lane_base + lane;
 #pragma unroll
-          for (int j = 0; j < 16; j += 4)
-            __stcg(wsp + j / 4, make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                                            __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3])));
+          for (int j = 0; j < 16; ++j) __stcg(wsp + j * kBM, __uint_as_float(r[j]));
         } else if (m_ok) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
@@ -366,43 +414,50 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (s_last) {
           __threadfence();
-          // sum the split planes in split order, two splits per round (up to 32 16-byte loads in flight)
-          constexpr int kChunk = BN < 64 ? BN : 64;
-          const int64_t plane4 = static_cast<int64_t>(total_tiles) * kBM * BN / 4;
-          const float4* wsp = reinterpret_cast<const float4*>(p.ws + (static_cast<int64_t>(t) * kBM + lane_base + lane) * BN);
+          // Sum the split planes of tile t in split order: the 128 epilogue threads sweep the
+          // [BN][128] tile as float4s (coalesced), 8 per thread per round, every split's loads
+          // of a round in flight together; the epilogue stores four outputs per float4.
+          constexpr int kU = 8;
+          constexpr int kN4 = BN * kBM / 4;
+          const int tid = threadIdx.x - 64;
+          const int64_t plane4 = static_cast<int64_t>(total_tiles) * BN * kBM / 4;
+          const float4* base4 = reinterpret_cast<const float4*>(p.ws + static_cast<int64_t>(t) * BN * kBM);
 #pragma unroll 1
-          for (int c = 0; c < BN; c += kChunk) {
-            float4 v4[kChunk / 4];
+          for (int e0 = tid; e0 < kN4; e0 += 128 * kU) {
+            float4 acc[kU];
 #pragma unroll
-            for (int q = 0; q < kChunk / 4; ++q) v4[q] = __ldcg(wsp + c / 4 + q);
+            for (int u = 0; u < kU; ++u) {
+              const int e = e0 + u * 128;
+              acc[u] = e < kN4 ? __ldcg(base4 + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
 #pragma unroll 1
-            for (int sp = 1; sp < ks; sp += 2) {
-              float4 x0[kChunk / 4], x1[kChunk / 4];
-              const bool two = sp + 1 < ks;
+            for (int sp = 1; sp < ks; ++sp) {
+              float4 x[kU];
 #pragma unroll
-              for (int q = 0; q < kChunk / 4; ++q) {
-                x0[q] = __ldcg(wsp + sp * plane4 + c / 4 + q);
-                x1[q] = two ? __ldcg(wsp + (sp + 1) * plane4 + c / 4 + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+              for (int u = 0; u < kU; ++u) {
+                const int e = e0 + u * 128;
+                x[u] = e < kN4 ? __ldcg(base4 + sp * plane4 + e) : make_float4(0.f, 0.f, 0.f, 0.f);
               }
 #pragma unroll
-              for (int q = 0; q < kChunk / 4; ++q) {
-                v4[q].x = (v4[q].x + x0[q].x) + x1[q].x;
-                v4[q].y = (v4[q].y + x0[q].y) + x1[q].y;
-                v4[q].z = (v4[q].z + x0[q].z) + x1[q].z;
-                v4[q].w = (v4[q].w + x0[q].w) + x1[q].w;
+              for (int u = 0; u < kU; ++u) {
+                acc[u].x += x[u].x;
+                acc[u].y += x[u].y;
+                acc[u].z += x[u].z;
+                acc[u].w += x[u].w;
               }
             }
-            if (m_ok) {
-              const float* vf = reinterpret_cast<const float*>(v4);
 #pragma unroll
-              for (int j = 0; j < kChunk; ++j) {
-                const int row = row0 + c + j;
-                if (row < row_end) {
-                  float v = epilogue_act(vf[j] + bias_v, p.act);
-                  if (p.residual != nullptr) v += __bfloat162float(p.residual[static_cast<int64_t>(row) * p.ldr + m]);
-                  if (p.out_f32) static_cast<float*>(p.out)[static_cast<int64_t>(row) * p.ldo + m] = v;
-                  else out_row_bf16(p, row)[m] = __float2bfloat16(v);
-                }
+            for (int u = 0; u < kU; ++u) {
+              const int e = e0 + u * 128;
+              if (e >= kN4) break;
+              const int tok = e / (kBM / 4);
+              const int mm = mt * kBM + (e - tok * (kBM / 4)) * 4;
+              const int row = row0 + tok;
+              if (row < row_end && mm < p.m_out) {
+                void* orow = p.out_f32 ? static_cast<void*>(static_cast<float*>(p.out) + static_cast<int64_t>(row) * p.ldo)
+                                       : static_cast<void*>(out_row_bf16(p, row));
+                store_out4(p.bias == nullptr ? nullptr : p.bias + static_cast<int64_t>(g) * p.m_out, p.residual, p.ldr,
+                           orow, p.out_f32, p.act, mm, p.m_out, p.vec4, row, acc[u]);
               }
             }
           }
@@ -420,7 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // Fallback finaliser (more tiles than arrival counters): sums the split planes
-// [splits][tiles][128][BN] in split order and applies the epilogue.
+// [splits][tiles][BN][128] in split order and applies the epilogue.
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int ks, int bn, int n_tiles, int total_tiles,
                                      int rows, int m_out, void* out, int64_t ldo, int out_f32,
                                      const __nv_bfloat16* __restrict__ bias,
@@ -432,7 +487,7 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int ks, int b
     const int row = static_cast<int>(i / m_out);
     const int m = static_cast<int>(i - static_cast<int64_t>(row) * m_out);
     const int t = (m / kBM) * n_tiles + row / bn;
-    const float* src = ws + (static_cast<int64_t>(t) * kBM + m % kBM) * bn + row % bn;
+    const float* src = ws + (static_cast<int64_t>(t) * bn + row % bn) * kBM + m % kBM;
     float v = 0.f;
     for (int s = 0; s < ks; ++s) v += __ldcg(src + s * plane);
     if (bias != nullptr) v += __bfloat162float(bias[m]);
@@ -516,6 +571,12 @@ cudaError_t launch(const GemmArgs& a, cudaStream_t stream) {
   p.status = a.status;
   p.k_splits = 1;
   p.ws = nullptr;
+  {
+    auto al = [](const void* q, int bytes) { return (reinterpret_cast<uintptr_t>(q) % bytes) == 0; };
+    const int ob = a.out_f32 ? 16 : 8;
+    p.vec4 = (a.m_out % 4 == 0) && (a.ldo % 4 == 0) && al(a.out, ob) && (a.bias == nullptr || al(a.bias, 8)) &&
+             (a.residual == nullptr || (a.ldr % 4 == 0 && al(a.residual, 8))) ? 1 : 0;
+  }
   p.counters = nullptr;
   p.peer_out = a.peer_out;
   p.rows_per = a.rows_per > 0 ? a.rows_per : 1;

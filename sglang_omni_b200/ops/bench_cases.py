@@ -75,6 +75,8 @@ def _time_cases() -> None:
         for _ in range(n):
             flush.zero_()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            # keep the GPU busy while the host enqueues fn, so the events time the device only
+            torch.cuda._sleep(200_000)
             a.record()
             fn()
             b.record()

@@ -100,3 +100,26 @@ def test_splitk_dense_repeated(rows, n, k):
     y2 = L.linear(x, w, bias=b, residual=r)
     _close(y1, ref)
     _close(y2, ref)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("mode", [1, 2])
+@pytest.mark.parametrize("rows,n,k,act,f32", [(64, 5120, 2048, None, False), (64, 130, 2048, "gelu", False),
+                                              (16, 2048, 4096, "silu", False), (33, 128, 2048, None, True),
+                                              (64, 516, 1024, "gelu_tanh", True)])
+def test_splitk_finalisers(monkeypatch, mode, rows, n, k, act, f32):
+    """Both split-K finalisers (second kernel / last split in the GEMM) against the fp32 oracle,
+    with bias, activation and residual, bf16 and fp32 outputs, and output widths that are not a
+    multiple of the 4-wide vector stores; two calls in a row must agree bit for bit."""
+    monkeypatch.setattr(L, "_SPLITK_MODE", mode)
+    torch.manual_seed(rows + n + mode)
+    x = torch.randn(rows, k, device="cuda").bfloat16()
+    w = (torch.randn(n, k, device="cuda") * 0.02).bfloat16()
+    b = torch.randn(n, device="cuda").bfloat16()
+    r = None if f32 else torch.randn(rows, n, device="cuda").bfloat16()
+    dt = torch.float32 if f32 else None
+    ref = L.linear_ref(x, w, b, r, act, torch.float32)
+    y1 = L.linear(x, w, bias=b, residual=r, act=act, out_dtype=dt)
+    y2 = L.linear(x, w, bias=b, residual=r, act=act, out_dtype=dt)
+    _close(y1, ref, 1e-2 if f32 else 2e-2)
+    assert torch.equal(y1, y2)
