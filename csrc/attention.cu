@@ -16,6 +16,7 @@
 #include <stdint.h>
 
 #include "omni_kernels.h"
+#include "pdl.cuh"
 
 namespace omni {
 namespace {
@@ -118,6 +119,7 @@ struct PrefillParams {
 
 template <int D>
 __global__ void __launch_bounds__(128) prefill_kernel(const PrefillParams p) {
+  grid_dep_launch();  // a dependent GEMM may start its prologue now
   using T = Tile<D>;
   constexpr int KS = D / 16;  // k-steps over head dim
   constexpr int NJ = D / 8;   // output n-tiles
@@ -342,6 +344,7 @@ struct DecodeParams {
 
 template <int D>
 __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
+  grid_dep_launch();  // a dependent GEMM may start its prologue now
   using T = Tile<D>;
   constexpr int KS = D / 16;
   constexpr int NJ = D / 8;
@@ -602,6 +605,7 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
 
 template <int D>
 __global__ void decode_combine_kernel(const DecodeParams p) {
+  grid_dep_launch();  // a dependent GEMM may start its prologue now
   const int head = blockIdx.x, b = blockIdx.y;
   const int kv_len = p.kv_lens[b];
   const int kps = split_keys(kv_len, p.keys_per_split, p.max_splits);

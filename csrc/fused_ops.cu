@@ -18,6 +18,7 @@
 #include <stdint.h>
 
 #include "omni_kernels.h"
+#include "pdl.cuh"
 
 namespace omni {
 namespace {
@@ -68,6 +69,7 @@ __device__ __forceinline__ int mrope_section(int j, const int* sec, int interlea
 
 template <int D>
 __global__ void __launch_bounds__(256) qkv_rope_store_kernel(RopeStoreArgs a) {
+  grid_dep_launch();  // a dependent GEMM may start its prologue now
   constexpr int PER = D / 32;  // elements per lane
   __shared__ float rope_row[8 * D];  // one row per warp (neox with half % 32 != 0)
   const int warp_global = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -174,6 +176,7 @@ __global__ void __launch_bounds__(256) qkv_rope_store_kernel(RopeStoreArgs a) {
 // One warp per token.  E <= 512 (E/32 values per lane).
 template <int PER>
 __global__ void moe_topk_kernel(MoeRouteArgs a) {
+  grid_dep_launch();  // a dependent GEMM may start its prologue now
   const int tok = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (tok >= a.tokens) return;
@@ -330,6 +333,7 @@ __global__ void moe_topk_kernel(MoeRouteArgs a) {
 
 // Offsets (exclusive scan of counts, computed by every CTA) + permutation + row gather.
 __global__ void moe_scatter_kernel(MoeRouteArgs a) {
+  grid_dep_launch();  // a dependent GEMM may start its prologue now
   extern __shared__ int s_off[];
   // exclusive scan of the expert histogram by warp 0 (32 experts per round)
   if (threadIdx.x < 32) {
@@ -399,6 +403,7 @@ __global__ void moe_scatter_kernel(MoeRouteArgs a) {
 // One CTA of 256 threads per token, VPT 16-byte vectors per thread.
 template <int VPT>
 __global__ void __launch_bounds__(256) moe_combine_kernel(MoeCombineArgs a) {
+  grid_dep_launch();  // a dependent GEMM may start its prologue now
   __shared__ int s_pos[16];
   __shared__ float s_w[16];
   __shared__ float red[8];
@@ -483,6 +488,7 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(MoeCombineArgs a) {
 // Embedding gather with multimodal overwrite
 // ---------------------------------------------------------------------------
 __global__ void embed_kernel(EmbedArgs a) {
+  grid_dep_launch();  // a dependent GEMM may start its prologue now
   const int tok = blockIdx.x;
   const int mm = a.mm_index ? a.mm_index[tok] : -1;
   const uint4* src;

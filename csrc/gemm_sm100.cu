@@ -14,12 +14,19 @@
 // Accumulators are double buffered in TMEM so the epilogue of tile i overlaps
 // the MMAs of tile i+1.
 //
+// Launched as a programmatic dependent launch: the prologue (barriers, TMEM,
+// tensor-map prefetch) and, for dense GEMMs, the first stages' weight tiles run
+// while the previous kernel of the stream finishes; every read of activations,
+// group offsets or residuals and every store comes after grid_dep_wait().
+//
 // Reference counterparts: SGLang QKVParallelLinear / RowParallelLinear /
 // FusedMoE as used by sglang_omni/models/qwen3_omni/thinker.py:192-213,402-412
 // and the talker's native MoE (sglang_omni/models/qwen3_omni/talker.py:242-247).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "omni_kernels.h"
@@ -52,6 +59,7 @@ struct DevParams {
   float* ws;             // [splits][tiles][BN][128] fp32 partial sums (each split owns its plane;
                          // token-major inside a tile, so stores and the finaliser's reads coalesce)
   int vec4;              // outputs / bias / residual allow 4-wide vector access (split-K finaliser)
+  int pdl_prefetch_a;    // programmatic dependent launch with static weights: prefetch them before the wait
   int* counters;         // [tiles] arrival counters, zero between calls
   const unsigned long long* peer_out;  // owner scatter: row r -> peer_out[r / rows_per] + r * ldo
   int rows_per;
@@ -159,7 +167,9 @@ __device__ __forceinline__ void decode_tile(int t, const int* prefix, const int*
   nt = local - mt * ntiles;
 }
 
-template <int BN, bool GATED>
+// ACT = false: the epilogue has no activation code at all (the common case; a
+// smaller kernel is fetched faster, which the few-tile decode GEMMs feel).
+template <int BN, bool GATED, bool ACT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                      const DevParams p) {
@@ -201,8 +211,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_b);
   }
-  // Group row offsets and tile prefix sums (warp 2).
+  // Group row offsets and tile prefix sums (warp 2); device offsets come from a
+  // previous kernel, dense GEMMs need none.
   if (warp == 2) {
+    if (p.offsets != nullptr) grid_dep_wait();
     int carry = 0;
     for (int base = 0; base < groups; base += 32) {
       const int g = base + lane;
@@ -236,6 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  grid_dep_launch();
 
   const uint32_t tmem_base = *tmem_slot;
   const int total_tiles = *total_tiles_s;
@@ -247,6 +260,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
+      // Dense GEMMs: issue the weight tiles of the first work item's first stages before
+      // waiting for the previous kernel (weights never depend on it); their activation tiles
+      // follow the wait on the same stage barriers.
+      int pre = 0;
+      if (p.pdl_prefetch_a && p.offsets == nullptr && p.wait_count == 0 && static_cast<int>(blockIdx.x) < total_work) {
+        const int w = blockIdx.x;
+        const int t = w / ks, split = w - t * ks;
+        int g, mt, nt;
+        decode_tile<BN>(t, prefix_s, offs_s, groups, g, mt, nt);
+        const int a_row = g * p.a_rows + mt * kBM;
+        const int kb0 = split * kb_per, kb1 = min(num_kb, kb0 + kb_per);
+        pre = min(C::kStages, kb1 - kb0);
+        for (int i = 0; i < pre; ++i) {
+          uint8_t* sa = smem + i * C::kStageBytes;
+          mbar_arrive_expect_tx(&full_bar[i], C::kStageBytes);
+          tma_load_2d(sa, &tmap_a, &full_bar[i], (kb0 + i) * kBK, a_row);
+          if (GATED) tma_load_2d(sa + C::kABytes, &tmap_a, &full_bar[i], (kb0 + i) * kBK, a_row + p.m_out);
+        }
+      }
+      grid_dep_wait();
       if (p.wait_count > 0) {
         // the activations are gathered from the other ranks: wait (bounded) until all have landed
         const uint32_t target = *reinterpret_cast<const volatile uint32_t*>(p.wait_seq);
@@ -275,6 +308,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int b_row = offs_s[g] + nt * BN;
         const int kb0 = split * kb_per, kb1 = min(num_kb, kb0 + kb_per);
         for (int kb = kb0; kb < kb1; ++kb) {
+          if (pre > 0 && w == static_cast<int>(blockIdx.x) && kb - kb0 < pre) {
+            // weight tile already in flight on this (fresh) stage: add the activation tile
+            tma_load_2d(smem + stage * C::kStageBytes + C::kABytes * (GATED ? 2 : 1), &tmap_b, &full_bar[stage],
+                        kb * kBK, b_row);
+            ++issued;
+            if (++stage == C::kStages) { stage = 0; phase ^= 1; }
+            continue;
+          }
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, p.status)) { ok = false; break; }
           uint8_t* sa = smem + stage * C::kStageBytes;
           uint8_t* sb = sa + C::kABytes * (GATED ? 2 : 1);
@@ -296,6 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
+    grid_dep_wait();  // nothing to do before the activations arrive; keeps the bounded waits short
     constexpr uint32_t idesc = umma_idesc_bf16_f32(kBM, BN);
     int stage = 0;
     uint32_t phase = 0;
@@ -344,6 +386,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
+    grid_dep_wait();  // residual / output buffers belong to the stream's earlier kernels
     const int lane_base = 32 * (warp & 3);
     int local = 0;
     for (int w = blockIdx.x; w < total_work; w += gridDim.x, ++local) {
@@ -385,9 +428,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 v = silu_f(v) * __uint_as_float(u[j]);
               } else {
                 v += bias_v;
-                if (p.act == kActGeluTanh) v = gelu_tanh_f(v);
-                else if (p.act == kActGeluErf) v = gelu_erf_f(v);
-                else if (p.act == kActSilu) v = silu_f(v);
+                if (ACT) {
+                  if (p.act == kActGeluTanh) v = gelu_tanh_f(v);
+                  else if (p.act == kActGeluErf) v = gelu_erf_f(v);
+                  else if (p.act == kActSilu) v = silu_f(v);
+                }
               }
               if (p.residual != nullptr) v += __bfloat162float(p.residual[static_cast<int64_t>(row) * p.ldr + m]);
               if (p.out_f32) {
@@ -541,13 +586,22 @@ int num_sms() {
   return n;
 }
 
-template <int BN, bool GATED>
+bool pdl_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = std::getenv("OMNI_PDL");
+    on = (e == nullptr || std::strcmp(e, "0") != 0) ? 1 : 0;
+  }
+  return on == 1;
+}
+
+template <int BN, bool GATED, bool ACT>
 cudaError_t launch(const GemmArgs& a, cudaStream_t stream) {
   using C = Cfg<BN, GATED>;
   static bool attr_set = false;
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_bf16_kernel<BN, GATED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         C::kSmemBytes);
+    cudaError_t e = cudaFuncSetAttribute(gemm_bf16_kernel<BN, GATED, ACT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
@@ -618,7 +672,20 @@ cudaError_t launch(const GemmArgs& a, cudaStream_t stream) {
   int grid = a.max_ctas > 0 ? a.max_ctas : num_sms();
   if (bound < grid) grid = static_cast<int>(bound);
   if (grid < 1) grid = 1;
-  gemm_bf16_kernel<BN, GATED><<<grid, kThreads, C::kSmemBytes, stream>>>(ta, tb, p);
+  const bool pdl = pdl_enabled();
+  p.pdl_prefetch_a = pdl && a.static_a ? 1 : 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t le = cudaLaunchKernelEx(&cfg, gemm_bf16_kernel<BN, GATED, ACT>, ta, tb, p);
+  if (le != cudaSuccess) return le;
   if (p.k_splits > 1 && p.counters == nullptr) {
     const long long n = static_cast<long long>(a.rows) * a.m_out;
     int rgrid = static_cast<int>((n + 255) / 256);
@@ -638,16 +705,23 @@ cudaError_t gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   if (a.rows == 0) return cudaSuccess;
   int hint = a.expected_rows_per_group > 0 ? a.expected_rows_per_group : a.rows;
   if (a.gated) {
-    if (hint <= 16) return launch<16, true>(a, stream);
-    if (hint <= 32) return launch<32, true>(a, stream);
-    if (hint <= 64) return launch<64, true>(a, stream);
-    return launch<128, true>(a, stream);
+    if (hint <= 16) return launch<16, true, false>(a, stream);
+    if (hint <= 32) return launch<32, true, false>(a, stream);
+    if (hint <= 64) return launch<64, true, false>(a, stream);
+    return launch<128, true, false>(a, stream);
   }
-  if (hint <= 16) return launch<16, false>(a, stream);
-  if (hint <= 32) return launch<32, false>(a, stream);
-  if (hint <= 64) return launch<64, false>(a, stream);
-  if (hint <= 128) return launch<128, false>(a, stream);
-  return launch<256, false>(a, stream);
+  if (a.act != kActNone) {
+    if (hint <= 16) return launch<16, false, true>(a, stream);
+    if (hint <= 32) return launch<32, false, true>(a, stream);
+    if (hint <= 64) return launch<64, false, true>(a, stream);
+    if (hint <= 128) return launch<128, false, true>(a, stream);
+    return launch<256, false, true>(a, stream);
+  }
+  if (hint <= 16) return launch<16, false, false>(a, stream);
+  if (hint <= 32) return launch<32, false, false>(a, stream);
+  if (hint <= 64) return launch<64, false, false>(a, stream);
+  if (hint <= 128) return launch<128, false, false>(a, stream);
+  return launch<256, false, false>(a, stream);
 }
 
 }  // namespace omni

@@ -7,6 +7,7 @@
 #include <cuda_bf16.h>
 
 #include "omni_kernels.h"
+#include "pdl.cuh"
 
 namespace omni {
 namespace {
@@ -42,6 +43,7 @@ template <int MAXV>
 __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
                                __nv_bfloat16* __restrict__ y, __nv_bfloat16* __restrict__ res, int rows, int hidden,
                                int64_t ld_x, int64_t ld_y, float eps) {
+  grid_dep_launch();  // a dependent GEMM may start its prologue now
   const int warps = blockDim.x >> 5;
   const int row = blockIdx.x * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -96,6 +98,7 @@ __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, const __nv_b
 __global__ void layernorm_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
                                  const __nv_bfloat16* __restrict__ b, __nv_bfloat16* __restrict__ y, int rows,
                                  int hidden, float eps) {
+  grid_dep_launch();  // a dependent GEMM may start its prologue now
   const int warps = blockDim.x >> 5;
   const int row = blockIdx.x * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -138,6 +141,7 @@ template <int VPT>
 __global__ void rmsnorm_row_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
                                    __nv_bfloat16* __restrict__ y, __nv_bfloat16* __restrict__ res, int hidden,
                                    int64_t ld_x, int64_t ld_y, float eps) {
+  grid_dep_launch();  // a dependent GEMM may start its prologue now
   __shared__ float red[32];
   const int row = blockIdx.x;
   const int nvec = hidden >> 3;

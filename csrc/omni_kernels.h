@@ -56,6 +56,10 @@ struct GemmArgs {
   const unsigned int* wait_seq;
   int wait_count;
   long long wait_timeout_ns;
+  // The weights (A) are not written by any kernel still in flight on the stream (model
+  // parameters): with programmatic dependent launch the GEMM may fetch its first weight
+  // tiles before the previous kernel has finished.
+  int static_a;
 };
 cudaError_t gemm_bf16(const GemmArgs& args, cudaStream_t stream);
 

@@ -35,6 +35,7 @@
 #include <stdint.h>
 
 #include "omni_kernels.h"
+#include "pdl.cuh"
 #include "sm100.cuh"
 
 namespace omni {
@@ -90,6 +91,7 @@ __device__ void wait_phase(const TpReduceArgs& a, int phase, uint32_t target) {
 
 template <int VPT>
 __global__ void __launch_bounds__(256) tp_reduce_norm_kernel(TpReduceArgs a) {
+  grid_dep_launch();  // a dependent GEMM may start its prologue now
   __shared__ uint32_t s_target;
   __shared__ int s_last;
   __shared__ float red[8];

@@ -30,6 +30,7 @@ from torch import nn
 
 from .. import ops
 from ..ops.attention import DecodeWorkspace
+from ..ops.gemm import static_weights
 from ..ops.moe import MoEWorkspace
 
 
@@ -316,6 +317,12 @@ class DecoderLM(nn.Module):
 
         kv_cache: [layers, 2, pages, Hkv, 64, D].
         """
+        if not self.embed.is_cuda:
+            return self._forward(fb, kv_cache)
+        with static_weights():  # the parameters are never written while a forward runs
+            return self._forward(fb, kv_cache)
+
+    def _forward(self, fb: ForwardBatch, kv_cache: torch.Tensor) -> torch.Tensor:
         cfg = self.cfg
         if fb.input_embeds is not None:
             x = fb.input_embeds
@@ -437,4 +444,7 @@ class DecoderLM(nn.Module):
                    shared_out=shared_out, shared_gate=shared_gate)
 
     def logits(self, hidden: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-        return ops.linear(hidden, self.head_weight, out=out, out_dtype=torch.float32)
+        if not hidden.is_cuda:
+            return ops.linear(hidden, self.head_weight, out=out, out_dtype=torch.float32)
+        with static_weights():
+            return ops.linear(hidden, self.head_weight, out=out, out_dtype=torch.float32)

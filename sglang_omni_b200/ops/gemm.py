@@ -10,7 +10,9 @@ sglang_omni/models/qwen3_omni/thinker.py:192-213,402-412.
 """
 from __future__ import annotations
 
+import contextlib
 import os
+import threading
 
 import torch
 import torch.nn.functional as F
@@ -41,6 +43,22 @@ def splitk_scratch(device: torch.device):
     return sc
 
 ACT_NONE, ACT_GELU_TANH, ACT_GELU_ERF, ACT_SILU = 0, 1, 2, 3
+
+# Inside ``static_weights()`` the dense GEMM is told that its weight operand is
+# not being written by any kernel still in flight on the stream (model
+# parameters), so with programmatic dependent launch it fetches its first
+# weight tiles while the previous kernel is still running.
+_tls = threading.local()
+
+
+@contextlib.contextmanager
+def static_weights():
+    prev = getattr(_tls, "static", False)
+    _tls.static = True
+    try:
+        yield
+    finally:
+        _tls.static = prev
 _ACTS = {None: ACT_NONE, "none": ACT_NONE, "gelu_tanh": ACT_GELU_TANH, "gelu_pytorch_tanh": ACT_GELU_TANH,
          "gelu": ACT_GELU_ERF, "gelu_erf": ACT_GELU_ERF, "silu": ACT_SILU}
 
@@ -105,7 +123,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias=None, residual=None, act=None,
     peer, rows_per = scatter if scatter is not None else (None, 0)
     wf, wseq, wt = wait if wait is not None else (None, None, 2.0)
     ext().gemm(w, x2, out, None, n, gated, bias, residual, act_code(act), rows, status_word(x.device), 0, ws, ctr,
-               peer, rows_per, wf, wseq, wt)
+               peer, rows_per, wf, wseq, wt, getattr(_tls, "static", False))
     return out
 
 

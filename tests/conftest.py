@@ -13,10 +13,16 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "slow: long-running test")
 
 
+GPU_TEST_TIMEOUT_S = 240  # a GPU test that runs longer has hung: fail it instead of holding the GPU
+
+
 def pytest_collection_modifyitems(config, items):
     import torch
 
     if torch.cuda.is_available():
+        for item in items:
+            if "gpu" in item.keywords and item.get_closest_marker("timeout") is None:
+                item.add_marker(pytest.mark.timeout(GPU_TEST_TIMEOUT_S))
         return
     skip = pytest.mark.skip(reason="no CUDA device")
     for item in items:

@@ -123,3 +123,24 @@ def test_splitk_finalisers(monkeypatch, mode, rows, n, k, act, f32):
     y2 = L.linear(x, w, bias=b, residual=r, act=act, out_dtype=dt)
     _close(y1, ref, 1e-2 if f32 else 2e-2)
     assert torch.equal(y1, y2)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("gated", [False, True])
+@pytest.mark.parametrize("rows,n,k", [(64, 1024, 2048), (16, 768, 1024), (300, 512, 512)])
+def test_static_weight_prefetch(gated, rows, n, k):
+    """Dense GEMMs inside static_weights() fetch their first weight tiles before the previous
+    kernel finishes (programmatic dependent launch); gate and up halves, every shape path."""
+    from sglang_omni_b200.ops import _ext
+
+    torch.manual_seed(rows + n)
+    x = torch.randn(rows, k, device="cuda").bfloat16()
+    w = (torch.randn(2 * n if gated else n, k, device="cuda") * 0.05).bfloat16()
+    ref = L.linear_ref(x, w, out_dtype=torch.float32, gated=gated)
+    x2 = torch.empty_like(x)
+    with L.static_weights():
+        x2.copy_(x)                      # the activations come from the kernel right before
+        y = L.linear(x2, w, gated=gated)
+    torch.cuda.synchronize()
+    _ext.check_status(x.device)
+    _close(y, ref)
