@@ -33,7 +33,7 @@ void gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& out, co
           const c10::optional<torch::Tensor>& status, int64_t max_ctas,
           const c10::optional<torch::Tensor>& splitk_ws, const c10::optional<torch::Tensor>& splitk_counters,
           const c10::optional<torch::Tensor>& peer_out, int64_t rows_per, const c10::optional<torch::Tensor>& wait_flags,
-          const c10::optional<torch::Tensor>& wait_seq, double wait_timeout_s, bool static_a) {
+          const c10::optional<torch::Tensor>& wait_seq, double wait_timeout_s, bool static_a, bool splitk_cluster) {
   OMNI_CHECK_CUDA(a);
   OMNI_CHECK_CUDA(b);
   OMNI_CHECK_CUDA(out);
@@ -120,6 +120,7 @@ void gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& out, co
     args.wait_timeout_ns = static_cast<long long>(wait_timeout_s * 1e9);
   }
   args.static_a = static_a ? 1 : 0;
+  args.splitk_cluster = splitk_cluster ? 1 : 0;
   check_launch(omni::gemm_bf16(args, at::cuda::getCurrentCUDAStream()), "gemm_bf16");
 }
 
@@ -724,7 +725,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("expected_rows"), py::arg("status"), py::arg("max_ctas") = 0, py::arg("splitk_ws") = py::none(),
         py::arg("splitk_counters") = py::none(), py::arg("peer_out") = py::none(), py::arg("rows_per") = 0,
         py::arg("wait_flags") = py::none(), py::arg("wait_seq") = py::none(), py::arg("wait_timeout_s") = 2.0,
-        py::arg("static_a") = false);
+        py::arg("static_a") = false, py::arg("splitk_cluster") = false);
   m.def("rmsnorm", &rmsnorm, "RMSNorm (+ fused residual add)");
   m.def("layernorm", &layernorm, "LayerNorm");
   m.def("attention_prefill", &attention_prefill, "paged / varlen GQA prefill attention");

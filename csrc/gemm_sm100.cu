@@ -60,6 +60,7 @@ struct DevParams {
                          // token-major inside a tile, so stores and the finaliser's reads coalesce)
   int vec4;              // outputs / bias / residual allow 4-wide vector access (split-K finaliser)
   int pdl_prefetch_a;    // programmatic dependent launch with static weights: prefetch them before the wait
+  int cluster_splitk;    // split-K over a thread-block cluster: partials stay in shared memory (DSMEM reduce)
   int* counters;         // [tiles] arrival counters, zero between calls
   const unsigned long long* peer_out;  // owner scatter: row r -> peer_out[r / rows_per] + r * ldo
   int rows_per;
@@ -411,7 +412,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_32x32b_x16(t_base + c, r);
         if (GATED) tmem_ld_32x32b_x16(t_base + BN + c, u);
         tmem_ld_wait();
-        if (ks > 1) {
+        if (ks > 1 && p.cluster_splitk) {
+          // split-K partial into this CTA's shared memory as a [BN][128] fp32 tile (the stage
+          // ring is idle: this CTA's only work item has finished its MMAs)
+          float* sp = reinterpret_cast<float*>(smem) + c * kBM + lane_base + lane;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) sp[j * kBM] = __uint_as_float(r[j]);
+        } else if (ks > 1) {
           // split-K partial into this split's plane [split][t][BN][128] (thread = one A row; for
           // each token a warp stores 32 consecutive floats); summed in split order by the
           // finaliser, so the result does not depend on which split arrives first
@@ -446,7 +453,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(&tempty_bar[acc]);
-      if (ks > 1 && p.counters != nullptr) {
+      if (ks > 1 && p.counters != nullptr && !p.cluster_splitk) {
         // The last split of this tile to arrive sums the partials and runs the epilogue:
         // no second launch.  Counters reset themselves for the next call / graph replay.
         __threadfence();
@@ -509,6 +516,56 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+  }
+
+  if (p.cluster_splitk) {
+    // Cluster split-K: CTA r of the cluster holds split r's partial tile in shared memory.
+    // After the cluster barrier each CTA sums one slice of the tile's token rows over every
+    // CTA's copy (distributed shared memory, in rank order, so the result does not depend
+    // on timing) and runs the epilogue; the second barrier keeps every CTA's shared memory
+    // alive until the others have read it.  Every thread of the CTA takes both barriers.
+    cluster_sync();
+    if (warp >= 2 && total_work > 0) {
+      const int t = static_cast<int>(blockIdx.x) / ks;
+      const uint32_t rank = cluster_ctarank();
+      int g, mt, nt;
+      decode_tile<BN>(t, prefix_s, offs_s, groups, g, mt, nt);
+      const int row0 = offs_s[g] + nt * BN;
+      const int row_end = offs_s[g + 1];
+      const int per = (BN + ks - 1) / ks;
+      const int tok_lo = static_cast<int>(rank) * per, tok_hi = min(BN, tok_lo + per);
+      const int n4 = max(0, tok_hi - tok_lo) * (kBM / 4);
+      const uint32_t base = smem_u32(smem) + static_cast<uint32_t>(tok_lo * kBM * 4);
+      const int tid = threadIdx.x - 64;
+#pragma unroll 1
+      for (int e = tid; e < n4; e += 128) {
+        const uint32_t off = static_cast<uint32_t>(e) * 16u;
+        float4 x[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          x[q] = q < ks ? ld_dsmem_f4(dsmem_addr(base + off, static_cast<uint32_t>(q))) : make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 acc = x[0];
+#pragma unroll
+        for (int q = 1; q < 8; ++q) {
+          if (q < ks) {
+            acc.x += x[q].x;
+            acc.y += x[q].y;
+            acc.z += x[q].z;
+            acc.w += x[q].w;
+          }
+        }
+        const int tok = tok_lo + e / (kBM / 4);
+        const int mm = mt * kBM + (e % (kBM / 4)) * 4;
+        const int row = row0 + tok;
+        if (row < row_end && mm < p.m_out) {
+          void* orow = p.out_f32 ? static_cast<void*>(static_cast<float*>(p.out) + static_cast<int64_t>(row) * p.ldo)
+                                 : static_cast<void*>(out_row_bf16(p, row));
+          store_out4(p.bias == nullptr ? nullptr : p.bias + static_cast<int64_t>(g) * p.m_out, p.residual, p.ldr, orow,
+                     p.out_f32, p.act, mm, p.m_out, p.vec4, row, acc);
+        }
+      }
+    }
+    cluster_sync();
   }
 
   tc_fence_before();
@@ -641,7 +698,8 @@ cudaError_t launch(const GemmArgs& a, cudaStream_t stream) {
   const int m_tiles = (a.m_out + kBM - 1) / kBM;
   const int num_kb = (a.k + kBK - 1) / kBK;
   // Split-K for dense GEMMs that would leave most SMs idle (decode projections).
-  if (!GATED && a.offsets == nullptr && a.splitk_ws != nullptr) {
+  p.cluster_splitk = 0;
+  if (!GATED && a.offsets == nullptr && (a.splitk_ws != nullptr || a.splitk_cluster)) {
     const long tiles = static_cast<long>(m_tiles) * ((a.rows + BN - 1) / BN);
     const int sms = num_sms();
     if (tiles * 2 <= sms && num_kb >= 4) {
@@ -653,7 +711,11 @@ cudaError_t launch(const GemmArgs& a, cudaStream_t stream) {
         const int per = (num_kb + ksp - 1) / ksp;
         ksp = (num_kb + per - 1) / per;  // no empty splits
         const long long plane = static_cast<long long>(m_tiles) * kBM * ((a.rows + BN - 1) / BN) * BN;
-        if (plane * ksp <= a.splitk_ws_floats) {
+        if (a.splitk_cluster && tiles * ksp <= sms) {
+          // one cluster of ksp CTAs per output tile: no global scratch, no arrival counters
+          p.k_splits = ksp;
+          p.cluster_splitk = 1;
+        } else if (plane * ksp <= a.splitk_ws_floats) {
           p.k_splits = ksp;
           p.ws = a.splitk_ws;
           // tiles within the counter slots: the last split finalises in-kernel (no reduce launch)
@@ -679,14 +741,27 @@ cudaError_t launch(const GemmArgs& a, cudaStream_t stream) {
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = C::kSmemBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (p.cluster_splitk) {
+    grid = static_cast<int>((static_cast<long>(m_tiles) * ((a.rows + BN - 1) / BN)) * p.k_splits);
+    cfg.gridDim = dim3(grid);
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = p.k_splits;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = na;
   cudaError_t le = cudaLaunchKernelEx(&cfg, gemm_bf16_kernel<BN, GATED, ACT>, ta, tb, p);
   if (le != cudaSuccess) return le;
-  if (p.k_splits > 1 && p.counters == nullptr) {
+  if (p.k_splits > 1 && p.counters == nullptr && !p.cluster_splitk) {
     const long long n = static_cast<long long>(a.rows) * a.m_out;
     int rgrid = static_cast<int>((n + 255) / 256);
     if (rgrid > 4 * num_sms()) rgrid = 4 * num_sms();

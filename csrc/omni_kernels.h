@@ -45,6 +45,9 @@ struct GemmArgs {
   long long splitk_ws_floats;
   int* splitk_counters;
   int splitk_counter_slots;
+  // Split-K over a thread-block cluster instead (one cluster of splits per output tile, the
+  // partial tiles reduced through distributed shared memory): needs no scratch at all.
+  int splitk_cluster;
   // Optional owner scatter (tensor parallel): bf16 output row r is stored at
   // peer_out[r / rows_per] + r * ldo, i.e. straight into the memory of the
   // rank that owns token r (over NVLink for the other ranks).

@@ -1,7 +1,8 @@
 """Small standalone kernel workloads for profiling (one kernel family per case,
 three launches, a few GB on the device at most):
 
-    python -m sglang_omni_b200.ops.bench_cases {moe_w13|dense_prefill|decode_attn|decode_dense|time}
+    python -m sglang_omni_b200.ops.bench_cases {moe_w13|dense_prefill|decode_attn|decode_dense|
+                                                prefill_attn|rmsnorm|rope_store|moe_route|sample|time}
 
 Used to produce the ncu summaries of the hot kernels.
 """
@@ -55,6 +56,63 @@ def run(case: str) -> None:
             L.linear(x, wq)
             L.linear(xo, wo)
             L.linear(x, wr, out_dtype=torch.float32)
+    elif case == "prefill_attn":
+        # one 8192-token prefill chunk: 8 requests x 1024 prompt tokens, 32 q / 4 kv heads x 128, causal
+        from . import prefill_tiles
+        R, P, hq, hkv, d = 8, 1024, 32, 4, 128
+        pages = P // 64
+        k = torch.randn(R * pages + 1, hkv, 64, d, device="cuda").bfloat16()
+        v = torch.randn_like(k)
+        bt = torch.arange(1, R * pages + 1, dtype=torch.int32, device="cuda").view(R, pages)
+        kl = torch.full((R,), P, dtype=torch.int32, device="cuda")
+        cu = torch.arange(0, R * P + 1, P, dtype=torch.int32, device="cuda")
+        tr, t0 = prefill_tiles([P] * R, hq // hkv)
+        tr = torch.tensor(tr, dtype=torch.int32, device="cuda")
+        t0 = torch.tensor(t0, dtype=torch.int32, device="cuda")
+        q = torch.randn(R * P, hq * d, device="cuda").bfloat16()
+        for _ in range(3):
+            A.prefill_attention(q, k, v, bt, cu, kl, tr, t0, hq, hkv, d)
+    elif case == "rmsnorm":
+        # fused residual add + RMSNorm over 65536 x 2048 bf16 (268 MB per tensor, > L2)
+        from .norm import rms_norm
+        x = torch.randn(65536, 2048, device="cuda").bfloat16()
+        r = torch.randn_like(x)
+        w = torch.randn(2048, device="cuda").bfloat16()
+        out = torch.empty_like(x)
+        for _ in range(3):
+            rms_norm(x, w, 1e-6, residual=r, out=out)
+    elif case == "rope_store":
+        # QK-RMSNorm + interleaved M-RoPE + paged KV store, 65536 tokens x (32 + 2 x 4) heads x 128
+        from .rope import qkv_rope_store, rope_tables
+        T, hq, hkv, d = 65536, 32, 4, 128
+        qkv = torch.randn(T, (hq + 2 * hkv) * d, device="cuda").bfloat16()
+        cos, sin = rope_tables(d, 1e6, 8192, "cuda")
+        pos = torch.randint(0, 8192, (3, T), dtype=torch.int32, device="cuda")
+        kc = torch.zeros(T // 64 + 1, hkv, 64, d, device="cuda").bfloat16()
+        vc = torch.zeros_like(kc)
+        slots = torch.arange(64, T + 64, dtype=torch.int32, device="cuda")
+        qn = torch.ones(d, device="cuda").bfloat16()
+        for _ in range(3):
+            qkv_rope_store(qkv, hq, hkv, d, pos, cos, sin, q_norm=qn, k_norm=qn, mrope_section=[24, 20, 20],
+                           slot_mapping=slots, k_cache=kc, v_cache=vc)
+    elif case == "moe_route":
+        # softmax top-8 of 128 experts + expert histogram / offsets + permuted gather of 8192 x 2048 rows
+        from .moe import MoEWorkspace, route
+        T, E, H = 8192, 128, 2048
+        ws = MoEWorkspace(T, E, 8, H, 768, "cuda")
+        logits = torch.randn(T, E, device="cuda")
+        x = torch.randn(T, H, device="cuda").bfloat16()
+        for _ in range(3):
+            route(logits, 8, ws=ws, x=x)
+    elif case == "sample":
+        # top-k 50 / top-p 0.9 / temperature 0.8 sampling of 64 x 151936 fp32 logits
+        from .sampling import SamplingTensors, sample
+        B, V = 64, 151936
+        logits = torch.randn(B, V, device="cuda")
+        st = SamplingTensors(torch.full((B,), 0.8, device="cuda"), torch.full((B,), 50, dtype=torch.int32, device="cuda"),
+                             torch.full((B,), 0.9, device="cuda"), torch.zeros(B, device="cuda"))
+        for _ in range(3):
+            sample(logits.clone(), st)
     elif case == "time":
         _time_cases()
         return

@@ -28,7 +28,9 @@ from ._ext import ext, status_word
 # utils.cuda_graph).  GEMMs needing more than the buffer fall back to no split.
 _SPLITK_FLOATS = 8 * 1024 * 1024
 _SPLITK_COUNTERS = 1024   # per-tile arrival counters of the in-kernel split-K finalisation
-_SPLITK_MODE = int(os.environ.get("OMNI_SPLITK", "2"))  # 2 in-kernel finalise, 1 reduce kernel, 0 off
+# 3: split-K over a thread-block cluster (partials reduced through distributed shared memory),
+# 2: the last split finalises from the global scratch, 1: a second kernel finalises, 0: off
+_SPLITK_MODE = int(os.environ.get("OMNI_SPLITK", "3"))
 _splitk: dict[tuple[int, int], tuple[torch.Tensor, torch.Tensor]] = {}
 
 
@@ -116,14 +118,14 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias=None, residual=None, act=None,
     x2 = x if x.is_contiguous() else x.contiguous()
     rows = x2.numel() // x2.shape[-1]
     ws, ctr = splitk_scratch(x.device)
-    if _SPLITK_MODE != 2:   # 0: no split-K, 1: split-K finalised by a second kernel
+    if _SPLITK_MODE not in (2, 3):   # 0: no split-K, 1: split-K finalised by a second kernel
         ctr = None
         if _SPLITK_MODE == 0:
             ws = None
     peer, rows_per = scatter if scatter is not None else (None, 0)
     wf, wseq, wt = wait if wait is not None else (None, None, 2.0)
     ext().gemm(w, x2, out, None, n, gated, bias, residual, act_code(act), rows, status_word(x.device), 0, ws, ctr,
-               peer, rows_per, wf, wseq, wt, getattr(_tls, "static", False))
+               peer, rows_per, wf, wseq, wt, getattr(_tls, "static", False), _SPLITK_MODE == 3)
     return out
 
 

@@ -103,12 +103,12 @@ def test_splitk_dense_repeated(rows, n, k):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("mode", [1, 2])
+@pytest.mark.parametrize("mode", [1, 2, 3])
 @pytest.mark.parametrize("rows,n,k,act,f32", [(64, 5120, 2048, None, False), (64, 130, 2048, "gelu", False),
                                               (16, 2048, 4096, "silu", False), (33, 128, 2048, None, True),
                                               (64, 516, 1024, "gelu_tanh", True)])
 def test_splitk_finalisers(monkeypatch, mode, rows, n, k, act, f32):
-    """Both split-K finalisers (second kernel / last split in the GEMM) against the fp32 oracle,
+    """Every split-K finaliser (second kernel / last split in the GEMM / cluster DSMEM reduce) against the fp32 oracle,
     with bias, activation and residual, bf16 and fp32 outputs, and output widths that are not a
     multiple of the 4-wide vector stores; two calls in a row must agree bit for bit."""
     monkeypatch.setattr(L, "_SPLITK_MODE", mode)
