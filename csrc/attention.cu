@@ -689,6 +689,7 @@ cudaError_t attention_prefill(const AttnPrefillArgs& a, cudaStream_t stream) {
   switch (a.head_dim) {
     case 64: return launch_prefill<64>(p, a.num_tiles, stream);
     case 80: return launch_prefill<80>(p, a.num_tiles, stream);
+    case 96: return launch_prefill<96>(p, a.num_tiles, stream);
     case 128: return launch_prefill<128>(p, a.num_tiles, stream);
     default: return cudaErrorInvalidValue;
   }

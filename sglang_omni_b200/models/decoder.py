@@ -62,6 +62,7 @@ class DecoderConfig:
     mrope_section: list | None = None   # e.g. [24, 20, 20]
     mrope_interleaved: bool = True
     qk_norm: bool = True
+    attention_bias: bool = False        # q / k / v projection biases (Qwen2)
     tie_word_embeddings: bool = False
     max_position: int = 65536
     dtype: torch.dtype = torch.bfloat16
@@ -155,6 +156,9 @@ class DecoderLM(nn.Module):
             L = nn.Module()
             L.ln1 = P(H)
             L.qkv = P(cfg.q_size + 2 * cfg.kv_size, H)
+            if cfg.attention_bias:
+                assert tp is None, "q/k/v biases are not sharded for tensor parallelism"
+                L.qkv_bias = P(cfg.q_size + 2 * cfg.kv_size)
             L.o = P(H, cfg.q_size)
             L.ln2 = P(H)
             if cfg.qk_norm:
@@ -198,7 +202,7 @@ class DecoderLM(nn.Module):
         for idx, (name, p) in enumerate(self.named_parameters()):
             if p.dim() == 1 and ("ln" in name or "norm" in name):
                 p.fill_(1.0)
-            elif name.endswith("router_bias"):
+            elif name.endswith(("router_bias", "qkv_bias")):
                 p.zero_()
             elif name.endswith((".w13", ".w2")):
                 for j in range(p.shape[0]):
@@ -346,7 +350,7 @@ class DecoderLM(nn.Module):
                 normed = ops.rms_norm(h, L.ln1, cfg.rms_norm_eps, residual=res)
             if i in fb.capture_layers:
                 fb.captured[i] = res.clone()
-            qkv = ops.linear(normed, L.qkv)
+            qkv = ops.linear(normed, L.qkv, bias=getattr(L, "qkv_bias", None))
             ops.qkv_rope_store(qkv, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, fb.positions, self.cos_tab,
                                self.sin_tab, rot, getattr(L, "q_norm", None), getattr(L, "k_norm", None),
                                cfg.rms_norm_eps, cfg.rope_neox, cfg.mrope_section, cfg.mrope_interleaved,

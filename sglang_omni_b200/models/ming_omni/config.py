@@ -1,6 +1,7 @@
-"""Pipeline configuration of Ming-Omni text output:
-preprocessing -> audio_encoder -> mm_aggregate -> thinker -> decode
-(stage names and routing as in sglang_omni/models/ming_omni/config.py:25-105)."""
+"""Pipeline configurations of Ming-Omni:
+text output   preprocessing -> audio_encoder -> mm_aggregate -> thinker -> decode;
+speech output the same, with the thinker fanning out to decode and talker
+(stage names and routing as in sglang_omni/models/ming_omni/config.py:25-202)."""
 from __future__ import annotations
 
 from typing import ClassVar
@@ -41,6 +42,28 @@ class MingOmniPipelineConfig(PipelineConfig):
     entry_stage: str = "preprocessing"
     stages: list[StageConfig] = Field(default_factory=lambda: ming_stages())
     terminal_stages: list[str] = Field(default_factory=lambda: ["decode"])
+
+
+def ming_speech_stages(overrides=None, device="cuda:0", talker_device=None, max_batch=64, max_context=8192,
+                       max_streams=32):
+    st = ming_stages(overrides, device, max_batch, max_context)
+    for s in st:
+        if s.name == "thinker":
+            s.get_next = f"{_N}.thinker_next_speech"
+    ov = {"overrides": overrides} if overrides else {}
+    st.append(StageConfig(name="talker", executor=ExecutorConfig(
+        factory=f"{_S}.create_talker_executor",
+        args={"device": talker_device or device, "max_streams": max_streams, **ov}),
+        get_next=f"{_N}.talker_next"))
+    return st
+
+
+class MingOmniSpeechPipelineConfig(PipelineConfig):
+    """Text + speech output: the talker (own Qwen2 LM + CFM/DiT + AudioVAE) speaks the thinker's text."""
+    architecture: ClassVar[str] = "BailingMM2NativeForConditionalGeneration"
+    entry_stage: str = "preprocessing"
+    stages: list[StageConfig] = Field(default_factory=lambda: ming_speech_stages())
+    terminal_stages: list[str] = Field(default_factory=lambda: ["decode", "talker"])
 
 
 EntryClass = MingOmniPipelineConfig

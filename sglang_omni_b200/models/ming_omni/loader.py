@@ -143,3 +143,91 @@ def eos_ids(model_path: str, overrides: dict | None = None) -> tuple:
     e = getattr(tok, "eos_token_id", None)
     return (int(e),) if e is not None else ()
 
+
+
+# ----------------------------------------------------------------------------- talker + AudioVAE
+TALKER_SPECIALS = ["<|im_start|>", "<|im_end|>", "<|vision_start|>", "<|vision_pad|>", "<|vision_end|>", "<audio>",
+                   "<audioPatch>", "<|endoftext|>"]
+
+
+def _talker_cfgs(model_path: str, overrides: dict | None):
+    """(MingTalkerConfig, AudioVAEConfig) from ``<model>/talker`` (config.json, llm/config.json)
+    and ``<model>/talker/vae`` when present, else the defaults; ``overrides`` =
+    {"talker": {...}, "talker_llm": {...}, "vae": {...}} shrink them for tests."""
+    import os
+
+    from .audio_vae import AudioVAEConfig
+    from .talker import MingTalkerConfig
+
+    tdir = os.path.join(model_path, "talker") if model_path else ""
+    tc, vc = MingTalkerConfig(), AudioVAEConfig()
+    if tdir and os.path.isfile(os.path.join(tdir, "config.json")):
+        with open(os.path.join(tdir, "config.json")) as f:
+            raw = json.load(f)
+        llm = {}
+        if os.path.isfile(os.path.join(tdir, "llm", "config.json")):
+            with open(os.path.join(tdir, "llm", "config.json")) as f:
+                llm = json.load(f)
+        tc = MingTalkerConfig.from_dict(raw, llm)
+        if os.path.isfile(os.path.join(tdir, "vae", "config.json")):
+            with open(os.path.join(tdir, "vae", "config.json")) as f:
+                vc = AudioVAEConfig.from_dict(json.load(f))
+    ov = overrides or {}
+    for k, v in (ov.get("talker") or {}).items():
+        setattr(tc, k, v)
+    for k, v in (ov.get("talker_llm") or {}).items():
+        setattr(tc.llm, k, v)
+    for k, v in (ov.get("vae") or {}).items():
+        setattr(vc, k, v)
+    vc.latent_dim = tc.latent_dim
+    return tc, vc, tdir
+
+
+def get_talker(model_path: str, device, overrides: dict | None = None):
+    from .talker import MingTalker
+
+    k = _key(model_path, "talker", device, overrides)
+    with _LOCK:
+        if k not in _CACHE:
+            tc, _, tdir = _talker_cfgs(model_path, overrides)
+            m = MingTalker(tc, device=device)
+            if tdir and has_checkpoint(tdir):
+                m.load_state_dict_ref(load_by_prefix(tdir, ""))
+            else:
+                m.random_init_(seed=SEEDS["llm"] + 40)
+            _CACHE[k] = _ready(m)
+        return _CACHE[k]
+
+
+def get_audio_vae(model_path: str, device, overrides: dict | None = None):
+    import os
+
+    from .audio_vae import AudioVAEDecoder
+
+    k = _key(model_path, "vae", device, overrides)
+    with _LOCK:
+        if k not in _CACHE:
+            _, vc, tdir = _talker_cfgs(model_path, overrides)
+            m = AudioVAEDecoder(vc, device=device)
+            vdir = os.path.join(tdir, "vae") if tdir else ""
+            if vdir and has_checkpoint(vdir):
+                m.load_state_dict_ref(load_by_prefix(vdir, ""))
+            else:
+                m.random_init_(seed=SEEDS["llm"] + 41)
+            _CACHE[k] = _ready(m)
+        return _CACHE[k]
+
+
+def get_talker_tokenizer(model_path: str, overrides: dict | None = None):
+    import os
+
+    k = _key(model_path, "talker_tok", "cpu", overrides)
+    with _LOCK:
+        if k not in _CACHE:
+            tdir = os.path.join(model_path, "talker", "llm") if model_path else ""
+            if tdir and os.path.isdir(tdir) and has_checkpoint(os.path.dirname(tdir)):
+                _CACHE[k] = load_tokenizer(tdir)
+            else:
+                tc, _, _ = _talker_cfgs(model_path, overrides)
+                _CACHE[k] = SpecialsByteTokenizer(TALKER_SPECIALS, tc.llm.vocab_size, eos="<|endoftext|>")
+        return _CACHE[k]

@@ -1,4 +1,4 @@
-"""Stage routing of the Ming-Omni text pipeline (stage names as in
+"""Stage routing of the Ming-Omni text and speech pipelines (stage names as in
 sglang_omni/models/ming_omni/pipeline/next_stage.py:11-67)."""
 from __future__ import annotations
 
@@ -7,6 +7,7 @@ AUDIO_STAGE = "audio_encoder"
 AGGREGATE_STAGE = "mm_aggregate"
 THINKER_STAGE = "thinker"
 DECODE_STAGE = "decode"
+TALKER_STAGE = "talker"
 
 
 def preprocessing_next(request_id, output):
@@ -25,5 +26,14 @@ def thinker_next(request_id, output):
     return DECODE_STAGE
 
 
+def thinker_next_speech(request_id, output):
+    """Speech output: the thinker's result goes to decode (text) and to the talker."""
+    return [DECODE_STAGE, TALKER_STAGE]
+
+
 def decode_next(request_id, output):
+    return None
+
+
+def talker_next(request_id, output):
     return None

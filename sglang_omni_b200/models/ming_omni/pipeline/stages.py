@@ -15,12 +15,19 @@
 """
 from __future__ import annotations
 
+import asyncio
+import logging
+import threading
+from collections import deque
+
 import torch
 
 from ....engines.omni.factory import create_encoder_engine
 from ....engines.omni.runtime.encoder import EncoderRequestData
 from ....executors import EngineExecutor, PreprocessingExecutor
+from ....executors.interface import Executor, ResultQueueMixin
 from ....ops.mel import LogMel
+from ....executors.preprocessing_executor import StageError
 from ....proto import StagePayload
 from ...qwen3_omni.pipeline import stages as qstages
 from .. import loader
@@ -29,6 +36,8 @@ from ..hf_config import (AUDIO_END, AUDIO_PATCH, AUDIO_START, ROLE_ASSISTANT, RO
 
 DEFAULT_SYSTEM_PROMPT = "你是一个友好的AI助手。"
 
+
+log = logging.getLogger(__name__)
 
 def build_prompt(tok, messages, text, audio_counts: list[int]):
     """Returns (ids, audio_spans [(start, end)] of the <audioPatch> runs)."""
@@ -131,3 +140,159 @@ def create_thinker_executor(model_path: str = "", device: str = "cuda:0", max_ba
 create_sglang_thinker_executor_from_config = create_thinker_executor
 create_aggregate_executor = qstages.create_aggregate_executor
 create_decode_executor = qstages.create_decode_executor
+
+
+# ----------------------------------------------------------------------------- talker (speech output)
+class MingTalkerExecutor(ResultQueueMixin, Executor):
+    """Speech from the thinker's text: every request becomes a talker stream; one
+    generator thread steps all live streams in lock step (one CUDA graph per
+    step and batch bucket) and decodes each finished stream's latents with the
+    AudioVAE.  The result carries ``audio_waveform`` / ``sample_rate`` /
+    ``duration`` (reference: MingTalkerExecutor,
+    sglang_omni/models/ming_omni/components/talker_executor.py:34-308)."""
+
+    def __init__(self, model_path: str, device: str, max_streams: int = 32, max_patches: int = 256,
+                 overrides: dict | None = None, use_graphs: bool = True, cfg_strength: float = 2.0,
+                 voice: str | None = None):
+        super().__init__()
+        from ..talker import MingSpeechGenerator
+
+        dev = torch.device(device)
+        self.device = dev
+        self.talker = loader.get_talker(model_path, dev, overrides)
+        self.vae = loader.get_audio_vae(model_path, dev, overrides)
+        self.tok = loader.get_talker_tokenizer(model_path, overrides)
+        self.gen = MingSpeechGenerator(self.talker, max_streams=max_streams, cfg_strength=cfg_strength,
+                                       use_graphs=use_graphs and dev.type == "cuda")
+        self.max_patches = max_patches
+        self.voice = voice
+        self._cv = threading.Condition()
+        self._new: deque = deque()
+        self._aborted: set[str] = set()
+        self._pending: dict[str, StagePayload] = {}
+        self._thread: threading.Thread | None = None
+        self._loop: asyncio.AbstractEventLoop | None = None
+        self._stop = False
+        self.error: BaseException | None = None
+
+    async def start(self):
+        self._loop = asyncio.get_running_loop()
+        if self._thread is None:
+            self._thread = threading.Thread(target=self._run, name="ming-talker", daemon=True)
+            self._thread.start()
+
+    async def stop(self):
+        with self._cv:
+            self._stop = True
+            self._cv.notify_all()
+
+    @staticmethod
+    def _text_of(data: dict) -> str:
+        for k in ("text", "generated_text"):
+            if data.get(k):
+                return str(data[k])
+        return str((data.get("stream_state") or {}).get("accumulated_text", ""))
+
+    async def add_request(self, payload: StagePayload) -> None:
+        if self._loop is None:
+            await self.start()
+        text = self._text_of(payload.data or {})
+        self._pending[payload.request_id] = payload
+        if self.error is not None:
+            self._deliver(payload.request_id, None, error=f"talker failed: {self.error}")
+            return
+        if not text.strip():
+            self._deliver(payload.request_id, None)
+            return
+        with self._cv:
+            self._new.append((payload.request_id, text))
+            self._cv.notify_all()
+
+    async def abort(self, request_id: str) -> None:
+        with self._cv:
+            self._aborted.add(request_id)
+            self._cv.notify_all()
+
+    def _deliver(self, rid: str, wav, error: str | None = None):
+        p = self._pending.pop(rid, None)
+        if p is None:
+            return
+        if error is not None:
+            item = StageError(rid, error)
+        else:
+            sr = self.vae.cfg.sample_rate
+            n = 0 if wav is None else int(wav.shape[-1])
+            item = StagePayload(rid, p.request, {"audio_waveform": wav, "sample_rate": sr, "duration": n / sr,
+                                                 "modality": "audio"})
+        self._loop.call_soon_threadsafe(self._results().put_nowait, item)
+
+    def _prefill_embeds(self, text: str) -> torch.Tensor:
+        from ..talker import build_talker_prompt
+
+        ids, _rows = build_talker_prompt(self.tok, text)
+        lm = self.talker.lm
+        idx = torch.tensor(ids, dtype=torch.long, device=self.device)
+        return lm.embed[idx]
+
+    def _run(self):
+        from ....utils.hostdev import own_stream
+
+        stream = own_stream(self.device)
+        if stream is not None:
+            torch.cuda.set_stream(stream)
+        try:
+            with torch.inference_mode():
+                self.gen.capture_all()
+                self._loop_body()
+        except BaseException as exc:  # fail every request of this stage, now and later
+            log.exception("Ming talker thread failed")
+            self.error = exc
+            for rid in list(self._pending):
+                self._deliver(rid, None, error=f"talker failed: {exc}")
+
+    def _loop_body(self):
+        live: dict = {}
+        while True:
+            with self._cv:
+                while not self._new and not live and not self._stop:
+                    self._cv.wait(timeout=0.5)
+                if self._stop:
+                    return
+                new, self._new = list(self._new), deque()
+                aborted, self._aborted = set(self._aborted), set()
+            for rid in aborted:
+                if rid in live:
+                    self.gen.remove(rid)
+                    live.pop(rid)
+                self._pending.pop(rid, None)
+            fresh = []
+            for rid, text in new:
+                if rid in aborted:
+                    continue
+                if len(live) + len(fresh) >= self.gen.max_streams:
+                    with self._cv:
+                        self._new.appendleft((rid, text))
+                    continue
+                st = self.gen.add_stream(rid, self._prefill_embeds(text), max_patches=self.max_patches)
+                fresh.append(st)
+                live[rid] = st
+            if fresh:
+                self.gen.prefill(fresh)
+            run = [s for s in live.values() if not s.done]
+            if run:
+                self.gen.step(run)
+            for rid, st in list(live.items()):
+                if st.done:
+                    lat = torch.stack(st.latents, 0).reshape(-1, self.talker.cfg.latent_dim)
+                    wav = self.vae.decode(lat.unsqueeze(0).to(self.device))[0].float().cpu().numpy()
+                    self.gen.remove(rid)
+                    live.pop(rid)
+                    self._deliver(rid, wav)
+
+
+def create_talker_executor(model_path: str = "", device: str = "cuda:0", voice: str | None = None,
+                           max_streams: int = 32, max_patches: int = 256, overrides: dict | None = None,
+                           use_graphs: bool = True, talker_model_path: str | None = None):
+    """The Ming TTS talker stage (own Qwen2 LM + CFM/DiT + aggregator + AudioVAE)."""
+    return MingTalkerExecutor(talker_model_path or model_path, device, max_streams=max_streams,
+                              max_patches=max_patches, overrides=overrides, use_graphs=use_graphs, voice=voice)

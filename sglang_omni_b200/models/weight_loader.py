@@ -73,6 +73,8 @@ def load_decoder_from_hf(model: DecoderLM, sd: dict[str, torch.Tensor], model_pr
         else:
             cp(L.qkv, sh("qkv", torch.cat([g(p + f"self_attn.{n}_proj.weight") for n in "qkv"], 0)))
         cp(L.o, sh("o", g(p + "self_attn.o_proj.weight")))
+        if getattr(cfg, "attention_bias", False):
+            cp(L.qkv_bias, torch.cat([g(p + f"self_attn.{n}_proj.bias") for n in "qkv"], 0))
         if cfg.qk_norm:
             cp(L.q_norm, g(p + "self_attn.q_norm.weight"))
             cp(L.k_norm, g(p + "self_attn.k_norm.weight"))
@@ -116,6 +118,10 @@ def export_decoder_to_hf(model: DecoderLM, model_prefix: str = "model.") -> dict
         out[p + "self_attn.q_proj.weight"] = L.qkv[:q].clone()
         out[p + "self_attn.k_proj.weight"] = L.qkv[q:q + kv].clone()
         out[p + "self_attn.v_proj.weight"] = L.qkv[q + kv:].clone()
+        if hasattr(L, "qkv_bias"):
+            out[p + "self_attn.q_proj.bias"] = L.qkv_bias[:q].clone()
+            out[p + "self_attn.k_proj.bias"] = L.qkv_bias[q:q + kv].clone()
+            out[p + "self_attn.v_proj.bias"] = L.qkv_bias[q + kv:].clone()
         out[p + "self_attn.o_proj.weight"] = L.o.clone()
         if cfg.qk_norm:
             out[p + "self_attn.q_norm.weight"] = L.q_norm.clone()

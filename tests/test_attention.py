@@ -96,7 +96,7 @@ def test_decode_context_longer_than_workspace():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("h,d", [(20, 64), (16, 80), (16, 128)])
+@pytest.mark.parametrize("h,d", [(20, 64), (16, 80), (16, 96), (16, 128)])
 def test_varlen_noncausal(h, d):
     lens = [5, 100, 33, 200]
     T = sum(lens)
