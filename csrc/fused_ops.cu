@@ -607,12 +607,70 @@ __device__ __forceinline__ float block_reduce(float v, float* sred, Op op, float
 struct MaxOp { __device__ float operator()(float a, float b) const { return fmaxf(a, b); } };
 struct SumOp { __device__ float operator()(float a, float b) const { return a + b; } };
 
+// Row sweeps: 16-byte loads (four per thread in flight) when the row is 16-byte
+// aligned, scalar otherwise; f(index, value).
+template <class F>
+__device__ __forceinline__ void row_for_each(const float* __restrict__ lg, int V, F f) {
+  int done = 0;
+  if ((reinterpret_cast<uintptr_t>(lg) & 15) == 0) {
+    const int n4 = V >> 2;
+    const float4* p4 = reinterpret_cast<const float4*>(lg);
+#pragma unroll 4
+    for (int j = threadIdx.x; j < n4; j += blockDim.x) {
+      const float4 v = p4[j];
+      f(4 * j, v.x);
+      f(4 * j + 1, v.y);
+      f(4 * j + 2, v.z);
+      f(4 * j + 3, v.w);
+    }
+    done = n4 << 2;
+  }
+  for (int i = done + threadIdx.x; i < V; i += blockDim.x) f(i, lg[i]);
+}
+
+// In-place transform x -> g(index, x) of the row, same access pattern.
+template <class G>
+__device__ __forceinline__ void row_transform(float* __restrict__ lg, int V, G g) {
+  int done = 0;
+  if ((reinterpret_cast<uintptr_t>(lg) & 15) == 0) {
+    const int n4 = V >> 2;
+    float4* p4 = reinterpret_cast<float4*>(lg);
+#pragma unroll 4
+    for (int j = threadIdx.x; j < n4; j += blockDim.x) {
+      float4 v = p4[j];
+      v.x = g(4 * j, v.x);
+      v.y = g(4 * j + 1, v.y);
+      v.z = g(4 * j + 2, v.z);
+      v.w = g(4 * j + 3, v.w);
+      p4[j] = v;
+    }
+    done = n4 << 2;
+  }
+  for (int i = done + threadIdx.x; i < V; i += blockDim.x) lg[i] = g(i, lg[i]);
+}
+
+__device__ __forceinline__ unsigned long long argmax_key(float x, int i) {
+  return (static_cast<unsigned long long>(f2key(x)) << 32) | (0xffffffffu - static_cast<uint32_t>(i));
+}
+
+constexpr int kSampleCand = 4096;   // candidates (value, index) kept in shared memory
+
+// One CTA (1024 threads) per row.  Full-row passes: (1) logits processing fused with
+// the row max / greedy argmax, (2) top-k threshold by a 4-pass radix select, (3) the
+// surviving candidates (>= the top-k / min-p threshold, or within 40 nats of the max
+// when only top-p is set) are compacted into shared memory; top-p's threshold search
+// and the Gumbel-max draw then run on the candidates only.  When more candidates than
+// fit survive, top-p and the draw sweep the full row instead.  The Gumbel noise of
+// token i depends only on (seed, step, i), so both routes draw the same token.
 __global__ void __launch_bounds__(1024) sample_kernel(SampleArgs a) {
   __shared__ float sred[33];
   __shared__ unsigned int hist[256];
   __shared__ uint32_t s_prefix;
   __shared__ int s_kleft;
   __shared__ unsigned long long s_best;
+  __shared__ int s_ncand;
+  __shared__ float cand_x[kSampleCand];
+  __shared__ int cand_i[kSampleCand];
   const int row = blockIdx.x;
   const int sr = a.row_slot ? a.row_slot[row] : row;  // state row
   float* lg = a.logits + static_cast<int64_t>(row) * a.logits_stride;
@@ -620,115 +678,149 @@ __global__ void __launch_bounds__(1024) sample_kernel(SampleArgs a) {
   const float temp = a.temperature ? a.temperature[sr] : 0.f;
   const float rep = a.rep_penalty ? a.rep_penalty[sr] : 1.f;
   const uint8_t* seen = a.seen ? a.seen + static_cast<int64_t>(sr) * a.seen_stride : nullptr;
-
-  // 1) logits processing in place: suppression ranges, repetition penalty, temperature
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    float x = lg[i];
-    if (a.suppress_lo >= 0 && i >= a.suppress_lo && i < a.suppress_hi && i != a.suppress_keep) x = -INFINITY;
-    if (seen && rep != 1.f && seen[i]) x = x > 0.f ? x / rep : x * rep;
-    if (temp > 0.f) x = x / temp;
-    lg[i] = x;
-  }
+  const bool greedy = !(temp > 0.f);
+  const bool suppress = a.suppress_lo >= 0;
+  const bool penal = seen != nullptr && rep != 1.f;
+  const float inv_t = greedy ? 1.f : 1.f / temp;
+  auto process = [&](int i, float x) {
+    if (suppress && i >= a.suppress_lo && i < a.suppress_hi && i != a.suppress_keep) x = -INFINITY;
+    if (penal && seen[i]) x = x > 0.f ? x / rep : x * rep;
+    return greedy ? x : x * inv_t;
+  };
+  if (threadIdx.x == 0) s_best = 0ull;
   __syncthreads();
-  // greedy
-  if (!(temp > 0.f)) {
-    unsigned long long best = 0ull;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) {
-      const unsigned long long key = (static_cast<unsigned long long>(f2key(lg[i])) << 32) | (0xffffffffu - i);
-      best = key > best ? key : best;
+
+  // 1) processing (written back only when it changes the row) + max / argmax
+  unsigned long long best = 0ull;
+  float m = -INFINITY;
+  if (suppress || penal || !greedy) {
+    row_transform(lg, V, [&](int i, float x) {
+      const float y = process(i, x);
+      m = fmaxf(m, y);
+      const unsigned long long k = argmax_key(y, i);
+      best = k > best ? k : best;
+      return y;
+    });
+  } else {
+    row_for_each(lg, V, [&](int i, float x) {
+      const unsigned long long k = argmax_key(x, i);
+      best = k > best ? k : best;
+    });
+  }
+  if (greedy) {
+    atomicMax(&s_best, best);
+    __syncthreads();
+  } else {
+    m = block_reduce(m, sred, MaxOp(), -INFINITY);
+  }
+  if (!greedy) {
+    // 2) top-k threshold by 4-pass radix select on order-preserving keys
+    float thr = -INFINITY;
+    const int topk = a.top_k ? a.top_k[sr] : 0;
+    if (topk > 0 && topk < V) {
+      if (threadIdx.x == 0) {
+        s_prefix = 0u;
+        s_kleft = topk;
+      }
+      for (int pass = 0; pass < 4; ++pass) {
+        const int shift = 24 - 8 * pass;
+        const uint32_t mask_hi = pass == 0 ? 0u : (0xffffffffu << (32 - 8 * pass));
+        for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0u;
+        __syncthreads();
+        const uint32_t pref = s_prefix;
+        row_for_each(lg, V, [&](int, float x) {
+          const uint32_t k = f2key(x);
+          if ((k & mask_hi) == pref) atomicAdd(&hist[(k >> shift) & 255u], 1u);
+        });
+        __syncthreads();
+        if (threadIdx.x == 0) {
+          int left = s_kleft;
+          int bin = 255;
+          for (; bin > 0; --bin) {
+            const int c = static_cast<int>(hist[bin]);
+            if (c >= left) break;
+            left -= c;
+          }
+          s_kleft = left;
+          s_prefix = pref | (static_cast<uint32_t>(bin) << shift);
+        }
+        __syncthreads();
+      }
+      thr = key2f(s_prefix);
     }
+    const float minp = a.min_p ? a.min_p[sr] : 0.f;
+    if (minp > 0.f) thr = fmaxf(thr, m + logf(minp));
+    const float topp = a.top_p ? a.top_p[sr] : 1.f;
+    // 3) candidates into shared memory (beyond 40 nats below the max a token's mass is < 5e-18
+    //    of the max's: negligible for top-p, never drawn in fp32 Gumbel-max either)
+    const float cthr = fmaxf(thr, m - 40.f);
+    if (threadIdx.x == 0) s_ncand = 0;
+    __syncthreads();
+    row_for_each(lg, V, [&](int i, float x) {
+      // warp-aggregated append: one shared-memory atomic per warp and element slot
+      const bool keep = x >= cthr && x > -INFINITY;
+      const unsigned act = __activemask();
+      const unsigned bal = __ballot_sync(act, keep);
+      if (bal == 0u) return;
+      const int leader = __ffs(act) - 1;
+      const int lane = threadIdx.x & 31;
+      int base = 0;
+      if (lane == leader) base = atomicAdd(&s_ncand, __popc(bal));
+      base = __shfl_sync(act, base, leader);
+      if (keep) {
+        const int slot = base + __popc(bal & ((1u << lane) - 1u));
+        if (slot < kSampleCand) {
+          cand_x[slot] = x;
+          cand_i[slot] = i;
+        }
+      }
+    });
+    __syncthreads();
+    const int nc = s_ncand;
+    const bool in_smem = nc <= kSampleCand;
+    auto for_kept = [&](auto f) {   // every kept token (>= thr), from shared memory or the row
+      if (in_smem) {
+        for (int j = threadIdx.x; j < nc; j += blockDim.x)
+          if (cand_x[j] >= thr) f(cand_i[j], cand_x[j]);
+      } else {
+        row_for_each(lg, V, [&](int i, float x) {
+          if (x >= thr && x > -INFINITY) f(i, x);
+        });
+      }
+    };
+    // 4) top-p threshold: largest v with sum_{x >= v} e^(x-m) >= p * Z (bisection)
+    if (topp < 1.f) {
+      float z = 0.f;
+      for_kept([&](int, float x) { z += __expf(x - m); });
+      z = block_reduce(z, sred, SumOp(), 0.f);
+      float lo = thr == -INFINITY ? m - 80.f : thr, hi = m;
+      for (int it = 0; it < 24; ++it) {
+        const float mid = 0.5f * (lo + hi);
+        float sm = 0.f;
+        for_kept([&](int, float x) {
+          if (x >= mid) sm += __expf(x - m);
+        });
+        sm = block_reduce(sm, sred, SumOp(), 0.f);
+        if (sm >= topp * z) lo = mid; else hi = mid;
+      }
+      thr = fmaxf(thr, lo);
+    }
+    // 5) Gumbel-max over the kept set
+    const uint64_t seed = a.seeds ? static_cast<uint64_t>(a.seeds[sr]) : 0x1234ull;
+    const uint64_t step = a.step ? static_cast<uint64_t>(a.step[sr]) : 0ull;
+    best = 0ull;
+    for_kept([&](int i, float x) {
+      const float u = uniform01(seed + 0x9E37ull * step, static_cast<uint64_t>(i));
+      const float gmb = -logf(-logf(u));
+      const unsigned long long k = argmax_key(x + gmb, i);
+      best = k > best ? k : best;
+    });
+    __syncthreads();
     if (threadIdx.x == 0) s_best = 0ull;
     __syncthreads();
     atomicMax(&s_best, best);
     __syncthreads();
-    if (threadIdx.x == 0) {
-      const int tok = static_cast<int>(0xffffffffu - static_cast<uint32_t>(s_best & 0xffffffffull));
-      a.out_tokens[row] = tok;
-      if (a.slot_tokens) a.slot_tokens[sr] = tok;
-      if (a.step) a.step[sr] += 1;
-      if (a.seen) a.seen[static_cast<int64_t>(sr) * a.seen_stride + tok] = 1;
-    }
-    return;
   }
-  float m = -INFINITY;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) m = fmaxf(m, lg[i]);
-  m = block_reduce(m, sred, MaxOp(), -INFINITY);
-  // 2) top-k threshold by 4-pass radix select on order-preserving keys
-  float thr = -INFINITY;
-  const int topk = a.top_k ? a.top_k[sr] : 0;
-  if (topk > 0 && topk < V) {
-    if (threadIdx.x == 0) {
-      s_prefix = 0u;
-      s_kleft = topk;
-    }
-    for (int pass = 0; pass < 4; ++pass) {
-      const int shift = 24 - 8 * pass;
-      const uint32_t mask_hi = pass == 0 ? 0u : (0xffffffffu << (32 - 8 * pass));
-      for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0u;
-      __syncthreads();
-      const uint32_t pref = s_prefix;
-      for (int i = threadIdx.x; i < V; i += blockDim.x) {
-        const uint32_t k = f2key(lg[i]);
-        if ((k & mask_hi) == pref) atomicAdd(&hist[(k >> shift) & 255u], 1u);
-      }
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        int left = s_kleft;
-        int bin = 255;
-        for (; bin > 0; --bin) {
-          const int c = static_cast<int>(hist[bin]);
-          if (c >= left) break;
-          left -= c;
-        }
-        s_kleft = left;
-        s_prefix = pref | (static_cast<uint32_t>(bin) << shift);
-      }
-      __syncthreads();
-    }
-    thr = key2f(s_prefix);
-  }
-  // 3) min-p threshold
-  const float minp = a.min_p ? a.min_p[sr] : 0.f;
-  if (minp > 0.f) thr = fmaxf(thr, m + logf(minp));
-  // 4) top-p threshold: largest v with sum_{x >= v} e^(x-m) >= p * Z (binary search)
-  const float topp = a.top_p ? a.top_p[sr] : 1.f;
-  if (topp < 1.f) {
-    float z = 0.f;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) {
-      const float x = lg[i];
-      if (x >= thr) z += __expf(x - m);
-    }
-    z = block_reduce(z, sred, SumOp(), 0.f);
-    float lo = thr == -INFINITY ? m - 80.f : thr, hi = m;
-    for (int it = 0; it < 24; ++it) {
-      const float mid = 0.5f * (lo + hi);
-      float s = 0.f;
-      for (int i = threadIdx.x; i < V; i += blockDim.x) {
-        const float x = lg[i];
-        if (x >= mid && x >= thr) s += __expf(x - m);
-      }
-      s = block_reduce(s, sred, SumOp(), 0.f);
-      if (s >= topp * z) lo = mid; else hi = mid;
-    }
-    thr = fmaxf(thr, lo);
-  }
-  // 5) Gumbel-max over the kept set
-  const uint64_t seed = a.seeds ? static_cast<uint64_t>(a.seeds[sr]) : 0x1234ull;
-  const uint64_t step = a.step ? static_cast<uint64_t>(a.step[sr]) : 0ull;
-  unsigned long long best = 0ull;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float x = lg[i];
-    if (x >= thr && x > -INFINITY) {
-      const float u = uniform01(seed + 0x9E37ull * step, static_cast<uint64_t>(i));
-      const float gmb = -logf(-logf(u));
-      const unsigned long long key = (static_cast<unsigned long long>(f2key(x + gmb)) << 32) | (0xffffffffu - i);
-      best = key > best ? key : best;
-    }
-  }
-  if (threadIdx.x == 0) s_best = 0ull;
-  __syncthreads();
-  atomicMax(&s_best, best);
-  __syncthreads();
   if (threadIdx.x == 0) {
     int tok = static_cast<int>(0xffffffffu - static_cast<uint32_t>(s_best & 0xffffffffull));
     if (s_best == 0ull) tok = 0;

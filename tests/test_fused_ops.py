@@ -212,3 +212,48 @@ def test_sampling_topk_topp_distribution():
     exp[top.indices] = pk
     assert (emp - exp).abs().max() < 0.04
     assert emp[exp == 0].sum() < 0.01
+
+
+@pytest.mark.gpu
+def test_sampling_topp_large_vocab_candidates():
+    """Top-p alone over a 151936-token row whose mass sits on 100 tokens: the candidates fit in
+    shared memory; the draws follow the renormalised nucleus."""
+    torch.manual_seed(2)
+    V, N, K = 151936, 1500, 100
+    base = torch.full((V,), -60.0)
+    hot = torch.randperm(V)[:K]
+    base[hot] = torch.randn(K) * 1.5
+    logits = base.cuda()[None].repeat(N, 1)
+    st = S.SamplingTensors(temperature=torch.ones(N, device="cuda"), top_p=torch.full((N,), 0.9, device="cuda"),
+                           seeds=torch.arange(N, dtype=torch.int64, device="cuda"),
+                           step=torch.zeros(N, dtype=torch.int32, device="cuda"))
+    tok = S.sample(logits, st).cpu().long()
+    p = torch.softmax(base.double(), -1)
+    ps, order = p.sort(descending=True)
+    keep = (ps.cumsum(0) - ps) < 0.9
+    exp = torch.zeros(V, dtype=torch.float64)
+    exp[order[keep]] = ps[keep] / ps[keep].sum()
+    emp = torch.bincount(tok, minlength=V).double() / N
+    assert emp[exp == 0].sum() == 0
+    assert (emp - exp).abs().max() < 0.05
+
+
+@pytest.mark.gpu
+def test_sampling_topp_flat_row_full_sweep():
+    """A flat 20000-token row leaves more candidates than shared memory holds: top-p and the
+    draw sweep the row; every draw must lie in the nucleus."""
+    torch.manual_seed(3)
+    V, N = 20000, 256
+    base = torch.randn(V) * 0.3
+    logits = base.cuda()[None].repeat(N, 1)
+    st = S.SamplingTensors(temperature=torch.ones(N, device="cuda"), top_p=torch.full((N,), 0.5, device="cuda"),
+                           seeds=torch.arange(N, dtype=torch.int64, device="cuda"),
+                           step=torch.zeros(N, dtype=torch.int32, device="cuda"))
+    tok = S.sample(logits, st).cpu().long()
+    p = torch.softmax(base.double(), -1)
+    ps, order = p.sort(descending=True)
+    keep = (ps.cumsum(0) - ps) < 0.5 + 1e-3     # bisection tolerance at the boundary
+    allowed = torch.zeros(V, dtype=torch.bool)
+    allowed[order[keep]] = True
+    assert bool(allowed[tok].all())
+    assert len(set(tok.tolist())) > N // 3      # draws spread over the nucleus
