@@ -339,9 +339,20 @@ __global__ void moe_scatter_kernel(MoeRouteArgs a) {
   if (threadIdx.x < 32) {
     const int lane = threadIdx.x;
     int carry = 0;
-    for (int base = 0; base < a.experts; base += 32) {
+    // all counts in flight at once (experts <= 512: 16 per lane), then the rounds of the scan
+    constexpr int kRounds = 16;
+    int cnt[kRounds];
+#pragma unroll
+    for (int r = 0; r < kRounds; ++r) {
+      const int e = 32 * r + lane;
+      cnt[r] = e < a.experts ? a.counts[e] : 0;
+    }
+#pragma unroll
+    for (int r = 0; r < kRounds; ++r) {
+      const int base = 32 * r;
+      if (base >= a.experts) break;
       const int e = base + lane;
-      const int c = e < a.experts ? a.counts[e] : 0;
+      const int c = cnt[r];
       int incl = c;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -374,10 +385,25 @@ __global__ void moe_scatter_kernel(MoeRouteArgs a) {
       copy = e >= a.local_e0 && e < a.local_e0 + a.local_el;
     }
     if (copy) {
-      const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.x) +
-                                                        static_cast<int64_t>(i / a.topk) * a.hidden);
-      uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.x_perm) + static_cast<int64_t>(pos) * a.hidden);
-      for (int v = lane; v < a.hidden / 8; v += 32) dst[v] = src[v];
+      const uint4* __restrict__ src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.x) +
+                                                                     static_cast<int64_t>(i / a.topk) * a.hidden);
+      uint4* __restrict__ dst =
+          reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.x_perm) + static_cast<int64_t>(pos) * a.hidden);
+      const int nv = a.hidden / 8;
+      // the whole row in flight (8 vectors per lane per round) before any store
+      for (int v0 = lane; v0 < nv; v0 += 32 * 8) {
+        uint4 buf[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int v = v0 + 32 * u;
+          if (v < nv) buf[u] = __ldg(src + v);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int v = v0 + 32 * u;
+          if (v < nv) dst[v] = buf[u];
+        }
+      }
     }
   }
   if (a.self_clean) {
@@ -428,8 +454,29 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(MoeCombineArgs a) {
     float acc[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-    for (int k = 0; k < a.topk; ++k) {
-      if (s_pos[k] < 0) continue;  // another rank's expert (tensor-parallel MoE)
+    // the first 8 expert rows are loaded together (8 loads in flight), then summed in k order
+    constexpr int kBatch = 8;
+    uint4 rows[kBatch];
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      rows[k] = make_uint4(0u, 0u, 0u, 0u);
+      if (k < a.topk && s_pos[k] >= 0)  // < 0: another rank's expert (tensor-parallel MoE)
+        rows[k] = __ldg(y + static_cast<int64_t>(s_pos[k]) * nvec + v);
+    }
+    uint4 res_v = make_uint4(0u, 0u, 0u, 0u);
+    if (a.residual != nullptr) res_v = static_cast<const uint4*>(a.residual)[static_cast<int64_t>(tok) * nvec + v];
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      if (k < a.topk && s_pos[k] >= 0) {
+        float f[8];
+        unpack8(rows[k], f);
+        const float w = s_w[k];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] += w * f[j];
+      }
+    }
+    for (int k = kBatch; k < a.topk; ++k) {
+      if (s_pos[k] < 0) continue;
       float f[8];
       unpack8(__ldg(y + static_cast<int64_t>(s_pos[k]) * nvec + v), f);
       const float w = s_w[k];
@@ -451,7 +498,7 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(MoeCombineArgs a) {
       uint4* rr = static_cast<uint4*>(a.residual) + static_cast<int64_t>(tok) * nvec + v;
       float r[8];
       unpack8(h, acc);
-      unpack8(*rr, r);
+      unpack8(res_v, r);
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[j] += r[j];
       const uint4 s = pack8(acc);
