@@ -61,6 +61,7 @@ struct DevParams {
   int vec4;              // outputs / bias / residual allow 4-wide vector access (split-K finaliser)
   int pdl_prefetch_a;    // programmatic dependent launch with static weights: prefetch them before the wait
   int cluster_splitk;    // split-K over a thread-block cluster: partials stay in shared memory (DSMEM reduce)
+  int vec8;              // outputs / residual rows allow 16-byte vectors of 8 (staged epilogue)
   int* counters;         // [tiles] arrival counters, zero between calls
   const unsigned long long* peer_out;  // owner scatter: row r -> peer_out[r / rows_per] + r * ldo
   int rows_per;
@@ -146,8 +147,12 @@ struct Cfg {
   static constexpr int kStagesRaw = (200 * 1024) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
   // tiles + 1 KB alignment slack + barriers and the group tables (4 KB + 2 * (kMaxGroups + 1) ints)
-  static constexpr int kAuxBytes = 1024 + 8 * (kMaxGroups + 1) + 512;
-  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kAuxBytes;
+  static constexpr int kAuxBytes = (1024 + 8 * (kMaxGroups + 1) + 512 + 15) / 16 * 16;
+  // wide token tiles stage each 16-token chunk of the epilogue through shared memory (two
+  // [16][128] fp32 buffers) so that outputs leave as 16-byte vectors along the feature axis
+  static constexpr bool kStagedEpi = BN >= 128;
+  static constexpr int kEpiBytes = kStagedEpi ? 2 * 16 * kBM * 4 : 0;
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kAuxBytes + kEpiBytes;
   static_assert(2 * kAccCols <= 512, "accumulators exceed TMEM");
   static_assert(kBBytes % 1024 == 0, "B tile must keep 1024-byte alignment");
 };
@@ -180,6 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
   uint8_t* aux = smem + C::kStages * C::kStageBytes;
+  float* epi = reinterpret_cast<float*>(aux + C::kAuxBytes);   // staged-epilogue buffers
   __shared__ int s_last;  // split-K: this CTA finalises the tile
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(aux);
   uint64_t* empty_bar = full_bar + C::kStages;
@@ -390,6 +396,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     grid_dep_wait();  // residual / output buffers belong to the stream's earlier kernels
     const int lane_base = 32 * (warp & 3);
     int local = 0;
+    int epi_ctr = 0;   // staged chunks so far (alternates the two buffers)
     for (int w = blockIdx.x; w < total_work; w += gridDim.x, ++local) {
       const int t = w / ks;
       int g, mt, nt;
@@ -425,6 +432,62 @@ __global__ void __launch_bounds__(kThreads, 1)
           float* wsp = p.ws + ((static_cast<int64_t>(w - t * ks) * total_tiles + t) * BN + c) * kBM + lane_base + lane;
 #pragma unroll
           for (int j = 0; j < 16; ++j) __stcg(wsp + j * kBM, __uint_as_float(r[j]));
+        } else if (C::kStagedEpi && p.vec8) {
+          // activations per thread (one feature m, 16 tokens), the chunk through shared memory,
+          // then each thread stores two vectors of 8 consecutive features of one token (and adds
+          // the matching 16-byte residual vectors).  One named barrier per chunk: a buffer is
+          // rewritten two chunks later, after every thread has passed the barrier in between.
+          float* stg = epi + (epi_ctr & 1) * (16 * kBM);
+          ++epi_ctr;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            float v = __uint_as_float(r[j]);
+            if (GATED) {
+              v = silu_f(v) * __uint_as_float(u[j]);
+            } else {
+              v += bias_v;
+              if (ACT) {
+                if (p.act == kActGeluTanh) v = gelu_tanh_f(v);
+                else if (p.act == kActGeluErf) v = gelu_erf_f(v);
+                else if (p.act == kActSilu) v = silu_f(v);
+              }
+            }
+            stg[j * kBM + lane_base + lane] = v;
+          }
+          asm volatile("bar.sync 2, 128;" ::: "memory");
+          const int tid = static_cast<int>(threadIdx.x) - 64;
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const int idx = tid + 128 * q;          // 16 tokens x 16 groups of 8 features
+            const int tok = idx >> 4, cg = (idx & 15) * 8;
+            const int row = row0 + c + tok;
+            const int mm = mt * kBM + cg;
+            if (row < row_end && mm < p.m_out) {
+              const float4 a0 = *reinterpret_cast<const float4*>(stg + tok * kBM + cg);
+              const float4 a1 = *reinterpret_cast<const float4*>(stg + tok * kBM + cg + 4);
+              float o[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+              if (p.residual != nullptr) {
+                const uint4 rv = *reinterpret_cast<const uint4*>(p.residual + static_cast<int64_t>(row) * p.ldr + mm);
+                const __nv_bfloat162* rh = reinterpret_cast<const __nv_bfloat162*>(&rv);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  o[2 * j] += __low2float(rh[j]);
+                  o[2 * j + 1] += __high2float(rh[j]);
+                }
+              }
+              if (p.out_f32) {
+                float* dst = static_cast<float*>(p.out) + static_cast<int64_t>(row) * p.ldo + mm;
+                reinterpret_cast<float4*>(dst)[0] = make_float4(o[0], o[1], o[2], o[3]);
+                reinterpret_cast<float4*>(dst)[1] = make_float4(o[4], o[5], o[6], o[7]);
+              } else {
+                uint4 ov;
+                __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&ov);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) oh[j] = __floats2bfloat162_rn(o[2 * j], o[2 * j + 1]);
+                *reinterpret_cast<uint4*>(out_row_bf16(p, row) + mm) = ov;
+              }
+            }
+          }
         } else if (m_ok) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
@@ -687,6 +750,8 @@ cudaError_t launch(const GemmArgs& a, cudaStream_t stream) {
     const int ob = a.out_f32 ? 16 : 8;
     p.vec4 = (a.m_out % 4 == 0) && (a.ldo % 4 == 0) && al(a.out, ob) && (a.bias == nullptr || al(a.bias, 8)) &&
              (a.residual == nullptr || (a.ldr % 4 == 0 && al(a.residual, 8))) ? 1 : 0;
+    p.vec8 = (a.m_out % 8 == 0) && (a.ldo % 8 == 0) && al(a.out, 16) &&
+             (a.residual == nullptr || (a.ldr % 8 == 0 && al(a.residual, 16))) ? 1 : 0;
   }
   p.counters = nullptr;
   p.peer_out = a.peer_out;

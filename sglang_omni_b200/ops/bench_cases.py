@@ -154,6 +154,16 @@ def _time_cases() -> None:
         "router 128x2048 T64 fp32": (t(lambda: L.linear(x, wr, out_dtype=torch.float32)), wr.numel() * 2),
         "lm_head 151936x2048 T64 fp32": (t(lambda: L.linear(x, wl, out_dtype=torch.float32)), wl.numel() * 2),
     }
+    import torch.nn.functional as F
+    flops = {}
+    xp = torch.randn(8192, 2048, device="cuda").bfloat16()
+    xo = torch.randn(8192, 4096, device="cuda").bfloat16()
+    for name, (xx, ww) in {"qkv prefill 8192x2048 -> 5120": (xp, wq), "o_proj prefill 8192x4096 -> 2048": (xo, wo)}.items():
+        f = 2.0 * xx.shape[0] * xx.shape[1] * ww.shape[0]
+        flops[name] = (t(lambda: L.linear(xx, ww)), f)
+        flops[name + " (cuBLAS)"] = (t(lambda: F.linear(xx, ww)), f)
+    for name, (us, f) in flops.items():
+        print(f"{name:40s} {us:8.2f} us  {f / us / 1e6:7.1f} TFLOP/s")
     B, hq, hkv, d, ctx = 64, 32, 4, 128, 1152
     pages = (ctx + 63) // 64
     k = torch.randn(B * pages + 1, hkv, 64, d, device="cuda").bfloat16()

@@ -144,3 +144,17 @@ def test_static_weight_prefetch(gated, rows, n, k):
     torch.cuda.synchronize()
     _ext.check_status(x.device)
     _close(y, ref)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("rows,n,k,f32", [(300, 512, 256, True), (1000, 1152, 512, False), (130, 264, 128, False)])
+def test_wide_tile_staged_epilogue(rows, n, k, f32):
+    """Token tiles of 128 / 256 stage the epilogue through shared memory (16-byte stores):
+    fp32 and bf16 outputs, bias + residual, partial last token tiles and feature tiles."""
+    torch.manual_seed(rows + n)
+    x = torch.randn(rows, k, device="cuda").bfloat16()
+    w = (torch.randn(n, k, device="cuda") * 0.05).bfloat16()
+    b = torch.randn(n, device="cuda").bfloat16()
+    r = None if f32 else torch.randn(rows, n, device="cuda").bfloat16()
+    y = L.linear(x, w, bias=b, residual=r, out_dtype=torch.float32 if f32 else None)
+    _close(y, L.linear_ref(x, w, b, r, None, torch.float32), 1e-2 if f32 else 2e-2)
