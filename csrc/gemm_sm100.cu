@@ -150,7 +150,7 @@ struct Cfg {
   static constexpr int kAuxBytes = (1024 + 8 * (kMaxGroups + 1) + 512 + 15) / 16 * 16;
   // wide token tiles stage each 16-token chunk of the epilogue through shared memory (two
   // [16][128] fp32 buffers) so that outputs leave as 16-byte vectors along the feature axis
-  static constexpr bool kStagedEpi = BN >= 128;
+  static constexpr bool kStagedEpi = BN >= 64;
   static constexpr int kEpiBytes = kStagedEpi ? 2 * 16 * kBM * 4 : 0;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kAuxBytes + kEpiBytes;
   static_assert(2 * kAccCols <= 512, "accumulators exceed TMEM");
