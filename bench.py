@@ -48,6 +48,9 @@ def parse():
     ap.add_argument("--s2pro-streams", type=int, default=64)
     ap.add_argument("--s2pro-audio-s", type=float, default=15.0)
     ap.add_argument("--thinker", type=int, default=1, help="run the thinker serving phase (headline value)")
+    ap.add_argument("--vision", type=int, default=1, help="also measure image+text -> text serving")
+    ap.add_argument("--vision-requests", type=int, default=64)
+    ap.add_argument("--vision-tokens", type=int, default=128)
     ap.add_argument("--ep", type=int, default=1,
                     help="N>1: experts sharded over the GPUs (expert parallel MoE over NVLink, data-parallel "
                          "attention); 0: one full replica per GPU")
@@ -107,6 +110,54 @@ def speech_phase(args, dev, rank):
             wall = time.perf_counter() - t0
             ttfa = sorted(r[0] for r in res if r[0] is not None)
             return (1e3 * statistics.median(ttfa) if ttfa else None, sum(r[1] for r in res) / wall, n * 4)
+
+    return asyncio.run(run())
+
+
+def vision_phase(args, dev, rank):
+    """Qwen3-Omni image + text -> text through the public Client API: N concurrent
+    requests, each one 448 x 448 RGB image of uniform uint8 pixels (vision tower:
+    27 layers, patch 16, 2 x 2 merge -> 196 image tokens) plus ~128 random prompt
+    tokens, 128 greedy output tokens.  Returns (output tok/s, TTFT p50 ms, image bytes in)."""
+    import asyncio
+
+    import numpy as np
+
+    from sglang_omni_b200.client import Client, GenerateRequest, SamplingParams
+    from sglang_omni_b200.config import PipelineRunner, compile_pipeline
+    from sglang_omni_b200.models.qwen3_omni.config import Qwen3OmniPipelineConfig, text_stages
+
+    cfg = Qwen3OmniPipelineConfig(model_path="random", stages=text_stages(
+        device=str(dev), max_batch=args.vision_requests, max_context=2048))
+    rng = np.random.default_rng(11 + rank)
+    imgs = [rng.integers(0, 256, (448, 448, 3), dtype=np.uint8) for _ in range(args.vision_requests)]
+    letters = "abcdefghijklmnopqrstuvwxyz"
+    prompts = ["".join(rng.choice(list(letters), 128)) for _ in range(args.vision_requests)]
+
+    async def run():
+        coord, stages = compile_pipeline(cfg)
+        async with PipelineRunner(coord, stages):
+            client = Client(coord)
+
+            async def one(i, tag):
+                t0 = time.perf_counter()
+                req = GenerateRequest(prompt=prompts[i], images=[imgs[i]], max_tokens=args.vision_tokens,
+                                      sampling=SamplingParams(temperature=0.0, ignore_eos=True), stream=True,
+                                      request_id=f"{tag}-{rank}-{i}")
+                first, ntok = None, 0
+                async for ch in client.generate(req):
+                    if ch.token_ids:
+                        if first is None:
+                            first = time.perf_counter() - t0
+                        ntok += len(ch.token_ids)
+                return first, ntok
+
+            await asyncio.gather(*[one(i, "vw") for i in range(min(4, args.vision_requests))])
+            t0 = time.perf_counter()
+            res = await asyncio.gather(*[one(i, "v") for i in range(args.vision_requests)])
+            wall = time.perf_counter() - t0
+            ttft = sorted(r[0] for r in res if r[0] is not None)
+            return sum(r[1] for r in res) / wall, (1e3 * statistics.median(ttft) if ttft else None)
 
     return asyncio.run(run())
 
@@ -292,6 +343,9 @@ def main():
         if args.speech:
             ttfa_ms, speech_tok_s, _ = speech_phase(args, dev, rank)
             line.update(ttfa_p50_ms=ttfa_ms, speech_text_tok_s=speech_tok_s, streams=args.speech_streams)
+        if args.vision:
+            v_tok_s, v_ttft = vision_phase(args, dev, rank)
+            line.update(vision_tok_s=v_tok_s, vision_ttft_p50_ms=v_ttft, vision_requests=args.vision_requests)
         if args.s2pro:
             a, b, c = s2pro_phase(args, dev, rank)
             line.update(s2pro_ttfa_p50_ms=a, s2pro_rtf=b, s2pro_audio_s_per_s=c, s2pro_streams=args.s2pro_streams)
@@ -387,6 +441,21 @@ def main():
             tt = torch.tensor([ttfa_ms or 0.0], dtype=torch.float64, device=dev)
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             ttfa_ms = float(tt[0])
+    vis = None
+    if args.vision and args.layers == 48:
+        v_tok_s, v_ttft = vision_phase(args, dev, rank)
+        t = torch.tensor([v_tok_s or 0.0, v_ttft or 0.0], dtype=torch.float64, device=dev)
+        if world > 1:
+            sm = t.clone()
+            dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+            mx = t.clone()
+            dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+            v_tok_s, v_ttft = float(sm[0]), float(mx[1])
+        vis = {"requests_per_gpu": args.vision_requests, "image": "448x448 uniform uint8 RGB (196 image tokens)",
+               "prompt_tokens": 128, "output_tokens": args.vision_tokens,
+               "output_tok_s": None if v_tok_s is None else round(v_tok_s, 2),
+               "ttft_p50_ms": None if v_ttft is None else round(v_ttft, 2),
+               "timing": "host wall clock through Client.generate (stream=True), whole job; TTFT max over ranks"}
     s2 = None
     if args.s2pro and args.layers == 48:
         a, b, c = s2pro_phase(args, dev, rank)
@@ -441,6 +510,7 @@ def main():
                               "max over ranks"},
             },
             "ttfa_p50_ms": None if ttfa_ms is None else round(ttfa_ms, 2),
+            "vision_image_text": vis,
             "s2pro_tts": s2,
             "e2e": {"value": round(e2e, 2), "unit": "output tokens/s, host wall clock through AREngine.generate",
                     "h2d_bytes_per_step": int(args.requests * args.prompt_len * 4),

@@ -187,18 +187,37 @@ def create_audio_encoder_executor(model_path: str = "", device: str = "cuda:0", 
 
 def create_image_encoder_executor(model_path: str = "", device: str = "cuda:0", max_batch_size: int = 32,
                                   overrides: dict | None = None):
-    def run(payload: StagePayload) -> StagePayload:
-        images = (payload.data or {}).get("images") or []
-        if not images:
-            return StagePayload(payload.request_id, payload.request, {"image_embeds": None})
-        from ..vision_encoder import encode_images
+    """The vision tower over a gathered burst of requests: one forward for every image of
+    the batch (ragged attention keeps images apart), split back per request."""
+    from ..vision_encoder import encode_images
 
-        out = encode_images(model_path, torch.device(device), images, overrides)
-        if torch.device(device).type == "cuda":
-            torch.cuda.current_stream().synchronize()  # the thinker reads these on its own stream
+    dev = torch.device(device)
+
+    def encode(inputs: dict) -> list:
+        per_req = inputs["images"]
+        flat = [im for ims in per_req for im in ims]
+        out = encode_images(model_path, dev, flat, overrides) if flat else None
+        res, i = [], 0
+        for ims in per_req:
+            n = len(ims)
+            res.append({"image_embeds": out["image_embeds"][i:i + n],
+                        "deepstack": [d[i:i + n] for d in out["deepstack"]],
+                        "image_grids": out["image_grids"][i:i + n]})
+            i += n
+        return res
+
+    engine = create_encoder_engine(encode, max_batch_size=max_batch_size, device=dev, cache_size=0)
+
+    def request_builder(payload: StagePayload):
+        images = (payload.data or {}).get("images") or []
+        return EncoderRequestData(inputs={"images": images}, skip=not images)
+
+    def result_builder(payload: StagePayload, out):
+        if not isinstance(out, dict):  # skipped request (no image)
+            out = {"image_embeds": None}
         return StagePayload(payload.request_id, payload.request, out)
 
-    return PreprocessingExecutor(run)
+    return EngineExecutor(engine, request_builder, result_builder)
 
 
 def create_aggregate_executor(**_):

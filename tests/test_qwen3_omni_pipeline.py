@@ -125,3 +125,39 @@ def test_speech_pipeline_gpu_end_to_end():
                 assert final.audio_data is not None and len(final.audio_data) > 0
 
     asyncio.run(main())
+
+
+def test_image_text_pipeline_batched_encoder_cpu():
+    """Image + text -> text: requests with and without images arrive together; the image
+    encoder stage runs the gathered images in one forward and splits the outputs back."""
+    from sglang_omni_b200.models.qwen3_omni.config import Qwen3OmniPipelineConfig
+
+    ov = dict(TINY, vision={"depth": 2, "hidden_size": 32, "num_heads": 2, "intermediate_size": 64,
+                            "patch_size": 4, "out_hidden_size": 64, "num_position_embeddings": 64,
+                            "deepstack_visual_indexes": [0], "dtype": torch.float32})
+    cfg = Qwen3OmniPipelineConfig(model_path="random", stages=text_stages(overrides=ov, device="cpu", max_batch=4,
+                                                                           max_context=1024))
+
+    async def main():
+        coord, stages = compile_pipeline(cfg)
+        async with PipelineRunner(coord, stages):
+            client = Client(coord)
+            rng = np.random.default_rng(1)
+            imgs = [rng.integers(0, 256, (16, 24, 3), dtype=np.uint8), rng.integers(0, 256, (8, 8, 3), dtype=np.uint8)]
+
+            async def one(req):
+                last = None
+                async for ch in client.generate(req):
+                    last = ch
+                return last
+
+            reqs = [GenerateRequest(prompt="what is this", images=[imgs[0]], max_tokens=4, stream=False,
+                                    sampling=SamplingParams(temperature=0.0, ignore_eos=True)),
+                    GenerateRequest(prompt="and this", images=[imgs[1], imgs[0]], max_tokens=3, stream=False,
+                                    sampling=SamplingParams(temperature=0.0, ignore_eos=True)),
+                    GenerateRequest(prompt="text only", max_tokens=5, stream=False,
+                                    sampling=SamplingParams(temperature=0.0, ignore_eos=True))]
+            return await asyncio.gather(*[one(r) for r in reqs])
+
+    outs = asyncio.run(main())
+    assert [len(o.token_ids) for o in outs] == [4, 3, 5]
