@@ -85,12 +85,28 @@ __global__ void __launch_bounds__(256) qkv_rope_store_kernel(RopeStoreArgs a) {
   // Lane owns elements e = lane + 32 * i (i < PER).  For neox rotation the
   // partner of e is e +- rot/2; we load the whole row into registers via
   // shared-free shuffles by owning both halves: element index mapping below.
+  // Every load this warp needs is issued before the first use (two dependent round trips:
+  // row / norm weights / positions, then the cos / sin table entries).
   float x[PER];
 #pragma unroll
   for (int i = 0; i < PER; ++i) x[i] = __bfloat162float(row[lane + 32 * i]);
+  const __nv_bfloat16* nw = is_v ? nullptr
+                                 : (is_q ? static_cast<const __nv_bfloat16*>(a.q_norm)
+                                         : static_cast<const __nv_bfloat16*>(a.k_norm));
+  float wn[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) wn[i] = nw != nullptr ? __bfloat162float(nw[lane + 32 * i]) : 1.f;
+  int pos3[3] = {0, 0, 0};
+  if (!is_v && a.rot_dim > 0) {
+    if (a.pos_rows == 3) {
+      pos3[0] = a.positions[tok];
+      pos3[1] = a.positions[a.tokens + tok];
+      pos3[2] = a.positions[2 * a.tokens + tok];
+    } else {
+      pos3[0] = pos3[1] = pos3[2] = a.positions[tok];
+    }
+  }
   if (!is_v) {
-    const __nv_bfloat16* nw = is_q ? static_cast<const __nv_bfloat16*>(a.q_norm)
-                                   : static_cast<const __nv_bfloat16*>(a.k_norm);
     if (nw != nullptr) {
       float ss = 0.f;
 #pragma unroll
@@ -98,18 +114,10 @@ __global__ void __launch_bounds__(256) qkv_rope_store_kernel(RopeStoreArgs a) {
       ss = warp_sum(ss);
       const float rstd = rsqrtf(ss / D + a.eps);
 #pragma unroll
-      for (int i = 0; i < PER; ++i) x[i] = bf16r(bf16r(x[i] * rstd) * __bfloat162float(nw[lane + 32 * i]));
+      for (int i = 0; i < PER; ++i) x[i] = bf16r(bf16r(x[i] * rstd) * wn[i]);
     }
     if (a.rot_dim > 0) {
       const int half = a.rot_dim / 2;
-      int pos3[3];
-      if (a.pos_rows == 3) {
-        pos3[0] = a.positions[tok];
-        pos3[1] = a.positions[a.tokens + tok];
-        pos3[2] = a.positions[2 * a.tokens + tok];
-      } else {
-        pos3[0] = pos3[1] = pos3[2] = a.positions[tok];
-      }
       float y[PER];
       // Partner of element e = lane + 32 i: neox with half % 32 == 0 -> same
       // lane, register i +- half/32; neox otherwise -> through this warp's

@@ -1,0 +1,139 @@
+"""Timing of the fused compute + collective paths against their NCCL baselines and rooflines.
+
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 -m sglang_omni_b200.parallel.bench_fused
+
+One process per GPU.  Every time is CUDA-event device time on the launching stream
+after warm-up, averaged over ``--iters`` iterations, the max over ranks.
+
+* TP reduce point (the thinker's o_proj at TP=N): the o_proj GEMM whose epilogue
+  stores every output row into its owner rank's partial slot (NVLink stores from
+  the GEMM) + the reduce / residual / RMSNorm / all-gather kernel, against the
+  NCCL baseline (plain GEMM, ``all_reduce``, RMSNorm).  Roofline: the slower of
+  the GEMM FLOPs at the measured sustained bf16 rate and the bytes each GPU must
+  send (its (N-1)/N partial rows + (N-1) copies of its normalised owned rows) at
+  the measured 770 GB/s per direction.
+* EP MoE layer (128 experts, top-8, hidden 2048, expert width 768 at EP=N): router,
+  count exchange, dispatch straight into the owners' expert-major buffers, the
+  local grouped GEMMs, combine back to the source slots and the top-k weighted
+  sum.  Roofline: the slower of this rank's expert weights at the measured HBM
+  copy rate and the dispatched + combined rows at 770 GB/s.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+import torch.distributed as dist
+
+HBM_GBS = 6546.9          # measured copy bandwidth (B200)
+BF16_TFLOPS = 1395.6      # measured sustained cuBLAS bf16
+NVLINK_GBS = 770.0        # measured peer copy per direction
+
+
+def _time(fn, iters: int) -> float:
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([a.elapsed_time(b) / iters * 1e3], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t[0])
+
+
+def tp_reduce_point(T: int, iters: int, rank: int, world: int) -> dict:
+    from ..ops import gemm, norm
+    from .tp import TPGroup
+
+    H, K = 2048, 4096 // world            # o_proj columns of this rank's heads
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device=dev).manual_seed(rank)
+    x = torch.randn(T, K, device=dev, generator=g).bfloat16()
+    w = (torch.randn(H, K, device=dev, generator=g) * 0.02).bfloat16()
+    nw = torch.ones(H, device=dev).bfloat16()
+    res = torch.randn(T, H, device=dev, generator=g).bfloat16()
+    tp = TPGroup(H, T, dev)
+    part = torch.empty(T, H, device=dev, dtype=torch.bfloat16)
+
+    def fused():
+        # the producer GEMM waits (in its TMA thread) for every owner's previous all-gather
+        # phase before overwriting their partial slots, as the decoder's GEMMs do
+        with gemm.static_weights():
+            gemm.linear(x, w, out=tp.part_local[:T], scatter=tp.scatter(T), wait=tp.wait)
+        tp.reduce_norm(res, nw, 1e-6, T)
+
+    def nccl():
+        gemm.linear(x, w, out=part)
+        dist.all_reduce(part)
+        norm.rms_norm(part, nw, 1e-6, residual=res)
+
+    t_f = _time(fused, iters)
+    t_n = _time(nccl, iters)
+    tp.close()
+    flops = 2.0 * T * K * H
+    send = T * H * 2 * (world - 1) / world * 2          # partial rows out + normalised rows to every peer
+    roof = max(flops / (BF16_TFLOPS * 1e6), send / (NVLINK_GBS * 1e3))
+    return {"path": "TP o_proj GEMM -> reduce-scatter + residual + RMSNorm + all-gather", "tokens": T,
+            "fused_us": round(t_f, 2), "nccl_us": round(t_n, 2), "roofline_us": round(roof, 2),
+            "fused_frac_of_roofline": round(roof / t_f, 3), "speedup_vs_nccl": round(t_n / t_f, 3)}
+
+
+def ep_moe_layer(T: int, iters: int, rank: int, world: int) -> dict:
+    from .ep_moe import EPMoE
+
+    E, topk, H, I = 128, 8, 2048, 768
+    El = E // world
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device=dev).manual_seed(rank)
+    x = torch.randn(T, H, device=dev, generator=g).bfloat16()
+    wr = (torch.randn(E, H, device=dev, generator=torch.Generator(device=dev).manual_seed(0)) * 0.02).bfloat16()
+    w13 = (torch.randn(El, 2 * I, H, device=dev, generator=g) * 0.02).bfloat16()
+    w2 = (torch.randn(El, H, I, device=dev, generator=g) * 0.02).bfloat16()
+    ep = EPMoE(E, topk, H, I, max_tokens=T, device=dev)
+    out = torch.empty_like(x)
+    t_f = _time(lambda: ep.forward(x, wr, w13, w2, out=out), iters)
+    ep.close()
+    wbytes = El * 3 * H * I * 2
+    rows = T * topk * (world - 1) / world                 # (token, k) rows that leave this rank
+    link = rows * H * 2 * 2                                # dispatched and combined back
+    roof = max(wbytes / (HBM_GBS * 1e3), link / (NVLINK_GBS * 1e3))
+    return {"path": "EP MoE layer: count exchange + dispatch into owners' expert buffers + grouped GEMMs + "
+                    "combine + top-k sum", "tokens_per_rank": T, "fused_us": round(t_f, 2),
+            "roofline_us": round(roof, 2), "fused_frac_of_roofline": round(roof / t_f, 3)}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--iters", type=int, default=20)
+    args = ap.parse_args()
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    from datetime import timedelta
+
+    dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=timedelta(seconds=300))
+    rank, world = dist.get_rank(), dist.get_world_size()
+    from ..ops import _ext
+
+    _ext.ext()
+    rows = []
+    for T in (64, 8192):
+        rows.append(tp_reduce_point(T, args.iters, rank, world))
+    for T in (64, 2048):
+        rows.append(ep_moe_layer(T, args.iters, rank, world))
+    _ext.check_status(torch.device("cuda", local))
+    if rank == 0:
+        for r in rows:
+            print(json.dumps({"world": world, **r}))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
