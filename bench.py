@@ -109,6 +109,9 @@ def speech_phase(args, dev, rank):
             res = await asyncio.gather(*[one(i, "s") for i in range(args.speech_streams)])
             wall = time.perf_counter() - t0
             ttfa = sorted(r[0] for r in res if r[0] is not None)
+            from sglang_omni_b200.utils import trace
+            if trace.ENABLED and rank == 0:   # OMNI_TRACE=1: median stage timeline of the measured streams
+                print(json.dumps({"speech_stage_timeline_ms": trace.summary(f"s-{rank}-")}), file=sys.stderr)
             return (1e3 * statistics.median(ttfa) if ttfa else None, sum(r[1] for r in res) / wall, n * 4)
 
     return asyncio.run(run())

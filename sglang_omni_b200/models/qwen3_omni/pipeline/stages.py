@@ -38,6 +38,7 @@ from ....executors import EngineExecutor, PreprocessingExecutor
 from ....executors.interface import Executor, ResultQueueMixin
 from ....executors.preprocessing_executor import StageError
 from ....ops.mel import LogMel
+from ....utils import trace
 from ....proto import StagePayload
 from ....utils.hostdev import adopt, h2d, own_stream
 from ...common.ar_stage import sampling_for
@@ -123,6 +124,7 @@ def create_preprocessing_executor(model_path: str = "", overrides: dict | None =
     unit = vcfg.patch_size * vcfg.spatial_merge_size
 
     def preprocess(payload: StagePayload) -> StagePayload:
+        trace.mark(payload.request_id, "0_preprocess_start")
         inp = payload.request.inputs if isinstance(payload.request.inputs, dict) else {}
         waves = [_load_audio(a) for a in (inp.get("audios") or [])]
         counts = [audio_tokens(w.numel()) for w in waves]
@@ -163,7 +165,7 @@ def create_audio_encoder_executor(model_path: str = "", device: str = "cuda:0", 
     def encode(inputs: dict) -> list:
         per_req = inputs["waves"]
         flat = [w for ws in per_req for w in ws]
-        mels = [mel(w.to(dev)) for w in flat]
+        mels = mel.batch(flat) if flat else []
         outs = enc(mels) if mels else []
         res, i = [], 0
         for ws in per_req:
@@ -174,12 +176,14 @@ def create_audio_encoder_executor(model_path: str = "", device: str = "cuda:0", 
     engine = create_encoder_engine(encode, max_batch_size=max_batch_size, device=dev, cache_size=0)
 
     def request_builder(payload: StagePayload):
+        trace.mark(payload.request_id, "0b_audio_encoder_queued")
         waves = (payload.data or {}).get("audio_waveforms") or []
         return EncoderRequestData(inputs={"waves": waves}, skip=not waves)
 
     def result_builder(payload: StagePayload, out):
         if not isinstance(out, dict):  # skipped request (no audio)
             out = {"audio_embeds": None}
+        trace.mark(payload.request_id, "1_audio_encoded")
         return StagePayload(payload.request_id, payload.request, out)
 
     return EngineExecutor(engine, request_builder, result_builder)
@@ -248,6 +252,7 @@ def create_thinker_executor(model_path: str = "", device: str = "cuda:0", max_ba
 
     def request_builder(payload: StagePayload) -> ARRequest:
         d = payload.data
+        trace.mark(payload.request_id, "1b_thinker_queued")
         sp = sampling_for(payload, "thinker")
         ids = list(d["prompt_token_ids"])
         req = ARRequest(rid=payload.request_id, prompt_ids=ids, sampling=sp,
@@ -301,6 +306,7 @@ def create_thinker_executor(model_path: str = "", device: str = "cuda:0", max_ba
 
     def stream_builder(payload: StagePayload, chunk):
         token, _ = chunk
+        trace.mark(payload.request_id, "2_thinker_first_token")
         d = detoks.get(payload.request_id)
         text = d.push(token) if d is not None else ""
         return {"modality": "text", "token_ids": [int(token)], "text": text}
@@ -445,6 +451,7 @@ class TalkerStreamingExecutor(ResultQueueMixin, Executor):
                 self._finish(s.rid, frames=s.frames)
                 self.gen.remove(s.rid)
             else:
+                trace.mark(s.rid, "3_talker_first_frame")
                 self._stream_fn(s.rid, {"codes": c}, self.code_target)
 
     def _loop_body(self):
@@ -598,6 +605,7 @@ class Code2WavStreamingExecutor(ResultQueueMixin, Executor):
                     continue
                 now = time.perf_counter()
                 for r, wav in out.items():
+                    trace.mark(r, "4_first_audio_chunk")
                     a = wav.float().cpu().numpy()
                     if r in self._audio:
                         self._audio[r].append(a)

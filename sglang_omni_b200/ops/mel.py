@@ -78,26 +78,51 @@ class LogMel:
 
     def __call__(self, audio: torch.Tensor) -> torch.Tensor:
         """audio: float [N] at 16 kHz -> log-mel [n_mels, N // 160]."""
-        audio = audio.to(self.device, torch.float32)
         if self.device.type != "cuda":
+            audio = audio.to(self.device, torch.float32)
             st = torch.stft(audio, N_FFT, HOP, window=self.window, return_complex=True)
             mag = st[..., :-1].abs() ** 2
             mel = self.filters @ mag
-        else:
-            x = torch.nn.functional.pad(audio[None, None], (N_FFT // 2, N_FFT // 2), mode="reflect")[0, 0]
-            frames = x.unfold(0, N_FFT, HOP)[:-1]  # [T, 400]
-            # scale into bf16 range well away from underflow, undo after squaring
-            scale = float(frames.abs().max().clamp_min(1e-8))
-            f = frames / scale
-            f_hi = f.to(torch.bfloat16)
-            f_lo = (f - f_hi.float()).to(torch.bfloat16)
-            spec = linear(torch.cat([f_hi, f_hi, f_lo], 1).contiguous(), self.basis, out_dtype=torch.float32)
-            re, im = spec[:, :201], spec[:, 201:402]
-            power = (re * re + im * im) * (scale * scale)  # [T, 201]
-            p = torch.zeros(power.shape[0], 208, dtype=torch.float32, device=self.device)
-            p[:, :201] = power
-            pmax = float(p.max().clamp_min(1e-20))
-            mel = linear((p / pmax).to(torch.bfloat16), self.fb, out_dtype=torch.float32).t() * pmax
-        log_spec = torch.clamp(mel, min=1e-10).log10()
-        log_spec = torch.maximum(log_spec, log_spec.max() - 8.0)
-        return (log_spec + 4.0) / 4.0
+            log_spec = torch.clamp(mel, min=1e-10).log10()
+            log_spec = torch.maximum(log_spec, log_spec.max() - 8.0)
+            return (log_spec + 4.0) / 4.0
+        return self.batch([audio])[0]
+
+    def batch(self, audios: list[torch.Tensor]) -> list[torch.Tensor]:
+        """Log-mel of several waveforms with one DFT GEMM and one mel GEMM over all their
+        frames.  The bf16 range scales (frame peak before the DFT, power peak before the
+        mel projection) are per waveform and stay on the device: no host round trip."""
+        if self.device.type != "cuda":
+            return [self(a) for a in audios]
+        frames, counts = [], []
+        for a in audios:
+            a = a.to(self.device, torch.float32, non_blocking=True)
+            x = torch.nn.functional.pad(a[None, None], (N_FFT // 2, N_FFT // 2), mode="reflect")[0, 0]
+            fr = x.unfold(0, N_FFT, HOP)[:-1]  # [T, 400]
+            frames.append(fr)
+            counts.append(fr.shape[0])
+        fa = torch.cat(frames, 0)
+        cnt = torch.tensor(counts, device=self.device)
+
+        def per_wave_peak(t):   # [rows, ...] -> [rows, 1]: the peak of each row's waveform
+            peaks = torch.stack([seg.abs().amax() for seg in torch.split(t, counts)])
+            return torch.repeat_interleave(peaks.clamp_min(1e-20), cnt)[:, None]
+
+        # scale into bf16 range well away from underflow, undo after squaring
+        scale = per_wave_peak(fa).clamp_min(1e-8)
+        f = fa / scale
+        f_hi = f.to(torch.bfloat16)
+        f_lo = (f - f_hi.float()).to(torch.bfloat16)
+        spec = linear(torch.cat([f_hi, f_hi, f_lo], 1).contiguous(), self.basis, out_dtype=torch.float32)
+        re, im = spec[:, :201], spec[:, 201:402]
+        power = (re * re + im * im) * (scale * scale)  # [T, 201]
+        p = torch.zeros(power.shape[0], 208, dtype=torch.float32, device=self.device)
+        p[:, :201] = power
+        pmax = per_wave_peak(p)
+        mel = linear((p / pmax).to(torch.bfloat16), self.fb, out_dtype=torch.float32) * pmax   # [T, n_mels]
+        out = []
+        for m in torch.split(mel, counts):
+            log_spec = torch.clamp(m.t(), min=1e-10).log10()
+            log_spec = torch.maximum(log_spec, log_spec.max() - 8.0)
+            out.append((log_spec + 4.0) / 4.0)
+        return out

@@ -76,6 +76,20 @@ def test_logmel_gpu_matches_stft():
 
 
 @pytest.mark.gpu
+def test_logmel_batch_matches_single():
+    """One batched call over waveforms of different lengths and loudness equals the per-waveform
+    oracle (each waveform keeps its own bf16 range scales)."""
+    torch.manual_seed(1)
+    audios = [torch.randn(16000 * 2) * 0.1, torch.randn(12345) * 3.0, torch.randn(4000) * 1e-3]
+    outs = LogMel(128, "cuda").batch(audios)
+    cpu = LogMel(128, "cpu")
+    for a, o in zip(audios, outs):
+        ref = cpu(a)
+        assert o.shape == ref.shape
+        assert (o.cpu() - ref).abs().max() < 0.05
+
+
+@pytest.mark.gpu
 def test_audio_encoder_gpu_matches_cpu():
     cfg = AudioEncoderConfig(num_mel_bins=128, encoder_layers=2, encoder_attention_heads=4, encoder_ffn_dim=512,
                              d_model=256, downsample_hidden_size=64, output_dim=128)
