@@ -147,17 +147,17 @@ class Qwen3OmniAudioEncoder(nn.Module):
         cfg = self.cfg
         dev = self.conv1_w.device
         cs = 2 * cfg.n_window
-        chunks, valid = [], []
+        # every mel cut into chunks of cs frames (the last one zero padded): one pad + view per
+        # request instead of one slice per chunk
+        parts, valid = [], []
         for m in mels:
             T = m.shape[1]
-            for s in range(0, T, cs):
-                c = m[:, s:s + cs]
-                valid.append(cnn_out_len(c.shape[1]))
-                if c.shape[1] < cs:
-                    c = torch.nn.functional.pad(c, (0, cs - c.shape[1]))
-                chunks.append(c)
-        N = len(chunks)
-        x = torch.stack(chunks, 0).to(dev, cfg.dtype).unsqueeze(-1).contiguous()  # [N, mel, cs, 1]
+            nc = (T + cs - 1) // cs
+            mp = torch.nn.functional.pad(m, (0, nc * cs - T)) if nc * cs != T else m
+            parts.append(mp.reshape(m.shape[0], nc, cs).permute(1, 0, 2))
+            valid += [cnn_out_len(cs)] * (T // cs) + ([cnn_out_len(T % cs)] if T % cs else [])
+        N = len(valid)
+        x = torch.cat(parts, 0).to(dev, cfg.dtype).unsqueeze(-1).contiguous()  # [N, mel, cs, 1]
         if x.is_cuda:
             x = torch.nn.functional.pad(x, (0, 7))  # channel pad to 8 for 16-byte rows
             w1 = torch.nn.functional.pad(self.conv1_w.view(-1, 16)[:, :9].reshape(-1, 9, 1), (0, 7)).reshape(-1, 72)
@@ -170,7 +170,11 @@ class Qwen3OmniAudioEncoder(nn.Module):
         h = h.permute(0, 2, 3, 1).reshape(N * t, C * F_).contiguous()
         h = ops.linear(h, self.conv_out_w).view(N, t, -1)
         h = h + self.pos[:t].to(h.dtype)
-        rows = torch.cat([h[i, :valid[i]] for i in range(N)], 0).contiguous()
+        if all(v == t for v in valid):
+            rows = h.reshape(N * t, -1)
+        else:   # drop the padded tail tokens of partial chunks with one gather
+            keep = np.concatenate([np.arange(v) + i * t for i, v in enumerate(valid)])
+            rows = h.reshape(N * t, -1).index_select(0, torch.from_numpy(keep).to(dev))
         # attention windows: every request's tokens cut into windows of win tokens
         win = cnn_out_len(cs) * (cfg.n_window_infer // cs)
         per_req = self.output_lengths([m.shape[1] for m in mels])
