@@ -15,8 +15,9 @@ after warm-up, averaged over ``--iters`` iterations, the max over ranks.
 * EP MoE layer (128 experts, top-8, hidden 2048, expert width 768 at EP=N): router,
   count exchange, dispatch straight into the owners' expert-major buffers, the
   local grouped GEMMs, combine back to the source slots and the top-k weighted
-  sum.  Roofline: the slower of this rank's expert weights at the measured HBM
-  copy rate and the dispatched + combined rows at 770 GB/s.
+  sum.  Roofline: the slowest of this rank's expert weights at the measured HBM
+  copy rate, the expert GEMM FLOPs at the sustained bf16 rate and the dispatched +
+  combined rows at 770 GB/s.
 """
 from __future__ import annotations
 
@@ -101,9 +102,10 @@ def ep_moe_layer(T: int, iters: int, rank: int, world: int) -> dict:
     t_f = _time(lambda: ep.forward(x, wr, w13, w2, out=out), iters)
     ep.close()
     wbytes = El * 3 * H * I * 2
+    flops = T * topk * 2.0 * 3 * H * I                    # rows landing on this rank (T * topk on average)
     rows = T * topk * (world - 1) / world                 # (token, k) rows that leave this rank
     link = rows * H * 2 * 2                                # dispatched and combined back
-    roof = max(wbytes / (HBM_GBS * 1e3), link / (NVLINK_GBS * 1e3))
+    roof = max(wbytes / (HBM_GBS * 1e3), flops / (BF16_TFLOPS * 1e6), link / (NVLINK_GBS * 1e3))
     return {"path": "EP MoE layer: count exchange + dispatch into owners' expert buffers + grouped GEMMs + "
                     "combine + top-k sum", "tokens_per_rank": T, "fused_us": round(t_f, 2),
             "roofline_us": round(roof, 2), "fused_frac_of_roofline": round(roof / t_f, 3)}
