@@ -95,6 +95,20 @@ def run(case: str) -> None:
         for _ in range(3):
             qkv_rope_store(qkv, hq, hkv, d, pos, cos, sin, q_norm=qn, k_norm=qn, mrope_section=[24, 20, 20],
                            slot_mapping=slots, k_cache=kc, v_cache=vc)
+    elif case == "rope_decode":
+        # the decode-step shape: 64 tokens x (32 + 2 x 4) heads x 128, M-RoPE, paged KV store
+        from .rope import qkv_rope_store, rope_tables
+        T, hq, hkv, d = 64, 32, 4, 128
+        qkv = torch.randn(T, (hq + 2 * hkv) * d, device="cuda").bfloat16()
+        cos, sin = rope_tables(d, 1e6, 8192, "cuda")
+        pos = torch.randint(0, 8192, (3, T), dtype=torch.int32, device="cuda")
+        kc = torch.zeros(1025, hkv, 64, d, device="cuda").bfloat16()
+        vc = torch.zeros_like(kc)
+        slots = torch.randint(64, 1025 * 64, (T,), dtype=torch.int32, device="cuda")
+        qn = torch.ones(d, device="cuda").bfloat16()
+        for _ in range(3):
+            qkv_rope_store(qkv, hq, hkv, d, pos, cos, sin, q_norm=qn, k_norm=qn, mrope_section=[24, 20, 20],
+                           slot_mapping=slots, k_cache=kc, v_cache=vc)
     elif case == "moe_route":
         # softmax top-8 of 128 experts + expert histogram / offsets + permuted gather of 8192 x 2048 rows
         from .moe import MoEWorkspace, route
