@@ -175,7 +175,9 @@ __device__ __forceinline__ void decode_tile(int t, const int* prefix, const int*
 
 // ACT = false: the epilogue has no activation code at all (the common case; a
 // smaller kernel is fetched faster, which the few-tile decode GEMMs feel).
-template <int BN, bool GATED, bool ACT>
+// CL = true: the split-K-over-a-cluster variant (only the cluster epilogue is compiled in, so
+// the few-tile decode GEMMs run a smaller kernel); CL = false: every other mode.
+template <int BN, bool GATED, bool ACT, bool CL>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                      const DevParams p) {
@@ -419,20 +421,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_32x32b_x16(t_base + c, r);
         if (GATED) tmem_ld_32x32b_x16(t_base + BN + c, u);
         tmem_ld_wait();
-        if (ks > 1 && p.cluster_splitk) {
+        if (CL) {
           // split-K partial into this CTA's shared memory as a [BN][128] fp32 tile (the stage
           // ring is idle: this CTA's only work item has finished its MMAs)
           float* sp = reinterpret_cast<float*>(smem) + c * kBM + lane_base + lane;
 #pragma unroll
           for (int j = 0; j < 16; ++j) sp[j * kBM] = __uint_as_float(r[j]);
-        } else if (ks > 1) {
+        } else if (!CL && ks > 1) {
           // split-K partial into this split's plane [split][t][BN][128] (thread = one A row; for
           // each token a warp stores 32 consecutive floats); summed in split order by the
           // finaliser, so the result does not depend on which split arrives first
           float* wsp = p.ws + ((static_cast<int64_t>(w - t * ks) * total_tiles + t) * BN + c) * kBM + lane_base + lane;
 #pragma unroll
           for (int j = 0; j < 16; ++j) __stcg(wsp + j * kBM, __uint_as_float(r[j]));
-        } else if (C::kStagedEpi && p.vec8) {
+        } else if (!CL && C::kStagedEpi && p.vec8) {
           // activations per thread (one feature m, 16 tokens), the chunk through shared memory,
           // then each thread stores two vectors of 8 consecutive features of one token (and adds
           // the matching 16-byte residual vectors).  One named barrier per chunk: a buffer is
@@ -488,7 +490,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
           }
-        } else if (m_ok) {
+        } else if (!CL && m_ok) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int row = row0 + c + j;
@@ -516,7 +518,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(&tempty_bar[acc]);
-      if (ks > 1 && p.counters != nullptr && !p.cluster_splitk) {
+      if (!CL && ks > 1 && p.counters != nullptr) {
         // The last split of this tile to arrive sums the partials and runs the epilogue:
         // no second launch.  Counters reset themselves for the next call / graph replay.
         __threadfence();
@@ -581,7 +583,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  if (p.cluster_splitk) {
+  if (CL) {
     // Cluster split-K: CTA r of the cluster holds split r's partial tile in shared memory.
     // After the cluster barrier each CTA sums one slice of the tile's token rows over every
     // CTA's copy (distributed shared memory, in rank order, so the result does not depend
@@ -720,9 +722,14 @@ cudaError_t launch(const GemmArgs& a, cudaStream_t stream) {
   using C = Cfg<BN, GATED>;
   static bool attr_set = false;
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_bf16_kernel<BN, GATED, ACT>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_bf16_kernel<BN, GATED, ACT, false>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
     if (e != cudaSuccess) return e;
+    if constexpr (!GATED) {
+      e = cudaFuncSetAttribute(gemm_bf16_kernel<BN, GATED, ACT, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               C::kSmemBytes);
+      if (e != cudaSuccess) return e;
+    }
     attr_set = true;
   }
   CUtensorMap ta, tb;
@@ -824,7 +831,13 @@ cudaError_t launch(const GemmArgs& a, cudaStream_t stream) {
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  cudaError_t le = cudaLaunchKernelEx(&cfg, gemm_bf16_kernel<BN, GATED, ACT>, ta, tb, p);
+  cudaError_t le;
+  if constexpr (!GATED) {
+    le = p.cluster_splitk ? cudaLaunchKernelEx(&cfg, gemm_bf16_kernel<BN, GATED, ACT, true>, ta, tb, p)
+                          : cudaLaunchKernelEx(&cfg, gemm_bf16_kernel<BN, GATED, ACT, false>, ta, tb, p);
+  } else {
+    le = cudaLaunchKernelEx(&cfg, gemm_bf16_kernel<BN, GATED, ACT, false>, ta, tb, p);
+  }
   if (le != cudaSuccess) return le;
   if (p.k_splits > 1 && p.counters == nullptr && !p.cluster_splitk) {
     const long long n = static_cast<long long>(a.rows) * a.m_out;
