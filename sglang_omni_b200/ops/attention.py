@@ -171,7 +171,13 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
         workspace = DecodeWorkspace(B, num_heads, head_dim, max_ctx, q.device)
     if _check.enabled():
         _check.check_paged("attention_decode", block_table, kv_lens, k_cache.shape[0])
+    # Large batches fill the GPU without fine splits: twice the keys per split halves the
+    # per-split setup and merge work (64 requests x 4 KV heads at ~1.2 k context: 54 vs 57 us).
+    # The split count stays within the workspace's max_splits, which was sized for the finer split.
+    kps = workspace.keys_per_split
+    if B * num_kv_heads >= 128 and kps < 512:
+        kps = 2 * kps
     ext().attention_decode(q, k_cache, v_cache, out, block_table, kv_lens, num_heads, num_kv_heads, head_dim, scale,
-                           workspace.keys_per_split, workspace.max_splits, workspace.part_o, workspace.part_lse,
+                           kps, workspace.max_splits, workspace.part_o, workspace.part_lse,
                            getattr(workspace, "counters", None))
     return out

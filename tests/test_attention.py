@@ -66,7 +66,7 @@ def test_prefill_paged(hq, hkv, q_lens, kv_extra):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("hq,hkv,d", [(32, 4, 128), (16, 2, 128), (32, 8, 128), (16, 8, 128), (8, 8, 64)])
-@pytest.mark.parametrize("kv_lens", [[1, 63, 64, 65, 1000], [3000, 17]])
+@pytest.mark.parametrize("kv_lens", [[1, 63, 64, 65, 1000], [3000, 17], [1100 + 7 * i for i in range(40)]])
 def test_decode_paged(hq, hkv, d, kv_lens):
     k, v, bt = _make_cache(kv_lens, hkv, d, "cuda", seed=3)
     B = len(kv_lens)
