@@ -43,6 +43,7 @@ def parse():
     ap.add_argument("--speech-streams", type=int, default=32)
     ap.add_argument("--speech-tokens", type=int, default=256)
     ap.add_argument("--speech-audio-s", type=float, default=10.0)
+    ap.add_argument("--speech-first-chunk", type=int, default=4, help="frames of the first Code2Wav chunk")
     ap.add_argument("--count-launches", type=int, default=1, help="count kernel launches in one extra untimed round")
     ap.add_argument("--s2pro", type=int, default=1, help="also measure the S2-Pro streaming TTS phase")
     ap.add_argument("--s2pro-streams", type=int, default=64)
@@ -75,7 +76,8 @@ def speech_phase(args, dev, rank):
     from sglang_omni_b200.models.qwen3_omni.config import Qwen3OmniSpeechPipelineConfig, text_stages
 
     cfg = Qwen3OmniSpeechPipelineConfig(model_path="random", stages=text_stages(
-        device=str(dev), max_batch=args.speech_streams, max_context=2048, speech=True, tail_frames=50))
+        device=str(dev), max_batch=args.speech_streams, max_context=2048, speech=True, tail_frames=50,
+        first_chunk=args.speech_first_chunk))
     rng = np.random.default_rng(7 + rank)
     n = int(16000 * args.speech_audio_s)
     audios = [(rng.standard_normal(n) * 0.1).astype(np.float32) for _ in range(args.speech_streams)]
@@ -111,7 +113,9 @@ def speech_phase(args, dev, rank):
             ttfa = sorted(r[0] for r in res if r[0] is not None)
             from sglang_omni_b200.utils import trace
             if trace.ENABLED and rank == 0:   # OMNI_TRACE=1: median stage timeline of the measured streams
-                print(json.dumps({"speech_stage_timeline_ms": trace.summary(f"s-{rank}-")}), file=sys.stderr)
+                print(json.dumps({"speech_stage_timeline_ms": trace.summary(f"s-{rank}-"),
+                                  "batches": [(st, n, round(1e3 * sec, 1)) for st, n, sec in trace.batches()]}),
+                      file=sys.stderr)
             return (1e3 * statistics.median(ttfa) if ttfa else None, sum(r[1] for r in res) / wall, n * 4)
 
     return asyncio.run(run())

@@ -163,10 +163,17 @@ def create_audio_encoder_executor(model_path: str = "", device: str = "cuda:0", 
     mel = LogMel(enc.cfg.num_mel_bins, dev)
 
     def encode(inputs: dict) -> list:
+        t0 = time.perf_counter()
         per_req = inputs["waves"]
         flat = [w for ws in per_req for w in ws]
         mels = mel.batch(flat) if flat else []
+        if trace.ENABLED and dev.type == "cuda":
+            torch.cuda.current_stream().synchronize()
+            trace.batch("audio_mel", len(flat), time.perf_counter() - t0)
         outs = enc(mels) if mels else []
+        if trace.ENABLED and dev.type == "cuda":
+            torch.cuda.current_stream().synchronize()
+            trace.batch("audio_encode_total", len(flat), time.perf_counter() - t0)
         res, i = [], 0
         for ws in per_req:
             res.append({"audio_embeds": outs[i:i + len(ws)]})

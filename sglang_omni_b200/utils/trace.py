@@ -43,3 +43,18 @@ def summary(prefix: str = "") -> dict[str, float]:
         for k, v in ev.items():
             out.setdefault(k, []).append(1e3 * (v - t0))
     return {k: round(statistics.median(v), 2) for k, v in sorted(out.items(), key=lambda kv: statistics.median(kv[1]))}
+
+
+_batches: list[tuple[str, int, float]] = []
+
+
+def batch(stage: str, size: int, seconds: float) -> None:
+    """Records one batched step of a stage (size, wall seconds)."""
+    if ENABLED:
+        with _lock:
+            _batches.append((stage, size, seconds))
+
+
+def batches() -> list[tuple[str, int, float]]:
+    with _lock:
+        return list(_batches)
