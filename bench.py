@@ -448,21 +448,6 @@ def main():
             tt = torch.tensor([ttfa_ms or 0.0], dtype=torch.float64, device=dev)
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             ttfa_ms = float(tt[0])
-    vis = None
-    if args.vision and args.layers == 48:
-        v_tok_s, v_ttft = vision_phase(args, dev, rank)
-        t = torch.tensor([v_tok_s or 0.0, v_ttft or 0.0], dtype=torch.float64, device=dev)
-        if world > 1:
-            sm = t.clone()
-            dist.all_reduce(sm, op=dist.ReduceOp.SUM)
-            mx = t.clone()
-            dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-            v_tok_s, v_ttft = float(sm[0]), float(mx[1])
-        vis = {"requests_per_gpu": args.vision_requests, "image": "448x448 uniform uint8 RGB (196 image tokens)",
-               "prompt_tokens": 128, "output_tokens": args.vision_tokens,
-               "output_tok_s": None if v_tok_s is None else round(v_tok_s, 2),
-               "ttft_p50_ms": None if v_ttft is None else round(v_ttft, 2),
-               "timing": "host wall clock through Client.generate (stream=True), whole job; TTFT max over ranks"}
     s2 = None
     if args.s2pro and args.layers == 48:
         a, b, c = s2pro_phase(args, dev, rank)
@@ -480,6 +465,21 @@ def main():
                        "DAC decoder 44.1 kHz; random init",
               "timing": "host wall clock through Client.generate (stream=True): first audio chunk p50; "
                         "RTF = request wall time / audio seconds; max over ranks"}
+    vis = None
+    if args.vision and args.layers == 48:
+        v_tok_s, v_ttft = vision_phase(args, dev, rank)
+        t = torch.tensor([v_tok_s or 0.0, v_ttft or 0.0], dtype=torch.float64, device=dev)
+        if world > 1:
+            sm = t.clone()
+            dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+            mx = t.clone()
+            dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+            v_tok_s, v_ttft = float(sm[0]), float(mx[1])
+        vis = {"requests_per_gpu": args.vision_requests, "image": "448x448 uniform uint8 RGB (196 image tokens)",
+               "prompt_tokens": 128, "output_tokens": args.vision_tokens,
+               "output_tok_s": None if v_tok_s is None else round(v_tok_s, 2),
+               "ttft_p50_ms": None if v_ttft is None else round(v_ttft, 2),
+               "timing": "host wall clock through Client.generate (stream=True), whole job; TTFT max over ranks"}
     if rank == 0:
         line = {
             "metric": "output tok/s + p50 time-to-first-audio-chunk, Qwen3-Omni-30B-A3B, 1/2/4/8 B200",

@@ -203,6 +203,9 @@ def create_image_encoder_executor(model_path: str = "", device: str = "cuda:0", 
     from ..vision_encoder import encode_images
 
     dev = torch.device(device)
+    # built now, not on the first request: building ends with a device-wide synchronize, which
+    # must not run while another stage's engine thread is capturing its CUDA graphs
+    loader.get_vision_encoder(model_path, dev, overrides)
 
     def encode(inputs: dict) -> list:
         per_req = inputs["images"]
