@@ -708,6 +708,18 @@ int num_sms() {
   return n;
 }
 
+// Largest split count of the split-K modes (OMNI_SPLITK_MAX, 2..8; default 8 = the portable
+// cluster size limit).
+int splitk_max() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("OMNI_SPLITK_MAX");
+    const int x = e ? std::atoi(e) : 8;
+    v = x < 2 ? 2 : (x > 8 ? 8 : x);
+  }
+  return v;
+}
+
 bool pdl_enabled() {
   static int on = -1;
   if (on < 0) {
@@ -778,7 +790,12 @@ cudaError_t launch(const GemmArgs& a, cudaStream_t stream) {
       // one wave: tiles * splits <= SMs (a partial second wave doubles the time)
       int ksp = static_cast<int>(sms / tiles);
       if (ksp > num_kb / 2) ksp = num_kb / 2;
-      if (ksp > 8) ksp = 8;   // the finaliser reads every split: keep its rounds few
+      const int kmax = splitk_max();
+      if (ksp > kmax) ksp = kmax;   // the finaliser reads every split: keep its rounds few
+      // Clusters of 8 are placed inside one GPC two at a time; more than a couple of them do
+      // not all fit at once and a second wave doubles the time (o_proj at 64 tokens: 16 tiles x 8
+      // splits 22.8 us, x 4 splits 17.3 us), so several tiles take clusters of at most 4.
+      if (a.splitk_cluster && tiles > 2 && ksp > 4) ksp = 4;
       if (ksp > 1) {
         const int per = (num_kb + ksp - 1) / ksp;
         ksp = (num_kb + per - 1) / per;  // no empty splits
