@@ -102,7 +102,7 @@ def create_audio_encoder_executor(model_path: str = "", device: str = "cuda:0", 
     def encode(inputs: dict) -> list:
         per_req = inputs["waves"]
         flat = [w for ws in per_req for w in ws]
-        mels = [mel(w.to(dev)) for w in flat]
+        mels = mel.batch(flat) if flat else []
         outs = enc(mels) if mels else []
         res, i = [], 0
         for ws in per_req:
