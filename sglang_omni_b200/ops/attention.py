@@ -137,6 +137,17 @@ def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqle
     return out
 
 
+_SM_COUNT: dict = {}
+
+
+def _resident_decode_ctas(device, head_dim: int) -> int:
+    """CTAs of the decode kernel that fit on the GPU at once (shared memory bound)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _SM_COUNT:
+        _SM_COUNT[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    return _SM_COUNT[idx] * (3 if head_dim > 64 else 6)
+
+
 class DecodeWorkspace:
     """Split-KV scratch of the decode kernel, sized for a max batch / context."""
 
@@ -174,10 +185,16 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     # Large batches fill the GPU without fine splits: twice the keys per split halves the
     # per-split setup and merge work (64 requests x 4 KV heads at ~1.2 k context: 54 vs 57 us).
     # The split count stays within the workspace's max_splits, which was sized for the finer split.
-    kps = workspace.keys_per_split
-    if B * num_kv_heads >= 128 and kps < 512:
+    # When the (request, KV head) pairs alone fill more than half of the resident CTA slots
+    # (148 SMs x 3 CTAs of 68 KB at head_dim 128, 6 at 64), any split adds a partial wave and
+    # the merge: one split per pair is fastest (64 x 4 pairs at 1.1-1.3 k context: 41-46 us vs
+    # 52-56 us at 512 keys per split, 56-62 us at 256).
+    kps, splits = workspace.keys_per_split, workspace.max_splits
+    if 2 * B * num_kv_heads > _resident_decode_ctas(q.device, head_dim):
+        splits = 1
+    elif B * num_kv_heads >= 128 and kps < 512:
         kps = 2 * kps
     ext().attention_decode(q, k_cache, v_cache, out, block_table, kv_lens, num_heads, num_kv_heads, head_dim, scale,
-                           kps, workspace.max_splits, workspace.part_o, workspace.part_lse,
+                           kps, splits, workspace.part_o, workspace.part_lse,
                            getattr(workspace, "counters", None))
     return out
