@@ -182,9 +182,9 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
         workspace = DecodeWorkspace(B, num_heads, head_dim, max_ctx, q.device)
     if _check.enabled():
         _check.check_paged("attention_decode", block_table, kv_lens, k_cache.shape[0])
-    # Large batches fill the GPU without fine splits: twice the keys per split halves the
-    # per-split setup and merge work (64 requests x 4 KV heads at ~1.2 k context: 54 vs 57 us).
-    # The split count stays within the workspace's max_splits, which was sized for the finer split.
+    # Batches of 128 or more pairs that do not take the single split below still fill most of the
+    # GPU: twice the keys per split halves the per-split setup and merge work.  The split count
+    # stays within the workspace's max_splits, which was sized for the finer split.
     # When the (request, KV head) pairs alone fill more than half of the resident CTA slots
     # (148 SMs x 3 CTAs of 68 KB at head_dim 128, 6 at 64), any split adds a partial wave and
     # the merge: one split per pair is fastest (64 x 4 pairs at 1.1-1.3 k context: 41-46 us vs

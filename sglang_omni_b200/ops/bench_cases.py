@@ -185,10 +185,11 @@ def _time_cases() -> None:
     bt = torch.arange(B * pages, dtype=torch.int32, device="cuda").view(B, pages)
     kl = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
     q = torch.randn(B, hq * d, device="cuda").bfloat16()
-    for kps in (128, 256, 512):
-        ws = A.DecodeWorkspace(B, hq, d, ctx, "cuda", keys_per_split=kps)
-        res[f"decode_attn B64 ctx1152 kps{kps}"] = (t(lambda: A.decode_attention(q, k, v, bt, kl, hq, hkv, d, ws)),
-                                                   2 * B * ctx * hkv * d * 2)
+    # 64 x 4 (request, KV head) pairs take one split each; 16 requests (64 pairs) split the keys
+    for nb in (B, 16):
+        ws = A.DecodeWorkspace(nb, hq, d, ctx, "cuda")
+        res[f"decode_attn B{nb} ctx1152"] = (t(lambda: A.decode_attention(q[:nb], k, v, bt[:nb], kl[:nb], hq, hkv, d,
+                                                                          ws)), 2 * nb * ctx * hkv * d * 2)
     for name, (us, nbytes) in res.items():
         print(f"{name:32s} {us:8.2f} us  {nbytes / us / 1e3:7.1f} GB/s")
 
