@@ -15,6 +15,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include "host_util.h"
 #include "omni_kernels.h"
 #include "pdl.cuh"
 
@@ -93,6 +94,14 @@ __device__ __forceinline__ void load_tile(__nv_bfloat16* dst, RowFn src_row, int
 // A block-table entry outside the cache reads the reserved padding page 0.
 __device__ __forceinline__ int checked_page(int page, int num_pages) {
   return (num_pages > 0 && static_cast<unsigned>(page) >= static_cast<unsigned>(num_pages)) ? 0 : page;
+}
+
+// A decode request sees at most the keys its block-table row can name
+// (bt_stride pages of 64): a longer kv_len would read past the row.
+__device__ __forceinline__ int decode_kv_len(const int* kv_lens, int b, int bt_stride) {
+  const int n = kv_lens[b];
+  const int cap = bt_stride > 0 ? bt_stride * 64 : n;
+  return n < cap ? n : cap;
 }
 
 struct PrefillParams {
@@ -354,7 +363,7 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
 
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int G = p.hq / p.hkv;
-  const int kv_len = p.kv_lens[b];
+  const int kv_len = decode_kv_len(p.kv_lens, b, p.bt_stride);
   const int kps = split_keys(kv_len, p.keys_per_split, p.max_splits);
   const int k_begin = split * kps;
   if (kv_len <= 0) {
@@ -607,7 +616,7 @@ template <int D>
 __global__ void decode_combine_kernel(const DecodeParams p) {
   grid_dep_launch();  // a dependent GEMM may start its prologue now
   const int head = blockIdx.x, b = blockIdx.y;
-  const int kv_len = p.kv_lens[b];
+  const int kv_len = decode_kv_len(p.kv_lens, b, p.bt_stride);
   const int kps = split_keys(kv_len, p.keys_per_split, p.max_splits);
   const int nsplit = (kv_len + kps - 1) / kps;
   if (nsplit <= 1) return;
@@ -629,12 +638,8 @@ __global__ void decode_combine_kernel(const DecodeParams p) {
 template <int D>
 cudaError_t launch_prefill(const PrefillParams& p, int num_tiles, cudaStream_t stream) {
   const int smem = 4 * Tile<D>::kElems * 2;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(prefill_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  cudaError_t e = ensure_smem_attr<prefill_kernel<D>>(smem);
+  if (e != cudaSuccess) return e;
   dim3 grid(num_tiles, p.hkv);
   prefill_kernel<D><<<grid, 128, smem, stream>>>(p);
   return cudaGetLastError();
@@ -645,12 +650,8 @@ cudaError_t launch_decode(const DecodeParams& p, int batch, cudaStream_t stream)
   const int tiles = 4 * Tile<D>::kElems * 2;
   const int red = 4 * 16 * D * 4 + 4 * 16 * 2 * 4;
   const int smem = tiles > red ? tiles : red;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(decode_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  cudaError_t e = ensure_smem_attr<decode_kernel<D>>(smem);
+  if (e != cudaSuccess) return e;
   dim3 grid(p.max_splits, p.hkv, batch);
   decode_kernel<D><<<grid, 128, smem, stream>>>(p);
   if (p.max_splits > 1 && p.counters == nullptr) {
@@ -664,7 +665,7 @@ cudaError_t launch_decode(const DecodeParams& p, int batch, cudaStream_t stream)
 
 cudaError_t attention_prefill(const AttnPrefillArgs& a, cudaStream_t stream) {
   if (a.num_tiles == 0) return cudaSuccess;
-  if (a.hq % a.hkv != 0 || 64 % (a.hq / a.hkv) != 0) return cudaErrorInvalidValue;
+  if (a.hq <= 0 || a.hkv <= 0 || a.hq % a.hkv != 0 || 64 % (a.hq / a.hkv) != 0) return cudaErrorInvalidValue;
   PrefillParams p;
   p.q = static_cast<const __nv_bfloat16*>(a.q);
   p.q_stride = a.q_stride;
@@ -697,7 +698,9 @@ cudaError_t attention_prefill(const AttnPrefillArgs& a, cudaStream_t stream) {
 
 cudaError_t attention_decode(const AttnDecodeArgs& a, cudaStream_t stream) {
   if (a.batch == 0) return cudaSuccess;
-  if (a.hq % a.hkv != 0 || a.hq / a.hkv > 16 || a.keys_per_split % kPage != 0) return cudaErrorInvalidValue;
+  if (a.batch < 0 || a.hq <= 0 || a.hkv <= 0 || a.max_splits < 1) return cudaErrorInvalidValue;
+  if (a.hq % a.hkv != 0 || a.hq / a.hkv > 16 || a.keys_per_split <= 0 || a.keys_per_split % kPage != 0)
+    return cudaErrorInvalidValue;
   DecodeParams p;
   p.q = static_cast<const __nv_bfloat16*>(a.q);
   p.q_stride = a.q_stride;
@@ -747,23 +750,28 @@ constexpr long long kNoAllocLseFloats = OMNI_NOALLOC_DECODE_LSE_FLOATS;
 static __device__ __align__(256) float g_noalloc_decode_scratch[kNoAllocPartFloats + kNoAllocLseFloats];
 
 constexpr int kNoAllocMaxDevices = 64;
-std::once_flag g_noalloc_once[kNoAllocMaxDevices];
+std::mutex g_noalloc_mu;
 float* g_noalloc_ptr[kNoAllocMaxDevices];
-cudaError_t g_noalloc_err[kNoAllocMaxDevices];
 
-// Device address of the scratch array on the current device, resolved once per
-// device with that device current.
+// Device address of the scratch array on the current device.  It is resolved
+// with that device current and kept only once the lookup succeeded: a lookup
+// that failed (for example because another library was capturing a stream at
+// that moment) is retried on the next call instead of being remembered.
 cudaError_t noalloc_scratch(float** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kNoAllocMaxDevices) return cudaErrorInvalidDevice;
-  std::call_once(g_noalloc_once[dev], [dev] {
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
     void* p = nullptr;
-    g_noalloc_err[dev] = cudaGetSymbolAddress(&p, g_noalloc_decode_scratch);
-    g_noalloc_ptr[dev] = g_noalloc_err[dev] == cudaSuccess ? static_cast<float*>(p) : nullptr;
-  });
-  if (g_noalloc_err[dev] != cudaSuccess) return g_noalloc_err[dev];
+    e = cudaGetSymbolAddress(&p, g_noalloc_decode_scratch);
+    if (e != cudaSuccess) {
+      cudaGetLastError();  // the failed lookup must not be reported by the caller's next CUDA call
+      return e;
+    }
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
   *out = g_noalloc_ptr[dev];
   return cudaSuccess;
 }
@@ -773,9 +781,28 @@ cudaError_t noalloc_scratch(float** out) {
 extern "C" __attribute__((visibility("default"))) int omni_attention_decode_noalloc(
     const void* q, long long q_stride, const void* k_cache, const void* v_cache, const int* block_table,
     int bt_stride, const int* kv_lens, int batch, int num_heads, int num_kv_heads, int head_dim, float scale,
-    int keys_per_split, int max_splits, void* out, long long out_stride, void* stream) {
+    int keys_per_split, int max_splits, int num_pages, void* out, long long out_stride, void* stream) {
+  // Shapes first, before any division by them.
+  const bool bad = batch < 0 || num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads != 0 ||
+                   num_heads / num_kv_heads > 16 || (head_dim != 64 && head_dim != 128) || keys_per_split <= 0 ||
+                   keys_per_split % 64 != 0 || max_splits < 1 || num_pages < 1 || bt_stride < 0 ||
+                   q_stride < static_cast<long long>(num_heads) * head_dim ||
+                   out_stride < static_cast<long long>(num_heads) * head_dim;
+  if (bad) {
+    std::fprintf(stderr,
+                 "omni_attention_decode_noalloc: invalid arguments (batch %d, heads %d / %d, head_dim %d, "
+                 "keys_per_split %d, max_splits %d, num_pages %d, strides q %lld out %lld block table %d)\n",
+                 batch, num_heads, num_kv_heads, head_dim, keys_per_split, max_splits, num_pages, q_stride, out_stride,
+                 bt_stride);
+    return OMNI_NOALLOC_ERR_INVALID;
+  }
+  if (batch > 0 && (q == nullptr || k_cache == nullptr || v_cache == nullptr || block_table == nullptr ||
+                    kv_lens == nullptr || out == nullptr)) {
+    std::fprintf(stderr, "omni_attention_decode_noalloc: null input or output pointer\n");
+    return OMNI_NOALLOC_ERR_INVALID;
+  }
   const long long slots = static_cast<long long>(batch) * num_heads * max_splits;
-  if (batch < 0 || max_splits < 1 || slots * head_dim > kNoAllocPartFloats || slots > kNoAllocLseFloats) {
+  if (slots * head_dim > kNoAllocPartFloats || slots > kNoAllocLseFloats) {
     std::fprintf(stderr,
                  "omni_attention_decode_noalloc: batch %d x heads %d x splits %d x head_dim %d needs %lld partial "
                  "floats and %lld LSE floats; the static scratch holds %lld and %lld\n",
@@ -783,6 +810,7 @@ extern "C" __attribute__((visibility("default"))) int omni_attention_decode_noal
                  kNoAllocLseFloats);
     return OMNI_NOALLOC_ERR_TOO_LARGE;
   }
+  if (batch == 0) return 0;
   float* scratch = nullptr;
   cudaError_t e = noalloc_scratch(&scratch);
   if (e != cudaSuccess) return static_cast<int>(e);
@@ -805,5 +833,6 @@ extern "C" __attribute__((visibility("default"))) int omni_attention_decode_noal
   a.out_stride = out_stride;
   a.part_o = scratch;
   a.part_lse = scratch + kNoAllocPartFloats;
+  a.num_pages = num_pages;  // block-table entries outside [0, num_pages) read page 0
   return static_cast<int>(omni::attention_decode(a, static_cast<cudaStream_t>(stream)));
 }

@@ -339,7 +339,9 @@ void moe_combine(const torch::Tensor& y_perm, const torch::Tensor& inv_perm, con
                  const c10::optional<torch::Tensor>& shared_gate, const c10::optional<torch::Tensor>& residual,
                  const c10::optional<torch::Tensor>& norm_w, const c10::optional<torch::Tensor>& normed, double eps,
                  const c10::optional<torch::Tensor>& local_offsets, const c10::optional<torch::Tensor>& peer_out,
-                 int64_t rows_per) {
+                 int64_t rows_per, const c10::optional<torch::Tensor>& wait_flags,
+                 const c10::optional<torch::Tensor>& wait_seq, const c10::optional<torch::Tensor>& status,
+                 double timeout_s) {
   OMNI_CHECK_CUDA(y_perm);
   OMNI_CHECK_BF16(y_perm);
   OMNI_CHECK_CONTIG(y_perm);
@@ -390,6 +392,15 @@ void moe_combine(const torch::Tensor& y_perm, const torch::Tensor& inv_perm, con
     a.rows_per = static_cast<int>(rows_per);
     a.out = nullptr;
   }
+  if (wait_flags.has_value()) {
+    TORCH_CHECK(wait_seq.has_value() && wait_flags->scalar_type() == at::kInt && wait_seq->scalar_type() == at::kInt,
+                "wait flags / sequence int32");
+    a.wait_flags = reinterpret_cast<const unsigned int*>(wait_flags->data_ptr<int>());
+    a.wait_seq = reinterpret_cast<const unsigned int*>(wait_seq->data_ptr<int>());
+    a.wait_count = static_cast<int>(wait_flags->numel());
+    a.wait_timeout_ns = static_cast<long long>(timeout_s * 1e9);
+  }
+  a.status = status_ptr(status);
   check_launch(omni::moe_combine(a, at::cuda::getCurrentCUDAStream()), "moe_combine");
 }
 
@@ -480,39 +491,116 @@ torch::Tensor tensor_at(int64_t ptr, const std::vector<int64_t>& shape, c10::Sca
                        at::TensorOptions().dtype(dtype).device(at::kCUDA, static_cast<c10::DeviceIndex>(device)));
 }
 
-// ---- expert-parallel exchange
-omni::EpArgs ep_args(const torch::Tensor& topk_ids, const torch::Tensor& peer_base, const std::vector<int64_t>& offs,
-                     int64_t rank, int64_t world, int64_t experts, int64_t hidden, int64_t cap_rows,
-                     int64_t max_slots, torch::Tensor& cursor, torch::Tensor& local_offsets, torch::Tensor& total_rows,
-                     torch::Tensor& epoch, const c10::optional<torch::Tensor>& status, double timeout_s) {
-  TORCH_CHECK(topk_ids.scalar_type() == at::kInt && topk_ids.dim() == 2 && topk_ids.is_contiguous(), "topk_ids");
-  TORCH_CHECK(peer_base.scalar_type() == at::kLong && peer_base.numel() == world, "peer_base int64 [world]");
-  TORCH_CHECK(offs.size() == 5, "five region offsets");
-  TORCH_CHECK(experts % world == 0 && hidden % 8 == 0, "experts % world, hidden % 8");
-  omni::EpArgs a{};
+// ---- expert-parallel MoE layer (csrc/ep_moe.cu + the EP modes of the grouped GEMM)
+// peer_base: int64 [world] symmetric-buffer bases; offs = {flags, cursor, recv_x, recv_tag, comb}.
+void ep_dispatch(const torch::Tensor& x, const torch::Tensor& topk_ids, const torch::Tensor& peer_base,
+                 const std::vector<int64_t>& offs, int64_t rank, int64_t world, int64_t experts, int64_t seg_cap,
+                 torch::Tensor& seq, torch::Tensor& arrive, const c10::optional<torch::Tensor>& status) {
+  OMNI_CHECK_CUDA(x);
+  OMNI_CHECK_BF16(x);
+  OMNI_CHECK_CONTIG(x);
+  TORCH_CHECK(topk_ids.scalar_type() == at::kInt && topk_ids.dim() == 2 && topk_ids.is_contiguous() &&
+                  topk_ids.size(0) == x.size(0), "topk_ids int32 [tokens, topk]");
+  TORCH_CHECK(peer_base.scalar_type() == at::kLong && peer_base.is_cuda() && peer_base.numel() == world,
+              "peer_base int64 [world] on the device");
+  TORCH_CHECK(offs.size() == 5 && world >= 1 && rank >= 0 && rank < world && experts % world == 0, "EP geometry");
+  TORCH_CHECK(seq.scalar_type() == at::kInt && arrive.scalar_type() == at::kInt, "seq / arrive int32");
+  const at::cuda::CUDAGuard guard(x.device());
+  omni::EpDispatchArgs a{};
   a.rank = static_cast<int>(rank);
   a.world = static_cast<int>(world);
   a.experts = static_cast<int>(experts);
   a.local_experts = static_cast<int>(experts / world);
   a.topk = static_cast<int>(topk_ids.size(1));
-  a.hidden = static_cast<int>(hidden);
-  a.tokens = static_cast<int>(topk_ids.size(0));
+  a.hidden = static_cast<int>(x.size(1));
+  a.tokens = static_cast<int>(x.size(0));
   a.topk_ids = topk_ids.data_ptr<int>();
+  a.x = x.data_ptr();
   a.peer_base = peer_base.data_ptr<int64_t>();
-  a.off_counts = offs[0];
-  a.off_flags = offs[1];
+  a.off_flags = offs[0];
+  a.off_cursor = offs[1];
   a.off_recv_x = offs[2];
-  a.off_recv_meta = offs[3];
-  a.off_comb = offs[4];
-  a.cap_rows = static_cast<int>(cap_rows);
-  a.max_slots = static_cast<int>(max_slots);
-  a.cursor = cursor.data_ptr<int>();
-  a.local_offsets = local_offsets.data_ptr<int>();
-  a.total_rows = total_rows.data_ptr<int>();
-  a.epoch = reinterpret_cast<uint32_t*>(epoch.data_ptr<int>());
+  a.off_recv_tag = offs[3];
+  a.seg_cap = static_cast<int>(seg_cap);
+  a.seq = reinterpret_cast<uint32_t*>(seq.data_ptr<int>());
+  a.arrive = arrive.data_ptr<int>();
   a.status = status_ptr(status);
-  a.timeout_ns = static_cast<uint64_t>(timeout_s * 1e9);
-  return a;
+  check_launch(omni::ep_dispatch(a, at::cuda::getCurrentCUDAStream()), "ep_dispatch");
+}
+
+// Grouped GEMM of an EP layer over the receive segments: group g = rows [g * seg_cap, + counts[g]).
+// w13 (gated): waits for the dispatch flags before reading counts, copies them to counts_copy.
+// w2: row_tag / peer_rows route every output row to its source rank's slot, then the completion
+// flags are raised (signal_flags: int64 [world] peer addresses) and the counters zero_ptr cleared.
+void gemm_ep(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& out, int64_t m_out, bool gated,
+             int64_t seg_cap, const torch::Tensor& counts, const c10::optional<torch::Tensor>& counts_copy,
+             const c10::optional<torch::Tensor>& wait_flags, const c10::optional<torch::Tensor>& wait_seq,
+             double timeout_s, const c10::optional<torch::Tensor>& row_tag,
+             const c10::optional<torch::Tensor>& peer_rows, int64_t tag_slots,
+             const c10::optional<torch::Tensor>& signal_flags, const c10::optional<torch::Tensor>& signal_seq,
+             const c10::optional<torch::Tensor>& arrive, const c10::optional<torch::Tensor>& zero,
+             int64_t expected_rows, const c10::optional<torch::Tensor>& status) {
+  OMNI_CHECK_CUDA(a);
+  OMNI_CHECK_CUDA(b);
+  OMNI_CHECK_BF16(a);
+  OMNI_CHECK_BF16(b);
+  OMNI_CHECK_CONTIG(a);
+  OMNI_CHECK_CONTIG(b);
+  TORCH_CHECK(a.dim() == 3, "expert weights [groups, rows, K]");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.stride(-1) == 1, "bf16 output rows");
+  const int64_t k = b.size(-1);
+  const int groups = static_cast<int>(a.size(0));
+  TORCH_CHECK(a.size(2) == k && (gated ? a.size(1) == 2 * m_out : a.size(1) >= m_out), "weight shape");
+  TORCH_CHECK(b.size(0) >= seg_cap * groups && seg_cap > 0, "B holds groups x seg_cap rows");
+  TORCH_CHECK(counts.scalar_type() == at::kInt && counts.is_cuda() && counts.numel() >= groups, "counts int32");
+  const at::cuda::CUDAGuard guard(b.device());
+  omni::GemmArgs args{};
+  args.a = a.data_ptr();
+  args.b = b.data_ptr();
+  args.out = out.data_ptr();
+  args.ldo = out.stride(0);
+  args.m_out = static_cast<int>(m_out);
+  args.a_rows = static_cast<int>(a.size(1));
+  args.k = static_cast<int>(k);
+  args.groups = groups;
+  args.rows = static_cast<int>(b.size(0));
+  args.expected_rows_per_group = static_cast<int>(expected_rows);
+  args.gated = gated ? 1 : 0;
+  args.status = status_ptr(status);
+  args.seg_cap = static_cast<int>(seg_cap);
+  args.seg_counts = counts.data_ptr<int>();
+  if (counts_copy.has_value()) args.seg_counts_copy = counts_copy->data_ptr<int>();
+  if (wait_flags.has_value()) {
+    TORCH_CHECK(wait_seq.has_value(), "wait needs the sequence word");
+    args.wait_flags = reinterpret_cast<const unsigned int*>(wait_flags->data_ptr<int>());
+    args.wait_seq = reinterpret_cast<const unsigned int*>(wait_seq->data_ptr<int>());
+    args.wait_count = static_cast<int>(wait_flags->numel());
+    args.wait_timeout_ns = static_cast<long long>(timeout_s * 1e9);
+    args.setup_wait = 1;
+  }
+  if (row_tag.has_value()) {
+    TORCH_CHECK(peer_rows.has_value() && peer_rows->scalar_type() == at::kLong && row_tag->scalar_type() == at::kInt &&
+                    row_tag->numel() >= 2 * b.size(0), "combine epilogue: int32 tags [rows, 2], int64 row bases");
+    args.row_tag = row_tag->data_ptr<int>();
+    args.peer_rows = reinterpret_cast<const unsigned long long*>(peer_rows->data_ptr<int64_t>());
+    args.tag_ranks = static_cast<int>(peer_rows->numel());
+    args.tag_slots = static_cast<int>(tag_slots);
+  } else {
+    TORCH_CHECK(out.size(0) >= b.size(0), "out rows");
+  }
+  if (signal_flags.has_value()) {
+    TORCH_CHECK(signal_seq.has_value() && arrive.has_value() && signal_flags->scalar_type() == at::kLong,
+                "completion signal: int64 flag addresses, sequence word, arrival counter");
+    args.signal_flags = reinterpret_cast<const unsigned long long*>(signal_flags->data_ptr<int64_t>());
+    args.signal_seq = reinterpret_cast<const unsigned int*>(signal_seq->data_ptr<int>());
+    args.signal_count = static_cast<int>(signal_flags->numel());
+    args.arrive_counter = arrive->data_ptr<int>();
+  }
+  if (zero.has_value()) {
+    args.zero_ptr = zero->data_ptr<int>();
+    args.zero_n = static_cast<int>(zero->numel());
+  }
+  check_launch(omni::gemm_bf16(args, at::cuda::getCurrentCUDAStream()), "gemm_ep");
 }
 
 // Tensor-parallel reduce point: ptrs = int64 [4, world] device table of the
@@ -568,42 +656,6 @@ void tp_wait(const torch::Tensor& ptrs, int64_t rank, int64_t world, torch::Tens
   const at::cuda::CUDAGuard guard(ptrs.device());
   auto a = tp_args(ptrs, rank, world, 0, 8, 1, 0, false, seq, counter, status, timeout_s);
   check_launch(omni::tp_wait(a, at::cuda::getCurrentCUDAStream()), "tp_wait");
-}
-
-void ep_counts(const torch::Tensor& topk_ids, const torch::Tensor& peer_base, const std::vector<int64_t>& offs,
-               int64_t rank, int64_t world, int64_t experts, int64_t hidden, int64_t cap_rows, int64_t max_slots,
-               torch::Tensor& cursor, torch::Tensor& local_offsets, torch::Tensor& total_rows, torch::Tensor& epoch,
-               const c10::optional<torch::Tensor>& status, double timeout_s) {
-  const at::cuda::CUDAGuard guard(topk_ids.device());
-  auto a = ep_args(topk_ids, peer_base, offs, rank, world, experts, hidden, cap_rows, max_slots, cursor, local_offsets,
-                   total_rows, epoch, status, timeout_s);
-  check_launch(omni::ep_counts(a, at::cuda::getCurrentCUDAStream()), "ep_counts");
-}
-
-void ep_dispatch(const torch::Tensor& x, const torch::Tensor& topk_ids, const torch::Tensor& peer_base,
-                 const std::vector<int64_t>& offs, int64_t rank, int64_t world, int64_t experts, int64_t cap_rows,
-                 int64_t max_slots, torch::Tensor& cursor, torch::Tensor& local_offsets, torch::Tensor& total_rows,
-                 torch::Tensor& epoch, const c10::optional<torch::Tensor>& status, double timeout_s) {
-  OMNI_CHECK_BF16(x);
-  OMNI_CHECK_CONTIG(x);
-  TORCH_CHECK(x.size(0) == topk_ids.size(0), "x rows != topk_ids rows");
-  const at::cuda::CUDAGuard guard(x.device());
-  auto a = ep_args(topk_ids, peer_base, offs, rank, world, experts, x.size(1), cap_rows, max_slots, cursor,
-                   local_offsets, total_rows, epoch, status, timeout_s);
-  a.x = x.data_ptr();
-  check_launch(omni::ep_dispatch(a, at::cuda::getCurrentCUDAStream()), "ep_dispatch");
-}
-
-void ep_combine(const torch::Tensor& y, const torch::Tensor& topk_ids, const torch::Tensor& peer_base,
-                const std::vector<int64_t>& offs, int64_t rank, int64_t world, int64_t experts, int64_t cap_rows,
-                int64_t max_slots, torch::Tensor& cursor, torch::Tensor& local_offsets, torch::Tensor& total_rows,
-                torch::Tensor& epoch, const c10::optional<torch::Tensor>& status, double timeout_s) {
-  OMNI_CHECK_BF16(y);
-  TORCH_CHECK(y.stride(-1) == 1, "y rows");
-  const at::cuda::CUDAGuard guard(y.device());
-  auto a = ep_args(topk_ids, peer_base, offs, rank, world, experts, y.size(1), cap_rows, max_slots, cursor,
-                   local_offsets, total_rows, epoch, status, timeout_s);
-  check_launch(omni::ep_combine(a, y.data_ptr(), y.stride(0), at::cuda::getCurrentCUDAStream()), "ep_combine");
 }
 
 void sample(torch::Tensor& logits, torch::Tensor& out_tokens, const c10::optional<torch::Tensor>& temperature,
@@ -741,7 +793,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("out"), py::arg("shared") = py::none(), py::arg("shared_gate") = py::none(),
         py::arg("residual") = py::none(), py::arg("norm_w") = py::none(), py::arg("normed") = py::none(),
         py::arg("eps") = 1e-6, py::arg("local_offsets") = py::none(), py::arg("peer_out") = py::none(),
-        py::arg("rows_per") = 0);
+        py::arg("rows_per") = 0, py::arg("wait_flags") = py::none(), py::arg("wait_seq") = py::none(),
+        py::arg("status") = py::none(), py::arg("timeout_s") = 2.0);
   m.def("embed", &embed, "embedding gather with multimodal overwrite");
   m.def("vq_embed", &vq_embed, "dual-AR input embedding with the scaled VQ codebook sum");
   m.def("ipc_alloc", &ipc_alloc, "cudaMalloc + zero, returns the device address");
@@ -753,9 +806,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_reduce_norm", &tp_reduce_norm, "tensor-parallel reduce-scatter + residual + RMSNorm + all-gather "
         "over peer memory");
   m.def("tp_wait", &tp_wait, "tensor-parallel: wait until every rank's gathered rows have landed");
-  m.def("ep_counts", &ep_counts, "expert-parallel: exchange per-expert counts, derive offsets");
-  m.def("ep_dispatch", &ep_dispatch, "expert-parallel: rows to their experts' ranks (expert-major) + barrier");
-  m.def("ep_combine", &ep_combine, "expert-parallel: expert outputs back to their source slots + barrier");
+  m.def("ep_dispatch", &ep_dispatch, "expert-parallel: every routed row into its expert owner's receive segment "
+                                      "(system-atomic reservations), then the dispatch flags");
+  m.def("gemm_ep", &gemm_ep, "expert-parallel grouped GEMM over receive segments (flag wait / combine epilogue / "
+                             "completion flags)");
   m.def("sample", &sample, "fused logits processing + sampling");
   m.def("snake", &snake, "Snake / SnakeBeta activation (channels-last)");
   m.def("conv1d_im2col", &conv1d_im2col, "causal dilated conv1d im2col rows");

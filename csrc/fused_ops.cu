@@ -53,6 +53,12 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16(x)); }
 
+__device__ __forceinline__ unsigned long long omni_globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
 // ---------------------------------------------------------------------------
 // QK norm + RoPE + KV store
 // ---------------------------------------------------------------------------
@@ -442,6 +448,27 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(MoeCombineArgs a) {
   __shared__ float s_w[16];
   __shared__ float red[8];
   const int tok = blockIdx.x;
+  if (a.wait_count > 0) {
+    // expert-parallel: the expert outputs of this rank's rows are stored by their owners; wait
+    // (bounded, wrap-safe compare) until every owner has raised its flag for this layer
+    if (threadIdx.x < 32) {
+      const uint32_t target = *reinterpret_cast<const volatile uint32_t*>(a.wait_seq);
+      const unsigned long long t0 = omni_globaltimer();
+      for (int i = threadIdx.x; i < a.wait_count; i += 32) {
+        uint32_t v;
+        while (true) {
+          asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a.wait_flags + i) : "memory");
+          if (static_cast<int>(v - target) >= 0) break;
+          if (omni_globaltimer() - t0 > static_cast<unsigned long long>(a.wait_timeout_ns)) {
+            if (a.status != nullptr) atomicCAS(a.status, 0, 2);  // peer timeout
+            break;
+          }
+        }
+      }
+    }
+    __syncthreads();
+    __threadfence_system();
+  }
   if (threadIdx.x < a.topk) {
     int pos = a.inv_perm[tok * a.topk + threadIdx.x];
     if (a.local_offsets != nullptr && (pos < a.local_offsets[0] || pos >= a.local_offsets[a.local_experts])) pos = -1;

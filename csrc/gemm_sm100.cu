@@ -29,6 +29,7 @@
 #include <cstring>
 #include <mutex>
 
+#include "host_util.h"
 #include "omni_kernels.h"
 #include "sm100.cuh"
 
@@ -69,9 +70,55 @@ struct DevParams {
   const unsigned int* wait_seq;
   int wait_count;
   long long wait_timeout_ns;
+  // expert-parallel fused modes (see GemmArgs)
+  int seg_cap;                         // > 0: group g = rows [g * seg_cap, + seg_counts[g])
+  const int* seg_counts;
+  int* seg_counts_copy;
+  int setup_wait;                      // the flags are awaited before the counts are read
+  const int* row_tag;                  // combine epilogue: row r -> peer_rows[tag.x] + tag.y * ldo
+  const unsigned long long* peer_rows;
+  int tag_ranks, tag_slots;
+  const unsigned long long* signal_flags;  // completion: last CTA release-stores *signal_seq there
+  const unsigned int* signal_seq;
+  int signal_count;
+  int* arrive_counter;
+  int* zero_ptr;
+  int zero_n;
 };
 
+// Bounded wait until every flags[i] (i < count) has reached *seq (wrap-safe compare); lane i
+// of the calling warp waits on flags i, i + 32, ...  Returns false after a timeout (status 2).
+__device__ __forceinline__ bool wait_flags_warp(const unsigned int* flags, const unsigned int* seq, int count,
+                                                long long timeout_ns, int* status, int lane) {
+  const uint32_t target = *reinterpret_cast<const volatile uint32_t*>(seq);
+  const uint64_t t0 = globaltimer_ns();
+  bool ok = true;
+  for (int i = lane; i < count && ok; i += 32) {
+    uint32_t v;
+    while (true) {
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + i) : "memory");
+      if (static_cast<int>(v - target) >= 0) break;
+      if (globaltimer_ns() - t0 > static_cast<uint64_t>(timeout_ns)) {
+        record_status(status, kStatusPeerTimeout);
+        ok = false;
+        break;
+      }
+    }
+  }
+  __syncwarp();
+  __threadfence_system();  // the other lanes' later reads follow every lane's acquire
+  return __all_sync(0xffffffffu, ok);
+}
+
+// Destination of bf16 output row `row`, or nullptr when a combine tag drops it.
 __device__ __forceinline__ __nv_bfloat16* out_row_bf16(const DevParams& p, int row) {
+  if (p.row_tag != nullptr) {
+    const int2 t = reinterpret_cast<const int2*>(p.row_tag)[row];
+    if (static_cast<unsigned>(t.x) >= static_cast<unsigned>(p.tag_ranks) ||
+        static_cast<unsigned>(t.y) >= static_cast<unsigned>(p.tag_slots))
+      return nullptr;
+    return reinterpret_cast<__nv_bfloat16*>(p.peer_rows[t.x]) + static_cast<int64_t>(t.y) * p.ldo;
+  }
   if (p.peer_out != nullptr)
     return reinterpret_cast<__nv_bfloat16*>(p.peer_out[row / p.rows_per]) + static_cast<int64_t>(row) * p.ldo;
   return static_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.ldo;
@@ -146,20 +193,23 @@ struct Cfg {
                                                            : 512;
   static constexpr int kStagesRaw = (200 * 1024) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
-  // tiles + 1 KB alignment slack + barriers and the group tables (4 KB + 2 * (kMaxGroups + 1) ints)
-  static constexpr int kAuxBytes = (1024 + 8 * (kMaxGroups + 1) + 512 + 15) / 16 * 16;
+  // tiles + 1 KB alignment slack + barriers and the group tables (starts, ends, tile prefix sums:
+  // 3 * (kMaxGroups + 1) ints after 512 bytes of barriers)
+  static constexpr int kAuxBytes = (1024 + 12 * (kMaxGroups + 1) + 512 + 15) / 16 * 16;
   // wide token tiles stage each 16-token chunk of the epilogue through shared memory (two
   // [16][128] fp32 buffers) so that outputs leave as 16-byte vectors along the feature axis
   static constexpr bool kStagedEpi = BN >= 64;
   static constexpr int kEpiBytes = kStagedEpi ? 2 * 16 * kBM * 4 : 0;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kAuxBytes + kEpiBytes;
   static_assert(2 * kAccCols <= 512, "accumulators exceed TMEM");
+  static_assert(kSmemBytes <= 232448, "shared memory exceeds 227 KB");
   static_assert(kBBytes % 1024 == 0, "B tile must keep 1024-byte alignment");
 };
 
+// Tile t -> group g, weight tile mt, token tile nt.  Group g's rows are [offs[g], ends[g]).
 template <int BN>
-__device__ __forceinline__ void decode_tile(int t, const int* prefix, const int* offs, int groups, int& g, int& mt,
-                                            int& nt) {
+__device__ __forceinline__ void decode_tile(int t, const int* prefix, const int* offs, const int* ends, int groups,
+                                            int& g, int& mt, int& nt) {
   int lo = 0, hi = groups - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
@@ -167,7 +217,7 @@ __device__ __forceinline__ void decode_tile(int t, const int* prefix, const int*
   }
   g = lo;
   const int local = t - prefix[g];
-  const int rows = offs[g + 1] - offs[g];
+  const int rows = ends[g] - offs[g];
   const int ntiles = (rows + BN - 1) / BN;
   mt = local / ntiles;
   nt = local - mt * ntiles;
@@ -199,6 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   int* total_tiles_s = const_cast<int*>(reinterpret_cast<volatile int*>(tmem_slot + 2));
   int* offs_s = reinterpret_cast<int*>(aux + 512);
   int* prefix_s = offs_s + (kMaxGroups + 1);
+  int* ends_s = prefix_s + (kMaxGroups + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -223,15 +274,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Group row offsets and tile prefix sums (warp 2); device offsets come from a
   // previous kernel, dense GEMMs need none.
   if (warp == 2) {
-    if (p.offsets != nullptr) grid_dep_wait();
+    if (p.offsets != nullptr || p.seg_counts != nullptr) grid_dep_wait();
+    // expert-parallel: every source has dispatched its rows (and its counter updates); after a
+    // timeout (status 2) the groups are taken as empty, so the CTA does no work
+    const bool counts_ok = !(p.setup_wait && p.wait_count > 0) ||
+                           wait_flags_warp(p.wait_flags, p.wait_seq, p.wait_count, p.wait_timeout_ns, p.status, lane);
     int carry = 0;
     for (int base = 0; base < groups; base += 32) {
       const int g = base + lane;
       int rows = 0;
       if (g < groups) {
-        const int o0 = p.offsets ? p.offsets[g] : 0;
-        const int o1 = p.offsets ? p.offsets[g + 1] : p.rows;
+        int o0, o1;
+        if (p.seg_counts != nullptr) {
+          int c = counts_ok ? p.seg_counts[g] : 0;
+          c = c < 0 ? 0 : (c > p.seg_cap ? p.seg_cap : c);
+          if (blockIdx.x == 0 && p.seg_counts_copy != nullptr) p.seg_counts_copy[g] = c;
+          o0 = g * p.seg_cap;
+          o1 = o0 + c;
+        } else {
+          o0 = p.offsets ? p.offsets[g] : 0;
+          o1 = p.offsets ? p.offsets[g + 1] : p.rows;
+        }
         offs_s[g] = o0;
+        ends_s[g] = o1;
         if (g == groups - 1) offs_s[groups] = o1;
         rows = o1 - o0;
       }
@@ -273,11 +338,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       // waiting for the previous kernel (weights never depend on it); their activation tiles
       // follow the wait on the same stage barriers.
       int pre = 0;
-      if (p.pdl_prefetch_a && p.offsets == nullptr && p.wait_count == 0 && static_cast<int>(blockIdx.x) < total_work) {
+      if (p.pdl_prefetch_a && p.offsets == nullptr && p.seg_counts == nullptr && p.wait_count == 0 &&
+          static_cast<int>(blockIdx.x) < total_work) {
         const int w = blockIdx.x;
         const int t = w / ks, split = w - t * ks;
         int g, mt, nt;
-        decode_tile<BN>(t, prefix_s, offs_s, groups, g, mt, nt);
+        decode_tile<BN>(t, prefix_s, offs_s, ends_s, groups, g, mt, nt);
         const int a_row = g * p.a_rows + mt * kBM;
         const int kb0 = split * kb_per, kb1 = min(num_kb, kb0 + kb_per);
         pre = min(C::kStages, kb1 - kb0);
@@ -289,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       grid_dep_wait();
-      if (p.wait_count > 0) {
+      if (p.wait_count > 0 && !p.setup_wait) {
         // the activations are gathered from the other ranks: wait (bounded) until all have landed
         const uint32_t target = *reinterpret_cast<const volatile uint32_t*>(p.wait_seq);
         const uint64_t t0 = globaltimer_ns();
@@ -305,6 +371,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           } while (true);
         }
       }
+      // Rows that peers stored with generic-proxy writes are read below by TMA (async proxy).
+      if (p.wait_count > 0) asm volatile("fence.proxy.async.global;" ::: "memory");
       int stage = 0;
       uint32_t phase = 0;
       long issued = 0;
@@ -312,7 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int w = blockIdx.x; w < total_work && ok; w += gridDim.x) {
         const int t = w / ks, split = w - t * ks;
         int g, mt, nt;
-        decode_tile<BN>(t, prefix_s, offs_s, groups, g, mt, nt);
+        decode_tile<BN>(t, prefix_s, offs_s, ends_s, groups, g, mt, nt);
         const int a_row = g * p.a_rows + mt * kBM;
         const int b_row = offs_s[g] + nt * BN;
         const int kb0 = split * kb_per, kb1 = min(num_kb, kb0 + kb_per);
@@ -402,14 +470,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int w = blockIdx.x; w < total_work; w += gridDim.x, ++local) {
       const int t = w / ks;
       int g, mt, nt;
-      decode_tile<BN>(t, prefix_s, offs_s, groups, g, mt, nt);
+      decode_tile<BN>(t, prefix_s, offs_s, ends_s, groups, g, mt, nt);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, p.status)) break;
       tc_fence_after();
       const int m = mt * kBM + lane_base + lane;
       const int row0 = offs_s[g] + nt * BN;
-      const int row_end = offs_s[g + 1];
+      const int row_end = ends_s[g];
       const bool m_ok = m < p.m_out;
       float bias_v = 0.f;
       if (p.bias != nullptr && m_ok) bias_v = __bfloat162float(p.bias[static_cast<int64_t>(g) * p.m_out + m]);
@@ -486,7 +554,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&ov);
 #pragma unroll
                 for (int j = 0; j < 4; ++j) oh[j] = __floats2bfloat162_rn(o[2 * j], o[2 * j + 1]);
-                *reinterpret_cast<uint4*>(out_row_bf16(p, row) + mm) = ov;
+                __nv_bfloat16* orow = out_row_bf16(p, row);
+                if (orow != nullptr) *reinterpret_cast<uint4*>(orow + mm) = ov;
               }
             }
           }
@@ -510,7 +579,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (p.out_f32) {
                 static_cast<float*>(p.out)[static_cast<int64_t>(row) * p.ldo + m] = v;
               } else {
-                out_row_bf16(p, row)[m] = __float2bfloat16(v);
+                __nv_bfloat16* orow = out_row_bf16(p, row);
+                if (orow != nullptr) orow[m] = __float2bfloat16(v);
               }
             }
           }
@@ -573,12 +643,35 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (row < row_end && mm < p.m_out) {
                 void* orow = p.out_f32 ? static_cast<void*>(static_cast<float*>(p.out) + static_cast<int64_t>(row) * p.ldo)
                                        : static_cast<void*>(out_row_bf16(p, row));
+                if (orow != nullptr)
                 store_out4(p.bias == nullptr ? nullptr : p.bias + static_cast<int64_t>(g) * p.m_out, p.residual, p.ldr,
                            orow, p.out_f32, p.act, mm, p.m_out, p.vec4, row, acc[u]);
               }
             }
           }
         }
+      }
+    }
+  }
+
+  if (!CL && warp >= 2 && p.signal_count > 0) {
+    // Completion signal (expert-parallel combine): each epilogue thread fences its stores at
+    // system scope, the CTA arrives once, and the last CTA to arrive release-stores the layer's
+    // sequence number into every peer's flag.  CTA 0 clears the per-expert counters first.
+    __threadfence_system();
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (threadIdx.x == 64) {
+      if (blockIdx.x == 0 && p.zero_ptr != nullptr) {
+        for (int i = 0; i < p.zero_n; ++i) p.zero_ptr[i] = 0;
+        __threadfence_system();
+      }
+      const int prev = atomicAdd(p.arrive_counter, 1);
+      if (prev == static_cast<int>(gridDim.x) - 1) {
+        *p.arrive_counter = 0;
+        __threadfence_system();
+        const uint32_t seq = *reinterpret_cast<const volatile uint32_t*>(p.signal_seq);
+        for (int d = 0; d < p.signal_count; ++d)
+          asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.signal_flags[d]), "r"(seq) : "memory");
       }
     }
   }
@@ -594,9 +687,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int t = static_cast<int>(blockIdx.x) / ks;
       const uint32_t rank = cluster_ctarank();
       int g, mt, nt;
-      decode_tile<BN>(t, prefix_s, offs_s, groups, g, mt, nt);
+      decode_tile<BN>(t, prefix_s, offs_s, ends_s, groups, g, mt, nt);
       const int row0 = offs_s[g] + nt * BN;
-      const int row_end = offs_s[g + 1];
+      const int row_end = ends_s[g];
       const int per = (BN + ks - 1) / ks;
       const int tok_lo = static_cast<int>(rank) * per, tok_hi = min(BN, tok_lo + per);
       const int n4 = max(0, tok_hi - tok_lo) * (kBM / 4);
@@ -625,6 +718,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (row < row_end && mm < p.m_out) {
           void* orow = p.out_f32 ? static_cast<void*>(static_cast<float*>(p.out) + static_cast<int64_t>(row) * p.ldo)
                                  : static_cast<void*>(out_row_bf16(p, row));
+          if (orow != nullptr)
           store_out4(p.bias == nullptr ? nullptr : p.bias + static_cast<int64_t>(g) * p.m_out, p.residual, p.ldr, orow,
                      p.out_f32, p.act, mm, p.m_out, p.vec4, row, acc);
         }
@@ -732,17 +826,13 @@ bool pdl_enabled() {
 template <int BN, bool GATED, bool ACT>
 cudaError_t launch(const GemmArgs& a, cudaStream_t stream) {
   using C = Cfg<BN, GATED>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_bf16_kernel<BN, GATED, ACT, false>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  {
+    cudaError_t e = ensure_smem_attr<gemm_bf16_kernel<BN, GATED, ACT, false>>(C::kSmemBytes);
     if (e != cudaSuccess) return e;
     if constexpr (!GATED) {
-      e = cudaFuncSetAttribute(gemm_bf16_kernel<BN, GATED, ACT, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               C::kSmemBytes);
+      e = ensure_smem_attr<gemm_bf16_kernel<BN, GATED, ACT, true>>(C::kSmemBytes);
       if (e != cudaSuccess) return e;
     }
-    attr_set = true;
   }
   CUtensorMap ta, tb;
   if (!make_tmap_2d(&ta, a.a, static_cast<uint64_t>(a.groups) * a.a_rows, a.k, a.k, kBM)) return cudaErrorInvalidValue;
@@ -779,11 +869,26 @@ cudaError_t launch(const GemmArgs& a, cudaStream_t stream) {
   p.wait_seq = a.wait_seq;
   p.wait_count = a.wait_flags != nullptr && a.wait_seq != nullptr ? a.wait_count : 0;
   p.wait_timeout_ns = a.wait_timeout_ns;
+  p.seg_cap = a.seg_cap;
+  p.seg_counts = a.seg_cap > 0 ? a.seg_counts : nullptr;
+  p.seg_counts_copy = a.seg_counts_copy;
+  p.setup_wait = a.setup_wait;
+  p.row_tag = a.row_tag;
+  p.peer_rows = a.peer_rows;
+  p.tag_ranks = a.tag_ranks;
+  p.tag_slots = a.tag_slots;
+  p.signal_flags = a.signal_flags;
+  p.signal_seq = a.signal_seq;
+  p.signal_count = a.signal_flags != nullptr && a.signal_seq != nullptr && a.arrive_counter != nullptr
+                       ? a.signal_count : 0;
+  p.arrive_counter = a.arrive_counter;
+  p.zero_ptr = a.zero_ptr;
+  p.zero_n = a.zero_n;
   const int m_tiles = (a.m_out + kBM - 1) / kBM;
   const int num_kb = (a.k + kBK - 1) / kBK;
   // Split-K for dense GEMMs that would leave most SMs idle (decode projections).
   p.cluster_splitk = 0;
-  if (!GATED && a.offsets == nullptr && (a.splitk_ws != nullptr || a.splitk_cluster)) {
+  if (!GATED && a.offsets == nullptr && a.seg_cap <= 0 && (a.splitk_ws != nullptr || a.splitk_cluster)) {
     const long tiles = static_cast<long>(m_tiles) * ((a.rows + BN - 1) / BN);
     const int sms = num_sms();
     if (tiles * 2 <= sms && num_kb >= 4) {
@@ -818,7 +923,8 @@ cudaError_t launch(const GemmArgs& a, cudaStream_t stream) {
     }
   }
   // Upper bound of the tile count: every group may add one partial token tile.
-  const long row_tiles = (a.offsets ? (static_cast<long>(a.rows) + BN - 1) / BN + a.groups : (a.rows + BN - 1) / BN);
+  const bool grouped = a.offsets != nullptr || a.seg_cap > 0;
+  const long row_tiles = (grouped ? (static_cast<long>(a.rows) + BN - 1) / BN + a.groups : (a.rows + BN - 1) / BN);
   const long bound = static_cast<long>(m_tiles) * (row_tiles > 0 ? row_tiles : 1) * p.k_splits;
   int grid = a.max_ctas > 0 ? a.max_ctas : num_sms();
   if (bound < grid) grid = static_cast<int>(bound);
@@ -872,7 +978,11 @@ cudaError_t launch(const GemmArgs& a, cudaStream_t stream) {
 cudaError_t gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   if (a.groups < 1 || a.groups > kMaxGroups || a.k <= 0 || a.m_out <= 0) return cudaErrorInvalidValue;
   if (a.k % 8 != 0) return cudaErrorInvalidValue;  // 16-byte row stride for TMA
-  if (a.rows == 0) return cudaSuccess;
+  if (a.seg_cap > 0 && (a.seg_counts == nullptr || static_cast<long long>(a.seg_cap) * a.groups > a.rows))
+    return cudaErrorInvalidValue;
+  if (a.row_tag != nullptr && (a.peer_rows == nullptr || a.out_f32 || a.tag_ranks < 1)) return cudaErrorInvalidValue;
+  // a GEMM that signals completion must run even without rows: its peers wait for the flags
+  if (a.rows == 0 && a.signal_count == 0) return cudaSuccess;
   int hint = a.expected_rows_per_group > 0 ? a.expected_rows_per_group : a.rows;
   if (a.gated) {
     if (hint <= 16) return launch<16, true, false>(a, stream);

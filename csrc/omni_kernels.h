@@ -63,6 +63,31 @@ struct GemmArgs {
   // parameters): with programmatic dependent launch the GEMM may fetch its first weight
   // tiles before the previous kernel has finished.
   int static_a;
+  // ---- expert-parallel fused modes (the grouped GEMMs of an EP MoE layer, csrc/ep_moe.cu)
+  // Segment layout instead of offsets: group g's rows are B rows [g * seg_cap, g * seg_cap +
+  // min(seg_counts[g], seg_cap)) and the output rows with the same indices.  CTA 0 copies the
+  // counts it used into seg_counts_copy (when set) for a later kernel of the layer.
+  int seg_cap;
+  const int* seg_counts;
+  int* seg_counts_copy;
+  // wait_flags are awaited before the group counts are read (they are final only then), not
+  // just before the first operand load.
+  int setup_wait;
+  // Combine epilogue: bf16 output row r is stored at peer_rows[row_tag[2r]] + row_tag[2r + 1] * ldo,
+  // i.e. into the slot of the routed row on its source rank; tags outside [0, tag_ranks) x
+  // [0, tag_slots) drop the row.
+  const int* row_tag;
+  const unsigned long long* peer_rows;
+  int tag_ranks, tag_slots;
+  // Completion signal: when every CTA has stored its outputs, the last CTA to finish
+  // release-stores *signal_seq into signal_flags[d] for d < signal_count (one address per
+  // rank).  CTA 0 first clears zero_ptr[0 .. zero_n).  arrive_counter is zero between calls.
+  const unsigned long long* signal_flags;
+  const unsigned int* signal_seq;
+  int signal_count;
+  int* arrive_counter;
+  int* zero_ptr;
+  int zero_n;
 };
 cudaError_t gemm_bf16(const GemmArgs& args, cudaStream_t stream);
 
@@ -191,6 +216,13 @@ struct MoeCombineArgs {
   int local_experts;
   const unsigned long long* peer_out;
   int rows_per;
+  // expert-parallel: wait (bounded) until wait_flags[i] reaches *wait_seq for i < wait_count
+  // (every expert owner has stored this rank's routed rows) before reading y_perm
+  const unsigned int* wait_flags;
+  const unsigned int* wait_seq;
+  int wait_count;
+  int* status;
+  long long wait_timeout_ns;
 };
 cudaError_t moe_combine(const MoeCombineArgs& a, cudaStream_t stream);
 
@@ -262,25 +294,27 @@ cudaError_t dwconv1d_causal(const void* x, const float* w, const float* bias, vo
 cudaError_t conv2d_im2col(const void* x, void* out, int N, int H, int W, int C, int Ho, int Wo, int kh, int kw,
                           int stride, int pad, int K_stride, cudaStream_t stream);
 
-// Expert-parallel MoE exchange over peer memory (csrc/ep_moe.cu).
-struct EpArgs {
+// Expert-parallel MoE dispatch over peer memory (csrc/ep_moe.cu).  Every rank's
+// symmetric buffer holds, at the same offsets:
+//   flags   u32 [2][world]        [0][s]: source s has dispatched this layer's rows here,
+//                                 [1][s]: owner s has stored this rank's expert outputs
+//   cursor  i32 [El]              rows received per local expert (peers add with system atomics)
+//   recv_x  bf16 [El * seg_cap, H]   segment g = rows routed to local expert g
+//   recv_tag i32 [El * seg_cap, 2]   (source rank, source slot = token * topk + k) of every row
+//   comb    bf16 [max_slots, H]   expert outputs of this rank's routed rows, by slot
+struct EpDispatchArgs {
   int rank, world, experts, local_experts, topk, hidden;
-  int tokens;                  // local tokens of this call
+  int tokens;                  // this rank's tokens
   const int* topk_ids;         // [tokens, topk]
-  const void* x;               // [tokens, hidden] bf16 (dispatch)
-  const int64_t* peer_base;    // [world] base address of every rank's symmetric buffer (this process's mapping)
-  int64_t off_counts, off_flags, off_recv_x, off_recv_meta, off_comb;
-  int cap_rows, max_slots;
-  int* cursor;                 // [experts] scratch
-  int* local_offsets;          // [local_experts + 1] group offsets of the received rows
-  int* total_rows;             // [1]
-  uint32_t* epoch;             // [1] layer counter, bumped by ep_counts
+  const void* x;               // [tokens, hidden] bf16
+  const int64_t* peer_base;    // [world] base address of every rank's symmetric buffer
+  int64_t off_flags, off_cursor, off_recv_x, off_recv_tag;
+  int seg_cap;
+  uint32_t* seq;               // [1] layer sequence number, bumped by the last CTA
+  int* arrive;                 // [1] CTA arrival counter, zero between calls
   int* status;
-  uint64_t timeout_ns;
 };
-cudaError_t ep_counts(const EpArgs& a, cudaStream_t stream);
-cudaError_t ep_dispatch(const EpArgs& a, cudaStream_t stream);
-cudaError_t ep_combine(const EpArgs& a, const void* y, int64_t y_stride, cudaStream_t stream);
+cudaError_t ep_dispatch(const EpDispatchArgs& a, cudaStream_t stream);
 
 // ---------------------------------------------------------------- tensor parallel
 struct TpReduceArgs {

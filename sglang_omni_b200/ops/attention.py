@@ -148,12 +148,17 @@ def _resident_decode_ctas(device, head_dim: int) -> int:
     return _SM_COUNT[idx] * (3 if head_dim > 64 else 6)
 
 
+# Keys per split of decode batches whose (request, KV head) pairs alone fill the GPU.
+FILL_SPLIT_KEYS = 2048
+
+
 class DecodeWorkspace:
     """Split-KV scratch of the decode kernel, sized for a max batch / context."""
 
     def __init__(self, max_batch: int, num_heads: int, head_dim: int, max_context: int, device,
                  keys_per_split: int = 256):
         self.keys_per_split = keys_per_split
+        self.max_context = max_context
         self.max_splits = max(1, (max_context + keys_per_split - 1) // keys_per_split)
         self.part_o = torch.empty(max_batch * num_heads * self.max_splits * head_dim, dtype=torch.float32,
                                   device=device)
@@ -189,11 +194,18 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     # (148 SMs x 3 CTAs of 68 KB at head_dim 128, 6 at 64), any split adds a partial wave and
     # the merge: one split per pair is fastest (64 x 4 pairs at 1.1-1.3 k context: 41-46 us vs
     # 52-56 us at 512 keys per split, 56-62 us at 256).
+    # The rule looks only at shapes known when a decode graph is captured, not at the context
+    # lengths of one step: GPU-filling batches take splits of FILL_SPLIT_KEYS keys, so contexts up
+    # to that length run as one split per pair while one much longer context (a skewed batch)
+    # still spreads over several CTAs instead of one CTA walking all of it.  The splits past a
+    # request's length exit at once.
     kps, splits = workspace.keys_per_split, workspace.max_splits
     if 2 * B * num_kv_heads > _resident_decode_ctas(q.device, head_dim):
-        splits = 1
+        kps = max(kps, FILL_SPLIT_KEYS)
     elif B * num_kv_heads >= 128 and kps < 512:
         kps = 2 * kps
+    # no grid slots for splits that no context within the workspace's bound can use
+    splits = max(1, min(splits, -(-getattr(workspace, "max_context", kps * splits) // kps)))
     ext().attention_decode(q, k_cache, v_cache, out, block_table, kv_lens, num_heads, num_kv_heads, head_dim, scale,
                            kps, splits, workspace.part_o, workspace.part_lse,
                            getattr(workspace, "counters", None))

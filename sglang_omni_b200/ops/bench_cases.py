@@ -190,8 +190,20 @@ def _time_cases() -> None:
         ws = A.DecodeWorkspace(nb, hq, d, ctx, "cuda")
         res[f"decode_attn B{nb} ctx1152"] = (t(lambda: A.decode_attention(q[:nb], k, v, bt[:nb], kl[:nb], hq, hkv, d,
                                                                           ws)), 2 * nb * ctx * hkv * d * 2)
+    # skewed batch: 63 requests at 1152 keys and one at 8192 (its pages follow the others')
+    long_pages = 8192 // 64
+    ks = torch.randn(B * pages + long_pages + 1, hkv, 64, d, device="cuda").bfloat16()
+    vs = torch.randn_like(ks)
+    bts = torch.zeros(B, long_pages, dtype=torch.int32, device="cuda")
+    bts[:, :pages] = bt
+    bts[B - 1] = torch.arange(B * pages, B * pages + long_pages, dtype=torch.int32, device="cuda")
+    kls = kl.clone()
+    kls[B - 1] = 8192
+    ws = A.DecodeWorkspace(B, hq, d, 8192, "cuda")
+    res["decode_attn B64 ctx1152 + one 8192"] = (t(lambda: A.decode_attention(q, ks, vs, bts, kls, hq, hkv, d, ws)),
+                                                 2 * (63 * ctx + 8192) * hkv * d * 2)
     for name, (us, nbytes) in res.items():
-        print(f"{name:32s} {us:8.2f} us  {nbytes / us / 1e3:7.1f} GB/s")
+        print(f"{name:36s} {us:8.2f} us  {nbytes / us / 1e3:7.1f} GB/s")
 
 
 if __name__ == "__main__":

@@ -12,11 +12,14 @@ after warm-up, averaged over ``--iters`` iterations, the max over ranks.
   the GEMM FLOPs at the measured sustained bf16 rate and the bytes each GPU must
   send (its (N-1)/N partial rows + (N-1) copies of its normalised owned rows) at
   the measured 770 GB/s per direction.
-* EP MoE layer (128 experts, top-8, hidden 2048, expert width 768 at EP=N): router,
-  count exchange, dispatch straight into the owners' expert-major buffers, the
-  local grouped GEMMs, combine back to the source slots and the top-k weighted
-  sum.  Roofline: the slowest of this rank's expert weights at the measured HBM
-  copy rate, the expert GEMM FLOPs at the sustained bf16 rate and the dispatched +
+* EP MoE layer (128 experts, top-8, hidden 2048, expert width 768 at EP=N): router
+  and top-k, dispatch straight into the owners' expert segments, the grouped GEMMs
+  (w13 waits for the dispatch flags itself, the w2 epilogue stores the rows into
+  the source ranks' slots), the top-k weighted sum waiting for the owners' flags;
+  against the NCCL all-to-all dispatcher (count all-to-all + host copy of the split
+  sizes, ``all_to_all_single`` of the rows both ways, the same grouped GEMMs).
+  Roofline: the slowest of this rank's expert weights at the measured HBM copy
+  rate, the expert GEMM FLOPs at the sustained bf16 rate and the dispatched +
   combined rows at 770 GB/s.
 """
 from __future__ import annotations
@@ -86,6 +89,57 @@ def tp_reduce_point(T: int, iters: int, rank: int, world: int) -> dict:
             "fused_frac_of_roofline": round(roof / t_f, 3), "speedup_vs_nccl": round(t_n / t_f, 3)}
 
 
+class _NcclEP:
+    """NCCL baseline of one EP MoE layer (the all-to-all token dispatcher of Megatron-style EP):
+    route, permute the rows by expert locally, exchange the per-expert counts with an
+    all-to-all, copy them to the host (the variable split sizes of the next all-to-all), send
+    the rows with ``all_to_all_single``, reorder them expert-major, run the same grouped
+    GEMMs, undo the reorder, send the outputs back and do the top-k weighted sum."""
+
+    def __init__(self, E, topk, H, I, T, world, rank, dev):
+        from ..ops.moe import MoEWorkspace
+
+        self.E, self.topk, self.H, self.I, self.world, self.rank = E, topk, H, I, world, rank
+        self.El = E // world
+        self.ws = MoEWorkspace(T, E, topk, H, I, dev)
+        self.dev = dev
+
+    def forward(self, x, wr, w13, w2, out):
+        from ..ops import gemm
+        from ..ops._ext import ext
+        from ..ops.moe import route
+
+        T, k, El, W = x.shape[0], self.topk, self.El, self.world
+        ws = self.ws
+        logits = gemm.linear(x, wr, out_dtype=torch.float32)
+        route(logits, k, ws=ws, x=x)                        # ids, weights, offsets, inv_perm, x_perm (expert-major)
+        cnt = (ws.offsets[1:] - ws.offsets[:-1]).view(W, El)  # rows of this rank for each (destination, expert)
+        rcnt = torch.empty_like(cnt)
+        dist.all_to_all_single(rcnt, cnt)                    # rows each source sends to my experts
+        c_send, c_recv = cnt.cpu(), rcnt.cpu()               # host sync: the split sizes
+        send = c_send.sum(1).tolist()
+        recv = c_recv.sum(1).tolist()
+        rows_in = sum(recv)
+        xr = torch.empty(rows_in, self.H, dtype=x.dtype, device=self.dev)
+        dist.all_to_all_single(xr, ws.x_perm[: T * k], recv, send)
+        # source-major [s][e] blocks -> expert-major [e][s]
+        starts = torch.cumsum(torch.cat([torch.zeros(1, dtype=torch.long), c_recv.flatten()]), 0)
+        idx = torch.cat([torch.arange(int(starts[s * El + e]), int(starts[s * El + e + 1]))
+                         for e in range(El) for s in range(W)]) if rows_in else torch.zeros(0, dtype=torch.long)
+        idx = idx.to(self.dev, non_blocking=True)
+        offs = torch.cat([torch.zeros(1, dtype=torch.long), torch.cumsum(c_recv.sum(0), 0)]).to(torch.int32)
+        offs = offs.to(self.dev, non_blocking=True)
+        xe = xr.index_select(0, idx)
+        h = gemm.grouped_linear(xe, w13, offs, gated=True, expected_rows=max(1, rows_in // El))
+        ye = gemm.grouped_linear(h, w2, offs, expected_rows=max(1, rows_in // El))
+        yr = torch.empty_like(xr)
+        yr.index_copy_(0, idx, ye)
+        yb = torch.empty(T * k, self.H, dtype=x.dtype, device=self.dev)
+        dist.all_to_all_single(yb, yr, send, recv)
+        ext().moe_combine(yb, ws.inv_perm[:T], ws.topk_w[:T], out, None, None)
+        return out
+
+
 def ep_moe_layer(T: int, iters: int, rank: int, world: int) -> dict:
     from .ep_moe import EPMoE
 
@@ -100,20 +154,30 @@ def ep_moe_layer(T: int, iters: int, rank: int, world: int) -> dict:
     ep = EPMoE(E, topk, H, I, max_tokens=T, device=dev)
     out = torch.empty_like(x)
     t_f = _time(lambda: ep.forward(x, wr, w13, w2, out=out), iters)
+    ref = _NcclEP(E, topk, H, I, T, world, rank, dev)
+    out_n = torch.empty_like(x)
+    t_n = _time(lambda: ref.forward(x, wr, w13, w2, out_n), iters)
+    ep.forward(x, wr, w13, w2, out=out)
+    torch.cuda.synchronize()
+    err = float((out.float() - out_n.float()).norm() / out_n.float().norm().clamp_min(1e-6))
     ep.close()
     wbytes = El * 3 * H * I * 2
     flops = T * topk * 2.0 * 3 * H * I                    # rows landing on this rank (T * topk on average)
     rows = T * topk * (world - 1) / world                 # (token, k) rows that leave this rank
     link = rows * H * 2 * 2                                # dispatched and combined back
     roof = max(wbytes / (HBM_GBS * 1e3), flops / (BF16_TFLOPS * 1e6), link / (NVLINK_GBS * 1e3))
-    return {"path": "EP MoE layer: count exchange + dispatch into owners' expert buffers + grouped GEMMs + "
-                    "combine + top-k sum", "tokens_per_rank": T, "fused_us": round(t_f, 2),
-            "roofline_us": round(roof, 2), "fused_frac_of_roofline": round(roof / t_f, 3)}
+    return {"path": "EP MoE layer: router + top-k, dispatch into the owners' expert segments (system-atomic "
+                    "reservations), w13 GEMM waiting on the dispatch flags, w2 GEMM storing rows into the "
+                    "source ranks' slots, combine waiting on the owners' flags", "tokens_per_rank": T,
+            "fused_us": round(t_f, 2), "nccl_us": round(t_n, 2), "roofline_us": round(roof, 2),
+            "fused_frac_of_roofline": round(roof / t_f, 3), "speedup_vs_nccl": round(t_n / t_f, 3),
+            "rel_diff_vs_nccl": round(err, 4)}
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--paths", default="tp,ep", help="comma list of tp, ep")
     args = ap.parse_args()
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -125,10 +189,13 @@ def main():
 
     _ext.ext()
     rows = []
-    for T in (64, 8192):
-        rows.append(tp_reduce_point(T, args.iters, rank, world))
-    for T in (64, 2048):
-        rows.append(ep_moe_layer(T, args.iters, rank, world))
+    paths = args.paths.split(",")
+    if "tp" in paths:
+        for T in (64, 8192):
+            rows.append(tp_reduce_point(T, args.iters, rank, world))
+    if "ep" in paths:
+        for T in (64, 2048):
+            rows.append(ep_moe_layer(T, args.iters, rank, world))
     _ext.check_status(torch.device("cuda", local))
     if rank == 0:
         for r in rows:

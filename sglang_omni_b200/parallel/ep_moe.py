@@ -1,23 +1,28 @@
 """Expert-parallel MoE over NVLink peer memory.
 
 Each rank of the EP group owns ``experts / world`` consecutive experts and runs
-attention on its own tokens (data-parallel attention).  One MoE layer:
+attention on its own tokens (data-parallel attention).  One MoE layer is four
+kernels after the router GEMM and top-k, with the two cross-rank waits inside
+the kernels that consume the data:
 
-  1. route locally (gate GEMM + top-k kernel);
-  2. ``ep_counts``: per-expert counts of every rank are exchanged through the
-     symmetric buffer; every rank derives the same row offsets;
-  3. ``ep_dispatch``: every (token, k) row is stored directly into its expert
-     owner's receive buffer, already in expert-major order (the permutation of
-     a local MoE and the all-to-all in one kernel), then a flag barrier;
-  4. the owner runs its two grouped GEMMs (gate/up with SiLU*up in the
-     epilogue, then down) over the received rows;
-  5. ``ep_combine``: every expert-output row is stored back into its source
-     rank's slot, flag barrier, and the source does the top-k weighted sum
-     (+ gated shared expert) with ``moe_combine``.
+  1. ``ep_dispatch``: every (token, k) row is stored straight into its expert
+     owner's receive segment for that expert (a CTA reserves its rows of an
+     expert with one system-scope atomic on the owner's counter, so no count
+     exchange comes first); the last CTA raises this rank's dispatch flag on
+     every peer;
+  2. the gated w13 grouped GEMM (tcgen05, SiLU*up in the epilogue) waits for
+     every source's dispatch flag, reads the final per-expert counts and runs
+     over the received segments (local memory, TMA);
+  3. the w2 grouped GEMM's epilogue stores each output row into the ``comb``
+     slot of the rank the row came from (over NVLink), then raises this rank's
+     combine flag on every peer;
+  4. ``moe_combine`` waits for every owner's combine flag, then does the top-k
+     weighted sum (+ the next block's residual add + RMSNorm).
 
-All steps are device-side (no host synchronisation), so a decode step with
-its 48 MoE layers is captured in one CUDA graph.  The reference only has
-SGLang's EP/all-reduce call sites, never enabled
+All steps are device-side (no host synchronisation, sequence numbers on the
+device), so a decode step with its 48 MoE layers is one CUDA graph.  Every rank
+must run every layer (the flags are collective).  The reference only has
+SGLang's EP / all-reduce call sites, never enabled
 (sglang_omni/models/qwen3_omni/thinker.py:402-453).
 """
 from __future__ import annotations
@@ -25,49 +30,59 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 
-from ..ops import route
 from ..ops._ext import ext, status_word
-from ..ops.gemm import grouped_linear, linear
+from ..ops.gemm import linear
 from .symm import RegionLayout, SymmetricBuffer
 
 
 class EPMoE:
     def __init__(self, experts: int, topk: int, hidden: int, inter: int, max_tokens: int, device,
-                 group=None, dtype=torch.bfloat16, cap_rows: int | None = None, timeout_s: float = 2.0):
+                 group=None, dtype=torch.bfloat16, timeout_s: float = 2.0):
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         assert experts % self.world == 0, "experts must divide evenly over the EP group"
         self.experts, self.topk, self.hidden, self.inter = experts, topk, hidden, inter
-        self.local_experts = experts // self.world
+        self.local_experts = El = experts // self.world
         self.max_tokens = max_tokens
         self.max_slots = max_tokens * topk
-        self.cap_rows = cap_rows or self.world * self.max_slots
-        self.device = torch.device(device)
+        # an expert receives at most one row per token of every rank
+        self.seg_cap = self.world * max_tokens
+        self.device = dev = torch.device(device)
         self.timeout_s = timeout_s
         lay = RegionLayout()
-        lay.add("counts", self.world * experts * 4)
-        lay.add("flags", 3 * self.world * 4)
-        lay.add("recv_x", self.cap_rows * hidden * 2)
-        lay.add("recv_meta", self.cap_rows * 2 * 4)
+        lay.add("flags", 2 * self.world * 4)
+        lay.add("cursor", El * 4)
+        lay.add("recv_x", El * self.seg_cap * hidden * 2)
+        lay.add("recv_tag", El * self.seg_cap * 2 * 4)
         lay.add("comb", self.max_slots * hidden * 2)
         self.layout = lay
-        self.buf = SymmetricBuffer(lay.size, group, self.device)
+        self.buf = SymmetricBuffer(lay.size, group, dev)
         o = lay.offsets
-        self.offs = [o["counts"], o["flags"], o["recv_x"], o["recv_meta"], o["comb"]]
-        self.recv_x = self.buf.view(o["recv_x"], (self.cap_rows, hidden), dtype)
+        self.offs = [o["flags"], o["cursor"], o["recv_x"], o["recv_tag"], o["comb"]]
+        self.flags = self.buf.view(o["flags"], (2, self.world), torch.int32)
+        self.cursor = self.buf.view(o["cursor"], (El,), torch.int32)
+        self.recv_x = self.buf.view(o["recv_x"], (El * self.seg_cap, hidden), dtype)
+        self.recv_tag = self.buf.view(o["recv_tag"], (El * self.seg_cap, 2), torch.int32)
         self.comb = self.buf.view(o["comb"], (self.max_slots, hidden), dtype)
-        dev = self.device
-        self.cursor = torch.zeros(experts, dtype=torch.int32, device=dev)
-        self.local_offsets = torch.zeros(self.local_experts + 1, dtype=torch.int32, device=dev)
-        self.total_rows = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.epoch = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.h_perm = torch.empty(self.cap_rows, inter, dtype=dtype, device=dev)
-        self.y_perm = torch.empty(self.cap_rows, hidden, dtype=dtype, device=dev)
+        with torch.cuda.device(dev):
+            self.flags.zero_()
+            self.cursor.zero_()
+            torch.cuda.synchronize(dev)
+        dist.barrier(group)
+        peers = self.buf.peers
+        r, w = self.rank, self.world
+        # where this rank raises its combine flag on every peer: flags[1][r] (the dispatch kernel
+        # derives flags[0][r] from the buffer bases itself)
+        self.sig_combine = torch.tensor([b + o["flags"] + 4 * (w + r) for b in peers], dtype=torch.int64, device=dev)
+        self.peer_comb = torch.tensor([b + o["comb"] for b in peers], dtype=torch.int64, device=dev)
+        self.seq = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.arrive = torch.zeros(2, dtype=torch.int32, device=dev)   # dispatch CTAs, w2 CTAs
+        self.seg_counts = torch.zeros(El, dtype=torch.int32, device=dev)
+        self.h_seg = torch.empty(El * self.seg_cap, inter, dtype=dtype, device=dev)
         self.slots = torch.arange(self.max_slots, dtype=torch.int32, device=dev)
-
-    def _common(self, ids):
-        return (ids, self.buf.peer_base, self.offs, self.rank, self.world, self.experts)
+        self.topk_ids = torch.empty(max_tokens, topk, dtype=torch.int32, device=dev)
+        self.topk_w = torch.empty(max_tokens, topk, dtype=torch.float32, device=dev)
 
     def forward(self, x: torch.Tensor, w_router: torch.Tensor, w13_local: torch.Tensor, w2_local: torch.Tensor,
                 renormalize: bool = True, mode: int = 0, bias=None, n_group: int = 1, topk_group: int = 1,
@@ -81,32 +96,29 @@ class EPMoE:
         T = x.shape[0]
         assert T <= self.max_tokens, f"{T} tokens > EP buffer capacity {self.max_tokens}"
         st = status_word(x.device)
-        logits = linear(x, w_router, out_dtype=torch.float32)
-        ids, w = route(logits, self.topk, mode, bias, n_group, topk_group, renormalize, scaling)
         e = ext()
-        ids_c = ids.contiguous()
-        e.ep_counts(ids_c, self.buf.peer_base, self.offs, self.rank, self.world, self.experts, self.hidden,
-                    self.cap_rows, self.max_slots, self.cursor, self.local_offsets, self.total_rows, self.epoch, st,
-                    self.timeout_s)
-        e.ep_dispatch(x.contiguous(), ids_c, self.buf.peer_base, self.offs, self.rank, self.world, self.experts,
-                      self.cap_rows, self.max_slots, self.cursor, self.local_offsets, self.total_rows, self.epoch, st,
-                      self.timeout_s)
+        logits = linear(x, w_router, out_dtype=torch.float32)
+        ids, w = self.topk_ids[:T], self.topk_w[:T]
+        e.moe_route(logits, self.topk, mode, bias, n_group, topk_group, renormalize, scaling, ids, w, None, None,
+                    None, None, None, None, 0, 0)
+        x = x.contiguous()
+        e.ep_dispatch(x, ids, self.buf.peer_base, self.offs, self.rank, self.world, self.experts, self.seg_cap,
+                      self.seq, self.arrive[0:1], st)
         exp_rows = max(1, (T * self.topk * self.world) // self.experts)
-        grouped_linear(self.recv_x, w13_local, self.local_offsets, gated=True, out=self.h_perm,
-                       expected_rows=exp_rows)
-        grouped_linear(self.h_perm, w2_local, self.local_offsets, gated=False, out=self.y_perm,
-                       expected_rows=exp_rows)
-        e.ep_combine(self.y_perm, ids_c, self.buf.peer_base, self.offs, self.rank, self.world, self.experts,
-                     self.cap_rows, self.max_slots, self.cursor, self.local_offsets, self.total_rows, self.epoch, st,
-                     self.timeout_s)
+        e.gemm_ep(w13_local, self.recv_x, self.h_seg, self.inter, True, self.seg_cap, self.cursor, self.seg_counts,
+                  self.flags[0], self.seq, self.timeout_s, None, None, 0, None, None, None, None, exp_rows, st)
+        e.gemm_ep(w2_local, self.h_seg, self.comb, self.hidden, False, self.seg_cap, self.seg_counts, None,
+                  None, None, self.timeout_s, self.recv_tag, self.peer_comb, self.max_slots, self.sig_combine,
+                  self.seq, self.arrive[1:2], self.cursor, exp_rows, st)
         if out is None:
             out = torch.empty_like(x)
         n = T * self.topk
+        wait = dict(wait_flags=self.flags[1], wait_seq=self.seq, status=st, timeout_s=self.timeout_s)
         if norm is not None:
             e.moe_combine(self.comb[:n], self.slots[:n].view(T, self.topk), w, None, shared_out, shared_gate,
-                          norm[0], norm[1], out, norm[2])
+                          norm[0], norm[1], out, norm[2], **wait)
         else:
-            e.moe_combine(self.comb[:n], self.slots[:n].view(T, self.topk), w, out, shared_out, shared_gate)
+            e.moe_combine(self.comb[:n], self.slots[:n].view(T, self.topk), w, out, shared_out, shared_gate, **wait)
         return out
 
     def close(self):
