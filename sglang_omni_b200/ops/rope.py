@@ -63,10 +63,12 @@ def apply_rope_ref(x, positions, cos_tab, sin_tab, rot_dim, neox=True, section=N
     return out
 
 
-def _rms(x, w, eps):
+def _rms(x, w, eps, dtype=torch.bfloat16):
+    """Per-head RMSNorm with the kernel's rounding points: the normalised value and the
+    weighted value are each rounded to the activation dtype (a no-op for fp32)."""
     xf = x.float()
-    y = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)).bfloat16().float()
-    return (y * w.float()).bfloat16().float()
+    y = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)).to(dtype).float()
+    return (y * w.float()).to(dtype).float()
 
 
 def qkv_rope_store_ref(qkv, hq, hkv, d, q_norm, k_norm, eps, positions, cos_tab, sin_tab, rot_dim, neox, section,
@@ -76,9 +78,9 @@ def qkv_rope_store_ref(qkv, hq, hkv, d, q_norm, k_norm, eps, positions, cos_tab,
     k = qkv[:, hq * d:(hq + hkv) * d].reshape(T, hkv, d).float()
     v = qkv[:, (hq + hkv) * d:(hq + 2 * hkv) * d].reshape(T, hkv, d)
     if q_norm is not None:
-        q = _rms(q, q_norm, eps)
+        q = _rms(q, q_norm, eps, qkv.dtype)
     if k_norm is not None:
-        k = _rms(k, k_norm, eps)
+        k = _rms(k, k_norm, eps, qkv.dtype)
     if rot_dim > 0:
         q = apply_rope_ref(q, positions, cos_tab, sin_tab, rot_dim, neox, section, interleaved)
         k = apply_rope_ref(k, positions, cos_tab, sin_tab, rot_dim, neox, section, interleaved)

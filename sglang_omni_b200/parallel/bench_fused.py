@@ -160,6 +160,34 @@ def ep_moe_layer(T: int, iters: int, rank: int, world: int) -> dict:
     ep.forward(x, wr, w13, w2, out=out)
     torch.cuda.synchronize()
     err = float((out.float() - out_n.float()).norm() / out_n.float().norm().clamp_min(1e-6))
+    # per-kernel device time inside the layer: an event after every launch
+    names: list = []
+    stamps: list = []
+
+    class _Marks(list):
+        def append(self, name):
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            names.append(name)
+            stamps.append(ev)
+
+    parts: dict = {}
+    for _ in range(iters):
+        names.clear()
+        stamps.clear()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        ep._marks = _Marks()
+        ep.forward(x, wr, w13, w2, out=out)
+        ep._marks = None
+        torch.cuda.synchronize()
+        prev = e0
+        for nm, ev in zip(names, stamps):
+            parts[nm] = parts.get(nm, 0.0) + prev.elapsed_time(ev) * 1e3 / iters
+            prev = ev
+    pt = torch.tensor([parts[n] for n in names], dtype=torch.float64, device=dev)
+    dist.all_reduce(pt, op=dist.ReduceOp.MAX)
+    breakdown = {n: round(float(v), 2) for n, v in zip(names, pt)}
     ep.close()
     wbytes = El * 3 * H * I * 2
     flops = T * topk * 2.0 * 3 * H * I                    # rows landing on this rank (T * topk on average)
@@ -171,7 +199,7 @@ def ep_moe_layer(T: int, iters: int, rank: int, world: int) -> dict:
                     "source ranks' slots, combine waiting on the owners' flags", "tokens_per_rank": T,
             "fused_us": round(t_f, 2), "nccl_us": round(t_n, 2), "roofline_us": round(roof, 2),
             "fused_frac_of_roofline": round(roof / t_f, 3), "speedup_vs_nccl": round(t_n / t_f, 3),
-            "rel_diff_vs_nccl": round(err, 4)}
+            "rel_diff_vs_nccl": round(err, 4), "breakdown_us_max_over_ranks": breakdown}
 
 
 def main():

@@ -83,6 +83,8 @@ class EPMoE:
         self.slots = torch.arange(self.max_slots, dtype=torch.int32, device=dev)
         self.topk_ids = torch.empty(max_tokens, topk, dtype=torch.int32, device=dev)
         self.topk_w = torch.empty(max_tokens, topk, dtype=torch.float32, device=dev)
+        # timing hook: a list that receives a name after each launch (the caller records an event)
+        self._marks = None
 
     def forward(self, x: torch.Tensor, w_router: torch.Tensor, w13_local: torch.Tensor, w2_local: torch.Tensor,
                 renormalize: bool = True, mode: int = 0, bias=None, n_group: int = 1, topk_group: int = 1,
@@ -97,19 +99,25 @@ class EPMoE:
         assert T <= self.max_tokens, f"{T} tokens > EP buffer capacity {self.max_tokens}"
         st = status_word(x.device)
         e = ext()
+        mark = self._marks.append if self._marks is not None else (lambda _n: None)
         logits = linear(x, w_router, out_dtype=torch.float32)
+        mark("router")
         ids, w = self.topk_ids[:T], self.topk_w[:T]
         e.moe_route(logits, self.topk, mode, bias, n_group, topk_group, renormalize, scaling, ids, w, None, None,
                     None, None, None, None, 0, 0)
+        mark("topk")
         x = x.contiguous()
         e.ep_dispatch(x, ids, self.buf.peer_base, self.offs, self.rank, self.world, self.experts, self.seg_cap,
                       self.seq, self.arrive[0:1], st)
+        mark("dispatch")
         exp_rows = max(1, (T * self.topk * self.world) // self.experts)
         e.gemm_ep(w13_local, self.recv_x, self.h_seg, self.inter, True, self.seg_cap, self.cursor, self.seg_counts,
                   self.flags[0], self.seq, self.timeout_s, None, None, 0, None, None, None, None, exp_rows, st)
+        mark("w13 (waits for dispatch)")
         e.gemm_ep(w2_local, self.h_seg, self.comb, self.hidden, False, self.seg_cap, self.seg_counts, None,
                   None, None, self.timeout_s, self.recv_tag, self.peer_comb, self.max_slots, self.sig_combine,
                   self.seq, self.arrive[1:2], self.cursor, exp_rows, st)
+        mark("w2 + combine stores")
         if out is None:
             out = torch.empty_like(x)
         n = T * self.topk
@@ -119,6 +127,7 @@ class EPMoE:
                           norm[0], norm[1], out, norm[2], **wait)
         else:
             e.moe_combine(self.comb[:n], self.slots[:n].view(T, self.topk), w, out, shared_out, shared_gate, **wait)
+        mark("top-k sum (waits for owners)")
         return out
 
     def close(self):
