@@ -11,8 +11,9 @@ from .request import ARRequest
 
 
 class PagedAREngineAdapter:
-    def __init__(self, engine: AREngine):
-        self.threaded = ThreadedAREngine(engine)
+    def __init__(self, engine: AREngine, threaded: ThreadedAREngine | None = None):
+        """``threaded``: the engine thread to use (a rank group's leader loop), default a plain one."""
+        self.threaded = threaded if threaded is not None else ThreadedAREngine(engine)
         self._started = False
 
     @property

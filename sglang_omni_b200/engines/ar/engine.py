@@ -67,6 +67,7 @@ class AREngine:
         self.num_steps = 0
         self.num_retractions = 0
         self.num_prefix_hit_tokens = 0
+        self.last_launched = False
 
     # ------------------------------------------------------------------ API
     def add_request(self, req: ARRequest):
@@ -238,6 +239,7 @@ class AREngine:
             finished += self._process(self.pending)
             self.pending = None
         self.num_steps += 1
+        self.last_launched = launched is not None   # one model forward ran in this step
         return finished
 
     def _process(self, out) -> list[ARRequest]:

@@ -13,6 +13,8 @@ ModelRunner + ForwardBatch (sglang_omni/engines/ar/sglang_backend/model_worker.p
 """
 from __future__ import annotations
 
+import zlib
+
 import numpy as np
 import torch
 
@@ -97,7 +99,9 @@ class ARModelRunner:
         self.top_p[s] = float(sp.top_p)
         self.min_p[s] = float(sp.min_p)
         self.rep[s] = float(sp.repetition_penalty)
-        self.seeds[s] = int(sp.seed if sp.seed is not None else hash(req.rid) & 0x7FFFFFFF)
+        # a stable function of the request id (str hash is salted per process): the ranks of a
+        # tensor-parallel group draw the same samples
+        self.seeds[s] = int(sp.seed if sp.seed is not None else zlib.crc32(req.rid.encode()) & 0x7FFFFFFF)
         self.step_ctr[s] = 0
         if self.seen is not None:
             self.seen[s].zero_()

@@ -40,15 +40,30 @@ def prompt_ids_of(data: Any) -> list[int]:
 
 def create_ar_executor(model, stage_name: str, tokenizer, max_batch: int = 64, max_context: int = 4096,
                        max_prefill_tokens: int = 8192, kv_pages: int | None = None, use_graphs: bool = True,
-                       eos_token_ids=(), default_max_new_tokens: int = 128, prefix_cache: bool = True) -> EngineExecutor:
-    cfg = model.cfg
-    dev = model.embed.device
+                       eos_token_ids=(), default_max_new_tokens: int = 128, prefix_cache: bool = True,
+                       rank_group=None) -> EngineExecutor:
+    """``rank_group``: a ``parallel.rank_group.GroupSpec`` (builder, mode, world, GPUs); the stage is
+    then served by that group (this process is its leader) and ``model`` is ignored."""
+    dev = model.embed.device if model is not None else (torch.device("cuda", torch.cuda.current_device())
+                                                        if rank_group is not None and rank_group.gpus
+                                                        else torch.device("cpu"))
     pages = kv_pages or (max_batch * ((max_context + 63) // 64) + 8)
-    pool = KVPool(cfg.num_layers, cfg.num_kv_heads, cfg.head_dim, pages, dev, cfg.dtype)
-    engine = AREngine(model, pool, max_batch=max_batch, max_prefill_tokens=max_prefill_tokens,
-                      max_context=max_context, use_graphs=use_graphs and dev.type == "cuda",
-                      eos_token_ids=eos_token_ids, prefix_cache=prefix_cache)
-    adapter = PagedAREngineAdapter(engine)
+    engine_args = dict(max_batch=max_batch, max_prefill_tokens=max_prefill_tokens, max_context=max_context,
+                       use_graphs=use_graphs and dev.type == "cuda", eos_token_ids=tuple(eos_token_ids),
+                       prefix_cache=prefix_cache)
+    if rank_group is not None:
+        from ...parallel.rank_group import GroupedAREngine, StageRankGroup
+
+        rank_group.engine_args = engine_args
+        rank_group.kv_pages = pages
+        rg = StageRankGroup(rank_group)
+        engine = rg.start()
+        adapter = PagedAREngineAdapter(engine, threaded=GroupedAREngine(engine, rg))
+    else:
+        cfg = model.cfg
+        pool = KVPool(cfg.num_layers, cfg.num_kv_heads, cfg.head_dim, pages, dev, cfg.dtype)
+        engine = AREngine(model, pool, **engine_args)
+        adapter = PagedAREngineAdapter(engine)
     detoks: dict[str, IncrementalDetokenizer] = {}
 
     def request_builder(payload: StagePayload) -> ARRequest:

@@ -447,6 +447,25 @@ class DecoderLM(nn.Module):
                    n_group=cfg.n_group, topk_group=cfg.topk_group, scaling=cfg.routed_scaling_factor,
                    shared_out=shared_out, shared_gate=shared_gate)
 
+    @torch.no_grad()
+    def ep_idle(self):
+        """An expert-parallel rank with no tokens this iteration: the MoE exchange of every layer
+        with zero rows (its experts still serve the rows the other ranks dispatch)."""
+        assert self.ep is not None, "idle forward of an expert-parallel model"
+        cfg = self.cfg
+        x = torch.empty(0, cfg.hidden_size, dtype=cfg.dtype, device=self.embed.device)
+        for i, L in enumerate(self.layers):
+            if cfg.is_moe_layer(i):
+                self.ep.forward(x, L.router, L.w13, L.w2, renormalize=cfg.norm_topk_prob, mode=cfg.router_mode,
+                                bias=getattr(L, "router_bias", None), n_group=cfg.n_group, topk_group=cfg.topk_group,
+                                scaling=cfg.routed_scaling_factor)
+
+    def close_parallel(self):
+        """Collective: releases the peer-memory buffers of the TP / EP exchange."""
+        par = self.tp if self.tp is not None else self.ep
+        if par is not None:
+            par.close()
+
     def logits(self, hidden: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         if not hidden.is_cuda:
             return ops.linear(hidden, self.head_weight, out=out, out_dtype=torch.float32)

@@ -70,6 +70,33 @@ def get_thinker(model_path: str, device, overrides: dict | None = None) -> Decod
         return m
 
 
+def build_thinker_rank(args: dict, rank: int, world: int, device, group, mode: str) -> DecoderLM:
+    """One rank of a thinker stage group (``parallel.rank_group``): ``tp`` holds this
+    rank's heads / expert slice / MLP slices with the fused TP reduce points, ``ep``
+    this rank's experts with the fused EP exchange (data-parallel attention), the
+    other modes a full copy.  Weights: the checkpoint's slices, or the same
+    deterministic random init as the single-GPU thinker."""
+    model_path = args.get("model_path", "")
+    cfg = _apply(_cfgs(model_path)["thinker"], (args.get("overrides") or {}).get("thinker"))
+    max_tokens = int(args.get("max_tokens", 8192))
+    tp = ep = None
+    if mode == "tp":
+        from ...parallel.tp import TPGroup
+
+        tp = TPGroup(cfg.hidden_size, max_tokens, device, group=group)
+    elif mode == "ep":
+        from ...parallel.ep_moe import EPMoE
+
+        ep = EPMoE(cfg.num_experts, cfg.topk, cfg.hidden_size, cfg.moe_intermediate_size, max_tokens=max_tokens,
+                   device=device, group=group)
+    m = DecoderLM(cfg, device=device, tp=tp, ep=ep)
+    if has_checkpoint(model_path):
+        load_decoder_from_hf(m, load_by_prefix(model_path, "thinker."), "model.", "lm_head.weight")
+    else:
+        m.random_init_(seed=SEEDS["thinker"])
+    return _ready(m)
+
+
 def thinker_embedding(model_path: str, device, overrides: dict | None = None) -> torch.Tensor:
     """The thinker's token-embedding table without building the whole thinker
     (reuses the thinker if this process already has it)."""

@@ -242,19 +242,49 @@ def create_aggregate_executor(**_):
 def create_thinker_executor(model_path: str = "", device: str = "cuda:0", max_batch: int = 64,
                             max_context: int = 4096, max_prefill_tokens: int = 8192, speech_target: str | None = None,
                             accept_hidden_layer: int = 24, overrides: dict | None = None, use_graphs: bool = True,
-                            model=None, tokenizer=None, eos_token_ids=THINKER_EOS_IDS, prefix_cache: bool = True):
+                            model=None, tokenizer=None, eos_token_ids=THINKER_EOS_IDS, prefix_cache: bool = True,
+                            tp_size: int = 1, ep_size: int = 1, gpus: list | None = None):
     """The thinker stage over the paged engine; ``model`` / ``tokenizer`` / ``eos_token_ids``
-    let another omni model (same request layout: prompt ids + audio / image spans) reuse it."""
+    let another omni model (same request layout: prompt ids + audio / image spans) reuse it.
+
+    ``tp_size`` / ``ep_size`` > 1 serve the thinker with a rank group of that many GPUs
+    (``gpus``: logical GPU per rank, default this device and the next ones): tensor
+    parallel (every rank runs every request) or expert parallel with data-parallel
+    attention (each request on one rank, the experts sharded)."""
     dev = torch.device(device)
-    model = model if model is not None else loader.get_thinker(model_path, dev, overrides)
+    pages = max_batch * ((max_context + 63) // 64) + 8
+    engine_args = dict(max_batch=max_batch, max_prefill_tokens=max_prefill_tokens, max_context=max_context,
+                       use_graphs=use_graphs and dev.type == "cuda", eos_token_ids=tuple(eos_token_ids),
+                       prefix_cache=prefix_cache)
+    if tp_size > 1 or ep_size > 1:
+        from ....parallel.rank_group import GroupedAREngine, GroupSpec, StageRankGroup
+
+        if tp_size > 1 and ep_size > 1:
+            raise NotImplementedError("a thinker stage group is either tensor parallel or expert parallel")
+        mode, world = ("tp", tp_size) if tp_size > 1 else ("ep", ep_size)
+        if mode == "ep" and speech_target is not None:
+            raise NotImplementedError("expert-parallel thinker groups serve text output; the talker needs the "
+                                      "hidden states of every request on the leader (use tp_size)")
+        if dev.type == "cuda":
+            torch.cuda.set_device(dev)
+        base = dev.index if dev.index is not None else 0
+        spec = GroupSpec(mode=mode, world=world, gpus=list(gpus) if gpus else list(range(base, base + world)),
+                         builder="sglang_omni_b200.models.qwen3_omni.loader.build_thinker_rank",
+                         builder_args={"model_path": model_path, "overrides": overrides,
+                                       "max_tokens": max(max_prefill_tokens, max_batch)},
+                         engine_args=engine_args, kv_pages=pages)
+        rg = StageRankGroup(spec)
+        engine = rg.start()
+        model = rg.model
+        adapter = PagedAREngineAdapter(engine, threaded=GroupedAREngine(engine, rg))
+    else:
+        model = model if model is not None else loader.get_thinker(model_path, dev, overrides)
+        cfg = model.cfg
+        pool = KVPool(cfg.num_layers, cfg.num_kv_heads, cfg.head_dim, pages, dev, cfg.dtype)
+        engine = AREngine(model, pool, **engine_args)
+        adapter = PagedAREngineAdapter(engine)
     tok = tokenizer if tokenizer is not None else load_tokenizer(model_path, model.cfg.vocab_size)
     cfg = model.cfg
-    pages = max_batch * ((max_context + 63) // 64) + 8
-    pool = KVPool(cfg.num_layers, cfg.num_kv_heads, cfg.head_dim, pages, dev, cfg.dtype)
-    engine = AREngine(model, pool, max_batch=max_batch, max_prefill_tokens=max_prefill_tokens,
-                      max_context=max_context, use_graphs=use_graphs and dev.type == "cuda",
-                      eos_token_ids=eos_token_ids, prefix_cache=prefix_cache)
-    adapter = PagedAREngineAdapter(engine)
     detoks: dict[str, IncrementalDetokenizer] = {}
     accept = min(accept_hidden_layer, cfg.num_layers)
 

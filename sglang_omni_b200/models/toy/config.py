@@ -50,17 +50,34 @@ def toy_decoder_config():
                          max_position=2048, dtype=torch.float32, name="toy_llama")
 
 
-def create_toy_decoder_executor(device: str = "cpu", max_batch: int = 8, seed: int = 0):
+def build_toy_rank(args: dict, rank: int, world: int, device, group, mode: str):
+    """A full copy of the toy decoder on every rank of a stage group (``replica`` / ``dp`` modes)."""
+    from ..decoder import DecoderLM
+
+    return DecoderLM(toy_decoder_config(), device=device).random_init_(seed=int(args.get("seed", 0)))
+
+
+def create_toy_decoder_executor(device: str = "cpu", max_batch: int = 8, seed: int = 0, group_mode: str | None = None,
+                                group_size: int = 1):
+    """``group_mode`` ("replica" or "dp") with ``group_size`` > 1 serves the decoder with a stage
+    rank group of that many processes (the plumbing of TP / EP stages, on CPU)."""
     import torch
 
     from ..common.ar_stage import create_ar_executor
     from ..common.tokenizer import ByteTokenizer
     from ..decoder import DecoderLM
 
+    common = dict(max_batch=max_batch, max_context=512, max_prefill_tokens=512, use_graphs=False,
+                  default_max_new_tokens=16)
+    if group_mode and group_size > 1:
+        from ...parallel.rank_group import GroupSpec
+
+        spec = GroupSpec(mode=group_mode, world=group_size, builder=f"{_P}.toy.config.build_toy_rank",
+                         builder_args={"seed": seed}, report_timeout_s=60.0)
+        return create_ar_executor(None, "decoder", ByteTokenizer(1000), rank_group=spec, **common)
     torch.manual_seed(seed)
     model = DecoderLM(toy_decoder_config(), device=device).random_init_(seed=seed)
-    return create_ar_executor(model, "decoder", ByteTokenizer(1000), max_batch=max_batch, max_context=512,
-                              max_prefill_tokens=512, use_graphs=False, default_max_new_tokens=16)
+    return create_ar_executor(model, "decoder", ByteTokenizer(1000), **common)
 
 
 EntryClass = ToyPipelineConfig

@@ -175,6 +175,8 @@ def ep_moe_layer(T: int, iters: int, rank: int, world: int) -> dict:
     for _ in range(iters):
         names.clear()
         stamps.clear()
+        # keep the GPU busy while the host enqueues the layer, so the events time the device only
+        torch.cuda._sleep(2_000_000)
         e0 = torch.cuda.Event(enable_timing=True)
         e0.record()
         ep._marks = _Marks()

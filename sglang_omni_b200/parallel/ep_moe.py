@@ -28,10 +28,10 @@ SGLang's EP / all-reduce call sites, never enabled
 from __future__ import annotations
 
 import torch
-import torch.distributed as dist
 
 from ..ops._ext import ext, status_word
 from ..ops.gemm import linear
+from .hostgroup import barrier, rank_of, world_of
 from .symm import RegionLayout, SymmetricBuffer
 
 
@@ -39,8 +39,8 @@ class EPMoE:
     def __init__(self, experts: int, topk: int, hidden: int, inter: int, max_tokens: int, device,
                  group=None, dtype=torch.bfloat16, timeout_s: float = 2.0):
         self.group = group
-        self.rank = dist.get_rank(group)
-        self.world = dist.get_world_size(group)
+        self.rank = rank_of(group)
+        self.world = world_of(group)
         assert experts % self.world == 0, "experts must divide evenly over the EP group"
         self.experts, self.topk, self.hidden, self.inter = experts, topk, hidden, inter
         self.local_experts = El = experts // self.world
@@ -69,7 +69,7 @@ class EPMoE:
             self.flags.zero_()
             self.cursor.zero_()
             torch.cuda.synchronize(dev)
-        dist.barrier(group)
+        barrier(group)
         peers = self.buf.peers
         r, w = self.rank, self.world
         # where this rank raises its combine flag on every peer: flags[1][r] (the dispatch kernel

@@ -8,27 +8,26 @@ peer-memory kernels take; ``view`` gives a local torch view of a region.
 from __future__ import annotations
 
 import torch
-import torch.distributed as dist
 
 from ..ops._ext import ext
+from .hostgroup import all_gather_object, barrier, rank_of, world_of
 
 
 class SymmetricBuffer:
     def __init__(self, nbytes: int, group=None, device=None):
         self.group = group
-        self.rank = dist.get_rank(group)
-        self.world = dist.get_world_size(group)
+        self.rank = rank_of(group)
+        self.world = world_of(group)
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.nbytes = int(nbytes)
         with torch.cuda.device(self.device):
             self.ptr = ext().ipc_alloc(self.nbytes)
             handle = ext().ipc_handle(self.ptr)
-        handles: list = [None] * self.world
-        dist.all_gather_object(handles, handle, group=group)
+        handles = all_gather_object(handle, group)
         with torch.cuda.device(self.device):
             self.peers = [self.ptr if r == self.rank else ext().ipc_open(handles[r]) for r in range(self.world)]
         self.peer_base = torch.tensor(self.peers, dtype=torch.int64, device=self.device)
-        dist.barrier(group)
+        barrier(group)
         self._closed = False
 
     def view(self, offset: int, shape, dtype) -> torch.Tensor:
@@ -44,12 +43,12 @@ class SymmetricBuffer:
         if self._closed:
             return
         torch.cuda.synchronize(self.device)
-        dist.barrier(self.group)
+        barrier(self.group)
         with torch.cuda.device(self.device):
             for r, p in enumerate(self.peers):
                 if r != self.rank:
                     ext().ipc_close(p)
-        dist.barrier(self.group)
+        barrier(self.group)
         with torch.cuda.device(self.device):
             ext().ipc_free(self.ptr)
         self._closed = True

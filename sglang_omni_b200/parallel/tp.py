@@ -29,9 +29,9 @@ sglang_omni/models/qwen3_omni/thinker.py:167-213 (QKV / o_proj split),
 from __future__ import annotations
 
 import torch
-import torch.distributed as dist
 
 from ..ops._ext import ext, status_word
+from .hostgroup import barrier, rank_of, world_of
 from .symm import RegionLayout, SymmetricBuffer
 
 
@@ -39,8 +39,8 @@ class TPGroup:
     def __init__(self, hidden: int, max_tokens: int, device, group=None, dtype=torch.bfloat16,
                  timeout_s: float = 2.0):
         self.group = group
-        self.rank = dist.get_rank(group)
-        self.world = dist.get_world_size(group)
+        self.rank = rank_of(group)
+        self.world = world_of(group)
         self.hidden, self.max_tokens = hidden, max_tokens
         self.device = torch.device(device)
         self.timeout_s = timeout_s
@@ -68,7 +68,7 @@ class TPGroup:
         self.seq = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.counter = torch.zeros(1, dtype=torch.int32, device=self.device)
         torch.cuda.synchronize(self.device)
-        dist.barrier(group)
+        barrier(group)
 
     # ------------------------------------------------------------ geometry
     def rows_per(self, tokens: int) -> int:

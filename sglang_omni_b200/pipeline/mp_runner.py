@@ -48,6 +48,8 @@ def _stage_process_entry(cfg_dict: dict, cfg_cls_path: str | None, stage_index: 
         if gpu is not None:
             visible = os.environ.get("CUDA_VISIBLE_DEVICES")
             phys = visible.split(",")[gpu] if visible else str(gpu)
+            # a stage's rank group (tp_size / ep_size > 1) maps its GPU list through the original mask
+            os.environ.setdefault("OMNI_VISIBLE_DEVICES_ORIG", visible or "")
             os.environ["CUDA_VISIBLE_DEVICES"] = phys
         import torch  # noqa: F401  (after the device mask)
 
