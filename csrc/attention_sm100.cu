@@ -1,0 +1,477 @@
+// Paged GQA prefill attention on the 5th-generation tensor cores (sm_100a).
+//
+// One CTA computes one 128-row query tile of one (request, KV head): the rows
+// are GQA-packed, row r = (token tok0 + r / G, query head h * G + r % G), so a
+// K/V block staged once serves all G heads.  Per 128-key block j:
+//
+//   S_j = Q K_j^T          tcgen05.mma (A = Q, B = K, both K-major in shared
+//                          memory), fp32 accumulator in TMEM (two buffers)
+//   P_j = exp2(S_j - m)    softmax warps: one thread per row reads its S row
+//                          with tcgen05.ld, masks (causal / context length),
+//                          keeps the running max m and sum l in registers,
+//                          writes P (bf16) into shared memory in the 128-byte
+//                          swizzled K-major layout (two buffers)
+//   O += P_j V_j           tcgen05.mma (A = P, B = V as an MN-major operand:
+//                          V rows are keys, 64 contiguous dims per 128-byte
+//                          row), accumulator in TMEM
+//
+// The running max is only raised when a block's max exceeds it by more than 8
+// (log2 units, i.e. P values stay below 2^8); the O row in TMEM is then
+// rescaled by its thread (tcgen05.ld / st) after the previous PV product has
+// completed.  The final O row is divided by l and stored as bf16.
+//
+// Warp roles (6 warps): warp 0 TMA producer (Q once, then K/V pages through the
+// block table into a two-stage ring, local memory only, no multicast), warp 1
+// TMEM allocator + MMA issuer (one elected lane), warps 2-5 softmax +
+// epilogue (warp w owns TMEM lanes 32 * (w % 4) .. + 31 = those query rows).
+// The MMA issue order S_0, S_1, PV_0, S_2, PV_1, ... lets the softmax of block
+// j overlap the PV product of block j-1.  Every wait is bounded (%globaltimer);
+// a wait that runs out records status 1, drains and frees TMEM.
+//
+// Tensor maps: Q as [tokens, Hq, D] (box 128 / G tokens x G heads x 64 dims),
+// the K / V cache of one layer as [pages * Hkv * 64, D] rows (box 64 x 64).
+//
+// Reference counterpart: the FlashInfer / TRT-LLM prefill attention behind
+// RadixAttention (sglang_omni/models/qwen3_omni/thinker.py:236-243).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include <mutex>
+
+#include "host_util.h"
+#include "omni_kernels.h"
+#include "sm100.cuh"
+
+namespace omni {
+namespace {
+
+constexpr int kRows = 128;          // packed query rows per tile
+constexpr int kBN = 128;            // keys per block (two pages)
+constexpr int kD = 128;             // head dim
+constexpr int kKvStages = 2;
+constexpr int kThreads = 192;
+constexpr int kRegion = kRows * 128;        // one 64-column region of a 128-row tile: 16 KB
+constexpr int kTileBytes = 2 * kRegion;     // 128 rows x 128 columns bf16: 32 KB
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleThreshold = 8.0f;   // log2 units
+constexpr int kTmemCols = 512;              // S0 | S1 | O (128 columns each)
+
+struct FaSmem {
+  // every tile 1024-byte aligned (128-byte swizzle atoms)
+  static constexpr int kQ = 0;
+  static constexpr int kK = kQ + kTileBytes;
+  static constexpr int kV = kK + kKvStages * kTileBytes;
+  static constexpr int kP = kV + kKvStages * kTileBytes;
+  static constexpr int kBars = kP + 2 * kTileBytes;
+  static constexpr int kBytes = kBars + 256 + 1024;   // barriers + alignment slack
+};
+static_assert(FaSmem::kBytes <= 232448, "shared memory exceeds 227 KB");
+
+struct FaParams {
+  const int* block_table;
+  int bt_stride;
+  const int* cu_q;
+  const int* kv_lens;
+  const int* tile_req;
+  const int* tile_tok0;
+  int hq, hkv, G;
+  float scale_log2;
+  int causal;
+  __nv_bfloat16* out;
+  int64_t out_stride;
+  int num_pages;
+  int* status;
+};
+
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+      "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
+      "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Generic-proxy writes of shared memory (P) become visible to the tensor core (async proxy).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// UMMA shared-memory descriptor of an MN-major operand in the 128-byte swizzled layout:
+// rows of 64 bf16 along MN (128 bytes), 8-row atoms along K (1024 bytes apart, SBO), MN
+// blocks of 64 columns `lbo` bytes apart (LBO).
+__device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t smem_addr, uint32_t lbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
+}
+
+// kind::f16 instruction descriptor, bf16 x bf16 -> f32, A K-major, B MN-major (bit 16).
+constexpr uint32_t umma_idesc_bf16_f32_bmn(int m, int n) { return umma_idesc_bf16_f32(m, n) | (1u << 16); }
+
+__device__ __forceinline__ int fa_page(const FaParams& p, int req, int idx) {
+  const int page = p.block_table[static_cast<int64_t>(req) * p.bt_stride + idx];
+  return (p.num_pages > 0 && static_cast<unsigned>(page) >= static_cast<unsigned>(p.num_pages)) ? 0 : page;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    fa_prefill_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
+                      const __grid_constant__ CUtensorMap tmap_v, const FaParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
+  uint8_t* sQ = smem + FaSmem::kQ;
+  uint8_t* sK = smem + FaSmem::kK;
+  uint8_t* sV = smem + FaSmem::kV;
+  uint8_t* sP = smem + FaSmem::kP;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + FaSmem::kBars);
+  uint64_t* q_full = bars;                 // [1]
+  uint64_t* kv_full = bars + 1;            // [2]
+  uint64_t* kv_empty = bars + 3;           // [2]
+  uint64_t* s_full = bars + 5;             // [2]
+  uint64_t* p_full = bars + 7;             // [2]
+  uint64_t* pv_done = bars + 9;            // [2]
+  uint64_t* drain = bars + 11;             // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x, h = blockIdx.y;
+  const int req = p.tile_req[tile];
+  const int tok0 = p.tile_tok0[tile];
+  const int q_begin = p.cu_q[req];
+  const int q_len = p.cu_q[req + 1] - q_begin;
+  const int kv_len = p.kv_lens[req];
+  const int tpt = kRows / p.G;                       // tokens per tile
+  const int past = kv_len - q_len;                   // keys before this chunk's first query
+  const int key_end = p.causal ? min(kv_len, past + min(q_len, tok0 + tpt)) : kv_len;
+  const int nb = key_end > 0 ? (key_end + kBN - 1) / kBN : 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&pv_done[i], 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmap_q);
+    tma_prefetch_desc(&tmap_k);
+    tma_prefetch_desc(&tmap_v);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0 && nb > 0) {
+      mbar_arrive_expect_tx(q_full, kTileBytes);
+      for (int r = 0; r < 2; ++r)
+        tma_load_3d(sQ + r * kRegion, &tmap_q, q_full, r * 64, h * p.G, q_begin + tok0);
+      bool ok = true;
+      for (int j = 0; j < nb && ok; ++j) {
+        const int s = j & 1;
+        if (j >= kKvStages && !mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, p.status)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&kv_full[s], 2 * kTileBytes);
+        const int pages = (kv_len + 63) / 64;
+        for (int pg = 0; pg < 2; ++pg) {
+          const int idx = 2 * j + pg;
+          // a block's second page past the context reads page 0 (masked): constant byte count
+          const int page = idx < pages ? fa_page(p, req, idx) : 0;
+          const int row = (page * p.hkv + h) * 64;
+          for (int r = 0; r < 2; ++r) {
+            tma_load_2d(sK + s * kTileBytes + r * kRegion + pg * (kRegion / 2), &tmap_k, &kv_full[s], r * 64, row);
+            tma_load_2d(sV + s * kTileBytes + r * kRegion + pg * (kRegion / 2), &tmap_v, &kv_full[s], r * 64, row);
+          }
+        }
+      }
+      // drain: the last loads of each stage landed before TMEM / smem go away
+      mbar_wait(q_full, 0, nullptr, p.status);
+      for (int j = max(0, nb - kKvStages); j < nb && ok; ++j) mbar_wait(&kv_full[j & 1], (j >> 1) & 1, nullptr, p.status);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc_s = umma_idesc_bf16_f32(kRows, kBN);
+    constexpr uint32_t idesc_o = umma_idesc_bf16_f32_bmn(kRows, kD);
+    bool ok = nb > 0 && mbar_wait(q_full, 0, abort_flag, p.status);
+    auto issue_pv = [&](int j) -> bool {
+      const int b = j & 1;
+      if (!mbar_wait(&p_full[b], (j >> 1) & 1, abort_flag, p.status)) return false;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t pa = smem_u32(sP + b * kTileBytes);
+        const uint32_t va = smem_u32(sV + (j & 1) * kTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint64_t adesc = umma_desc_sw128(pa + (kk >> 2) * kRegion) + 2 * (kk & 3);
+          const uint64_t bdesc = umma_desc_sw128_mn(va + kk * 16 * 128, kRegion);
+          umma_f16_ss(tmem + 256, adesc, bdesc, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&pv_done[b]);
+        umma_commit(&kv_empty[j & 1]);
+      }
+      __syncwarp();
+      return true;
+    };
+    for (int j = 0; j < nb && ok; ++j) {
+      const int s = j & 1;
+      if (!mbar_wait(&kv_full[s], (j >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t qa = smem_u32(sQ);
+        const uint32_t ka = smem_u32(sK + s * kTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          const uint64_t adesc = umma_desc_sw128(qa + (kk >> 2) * kRegion) + 2 * (kk & 3);
+          const uint64_t bdesc = umma_desc_sw128(ka + (kk >> 2) * kRegion) + 2 * (kk & 3);
+          umma_f16_ss(tmem + s * 128, adesc, bdesc, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[s]);
+      }
+      __syncwarp();
+      if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+    }
+    if (ok && nb > 0) issue_pv(nb - 1);
+    if (lane == 0) {
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr, p.status);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;                  // query row = TMEM lane
+    const int tok = tok0 + r / p.G;
+    const bool row_ok = tok < q_len;
+    const int qpos = past + tok;                        // absolute position of this query
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nb && ok; ++j) {
+      const int b = j & 1;
+      if (!mbar_wait(&s_full[b], (j >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
+      tc_fence_after();
+      float s[kBN];
+#pragma unroll
+      for (int c = 0; c < kBN; c += 32) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem + lane_addr + b * 128 + c, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[c + i] = __uint_as_float(v[i]);
+      }
+      const int k0 = j * kBN;
+      const int lim = p.causal ? min(kv_len, qpos + 1) : kv_len;   // keys [0, lim) are visible
+      float mb = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < kBN; ++i) {
+        const float x = (k0 + i < lim) ? s[i] * p.scale_log2 : -INFINITY;
+        s[i] = x;
+        mb = fmaxf(mb, x);
+      }
+      if (mb > m_run + kRescaleThreshold || (m_run == -INFINITY && mb > -INFINITY)) {
+        if (j > 0 && m_run > -INFINITY) {
+          // O holds sum over earlier blocks at max m_run: rescale once the previous PV is done
+          if (!mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
+          tc_fence_after();
+          const float f = exp2f(m_run - mb);
+#pragma unroll 1
+          for (int c = 0; c < kD; c += 32) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(tmem + lane_addr + 256 + c, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * f);
+            tmem_st_32x32b_x32(tmem + lane_addr + 256 + c, v);
+          }
+          tmem_st_wait();
+          l_run *= f;
+        }
+        m_run = mb;
+      }
+      const float msub = m_run == -INFINITY ? 0.f : m_run;
+      // P buffer b was last read by PV_{j-2}
+      if (j >= 2 && !mbar_wait(&pv_done[b], ((j - 2) >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
+      uint8_t* prow = sP + b * kTileBytes + r * 128;
+      float lsum = 0.f;
+#pragma unroll
+      for (int c8 = 0; c8 < kBN / 8; ++c8) {
+        float e[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          e[i] = exp2f(s[c8 * 8 + i] - msub);
+          lsum += e[i];
+        }
+        uint4 pk;
+        pk.x = pack_bf16x2(e[0], e[1]);
+        pk.y = pack_bf16x2(e[2], e[3]);
+        pk.z = pack_bf16x2(e[4], e[5]);
+        pk.w = pack_bf16x2(e[6], e[7]);
+        const int region = c8 >> 3, chunk = c8 & 7;
+        *reinterpret_cast<uint4*>(prow + region * kRegion + ((chunk ^ (r & 7)) << 4)) = pk;
+      }
+      l_run += lsum;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[b]);
+    }
+    // epilogue: O / l once the last PV product is done
+    if (ok && nb > 0 && mbar_wait(&pv_done[(nb - 1) & 1], ((nb - 1) >> 1) & 1, abort_flag, p.status)) {
+      tc_fence_after();
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      __nv_bfloat16* orow =
+          p.out + static_cast<int64_t>(q_begin + tok) * p.out_stride + static_cast<int64_t>(h * p.G + r % p.G) * kD;
+#pragma unroll 1
+      for (int c = 0; c < kD; c += 32) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem + lane_addr + 256 + c, v);
+        tmem_ld_wait();
+        if (row_ok) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 o;
+            o.x = pack_bf16x2(__uint_as_float(v[i]) * inv, __uint_as_float(v[i + 1]) * inv);
+            o.y = pack_bf16x2(__uint_as_float(v[i + 2]) * inv, __uint_as_float(v[i + 3]) * inv);
+            o.z = pack_bf16x2(__uint_as_float(v[i + 4]) * inv, __uint_as_float(v[i + 5]) * inv);
+            o.w = pack_bf16x2(__uint_as_float(v[i + 6]) * inv, __uint_as_float(v[i + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + c + i) = o;
+          }
+        }
+      }
+    } else if (nb == 0 && row_ok) {
+      __nv_bfloat16* orow =
+          p.out + static_cast<int64_t>(q_begin + tok) * p.out_stride + static_cast<int64_t>(h * p.G + r % p.G) * kD;
+      for (int c = 0; c < kD; c += 8) *reinterpret_cast<uint4*>(orow + c) = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+bool encode(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides_bytes,
+            const cuuint32_t* box) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims, strides_bytes, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+// Paged mode, head_dim 128, G = Hq / Hkv in {1, 2, 4, 8, 16}, no sliding window; tiles of 128 packed rows.
+bool attention_prefill_sm100_supported(const AttnPrefillArgs& a) {
+  if (a.block_table == nullptr || a.head_dim != kD || a.window > 0 || a.hkv <= 0 || a.hq % a.hkv != 0) return false;
+  const int G = a.hq / a.hkv;
+  return G >= 1 && G <= 16 && kRows % G == 0 && (a.q_stride * 2) % 16 == 0 &&
+         (reinterpret_cast<uintptr_t>(a.q) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.k) & 15) == 0 &&
+         (reinterpret_cast<uintptr_t>(a.v) & 15) == 0 && (a.out_stride % 8) == 0;
+}
+
+cudaError_t attention_prefill_sm100(const AttnPrefillArgs& a, cudaStream_t stream) {
+  if (a.num_tiles == 0) return cudaSuccess;
+  if (!attention_prefill_sm100_supported(a) || a.num_pages <= 0) return cudaErrorInvalidValue;
+  const int G = a.hq / a.hkv;
+  CUtensorMap tq, tk, tv;
+  // Q [tokens, Hq, D]: the tensor spans every row the tile table can address (q rows are
+  // never written past the last request; rows past a request's end are masked)
+  {
+    const cuuint64_t rows = static_cast<cuuint64_t>(a.q_rows > 0 ? a.q_rows : 1);
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(a.hq), rows};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(kD) * 2, static_cast<cuuint64_t>(a.q_stride) * 2};
+    cuuint32_t box[3] = {64, static_cast<cuuint32_t>(G), static_cast<cuuint32_t>(kRows / G)};
+    if (!encode(&tq, a.q, 3, dims, strides, box)) return cudaErrorInvalidValue;
+  }
+  {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(a.num_pages) * a.hkv * 64};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(kD) * 2};
+    cuuint32_t box[2] = {64, 64};
+    if (!encode(&tk, a.k, 2, dims, strides, box) || !encode(&tv, a.v, 2, dims, strides, box))
+      return cudaErrorInvalidValue;
+  }
+  FaParams p;
+  p.block_table = a.block_table;
+  p.bt_stride = a.bt_stride;
+  p.cu_q = a.cu_q;
+  p.kv_lens = a.kv_lens;
+  p.tile_req = a.tile_req;
+  p.tile_tok0 = a.tile_tok0;
+  p.hq = a.hq;
+  p.hkv = a.hkv;
+  p.G = G;
+  p.scale_log2 = a.scale * kLog2e;
+  p.causal = a.causal;
+  p.out = static_cast<__nv_bfloat16*>(a.out);
+  p.out_stride = a.out_stride;
+  p.num_pages = a.num_pages;
+  p.status = a.status;
+  cudaError_t e = ensure_smem_attr<fa_prefill_kernel>(FaSmem::kBytes);
+  if (e != cudaSuccess) return e;
+  dim3 grid(a.num_tiles, a.hkv);
+  fa_prefill_kernel<<<grid, kThreads, FaSmem::kBytes, stream>>>(tq, tk, tv, p);
+  return cudaGetLastError();
+}
+
+}  // namespace omni

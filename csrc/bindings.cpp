@@ -177,7 +177,8 @@ void attention_prefill(const torch::Tensor& q, const torch::Tensor& k, const tor
                        const c10::optional<torch::Tensor>& block_table, const torch::Tensor& cu_q,
                        const torch::Tensor& kv_lens, const c10::optional<torch::Tensor>& cu_kv,
                        const torch::Tensor& tile_req, const torch::Tensor& tile_tok0, int64_t hq, int64_t hkv,
-                       int64_t head_dim, double scale, bool causal, int64_t window) {
+                       int64_t head_dim, double scale, bool causal, int64_t window, int64_t tile_rows,
+                       const c10::optional<torch::Tensor>& status) {
   OMNI_CHECK_CUDA(q);
   OMNI_CHECK_BF16(q);
   OMNI_CHECK_BF16(k);
@@ -211,6 +212,12 @@ void attention_prefill(const torch::Tensor& q, const torch::Tensor& k, const tor
   a.out_stride = out.stride(0);
   a.window = static_cast<int>(window);
   a.num_pages = block_table.has_value() ? static_cast<int>(k.size(0)) : 0;
+  a.tile_rows = static_cast<int>(tile_rows);
+  a.q_rows = static_cast<int>(q.size(0));
+  a.status = status_ptr(status);
+  TORCH_CHECK(tile_rows == 64 || tile_rows == 128, "tile_rows must be 64 or 128");
+  TORCH_CHECK(tile_rows == 64 || omni::attention_prefill_sm100_supported(a),
+              "128-row tiles need the paged tcgen05 kernel (head_dim 128, no window, aligned rows)");
   check_launch(omni::attention_prefill(a, at::cuda::getCurrentCUDAStream()), "attention_prefill");
 }
 
@@ -780,7 +787,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("static_a") = false, py::arg("splitk_cluster") = false);
   m.def("rmsnorm", &rmsnorm, "RMSNorm (+ fused residual add)");
   m.def("layernorm", &layernorm, "LayerNorm");
-  m.def("attention_prefill", &attention_prefill, "paged / varlen GQA prefill attention");
+  m.def("attention_prefill", &attention_prefill, "paged / varlen GQA prefill attention", py::arg("q"), py::arg("k"),
+        py::arg("v"), py::arg("out"), py::arg("block_table"), py::arg("cu_q"), py::arg("kv_lens"), py::arg("cu_kv"),
+        py::arg("tile_req"), py::arg("tile_tok0"), py::arg("hq"), py::arg("hkv"), py::arg("head_dim"),
+        py::arg("scale"), py::arg("causal"), py::arg("window"), py::arg("tile_rows") = 64,
+        py::arg("status") = py::none());
   m.def("attention_decode", &attention_decode, "paged split-KV GQA decode attention");
   m.def("qkv_rope_store", &qkv_rope_store, "QK RMSNorm + (M-)RoPE + paged KV store");
   m.def("moe_route", &moe_route, "MoE top-k routing + permutation + gather", py::arg("logits"), py::arg("topk"),

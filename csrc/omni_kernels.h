@@ -125,8 +125,14 @@ struct AttnPrefillArgs {
   int window;             // > 0: causal sliding window (a query sees its last `window` keys)
   int num_pages;          // paged mode: pages in the cache; block-table entries outside [0, num_pages)
                           // read page 0 (the reserved padding page). 0 = unchecked
+  int tile_rows;          // packed query rows per tile: 64 (mma.sync kernel) or 128 (tcgen05 kernel,
+                          // csrc/attention_sm100.cu: paged, head_dim 128, no window)
+  int q_rows;             // rows of q (tokens of the batch)
+  int* status;            // bounded-wait status word (tcgen05 kernel), may be nullptr
 };
 cudaError_t attention_prefill(const AttnPrefillArgs& a, cudaStream_t stream);
+bool attention_prefill_sm100_supported(const AttnPrefillArgs& a);
+cudaError_t attention_prefill_sm100(const AttnPrefillArgs& a, cudaStream_t stream);
 
 struct AttnDecodeArgs {
   const void* q;          // [B, hq, D] rows of stride q_stride

@@ -142,7 +142,8 @@ def compile_pipeline(cfg: PipelineConfig, run_id: str | None = None) -> tuple[Co
     names = [s.name for s in stages_cfg]
     endpoints = allocate_endpoints(cfg, names, run_id, multiprocess=False)
     terminals = [name_map.get(t, t) for t in cfg.terminal_stages]
-    coordinator = Coordinator(endpoints.completion, endpoints.abort, entry, terminals)
+    coordinator = Coordinator(endpoints.completion, endpoints.abort, entry, terminals,
+                              request_timeout_s=cfg.request_timeout_s)
     receivers = {name_map.get(t.to_stage, t.to_stage) for s in stages_cfg for t in s.stream_to}
     stages = []
     for i, s in enumerate(stages_cfg):

@@ -75,6 +75,8 @@ class PipelineConfig(BaseModel):
     completion_endpoint: str | None = None
     abort_endpoint: str | None = None
     config_cls: str | None = None
+    # a request not completed this long after submission fails with a timeout (None: no deadline)
+    request_timeout_s: float | None = None
 
     def model_post_init(self, __context: Any = None) -> None:
         self._validate_general()

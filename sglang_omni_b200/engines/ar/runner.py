@@ -19,7 +19,7 @@ import numpy as np
 import torch
 
 from ...models.decoder import DecoderLM, ForwardBatch
-from ...ops import prefill_tiles
+from ...ops import prefill_tile_rows, prefill_tiles
 from ...ops.sampling import SamplingTensors, sample
 from ...environ import environ
 from ...utils.cuda_graph import capture_graph
@@ -168,7 +168,9 @@ class ARModelRunner:
                 logits_rows.append(off + n - 1)
                 sample_reqs.append(r)
             off += n
-        req_t, tok0_t = prefill_tiles(q_lens, self.cfg.num_heads // self.cfg.num_kv_heads)
+        G = self.cfg.num_heads // self.cfg.num_kv_heads
+        rows = prefill_tile_rows(self.cfg.head_dim, G) if self.is_cuda else 64
+        req_t, tok0_t = prefill_tiles(q_lens, G, rows)
         as_dev = lambda a: h2d(a, dev)  # noqa: E731
         if any_embeds:
             parts = []
@@ -213,7 +215,7 @@ class ARModelRunner:
             is_decode=False, positions=as_dev(pos), slot_mapping=as_dev(slots), kv_lens=as_dev(kv_lens),
             block_table=as_dev(bt), input_ids=as_dev(ids) if input_embeds is None else None,
             input_embeds=input_embeds, cu_q=as_dev(cu), tile_req=h2d(req_t, dev, torch.int32),
-            tile_tok0=h2d(tok0_t, dev, torch.int32),
+            tile_tok0=h2d(tok0_t, dev, torch.int32), tile_rows=rows,
             logits_indices=as_dev(np.asarray(logits_rows, dtype=np.int32)) if logits_rows else None,
             mm_index=mm_index, mm_embeds=mm_embeds, deepstack=deepstack, capture_layers=capture,
         )

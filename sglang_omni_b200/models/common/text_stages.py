@@ -35,7 +35,13 @@ def create_text_preprocessing_executor(model_path: str = "", vocab_size: int = 1
     return PreprocessingExecutor(preprocess)
 
 
-def create_identity_executor(**_):
+def create_identity_executor(inject_faults: list | None = None, **_):
+    """Passes payloads through.  ``inject_faults``: control-plane fault rules
+    (``pipeline.faults.FaultRule`` fields) installed in this stage's process (tests)."""
+    if inject_faults:
+        from ...pipeline import faults
+
+        faults.inject([faults.FaultRule(**r) for r in inject_faults])
     return PreprocessingExecutor(lambda p: p)
 
 

@@ -107,6 +107,7 @@ class ForwardBatch:
     cu_q: torch.Tensor | None = None        # prefill: int32 [B + 1]
     tile_req: torch.Tensor | None = None
     tile_tok0: torch.Tensor | None = None
+    tile_rows: int = 64                     # packed rows per prefill tile (ops.prefill_tile_rows)
     logits_indices: torch.Tensor | None = None  # rows whose logits are needed
     mm_index: torch.Tensor | None = None    # int32 [T] row of mm_embeds or -1
     mm_embeds: torch.Tensor | None = None
@@ -361,7 +362,7 @@ class DecoderLM(nn.Module):
             else:
                 attn = ops.prefill_attention(qkv, kv_cache[i, 0], kv_cache[i, 1], fb.block_table, fb.cu_q,
                                              fb.kv_lens, fb.tile_req, fb.tile_tok0, cfg.num_heads,
-                                             cfg.num_kv_heads, cfg.head_dim, scale)
+                                             cfg.num_kv_heads, cfg.head_dim, scale, tile_rows=fb.tile_rows)
             o = ops.linear(attn, L.o)
             normed2 = ops.rms_norm(o, L.ln2, cfg.rms_norm_eps, residual=res)
             has_ds = fb.deepstack is not None and i < len(fb.deepstack) and fb.deepstack[i] is not None
@@ -391,7 +392,8 @@ class DecoderLM(nn.Module):
             return ops.decode_attention(qkv, kv_cache[i, 0], kv_cache[i, 1], fb.block_table, fb.kv_lens,
                                         cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, self._dec_ws, scale)
         return ops.prefill_attention(qkv, kv_cache[i, 0], kv_cache[i, 1], fb.block_table, fb.cu_q, fb.kv_lens,
-                                     fb.tile_req, fb.tile_tok0, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, scale)
+                                     fb.tile_req, fb.tile_tok0, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, scale,
+                                     tile_rows=fb.tile_rows)
 
     def _forward_tp(self, fb: ForwardBatch, kv_cache: torch.Tensor, res: torch.Tensor) -> torch.Tensor:
         """Tensor-parallel forward: local heads / experts / MLP slices, every reduce point
@@ -403,8 +405,6 @@ class DecoderLM(nn.Module):
         nl = len(self.layers)
         if not res.is_cuda:
             raise RuntimeError("tensor parallelism runs on CUDA devices only")
-        if fb.deepstack is not None and any(d is not None for d in fb.deepstack):
-            raise NotImplementedError("deepstack injection under tensor parallelism")
         scatter = tp.scatter(T)
         normed, wait = ops.rms_norm(res, self.layers[0].ln1, eps), None
         if 0 in fb.capture_layers:
@@ -414,6 +414,12 @@ class DecoderLM(nn.Module):
             ops.linear(attn, L.o, out=tp.part_local[:T], scatter=scatter)
             normed2 = tp.reduce_norm(res, L.ln2, eps, T)
             self._mlp_tp(L, normed2, i, T, scatter)
+            if fb.deepstack is not None and i < len(fb.deepstack) and fb.deepstack[i] is not None:
+                # deep-stack visual rows join the block output: the owner of each row adds them to
+                # its residual rows before the reduce point sums the partials into them (the
+                # other rows of `res` are not this rank's and are never read)
+                pos, emb = fb.deepstack[i]
+                res.index_add_(0, pos, emb.to(res.dtype))
             last = i + 1 == nl
             cap = (i + 1) in fb.capture_layers
             normed = tp.reduce_norm(res, self.final_norm if last else self.layers[i + 1].ln1, eps, T,

@@ -215,11 +215,13 @@ class DualARGenerator:
         d = lambda a: h2d(a, dev)  # noqa: E731
         x = ops.vq_embed(sl.embed, m.codebook_embeddings, d(all_codes), cfg.codebook_size, cfg.vq_scale,
                          cfg.semantic_begin_id, cfg.semantic_end_id, ids=d(ids), code_row=d(code_rows))
-        req, tok0 = ops.prefill_tiles(lens, sl.cfg.num_heads // sl.cfg.num_kv_heads)
+        G = sl.cfg.num_heads // sl.cfg.num_kv_heads
+        rows = ops.prefill_tile_rows(sl.cfg.head_dim, G) if dev.type == "cuda" else 64
+        req, tok0 = ops.prefill_tiles(lens, G, rows)
         fb = ForwardBatch(is_decode=False, positions=d(pos), slot_mapping=d(slot_map),
                           kv_lens=h2d(lens, dev, torch.int32), block_table=d(bt),
                           input_embeds=x, cu_q=d(cu), tile_req=h2d(req, dev, torch.int32),
-                          tile_tok0=h2d(tok0, dev, torch.int32), logits_indices=d(cu[1:] - 1))
+                          tile_tok0=h2d(tok0, dev, torch.int32), tile_rows=rows, logits_indices=d(cu[1:] - 1))
         hidden = sl(fb, self.pool.kv)
         slots = h2d([s.slot for s in streams], dev, torch.int32)
         out = self._tail(hidden, slots)

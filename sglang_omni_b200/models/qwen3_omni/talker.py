@@ -350,13 +350,15 @@ class SpeechGenerator:
         bt = np.zeros((len(streams), max(len(s.pages) for s in streams)), dtype=np.int32)
         for i, s in enumerate(streams):
             bt[i, :len(s.pages)] = s.pages
-        req, tok0 = ops.prefill_tiles(lens, tl.cfg.num_heads // tl.cfg.num_kv_heads)
+        G = tl.cfg.num_heads // tl.cfg.num_kv_heads
+        rows = ops.prefill_tile_rows(tl.cfg.head_dim, G) if dev.type == "cuda" else 64
+        req, tok0 = ops.prefill_tiles(lens, G, rows)
         d = lambda a: h2d(a, dev)  # noqa: E731
         fb = ForwardBatch(is_decode=False, positions=d(np.stack([pos] * 3)), slot_mapping=d(slot_map),
                           kv_lens=h2d(lens, dev, torch.int32), block_table=d(bt),
                           input_embeds=torch.cat(embeds, 0).to(tl.cfg.dtype), cu_q=d(cu),
                           tile_req=h2d(req, dev, torch.int32), tile_tok0=h2d(tok0, dev, torch.int32),
-                          logits_indices=d(cu[1:] - 1))
+                          tile_rows=rows, logits_indices=d(cu[1:] - 1))
         hidden = tl(fb, self.pool.kv)
         slots = h2d([s.slot for s in streams], dev, torch.int32)
         cp_bt = (slots + 1).view(-1, 1).to(torch.int32)

@@ -10,19 +10,30 @@ non-causal SDPA (transformers qwen3_omni_moe audio / vision towers).
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 import torch.nn.functional as F
 
 from . import _check
-from ._ext import ext
+from ._ext import ext, status_word
 
 PAGE = 64
 
 
-def prefill_tiles(q_lens: list[int], group: int) -> tuple[list[int], list[int]]:
-    """64-row query tiles of the GQA-packed prefill kernel: (request, first token) per tile."""
-    tpt = max(1, 64 // group)
+def prefill_tile_rows(head_dim: int, group: int, paged: bool = True, window: int = 0) -> int:
+    """Packed query rows per tile of the prefill kernel that serves this shape: 128 for the
+    tcgen05 kernel (paged K/V, head_dim 128, no sliding window, G | 128), else 64 for the
+    mma.sync kernel.  OMNI_FA_SM100=0 keeps the 64-row kernel everywhere."""
+    if os.environ.get("OMNI_FA_SM100", "1") == "0":
+        return 64
+    return 128 if paged and head_dim == 128 and window == 0 and 128 % max(1, group) == 0 else 64
+
+
+def prefill_tiles(q_lens: list[int], group: int, rows: int = 64) -> tuple[list[int], list[int]]:
+    """Query tiles of the GQA-packed prefill kernels: (request, first token) per tile of
+    `rows` packed rows (rows / group tokens)."""
+    tpt = max(1, rows // group)
     req, tok0 = [], []
     for b, n in enumerate(q_lens):
         for t in range(0, n, tpt):
@@ -84,8 +95,11 @@ def varlen_attention_ref(q, k, v, cu_seqlens, scale, causal=False, window=0):
 def prefill_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table: torch.Tensor,
                       cu_q: torch.Tensor, kv_lens: torch.Tensor, tile_req: torch.Tensor, tile_tok0: torch.Tensor,
                       num_heads: int, num_kv_heads: int, head_dim: int, scale: float | None = None,
-                      out: torch.Tensor | None = None, causal: bool = True) -> torch.Tensor:
-    """Causal prefill over the paged cache. q: [T, Hq * D] rows (any row stride)."""
+                      out: torch.Tensor | None = None, causal: bool = True, tile_rows: int = 64) -> torch.Tensor:
+    """Causal prefill over the paged cache. q: [T, Hq * D] rows (any row stride).
+
+    ``tile_rows``: rows of the tiles in tile_req / tile_tok0 (``prefill_tile_rows``): 128 runs
+    the tcgen05 kernel, 64 the mma.sync kernel."""
     scale = scale if scale is not None else 1.0 / math.sqrt(head_dim)
     q3 = q.view(q.shape[0], -1) if q.dim() == 2 else q
     if out is None:
@@ -99,7 +113,7 @@ def prefill_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Ten
         _check.check_paged("attention_prefill", block_table, kv_lens, k_cache.shape[0], cu_q, q.shape[0])
         _check.check_tiles("attention_prefill", tile_req, tile_tok0, cu_q)
     ext().attention_prefill(q3, k_cache, v_cache, out, block_table, cu_q, kv_lens, None, tile_req, tile_tok0,
-                            num_heads, num_kv_heads, head_dim, scale, causal, 0)
+                            num_heads, num_kv_heads, head_dim, scale, causal, 0, tile_rows, status_word(q.device))
     return out
 
 

@@ -8,6 +8,7 @@ Used to produce the ncu summaries of the hot kernels.
 """
 from __future__ import annotations
 
+import os
 import sys
 
 import torch
@@ -66,12 +67,13 @@ def run(case: str) -> None:
         bt = torch.arange(1, R * pages + 1, dtype=torch.int32, device="cuda").view(R, pages)
         kl = torch.full((R,), P, dtype=torch.int32, device="cuda")
         cu = torch.arange(0, R * P + 1, P, dtype=torch.int32, device="cuda")
-        tr, t0 = prefill_tiles([P] * R, hq // hkv)
+        rows = int(os.environ.get("OMNI_BENCH_TILE_ROWS", "128"))   # 128: tcgen05 kernel, 64: mma.sync
+        tr, t0 = prefill_tiles([P] * R, hq // hkv, rows)
         tr = torch.tensor(tr, dtype=torch.int32, device="cuda")
         t0 = torch.tensor(t0, dtype=torch.int32, device="cuda")
         q = torch.randn(R * P, hq * d, device="cuda").bfloat16()
         for _ in range(3):
-            A.prefill_attention(q, k, v, bt, cu, kl, tr, t0, hq, hkv, d)
+            A.prefill_attention(q, k, v, bt, cu, kl, tr, t0, hq, hkv, d, tile_rows=rows)
     elif case == "rmsnorm":
         # fused residual add + RMSNorm over 65536 x 2048 bf16 (268 MB per tensor, > L2)
         from .norm import rms_norm
@@ -176,8 +178,25 @@ def _time_cases() -> None:
         f = 2.0 * xx.shape[0] * xx.shape[1] * ww.shape[0]
         flops[name] = (t(lambda: L.linear(xx, ww)), f)
         flops[name + " (cuBLAS)"] = (t(lambda: F.linear(xx, ww)), f)
+    # paged causal prefill attention, 8 x 1024 tokens, 32 q / 4 kv heads x 128 (half the QK^T / PV work is masked)
+    from . import prefill_tiles
+    R, P, hq, hkv, d = 8, 1024, 32, 4, 128
+    pages = P // 64
+    k = torch.randn(R * pages + 1, hkv, 64, d, device="cuda").bfloat16()
+    v = torch.randn_like(k)
+    bt = torch.arange(1, R * pages + 1, dtype=torch.int32, device="cuda").view(R, pages)
+    kl = torch.full((R,), P, dtype=torch.int32, device="cuda")
+    cu = torch.arange(0, R * P + 1, P, dtype=torch.int32, device="cuda")
+    q = torch.randn(R * P, hq * d, device="cuda").bfloat16()
+    f_attn = 4.0 * R * (P * (P + 1) / 2) * hq * d   # causal: QK^T + PV over the visible keys
+    for rows, tag in ((64, "mma.sync"), (128, "tcgen05")):
+        tr, t0 = prefill_tiles([P] * R, hq // hkv, rows)
+        tr = torch.tensor(tr, dtype=torch.int32, device="cuda")
+        t0 = torch.tensor(t0, dtype=torch.int32, device="cuda")
+        flops[f"prefill attn 8x1024 causal 32/4x128 ({tag})"] = (
+            t(lambda: A.prefill_attention(q, k, v, bt, cu, kl, tr, t0, hq, hkv, d, tile_rows=rows)), f_attn)
     for name, (us, f) in flops.items():
-        print(f"{name:40s} {us:8.2f} us  {f / us / 1e6:7.1f} TFLOP/s")
+        print(f"{name:44s} {us:8.2f} us  {f / us / 1e6:7.1f} TFLOP/s")
     B, hq, hkv, d, ctx = 64, 32, 4, 128, 1152
     pages = (ctx + 63) // 64
     k = torch.randn(B * pages + 1, hkv, 64, d, device="cuda").bfloat16()

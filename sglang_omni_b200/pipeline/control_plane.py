@@ -109,7 +109,10 @@ class _LocalSub:
 
 
 def _push(endpoint: str, bind: bool = False):
-    return _LocalPush(endpoint) if endpoint.startswith(LOCAL_PREFIX) else PushSocket(endpoint, bind)
+    sock = _LocalPush(endpoint) if endpoint.startswith(LOCAL_PREFIX) else PushSocket(endpoint, bind)
+    from . import faults
+
+    return faults.FaultyPush(sock, endpoint) if faults.active() else sock
 
 
 def _pull(endpoint: str):

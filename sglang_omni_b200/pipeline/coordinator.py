@@ -31,11 +31,18 @@ class _Req:
     stream: asyncio.Queue | None = None
     terminal_results: dict[str, Any] = field(default_factory=dict)
     submitted_at: float = field(default_factory=time.perf_counter)
+    last_seq: dict[str, int] = field(default_factory=dict)   # stage -> last stream chunk number seen
 
 
 class Coordinator:
     def __init__(self, completion_endpoint: str, abort_endpoint: str, entry_stage: str,
-                 terminal_stages: list[str] | None = None, max_retained: int = 10000):
+                 terminal_stages: list[str] | None = None, max_retained: int = 10000,
+                 request_timeout_s: float | None = None):
+        """``request_timeout_s``: a request that has not completed this long after its
+        submission fails with a TimeoutError and is aborted in every stage (a lost
+        completion or a stalled stage then ends in an error instead of a hang)."""
+        self.request_timeout_s = request_timeout_s
+        self._watchdog: asyncio.Task | None = None
         self.cp = CoordinatorControlPlane(completion_endpoint, abort_endpoint)
         self.entry_stage = entry_stage
         self.terminal_stages = list(terminal_stages or [])
@@ -52,6 +59,23 @@ class Coordinator:
     async def start(self):
         await self.cp.start()
         self.running = True
+        if self.request_timeout_s:
+            self._watchdog = asyncio.ensure_future(self._deadline_loop())
+
+    async def _deadline_loop(self):
+        period = max(0.01, min(1.0, self.request_timeout_s / 4))
+        while True:
+            await asyncio.sleep(period)
+            now = time.perf_counter()
+            late = [rid for rid, r in self._reqs.items() if now - r.submitted_at > self.request_timeout_s]
+            for rid in late:
+                log.warning("request %s exceeded its %.1fs deadline", rid, self.request_timeout_s)
+                try:
+                    await self.cp.broadcast(AbortMessage(rid))
+                except Exception:
+                    log.exception("abort broadcast for %s failed", rid)
+                self._finish(rid, RequestState.FAILED,
+                             exc=TimeoutError(f"request {rid} did not complete within {self.request_timeout_s}s"))
 
     async def stop(self):
         self.running = False
@@ -62,6 +86,8 @@ class Coordinator:
                 pass
         if self._loop_task is not None:
             self._loop_task.cancel()
+        if self._watchdog is not None:
+            self._watchdog.cancel()
         self.cp.close()
 
     # ------------------------------------------------------------------ submission
@@ -113,6 +139,10 @@ class Coordinator:
                 elif isinstance(msg, StreamMessage):
                     r = self._reqs.get(msg.request_id)
                     if r is not None and r.stream is not None:
+                        if msg.seq is not None:   # a duplicated (re-sent) chunk is dropped
+                            if msg.seq <= r.last_seq.get(msg.from_stage, -1):
+                                continue
+                            r.last_seq[msg.from_stage] = msg.seq
                         r.stream.put_nowait(msg)
             except Exception:
                 log.exception("coordinator failed on %s", type(msg).__name__)

@@ -98,7 +98,8 @@ class MultiProcessPipelineRunner:
         names = [s.name for s in stages_cfg]
         endpoints = allocate_endpoints(self.cfg, names, self.run_id)
         terminals = [name_map.get(t, t) for t in self.cfg.terminal_stages]
-        self.coordinator = Coordinator(endpoints.completion, endpoints.abort, entry, terminals)
+        self.coordinator = Coordinator(endpoints.completion, endpoints.abort, entry, terminals,
+                                       request_timeout_s=self.cfg.request_timeout_s)
         await self.coordinator.start()
         for n in names:
             self.coordinator.register_stage(n, endpoints.stages[n])

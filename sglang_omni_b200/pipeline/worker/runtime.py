@@ -146,10 +146,12 @@ class Worker:
 
     async def _forward_client_stream(self, rid: str, it):
         try:
+            seq = 0
             async for chunk in it:
                 modality = chunk.get("modality") if isinstance(chunk, dict) else None
                 await self.cp.send_to_coordinator(StreamMessage(rid, self.stage_name, chunk, self.stage_id,
-                                                                self.stage_name, modality))
+                                                                self.stage_name, modality, seq))
+                seq += 1
         except asyncio.CancelledError:
             raise
         except Exception:

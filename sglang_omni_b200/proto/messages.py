@@ -94,16 +94,20 @@ class StreamMessage:
     stage_id: int | None = None
     stage_name: str | None = None
     modality: str | None = None
+    seq: int | None = None      # per (request, stage) chunk number: duplicates are dropped
 
     def to_dict(self):
-        return {"type": "stream", "request_id": self.request_id, "from_stage": self.from_stage,
-                "chunk": _pack_obj(self.chunk), "stage_id": self.stage_id, "stage_name": self.stage_name,
-                "modality": self.modality}
+        d = {"type": "stream", "request_id": self.request_id, "from_stage": self.from_stage,
+             "chunk": _pack_obj(self.chunk), "stage_id": self.stage_id, "stage_name": self.stage_name,
+             "modality": self.modality}
+        if self.seq is not None:
+            d["seq"] = self.seq
+        return d
 
     @classmethod
     def from_dict(cls, d):
         return cls(d["request_id"], d["from_stage"], _unpack_obj(d.get("chunk")), d.get("stage_id"),
-                   d.get("stage_name"), d.get("modality"))
+                   d.get("stage_name"), d.get("modality"), d.get("seq"))
 
 
 @dataclass

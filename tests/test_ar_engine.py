@@ -4,7 +4,7 @@ import torch
 
 from sglang_omni_b200.engines.ar import AREngine, ARRequest, KVPool
 from sglang_omni_b200.models.decoder import DecoderConfig, DecoderLM, ForwardBatch
-from sglang_omni_b200.ops import prefill_tiles
+from sglang_omni_b200.ops import prefill_tile_rows, prefill_tiles
 from sglang_omni_b200.sampling_params import SamplingParams
 
 
@@ -26,7 +26,9 @@ def full_logits(model, tokens, device):
     pages = pool.alloc((T + 63) // 64)
     t = torch.arange(T)
     slots = (torch.tensor(pages)[t // 64] * 64 + t % 64).to(torch.int32)
-    req, tok0 = prefill_tiles([T], cfg.num_heads // cfg.num_kv_heads)
+    G = cfg.num_heads // cfg.num_kv_heads
+    rows = prefill_tile_rows(cfg.head_dim, G) if torch.device(device).type == "cuda" else 64
+    req, tok0 = prefill_tiles([T], G, rows)
     pos = torch.arange(T, dtype=torch.int32)
     fb = ForwardBatch(is_decode=False, positions=torch.stack([pos] * 3).to(device), slot_mapping=slots.to(device),
                       kv_lens=torch.tensor([T], dtype=torch.int32, device=device),
@@ -34,7 +36,7 @@ def full_logits(model, tokens, device):
                       input_ids=torch.tensor(tokens, dtype=torch.int32, device=device),
                       cu_q=torch.tensor([0, T], dtype=torch.int32, device=device),
                       tile_req=torch.tensor(req, dtype=torch.int32, device=device),
-                      tile_tok0=torch.tensor(tok0, dtype=torch.int32, device=device))
+                      tile_tok0=torch.tensor(tok0, dtype=torch.int32, device=device), tile_rows=rows)
     h = model(fb, pool.kv)
     return model.logits(h).float().cpu()
 

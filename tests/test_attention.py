@@ -46,22 +46,42 @@ def test_paged_ref_matches_dense_sdpa():
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("rows", [64, 128])
 @pytest.mark.parametrize("hq,hkv", [(32, 4), (16, 2), (32, 8), (16, 8)])
 @pytest.mark.parametrize("q_lens,kv_extra", [([1, 7, 64, 130], [0, 5, 0, 100]), ([300], [0]), ([9, 1], [200, 1000])])
-def test_prefill_paged(hq, hkv, q_lens, kv_extra):
+def test_prefill_paged(hq, hkv, q_lens, kv_extra, rows):
+    """rows=64: the mma.sync kernel; rows=128: the tcgen05 kernel (TMEM S / O, TMA K/V pages)."""
+    _prefill_case(hq, hkv, q_lens, kv_extra, rows)
+
+
+def _prefill_case(hq, hkv, q_lens, kv_extra, rows, q_scale=0.5, seed=0):
     d = 128
     kv_lens = [q + e for q, e in zip(q_lens, kv_extra)]
-    k, v, bt = _make_cache(kv_lens, hkv, d, "cuda")
+    k, v, bt = _make_cache(kv_lens, hkv, d, "cuda", seed=seed)
     T = sum(q_lens)
-    q = (torch.randn(T, hq * d, device="cuda") * 0.5).bfloat16()
+    g = torch.Generator(device="cuda").manual_seed(seed + 1)
+    q = (torch.randn(T, hq * d, device="cuda", generator=g) * q_scale).bfloat16()
     cu = torch.tensor([0] + list(torch.tensor(q_lens).cumsum(0).tolist()), dtype=torch.int32, device="cuda")
     kl = torch.tensor(kv_lens, dtype=torch.int32, device="cuda")
-    req, tok0 = A.prefill_tiles(q_lens, hq // hkv)
+    req, tok0 = A.prefill_tiles(q_lens, hq // hkv, rows)
     tr = torch.tensor(req, dtype=torch.int32, device="cuda")
     tt = torch.tensor(tok0, dtype=torch.int32, device="cuda")
-    out = A.prefill_attention(q, k, v, bt, cu, kl, tr, tt, hq, hkv, d)
+    out = A.prefill_attention(q, k, v, bt, cu, kl, tr, tt, hq, hkv, d, tile_rows=rows)
+    torch.cuda.synchronize()
+    from sglang_omni_b200.ops._ext import check_status
+
+    check_status(torch.device("cuda", 0))
     ref = A.paged_attention_ref(q.view(T, hq, d), k, v, bt, cu, kl, 1 / math.sqrt(d), True)
     torch.testing.assert_close(out.float().view(T, hq, d), ref, atol=2e-2, rtol=2e-2)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("hq,hkv", [(16, 16), (32, 2), (32, 4)])
+def test_prefill_tcgen05_long_and_rescaled(hq, hkv):
+    """The tcgen05 kernel over many key blocks (1024-token prompts after a cached prefix), MHA and
+    16-head groups, and large scores (q x 4) so the running max is raised and O rescaled in TMEM."""
+    _prefill_case(hq, hkv, [1024, 333], [0, 700], 128, q_scale=0.5, seed=5)
+    _prefill_case(hq, hkv, [512, 77], [64, 0], 128, q_scale=4.0, seed=6)
 
 
 @pytest.mark.gpu

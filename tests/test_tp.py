@@ -75,6 +75,34 @@ def _free_port():
     return p
 
 
+def _ds_logits(model, tokens, device, deepstack):
+    """Teacher-forced logits of one prefill with deep-stack rows added after layers 0 .. n-1."""
+    from sglang_omni_b200.engines.ar import KVPool
+    from sglang_omni_b200.models.decoder import ForwardBatch
+    from sglang_omni_b200.ops import prefill_tile_rows, prefill_tiles
+
+    cfg = model.cfg
+    T = len(tokens)
+    pool = KVPool(cfg.num_layers, cfg.num_kv_heads, cfg.head_dim, (T + 63) // 64 + 2, device, cfg.dtype)
+    pages = pool.alloc((T + 63) // 64)
+    t = torch.arange(T)
+    slots = (torch.tensor(pages)[t // 64] * 64 + t % 64).to(torch.int32)
+    G = cfg.num_heads // cfg.num_kv_heads
+    rows = prefill_tile_rows(cfg.head_dim, G)
+    req, tok0 = prefill_tiles([T], G, rows)
+    pos = torch.arange(T, dtype=torch.int32)
+    d = lambda x: x.to(device)  # noqa: E731
+    fb = ForwardBatch(is_decode=False, positions=d(torch.stack([pos] * 3)), slot_mapping=d(slots),
+                      kv_lens=d(torch.tensor([T], dtype=torch.int32)), block_table=d(torch.tensor([pages],
+                                                                                                   dtype=torch.int32)),
+                      input_ids=d(torch.tensor(tokens, dtype=torch.int32)), cu_q=d(torch.tensor([0, T],
+                                                                                             dtype=torch.int32)),
+                      tile_req=d(torch.tensor(req, dtype=torch.int32)), tile_tok0=d(torch.tensor(tok0,
+                                                                                              dtype=torch.int32)),
+                      tile_rows=rows, deepstack=list(deepstack))
+    return model.logits(model(fb, pool.kv)).float().cpu()
+
+
 def _worker(rank, world, port, q):
     import torch.distributed as dist
     from datetime import timedelta
@@ -103,6 +131,13 @@ def _worker(rank, world, port, q):
             torch.cuda.synchronize()
             check_status(dev)
             errs[f"prefill_moe{moe}"] = float((a - b).norm() / a.norm())
+            # deep-stack rows injected into the first two layers' outputs (vision positions 10..41)
+            gds = torch.Generator(device=dev).manual_seed(9)
+            pos = torch.arange(10, 42, device=dev)
+            ds = [(pos, torch.randn(32, cfg.hidden_size, device=dev, generator=gds).bfloat16()) for _ in range(2)]
+            a = _ds_logits(ref, toks, dev, ds)
+            b = _ds_logits(m, toks, dev, ds)
+            errs[f"prefill_deepstack_moe{moe}"] = float((a - b).norm() / a.norm())
             # engine: greedy decode, graphs on / off, identical requests on both ranks
             for graphs in (False, True):
                 pool = KVPool(m.cfg.num_layers, m.cfg.num_kv_heads, m.cfg.head_dim, 128, dev, m.cfg.dtype)
