@@ -21,6 +21,7 @@ import asyncio
 import base64
 import io
 import logging
+import os
 import threading
 import time
 from collections import deque
@@ -29,7 +30,6 @@ from typing import Any
 import numpy as np
 import torch
 
-from ....client.audio import decode_wav
 from ....engines.ar import AREngine, ARRequest, KVPool
 from ....engines.ar.adapter import PagedAREngineAdapter
 from ....engines.omni.factory import create_encoder_engine
@@ -37,6 +37,7 @@ from ....engines.omni.runtime.encoder import EncoderRequestData
 from ....executors import EngineExecutor, PreprocessingExecutor
 from ....executors.interface import Executor, ResultQueueMixin
 from ....executors.preprocessing_executor import StageError
+from ....pipeline import fastlane
 from ....ops.mel import LogMel
 from ....utils import trace
 from ....proto import StagePayload
@@ -64,17 +65,18 @@ def _load_image(item: Any) -> np.ndarray:
     """uint8 RGB [H, W, 3] from an array / nested list / PIL image / path / base64 (PNG/JPEG via PIL)."""
     if isinstance(item, dict):
         item = item.get("url") or item.get("image") or item.get("data")
-    if isinstance(item, str):
+    if isinstance(item, (str, bytes, bytearray)):
         from PIL import Image
 
-        if item.startswith("data:"):
-            item = item.split(",", 1)[1]
-        try:
+        from ....preprocessing.media import fetch, is_url
+
+        if isinstance(item, (bytes, bytearray)):
+            raw = bytes(item)
+        elif is_url(item) or os.path.exists(item):
+            raw = fetch(item)
+        else:
             raw = base64.b64decode(item, validate=True)
-            img = Image.open(io.BytesIO(raw))
-        except Exception:
-            img = Image.open(item)
-        item = np.asarray(img.convert("RGB"))
+        item = np.asarray(Image.open(io.BytesIO(raw)).convert("RGB"))
     arr = np.asarray(item)
     if arr.dtype != np.uint8:
         arr = np.clip(arr, 0, 255).astype(np.uint8)
@@ -84,26 +86,11 @@ def _load_image(item: Any) -> np.ndarray:
 
 
 def _load_audio(item: Any) -> torch.Tensor:
-    """Waveform at 16 kHz from an array / list / {"array", "sampling_rate"} / wav path / base64 wav."""
-    sr = SAMPLE_RATE_IN
-    if isinstance(item, dict):
-        sr = int(item.get("sampling_rate", SAMPLE_RATE_IN))
-        item = item.get("array", item.get("data", item.get("path")))
-    if isinstance(item, str):
-        if item.startswith("data:"):
-            item = item.split(",", 1)[1]
-        try:
-            raw = base64.b64decode(item, validate=True)
-        except Exception:
-            with open(item, "rb") as f:
-                raw = f.read()
-        x, sr = decode_wav(raw)
-        item = x
-    x = torch.as_tensor(np.asarray(item, dtype=np.float32)).reshape(-1)
-    if sr != SAMPLE_RATE_IN:
-        n = int(round(x.numel() * SAMPLE_RATE_IN / sr))
-        x = torch.nn.functional.interpolate(x[None, None], size=n, mode="linear", align_corners=False)[0, 0]
-    return x
+    """Waveform at 16 kHz from an array / list / {"array", "sampling_rate"} / WAV path, URL, data
+    URI or base64 (polyphase resampling for other rates)."""
+    from ....preprocessing.media import load_audio
+
+    return torch.from_numpy(load_audio(item, SAMPLE_RATE_IN))
 
 
 def create_preprocessing_executor(model_path: str = "", overrides: dict | None = None):
@@ -134,18 +121,26 @@ def create_preprocessing_executor(model_path: str = "", overrides: dict | None =
             th = max(unit, round(im.shape[0] / unit) * unit)
             tw = max(unit, round(im.shape[1] / unit) * unit)
             grids.append((1, th // unit, tw // unit))
-        if inp.get("prompt_token_ids") is not None and not waves and not images:
+        from ....preprocessing.media import load_video, video_grid
+
+        if (payload.request.params or {}).get("use_audio_in_video"):
+            raise ValueError("use_audio_in_video is not supported: pass the video's audio track in 'audios'")
+        videos = [load_video(v) for v in (inp.get("videos") or [])]
+        vgrids = [video_grid(v["frames"], unit) for v in videos]
+        if inp.get("prompt_token_ids") is not None and not waves and not images and not videos:
             ids = list(inp["prompt_token_ids"])
             p = torch.arange(len(ids), dtype=torch.int32)
             pos, delta, spans = torch.stack([p, p, p]), 0, []
+            image_spans = []
         else:
-            lay = build_prompt(tok, inp.get("messages"), inp.get("prompt"), counts, image_grids=grids)
+            lay = build_prompt(tok, inp.get("messages"), inp.get("prompt"), counts, image_grids=grids,
+                               video_grids=vgrids, video_second_per_grid=[v["second_per_grid"] for v in videos])
             ids = lay.ids
             pos, delta = mrope_positions(lay)
             spans = lay.audio_spans
-            image_spans = lay.image_spans
-        if inp.get("prompt_token_ids") is not None and not waves and not images:
-            image_spans = []
+            # images then videos: the vision stage encodes the items in this order
+            image_spans = lay.image_spans + lay.video_spans
+            images = images + videos
         data = {"prompt_token_ids": ids, "audio_waveforms": waves, "audio_spans": spans,
                 "images": images, "image_spans": image_spans,
                 "mrope_positions": pos, "mrope_delta": delta,
@@ -337,7 +332,10 @@ def create_thinker_executor(model_path: str = "", device: str = "cuda:0", max_ba
                             mask[a:b] = True
                         msg["mm_mask"] = mask
                         msg["mm_hidden_parts"] = list(ph)
-                if ex._stream_fn is not None:
+                lane = fastlane.get(speech_target)
+                if lane is not None:      # talker in this process: straight to its thread
+                    lane.deliver_many([(_rid, msg)])
+                elif ex._stream_fn is not None:
                     ex._stream_fn(_rid, msg, speech_target)
 
             req.on_token = on_token
@@ -385,8 +383,9 @@ class TalkerStreamingExecutor(ResultQueueMixin, Executor):
 
     def __init__(self, model_path: str, device: str, max_streams: int = 64, code_target: str = "code2wav",
                  overrides: dict | None = None, max_frames: int = 4096, use_graphs: bool = True,
-                 tail_frames: int = 50):
+                 tail_frames: int = 50, stage_name: str = "talker_ar"):
         super().__init__()
+        self.stage_name = stage_name
         dev = torch.device(device)
         self.device = dev
         self.talker = loader.get_talker(model_path, dev, overrides)
@@ -409,13 +408,25 @@ class TalkerStreamingExecutor(ResultQueueMixin, Executor):
 
     async def start(self):
         self._loop = asyncio.get_running_loop()
+        fastlane.register(self.stage_name, self)
         if self._thread is None:
             self._thread = threading.Thread(target=self._run, name="talker", daemon=True)
             self._thread.start()
 
     async def stop(self):
+        fastlane.unregister(self.stage_name, self)
         with self._cv:
             self._stop = True
+            self._cv.notify_all()
+
+    def deliver_many(self, items):
+        """Fast lane from the thinker's engine thread: token (and first-token prompt hidden
+        state) items of any streams, applied under the generator's lock."""
+        with self._cv:
+            for rid, data in items:
+                if "mm_hidden_parts" in data:
+                    self._first[rid] = {"mm_mask": data["mm_mask"], "parts": data["mm_hidden_parts"]}
+                self._tokens.setdefault(rid, []).append(int(data["token_id"]))
             self._cv.notify_all()
 
     async def add_request(self, payload: StagePayload) -> None:
@@ -425,7 +436,7 @@ class TalkerStreamingExecutor(ResultQueueMixin, Executor):
         speaker = (meta.get("audio") or {}).get("voice") or meta.get("voice")
         self._pending[rid] = {"payload": payload, "t0": time.perf_counter()}
         with self._cv:
-            self._tokens[rid] = []
+            self._tokens.setdefault(rid, [])      # fast-lane tokens may have arrived already
             self._new.append((rid, list(d.get("prompt_token_ids") or []), speaker))
             self._cv.notify_all()
         asyncio.ensure_future(self._pump(rid))
@@ -484,15 +495,23 @@ class TalkerStreamingExecutor(ResultQueueMixin, Executor):
     def _emit(self, streams, codes: torch.Tensor):
         host = codes.cpu().tolist()
         eos = self.talker.special.codec_eos
+        lane = fastlane.get(self.code_target)   # vocoder in this process: one hand-off per step
+        batch = []
         for s, c in zip(streams, host):
             if c[0] == eos or s.frames >= s.max_frames:
                 s.finished = True
-                self._stream_fn(s.rid, {"codes": [], "eos": True}, self.code_target)
+                if lane is None:
+                    self._stream_fn(s.rid, {"codes": [], "eos": True}, self.code_target)
                 self._finish(s.rid, frames=s.frames)
                 self.gen.remove(s.rid)
             else:
                 trace.mark(s.rid, "3_talker_first_frame")
-                self._stream_fn(s.rid, {"codes": c}, self.code_target)
+                if lane is not None:
+                    batch.append((s.rid, {"codes": c}))
+                else:
+                    self._stream_fn(s.rid, {"codes": c}, self.code_target)
+        if batch:
+            lane.deliver_many(batch)
 
     def _loop_body(self):
         gen = self.gen
@@ -600,16 +619,56 @@ class Code2WavStreamingExecutor(ResultQueueMixin, Executor):
         self._flushed: dict[str, asyncio.Future] = {}
         self._wake: asyncio.Event | None = None
         self._loop_task: asyncio.Task | None = None
+        self.stage_name = "code2wav"
+        self._lane_lock = threading.Lock()
+        self._lane_items: list = []      # fast-lane frames not yet applied on the event loop
+        self._early: dict[str, list] = {}  # frames of streams whose request has not arrived yet
+        self._loop: asyncio.AbstractEventLoop | None = None
+
+    async def start(self):
+        self._loop = asyncio.get_running_loop()
+        fastlane.register(self.stage_name, self)
+
+    async def stop(self):
+        fastlane.unregister(self.stage_name, self)
+
+    def deliver_many(self, items):
+        """Fast lane from the talker thread: one callback on the event loop per batch."""
+        with self._lane_lock:
+            first = not self._lane_items
+            self._lane_items.extend(items)
+        if first and self._loop is not None:
+            self._loop.call_soon_threadsafe(self._apply_lane)
+
+    def _apply_lane(self):
+        with self._lane_lock:
+            items, self._lane_items = self._lane_items, []
+        woke = False
+        for rid, data in items:
+            if rid not in self._streams:
+                if len(self._early) < 4096:   # frames of a stream that ended or was aborted are dropped
+                    self._early.setdefault(rid, []).append(data)
+                continue
+            self.sc.add_codes(rid, torch.tensor(data["codes"], dtype=torch.long))
+            woke = woke or self.sc.ready(rid)
+        if woke and self._wake is not None:
+            self._wake.set()
 
     async def add_request(self, payload: StagePayload) -> None:
         rid = payload.request_id
         if self._wake is None:
             self._wake = asyncio.Event()
+        if self._loop is None:
+            self._loop = asyncio.get_running_loop()
         if self._loop_task is None or self._loop_task.done():
             self._loop_task = asyncio.ensure_future(self._decoder_loop())
         self._streams[rid] = asyncio.Queue()
         self._audio[rid] = []
         self._flushed[rid] = asyncio.get_running_loop().create_future()
+        for data in self._early.pop(rid, []):
+            self.sc.add_codes(rid, torch.tensor(data["codes"], dtype=torch.long))
+        if self.sc.ready(rid):
+            self._wake.set()
         asyncio.ensure_future(self._run(payload))
 
     def stream(self, request_id: str):
@@ -688,6 +747,7 @@ class Code2WavStreamingExecutor(ResultQueueMixin, Executor):
 
     def _cleanup(self, rid: str):
         self.sc.close(rid)
+        self._early.pop(rid, None)
         self._finals.discard(rid)
         self._flushed.pop(rid, None)
         self._audio.pop(rid, None)

@@ -254,14 +254,42 @@ def image_to_patches(img: np.ndarray, cfg: VisionConfig, size: int | None = None
     return torch.from_numpy(np.ascontiguousarray(x).reshape(gh * gw, -1)), (1, gh, gw)
 
 
+def video_to_patches(frames: np.ndarray, cfg: VisionConfig, max_pixels: int = 448 * 448):
+    """uint8 RGB frames [N, H, W, 3] (N a multiple of the temporal patch) -> (patches
+    [t * gh * gw, patch_dim] float32, grid (t, gh, gw)): every frame resized (nearest) to the
+    grid of ``media.video_grid``, normalised, consecutive frame pairs forming one temporal
+    patch, cut in the merge-block order of the encoder (the image path with t > 1)."""
+    from ...preprocessing.media import video_grid
+
+    p, ms, tp = cfg.patch_size, cfg.spatial_merge_size, cfg.temporal_patch_size
+    n, H, W = frames.shape[:3]
+    t, mh, mw = video_grid(frames, p * ms, max_pixels)
+    th, tw = mh * p * ms, mw * p * ms
+    if (th, tw) != (H, W):
+        yi = (np.arange(th) * H / th).astype(int)
+        xi = (np.arange(tw) * W / tw).astype(int)
+        frames = frames[:, yi][:, :, xi]
+    x = (frames.astype(np.float32) / 255.0 - np.array(IMAGE_MEAN, np.float32)) / np.array(IMAGE_STD, np.float32)
+    x = x[: t * tp].transpose(0, 3, 1, 2)  # [t * tp, C, H, W]
+    gh, gw = th // p, tw // p
+    x = x.reshape(t, tp, 3, gh // ms, ms, p, gw // ms, ms, p)
+    x = x.transpose(0, 3, 6, 4, 7, 2, 1, 5, 8)  # t, bh, bw, mh, mw, C, tp, ph, pw
+    return torch.from_numpy(np.ascontiguousarray(x).reshape(t * gh * gw, -1)), (t, gh, gw)
+
+
 def encode_images(model_path: str, device, images: list, overrides: dict | None = None) -> dict:
+    """One vision-tower forward over images (uint8 [H, W, 3]) and videos (``{"frames": uint8
+    [N, H, W, 3], ...}`` from ``media.load_video``), in order; per item embeds, deep-stack
+    rows and merged (t, h, w) grids."""
     from . import loader
 
     enc = loader.get_vision_encoder(model_path, device, overrides)
     patches, grids = [], []
     for im in images:
-        arr = np.asarray(im, dtype=np.uint8)
-        pt, g = image_to_patches(arr, enc.cfg)
+        if isinstance(im, dict):
+            pt, g = video_to_patches(np.asarray(im["frames"], dtype=np.uint8), enc.cfg)
+        else:
+            pt, g = image_to_patches(np.asarray(im, dtype=np.uint8), enc.cfg)
         patches.append(pt)
         grids.append(g)
     emb, ds = enc(torch.cat(patches, 0), grids)

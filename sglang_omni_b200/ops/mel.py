@@ -95,8 +95,15 @@ class LogMel:
         if self.device.type != "cuda":
             return [self(a) for a in audios]
         frames, counts = [], []
-        for a in audios:
-            a = a.to(self.device, torch.float32, non_blocking=True)
+        # one pinned host buffer and one copy for every waveform of the batch (a pageable copy
+        # per waveform blocks the host thread each time)
+        host = [a.reshape(-1).to(torch.float32) for a in audios]
+        if all(not h.is_cuda for h in host):
+            flat = torch.cat(host).pin_memory().to(self.device, non_blocking=True)
+            dev_waves = list(torch.split(flat, [h.numel() for h in host]))
+        else:
+            dev_waves = [h.to(self.device, non_blocking=True) for h in host]
+        for a in dev_waves:
             x = torch.nn.functional.pad(a[None, None], (N_FFT // 2, N_FFT // 2), mode="reflect")[0, 0]
             fr = x.unfold(0, N_FFT, HOP)[:-1]  # [T, 400]
             frames.append(fr)

@@ -32,13 +32,11 @@ model_worker.py:107-118).
 """
 from __future__ import annotations
 
-import asyncio
 import copy
 import logging
 import multiprocessing as mp
 import os
 import socket
-import threading
 import time
 from dataclasses import dataclass, field
 
