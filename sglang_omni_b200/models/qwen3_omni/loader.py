@@ -49,6 +49,8 @@ def _cfgs(model_path):
 
 def _apply(cfg, over: dict | None):
     for k, v in (over or {}).items():
+        if k == "dtype" and isinstance(v, str):   # YAML configs name dtypes ("float32", "bfloat16")
+            v = getattr(torch, v.replace("torch.", ""))
         setattr(cfg, k, v)
     return cfg
 

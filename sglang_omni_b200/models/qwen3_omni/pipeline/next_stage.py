@@ -39,3 +39,16 @@ def talker_next(request_id, payload):
 
 def code2wav_next(request_id, payload):
     return None
+
+
+# names of the reference's 9-stage speech layout (talker_ar -> code_predictor -> code2wav)
+def thinker_next_speech(request_id, payload):
+    return DECODE_STAGE
+
+
+def talker_ar_next(request_id, payload):
+    return None
+
+
+def code_predictor_next(request_id, payload):
+    return None

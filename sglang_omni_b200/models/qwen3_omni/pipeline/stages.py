@@ -151,9 +151,15 @@ def create_preprocessing_executor(model_path: str = "", overrides: dict | None =
 
 
 # ----------------------------------------------------------------------------- encoders
+def _device(device: str) -> str:
+    """Reference configs say "cuda": this process's first visible GPU."""
+    return "cuda:0" if device == "cuda" else device
+
+
 def create_audio_encoder_executor(model_path: str = "", device: str = "cuda:0", max_batch_size: int = 32,
-                                  overrides: dict | None = None):
-    dev = torch.device(device)
+                                  overrides: dict | None = None, dtype=None):
+    """``dtype``: accepted for reference configs; the tower runs in its configured dtype."""
+    dev = torch.device(_device(device))
     enc = loader.get_audio_encoder(model_path, dev, overrides)
     mel = LogMel(enc.cfg.num_mel_bins, dev)
 
@@ -192,12 +198,12 @@ def create_audio_encoder_executor(model_path: str = "", device: str = "cuda:0", 
 
 
 def create_image_encoder_executor(model_path: str = "", device: str = "cuda:0", max_batch_size: int = 32,
-                                  overrides: dict | None = None):
+                                  overrides: dict | None = None, dtype=None):
     """The vision tower over a gathered burst of requests: one forward for every image of
     the batch (ragged attention keeps images apart), split back per request."""
     from ..vision_encoder import encode_images
 
-    dev = torch.device(device)
+    dev = torch.device(_device(device))
     # built now, not on the first request: building ends with a device-wide synchronize, which
     # must not run while another stage's engine thread is capturing its CUDA graphs
     loader.get_vision_encoder(model_path, dev, overrides)
@@ -365,6 +371,30 @@ def create_thinker_executor(model_path: str = "", device: str = "cuda:0", max_ba
     return ex
 
 
+def create_sglang_thinker_executor_from_config(model_path: str = "", device: str = "cuda",
+                                               thinker_max_seq_len: int = 8192, speech_enabled: bool = False,
+                                               **kw):
+    """Factory name and arguments of the reference's thinker stage
+    (sglang_omni/models/qwen3_omni/config.py:160-168): the paged-engine thinker, streaming
+    to the talker when speech is enabled."""
+    from .next_stage import TALKER_AR_STAGE
+
+    kw.setdefault("max_context", thinker_max_seq_len)
+    return create_thinker_executor(model_path=model_path, device=_device(device),
+                                   speech_target=TALKER_AR_STAGE if speech_enabled else None, **kw)
+
+
+def create_talker_ar_executor_from_config(model_path: str = "", device: str = "cuda", talker_max_seq_len: int = 8192,
+                                          speech_enabled: bool = True, feedback_enabled: bool = True, **kw):
+    """Factory name and arguments of the reference's talker stage (config.py:179-192).  The
+    code predictor runs inside this stage (one CUDA graph per frame); its frames go to the
+    ``code_predictor`` stage of the reference layout, which forwards them to code2wav."""
+    from .next_stage import CODE_PREDICTOR_STAGE
+
+    kw.setdefault("max_frames", talker_max_seq_len)
+    return TalkerStreamingExecutor(model_path, _device(device), code_target=CODE_PREDICTOR_STAGE, **kw)
+
+
 def create_decode_executor(**_):
     def run(payload: StagePayload) -> StagePayload:
         d = dict(payload.data or {})
@@ -506,6 +536,8 @@ class TalkerStreamingExecutor(ResultQueueMixin, Executor):
                 self.gen.remove(s.rid)
             else:
                 trace.mark(s.rid, "3_talker_first_frame")
+                if trace.ENABLED and s.frames >= 4:
+                    trace.mark(s.rid, "3b_talker_frame_4")
                 if lane is not None:
                     batch.append((s.rid, {"codes": c}))
                 else:
@@ -650,7 +682,10 @@ class Code2WavStreamingExecutor(ResultQueueMixin, Executor):
                     self._early.setdefault(rid, []).append(data)
                 continue
             self.sc.add_codes(rid, torch.tensor(data["codes"], dtype=torch.long))
-            woke = woke or self.sc.ready(rid)
+            ready = self.sc.ready(rid)
+            if ready:
+                trace.mark(rid, "3c_vocoder_chunk_ready")
+            woke = woke or ready
         if woke and self._wake is not None:
             self._wake.set()
 
@@ -693,6 +728,8 @@ class Code2WavStreamingExecutor(ResultQueueMixin, Executor):
             finals = {r for r in live if r in self._finals}
             ready = [r for r in live if self.sc.ready(r, r in finals)]
             if ready:
+                for r in ready:
+                    trace.mark(r, "3d_vocoder_decode_start")
                 try:
                     out = await asyncio.to_thread(self.sc.decode_ready, ready, False, finals)
                 except Exception as exc:  # fail the streams of this batch only

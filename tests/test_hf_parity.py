@@ -179,3 +179,38 @@ def test_code_predictor_backbone_matches_hf():
     o = _ours_forward(ours, tokens, pos)
     err = float((o - r).norm() / r.norm())
     assert err < 1e-4, err
+
+
+def test_mrope_video_positions_match_hf_get_rope_index():
+    """Image + video + audio prompt (2 fps sampling: 1 s per temporal patch)."""
+    import types
+
+    from sglang_omni_b200.models.qwen3_omni import engine_io as eio
+    from sglang_omni_b200.models.qwen3_omni.hf_config import (AUDIO_START_TOKEN_ID, AUDIO_TOKEN_ID, IMAGE_TOKEN_ID,
+                                                              VIDEO_TOKEN_ID, VISION_START_TOKEN_ID)
+
+    cls = hm.Qwen3OmniMoePreTrainedModelForConditionalGeneration
+    fake = types.SimpleNamespace(
+        config=types.SimpleNamespace(image_token_id=IMAGE_TOKEN_ID, video_token_id=VIDEO_TOKEN_ID,
+                                     audio_token_id=AUDIO_TOKEN_ID, vision_start_token_id=VISION_START_TOKEN_ID,
+                                     audio_start_token_id=AUDIO_START_TOKEN_ID, position_id_per_seconds=25),
+        spatial_merge_size=2)
+    fake.get_llm_pos_ids_for_vision = types.MethodType(cls.get_llm_pos_ids_for_vision, fake)
+
+    class Tok:
+        def encode(self, s):
+            return [1000 + (ord(c) % 50) for c in s]
+
+    mel = 500
+    n_audio = int(hm._get_feat_extract_output_lengths(torch.tensor(mel)))
+    for spg in (1.0, 2.0):
+        lay = eio.build_prompt(Tok(), None, "what happens", [n_audio], image_grids=[(1, 3, 4)],
+                               video_grids=[(3, 2, 3)], video_second_per_grid=[spg])
+        ours, delta = eio.mrope_positions(lay)
+        ids = torch.tensor([lay.ids])
+        ref, ref_delta = cls.get_rope_index(fake, ids, image_grid_thw=torch.tensor([[1, 6, 8]]),
+                                            video_grid_thw=torch.tensor([[3, 4, 6]]),
+                                            audio_seqlens=torch.tensor([mel]), attention_mask=torch.ones_like(ids),
+                                            second_per_grids=torch.tensor([spg]))
+        assert torch.equal(ours.long(), ref[:, 0].long()), (spg, ours, ref[:, 0])
+        assert delta == int(ref_delta[0])

@@ -161,3 +161,84 @@ def test_image_text_pipeline_batched_encoder_cpu():
 
     outs = asyncio.run(main())
     assert [len(o.token_ids) for o in outs] == [4, 3, 5]
+
+
+def _reference_speech_yaml(tmp_path):
+    """The reference's 9-stage speech layout (sglang_omni/models/qwen3_omni/config.py:104-221)
+    as YAML, with its factory / routing paths and arguments; only the tiny-model overrides and
+    CPU devices are added for this test."""
+    import yaml
+
+    S = "sglang_omni.models.qwen3_omni.pipeline.stages"
+    N = "sglang_omni.models.qwen3_omni.pipeline.next_stage"
+    C = "sglang_omni.models.qwen3_omni.components"
+    ov = {"overrides": {k: {a: ("float32" if b is torch.float32 else b) for a, b in v.items()}
+                        for k, v in TINY.items()}}
+
+    def stage(name, factory, args, nxt, stream_to=(), **extra):
+        d = {"name": name, "executor": {"factory": factory, "args": args}, "get_next": f"{N}.{nxt}",
+             "relay": {"device": "cpu"}, "stream_to": [{"to_stage": t, "bootstrap": b} for t, b in stream_to]}
+        d.update(extra)
+        return d
+
+    cfg = {
+        "model_path": "random", "entry_stage": "preprocessing", "terminal_stages": ["decode", "code2wav"],
+        "gpu_placement": {"thinker": 0, "talker_ar": 1, "code_predictor": 1, "code2wav": 1},
+        "stages": [
+            stage("preprocessing", f"{S}.create_preprocessing_executor", dict(ov), "preprocessing_next"),
+            stage("image_encoder", f"{S}.create_image_encoder_executor", {"device": "cpu", "dtype": None, **ov},
+                  "encoder_next"),
+            stage("audio_encoder", f"{S}.create_audio_encoder_executor", {"device": "cpu", "dtype": None, **ov},
+                  "encoder_next"),
+            stage("mm_aggregate", f"{S}.create_aggregate_executor", {}, "aggregate_next",
+                  input_handler={"type": "aggregated", "sources": ["preprocessing", "image_encoder", "audio_encoder"],
+                                 "merge_fn": "sglang_omni.models.qwen3_omni.pipeline.merge.merge_for_thinker"}),
+            stage("thinker", f"{S}.create_sglang_thinker_executor_from_config",
+                  {"thinker_max_seq_len": 1024, "speech_enabled": True, "device": "cpu", "max_batch": 4, **ov},
+                  "thinker_next_speech", stream_to=[("talker_ar", True)]),
+            stage("decode", f"{S}.create_decode_executor", {}, "decode_next"),
+            stage("talker_ar", f"{S}.create_talker_ar_executor_from_config",
+                  {"talker_max_seq_len": 1024, "speech_enabled": True, "feedback_enabled": True, "device": "cpu",
+                   "max_streams": 4, "tail_frames": 12, **ov}, "talker_ar_next", stream_to=[("code_predictor", True)]),
+            stage("code_predictor", f"{C}.code_predictor_executor.create_code_predictor_executor_from_config",
+                  {"code_predictor_max_seq_len": 256}, "code_predictor_next",
+                  stream_to=[("code2wav", True), ("talker_ar", False)]),
+            stage("code2wav", f"{C}.code2wav_executor.create_code2wav_executor", {"device": "cpu", **ov},
+                  "code2wav_next"),
+        ],
+    }
+    p = tmp_path / "qwen3_omni_speech_reference_layout.yaml"
+    p.write_text(yaml.safe_dump(cfg, sort_keys=False))
+    return p
+
+
+@pytest.mark.parametrize("fast_lanes", [True, False])
+def test_reference_layout_yaml_runs(tmp_path, monkeypatch, fast_lanes):
+    """A config in the reference's 9-stage layout compiles and serves a speech request."""
+    from sglang_omni_b200.config.manager import ConfigManager
+    from sglang_omni_b200.pipeline import fastlane
+
+    if not fast_lanes:   # every hop over the relay, as between stage processes
+        monkeypatch.setattr(fastlane, "get", lambda stage: None)
+    cfg = ConfigManager.from_file(str(_reference_speech_yaml(tmp_path)))
+    assert [s.name for s in cfg.stages][-3:] == ["talker_ar", "code_predictor", "code2wav"]
+
+    async def main():
+        coord, stages = compile_pipeline(cfg)
+        async with PipelineRunner(coord, stages):
+            client = Client(coord)
+            audio = (np.random.default_rng(2).standard_normal(16000) * 0.1).astype(np.float32)
+            req = GenerateRequest(prompt="hi", audios=[audio], max_tokens=5,
+                                  sampling=SamplingParams(temperature=0.0, ignore_eos=True),
+                                  output_modalities=["text", "audio"], stream=True)
+            text, audio_chunks, final = [], [], None
+            async for ch in client.generate(req):
+                if ch.finish_reason is not None:
+                    final = ch
+                elif ch.modality == "audio":
+                    audio_chunks.append(ch)
+                elif ch.token_ids:
+                    text += ch.token_ids
+            assert len(text) == 5 and audio_chunks and final is not None
+
+    asyncio.run(main())

@@ -63,3 +63,19 @@ def test_vision_gpu_matches_cpu_head_dim_72():
     out, ds = gpu(px, [grid])
     assert (out.float().cpu() - ref).abs().max() / ref.abs().max() < 0.05
     assert (ds[0].float().cpu() - ref_ds[0]).abs().max() / ref_ds[0].abs().max() < 0.05
+
+
+def test_vision_video_matches_hf_cpu():
+    """A 4-frame clip (two temporal patches) through our patching + tower and HF's."""
+    from sglang_omni_b200.models.qwen3_omni.vision_encoder import video_to_patches
+
+    m, ours = tiny()
+    rng = np.random.default_rng(3)
+    frames = rng.integers(0, 256, (4, 16, 24, 3), dtype=np.uint8)
+    px, grid = video_to_patches(frames, ours.cfg, max_pixels=16 * 24)
+    assert grid == (2, 4, 6)
+    with torch.no_grad():
+        ref = m(px, grid_thw=torch.tensor([grid]))
+        out, ds = ours(px, [grid])
+    ref_main = ref.pooler_output if getattr(ref, "pooler_output", None) is not None else ref.last_hidden_state
+    assert (out - ref_main).abs().max() / ref_main.abs().max() < 1e-3
