@@ -665,7 +665,7 @@ cudaError_t launch_decode(const DecodeParams& p, int batch, cudaStream_t stream)
 
 cudaError_t attention_prefill(const AttnPrefillArgs& a, cudaStream_t stream) {
   if (a.num_tiles == 0) return cudaSuccess;
-  if (a.tile_rows == 128) return attention_prefill_sm100(a, stream);
+  if (a.tile_rows == 128 || a.tile_rows == 256) return attention_prefill_sm100(a, stream);
   if (a.hq <= 0 || a.hkv <= 0 || a.hq % a.hkv != 0 || 64 % (a.hq / a.hkv) != 0) return cudaErrorInvalidValue;
   PrefillParams p;
   p.q = static_cast<const __nv_bfloat16*>(a.q);

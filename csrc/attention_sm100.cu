@@ -394,6 +394,275 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------ two-tile (ping-pong) variant
+// One CTA = two 128-row query tiles (A, B) sharing every 64-key K/V block (one page).  The MMA
+// issue order  PV_A(j), S_A(j+1), PV_B(j), S_B(j+1)  lets the softmax of tile A on block j+1
+// overlap the softmax of tile B on block j and the tensor core's work for the other tile.
+// TMEM: S_A | S_B (64 columns each), O_A | O_B (128 each).  Warps: 0 producer, 1 MMA,
+// 2-5 softmax + epilogue of tile A, 6-9 of tile B.
+namespace pp {
+constexpr int kPBN = 64;              // keys per block (one page)
+constexpr int kStages = 3;
+constexpr int kThreads = 320;
+constexpr int kQBytes = kRows * kD * 2;            // 32 KB per tile
+constexpr int kKVBytes = kPBN * kD * 2;             // 16 KB (two 64-column regions of 8 KB)
+constexpr int kPBytes = kRows * kPBN * 2;           // 16 KB
+constexpr int kQ = 0;
+constexpr int kK = kQ + 2 * kQBytes;
+constexpr int kV = kK + kStages * kKVBytes;
+constexpr int kP = kV + kStages * kKVBytes;
+constexpr int kBars = kP + 2 * kPBytes;
+constexpr int kSmem = kBars + 256 + 1024;
+static_assert(kSmem <= 232448, "shared memory exceeds 227 KB");
+}  // namespace pp
+
+__global__ void __launch_bounds__(pp::kThreads, 1)
+    fa_prefill_pp_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
+                         const __grid_constant__ CUtensorMap tmap_v, const FaParams p) {
+  using namespace pp;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBars);
+  uint64_t* q_full = bars;                   // [1]
+  uint64_t* kv_full = bars + 1;              // [kStages]
+  uint64_t* kv_empty = kv_full + kStages;    // [kStages]
+  uint64_t* s_full = kv_empty + kStages;     // [2] tile A / B
+  uint64_t* p_full = s_full + 2;             // [2]
+  uint64_t* pv_done = p_full + 2;            // [2]
+  uint64_t* drain = pv_done + 2;             // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x, h = blockIdx.y;
+  const int req = p.tile_req[tile];
+  const int tok0 = p.tile_tok0[tile];
+  const int q_begin = p.cu_q[req];
+  const int q_len = p.cu_q[req + 1] - q_begin;
+  const int kv_len = p.kv_lens[req];
+  const int tpt = kRows / p.G;                       // tokens per 128-row tile
+  const int past = kv_len - q_len;
+  const int key_end = p.causal ? min(kv_len, past + min(q_len, tok0 + 2 * tpt)) : kv_len;
+  const int nb = key_end > 0 ? (key_end + kPBN - 1) / kPBN : 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&pv_done[i], 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmap_q);
+    tma_prefetch_desc(&tmap_k);
+    tma_prefetch_desc(&tmap_v);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto s_col = [](int t) -> uint32_t { return static_cast<uint32_t>(t) * 64u; };           // S_A | S_B
+  auto o_col = [](int t) -> uint32_t { return 128u + static_cast<uint32_t>(t) * 128u; };   // O_A | O_B
+
+  if (warp == 0) {
+    if (lane == 0 && nb > 0) {
+      mbar_arrive_expect_tx(q_full, 2 * kQBytes);
+      for (int t = 0; t < 2; ++t)
+        for (int r = 0; r < 2; ++r)
+          tma_load_3d(smem + kQ + t * kQBytes + r * (kQBytes / 2), &tmap_q, q_full, r * 64, h * p.G,
+                      q_begin + tok0 + t * tpt);
+      const int pages = (kv_len + 63) / 64;
+      bool ok = true;
+      for (int j = 0; j < nb && ok; ++j) {
+        const int s = j % kStages;
+        if (j >= kStages && !mbar_wait(&kv_empty[s], ((j / kStages) & 1) ^ 1, abort_flag, p.status)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&kv_full[s], 2 * kKVBytes);
+        const int page = j < pages ? fa_page(p, req, j) : 0;
+        const int row = (page * p.hkv + h) * 64;
+        for (int r = 0; r < 2; ++r) {
+          tma_load_2d(smem + kK + s * kKVBytes + r * (kKVBytes / 2), &tmap_k, &kv_full[s], r * 64, row);
+          tma_load_2d(smem + kV + s * kKVBytes + r * (kKVBytes / 2), &tmap_v, &kv_full[s], r * 64, row);
+        }
+      }
+      mbar_wait(q_full, 0, nullptr, p.status);
+      for (int j = max(0, nb - kStages); j < nb && ok; ++j)
+        mbar_wait(&kv_full[j % kStages], (j / kStages) & 1, nullptr, p.status);
+    }
+  } else if (warp == 1) {
+    constexpr uint32_t idesc_s = umma_idesc_bf16_f32(kRows, kPBN);
+    constexpr uint32_t idesc_o = umma_idesc_bf16_f32_bmn(kRows, kD);
+    bool ok = nb > 0 && mbar_wait(q_full, 0, abort_flag, p.status);
+    auto issue_s = [&](int t, int j) -> bool {
+      const int s = j % kStages;
+      if (t == 0 && !mbar_wait(&kv_full[s], (j / kStages) & 1, abort_flag, p.status)) return false;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t qa = smem_u32(smem + kQ + t * kQBytes);
+        const uint32_t ka = smem_u32(smem + kK + s * kKVBytes);
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          const uint64_t adesc = umma_desc_sw128(qa + (kk >> 2) * (kQBytes / 2)) + 2 * (kk & 3);
+          const uint64_t bdesc = umma_desc_sw128(ka + (kk >> 2) * (kKVBytes / 2)) + 2 * (kk & 3);
+          umma_f16_ss(tmem + s_col(t), adesc, bdesc, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[t]);
+      }
+      __syncwarp();
+      return true;
+    };
+    auto issue_pv = [&](int t, int j) -> bool {
+      if (!mbar_wait(&p_full[t], j & 1, abort_flag, p.status)) return false;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t pa = smem_u32(smem + kP + t * kPBytes);
+        const uint32_t va = smem_u32(smem + kV + (j % kStages) * kKVBytes);
+#pragma unroll
+        for (int kk = 0; kk < kPBN / 16; ++kk) {
+          const uint64_t adesc = umma_desc_sw128(pa) + 2 * kk;
+          const uint64_t bdesc = umma_desc_sw128_mn(va + kk * 16 * 128, kKVBytes / 2);
+          umma_f16_ss(tmem + o_col(t), adesc, bdesc, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&pv_done[t]);
+        if (t == 1) umma_commit(&kv_empty[j % kStages]);
+      }
+      __syncwarp();
+      return true;
+    };
+    if (ok) ok = issue_s(0, 0) && issue_s(1, 0);
+    for (int j = 0; j < nb && ok; ++j) {
+      if (!issue_pv(0, j)) { ok = false; break; }
+      if (j + 1 < nb && !issue_s(0, j + 1)) { ok = false; break; }
+      if (!issue_pv(1, j)) { ok = false; break; }
+      if (j + 1 < nb && !issue_s(1, j + 1)) { ok = false; break; }
+    }
+    if (lane == 0) {
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr, p.status);
+    }
+    __syncwarp();
+  } else {
+    const int t = warp < 6 ? 0 : 1;                   // tile of this warpgroup
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;                  // row within the tile = TMEM lane
+    const int tok = tok0 + t * tpt + r / p.G;
+    const bool row_ok = tok < q_len;
+    const int qpos = past + tok;
+    const int lim = p.causal ? min(kv_len, qpos + 1) : kv_len;   // keys [0, lim) are visible
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    uint8_t* prow = smem + kP + t * kPBytes + r * 128;
+    for (int j = 0; j < nb && ok; ++j) {
+      if (!mbar_wait(&s_full[t], j & 1, abort_flag, p.status)) { ok = false; break; }
+      tc_fence_after();
+      float s[kPBN];
+#pragma unroll
+      for (int c = 0; c < kPBN; c += 32) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem + lane_addr + s_col(t) + c, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[c + i] = __uint_as_float(v[i]);
+      }
+      const int k0 = j * kPBN;
+      float mb = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < kPBN; ++i) {
+        const float x = (k0 + i < lim) ? s[i] * p.scale_log2 : -INFINITY;
+        s[i] = x;
+        mb = fmaxf(mb, x);
+      }
+      // the previous PV of this tile has read P and (for a rescale) finished accumulating O
+      if (j > 0 && !mbar_wait(&pv_done[t], (j - 1) & 1, abort_flag, p.status)) { ok = false; break; }
+      if (mb > m_run + kRescaleThreshold || (m_run == -INFINITY && mb > -INFINITY)) {
+        if (j > 0 && m_run > -INFINITY) {
+          tc_fence_after();
+          const float f = exp2f(m_run - mb);
+#pragma unroll 1
+          for (int c = 0; c < kD; c += 32) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(tmem + lane_addr + o_col(t) + c, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * f);
+            tmem_st_32x32b_x32(tmem + lane_addr + o_col(t) + c, v);
+          }
+          tmem_st_wait();
+          l_run *= f;
+        }
+        m_run = mb;
+      }
+      const float msub = m_run == -INFINITY ? 0.f : m_run;
+      float lsum = 0.f;
+#pragma unroll
+      for (int c8 = 0; c8 < kPBN / 8; ++c8) {
+        float e[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          e[i] = exp2f(s[c8 * 8 + i] - msub);
+          lsum += e[i];
+        }
+        uint4 pk;
+        pk.x = pack_bf16x2(e[0], e[1]);
+        pk.y = pack_bf16x2(e[2], e[3]);
+        pk.z = pack_bf16x2(e[4], e[5]);
+        pk.w = pack_bf16x2(e[6], e[7]);
+        *reinterpret_cast<uint4*>(prow + ((c8 ^ (r & 7)) << 4)) = pk;
+      }
+      l_run += lsum;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[t]);
+    }
+    __nv_bfloat16* orow =
+        p.out + static_cast<int64_t>(q_begin + tok) * p.out_stride + static_cast<int64_t>(h * p.G + r % p.G) * kD;
+    if (ok && nb > 0 && mbar_wait(&pv_done[t], (nb - 1) & 1, abort_flag, p.status)) {
+      tc_fence_after();
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+#pragma unroll 1
+      for (int c = 0; c < kD; c += 32) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem + lane_addr + o_col(t) + c, v);
+        tmem_ld_wait();
+        if (row_ok) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 o;
+            o.x = pack_bf16x2(__uint_as_float(v[i]) * inv, __uint_as_float(v[i + 1]) * inv);
+            o.y = pack_bf16x2(__uint_as_float(v[i + 2]) * inv, __uint_as_float(v[i + 3]) * inv);
+            o.z = pack_bf16x2(__uint_as_float(v[i + 4]) * inv, __uint_as_float(v[i + 5]) * inv);
+            o.w = pack_bf16x2(__uint_as_float(v[i + 6]) * inv, __uint_as_float(v[i + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + c + i) = o;
+          }
+        }
+      }
+    } else if (nb == 0 && row_ok) {
+      for (int c = 0; c < kD; c += 8) *reinterpret_cast<uint4*>(orow + c) = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
 // ------------------------------------------------------------------ host side
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -467,10 +736,16 @@ cudaError_t attention_prefill_sm100(const AttnPrefillArgs& a, cudaStream_t strea
   p.out_stride = a.out_stride;
   p.num_pages = a.num_pages;
   p.status = a.status;
-  cudaError_t e = ensure_smem_attr<fa_prefill_kernel>(FaSmem::kBytes);
-  if (e != cudaSuccess) return e;
   dim3 grid(a.num_tiles, a.hkv);
-  fa_prefill_kernel<<<grid, kThreads, FaSmem::kBytes, stream>>>(tq, tk, tv, p);
+  if (a.tile_rows == 256) {
+    cudaError_t e = ensure_smem_attr<fa_prefill_pp_kernel>(pp::kSmem);
+    if (e != cudaSuccess) return e;
+    fa_prefill_pp_kernel<<<grid, pp::kThreads, pp::kSmem, stream>>>(tq, tk, tv, p);
+  } else {
+    cudaError_t e = ensure_smem_attr<fa_prefill_kernel>(FaSmem::kBytes);
+    if (e != cudaSuccess) return e;
+    fa_prefill_kernel<<<grid, kThreads, FaSmem::kBytes, stream>>>(tq, tk, tv, p);
+  }
   return cudaGetLastError();
 }
 

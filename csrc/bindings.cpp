@@ -215,9 +215,9 @@ void attention_prefill(const torch::Tensor& q, const torch::Tensor& k, const tor
   a.tile_rows = static_cast<int>(tile_rows);
   a.q_rows = static_cast<int>(q.size(0));
   a.status = status_ptr(status);
-  TORCH_CHECK(tile_rows == 64 || tile_rows == 128, "tile_rows must be 64 or 128");
+  TORCH_CHECK(tile_rows == 64 || tile_rows == 128 || tile_rows == 256, "tile_rows must be 64, 128 or 256");
   TORCH_CHECK(tile_rows == 64 || omni::attention_prefill_sm100_supported(a),
-              "128-row tiles need the paged tcgen05 kernel (head_dim 128, no window, aligned rows)");
+              "128 / 256-row tiles need the paged tcgen05 kernel (head_dim 128, no window, aligned rows)");
   check_launch(omni::attention_prefill(a, at::cuda::getCurrentCUDAStream()), "attention_prefill");
 }
 

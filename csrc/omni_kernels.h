@@ -125,8 +125,9 @@ struct AttnPrefillArgs {
   int window;             // > 0: causal sliding window (a query sees its last `window` keys)
   int num_pages;          // paged mode: pages in the cache; block-table entries outside [0, num_pages)
                           // read page 0 (the reserved padding page). 0 = unchecked
-  int tile_rows;          // packed query rows per tile: 64 (mma.sync kernel) or 128 (tcgen05 kernel,
-                          // csrc/attention_sm100.cu: paged, head_dim 128, no window)
+  int tile_rows;          // packed query rows per tile: 64 (mma.sync kernel), 128 (tcgen05 kernel,
+                          // csrc/attention_sm100.cu: paged, head_dim 128, no window) or 256 (its
+                          // two-tile ping-pong variant)
   int q_rows;             // rows of q (tokens of the batch)
   int* status;            // bounded-wait status word (tcgen05 kernel), may be nullptr
 };

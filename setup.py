@@ -61,5 +61,7 @@ setup(
     version="0.1.0",
     packages=["sglang_omni_b200"],
     ext_modules=ext_modules,
+    # the reference's command name (pyproject.toml:68 there): sgl-omni serve | config view | config export
+    entry_points={"console_scripts": ["sgl-omni=sglang_omni_b200.cli.cli:main"]},
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
 )

@@ -46,7 +46,7 @@ def cmd_config(args, extra):
 
 
 def main(argv=None):
-    ap = argparse.ArgumentParser(prog="sgl-omni-b200")
+    ap = argparse.ArgumentParser(prog="sgl-omni")
     sub = ap.add_subparsers(dest="cmd", required=True)
     s = sub.add_parser("serve")
     s.add_argument("--model-path")

@@ -22,12 +22,16 @@ PAGE = 64
 
 
 def prefill_tile_rows(head_dim: int, group: int, paged: bool = True, window: int = 0) -> int:
-    """Packed query rows per tile of the prefill kernel that serves this shape: 128 for the
-    tcgen05 kernel (paged K/V, head_dim 128, no sliding window, G | 128), else 64 for the
-    mma.sync kernel.  OMNI_FA_SM100=0 keeps the 64-row kernel everywhere."""
+    """Packed query rows per tile of the prefill kernel that serves this shape: 256 (or 128 with
+    OMNI_FA_TILE_ROWS=128) for the tcgen05 kernels (paged K/V, head_dim 128, no sliding
+    window, G | 128), else 64 for the mma.sync kernel.  OMNI_FA_SM100=0 keeps the 64-row
+    kernel everywhere."""
     if os.environ.get("OMNI_FA_SM100", "1") == "0":
         return 64
-    return 128 if paged and head_dim == 128 and window == 0 and 128 % max(1, group) == 0 else 64
+    if not (paged and head_dim == 128 and window == 0 and 128 % max(1, group) == 0):
+        return 64
+    # 256: two 128-row tiles per CTA whose softmax and tensor-core work overlap; 128: one tile
+    return int(os.environ.get("OMNI_FA_TILE_ROWS", "256"))
 
 
 def prefill_tiles(q_lens: list[int], group: int, rows: int = 64) -> tuple[list[int], list[int]]:

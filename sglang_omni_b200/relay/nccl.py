@@ -45,7 +45,9 @@ class NcclRelay(Relay):
         if dst is not None:
             with torch.cuda.stream(self._stream):
                 work = dist.isend(buf, dst, group=self.group)
+                work.wait()            # the side stream (not the host) waits for the send
             ev.record(self._stream)
+            # the buffer stays referenced until the request is cleaned up
             self._inflight.setdefault(request_id, []).append((buf, work))
         return RelayOperation({"relay": "nccl", "src": self.rank, "nbytes": int(buf.numel())},
                               result=(buf, ev))
@@ -57,18 +59,20 @@ class NcclRelay(Relay):
                                                                                        device=self.device)
         with torch.cuda.stream(self._stream):
             work = dist.irecv(out, int(metadata["src"]), group=self.group)
+            work.wait()                # the side stream waits for the receive; the event marks its end
         ev = torch.cuda.Event()
         ev.record(self._stream)
+        consumer = torch.cuda.current_stream(self.device)
 
         async def _wait():
+            # bounded host poll of the event (30 s), then the consumer's stream is ordered after it
             for _ in range(300000):
                 if ev.query():
-                    torch.cuda.current_stream(self.device).wait_stream(self._stream)
+                    consumer.wait_event(ev)
                     return out
                 await asyncio.sleep(0.0001)
             raise TimeoutError("nccl relay receive timed out")
 
-        work.wait()
         return RelayOperation(metadata, future=asyncio.ensure_future(_wait()))
 
     def cleanup(self, request_id):

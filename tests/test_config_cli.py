@@ -60,3 +60,20 @@ def test_cli_config_view(tmp_path):
                          capture_output=True, text=True, timeout=120)
     assert out.returncode == 0, out.stderr
     assert "decoder" in out.stdout
+
+
+def test_console_script_declared():
+    """``sgl-omni`` (the reference's command name) is a console script of the package."""
+    import os
+    import re
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    src = open(os.path.join(root, "setup.py")).read()
+    assert re.search(r'"sgl-omni=sglang_omni_b200\.cli\.cli:main"', src)
+    from sglang_omni_b200.cli.cli import main
+
+    import pytest
+
+    with pytest.raises(SystemExit) as e:
+        main(["--help"])
+    assert e.value.code == 0
