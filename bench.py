@@ -48,6 +48,8 @@ def parse():
     ap.add_argument("--s2pro", type=int, default=1, help="also measure the S2-Pro streaming TTS phase")
     ap.add_argument("--s2pro-streams", type=int, default=64)
     ap.add_argument("--s2pro-audio-s", type=float, default=15.0)
+    ap.add_argument("--s2pro-c1", type=int, default=1,
+                    help="also run the S2-Pro phase with one stream (the concurrency of the published numbers)")
     ap.add_argument("--thinker", type=int, default=1, help="run the thinker serving phase (headline value)")
     ap.add_argument("--vision", type=int, default=1, help="also measure image+text -> text serving")
     ap.add_argument("--vision-requests", type=int, default=64)
@@ -448,7 +450,18 @@ def main():
             tt = torch.tensor([ttfa_ms or 0.0], dtype=torch.float64, device=dev)
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             ttfa_ms = float(tt[0])
-    s2 = None
+    s2 = s2c1 = None
+    if args.s2pro and args.s2pro_c1 and args.layers == 48:
+        import copy
+
+        a1 = copy.copy(args)
+        a1.s2pro_streams = 1
+        t1, r1, c1 = s2pro_phase(a1, dev, rank)
+        s2c1 = {"streams": 1, "ttfa_ms": None if t1 is None else round(t1, 2),
+                "rtf": None if r1 is None else round(r1, 4),
+                "decode_tok_s": None if c1 is None else round(c1 * 44100 / 2048, 2),
+                "timing": "host wall clock through Client.generate, one stream (rank 0's GPU)",
+                "published_reference_h200": {"rtf": 0.34, "decode_tok_s": 63.3, "ttfa_ms": 140}}
     if args.s2pro and args.layers == 48:
         a, b, c = s2pro_phase(args, dev, rank)
         t = torch.tensor([a or 0.0, b or 0.0, c or 0.0], dtype=torch.float64, device=dev)
@@ -519,6 +532,7 @@ def main():
             "ttfa_p50_ms": None if ttfa_ms is None else round(ttfa_ms, 2),
             "vision_image_text": vis,
             "s2pro_tts": s2,
+            "s2pro_tts_single_stream": s2c1,
             "e2e": {"value": round(e2e, 2), "unit": "output tokens/s, host wall clock through AREngine.generate",
                     "h2d_bytes_per_step": int(args.requests * args.prompt_len * 4),
                     "d2h_bytes_per_step": int(args.requests * args.output_len * 4)},

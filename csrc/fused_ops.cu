@@ -184,6 +184,120 @@ __global__ void __launch_bounds__(256) qkv_rope_store_kernel(RopeStoreArgs a) {
   }
 }
 
+// head_dim 128 fast path: one warp = one token x up to kHeadsPerWarp consecutive heads.  Lane l
+// owns elements 4l .. 4l+3 (8-byte loads and stores, a head row is one coalesced 256-byte
+// access).  The token's cos / sin entries (one per rotated element of the lane, M-RoPE section
+// by element) are loaded once and serve every q / k head of the warp; the neox partner element
+// e +- rot/2 sits in the same register of lane l +- rot/8 (a shuffle), the interleaved partner
+// e ^ 1 in the lane's own registers.  Every head's row load of the warp is issued before the
+// first use.
+constexpr int kRopeHeadsPerWarp = 4;
+
+__device__ __forceinline__ void load4_bf16(const __nv_bfloat16* p, float (&v)[4]) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+}
+
+__device__ __forceinline__ void store4_bf16(__nv_bfloat16* p, const float (&v)[4]) {
+  const __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]);
+  const __nv_bfloat162 b = __floats2bfloat162_rn(v[2], v[3]);
+  uint2 u;
+  u.x = *reinterpret_cast<const uint32_t*>(&a);
+  u.y = *reinterpret_cast<const uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(p) = u;
+}
+
+__global__ void __launch_bounds__(256) qkv_rope_store_d128_kernel(RopeStoreArgs a) {
+  grid_dep_launch();  // a dependent GEMM may start its prologue now
+  constexpr int D = 128;
+  const int heads = a.hq + 2 * a.hkv;
+  const int chunks = (heads + kRopeHeadsPerWarp - 1) / kRopeHeadsPerWarp;
+  const long wg = static_cast<long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int tok = static_cast<int>(wg / chunks);
+  if (tok >= a.tokens) return;
+  const int h0 = static_cast<int>(wg - static_cast<long>(tok) * chunks) * kRopeHeadsPerWarp;
+  const int e0 = 4 * lane;
+  __nv_bfloat16* base = static_cast<__nv_bfloat16*>(a.qkv) + static_cast<int64_t>(tok) * a.qkv_stride;
+  // every row of the warp in flight first
+  float x[kRopeHeadsPerWarp][4];
+#pragma unroll
+  for (int u = 0; u < kRopeHeadsPerWarp; ++u) {
+    const int head = h0 + u;
+    if (head < heads) load4_bf16(base + head * D + e0, x[u]);
+  }
+  const bool any_qk = h0 < a.hq + a.hkv;
+  float wq[4] = {1.f, 1.f, 1.f, 1.f}, wk[4] = {1.f, 1.f, 1.f, 1.f};
+  if (any_qk && a.q_norm != nullptr) load4_bf16(static_cast<const __nv_bfloat16*>(a.q_norm) + e0, wq);
+  if (any_qk && a.k_norm != nullptr) load4_bf16(static_cast<const __nv_bfloat16*>(a.k_norm) + e0, wk);
+  // this lane's cos / sin, shared by the warp's q / k heads
+  const int rot = a.rot_dim, half = rot >> 1;
+  float cs[4] = {1.f, 1.f, 1.f, 1.f}, sn[4] = {0.f, 0.f, 0.f, 0.f};
+  if (any_qk && rot > 0) {
+    const int p0 = a.positions[tok];
+    const int p1 = a.pos_rows == 3 ? a.positions[a.tokens + tok] : p0;
+    const int p2 = a.pos_rows == 3 ? a.positions[2 * a.tokens + tok] : p0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int e = e0 + k;
+      if (e < rot) {
+        const int j = a.neox ? (e < half ? e : e - half) : (e >> 1);
+        const int sec = a.pos_rows == 3 ? mrope_section(j, a.section, a.interleaved) : 0;
+        const int pos = sec == 0 ? p0 : (sec == 1 ? p1 : p2);
+        const int64_t idx = static_cast<int64_t>(pos) * half + j;
+        const float sgn = a.neox ? (e < half ? -1.f : 1.f) : ((e & 1) ? 1.f : -1.f);
+        cs[k] = a.cos_tab[idx];
+        sn[k] = sgn * a.sin_tab[idx];
+      }
+    }
+  }
+  const int shift = half >> 2;                       // neox partner lane distance
+  const int src_lane = e0 < half ? lane + shift : lane - shift;
+  int slot = -1;
+  if (a.slot_mapping != nullptr && h0 + kRopeHeadsPerWarp > a.hq) {
+    slot = a.slot_mapping[tok];
+    if (a.num_slots != 0 && slot >= a.num_slots) slot = -1;
+  }
+#pragma unroll
+  for (int u = 0; u < kRopeHeadsPerWarp; ++u) {
+    const int head = h0 + u;
+    if (head >= heads) break;                         // warp-uniform
+    const bool is_q = head < a.hq;
+    const bool is_v = head >= a.hq + a.hkv;
+    float (&v)[4] = x[u];
+    if (!is_v) {
+      if (is_q ? a.q_norm != nullptr : a.k_norm != nullptr) {
+        float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+        ss = warp_sum(ss);
+        const float rstd = rsqrtf(ss / D + a.eps);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v[k] = bf16r(bf16r(v[k] * rstd) * (is_q ? wq[k] : wk[k]));
+      }
+      if (rot > 0) {
+        float pv[4];
+        if (a.neox) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) pv[k] = __shfl_sync(0xffffffffu, v[k], src_lane);
+        } else {
+          pv[0] = v[1]; pv[1] = v[0]; pv[2] = v[3]; pv[3] = v[2];
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (e0 + k < rot) v[k] = v[k] * cs[k] + pv[k] * sn[k];
+      }
+      store4_bf16(base + head * D + e0, v);
+    }
+    if (!is_q && slot >= 0) {
+      const int h = is_v ? head - a.hq - a.hkv : head - a.hq;
+      const int page = slot >> 6, off = slot & 63;
+      __nv_bfloat16* cache = static_cast<__nv_bfloat16*>(is_v ? a.v_cache : a.k_cache);
+      store4_bf16(cache + ((static_cast<int64_t>(page) * a.hkv + h) * 64 + off) * D + e0, v);
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // MoE routing
 // ---------------------------------------------------------------------------
@@ -917,8 +1031,17 @@ __global__ void __launch_bounds__(1024) sample_kernel(SampleArgs a) {
 
 cudaError_t qkv_rope_store(const RopeStoreArgs& a, cudaStream_t stream) {
   if (a.tokens == 0) return cudaSuccess;
-  const long warps = static_cast<long>(a.tokens) * (a.hq + 2 * a.hkv);
   const int threads = 256;
+  const bool vec_ok = (a.qkv_stride % 4) == 0 && (reinterpret_cast<uintptr_t>(a.qkv) & 7) == 0 &&
+                      (a.k_cache == nullptr || (reinterpret_cast<uintptr_t>(a.k_cache) & 7) == 0) &&
+                      (a.v_cache == nullptr || (reinterpret_cast<uintptr_t>(a.v_cache) & 7) == 0);
+  if (a.head_dim == 128 && a.rot_dim % 8 == 0 && a.rot_dim <= 128 && vec_ok) {
+    const int chunks = (a.hq + 2 * a.hkv + kRopeHeadsPerWarp - 1) / kRopeHeadsPerWarp;
+    const long warps = static_cast<long>(a.tokens) * chunks;
+    qkv_rope_store_d128_kernel<<<(warps + 7) / 8, threads, 0, stream>>>(a);
+    return cudaGetLastError();
+  }
+  const long warps = static_cast<long>(a.tokens) * (a.hq + 2 * a.hkv);
   const long grid = (warps + 7) / 8;
   switch (a.head_dim) {
     case 32: qkv_rope_store_kernel<32><<<grid, threads, 0, stream>>>(a); break;

@@ -57,22 +57,12 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def physical_gpu(logical: int) -> str:
-    """Physical index of logical GPU `logical` of the pipeline (before a stage process
-    narrowed CUDA_VISIBLE_DEVICES to its own GPU)."""
-    visible = os.environ.get("OMNI_VISIBLE_DEVICES_ORIG", os.environ.get("CUDA_VISIBLE_DEVICES"))
-    if visible:
-        ids = [v.strip() for v in visible.split(",") if v.strip()]
-        return ids[logical]
-    return str(logical)
-
-
 @dataclass
 class GroupSpec:
     """Everything a follower needs to rebuild its rank (picklable)."""
     mode: str
     world: int
-    gpus: list = field(default_factory=list)   # logical GPU per rank; empty = CPU
+    gpus: list = field(default_factory=list)   # GPU index per rank (in the pipeline's visible set); empty = CPU
     builder: str = ""                           # "module.fn": fn(args, rank, world, device, group) -> model
     builder_args: dict = field(default_factory=dict)
     engine_args: dict = field(default_factory=dict)
@@ -84,7 +74,7 @@ class GroupSpec:
     report_timeout_s: float = 120.0
 
     def device_of(self, rank: int) -> torch.device:
-        return torch.device("cuda", 0) if self.gpus else torch.device("cpu")
+        return torch.device("cuda", int(self.gpus[rank])) if self.gpus else torch.device("cpu")
 
     @property
     def sharded(self) -> bool:
@@ -140,8 +130,14 @@ def _step(eng: AREngine, model, spec: GroupSpec) -> list:
 def _follower_main(spec: GroupSpec, rank: int):  # pragma: no cover - runs in a spawned process
     import zmq
 
-    if spec.gpus:
-        os.environ["CUDA_VISIBLE_DEVICES"] = physical_gpu(spec.gpus[rank])
+    if spec.gpus and os.environ.get("OMNI_VISIBLE_DEVICES_ORIG") is not None:
+        # a stage process narrowed the mask to its own GPU: every GPU of the group must be visible
+        # (CUDA IPC maps the peers' buffers), so restore the pipeline's mask
+        orig = os.environ["OMNI_VISIBLE_DEVICES_ORIG"]
+        if orig:
+            os.environ["CUDA_VISIBLE_DEVICES"] = orig
+        else:
+            os.environ.pop("CUDA_VISIBLE_DEVICES", None)
     device = spec.device_of(rank)
     if device.type == "cuda":
         torch.cuda.set_device(device)

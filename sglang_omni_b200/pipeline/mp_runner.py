@@ -45,28 +45,31 @@ def _stage_process_entry(cfg_dict: dict, cfg_cls_path: str | None, stage_index: 
         stages_cfg, name_map, _ = cfg.apply_fusion()
         s = stages_cfg[stage_index]
         gpu = cfg.gpu_placement.get(s.name)
-        if gpu is not None:
+        group_stage = any(int(s.executor.args.get(k, 1) or 1) > 1 for k in ("tp_size", "ep_size"))
+        if gpu is not None and not group_stage:
             visible = os.environ.get("CUDA_VISIBLE_DEVICES")
             phys = visible.split(",")[gpu] if visible else str(gpu)
-            # a stage's rank group (tp_size / ep_size > 1) maps its GPU list through the original mask
             os.environ.setdefault("OMNI_VISIBLE_DEVICES_ORIG", visible or "")
             os.environ["CUDA_VISIBLE_DEVICES"] = phys
+        # a stage served by a rank group (tp_size / ep_size > 1) keeps every GPU visible: its ranks
+        # map each other's buffers through CUDA IPC; it runs on GPU `gpu` of the pipeline's set
         import torch  # noqa: F401  (after the device mask)
 
+        local_gpu = (gpu if group_stage else 0) if gpu is not None else None
         relay_ranks = None
         if dist_env is not None:
             os.environ.update({k: str(v) for k, v in dist_env.items()})
             import torch.distributed as dist
             from datetime import timedelta
 
-            torch.cuda.set_device(0)
+            torch.cuda.set_device(local_gpu or 0)
             dist.init_process_group("nccl", rank=stage_index, world_size=len(stages_cfg),
                                     timeout=timedelta(seconds=120))
             relay_ranks = {st.name: i for i, st in enumerate(stages_cfg)}
         endpoints = allocate_endpoints(cfg, [st.name for st in stages_cfg], run_id)
         receivers = {name_map.get(t.to_stage, t.to_stage) for st in stages_cfg for t in st.stream_to}
         stage = build_stage(cfg, s, endpoints, name_map, receivers, stage_index, multiprocess=True,
-                            gpu_id=0 if gpu is not None else None, relay_ranks=relay_ranks)
+                            gpu_id=local_gpu, relay_ranks=relay_ranks)
 
         async def main():
             await stage.start()
