@@ -206,13 +206,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive_expect_tx(q_full, kTileBytes);
       for (int r = 0; r < 2; ++r)
         tma_load_3d(sQ + r * kRegion, &tmap_q, q_full, r * 64, h * p.G, q_begin + tok0);
-      bool ok = true;
-      for (int j = 0; j < nb && ok; ++j) {
+      int issued = 0;   // blocks whose loads were issued
+      for (int j = 0; j < nb; ++j) {
         const int s = j & 1;
-        if (j >= kKvStages && !mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, p.status)) {
-          ok = false;
-          break;
-        }
+        if (j >= kKvStages && !mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, p.status)) break;
+        issued = j + 1;
         mbar_arrive_expect_tx(&kv_full[s], 2 * kTileBytes);
         const int pages = (kv_len + 63) / 64;
         for (int pg = 0; pg < 2; ++pg) {
@@ -226,9 +224,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      // drain: the last loads of each stage landed before TMEM / smem go away
+      // drain: every issued load has landed before the CTA's shared memory goes away (also
+      // after an aborted wait, so no late copy writes into the next CTA on this SM)
       mbar_wait(q_full, 0, nullptr, p.status);
-      for (int j = max(0, nb - kKvStages); j < nb && ok; ++j) mbar_wait(&kv_full[j & 1], (j >> 1) & 1, nullptr, p.status);
+      for (int j = max(0, issued - kKvStages); j < issued; ++j)
+        mbar_wait(&kv_full[j & 1], (j >> 1) & 1, nullptr, p.status);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -483,13 +483,11 @@ __global__ void __launch_bounds__(pp::kThreads, 1)
           tma_load_3d(smem + kQ + t * kQBytes + r * (kQBytes / 2), &tmap_q, q_full, r * 64, h * p.G,
                       q_begin + tok0 + t * tpt);
       const int pages = (kv_len + 63) / 64;
-      bool ok = true;
-      for (int j = 0; j < nb && ok; ++j) {
+      int issued = 0;   // blocks whose loads were issued
+      for (int j = 0; j < nb; ++j) {
         const int s = j % kStages;
-        if (j >= kStages && !mbar_wait(&kv_empty[s], ((j / kStages) & 1) ^ 1, abort_flag, p.status)) {
-          ok = false;
-          break;
-        }
+        if (j >= kStages && !mbar_wait(&kv_empty[s], ((j / kStages) & 1) ^ 1, abort_flag, p.status)) break;
+        issued = j + 1;
         mbar_arrive_expect_tx(&kv_full[s], 2 * kKVBytes);
         const int page = j < pages ? fa_page(p, req, j) : 0;
         const int row = (page * p.hkv + h) * 64;
@@ -499,7 +497,7 @@ __global__ void __launch_bounds__(pp::kThreads, 1)
         }
       }
       mbar_wait(q_full, 0, nullptr, p.status);
-      for (int j = max(0, nb - kStages); j < nb && ok; ++j)
+      for (int j = max(0, issued - kStages); j < issued; ++j)
         mbar_wait(&kv_full[j % kStages], (j / kStages) & 1, nullptr, p.status);
     }
   } else if (warp == 1) {

@@ -642,7 +642,8 @@ omni::TpReduceArgs tp_args(const torch::Tensor& ptrs, int64_t rank, int64_t worl
 void tp_reduce_norm(const torch::Tensor& ptrs, int64_t rank, int64_t world, int64_t tokens, int64_t rows_per,
                     int64_t max_tokens, torch::Tensor& residual, const torch::Tensor& norm_w, double eps,
                     bool gather_residual, torch::Tensor& seq, torch::Tensor& counter,
-                    const c10::optional<torch::Tensor>& status, double timeout_s) {
+                    const c10::optional<torch::Tensor>& status, double timeout_s, bool single_src,
+                    bool gather_local) {
   OMNI_CHECK_CUDA(residual);
   OMNI_CHECK_BF16(residual);
   OMNI_CHECK_CONTIG(residual);
@@ -655,6 +656,9 @@ void tp_reduce_norm(const torch::Tensor& ptrs, int64_t rank, int64_t world, int6
   a.residual = residual.data_ptr();
   a.norm_w = norm_w.data_ptr();
   a.eps = static_cast<float>(eps);
+  a.single_src = single_src ? 1 : 0;
+  a.gather_local = gather_local ? 1 : 0;
+  TORCH_CHECK(!(gather_local && gather_residual), "gather_local with gather_residual");
   check_launch(omni::tp_reduce_norm(a, at::cuda::getCurrentCUDAStream()), "tp_reduce_norm");
 }
 
@@ -699,6 +703,65 @@ void sample(torch::Tensor& logits, torch::Tensor& out_tokens, const c10::optiona
   a.row_slot = opt_ptr<int>(row_slot);
   a.slot_tokens = opt_mut<int>(slot_tokens);
   check_launch(omni::sample(a, at::cuda::getCurrentCUDAStream()), "sample");
+}
+
+void vocab_sample(torch::Tensor& logits, torch::Tensor& out_tokens, const torch::Tensor& peer_xchg,
+                  const torch::Tensor& peer_flags, int64_t rank, int64_t world, int64_t cand, int64_t max_rows,
+                  int64_t vocab0, int64_t vocab_local, int64_t vocab, torch::Tensor& seq, torch::Tensor& counter,
+                  const c10::optional<torch::Tensor>& inexact, const c10::optional<torch::Tensor>& status,
+                  double timeout_s, const c10::optional<torch::Tensor>& temperature,
+                  const c10::optional<torch::Tensor>& top_k, const c10::optional<torch::Tensor>& top_p,
+                  const c10::optional<torch::Tensor>& min_p, const c10::optional<torch::Tensor>& rep_penalty,
+                  const c10::optional<torch::Tensor>& seen, int64_t suppress_lo, int64_t suppress_hi,
+                  int64_t suppress_keep, const c10::optional<torch::Tensor>& seeds,
+                  const c10::optional<torch::Tensor>& step, const c10::optional<torch::Tensor>& row_slot,
+                  const c10::optional<torch::Tensor>& slot_tokens, int64_t phases) {
+  OMNI_CHECK_CUDA(logits);
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.stride(-1) == 1, "logits fp32 with unit column stride");
+  TORCH_CHECK(logits.size(1) >= vocab_local, "logits narrower than the vocabulary slice");
+  TORCH_CHECK(peer_xchg.scalar_type() == at::kLong && peer_xchg.numel() == world, "peer_xchg: int64 [world]");
+  TORCH_CHECK(peer_flags.scalar_type() == at::kLong && peer_flags.numel() == world, "peer_flags: int64 [world]");
+  TORCH_CHECK(seq.scalar_type() == at::kInt && counter.scalar_type() == at::kInt, "seq / counter int32");
+  const at::cuda::CUDAGuard guard(logits.device());
+  omni::VocabSampleArgs a{};
+  a.logits = logits.data_ptr<float>();
+  a.logits_stride = logits.stride(0);
+  a.rows = static_cast<int>(logits.size(0));
+  a.vocab_local = static_cast<int>(vocab_local);
+  a.vocab0 = static_cast<int>(vocab0);
+  a.vocab = static_cast<int>(vocab);
+  a.rank = static_cast<int>(rank);
+  a.world = static_cast<int>(world);
+  a.cand = static_cast<int>(cand);
+  a.max_rows = static_cast<int>(max_rows);
+  a.peer_xchg = peer_xchg.data_ptr<int64_t>();
+  a.peer_flags = peer_flags.data_ptr<int64_t>();
+  a.seq = seq.data_ptr<int>();
+  a.counter = counter.data_ptr<int>();
+  a.inexact = opt_mut<int>(inexact);
+  a.status = status_ptr(status);
+  a.timeout_ns = static_cast<int64_t>(timeout_s * 1e9);
+  a.temperature = opt_ptr<float>(temperature);
+  a.top_k = opt_ptr<int>(top_k);
+  a.top_p = opt_ptr<float>(top_p);
+  a.min_p = opt_ptr<float>(min_p);
+  a.rep_penalty = opt_ptr<float>(rep_penalty);
+  if (seen.has_value()) {
+    TORCH_CHECK(seen->scalar_type() == at::kByte && seen->size(1) >= vocab, "seen: uint8 [slots, >= vocab]");
+    a.seen = seen->data_ptr<uint8_t>();
+    a.seen_stride = seen->stride(0);
+  }
+  a.suppress_lo = static_cast<int>(suppress_lo);
+  a.suppress_hi = static_cast<int>(suppress_hi);
+  a.suppress_keep = static_cast<int>(suppress_keep);
+  a.seeds = seeds.has_value() ? seeds->data_ptr<int64_t>() : nullptr;
+  a.step = opt_mut<int>(step);
+  a.out_tokens = out_tokens.data_ptr<int>();
+  a.row_slot = opt_ptr<int>(row_slot);
+  a.slot_tokens = opt_mut<int>(slot_tokens);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  if (phases & 1) check_launch(omni::vocab_sample_local(a, stream), "vocab_sample_local");
+  if (phases & 2) check_launch(omni::vocab_sample_merge(a, stream), "vocab_sample_merge");
 }
 
 void snake(const torch::Tensor& x, const torch::Tensor& alpha, const c10::optional<torch::Tensor>& beta,
@@ -815,13 +878,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_close", &ipc_close, "unmaps a peer buffer");
   m.def("tensor_at", &tensor_at, "non-owning CUDA tensor over a device address");
   m.def("tp_reduce_norm", &tp_reduce_norm, "tensor-parallel reduce-scatter + residual + RMSNorm + all-gather "
-        "over peer memory");
+        "over peer memory", py::arg("ptrs"), py::arg("rank"), py::arg("world"), py::arg("tokens"), py::arg("rows_per"),
+        py::arg("max_tokens"), py::arg("residual"), py::arg("norm_w"), py::arg("eps"), py::arg("gather_residual"),
+        py::arg("seq"), py::arg("counter"), py::arg("status"), py::arg("timeout_s"), py::arg("single_src") = false,
+        py::arg("gather_local") = false);
   m.def("tp_wait", &tp_wait, "tensor-parallel: wait until every rank's gathered rows have landed");
   m.def("ep_dispatch", &ep_dispatch, "expert-parallel: every routed row into its expert owner's receive segment "
                                       "(system-atomic reservations), then the dispatch flags");
   m.def("gemm_ep", &gemm_ep, "expert-parallel grouped GEMM over receive segments (flag wait / combine epilogue / "
                              "completion flags)");
   m.def("sample", &sample, "fused logits processing + sampling");
+  m.def("vocab_sample", &vocab_sample, "vocab-parallel sampling: per-rank candidate records over peer memory "
+                                       "(phase 1) and the merged draw (phase 2)");
   m.def("snake", &snake, "Snake / SnakeBeta activation (channels-last)");
   m.def("conv1d_im2col", &conv1d_im2col, "causal dilated conv1d im2col rows");
   m.def("conv_transpose_ola", &conv_transpose_ola, "transposed-conv overlap-add + bias + causal trim");

@@ -289,6 +289,46 @@ struct SampleArgs {
 };
 cudaError_t sample(const SampleArgs& a, cudaStream_t stream);
 
+// ---------------------------------------------------------------- vocab-parallel sampling
+// The LM head split over the vocabulary: rank r holds logits columns
+// [vocab0, vocab0 + vocab_local) of the full vocabulary.  ``vocab_sample_local``
+// processes this rank's slice (same rules as ``sample``) and publishes one record
+// per row into every rank's exchange region: its max, sum of exp, the greedy /
+// Gumbel-max winner of the slice and its top-``cand`` (value, token) pairs.
+// ``vocab_sample_merge`` waits (bounded) for every rank's records and draws the
+// token from them; every rank draws the same token.
+constexpr int kVpMaxCand = 256;
+constexpr int kVpMaxWorld = 8;
+constexpr int kVpHeaderBytes = 32;
+struct VocabSampleArgs {
+  float* logits;              // [rows, logits_stride] fp32 slice of this rank (processed in place)
+  int64_t logits_stride;
+  int rows, vocab_local, vocab0, vocab;
+  int rank, world, cand, max_rows;
+  const int64_t* peer_xchg;   // [world] base of every rank's exchange region
+  const int64_t* peer_flags;  // [world] base of every rank's u32 flags[world]
+  int* seq;                   // device sequence number of the exchange
+  int* counter;               // CTA arrival counter of the local phase
+  int* status;
+  int64_t timeout_ns;
+  int* inexact;               // rows drawn from an incomplete candidate set (counter)
+  const float* temperature;
+  const int* top_k;
+  const float* top_p;
+  const float* min_p;
+  const float* rep_penalty;
+  uint8_t* seen;              // full-vocabulary seen mask [slots, seen_stride]
+  int64_t seen_stride;
+  int suppress_lo, suppress_hi, suppress_keep;  // full-vocabulary ids
+  const int64_t* seeds;
+  int* step;
+  int* out_tokens;
+  const int* row_slot;
+  int* slot_tokens;
+};
+cudaError_t vocab_sample_local(const VocabSampleArgs& a, cudaStream_t stream);
+cudaError_t vocab_sample_merge(const VocabSampleArgs& a, cudaStream_t stream);
+
 // ---------------------------------------------------------------- audio / vocoder ops (channels-last)
 cudaError_t snake(const void* x, const float* alpha, const float* beta, void* y, int64_t n, int C, int log_scale,
                   cudaStream_t stream);
@@ -337,6 +377,8 @@ struct TpReduceArgs {
   int* counter;            // local CTA arrival counter, zero between calls
   int* status;
   long long timeout_ns;
+  int single_src;          // 1: the owned rows are already reduced in part[rank] (sum that slot only)
+  int gather_local;        // 1: store the normalised rows into this rank's gath only (no all-gather)
 };
 cudaError_t tp_reduce_norm(const TpReduceArgs& a, cudaStream_t stream);
 cudaError_t tp_wait(const TpReduceArgs& a, cudaStream_t stream);

@@ -23,6 +23,10 @@
 //      rank's gath / gres;
 //   5. the last CTA to finish release-stores phase B = seq + 1 into every peer
 //      and advances seq.
+// Two variants serve attention TP combined with expert-parallel MoE: ``gather_local``
+// keeps the normalised owned rows on this rank (they feed the EP dispatch, which
+// moves each token once), and ``single_src`` takes the owned rows already reduced
+// in part[rank] (the EP combine's output) instead of summing world partials.
 // The consumer (the next GEMM, see GemmArgs::wait_flags, or tp_wait) waits for
 // phase B == seq from every rank before it reads gath.  seq lives on the
 // device, so the whole sequence is captured in a CUDA graph and replayed.
@@ -119,7 +123,8 @@ __global__ void __launch_bounds__(256) tp_reduce_norm_kernel(TpReduceArgs a) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[j] = 0.f;
       const uint4* part = reinterpret_cast<const uint4*>(a.peer_part[a.rank]);
-      for (int s = 0; s < a.world; ++s) {
+      const int s0 = a.single_src ? a.rank : 0, s1 = a.single_src ? a.rank + 1 : a.world;
+      for (int s = s0; s < s1; ++s) {
         float f[8];
         unpack8(__ldcg(part + (static_cast<int64_t>(s) * a.max_tokens + row) * nvec + v), f);
 #pragma unroll
@@ -161,7 +166,8 @@ __global__ void __launch_bounds__(256) tp_reduce_norm_kernel(TpReduceArgs a) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) o[j] = __bfloat162float(__float2bfloat16(vals[i][j] * rstd)) * wf[j];
       const uint4 ov = pack8(o);
-      for (int d = 0; d < a.world; ++d)
+      const int d0 = a.gather_local ? a.rank : 0, d1 = a.gather_local ? a.rank + 1 : a.world;
+      for (int d = d0; d < d1; ++d)
         reinterpret_cast<uint4*>(a.peer_gath[d])[static_cast<int64_t>(row) * nvec + v] = ov;
     }
   }

@@ -234,9 +234,8 @@ class ARModelRunner:
             captured["_cu"] = cu
         if not logits_rows:
             return None
-        logits = self.model.logits(hidden)
         row_slot = h2d([r.slot for r in sample_reqs], dev, torch.int32)
-        toks = sample(logits, self.st, self.suppress, row_slot=row_slot, slot_tokens=self.slot_tokens)
+        toks = self._sample(hidden, row_slot)
         n = len(sample_reqs)
         host = self._next_tok_host()[:n]
         host.copy_(toks, non_blocking=True)
@@ -269,9 +268,16 @@ class ARModelRunner:
         fb = ForwardBatch(is_decode=True, positions=positions, slot_mapping=slot_mapping, kv_lens=kv_lens,
                           block_table=bt, input_ids=ids, capture_layers=self._capture_layers)
         hidden = self.model(fb, self.pool.kv)
-        logits = self.model.logits(hidden)
-        toks = sample(logits, self.st, self.suppress, row_slot=slots, slot_tokens=self.slot_tokens)
+        toks = self._sample(hidden, slots)
         return toks, hidden, fb.captured
+
+    def _sample(self, hidden: torch.Tensor, row_slot: torch.Tensor) -> torch.Tensor:
+        """LM head + sampling (the model's vocab-parallel path under TP)."""
+        fn = getattr(self.model, "sample_tokens", None)
+        if fn is not None:
+            return fn(hidden, self.st, self.suppress, row_slot=row_slot, slot_tokens=self.slot_tokens)
+        return sample(self.model.logits(hidden), self.st, self.suppress, row_slot=row_slot,
+                      slot_tokens=self.slot_tokens)
 
     _capture_layers: tuple = ()
 

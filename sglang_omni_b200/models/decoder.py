@@ -119,7 +119,8 @@ class ForwardBatch:
 class DecoderLM(nn.Module):
     """Weights as plain parameters in fused layouts; forward is op-by-op on the kernels."""
 
-    def __init__(self, cfg: DecoderConfig, device="cpu", ep=None, tp=None):
+    def __init__(self, cfg: DecoderConfig, device="cpu", ep=None, tp=None, vocab_parallel: bool = True,
+                 vocab_cand: int = 64):
         """``ep``: an ``parallel.EPMoE`` exchange; this rank then holds experts
         [ep.rank * El, (ep.rank + 1) * El) and the MoE layers run expert-parallel.
 
@@ -127,9 +128,16 @@ class DecoderLM(nn.Module):
         (``self.cfg`` describes the local attention: local head counts), the
         matching o_proj columns, experts [rank * E / world, ...) and slices of the
         shared-expert / dense MLP intermediate; every rank runs every token and the
-        reduce points are the fused peer-memory kernels of ``parallel.tp``."""
+        reduce points are the fused peer-memory kernels of ``parallel.tp``.
+
+        Both: attention and dense MLPs are tensor-parallel over ``tp`` and the MoE layers
+        expert-parallel over ``ep`` (experts [ep.rank * El, ...), shared experts whole).
+        After the o_proj reduce point each TP rank keeps the normalised rows it owns and
+        dispatches only those, so every token crosses the EP exchange once; the EP
+        combine writes the owned rows' expert output into the TP partial slot and the
+        next reduce point adds the residual, normalises and all-gathers them.  With
+        ep.world > tp.world the TP groups are data-parallel replicas of the attention."""
         super().__init__()
-        assert ep is None or tp is None, "expert parallel and tensor parallel are separate layouts"
         self.full_cfg = cfg
         self.tp = tp
         self._tp_split = None
@@ -138,12 +146,14 @@ class DecoderLM(nn.Module):
 
             qh, kvh = head_split(cfg.num_heads, cfg.num_kv_heads, tp.rank, tp.world)
             self._tp_split = (qh, kvh)
-            assert cfg.num_experts % tp.world == 0 or not cfg.num_experts
-            for w in (cfg.intermediate_size, cfg.shared_expert_intermediate_size):
+            assert ep is not None or cfg.num_experts % tp.world == 0 or not cfg.num_experts
+            shared_w = cfg.shared_expert_intermediate_size
+            for w in (cfg.intermediate_size, 0 if ep is not None else shared_w):
                 assert w % tp.world == 0, "MLP widths must divide over the TP group"
             cfg = dataclasses.replace(cfg, num_heads=len(qh), num_kv_heads=len(kvh),
                                       intermediate_size=cfg.intermediate_size // tp.world,
-                                      shared_expert_intermediate_size=cfg.shared_expert_intermediate_size // tp.world)
+                                      shared_expert_intermediate_size=shared_w if ep is not None
+                                      else shared_w // tp.world)
         self.cfg = cfg
         self.ep = ep
         par = ep if ep is not None else tp
@@ -184,7 +194,17 @@ class DecoderLM(nn.Module):
                 L.mlp2 = P(H, cfg.intermediate_size)
             self.layers.append(L)
         self.final_norm = P(H)
-        self.lm_head = None if cfg.tie_word_embeddings else P(cfg.vocab_size, H)
+        # Under TP the LM head is split over the vocabulary (rows [vocab0, vocab0 + vocab_local)
+        # on this rank, zero-padded to a 16-multiple width) and tokens are drawn by the
+        # vocab-parallel sampler (parallel/vocab.py) without gathering the logits.
+        self.vocab_sampler = None
+        self._vslice = (0, cfg.vocab_size, cfg.vocab_size)
+        if tp is not None and vocab_parallel:
+            from ..parallel.vocab import vocab_slice
+
+            self._vslice = vocab_slice(cfg.vocab_size, tp.rank, tp.world)
+        head_rows = self._vslice[2] if tp is not None and vocab_parallel else cfg.vocab_size
+        self.lm_head = None if cfg.tie_word_embeddings else P(head_rows, H)
         rot = cfg.rotary_dim or cfg.head_dim
         cos, sin = ops.rope_tables(rot, cfg.rope_theta, cfg.max_position, device, round_bf16=cfg.dtype == torch.bfloat16)
         self.register_buffer("cos_tab", cos, persistent=False)
@@ -192,6 +212,11 @@ class DecoderLM(nn.Module):
         self._moe_ws: MoEWorkspace | None = None
         self._dec_ws: DecodeWorkspace | None = None
         self._retired_ws: list = []
+        if tp is not None and vocab_parallel and torch.device(device).type == "cuda":
+            from ..parallel.vocab import VocabParallelSampler
+
+            self.vocab_sampler = VocabParallelSampler(cfg.vocab_size, min(tp.max_tokens, 512), device,
+                                                      group=tp.group, cand=vocab_cand, timeout_s=tp.timeout_s)
 
     # ------------------------------------------------------------------ init
     @torch.no_grad()
@@ -221,13 +246,15 @@ class DecoderLM(nn.Module):
         return self
 
     # ------------------------------------------------------------------ tensor-parallel slices
-    _TP_KINDS = ("qkv", "o", "s13", "s2", "mlp13", "mlp2")
+    _TP_KINDS = ("qkv", "o", "s13", "s2", "mlp13", "mlp2", "lm_head")
 
     def full_shape(self, kind: str, p: torch.Tensor):
         """Unsharded shape of a tensor-parallel parameter (None if not sharded)."""
-        if self.tp is None or kind not in self._TP_KINDS:
+        if self.tp is None or kind not in self._TP_KINDS or (self.ep is not None and kind in ("s13", "s2")):
             return None
         f, H, D = self.full_cfg, self.full_cfg.hidden_size, self.full_cfg.head_dim
+        if kind == "lm_head":
+            return None if self._vslice[2] == f.vocab_size else (f.vocab_size, H)
         return {"qkv": (f.q_size + 2 * f.kv_size, H), "o": (H, f.q_size),
                 "s13": (2 * f.shared_expert_intermediate_size, H), "s2": (H, f.shared_expert_intermediate_size),
                 "mlp13": (2 * f.intermediate_size, H), "mlp2": (H, f.intermediate_size)}[kind]
@@ -235,11 +262,18 @@ class DecoderLM(nn.Module):
     def shard(self, kind: str, full: torch.Tensor) -> torch.Tensor:
         """This rank's slice of an unsharded tensor (identity without TP): QKV rows of
         the local heads, o_proj columns, gate/up rows and down columns of the MLPs."""
-        if self.tp is None or kind not in self._TP_KINDS:
+        if self.tp is None or kind not in self._TP_KINDS or (self.ep is not None and kind in ("s13", "s2")):
             return full
         f, D = self.full_cfg, self.full_cfg.head_dim
         qh, kvh = self._tp_split
         r, w = self.tp.rank, self.tp.world
+        if kind == "lm_head":
+            v0, vl, width = self._vslice
+            if width == full.shape[0]:
+                return full
+            out = full.new_zeros(width, full.shape[1])
+            out[:vl] = full[v0:v0 + vl]
+            return out
         if kind == "qkv":
             q = full[qh.start * D:qh.stop * D]
             k = full[f.q_size + kvh.start * D:f.q_size + kvh.stop * D]
@@ -256,7 +290,11 @@ class DecoderLM(nn.Module):
 
     @property
     def head_weight(self):
-        return self.embed if self.lm_head is None else self.lm_head
+        """LM-head rows of this rank (the vocabulary slice under vocab-parallel TP)."""
+        if self.lm_head is not None:
+            return self.lm_head
+        v0, vl, width = self._vslice
+        return self.embed if vl == self.cfg.vocab_size else self.embed[v0:v0 + vl]
 
     # ------------------------------------------------------------------ workspaces
     def ensure_workspaces(self, max_tokens: int, max_batch: int, max_context: int):
@@ -412,8 +450,12 @@ class DecoderLM(nn.Module):
         for i, L in enumerate(self.layers):
             attn = self._attention(L, i, normed, fb, kv_cache, wait)
             ops.linear(attn, L.o, out=tp.part_local[:T], scatter=scatter)
-            normed2 = tp.reduce_norm(res, L.ln2, eps, T)
-            self._mlp_tp(L, normed2, i, T, scatter)
+            ep_layer = self.ep is not None and cfg.is_moe_layer(i)
+            normed2 = tp.reduce_norm(res, L.ln2, eps, T, local_only=ep_layer)
+            if ep_layer:
+                self._moe_tp_ep(L, normed2, T)
+            else:
+                self._mlp_tp(L, normed2, i, T, scatter)
             if fb.deepstack is not None and i < len(fb.deepstack) and fb.deepstack[i] is not None:
                 # deep-stack visual rows join the block output: the owner of each row adds them to
                 # its residual rows before the reduce point sums the partials into them (the
@@ -423,7 +465,7 @@ class DecoderLM(nn.Module):
             last = i + 1 == nl
             cap = (i + 1) in fb.capture_layers
             normed = tp.reduce_norm(res, self.final_norm if last else self.layers[i + 1].ln1, eps, T,
-                                    gather_residual=cap)
+                                    gather_residual=cap, single_src=ep_layer)
             wait = tp.wait
             if cap:
                 tp.wait_gather()
@@ -432,6 +474,22 @@ class DecoderLM(nn.Module):
         if fb.logits_indices is not None:
             return normed[fb.logits_indices.long()]
         return normed.clone()
+
+    def _moe_tp_ep(self, L, x, T):
+        """Expert-parallel MoE of the rows this TP rank owns (normalised in ``x[owned]`` by a
+        local-only reduce point); the combined rows land in this rank's partial slot."""
+        cfg, tp = self.cfg, self.tp
+        a, b = tp.owned(T)
+        xo = x[a:b]
+        shared_out = shared_gate = None
+        if cfg.shared_expert_intermediate_size and b > a:
+            shared_out = ops.linear(ops.linear(xo, L.s13, gated=True), L.s2)
+            if cfg.shared_expert_gate:
+                shared_gate = ops.linear(xo, L.sgate, out_dtype=torch.float32)
+        self.ep.forward(xo, L.router, L.w13, L.w2, renormalize=cfg.norm_topk_prob, mode=cfg.router_mode,
+                        bias=getattr(L, "router_bias", None), n_group=cfg.n_group, topk_group=cfg.topk_group,
+                        scaling=cfg.routed_scaling_factor, shared_out=shared_out, shared_gate=shared_gate,
+                        out=tp.part_local[a:b])
 
     def _mlp_tp(self, L, x, i, T, scatter):
         """MLP of layer i on the gathered rows ``x``; writes this rank's partial rows to their owners."""
@@ -468,12 +526,44 @@ class DecoderLM(nn.Module):
 
     def close_parallel(self):
         """Collective: releases the peer-memory buffers of the TP / EP exchange."""
-        par = self.tp if self.tp is not None else self.ep
-        if par is not None:
-            par.close()
+        if self.vocab_sampler is not None:
+            self.vocab_sampler.close()
+            self.vocab_sampler = None
+        for par in (self.tp, self.ep):
+            if par is not None:
+                par.close()
 
-    def logits(self, hidden: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    def local_logits(self, hidden: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """fp32 logits of this rank's LM-head rows (all of them without vocab-parallel TP)."""
         if not hidden.is_cuda:
             return ops.linear(hidden, self.head_weight, out=out, out_dtype=torch.float32)
         with static_weights():
             return ops.linear(hidden, self.head_weight, out=out, out_dtype=torch.float32)
+
+    def logits(self, hidden: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Full-vocabulary fp32 logits.  Under vocab-parallel TP the slices are all-gathered
+        with torch.distributed (a process group must be initialised); the serving path
+        never calls this, it draws tokens with :meth:`sample_tokens`."""
+        if self.vocab_sampler is None:
+            return self.local_logits(hidden, out)
+        import torch.distributed as dist
+
+        loc = self.local_logits(hidden)
+        parts = [torch.empty_like(loc) for _ in range(self.tp.world)]
+        dist.all_gather(parts, loc.contiguous())
+        full = torch.cat(parts, 1)[:, :self.full_cfg.vocab_size]
+        if out is not None:
+            out.copy_(full)
+            return out
+        return full
+
+    def sample_tokens(self, hidden: torch.Tensor, st=None, suppress=(-1, -1, -1), out: torch.Tensor | None = None,
+                      row_slot: torch.Tensor | None = None, slot_tokens: torch.Tensor | None = None) -> torch.Tensor:
+        """LM head + sampling: int32 tokens [rows] (identical on every TP rank)."""
+        from ..ops.sampling import sample
+
+        if self.vocab_sampler is None:
+            return sample(self.local_logits(hidden), st, suppress, out=out, row_slot=row_slot,
+                          slot_tokens=slot_tokens)
+        return self.vocab_sampler.sample(self.local_logits(hidden), st, suppress, out=out, row_slot=row_slot,
+                                         slot_tokens=slot_tokens)

@@ -103,7 +103,7 @@ def load_decoder_from_hf(model: DecoderLM, sd: dict[str, torch.Tensor], model_pr
             cp(L.mlp2, sh("mlp2", g(p + "mlp.down_proj.weight")))
     cp(model.final_norm, g("norm.weight"))
     if model.lm_head is not None and lm_head_key is not None and lm_head_key in sd:
-        cp(model.lm_head, sd[lm_head_key])
+        cp(model.lm_head, sh("lm_head", sd[lm_head_key]))
 
 
 def export_decoder_to_hf(model: DecoderLM, model_prefix: str = "model.") -> dict[str, torch.Tensor]:

@@ -91,13 +91,18 @@ class TPGroup:
 
     # ------------------------------------------------------------ reduce point
     def reduce_norm(self, residual: torch.Tensor, norm_w: torch.Tensor, eps: float, tokens: int,
-                    gather_residual: bool = False) -> torch.Tensor:
+                    gather_residual: bool = False, single_src: bool = False,
+                    local_only: bool = False) -> torch.Tensor:
         """Sums the partials of the owned rows + residual (updated in place on the owned
         rows), RMSNorm, all-gather.  Returns ``gath[:tokens]`` (read it only through a
-        GEMM given ``wait=self.wait``, or after :meth:`wait_gather`)."""
+        GEMM given ``wait=self.wait``, or after :meth:`wait_gather`).
+
+        ``single_src``: the owned rows were already reduced into ``part_local`` (an
+        expert-parallel combine); ``local_only``: the normalised owned rows stay on this
+        rank (``gath[owned]``, read in stream order) instead of being all-gathered."""
         ext().tp_reduce_norm(self.ptrs, self.rank, self.world, tokens, self.rows_per(tokens), self.max_tokens,
                              residual, norm_w, eps, gather_residual, self.seq, self.counter,
-                             status_word(self.device), self.timeout_s)
+                             status_word(self.device), self.timeout_s, single_src, local_only)
         return self.gath[:tokens]
 
     def wait_gather(self):

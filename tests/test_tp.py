@@ -45,6 +45,7 @@ class _FakeTP:
 def test_shards_reassemble_cpu():
     """Concatenating every rank's slices gives back the unsharded tensors."""
     from sglang_omni_b200.parallel.tp import head_split
+    from sglang_omni_b200.parallel.vocab import vocab_slice
 
     cfg = _cfg(True, dtype=torch.float32)
     full = DecoderLM(cfg).random_init_(seed=3)
@@ -65,6 +66,10 @@ def test_shards_reassemble_cpu():
         assert torch.equal(P.s2, L0.s2[:, r * Is:(r + 1) * Is])
         assert torch.equal(P.router, L0.router) and torch.equal(m.embed, full.embed)
         assert m.cfg.num_heads == cfg.num_heads // world and m.cfg.num_kv_heads == 1
+        # vocab-parallel LM head: this rank's vocabulary rows, zero padded to the slice width
+        v0, vl, width = vocab_slice(cfg.vocab_size, r, world)
+        assert m.lm_head.shape[0] == width
+        assert torch.equal(m.lm_head[:vl], full.lm_head[v0:v0 + vl]) and not m.lm_head[vl:].any()
 
 
 def _free_port():
@@ -162,6 +167,20 @@ def _worker(rank, world, port, q):
                 other = mine.clone()
                 dist.broadcast(other, 0)
                 errs[f"rank_mismatch_moe{moe}_graphs{graphs}"] = float((mine != other).sum())
+                # sampled decode through the vocab-parallel head: every rank draws the same tokens
+                for r in reqs:
+                    r.output_ids.clear()
+                sreqs = [ARRequest(rid=f"s{i}", prompt_ids=list(r.prompt_ids),
+                                   sampling=SamplingParams(temperature=0.8, top_k=20, seed=100 + i, ignore_eos=True),
+                                   max_new_tokens=12) for i, r in enumerate(reqs)]
+                eng.generate(sreqs)
+                torch.cuda.synchronize()
+                check_status(dev)
+                mine = torch.tensor([t for r in sreqs for t in r.output_ids], device=dev)
+                other = mine.clone()
+                dist.broadcast(other, 0)
+                errs[f"sampled_rank_mismatch_moe{moe}_graphs{graphs}"] = float((mine != other).sum())
+                errs[f"vocab_inexact_moe{moe}_graphs{graphs}"] = float(m.vocab_sampler.inexact_rows)
                 eng = pool = None
             m = None
             import gc
@@ -175,6 +194,103 @@ def _worker(rank, world, port, q):
         import traceback
 
         q.put((rank, None, traceback.format_exc()))
+
+
+def _worker_tpep(rank, world, port, q):
+    """Attention TP over both ranks combined with expert-parallel MoE over both ranks."""
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    try:
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=60))
+        from sglang_omni_b200.engines.ar import AREngine, ARRequest, KVPool
+        from sglang_omni_b200.ops._ext import check_status
+        from sglang_omni_b200.parallel import EPMoE, TPGroup
+        from sglang_omni_b200.sampling_params import SamplingParams
+        from test_ar_engine import full_logits
+
+        errs = {}
+        cfg = _cfg(True)
+        ref = DecoderLM(cfg, device=dev).random_init_(seed=11, std=0.05)
+        tp = TPGroup(cfg.hidden_size, 512, dev)
+        ep = EPMoE(cfg.num_experts, cfg.topk, cfg.hidden_size, cfg.moe_intermediate_size, max_tokens=512,
+                   device=dev)
+        m = DecoderLM(cfg, device=dev, tp=tp, ep=ep).random_init_(seed=11, std=0.05)
+        assert m.layers[1].w13.shape[0] == cfg.num_experts // world
+        assert m.layers[1].s13.shape[0] == 2 * cfg.shared_expert_intermediate_size   # shared expert whole
+        toks = torch.randint(0, cfg.vocab_size, (150,), generator=torch.Generator().manual_seed(5)).tolist()
+        a = full_logits(ref, toks, dev)
+        b = full_logits(m, toks, dev)
+        torch.cuda.synchronize()
+        check_status(dev)
+        errs["prefill_tpep"] = float((a - b).norm() / a.norm())
+        for graphs in (False, True):
+            pool = KVPool(m.cfg.num_layers, m.cfg.num_kv_heads, m.cfg.head_dim, 128, dev, m.cfg.dtype)
+            eng = AREngine(m, pool, max_batch=4, max_prefill_tokens=128, max_context=512, use_graphs=graphs)
+            g = torch.Generator().manual_seed(7)
+            reqs = [ARRequest(rid=f"r{i}", prompt_ids=torch.randint(0, cfg.vocab_size, (20 + 13 * i,),
+                                                                   generator=g).tolist(),
+                              sampling=SamplingParams(temperature=0.0, ignore_eos=True), max_new_tokens=10)
+                    for i in range(5)]
+            eng.generate(reqs)
+            torch.cuda.synchronize()
+            check_status(dev)
+            worst = 0.0
+            for r in reqs:
+                lg = full_logits(ref, list(r.prompt_ids) + r.output_ids, dev)
+                for i, tok in enumerate(r.output_ids):
+                    row = lg[len(r.prompt_ids) - 1 + i]
+                    worst = max(worst, float(row.max() - row[tok]))
+            errs[f"greedy_gap_tpep_graphs{graphs}"] = worst
+            mine = torch.tensor([t for r in reqs for t in r.output_ids], device=dev)
+            other = mine.clone()
+            dist.broadcast(other, 0)
+            errs[f"rank_mismatch_tpep_graphs{graphs}"] = float((mine != other).sum())
+            eng = pool = None
+        m.close_parallel()
+        dist.destroy_process_group()
+        q.put((rank, errs, None))
+    except Exception:  # report instead of hanging the parent
+        import traceback
+
+        q.put((rank, None, traceback.format_exc()))
+
+
+def _run2(target):
+    import sys
+
+    import torch.multiprocessing as mp
+
+    sys.path.insert(0, os.path.dirname(__file__))
+    world = 2
+    ctx = mp.get_context("spawn")
+    qu = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=target, args=(r, world, port, qu)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [qu.get(timeout=600) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    return res
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp_ep_combined_matches_unsharded():
+    for rank, errs, tb in _run2(_worker_tpep):
+        assert tb is None, tb
+        for k, v in errs.items():
+            if k.startswith("prefill"):
+                assert v < 0.03, (rank, k, v)
+            elif k.startswith("greedy"):
+                assert v < 0.2, (rank, k, v)
+            else:
+                assert v == 0, (rank, k, v)
 
 
 @pytest.mark.gpu
