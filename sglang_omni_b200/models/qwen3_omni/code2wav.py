@@ -193,11 +193,27 @@ class Code2Wav(nn.Module):
         self.conv_out_b.copy_(g(f"decoder.{n + 1}.conv.bias"))
 
     # ------------------------------------------------------------------ forward
-    def _transformer(self, x: torch.Tensor, B: int, T: int) -> torch.Tensor:
+    def make_aux(self, B: int, T: int, device) -> dict:
+        """Device-side index tensors of a [B, T] window batch (positions, sequence offsets,
+        attention tiles), built once per shape so a captured forward does no host copies."""
+        from ...ops.attention import prefill_tiles
+
+        cfg = self.cfg
+        req, tok0 = prefill_tiles([T] * B, cfg.num_heads // cfg.num_kv_heads)
+        return {"pos": torch.arange(T, dtype=torch.int32, device=device).repeat(B),
+                "cu": torch.arange(0, (B + 1) * T, T, dtype=torch.int32, device=device),
+                "tiles": (torch.tensor(req, dtype=torch.int32, device=device),
+                          torch.tensor(tok0, dtype=torch.int32, device=device))}
+
+    def _transformer(self, x: torch.Tensor, B: int, T: int, aux: dict | None = None) -> torch.Tensor:
         cfg = self.cfg
         H, nh, nkv, hd = cfg.hidden_size, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
-        pos = torch.arange(T, dtype=torch.int32, device=x.device).repeat(B)
-        cu = torch.arange(0, (B + 1) * T, T, dtype=torch.int32, device=x.device)
+        if aux is not None:
+            pos, cu, tiles = aux["pos"], aux["cu"], aux["tiles"]
+        else:
+            pos = torch.arange(T, dtype=torch.int32, device=x.device).repeat(B)
+            cu = torch.arange(0, (B + 1) * T, T, dtype=torch.int32, device=x.device)
+            tiles = None
         h = x
         for L in self.layers:
             n1 = ops.rms_norm(h, L.ln1, cfg.rms_norm_eps)
@@ -209,7 +225,7 @@ class Code2Wav(nn.Module):
             v = qkv[:, (nh + nkv) * hd:]
             if qkv.is_cuda:
                 attn = ops.varlen_attention(q, k, v, cu, nh, nkv, hd, causal=True, window=cfg.sliding_window,
-                                            q_lens=[T] * B)
+                                            q_lens=[T] * B, tiles=tiles)
             else:
                 attn = ops.varlen_attention(q.contiguous(), k.contiguous(), v.contiguous(), cu, nh, nkv, hd,
                                             causal=True, window=cfg.sliding_window)
@@ -220,13 +236,13 @@ class Code2Wav(nn.Module):
             h = h + (m.float() * L.mlp_scale.float()).to(h.dtype)
         return ops.rms_norm(h, self.final_norm, cfg.rms_norm_eps)
 
-    def forward(self, codes: torch.Tensor) -> torch.Tensor:
-        """codes [B, Q, T] int -> waveform [B, T * total_upsample] float32."""
+    def forward(self, codes: torch.Tensor, aux: dict | None = None) -> torch.Tensor:
+        """codes [B, Q, T] int -> waveform [B, T * total_upsample] float32 (``aux``: ``make_aux``)."""
         cfg = self.cfg
         B, Q, T = codes.shape
         idx = (codes.long() + self.code_offset.view(1, -1, 1)).permute(0, 2, 1)  # [B, T, Q]
         x = self.code_embedding[idx].float().mean(2).to(cfg.dtype).reshape(B * T, cfg.hidden_size)
-        x = self._transformer(x, B, T).view(B, T, cfg.hidden_size)
+        x = self._transformer(x, B, T, aux).view(B, T, cfg.hidden_size)
         for f, U in zip(cfg.upsampling_ratios, self.up):
             Tc = x.shape[1]
             y = ops.linear(x.contiguous(), U.tconv_w)  # [B, T, f*C]
@@ -251,6 +267,78 @@ class Code2Wav(nn.Module):
         return wav.float().reshape(B, -1).clamp(-1.0, 1.0)
 
 
+class Code2WavGraphs:
+    """CUDA graphs of the vocoder forward, one per (batch bucket, window length).
+
+    A streaming chunk runs ~150 kernels; launched from Python in a process whose
+    thinker and talker threads hold the interpreter between their own launches,
+    that costs far more than the GPU time.  A replay is one launch.  Batches are
+    padded to the next bucket (padding rows decode code 0 and are dropped);
+    windows that were not captured (final flushes of odd length) run eagerly.
+    The returned rows view the graph's output buffer: read them before the same
+    (bucket, window) graph replays again."""
+
+    BUCKETS = (1, 2, 4, 8, 16, 32, 64, 128)
+
+    def __init__(self, model: "Code2Wav", max_batch: int = 32):
+        self.model = model
+        self.max_batch = max_batch
+        self.graphs: dict[tuple[int, int], tuple] = {}
+        self._pool = None
+
+    @torch.no_grad()
+    def capture(self, B: int, W: int) -> None:
+        m = self.model
+        dev = m.code_embedding.device
+        codes = torch.zeros(B, m.cfg.num_quantizers, W, dtype=torch.long, device=dev)
+        aux = m.make_aux(B, W, dev)
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            m(codes, aux)            # warm-up: workspaces and kernel attributes outside the capture
+        torch.cuda.current_stream(dev).wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, pool=self._pool):
+            out = m(codes, aux)
+        self._pool = g.pool()
+        self.graphs[(B, W)] = (g, codes, aux, out)
+
+    def capture_windows(self, windows, max_batch: int | None = None) -> None:
+        top = max_batch or self.max_batch
+        for W in sorted(set(windows)):
+            for B in self.BUCKETS:
+                if B > top:
+                    break
+                if (B, W) not in self.graphs:
+                    self.capture(B, W)
+
+    @torch.no_grad()
+    def __call__(self, codes: torch.Tensor) -> torch.Tensor:
+        B, _, W = codes.shape
+        Bb = next((b for b in self.BUCKETS if b >= B), None)
+        hit = self.graphs.get((Bb, W)) if Bb is not None else None
+        if hit is None:
+            return self.model(codes)
+        g, buf, _, out = hit
+        buf[:B].copy_(codes, non_blocking=True)
+        if B < Bb:
+            buf[B:].zero_()
+        g.replay()
+        return out[:B]
+
+
+def chunk_windows(chunk: int, left_context: int, first_chunk: int) -> list[int]:
+    """Window lengths (context + new frames) of a stream's successive full chunks."""
+    out, emitted = [], 0
+    while True:
+        new = first_chunk if emitted == 0 else chunk
+        w = min(left_context, emitted) + new
+        if w in out:
+            return out
+        out.append(w)
+        emitted += new
+
+
 @dataclass
 class _StreamState:
     codes: list = field(default_factory=list)   # list of [Q] code columns
@@ -262,12 +350,18 @@ class StreamingCode2Wav:
     the end) each ready stream decodes ``context + new`` frames; ready streams
     with equal window length are batched into one forward."""
 
-    def __init__(self, model: Code2Wav, chunk: int = 10, left_context: int = 25, first_chunk: int | None = None):
+    def __init__(self, model: Code2Wav, chunk: int = 10, left_context: int = 25, first_chunk: int | None = None,
+                 graphs: Code2WavGraphs | None = None):
         self.model = model
         self.chunk = chunk
         self.left_context = left_context
         self.first_chunk = first_chunk or chunk
         self.streams: dict[str, _StreamState] = {}
+        self.graphs = graphs
+        self._pinned: torch.Tensor | None = None
+
+    def windows(self) -> list[int]:
+        return chunk_windows(self.chunk, self.left_context, self.first_chunk)
 
     def add_codes(self, rid: str, codes: torch.Tensor) -> None:
         """codes: [Q] or [T, Q] frames for stream rid."""
@@ -285,11 +379,13 @@ class StreamingCode2Wav:
         return pending >= need or (final and pending > 0)
 
     @torch.no_grad()
-    def decode_ready(self, rids: list[str], final: bool = False, finals=None) -> dict[str, torch.Tensor]:
+    def decode_ready(self, rids: list[str], final: bool = False, finals=None,
+                     to_host: bool = False) -> dict[str, torch.Tensor]:
         """Returns {rid: float32 waveform of the new frames} for every ready stream.
 
         ``final`` (all streams) or ``finals`` (a set of stream ids) flush the streams
-        whose last frame has arrived."""
+        whose last frame has arrived.  ``to_host``: numpy arrays, copied with one
+        device-to-host transfer per window group on the current stream."""
         up = self.model.cfg.total_upsample
         groups: dict[tuple[int, int], list[tuple[str, torch.Tensor]]] = {}
         for rid in rids:
@@ -309,11 +405,26 @@ class StreamingCode2Wav:
             groups.setdefault((window.shape[1], ctx), []).append((rid, window))
             st.emitted_frames = end
         out = {}
+        dev = self.model.code_embedding.device
+        run = self.graphs if self.graphs is not None and dev.type == "cuda" else self.model
         for (W, ctx), items in groups.items():
-            codes = torch.stack([w for _, w in items], 0).to(self.model.code_embedding.device)
-            wav = self.model(codes)
-            for (rid, _), wv in zip(items, wav):
-                out[rid] = wv[ctx * up:]
+            codes = torch.stack([w for _, w in items], 0).to(dev, non_blocking=True)
+            wav = run(codes)
+            if to_host and wav.is_cuda:
+                n = wav[:, ctx * up:]
+                if self._pinned is None or self._pinned.numel() < n.numel():
+                    self._pinned = torch.empty(max(n.numel(), 1 << 20), dtype=torch.float32, pin_memory=True)
+                host = self._pinned[:n.numel()].view(n.shape)
+                host.copy_(n, non_blocking=True)
+                torch.cuda.current_stream(dev).synchronize()
+                for (rid, _), wv in zip(items, host):
+                    out[rid] = wv.numpy().copy()
+            elif to_host:
+                for (rid, _), wv in zip(items, wav):
+                    out[rid] = wv[ctx * up:].float().numpy().copy()
+            else:
+                for (rid, _), wv in zip(items, wav):
+                    out[rid] = wv[ctx * up:]
         return out
 
     def close(self, rid: str) -> None:

@@ -48,7 +48,7 @@ from .. import loader
 from ..engine_io import build_prompt, mrope_positions
 from ..hf_config import THINKER_EOS_IDS
 from ..talker import SpeechGenerator, build_talker_prefill
-from ..code2wav import StreamingCode2Wav
+from ..code2wav import Code2WavGraphs, StreamingCode2Wav
 
 log = logging.getLogger(__name__)
 SAMPLE_RATE_IN = 16000
@@ -640,11 +640,16 @@ class Code2WavStreamingExecutor(ResultQueueMixin, Executor):
     (instead of one forward per stream), off the event loop."""
 
     def __init__(self, model_path: str, device: str, chunk: int = 10, left_context: int = 25,
-                 first_chunk: int | None = None, overrides: dict | None = None):
+                 first_chunk: int | None = None, overrides: dict | None = None, use_graphs: bool = True,
+                 max_streams: int = 32):
         super().__init__()
         dev = torch.device(device)
         self.model = loader.get_code2wav(model_path, dev, overrides)
-        self.sc = StreamingCode2Wav(self.model, chunk, left_context, first_chunk)
+        graphs = Code2WavGraphs(self.model, max_streams) if use_graphs and dev.type == "cuda" else None
+        self.sc = StreamingCode2Wav(self.model, chunk, left_context, first_chunk, graphs=graphs)
+        # its own high-priority stream: a chunk's kernels and its host copy wait for nothing
+        # the thinker / talker threads queued
+        self._stream = torch.cuda.Stream(device=dev, priority=-1) if dev.type == "cuda" else None
         self._streams: dict[str, asyncio.Queue] = {}
         self._audio: dict[str, list] = {}
         self._finals: set[str] = set()
@@ -659,7 +664,20 @@ class Code2WavStreamingExecutor(ResultQueueMixin, Executor):
 
     async def start(self):
         self._loop = asyncio.get_running_loop()
+        if self.sc.graphs is not None:
+            await asyncio.to_thread(self._capture)
         fastlane.register(self.stage_name, self)
+
+    def _capture(self):
+        with torch.cuda.stream(self._stream), torch.inference_mode():
+            self.sc.graphs.capture_windows(self.sc.windows())
+
+    def _decode(self, ready, finals):
+        """One batched decode of the ready streams on this stage's stream; host arrays."""
+        if self._stream is None:
+            return self.sc.decode_ready(ready, False, finals, to_host=True)
+        with torch.cuda.stream(self._stream), torch.inference_mode():
+            return self.sc.decode_ready(ready, False, finals, to_host=True)
 
     async def stop(self):
         fastlane.unregister(self.stage_name, self)
@@ -731,7 +749,7 @@ class Code2WavStreamingExecutor(ResultQueueMixin, Executor):
                 for r in ready:
                     trace.mark(r, "3d_vocoder_decode_start")
                 try:
-                    out = await asyncio.to_thread(self.sc.decode_ready, ready, False, finals)
+                    out = await asyncio.to_thread(self._decode, ready, finals)
                 except Exception as exc:  # fail the streams of this batch only
                     log.exception("code2wav batch failed")
                     for r in ready:
@@ -740,9 +758,8 @@ class Code2WavStreamingExecutor(ResultQueueMixin, Executor):
                             f.set_exception(exc)
                     continue
                 now = time.perf_counter()
-                for r, wav in out.items():
+                for r, a in out.items():
                     trace.mark(r, "4_first_audio_chunk")
-                    a = wav.float().cpu().numpy()
                     if r in self._audio:
                         self._audio[r].append(a)
                     q = self._streams.get(r)
@@ -800,5 +817,7 @@ class Code2WavStreamingExecutor(ResultQueueMixin, Executor):
 
 
 def create_code2wav_executor(model_path: str = "", device: str = "cuda:0", chunk: int = 10,
-                             left_context: int = 25, first_chunk: int | None = None, overrides: dict | None = None):
-    return Code2WavStreamingExecutor(model_path, device, chunk, left_context, first_chunk, overrides)
+                             left_context: int = 25, first_chunk: int | None = None, overrides: dict | None = None,
+                             use_graphs: bool = True, max_streams: int = 32):
+    return Code2WavStreamingExecutor(model_path, device, chunk, left_context, first_chunk, overrides,
+                                     use_graphs=use_graphs, max_streams=max_streams)

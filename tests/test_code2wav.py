@@ -96,3 +96,39 @@ def test_code2wav_gpu_matches_cpu():
         out = gpu(codes.cuda()).cpu()
     # bf16 kernels vs the fp32 oracle: relative L2 error of the waveform
     assert float((out - ref).norm() / ref.norm().clamp_min(1e-6)) < 0.05
+
+
+@pytest.mark.gpu
+def test_code2wav_graphs_match_eager():
+    """Captured (batch bucket, window) graphs give the eager forward's waveform, padded
+    batches and uncaptured windows included, and the streaming decoder's host output is
+    the same through graphs as without."""
+    from sglang_omni_b200.models.qwen3_omni.code2wav import Code2WavGraphs, chunk_windows
+
+    cfg = Code2WavConfig(codebook_size=64, hidden_size=256, num_heads=4, num_kv_heads=4, sliding_window=16,
+                         intermediate_size=512, num_layers=2, num_quantizers=4, upsample_rates=(4, 2),
+                         upsampling_ratios=(2,), decoder_dim=256)
+    m = Code2Wav(cfg, device="cuda").random_init_(seed=4, std=0.05)
+    g = Code2WavGraphs(m, max_batch=8)
+    wins = chunk_windows(3, 4, 2)
+    g.capture_windows(wins)
+    gen = torch.Generator().manual_seed(1)
+    with torch.no_grad():
+        for B in (1, 3, 8):
+            for W in wins + [5]:          # 5 is not captured: eager
+                codes = torch.randint(0, 64, (B, 4, W), generator=gen).cuda()
+                ref = m(codes)
+                got = g(codes).clone()
+                torch.testing.assert_close(got, ref, atol=2e-3, rtol=1e-3)
+    a = StreamingCode2Wav(m, chunk=3, left_context=4, first_chunk=2, graphs=g)
+    b = StreamingCode2Wav(m, chunk=3, left_context=4, first_chunk=2)
+    codes = torch.randint(0, 64, (5, 4, 14), generator=gen)
+    for t in range(14):
+        for s in range(5):
+            a.add_codes(f"s{s}", codes[s, :, t])
+            b.add_codes(f"s{s}", codes[s, :, t])
+        ra = a.decode_ready([f"s{s}" for s in range(5)], to_host=True)
+        rb = b.decode_ready([f"s{s}" for s in range(5)])
+        assert ra.keys() == rb.keys()
+        for k in ra:
+            torch.testing.assert_close(torch.from_numpy(ra[k]), rb[k].float().cpu(), atol=2e-3, rtol=1e-3)
