@@ -142,6 +142,25 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
+// 2^x by the SFU's approximate base-2 exponential (denormal results flush to zero: the
+// probabilities are rounded to bf16 anyway).
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Row max of n raw scores with 8 independent partial maxima (no 64-long dependency chain).
+template <int N>
+__device__ __forceinline__ float row_max(const float (&s)[N]) {
+  float m[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m[i] = s[i];
+#pragma unroll
+  for (int i = 8; i < N; ++i) m[i & 7] = fmaxf(m[i & 7], s[i]);
+  return fmaxf(fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3])), fmaxf(fmaxf(m[4], m[5]), fmaxf(m[6], m[7])));
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     fa_prefill_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                       const __grid_constant__ CUtensorMap tmap_v, const FaParams p) {
@@ -293,29 +312,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&s_full[b], (j >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
       tc_fence_after();
       float s[kBN];
+      {
+        uint32_t v[kBN];
 #pragma unroll
-      for (int c = 0; c < kBN; c += 32) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem + lane_addr + b * 128 + c, v);
+        for (int c = 0; c < kBN; c += 32)
+          tmem_ld_32x32b_x32(tmem + lane_addr + b * 128 + c, *reinterpret_cast<uint32_t(*)[32]>(v + c));
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) s[c + i] = __uint_as_float(v[i]);
+        for (int i = 0; i < kBN; ++i) s[i] = __uint_as_float(v[i]);
       }
       const int k0 = j * kBN;
       const int lim = p.causal ? min(kv_len, qpos + 1) : kv_len;   // keys [0, lim) are visible
-      float mb = -INFINITY;
+      if (k0 + kBN > lim) {   // diagonal / last block: mask the invisible keys
 #pragma unroll
-      for (int i = 0; i < kBN; ++i) {
-        const float x = (k0 + i < lim) ? s[i] * p.scale_log2 : -INFINITY;
-        s[i] = x;
-        mb = fmaxf(mb, x);
+        for (int i = 0; i < kBN; ++i) s[i] = (k0 + i < lim) ? s[i] : -INFINITY;
       }
+      const float mraw = row_max(s);
+      const float mb = mraw == -INFINITY ? -INFINITY : mraw * p.scale_log2;   // log2 units
       if (mb > m_run + kRescaleThreshold || (m_run == -INFINITY && mb > -INFINITY)) {
         if (j > 0 && m_run > -INFINITY) {
           // O holds sum over earlier blocks at max m_run: rescale once the previous PV is done
           if (!mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
           tc_fence_after();
-          const float f = exp2f(m_run - mb);
+          const float f = ex2_ftz(m_run - mb);
 #pragma unroll 1
           for (int c = 0; c < kD; c += 32) {
             uint32_t v[32];
@@ -334,14 +353,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       // P buffer b was last read by PV_{j-2}
       if (j >= 2 && !mbar_wait(&pv_done[b], ((j - 2) >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
       uint8_t* prow = sP + b * kTileBytes + r * 128;
-      float lsum = 0.f;
+      float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c8 = 0; c8 < kBN / 8; ++c8) {
         float e[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          e[i] = exp2f(s[c8 * 8 + i] - msub);
-          lsum += e[i];
+          e[i] = ex2_ftz(fmaf(s[c8 * 8 + i], p.scale_log2, -msub));
+          ls[i] += e[i];
         }
         uint4 pk;
         pk.x = pack_bf16x2(e[0], e[1]);
@@ -351,7 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int region = c8 >> 3, chunk = c8 & 7;
         *reinterpret_cast<uint4*>(prow + region * kRegion + ((chunk ^ (r & 7)) << 4)) = pk;
       }
-      l_run += lsum;
+      l_run += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&p_full[b]);
@@ -568,28 +587,28 @@ __global__ void __launch_bounds__(pp::kThreads, 1)
       if (!mbar_wait(&s_full[t], j & 1, abort_flag, p.status)) { ok = false; break; }
       tc_fence_after();
       float s[kPBN];
+      {
+        uint32_t v[kPBN];
 #pragma unroll
-      for (int c = 0; c < kPBN; c += 32) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem + lane_addr + s_col(t) + c, v);
+        for (int c = 0; c < kPBN; c += 32)
+          tmem_ld_32x32b_x32(tmem + lane_addr + s_col(t) + c, *reinterpret_cast<uint32_t(*)[32]>(v + c));
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) s[c + i] = __uint_as_float(v[i]);
+        for (int i = 0; i < kPBN; ++i) s[i] = __uint_as_float(v[i]);
       }
       const int k0 = j * kPBN;
-      float mb = -INFINITY;
+      if (k0 + kPBN > lim) {   // diagonal / last block: mask the invisible keys
 #pragma unroll
-      for (int i = 0; i < kPBN; ++i) {
-        const float x = (k0 + i < lim) ? s[i] * p.scale_log2 : -INFINITY;
-        s[i] = x;
-        mb = fmaxf(mb, x);
+        for (int i = 0; i < kPBN; ++i) s[i] = (k0 + i < lim) ? s[i] : -INFINITY;
       }
+      const float mraw = row_max(s);
+      const float mb = mraw == -INFINITY ? -INFINITY : mraw * p.scale_log2;   // log2 units
       // the previous PV of this tile has read P and (for a rescale) finished accumulating O
       if (j > 0 && !mbar_wait(&pv_done[t], (j - 1) & 1, abort_flag, p.status)) { ok = false; break; }
       if (mb > m_run + kRescaleThreshold || (m_run == -INFINITY && mb > -INFINITY)) {
         if (j > 0 && m_run > -INFINITY) {
           tc_fence_after();
-          const float f = exp2f(m_run - mb);
+          const float f = ex2_ftz(m_run - mb);
 #pragma unroll 1
           for (int c = 0; c < kD; c += 32) {
             uint32_t v[32];
@@ -605,14 +624,14 @@ __global__ void __launch_bounds__(pp::kThreads, 1)
         m_run = mb;
       }
       const float msub = m_run == -INFINITY ? 0.f : m_run;
-      float lsum = 0.f;
+      float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c8 = 0; c8 < kPBN / 8; ++c8) {
         float e[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          e[i] = exp2f(s[c8 * 8 + i] - msub);
-          lsum += e[i];
+          e[i] = ex2_ftz(fmaf(s[c8 * 8 + i], p.scale_log2, -msub));
+          ls[i] += e[i];
         }
         uint4 pk;
         pk.x = pack_bf16x2(e[0], e[1]);
@@ -621,7 +640,7 @@ __global__ void __launch_bounds__(pp::kThreads, 1)
         pk.w = pack_bf16x2(e[6], e[7]);
         *reinterpret_cast<uint4*>(prow + ((c8 ^ (r & 7)) << 4)) = pk;
       }
-      l_run += lsum;
+      l_run += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&p_full[t]);

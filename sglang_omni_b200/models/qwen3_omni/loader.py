@@ -75,12 +75,14 @@ def get_thinker(model_path: str, device, overrides: dict | None = None) -> Decod
 def build_thinker_rank(args: dict, rank: int, world: int, device, group, mode: str) -> DecoderLM:
     """One rank of a thinker stage group (``parallel.rank_group``): ``tp`` holds this
     rank's heads / expert slice / MLP slices with the fused TP reduce points, ``ep``
-    this rank's experts with the fused EP exchange (data-parallel attention), the
-    other modes a full copy.  Weights: the checkpoint's slices, or the same
+    this rank's experts with the fused EP exchange (data-parallel attention; with
+    ``args["tp"]`` > 1 the attention is tensor parallel inside groups of that many
+    ranks), the other modes a full copy.  Weights: the checkpoint's slices, or the same
     deterministic random init as the single-GPU thinker."""
     model_path = args.get("model_path", "")
     cfg = _apply(_cfgs(model_path)["thinker"], (args.get("overrides") or {}).get("thinker"))
     max_tokens = int(args.get("max_tokens", 8192))
+    tp_size = int(args.get("tp", 1))
     tp = ep = None
     if mode == "tp":
         from ...parallel.tp import TPGroup
@@ -89,6 +91,12 @@ def build_thinker_rank(args: dict, rank: int, world: int, device, group, mode: s
     elif mode == "ep":
         from ...parallel.ep_moe import EPMoE
 
+        if tp_size > 1:   # attention TP inside this rank's data-parallel group, EP over every rank
+            from ...parallel.tp import TPGroup
+
+            g0 = rank // tp_size * tp_size
+            sub = group.subgroup(list(range(g0, g0 + tp_size)), f"tp{g0 // tp_size}")
+            tp = TPGroup(cfg.hidden_size, max_tokens, device, group=sub)
         ep = EPMoE(cfg.num_experts, cfg.topk, cfg.hidden_size, cfg.moe_intermediate_size, max_tokens=max_tokens,
                    device=device, group=group)
     m = DecoderLM(cfg, device=device, tp=tp, ep=ep)

@@ -261,8 +261,13 @@ def create_thinker_executor(model_path: str = "", device: str = "cuda:0", max_ba
         from ....parallel.rank_group import GroupedAREngine, GroupSpec, StageRankGroup
 
         if tp_size > 1 and ep_size > 1:
-            raise NotImplementedError("a thinker stage group is either tensor parallel or expert parallel")
-        mode, world = ("tp", tp_size) if tp_size > 1 else ("ep", ep_size)
+            # attention TP inside data-parallel groups of tp_size ranks, experts over ep_size ranks
+            if ep_size % tp_size != 0:
+                raise ValueError(f"ep_size {ep_size} must be a multiple of tp_size {tp_size}")
+            mode, world, group_tp = "ep", ep_size, tp_size
+        else:
+            mode, world = ("tp", tp_size) if tp_size > 1 else ("ep", ep_size)
+            group_tp = 1
         if mode == "ep" and speech_target is not None:
             raise NotImplementedError("expert-parallel thinker groups serve text output; the talker needs the "
                                       "hidden states of every request on the leader (use tp_size)")
@@ -273,7 +278,7 @@ def create_thinker_executor(model_path: str = "", device: str = "cuda:0", max_ba
                          builder="sglang_omni_b200.models.qwen3_omni.loader.build_thinker_rank",
                          builder_args={"model_path": model_path, "overrides": overrides,
                                        "max_tokens": max(max_prefill_tokens, max_batch)},
-                         engine_args=engine_args, kv_pages=pages)
+                         engine_args=engine_args, kv_pages=pages, tp=group_tp)
         rg = StageRankGroup(spec)
         engine = rg.start()
         model = rg.model

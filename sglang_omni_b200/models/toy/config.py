@@ -58,9 +58,10 @@ def build_toy_rank(args: dict, rank: int, world: int, device, group, mode: str):
 
 
 def create_toy_decoder_executor(device: str = "cpu", max_batch: int = 8, seed: int = 0, group_mode: str | None = None,
-                                group_size: int = 1):
+                                group_size: int = 1, group_tp: int = 1):
     """``group_mode`` ("replica" or "dp") with ``group_size`` > 1 serves the decoder with a stage
-    rank group of that many processes (the plumbing of TP / EP stages, on CPU)."""
+    rank group of that many processes (the plumbing of TP / EP stages, on CPU); ``group_tp`` > 1
+    (``dp``) forms lock-step groups of that many ranks, the plumbing of TP x EP stages."""
     import torch
 
     from ..common.ar_stage import create_ar_executor
@@ -73,7 +74,7 @@ def create_toy_decoder_executor(device: str = "cpu", max_batch: int = 8, seed: i
         from ...parallel.rank_group import GroupSpec
 
         spec = GroupSpec(mode=group_mode, world=group_size, builder=f"{_P}.toy.config.build_toy_rank",
-                         builder_args={"seed": seed}, report_timeout_s=60.0)
+                         builder_args={"seed": seed}, report_timeout_s=60.0, tp=group_tp)
         return create_ar_executor(None, "decoder", ByteTokenizer(1000), rank_group=spec, **common)
     torch.manual_seed(seed)
     model = DecoderLM(toy_decoder_config(), device=device).random_init_(seed=seed)

@@ -26,6 +26,16 @@ class HostGroup:
                                    wait_for_workers=False)
         self._n = 0
 
+    def subgroup(self, ranks: list[int], tag: str) -> "HostGroup":
+        """A group of some of this group's ranks over the same store (call on those ranks only;
+        ``tag`` distinguishes concurrent subgroups)."""
+        sub = HostGroup.__new__(HostGroup)
+        sub.rank, sub.world = list(ranks).index(self.rank), len(ranks)
+        sub.prefix = f"{self.prefix}/{tag}"
+        sub.store = self.store
+        sub._n = 0
+        return sub
+
     def _key(self, tag: str) -> str:
         return f"{self.prefix}/{self._n}/{tag}"
 

@@ -18,8 +18,14 @@ of its own; the leader forwards what its scheduler receives:
   with zero tokens).  Followers report, after every iteration, whether they
   still have work and the tokens they produced; the leader routes those to the
   requests' streams and futures.
+* ``ep`` with ``tp`` > 1 -- attention tensor parallel inside data-parallel
+  groups of ``tp`` consecutive ranks, MoE expert parallel over all ranks: a
+  request goes to one group (every rank of it adds the request in the same
+  iteration and steps in lock step, as in ``tp``), the group's first rank
+  reports its tokens, and idle groups run the idle forward.
 * ``replica`` / ``dp`` -- the same protocols without a sharded model (every
-  rank holds a full copy); they run on CPU as well and test the plumbing.
+  rank holds a full copy; ``dp`` with ``tp`` > 1 has lock-step groups); they run
+  on CPU as well and test the plumbing.
 
 Bootstrap (CUDA IPC handles of the symmetric buffers) goes over a TCP store
 (``HostGroup``), the per-iteration control over ZMQ (leader PUB -> followers,
@@ -72,6 +78,18 @@ class GroupSpec:
     pub_port: int = 0
     pull_port: int = 0
     report_timeout_s: float = 120.0
+    tp: int = 1                                 # ranks per data-parallel group (distributing modes)
+
+    @property
+    def groups(self) -> int:
+        return self.world // self.tp
+
+    def group_of(self, rank: int) -> int:
+        return rank // self.tp
+
+    def reports_events(self, rank: int) -> bool:
+        """The first rank of a data-parallel group reports its requests' tokens."""
+        return self.distributes and rank % self.tp == 0
 
     def device_of(self, rank: int) -> torch.device:
         return torch.device("cuda", int(self.gpus[rank])) if self.gpus else torch.device("cpu")
@@ -91,7 +109,9 @@ def _build_rank(spec: GroupSpec, rank: int, device: torch.device):
     from .hostgroup import HostGroup
 
     group = HostGroup(spec.host, spec.store_port, rank, spec.world, timeout_s=spec.report_timeout_s)
-    model = import_string(spec.builder)(dict(spec.builder_args), rank, spec.world, device, group, spec.mode)
+    args = dict(spec.builder_args)
+    args.setdefault("tp", spec.tp)
+    model = import_string(spec.builder)(args, rank, spec.world, device, group, spec.mode)
     cfg = model.cfg
     pool = KVPool(cfg.num_layers, cfg.num_kv_heads, cfg.head_dim, spec.kv_pages, device, cfg.dtype)
     eng = AREngine(model, pool, **spec.engine_args)
@@ -161,24 +181,25 @@ def _follower_main(spec: GroupSpec, rank: int):  # pragma: no cover - runs in a 
             msg = sub.recv_pyobj()
             if msg["kind"] == "stop":
                 break
+            head = spec.reports_events(rank)
             for kind, dst, x in msg["items"]:
-                if dst not in (-1, rank):
+                if dst not in (-1, spec.group_of(rank)):
                     continue
                 if kind == "add":
-                    if spec.distributes:
+                    if head:
                         x.on_token = on_token
                     try:
                         eng.add_request(x)
                     except Exception as exc:   # the leader rejects the same request (tp) or reports it
-                        if spec.distributes:
+                        if head:
                             events.append(("done", x.rid, [], f"error: {exc}"))
                 elif kind == "abort":
                     r = eng.requests.get(x)
-                    if r is not None and eng.abort(x) and spec.distributes:
+                    if r is not None and eng.abort(x) and head:
                         events.append(("done", r.rid, list(r.output_ids), r.finish_reason))
             if msg["step"]:
                 for r in _step(eng, model, spec):
-                    if spec.distributes:
+                    if head:
                         events.append(("done", r.rid, list(r.output_ids), r.finish_reason))
             if spec.distributes:
                 push.send_pyobj({"it": msg["it"], "rank": rank, "has_work": eng.has_work(), "events": events})
@@ -211,6 +232,8 @@ class StageRankGroup:
         assert spec.mode in MODES, f"unknown rank-group mode {spec.mode!r}"
         assert spec.world >= 2, "a rank group has at least two ranks"
         assert not spec.gpus or len(spec.gpus) == spec.world, "one GPU per rank"
+        assert spec.tp >= 1 and spec.world % spec.tp == 0, "data-parallel groups of tp ranks"
+        assert spec.tp == 1 or spec.distributes, "tp groups apply to the distributing modes"
         spec.store_port = spec.store_port or _free_port()
         spec.pub_port = spec.pub_port or _free_port()
         spec.pull_port = spec.pull_port or _free_port()
@@ -324,7 +347,7 @@ class GroupedAREngine(ThreadedAREngine):
         self.spec = group.spec
         self._owner: dict[str, int] = {}               # rid -> rank (distributing modes)
         self._remote: dict[str, ARRequest] = {}        # requests served by a follower
-        self._load = [0] * self.spec.world
+        self._load = [0] * self.spec.groups          # requests per data-parallel group
         self._follower_work = [False] * self.spec.world
         self.served_local = 0    # requests this rank ran (distributing modes)
         self.served_remote = 0   # requests a follower ran
@@ -382,12 +405,14 @@ class GroupedAREngine(ThreadedAREngine):
                 for kind, x in inbox:
                     if kind == "add":
                         if spec.distributes:
-                            dst = min(range(spec.world), key=lambda r: (self._load[r], r))
+                            dst = min(range(spec.groups), key=lambda g: (self._load[g], g))
                             self._load[dst] += 1
                             self._owner[x.rid] = dst
                             if dst == 0:
                                 local.append((kind, x))
                                 self.served_local += 1
+                                if spec.tp > 1:      # the other ranks of the leader's group
+                                    items.append(("add", 0, _stable_copy(x)))
                             else:
                                 self.served_remote += 1
                                 self._remote[x.rid] = x
@@ -397,7 +422,7 @@ class GroupedAREngine(ThreadedAREngine):
                             local.append((kind, x))
                     elif kind == "abort":
                         dst = self._owner.get(x, 0) if spec.distributes else -1
-                        if dst != 0:
+                        if dst != 0 or spec.tp > 1:
                             items.append(("abort", dst, x))
                         if dst in (0, -1):
                             local.append((kind, x))

@@ -45,13 +45,13 @@ async def _run(cfg, prompts, max_tokens=12):
         return await asyncio.gather(*[one(i) for i in range(len(prompts))])
 
 
-def _group_cfg(tmp_path, mode):
+def _group_cfg(tmp_path, mode, size=2, tp=1):
     base = ToyPipelineConfig()
     d = base.model_dump()
     for st in d["stages"]:
         if st["name"] == "decoder":
-            st["executor"]["args"].update({"group_mode": mode, "group_size": 2})
-    p = tmp_path / f"toy_{mode}.yaml"
+            st["executor"]["args"].update({"group_mode": mode, "group_size": size, "group_tp": tp})
+    p = tmp_path / f"toy_{mode}_{size}_{tp}.yaml"
     p.write_text(yaml.safe_dump(d))
     return ConfigManager.from_file(str(p))
 
@@ -64,6 +64,16 @@ def test_two_rank_stage_group_from_yaml_matches_single_process(tmp_path, mode):
     outs = asyncio.run(_run(cfg, prompts))
     assert outs == ref
     assert all(len(o) == 12 for o in outs)
+
+
+def test_four_rank_group_of_two_lockstep_pairs_matches_single_process(tmp_path):
+    """The plumbing of attention TP x expert parallel stages: 4 ranks in two data-parallel
+    groups of 2 lock-step ranks; requests spread over the groups, every rank of a group runs
+    them, the group's first rank reports the tokens."""
+    prompts = _prompts()
+    ref = asyncio.run(_run(ToyPipelineConfig(), prompts))
+    outs = asyncio.run(_run(_group_cfg(tmp_path, "dp", size=4, tp=2), prompts))
+    assert outs == ref
 
 
 def test_rank_group_dp_spreads_requests_and_survives_idle_ranks():
