@@ -288,18 +288,16 @@ class Code2WavGraphs:
 
     @torch.no_grad()
     def capture(self, B: int, W: int) -> None:
+        """Captured in the thread-local mode on a private stream (other stages' threads keep
+        running their GPU work meanwhile)."""
+        from ...utils.cuda_graph import capture_graph
+
         m = self.model
         dev = m.code_embedding.device
         codes = torch.zeros(B, m.cfg.num_quantizers, W, dtype=torch.long, device=dev)
         aux = m.make_aux(B, W, dev)
-        side = torch.cuda.Stream(device=dev)
-        side.wait_stream(torch.cuda.current_stream(dev))
-        with torch.cuda.stream(side):
-            m(codes, aux)            # warm-up: workspaces and kernel attributes outside the capture
-        torch.cuda.current_stream(dev).wait_stream(side)
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, pool=self._pool):
-            out = m(codes, aux)
+        with torch.cuda.device(dev):
+            g, out = capture_graph(lambda: m(codes, aux), warmup=1, pool=self._pool)
         self._pool = g.pool()
         self.graphs[(B, W)] = (g, codes, aux, out)
 
