@@ -53,6 +53,9 @@ def parse():
     ap.add_argument("--thinker", type=int, default=1, help="run the thinker serving phase (headline value)")
     ap.add_argument("--vision", type=int, default=1, help="also measure image+text -> text serving")
     ap.add_argument("--vision-requests", type=int, default=64)
+    ap.add_argument("--vision-group", type=int, default=1,
+                    help="N > 1: also serve image+text with one pipeline whose thinker is a TP x EP rank group "
+                         "over all GPUs")
     ap.add_argument("--vision-tokens", type=int, default=128)
     ap.add_argument("--ep", type=int, default=1,
                     help="N>1: experts sharded over the GPUs (expert parallel MoE over NVLink, data-parallel "
@@ -169,6 +172,62 @@ def vision_phase(args, dev, rank):
             return sum(r[1] for r in res) / wall, (1e3 * statistics.median(ttft) if ttft else None)
 
     return asyncio.run(run())
+
+
+def vision_group_phase(args, world):
+    """Image + text -> text through ONE pipeline whose thinker stage is a rank group over all
+    GPUs: attention tensor parallel inside data-parallel groups of min(4, N) ranks, MoE experts
+    over all N ranks (N=8: TP=4 x EP=8), 64 concurrent requests in total.  Runs on rank 0 (the
+    group's leader spawns one follower process per other GPU).  Returns (output tok/s, TTFT p50 ms)."""
+    import asyncio
+
+    import numpy as np
+
+    from sglang_omni_b200.client import Client, GenerateRequest, SamplingParams
+    from sglang_omni_b200.config import PipelineRunner, compile_pipeline
+    from sglang_omni_b200.models.qwen3_omni.config import Qwen3OmniPipelineConfig, text_stages
+
+    tp = min(4, world)
+    par = {"tp_size": tp, "ep_size": world, "gpus": list(range(world))}
+    cfg = Qwen3OmniPipelineConfig(model_path="random", stages=text_stages(
+        device="cuda:0", max_batch=args.vision_requests, max_context=2048, thinker_parallel=par))
+    rng = np.random.default_rng(29)
+    imgs = [rng.integers(0, 256, (448, 448, 3), dtype=np.uint8) for _ in range(args.vision_requests)]
+    letters = "abcdefghijklmnopqrstuvwxyz"
+    prompts = ["".join(rng.choice(list(letters), 128)) for _ in range(args.vision_requests)]
+
+    async def run():
+        coord, stages = compile_pipeline(cfg)
+        async with PipelineRunner(coord, stages):
+            client = Client(coord)
+
+            async def one(i, tag):
+                t0 = time.perf_counter()
+                req = GenerateRequest(prompt=prompts[i], images=[imgs[i]], max_tokens=args.vision_tokens,
+                                      sampling=SamplingParams(temperature=0.0, ignore_eos=True), stream=True,
+                                      request_id=f"{tag}-{i}")
+                first, ntok = None, 0
+                async for ch in client.generate(req):
+                    if ch.token_ids:
+                        if first is None:
+                            first = time.perf_counter() - t0
+                        ntok += len(ch.token_ids)
+                return first, ntok
+
+            await asyncio.gather(*[one(i, "gw") for i in range(min(8, args.vision_requests))])
+            t0 = time.perf_counter()
+            res = await asyncio.gather(*[one(i, "g") for i in range(args.vision_requests)])
+            wall = time.perf_counter() - t0
+            ttft = sorted(r[0] for r in res if r[0] is not None)
+            return sum(r[1] for r in res) / wall, (1e3 * statistics.median(ttft) if ttft else None)
+
+    tok_s, ttft = asyncio.run(run())
+    return {"thinker_parallel": f"tp{tp} x ep{world} (attention TP in {world // tp} data-parallel group(s), "
+                                f"experts over {world} GPUs)",
+            "requests": args.vision_requests, "output_tokens": args.vision_tokens,
+            "output_tok_s": None if tok_s is None else round(tok_s, 2),
+            "ttft_p50_ms": None if ttft is None else round(ttft, 2),
+            "timing": "host wall clock through Client.generate (stream=True), one pipeline on rank 0"}
 
 
 def s2pro_phase(args, dev, rank):
@@ -493,6 +552,14 @@ def main():
                "output_tok_s": None if v_tok_s is None else round(v_tok_s, 2),
                "ttft_p50_ms": None if v_ttft is None else round(v_ttft, 2),
                "timing": "host wall clock through Client.generate (stream=True), whole job; TTFT max over ranks"}
+    vis_group = None
+    if args.vision and args.vision_group and world > 1 and args.layers == 48:
+        if rank == 0:
+            try:
+                vis_group = vision_group_phase(args, world)
+            except Exception as exc:   # reported in the line; the headline number stands on its own
+                vis_group = {"error": f"{type(exc).__name__}: {exc}"[:400]}
+        dist.barrier()
     if rank == 0:
         line = {
             "metric": "output tok/s + p50 time-to-first-audio-chunk, Qwen3-Omni-30B-A3B, 1/2/4/8 B200",
@@ -531,6 +598,7 @@ def main():
             },
             "ttfa_p50_ms": None if ttfa_ms is None else round(ttfa_ms, 2),
             "vision_image_text": vis,
+            "vision_image_text_tp_ep": vis_group,
             "s2pro_tts": s2,
             "s2pro_tts_single_stream": s2c1,
             "e2e": {"value": round(e2e, 2), "unit": "output tokens/s, host wall clock through AREngine.generate",

@@ -24,10 +24,12 @@ _N = "sglang_omni_b200.models.qwen3_omni.pipeline.next_stage"
 
 
 def text_stages(overrides=None, device="cuda:0", max_batch=64, max_context=4096, speech=False, tail_frames=50,
-                first_chunk=4):
-    """``first_chunk``: frames of the first Code2Wav chunk (later chunks are 10 frames of 80 ms)."""
+                first_chunk=4, thinker_parallel: dict | None = None):
+    """``first_chunk``: frames of the first Code2Wav chunk (later chunks are 10 frames of 80 ms);
+    ``thinker_parallel``: ``tp_size`` / ``ep_size`` / ``gpus`` of a thinker rank group."""
     ov = {"overrides": overrides} if overrides else {}
-    thinker_args = {"device": device, "max_batch": max_batch, "max_context": max_context, **ov}
+    thinker_args = {"device": device, "max_batch": max_batch, "max_context": max_context, **ov,
+                    **(thinker_parallel or {})}
     if speech:
         thinker_args["speech_target"] = "talker_ar"
     stages = [
