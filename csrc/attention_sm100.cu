@@ -150,6 +150,15 @@ __device__ __forceinline__ float ex2_ftz(float x) {
   return y;
 }
 
+// A bounded wait whose outcome is the same in every lane of the warp (the warp-collective
+// tcgen05 loads / stores that follow must never run with part of the warp gone after a
+// timeout); `site` names the wait in the status code (16 + site).
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status,
+                                          int site) {
+  const bool ok = mbar_wait(bar, parity, abort_flag, status, kWaitTimeoutNs, kStatusWaitSite + site);
+  return __all_sync(0xffffffffu, ok);
+}
+
 // Row max of n raw scores with 8 independent partial maxima (no 64-long dependency chain).
 template <int N>
 __device__ __forceinline__ float row_max(const float (&s)[N]) {
@@ -228,7 +237,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int issued = 0;   // blocks whose loads were issued
       for (int j = 0; j < nb; ++j) {
         const int s = j & 1;
-        if (j >= kKvStages && !mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, p.status)) break;
+        if (j >= kKvStages && !mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, p.status, kWaitTimeoutNs,
+                                         kStatusWaitSite + 8))
+          break;
         issued = j + 1;
         mbar_arrive_expect_tx(&kv_full[s], 2 * kTileBytes);
         const int pages = (kv_len + 63) / 64;
@@ -253,10 +264,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     constexpr uint32_t idesc_s = umma_idesc_bf16_f32(kRows, kBN);
     constexpr uint32_t idesc_o = umma_idesc_bf16_f32_bmn(kRows, kD);
-    bool ok = nb > 0 && mbar_wait(q_full, 0, abort_flag, p.status);
+    bool ok = nb > 0 && warp_wait(q_full, 0, abort_flag, p.status, 5);
     auto issue_pv = [&](int j) -> bool {
       const int b = j & 1;
-      if (!mbar_wait(&p_full[b], (j >> 1) & 1, abort_flag, p.status)) return false;
+      if (!warp_wait(&p_full[b], (j >> 1) & 1, abort_flag, p.status, 6)) return false;
       tc_fence_after();
       if (lane == 0) {
         const uint32_t pa = smem_u32(sP + b * kTileBytes);
@@ -275,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     for (int j = 0; j < nb && ok; ++j) {
       const int s = j & 1;
-      if (!mbar_wait(&kv_full[s], (j >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
+      if (!warp_wait(&kv_full[s], (j >> 1) & 1, abort_flag, p.status, 7)) { ok = false; break; }
       tc_fence_after();
       if (lane == 0) {
         const uint32_t qa = smem_u32(sQ);
@@ -309,7 +320,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int j = 0; j < nb && ok; ++j) {
       const int b = j & 1;
-      if (!mbar_wait(&s_full[b], (j >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
+      if (!warp_wait(&s_full[b], (j >> 1) & 1, abort_flag, p.status, 1)) { ok = false; break; }
       tc_fence_after();
       float s[kBN];
       {
@@ -332,7 +343,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (mb > m_run + kRescaleThreshold || (m_run == -INFINITY && mb > -INFINITY)) {
         if (j > 0 && m_run > -INFINITY) {
           // O holds sum over earlier blocks at max m_run: rescale once the previous PV is done
-          if (!mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
+          if (!warp_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, p.status, 2)) { ok = false; break; }
           tc_fence_after();
           const float f = ex2_ftz(m_run - mb);
 #pragma unroll 1
@@ -351,7 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const float msub = m_run == -INFINITY ? 0.f : m_run;
       // P buffer b was last read by PV_{j-2}
-      if (j >= 2 && !mbar_wait(&pv_done[b], ((j - 2) >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
+      if (j >= 2 && !warp_wait(&pv_done[b], ((j - 2) >> 1) & 1, abort_flag, p.status, 3)) { ok = false; break; }
       uint8_t* prow = sP + b * kTileBytes + r * 128;
       float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -376,7 +387,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(&p_full[b]);
     }
     // epilogue: O / l once the last PV product is done
-    if (ok && nb > 0 && mbar_wait(&pv_done[(nb - 1) & 1], ((nb - 1) >> 1) & 1, abort_flag, p.status)) {
+    if (ok && nb > 0 && warp_wait(&pv_done[(nb - 1) & 1], ((nb - 1) >> 1) & 1, abort_flag, p.status, 4)) {
       tc_fence_after();
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
       __nv_bfloat16* orow =
@@ -505,7 +516,9 @@ __global__ void __launch_bounds__(pp::kThreads, 1)
       int issued = 0;   // blocks whose loads were issued
       for (int j = 0; j < nb; ++j) {
         const int s = j % kStages;
-        if (j >= kStages && !mbar_wait(&kv_empty[s], ((j / kStages) & 1) ^ 1, abort_flag, p.status)) break;
+        if (j >= kStages && !mbar_wait(&kv_empty[s], ((j / kStages) & 1) ^ 1, abort_flag, p.status, kWaitTimeoutNs,
+                                       kStatusWaitSite + 17))
+          break;
         issued = j + 1;
         mbar_arrive_expect_tx(&kv_full[s], 2 * kKVBytes);
         const int page = j < pages ? fa_page(p, req, j) : 0;
@@ -522,10 +535,10 @@ __global__ void __launch_bounds__(pp::kThreads, 1)
   } else if (warp == 1) {
     constexpr uint32_t idesc_s = umma_idesc_bf16_f32(kRows, kPBN);
     constexpr uint32_t idesc_o = umma_idesc_bf16_f32_bmn(kRows, kD);
-    bool ok = nb > 0 && mbar_wait(q_full, 0, abort_flag, p.status);
+    bool ok = nb > 0 && warp_wait(q_full, 0, abort_flag, p.status, 14);
     auto issue_s = [&](int t, int j) -> bool {
       const int s = j % kStages;
-      if (t == 0 && !mbar_wait(&kv_full[s], (j / kStages) & 1, abort_flag, p.status)) return false;
+      if (t == 0 && !warp_wait(&kv_full[s], (j / kStages) & 1, abort_flag, p.status, 15)) return false;
       tc_fence_after();
       if (lane == 0) {
         const uint32_t qa = smem_u32(smem + kQ + t * kQBytes);
@@ -542,7 +555,7 @@ __global__ void __launch_bounds__(pp::kThreads, 1)
       return true;
     };
     auto issue_pv = [&](int t, int j) -> bool {
-      if (!mbar_wait(&p_full[t], j & 1, abort_flag, p.status)) return false;
+      if (!warp_wait(&p_full[t], j & 1, abort_flag, p.status, 16)) return false;
       tc_fence_after();
       if (lane == 0) {
         const uint32_t pa = smem_u32(smem + kP + t * kPBytes);
@@ -584,7 +597,7 @@ __global__ void __launch_bounds__(pp::kThreads, 1)
     bool ok = true;
     uint8_t* prow = smem + kP + t * kPBytes + r * 128;
     for (int j = 0; j < nb && ok; ++j) {
-      if (!mbar_wait(&s_full[t], j & 1, abort_flag, p.status)) { ok = false; break; }
+      if (!warp_wait(&s_full[t], j & 1, abort_flag, p.status, 11)) { ok = false; break; }
       tc_fence_after();
       float s[kPBN];
       {
@@ -604,7 +617,7 @@ __global__ void __launch_bounds__(pp::kThreads, 1)
       const float mraw = row_max(s);
       const float mb = mraw == -INFINITY ? -INFINITY : mraw * p.scale_log2;   // log2 units
       // the previous PV of this tile has read P and (for a rescale) finished accumulating O
-      if (j > 0 && !mbar_wait(&pv_done[t], (j - 1) & 1, abort_flag, p.status)) { ok = false; break; }
+      if (j > 0 && !warp_wait(&pv_done[t], (j - 1) & 1, abort_flag, p.status, 12)) { ok = false; break; }
       if (mb > m_run + kRescaleThreshold || (m_run == -INFINITY && mb > -INFINITY)) {
         if (j > 0 && m_run > -INFINITY) {
           tc_fence_after();
@@ -647,7 +660,7 @@ __global__ void __launch_bounds__(pp::kThreads, 1)
     }
     __nv_bfloat16* orow =
         p.out + static_cast<int64_t>(q_begin + tok) * p.out_stride + static_cast<int64_t>(h * p.G + r % p.G) * kD;
-    if (ok && nb > 0 && mbar_wait(&pv_done[t], (nb - 1) & 1, abort_flag, p.status)) {
+    if (ok && nb > 0 && warp_wait(&pv_done[t], (nb - 1) & 1, abort_flag, p.status, 13)) {
       tc_fence_after();
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
 #pragma unroll 1

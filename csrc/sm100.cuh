@@ -25,6 +25,7 @@ enum StatusCode : int {
   kStatusPeerTimeout = 2,   // a peer flag (P2P / NVLS) never arrived
   kStatusBadShape = 3,      // a launch received an unsupported shape
   kStatusBounds = 4,        // a device bounds check fired (debug builds)
+  kStatusWaitSite = 16,     // 16 + k: the mbarrier wait at site k of a kernel timed out
 };
 
 // Default limit of one bounded wait: 2 s of wall clock.
@@ -83,7 +84,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
 // after `timeout_ns`; in the latter case it raises the flag and records the
 // status code itself.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int* status, uint64_t timeout_ns = kWaitTimeoutNs) {
+                                          int* status, uint64_t timeout_ns = kWaitTimeoutNs,
+                                          int code = kStatusMbarTimeout) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
@@ -95,7 +97,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     if (abort_flag != nullptr && *abort_flag) return false;
     if (globaltimer_ns() - t0 > timeout_ns) {
       if (abort_flag != nullptr) *abort_flag = 1;
-      record_status(status, kStatusMbarTimeout);
+      record_status(status, code);
       return false;
     }
   }

@@ -65,4 +65,7 @@ def check_status(device: torch.device | None = None) -> None:
     code = int(t.item())
     if code != 0:
         t.zero_()
-        raise RuntimeError(f"device kernel error {code}: {STATUS_MESSAGES.get(code, 'unknown')}")
+        msg = STATUS_MESSAGES.get(code)
+        if msg is None and code >= 16:
+            msg = f"mbarrier wait at site {code - 16} timed out inside a kernel"
+        raise RuntimeError(f"device kernel error {code}: {msg or 'unknown'}")

@@ -32,12 +32,12 @@ def prefill_tile_rows(head_dim: int, group: int, paged: bool = True, window: int
         return 64
     if group > PP_MAX_GROUP:
         return 128
-    # 256: two 128-row tiles per CTA whose softmax and tensor-core work overlap; 128: one tile
-    return int(os.environ.get("OMNI_FA_TILE_ROWS", "256"))
+    # 128: one tile per CTA; 256 (opt-in): two tiles whose softmax and tensor-core work overlap
+    return int(os.environ.get("OMNI_FA_TILE_ROWS", "128"))
 
 
-# The two-tile kernel serves GQA groups up to 8 query heads per KV head: a 16-head group did
-# not finish on the GPU (cause not found yet), so those shapes run the one-tile kernel.
+# The two-tile kernel is opt-in (OMNI_FA_TILE_ROWS=256): on long prompts after a cached prefix
+# with GQA groups of 8 and 16 query heads it did not finish on the GPU (cause not found yet).
 PP_MAX_GROUP = 8
 
 

@@ -67,7 +67,7 @@ def run(case: str) -> None:
         bt = torch.arange(1, R * pages + 1, dtype=torch.int32, device="cuda").view(R, pages)
         kl = torch.full((R,), P, dtype=torch.int32, device="cuda")
         cu = torch.arange(0, R * P + 1, P, dtype=torch.int32, device="cuda")
-        rows = int(os.environ.get("OMNI_BENCH_TILE_ROWS", "256"))   # 256 / 128: tcgen05 kernels, 64: mma.sync
+        rows = int(os.environ.get("OMNI_BENCH_TILE_ROWS", "128"))   # 128: tcgen05 kernel, 64: mma.sync
         tr, t0 = prefill_tiles([P] * R, hq // hkv, rows)
         tr = torch.tensor(tr, dtype=torch.int32, device="cuda")
         t0 = torch.tensor(t0, dtype=torch.int32, device="cuda")
@@ -189,7 +189,7 @@ def _time_cases() -> None:
     cu = torch.arange(0, R * P + 1, P, dtype=torch.int32, device="cuda")
     q = torch.randn(R * P, hq * d, device="cuda").bfloat16()
     f_attn = 4.0 * R * (P * (P + 1) / 2) * hq * d   # causal: QK^T + PV over the visible keys
-    for rows, tag in ((64, "mma.sync"), (128, "tcgen05"), (256, "tcgen05 2-tile")):
+    for rows, tag in ((64, "mma.sync"), (128, "tcgen05")):
         tr, t0 = prefill_tiles([P] * R, hq // hkv, rows)
         tr = torch.tensor(tr, dtype=torch.int32, device="cuda")
         t0 = torch.tensor(t0, dtype=torch.int32, device="cuda")
@@ -221,6 +221,29 @@ def _time_cases() -> None:
     ws = A.DecodeWorkspace(B, hq, d, 8192, "cuda")
     res["decode_attn B64 ctx1152 + one 8192"] = (t(lambda: A.decode_attention(q, ks, vs, bts, kls, hq, hkv, d, ws)),
                                                  2 * (63 * ctx + 8192) * hkv * d * 2)
+    # memory-bound prefill kernels (inputs larger than L2)
+    from .norm import rms_norm
+    from .rope import qkv_rope_store, rope_tables
+
+    xn = torch.randn(65536, 2048, device="cuda").bfloat16()
+    rn = torch.randn_like(xn)
+    wn = torch.randn(2048, device="cuda").bfloat16()
+    on = torch.empty_like(xn)
+    res["add + RMSNorm 65536x2048"] = (t(lambda: rms_norm(xn, wn, 1e-6, residual=rn, out=on), n=10),
+                                       4 * xn.numel() * 2)   # read x, residual; write residual, out
+    del xn, rn, on
+    T, hq, hkv, d = 65536, 32, 4, 128
+    qkv = torch.randn(T, (hq + 2 * hkv) * d, device="cuda").bfloat16()
+    cos, sin = rope_tables(d, 1e6, 8192, "cuda")
+    pos = torch.randint(0, 8192, (3, T), dtype=torch.int32, device="cuda")
+    kc = torch.zeros(T // 64 + 1, hkv, 64, d, device="cuda").bfloat16()
+    vc = torch.zeros_like(kc)
+    slots = torch.arange(64, T + 64, dtype=torch.int32, device="cuda")
+    qn = torch.ones(d, device="cuda").bfloat16()
+    res["QK-norm + M-RoPE + KV store 65536 tok"] = (
+        t(lambda: qkv_rope_store(qkv, hq, hkv, d, pos, cos, sin, q_norm=qn, k_norm=qn, mrope_section=[24, 20, 20],
+                                 slot_mapping=slots, k_cache=kc, v_cache=vc), n=10),
+        qkv.numel() * 2 + T * (hq + 2 * hkv) * d * 2)   # read q, k, v rows; write q in place, k / v pages
     for name, (us, nbytes) in res.items():
         print(f"{name:36s} {us:8.2f} us  {nbytes / us / 1e3:7.1f} GB/s")
 
