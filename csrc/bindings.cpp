@@ -411,6 +411,24 @@ void moe_combine(const torch::Tensor& y_perm, const torch::Tensor& inv_perm, con
   check_launch(omni::moe_combine(a, at::cuda::getCurrentCUDAStream()), "moe_combine");
 }
 
+void rope_half_inplace(torch::Tensor& x, int64_t heads, int64_t head_stride, int64_t rot, const torch::Tensor& cos,
+                       const torch::Tensor& sin) {
+  OMNI_CHECK_CUDA(x);
+  OMNI_CHECK_BF16(x);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x: [rows, cols] with unit column stride");
+  TORCH_CHECK(heads * head_stride <= x.size(1), "heads exceed the row");
+  TORCH_CHECK(cos.scalar_type() == at::kFloat && sin.scalar_type() == at::kFloat && cos.dim() == 2 &&
+                  cos.sizes() == sin.sizes() && cos.stride(1) == 1 && sin.stride(1) == 1 &&
+                  cos.stride(0) == sin.stride(0) && cos.size(0) >= x.size(0) && cos.size(1) >= rot,
+              "cos / sin: fp32 [rows, >= rot]");
+  const at::cuda::CUDAGuard guard(x.device());
+  check_launch(omni::rope_half_inplace(x.data_ptr(), x.stride(0), static_cast<int>(x.size(0)),
+                                       static_cast<int>(heads), static_cast<int>(head_stride),
+                                       static_cast<int>(rot), cos.data_ptr<float>(), sin.data_ptr<float>(),
+                                       cos.stride(0), at::cuda::getCurrentCUDAStream()),
+               "rope_half_inplace");
+}
+
 void embed(const torch::Tensor& ids, const torch::Tensor& table, torch::Tensor& out,
            const c10::optional<torch::Tensor>& mm_index, const c10::optional<torch::Tensor>& mm_embeds) {
   OMNI_CHECK_CUDA(ids);
@@ -870,6 +888,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("rows_per") = 0, py::arg("wait_flags") = py::none(), py::arg("wait_seq") = py::none(),
         py::arg("status") = py::none(), py::arg("timeout_s") = 2.0);
   m.def("embed", &embed, "embedding gather with multimodal overwrite");
+  m.def("rope_half_inplace", &rope_half_inplace, "in-place rotate-half RoPE with per-row angles");
   m.def("vq_embed", &vq_embed, "dual-AR input embedding with the scaled VQ codebook sum");
   m.def("ipc_alloc", &ipc_alloc, "cudaMalloc + zero, returns the device address");
   m.def("ipc_free", &ipc_free, "cudaFree");

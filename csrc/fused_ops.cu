@@ -13,6 +13,8 @@
 // FusedMoE routing (thinker.py:395-412, ming_omni/thinker.py:370-462), the
 // omni embedding injection (engines/omni/runtime/sglang_ar.py:548-701) and the
 // sampling path (engines/omni/runtime/sglang_ar.py:882-1032).
+#include <algorithm>
+
 #include <cuda_bf16.h>
 #include <float.h>
 #include <stdint.h>
@@ -1004,6 +1006,40 @@ cudaError_t vq_embed(const VqEmbedArgs& a, cudaStream_t stream) {
   if (a.tokens == 0) return cudaSuccess;
   if (a.hidden % 8 != 0 || a.ncb > 32 || a.ncb < 1) return cudaErrorInvalidValue;
   vq_embed_kernel<<<a.tokens, 128, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+namespace {
+// One thread per (row, head, pair i): x_i, x_{i+half} -> rotated in fp32, stored as bf16.
+__global__ void __launch_bounds__(256) rope_half_inplace_kernel(__nv_bfloat16* __restrict__ x, int64_t row_stride,
+                                                                int rows, int heads, int head_stride, int half,
+                                                                const float* __restrict__ cs,
+                                                                const float* __restrict__ sn, int64_t cs_stride) {
+  const int64_t total = static_cast<int64_t>(rows) * heads * half;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int i = static_cast<int>(idx % half);
+    const int64_t th = idx / half;
+    const int h = static_cast<int>(th % heads);
+    const int64_t t = th / heads;
+    __nv_bfloat16* p = x + t * row_stride + static_cast<int64_t>(h) * head_stride;
+    const float a = __bfloat162float(p[i]), b = __bfloat162float(p[i + half]);
+    const float* c = cs + t * cs_stride;
+    const float* s = sn + t * cs_stride;
+    p[i] = __float2bfloat16(a * c[i] - b * s[i]);
+    p[i + half] = __float2bfloat16(b * c[i + half] + a * s[i + half]);
+  }
+}
+}  // namespace
+
+cudaError_t rope_half_inplace(void* x, int64_t row_stride, int rows, int heads, int head_stride, int rot,
+                              const float* cos, const float* sin, int64_t cs_stride, cudaStream_t stream) {
+  if (rows == 0 || heads == 0) return cudaSuccess;
+  if (rot <= 0 || rot % 2 != 0 || rot > head_stride) return cudaErrorInvalidValue;
+  const int64_t total = static_cast<int64_t>(rows) * heads * (rot / 2);
+  const int64_t grid = std::min<int64_t>((total + 255) / 256, 148 * 16);
+  rope_half_inplace_kernel<<<static_cast<int>(grid), 256, 0, stream>>>(
+      static_cast<__nv_bfloat16*>(x), row_stride, rows, heads, head_stride, rot / 2, cos, sin, cs_stride);
   return cudaGetLastError();
 }
 

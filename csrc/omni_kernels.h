@@ -244,6 +244,12 @@ struct EmbedArgs {
 };
 cudaError_t embed(const EmbedArgs& a, cudaStream_t stream);
 
+// In-place rotate-half RoPE over the first `rot` dims of `heads` heads per row (head h at
+// column h * head_stride), angles given per row: cos / sin fp32 [rows, rot] (row stride cs_stride).
+// The vision tower's 2-D rotary embedding on the q and k heads of its fused QKV rows.
+cudaError_t rope_half_inplace(void* x, int64_t row_stride, int rows, int heads, int head_stride, int rot,
+                              const float* cos, const float* sin, int64_t cs_stride, cudaStream_t stream);
+
 // Dual-AR (S2-Pro) input embedding: token embedding plus, at VQ positions, the
 // sum of one codebook embedding per codebook, scaled:
 //   out[t] = vq(t) ? bf16(bf16(E[id] + bf16(sum_c CB[c * cb_size + code_c])) * scale) : E[id]

@@ -188,7 +188,10 @@ class Qwen3OmniAudioEncoder(nn.Module):
         for L in self.layers:
             n1 = ops.layer_norm(hs, L.ln1_w, L.ln1_b, 1e-5)
             qkv = ops.linear(n1, L.qkv_w, bias=L.qkv_b)
-            q, k, v = qkv[:, :d].contiguous(), qkv[:, d:2 * d].contiguous(), qkv[:, 2 * d:].contiguous()
+            if qkv.is_cuda:   # strided q / k / v views of the fused rows (the kernel takes row strides)
+                q, k, v = qkv[:, :d], qkv[:, d:2 * d], qkv[:, 2 * d:]
+            else:
+                q, k, v = qkv[:, :d].contiguous(), qkv[:, d:2 * d].contiguous(), qkv[:, 2 * d:].contiguous()
             a = ops.varlen_attention(q, k, v, cu, nh, nh, hd, q_lens=lens)
             hs = ops.linear(a, L.o_w, bias=L.o_b, residual=hs)
             n2 = ops.layer_norm(hs, L.ln2_w, L.ln2_b, 1e-5)

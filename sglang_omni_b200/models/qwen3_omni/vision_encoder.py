@@ -149,6 +149,24 @@ class Qwen3OmniVisionEncoder(nn.Module):
             c(M.fc2_w, sd[pre + "mlp.2.weight"]); c(M.fc2_b, sd[pre + "mlp.2.bias"])  # noqa: E702
 
     # ------------------------------------------------------------------ positions
+    def _per_grid(self, grids, what: str, device) -> torch.Tensor:
+        """Interpolated position embeddings ("pos", fp32) or rotary angles ("cos" / "sin", fp32)
+        of a batch of grids; each distinct (t, h, w) is computed once and kept (a batch of
+        same-size images repeats one grid)."""
+        cache = self.__dict__.setdefault("_grid_cache", {})
+        parts = []
+        for g in grids:
+            key = (tuple(int(v) for v in g), str(device))
+            hit = cache.get(key)
+            if hit is None:
+                pe = self._pos_embed([g]).to(device).float()
+                c, s_ = self._rope_cos_sin([g], device)
+                hit = {"pos": pe, "cos": c.float().contiguous(), "sin": s_.float().contiguous()}
+                if len(cache) < 256:
+                    cache[key] = hit
+            parts.append(hit[what])
+        return parts[0] if len(parts) == 1 else torch.cat(parts, 0)
+
     def _pos_embed(self, grids):
         cfg = self.cfg
         side = int(math.isqrt(cfg.num_position_embeddings))
@@ -192,8 +210,9 @@ class Qwen3OmniVisionEncoder(nn.Module):
         dev = self.patch_w.device
         nh, hd, kd, d = cfg.num_heads, cfg.head_dim, cfg.kernel_head_dim, cfg.hidden_size
         x = ops.linear(patches.to(dev, cfg.dtype).contiguous(), self.patch_w, bias=self.patch_b)
-        x = (x.float() + self._pos_embed(grids).to(dev)).to(cfg.dtype)
-        cos, sin = self._rope_cos_sin(grids, dev)
+        x = (x.float() + self._per_grid(grids, "pos", dev)).to(cfg.dtype)
+        cos = self._per_grid(grids, "cos", dev)
+        sin = self._per_grid(grids, "sin", dev)
         lens = [t * h * w for t, h, w in grids]
         cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32, device=dev)
         seq_lens = [h * w for t, h, w in grids for _ in range(t)]
@@ -202,15 +221,21 @@ class Qwen3OmniVisionEncoder(nn.Module):
         ds_out = []
         for li, B in enumerate(self.blocks):
             n1 = ops.layer_norm(x, B.n1_w, B.n1_b, 1e-6)
-            qkv = ops.linear(n1, B.qkv_w, bias=B.qkv_b).view(T, 3, nh, kd)
-            qk = qkv[:, :2, :, :hd].float()
-            qk = (qk * cos[:, None, None] + _rot_half(qk) * sin[:, None, None]).to(cfg.dtype)
-            q = torch.zeros(T, nh, kd, dtype=cfg.dtype, device=dev)
-            k = torch.zeros_like(q)
-            q[..., :hd], k[..., :hd] = qk[:, 0], qk[:, 1]
-            v = qkv[:, 2].contiguous()
-            a = ops.varlen_attention(q.view(T, -1), k.view(T, -1), v.view(T, -1), cu_att, nh, nh, kd,
-                                     scale=1.0 / math.sqrt(hd), q_lens=seq_lens)
+            qkv = ops.linear(n1, B.qkv_w, bias=B.qkv_b)
+            if qkv.is_cuda:
+                # RoPE in place on the q and k heads (their padding columns stay zero); q / k / v
+                # go to the attention as strided views of the fused rows
+                ops.rope_half_inplace(qkv, 2 * nh, kd, hd, cos, sin)
+                q, k, v = qkv[:, :nh * kd], qkv[:, nh * kd:2 * nh * kd], qkv[:, 2 * nh * kd:]
+            else:
+                qkv = qkv.view(T, 3, nh, kd)
+                qk = qkv[:, :2, :, :hd].float()
+                qk = (qk * cos[:, None, None] + _rot_half(qk) * sin[:, None, None]).to(cfg.dtype)
+                q = torch.zeros(T, nh, kd, dtype=cfg.dtype, device=dev)
+                k = torch.zeros_like(q)
+                q[..., :hd], k[..., :hd] = qk[:, 0], qk[:, 1]
+                q, k, v = q.view(T, -1), k.view(T, -1), qkv[:, 2].contiguous().view(T, -1)
+            a = ops.varlen_attention(q, k, v, cu_att, nh, nh, kd, scale=1.0 / math.sqrt(hd), q_lens=seq_lens)
             x = ops.linear(a, B.proj_w, bias=B.proj_b, residual=x)
             n2 = ops.layer_norm(x, B.n2_w, B.n2_b, 1e-6)
             f = ops.linear(n2, B.fc1_w, bias=B.fc1_b, act="gelu_tanh")

@@ -11,6 +11,8 @@ from __future__ import annotations
 
 import math
 import os
+import threading
+from collections import OrderedDict
 
 import torch
 import torch.nn.functional as F
@@ -146,22 +148,53 @@ def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqle
                                    v.reshape(T, num_kv_heads, head_dim), cu_seqlens, scale, causal, window)
         out.copy_(ref.reshape(out.shape))
         return out
+    lens = None
     if tiles is None:
         if q_lens is None:
             cu = cu_seqlens.tolist()
             q_lens = [cu[i + 1] - cu[i] for i in range(len(cu) - 1)]
-        req, tok0 = prefill_tiles(q_lens, num_heads // num_kv_heads)
-        tiles = (torch.tensor(req, dtype=torch.int32, device=q.device),
-                 torch.tensor(tok0, dtype=torch.int32, device=q.device))
-    lens = cu_seqlens[1:] - cu_seqlens[:-1]
+        tiles_req, tiles_tok0, lens = varlen_plan(q_lens, num_heads // num_kv_heads, q.device)
+        tiles = (tiles_req, tiles_tok0)
+    if lens is None:
+        lens = (cu_seqlens[1:] - cu_seqlens[:-1]).to(torch.int32)
     if _check.enabled():
         _check.check_range("varlen_attention", "cu_seqlens", cu_seqlens, 0, T + 1)
         if bool((lens < 0).any()):
             raise _check.LaunchCheckError("varlen_attention: cu_seqlens not monotone")
         _check.check_tiles("varlen_attention", tiles[0], tiles[1], cu_seqlens)
-    ext().attention_prefill(q, k, v, out, None, cu_seqlens, lens.to(torch.int32), cu_seqlens, tiles[0], tiles[1],
+    ext().attention_prefill(q, k, v, out, None, cu_seqlens, lens, cu_seqlens, tiles[0], tiles[1],
                             num_heads, num_kv_heads, head_dim, scale, causal, window)
     return out
+
+
+_PLANS: "OrderedDict[tuple, tuple]" = OrderedDict()
+_PLANS_LOCK = threading.Lock()
+_PLANS_MAX = 64
+
+
+def varlen_plan(q_lens: list[int], group: int, device) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Device tile table (request, first token) and lengths of a ragged batch, built once per
+    (lengths, group, device) and reused: an encoder calls the attention once per layer with the
+    same layout, and a fresh host-to-device upload per layer would stall the host on the stream."""
+    device = torch.device(device)
+    key = (tuple(int(n) for n in q_lens), int(group), device.index)
+    with _PLANS_LOCK:
+        hit = _PLANS.get(key)
+        if hit is not None:
+            _PLANS.move_to_end(key)
+            return hit[:3]
+    req, tok0 = prefill_tiles(list(key[0]), group)
+    n = len(req)
+    host = torch.tensor(req + tok0 + list(key[0]), dtype=torch.int32)
+    if device.type == "cuda":
+        host = host.pin_memory()
+    dev = host.to(device, non_blocking=True)
+    plan = (dev[:n], dev[n:2 * n], dev[2 * n:], host)   # the pinned source lives as long as the plan
+    with _PLANS_LOCK:
+        _PLANS[key] = plan
+        while len(_PLANS) > _PLANS_MAX:
+            _PLANS.popitem(last=False)
+    return plan[:3]
 
 
 _SM_COUNT: dict = {}

@@ -115,3 +115,20 @@ def qkv_rope_store(qkv: torch.Tensor, num_heads: int, num_kv_heads: int, head_di
                          list(mrope_section or [0, 0, 0]), interleaved, cos_tab, sin_tab, rot, neox, slot_mapping,
                          k_cache, v_cache)
     return qkv
+
+
+def rope_half_inplace(x: torch.Tensor, heads: int, head_stride: int, rot: int, cos: torch.Tensor,
+                      sin: torch.Tensor) -> torch.Tensor:
+    """In place on ``x`` [rows, cols] bf16: for each of ``heads`` heads (head h at column
+    h * head_stride) the first ``rot`` dims rotate by per-row angles, rotate-half style
+    (x1, x2) -> (x1 cos - x2 sin, x2 cos + x1 sin) in fp32 -- the vision tower's 2-D
+    rotary embedding (transformers' apply_rotary_pos_emb_vision).  cos / sin: fp32 [rows, rot]."""
+    if not x.is_cuda:
+        v = x.view(x.shape[0], -1)[:, :heads * head_stride].reshape(x.shape[0], heads, head_stride)
+        r = v[..., :rot].float()
+        h = rot // 2
+        rot_half = torch.cat([-r[..., h:], r[..., :h]], -1)
+        v[..., :rot] = (r * cos[:, None, :rot] + rot_half * sin[:, None, :rot]).to(x.dtype)
+        return x
+    ext().rope_half_inplace(x, heads, head_stride, rot, cos, sin)
+    return x

@@ -257,3 +257,23 @@ def test_sampling_topp_flat_row_full_sweep():
     allowed[order[keep]] = True
     assert bool(allowed[tok].all())
     assert len(set(tok.tolist())) > N // 3      # draws spread over the nucleus
+
+
+@pytest.mark.gpu
+def test_rope_half_inplace_matches_fp32_reference():
+    """The vision tower's in-place 2-D RoPE on padded q / k heads of fused QKV rows: rotated
+    columns match the fp32 rotate-half formula, padding columns and v stay untouched."""
+    from sglang_omni_b200.ops.rope import rope_half_inplace
+
+    T, nh, kd, hd = 300, 16, 80, 72
+    g = torch.Generator().manual_seed(3)
+    qkv = torch.randn(T, 3 * nh * kd, generator=g).bfloat16()
+    qkv.view(T, 3, nh, kd)[..., hd:] = 0
+    ang = torch.rand(T, hd // 2, generator=g) * 20
+    ang = torch.cat([ang, ang], -1)
+    cos, sin = ang.cos(), ang.sin()
+    ref = rope_half_inplace(qkv.clone(), 2 * nh, kd, hd, cos, sin)          # CPU: the torch formula
+    got = rope_half_inplace(qkv.cuda(), 2 * nh, kd, hd, cos.cuda(), sin.cuda()).cpu()
+    torch.testing.assert_close(got.float(), ref.float(), atol=1e-2, rtol=1e-2)
+    assert torch.equal(got.view(T, 3, nh, kd)[:, 2], qkv.view(T, 3, nh, kd)[:, 2])
+    assert not got.view(T, 3, nh, kd)[..., hd:].any()
