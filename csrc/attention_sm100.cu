@@ -340,12 +340,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const float mraw = row_max(s);
       const float mb = mraw == -INFINITY ? -INFINITY : mraw * p.scale_log2;   // log2 units
-      if (mb > m_run + kRescaleThreshold || (m_run == -INFINITY && mb > -INFINITY)) {
-        if (j > 0 && m_run > -INFINITY) {
+      // Lazy rescale, decided per row but executed per warp: the TMEM loads / stores are
+      // warp-collective, so when any row of the warp raises its max every lane takes the
+      // branch (rows that keep their max scale by 1).
+      const bool grow = mb > m_run + kRescaleThreshold || (m_run == -INFINITY && mb > -INFINITY);
+      if (__any_sync(0xffffffffu, grow)) {
+        const bool scale_o = grow && j > 0 && m_run > -INFINITY;
+        if (__any_sync(0xffffffffu, scale_o)) {
           // O holds sum over earlier blocks at max m_run: rescale once the previous PV is done
           if (!warp_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, p.status, 2)) { ok = false; break; }
           tc_fence_after();
-          const float f = ex2_ftz(m_run - mb);
+          const float f = scale_o ? ex2_ftz(m_run - mb) : 1.f;
 #pragma unroll 1
           for (int c = 0; c < kD; c += 32) {
             uint32_t v[32];
@@ -358,7 +363,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st_wait();
           l_run *= f;
         }
-        m_run = mb;
+        if (grow) m_run = mb;
       }
       const float msub = m_run == -INFINITY ? 0.f : m_run;
       // P buffer b was last read by PV_{j-2}
@@ -618,10 +623,13 @@ __global__ void __launch_bounds__(pp::kThreads, 1)
       const float mb = mraw == -INFINITY ? -INFINITY : mraw * p.scale_log2;   // log2 units
       // the previous PV of this tile has read P and (for a rescale) finished accumulating O
       if (j > 0 && !warp_wait(&pv_done[t], (j - 1) & 1, abort_flag, p.status, 12)) { ok = false; break; }
-      if (mb > m_run + kRescaleThreshold || (m_run == -INFINITY && mb > -INFINITY)) {
-        if (j > 0 && m_run > -INFINITY) {
+      // lazy rescale, warp-uniform (see the one-tile kernel)
+      const bool grow = mb > m_run + kRescaleThreshold || (m_run == -INFINITY && mb > -INFINITY);
+      if (__any_sync(0xffffffffu, grow)) {
+        const bool scale_o = grow && j > 0 && m_run > -INFINITY;
+        if (__any_sync(0xffffffffu, scale_o)) {
           tc_fence_after();
-          const float f = ex2_ftz(m_run - mb);
+          const float f = scale_o ? ex2_ftz(m_run - mb) : 1.f;
 #pragma unroll 1
           for (int c = 0; c < kD; c += 32) {
             uint32_t v[32];
@@ -634,7 +642,7 @@ __global__ void __launch_bounds__(pp::kThreads, 1)
           tmem_st_wait();
           l_run *= f;
         }
-        m_run = mb;
+        if (grow) m_run = mb;
       }
       const float msub = m_run == -INFINITY ? 0.f : m_run;
       float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};

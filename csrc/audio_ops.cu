@@ -131,6 +131,36 @@ __global__ void conv2d_im2col_kernel(const __nv_bfloat16* __restrict__ x, __nv_b
   }
 }
 
+// The same layout when C % 8 == 0 and rows are 16-byte aligned: one warp per (output row,
+// tap) copies the tap's C channels as 16-byte vectors (or zeros outside the input), so reads
+// and writes are contiguous 16 * C-byte runs and the index math is paid once per warp.
+__global__ void __launch_bounds__(256) conv2d_im2col_vec8_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                 __nv_bfloat16* __restrict__ out, int N, int H, int W,
+                                                                 int C, int Ho, int Wo, int kh, int kw, int stride,
+                                                                 int pad, int K_stride) {
+  const int lane = threadIdx.x & 31;
+  const int64_t items = static_cast<int64_t>(N) * Ho * Wo * kh * kw;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const int nv = C >> 3;
+  for (int64_t it = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); it < items;
+       it += warps) {
+    const int tap = static_cast<int>(it % (kh * kw));
+    const int64_t row = it / (kh * kw);
+    const int ky = tap / kw, kx = tap % kw;
+    const int wo = static_cast<int>(row % Wo);
+    const int ho = static_cast<int>((row / Wo) % Ho);
+    const int n = static_cast<int>(row / (static_cast<int64_t>(Wo) * Ho));
+    const int hi = ho * stride + ky - pad, wi = wo * stride + kx - pad;
+    uint4* dst = reinterpret_cast<uint4*>(out + row * K_stride + static_cast<int64_t>(tap) * C);
+    if (hi >= 0 && hi < H && wi >= 0 && wi < W) {
+      const uint4* src = reinterpret_cast<const uint4*>(x + ((static_cast<int64_t>(n) * H + hi) * W + wi) * C);
+      for (int v = lane; v < nv; v += 32) dst[v] = __ldg(src + v);
+    } else {
+      for (int v = lane; v < nv; v += 32) dst[v] = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+}
+
 int grid_for(int64_t n) {
   int64_t g = (n + 255) / 256;
   if (g > 148 * 16) g = 148 * 16;
@@ -182,6 +212,16 @@ cudaError_t conv2d_im2col(const void* x, void* out, int N, int H, int W, int C, 
                           int stride, int pad, int K_stride, cudaStream_t stream) {
   const int64_t n = static_cast<int64_t>(N) * Ho * Wo * kh * kw * C;
   if (n == 0) return cudaSuccess;
+  if (C % 8 == 0 && K_stride % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+    const int64_t warps = static_cast<int64_t>(N) * Ho * Wo * kh * kw;
+    int64_t grid = (warps + 7) / 8;
+    if (grid > 148 * 32) grid = 148 * 32;
+    conv2d_im2col_vec8_kernel<<<static_cast<int>(grid), 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(out), N, H, W, C, Ho, Wo, kh, kw, stride,
+        pad, K_stride);
+    return cudaGetLastError();
+  }
   conv2d_im2col_kernel<<<grid_for(n), 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x),
                                                         static_cast<__nv_bfloat16*>(out), N, H, W, C, Ho, Wo, kh, kw,
                                                         stride, pad, K_stride);

@@ -473,7 +473,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       decode_tile<BN>(t, prefix_s, offs_s, ends_s, groups, g, mt, nt);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, p.status)) break;
+      // warp-uniform outcome: the TMEM loads below are warp-collective
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, p.status))) break;
       tc_fence_after();
       const int m = mt * kBM + lane_base + lane;
       const int row0 = offs_s[g] + nt * BN;

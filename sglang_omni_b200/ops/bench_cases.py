@@ -178,6 +178,22 @@ def _time_cases() -> None:
         f = 2.0 * xx.shape[0] * xx.shape[1] * ww.shape[0]
         flops[name] = (t(lambda: L.linear(xx, ww)), f)
         flops[name + " (cuBLAS)"] = (t(lambda: F.linear(xx, ww)), f)
+    # encoder GEMMs: vision tower (64 images x 784 patches, d 1152, MLP 4304, QKV padded to 80 / head)
+    # and audio tower (32 x 10 s -> 4160 tokens, d 1280, MLP 5120)
+    enc = {
+        "vision qkv 50176x1152 -> 3840": (50176, 1152, 3840),
+        "vision fc1 50176x1152 -> 4304": (50176, 1152, 4304),
+        "vision fc2 50176x4304 -> 1152": (50176, 4304, 1152),
+        "audio qkv 4160x1280 -> 3840": (4160, 1280, 3840),
+        "audio fc1 4160x1280 -> 5120": (4160, 1280, 5120),
+    }
+    for name, (M, K, N) in enc.items():
+        xx = torch.randn(M, K, device="cuda").bfloat16()
+        ww = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
+        f = 2.0 * M * K * N
+        flops[name] = (t(lambda: L.linear(xx, ww), n=10), f)
+        flops[name + " (cuBLAS)"] = (t(lambda: F.linear(xx, ww), n=10), f)
+        del xx, ww
     # paged causal prefill attention, 8 x 1024 tokens, 32 q / 4 kv heads x 128 (half the QK^T / PV work is masked)
     from . import prefill_tiles
     R, P, hq, hkv, d = 8, 1024, 32, 4, 128
