@@ -89,12 +89,12 @@ class LogMel:
         return self.batch([audio])[0]
 
     def batch(self, audios: list[torch.Tensor]) -> list[torch.Tensor]:
-        """Log-mel of several waveforms with one DFT GEMM and one mel GEMM over all their
-        frames.  The bf16 range scales (frame peak before the DFT, power peak before the
-        mel projection) are per waveform and stay on the device: no host round trip."""
+        """Log-mel of several waveforms: waveforms of equal length are framed, scaled and
+        projected together (one DFT GEMM and one mel GEMM per length), with per-waveform bf16
+        range scales (frame peak before the DFT, power peak before the mel projection) kept
+        on the device: no host round trip and no per-waveform kernels."""
         if self.device.type != "cuda":
             return [self(a) for a in audios]
-        frames, counts = [], []
         # one pinned host buffer and one copy for every waveform of the batch (a pageable copy
         # per waveform blocks the host thread each time)
         host = [a.reshape(-1).to(torch.float32) for a in audios]
@@ -103,33 +103,33 @@ class LogMel:
             dev_waves = list(torch.split(flat, [h.numel() for h in host]))
         else:
             dev_waves = [h.to(self.device, non_blocking=True) for h in host]
-        for a in dev_waves:
-            x = torch.nn.functional.pad(a[None, None], (N_FFT // 2, N_FFT // 2), mode="reflect")[0, 0]
-            fr = x.unfold(0, N_FFT, HOP)[:-1]  # [T, 400]
-            frames.append(fr)
-            counts.append(fr.shape[0])
-        fa = torch.cat(frames, 0)
-        cnt = torch.tensor(counts, device=self.device)
+        groups: dict[int, list[int]] = {}
+        for i, w in enumerate(dev_waves):
+            groups.setdefault(w.numel(), []).append(i)
+        out: list = [None] * len(dev_waves)
+        for idxs in groups.values():
+            for i, m in zip(idxs, self._group(torch.stack([dev_waves[i] for i in idxs]))):
+                out[i] = m
+        return out
 
-        def per_wave_peak(t):   # [rows, ...] -> [rows, 1]: the peak of each row's waveform
-            peaks = torch.stack([seg.abs().amax() for seg in torch.split(t, counts)])
-            return torch.repeat_interleave(peaks.clamp_min(1e-20), cnt)[:, None]
-
+    def _group(self, x: torch.Tensor) -> torch.Tensor:
+        """x [b, N] equal-length waveforms -> [b, n_mels, N // 160]."""
+        b = x.shape[0]
+        xp = torch.nn.functional.pad(x[:, None], (N_FFT // 2, N_FFT // 2), mode="reflect")[:, 0]
+        fr = xp.unfold(1, N_FFT, HOP)[:, :-1]                       # [b, T, 400]
+        T = fr.shape[1]
         # scale into bf16 range well away from underflow, undo after squaring
-        scale = per_wave_peak(fa).clamp_min(1e-8)
-        f = fa / scale
+        scale = fr.abs().amax(dim=(1, 2), keepdim=True).clamp_min(1e-8)   # [b, 1, 1]
+        f = (fr / scale).reshape(b * T, N_FFT)
         f_hi = f.to(torch.bfloat16)
         f_lo = (f - f_hi.float()).to(torch.bfloat16)
         spec = linear(torch.cat([f_hi, f_hi, f_lo], 1).contiguous(), self.basis, out_dtype=torch.float32)
         re, im = spec[:, :201], spec[:, 201:402]
-        power = (re * re + im * im) * (scale * scale)  # [T, 201]
-        p = torch.zeros(power.shape[0], 208, dtype=torch.float32, device=self.device)
-        p[:, :201] = power
-        pmax = per_wave_peak(p)
-        mel = linear((p / pmax).to(torch.bfloat16), self.fb, out_dtype=torch.float32) * pmax   # [T, n_mels]
-        out = []
-        for m in torch.split(mel, counts):
-            log_spec = torch.clamp(m.t(), min=1e-10).log10()
-            log_spec = torch.maximum(log_spec, log_spec.max() - 8.0)
-            out.append((log_spec + 4.0) / 4.0)
-        return out
+        p = torch.zeros(b * T, 208, dtype=torch.float32, device=self.device)
+        p[:, :201] = (re * re + im * im).view(b, T, 201).mul_(scale * scale).view(b * T, 201)
+        pmax = p.view(b, T, 208).amax(dim=(1, 2), keepdim=True).clamp_min(1e-20)   # [b, 1, 1]
+        mel = linear((p.view(b, T, 208) / pmax).view(b * T, 208).to(torch.bfloat16), self.fb,
+                     out_dtype=torch.float32).view(b, T, -1) * pmax               # [b, T, n_mels]
+        log_spec = torch.clamp(mel, min=1e-10).log10()
+        log_spec = torch.maximum(log_spec, log_spec.amax(dim=(1, 2), keepdim=True) - 8.0)
+        return ((log_spec + 4.0) / 4.0).transpose(1, 2)

@@ -80,7 +80,8 @@ def test_logmel_batch_matches_single():
     """One batched call over waveforms of different lengths and loudness equals the per-waveform
     oracle (each waveform keeps its own bf16 range scales)."""
     torch.manual_seed(1)
-    audios = [torch.randn(16000 * 2) * 0.1, torch.randn(12345) * 3.0, torch.randn(4000) * 1e-3]
+    audios = [torch.randn(16000 * 2) * 0.1, torch.randn(12345) * 3.0, torch.randn(4000) * 1e-3,
+              torch.randn(16000 * 2) * 2.0]   # equal lengths are framed together, scales stay per waveform
     outs = LogMel(128, "cuda").batch(audios)
     cpu = LogMel(128, "cpu")
     for a, o in zip(audios, outs):
