@@ -43,7 +43,7 @@ def parse():
     ap.add_argument("--speech-streams", type=int, default=32)
     ap.add_argument("--speech-tokens", type=int, default=256)
     ap.add_argument("--speech-audio-s", type=float, default=10.0)
-    ap.add_argument("--speech-first-chunk", type=int, default=4, help="frames of the first Code2Wav chunk")
+    ap.add_argument("--speech-first-chunk", type=int, default=2, help="frames of the first Code2Wav chunk")
     ap.add_argument("--count-launches", type=int, default=1, help="count kernel launches in one extra untimed round")
     ap.add_argument("--s2pro", type=int, default=1, help="also measure the S2-Pro streaming TTS phase")
     ap.add_argument("--s2pro-streams", type=int, default=64)
@@ -165,9 +165,16 @@ def vision_phase(args, dev, rank):
                 return first, ntok
 
             await asyncio.gather(*[one(i, "vw") for i in range(min(4, args.vision_requests))])
+            from sglang_omni_b200.utils import trace
+
+            trace.clear()
             t0 = time.perf_counter()
             res = await asyncio.gather(*[one(i, "v") for i in range(args.vision_requests)])
             wall = time.perf_counter() - t0
+            if trace.ENABLED and rank == 0:   # OMNI_TRACE=1: median stage timeline of the measured requests
+                print(json.dumps({"vision_stage_timeline_ms": trace.summary(f"v-{rank}-"),
+                                  "batches": [(st, n, round(1e3 * sec, 1)) for st, n, sec in trace.batches()]}),
+                      file=sys.stderr)
             ttft = sorted(r[0] for r in res if r[0] is not None)
             return sum(r[1] for r in res) / wall, (1e3 * statistics.median(ttft) if ttft else None)
 

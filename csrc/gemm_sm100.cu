@@ -53,6 +53,8 @@ struct DevParams {
   int a_rows;
   int k;
   int groups;
+  int m_tiles;           // weight tiles of the output (dense GEMMs)
+  int mt_fast;           // 1: tile order walks the weight tiles fastest (large token operand)
   int out_f32;
   int act;
   int* status;
@@ -207,9 +209,13 @@ struct Cfg {
 };
 
 // Tile t -> group g, weight tile mt, token tile nt.  Group g's rows are [offs[g], ends[g]).
+// Order: token tiles fastest (a weight tile stays hot while the CTAs of a wave walk the token
+// tiles: decode and MoE, where the weights are the big operand), or with `mt_fast` weight tiles
+// fastest (a dense GEMM whose token operand is larger than L2: the CTAs of a wave share a few
+// token tiles, each read from DRAM once, while the weights stay in L2).
 template <int BN>
 __device__ __forceinline__ void decode_tile(int t, const int* prefix, const int* offs, const int* ends, int groups,
-                                            int& g, int& mt, int& nt) {
+                                            int& g, int& mt, int& nt, int mtiles = 0, int mt_fast = 0) {
   int lo = 0, hi = groups - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
@@ -217,6 +223,11 @@ __device__ __forceinline__ void decode_tile(int t, const int* prefix, const int*
   }
   g = lo;
   const int local = t - prefix[g];
+  if (mt_fast) {
+    nt = local / mtiles;
+    mt = local - nt * mtiles;
+    return;
+  }
   const int rows = ends[g] - offs[g];
   const int ntiles = (rows + BN - 1) / BN;
   mt = local / ntiles;
@@ -343,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int w = blockIdx.x;
         const int t = w / ks, split = w - t * ks;
         int g, mt, nt;
-        decode_tile<BN>(t, prefix_s, offs_s, ends_s, groups, g, mt, nt);
+        decode_tile<BN>(t, prefix_s, offs_s, ends_s, groups, g, mt, nt, p.m_tiles, p.mt_fast);
         const int a_row = g * p.a_rows + mt * kBM;
         const int kb0 = split * kb_per, kb1 = min(num_kb, kb0 + kb_per);
         pre = min(C::kStages, kb1 - kb0);
@@ -380,7 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int w = blockIdx.x; w < total_work && ok; w += gridDim.x) {
         const int t = w / ks, split = w - t * ks;
         int g, mt, nt;
-        decode_tile<BN>(t, prefix_s, offs_s, ends_s, groups, g, mt, nt);
+        decode_tile<BN>(t, prefix_s, offs_s, ends_s, groups, g, mt, nt, p.m_tiles, p.mt_fast);
         const int a_row = g * p.a_rows + mt * kBM;
         const int b_row = offs_s[g] + nt * BN;
         const int kb0 = split * kb_per, kb1 = min(num_kb, kb0 + kb_per);
@@ -470,7 +481,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int w = blockIdx.x; w < total_work; w += gridDim.x, ++local) {
       const int t = w / ks;
       int g, mt, nt;
-      decode_tile<BN>(t, prefix_s, offs_s, ends_s, groups, g, mt, nt);
+      decode_tile<BN>(t, prefix_s, offs_s, ends_s, groups, g, mt, nt, p.m_tiles, p.mt_fast);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       // warp-uniform outcome: the TMEM loads below are warp-collective
@@ -688,7 +699,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int t = static_cast<int>(blockIdx.x) / ks;
       const uint32_t rank = cluster_ctarank();
       int g, mt, nt;
-      decode_tile<BN>(t, prefix_s, offs_s, ends_s, groups, g, mt, nt);
+      decode_tile<BN>(t, prefix_s, offs_s, ends_s, groups, g, mt, nt, p.m_tiles, p.mt_fast);
       const int row0 = offs_s[g] + nt * BN;
       const int row_end = ends_s[g];
       const int per = (BN + ks - 1) / ks;
@@ -887,6 +898,13 @@ cudaError_t launch(const GemmArgs& a, cudaStream_t stream) {
   p.zero_n = a.zero_n;
   const int m_tiles = (a.m_out + kBM - 1) / kBM;
   const int num_kb = (a.k + kBK - 1) / kBK;
+  p.m_tiles = m_tiles;
+  {
+    // a dense GEMM whose token operand exceeds L2 while its weights fit: weight tiles fastest
+    const double w_bytes = static_cast<double>(a.m_out) * (GATED ? 2 : 1) * a.k * 2.0;
+    const double x_bytes = static_cast<double>(a.rows) * a.k * 2.0;
+    p.mt_fast = (a.groups == 1 && a.offsets == nullptr && a.seg_cap <= 0 && x_bytes > 64e6 && w_bytes <= 64e6) ? 1 : 0;
+  }
   // Split-K for dense GEMMs that would leave most SMs idle (decode projections).
   p.cluster_splitk = 0;
   if (!GATED && a.offsets == nullptr && a.seg_cap <= 0 && (a.splitk_ws != nullptr || a.splitk_cluster)) {

@@ -211,7 +211,11 @@ def create_image_encoder_executor(model_path: str = "", device: str = "cuda:0", 
     def encode(inputs: dict) -> list:
         per_req = inputs["images"]
         flat = [im for ims in per_req for im in ims]
+        t0 = time.perf_counter()
         out = encode_images(model_path, dev, flat, overrides) if flat else None
+        if trace.ENABLED and flat:
+            torch.cuda.synchronize(dev) if dev.type == "cuda" else None
+            trace.batch("image_encode", len(flat), time.perf_counter() - t0)
         res, i = [], 0
         for ims in per_req:
             n = len(ims)
@@ -225,11 +229,15 @@ def create_image_encoder_executor(model_path: str = "", device: str = "cuda:0", 
 
     def request_builder(payload: StagePayload):
         images = (payload.data or {}).get("images") or []
+        if images:
+            trace.mark(payload.request_id, "0c_image_encoder_queued")
         return EncoderRequestData(inputs={"images": images}, skip=not images)
 
     def result_builder(payload: StagePayload, out):
         if not isinstance(out, dict):  # skipped request (no image)
             out = {"image_embeds": None}
+        else:
+            trace.mark(payload.request_id, "1c_image_encoded")
         return StagePayload(payload.request_id, payload.request, out)
 
     return EngineExecutor(engine, request_builder, result_builder)

@@ -279,6 +279,41 @@ def image_to_patches(img: np.ndarray, cfg: VisionConfig, size: int | None = None
     return torch.from_numpy(np.ascontiguousarray(x).reshape(gh * gw, -1)), (1, gh, gw)
 
 
+def images_to_patches_device(images: list[np.ndarray], cfg: VisionConfig, device) -> tuple[torch.Tensor, list]:
+    """``image_to_patches`` for a batch on the GPU: the uint8 pixels travel (one pinned copy per
+    image shape), the nearest resize, normalisation, temporal repeat and merge-block patch order
+    run as device ops.  Returns (patches [sum N_i, patch_dim] fp32 in input order, grids)."""
+    p, ms, tp = cfg.patch_size, cfg.spatial_merge_size, cfg.temporal_patch_size
+    unit = p * ms
+    mean = torch.tensor(IMAGE_MEAN, dtype=torch.float32, device=device)
+    std = torch.tensor(IMAGE_STD, dtype=torch.float32, device=device)
+    by_shape: dict[tuple, list[int]] = {}
+    for i, im in enumerate(images):
+        by_shape.setdefault(tuple(im.shape), []).append(i)
+    parts: list = [None] * len(images)
+    grids: list = [None] * len(images)
+    for shape, idxs in by_shape.items():
+        H, W = shape[:2]
+        th = max(unit, round(H / unit) * unit)
+        tw = max(unit, round(W / unit) * unit)
+        host = torch.from_numpy(np.ascontiguousarray(np.stack([images[i] for i in idxs]))).pin_memory()
+        x = host.to(device, non_blocking=True)                                # [b, H, W, 3] uint8
+        if (th, tw) != (H, W):
+            yi = torch.from_numpy((np.arange(th) * H / th).astype(np.int64)).to(device)
+            xi = torch.from_numpy((np.arange(tw) * W / tw).astype(np.int64)).to(device)
+            x = x.index_select(1, yi).index_select(2, xi)
+        x = (x.float() / 255.0 - mean) / std                                   # [b, th, tw, 3]
+        b = x.shape[0]
+        gh, gw = th // p, tw // p
+        x = x.permute(0, 3, 1, 2)[:, None].expand(b, tp, 3, th, tw)           # [b, tp, C, H, W]
+        x = x.reshape(b, tp, 3, gh // ms, ms, p, gw // ms, ms, p)
+        x = x.permute(0, 3, 6, 4, 7, 2, 1, 5, 8).reshape(b, gh * gw, -1)      # bh, bw, mh, mw, C, tp, ph, pw
+        for j, i in enumerate(idxs):
+            parts[i] = x[j]
+            grids[i] = (1, gh, gw)
+    return torch.cat(parts, 0), grids
+
+
 def video_to_patches(frames: np.ndarray, cfg: VisionConfig, max_pixels: int = 448 * 448):
     """uint8 RGB frames [N, H, W, 3] (N a multiple of the temporal patch) -> (patches
     [t * gh * gw, patch_dim] float32, grid (t, gh, gw)): every frame resized (nearest) to the
@@ -309,14 +344,25 @@ def encode_images(model_path: str, device, images: list, overrides: dict | None 
     from . import loader
 
     enc = loader.get_vision_encoder(model_path, device, overrides)
-    patches, grids = [], []
-    for im in images:
+    dev = torch.device(device)
+    still = [i for i, im in enumerate(images) if not isinstance(im, dict)]
+    patches, grids = [None] * len(images), [None] * len(images)
+    if still and dev.type == "cuda":
+        # images: patch extraction on the GPU (the host only ships uint8 pixels)
+        pt, gs = images_to_patches_device([np.asarray(images[i], dtype=np.uint8) for i in still], enc.cfg, dev)
+        ofs = 0
+        for i, g in zip(still, gs):
+            n = g[0] * g[1] * g[2]
+            patches[i], grids[i] = pt[ofs:ofs + n], g
+            ofs += n
+    for i, im in enumerate(images):
+        if patches[i] is not None:
+            continue
         if isinstance(im, dict):
             pt, g = video_to_patches(np.asarray(im["frames"], dtype=np.uint8), enc.cfg)
         else:
             pt, g = image_to_patches(np.asarray(im, dtype=np.uint8), enc.cfg)
-        patches.append(pt)
-        grids.append(g)
+        patches[i], grids[i] = pt.to(dev), g
     emb, ds = enc(torch.cat(patches, 0), grids)
     ms2 = enc.cfg.spatial_merge_size ** 2
     counts = [t * h * w // ms2 for t, h, w in grids]

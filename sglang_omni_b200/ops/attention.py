@@ -32,15 +32,8 @@ def prefill_tile_rows(head_dim: int, group: int, paged: bool = True, window: int
         return 64
     if not (paged and head_dim == 128 and window == 0 and 128 % max(1, group) == 0):
         return 64
-    if group > PP_MAX_GROUP:
-        return 128
-    # 128: one tile per CTA; 256 (opt-in): two tiles whose softmax and tensor-core work overlap
-    return int(os.environ.get("OMNI_FA_TILE_ROWS", "128"))
-
-
-# The two-tile kernel is opt-in (OMNI_FA_TILE_ROWS=256): on long prompts after a cached prefix
-# with GQA groups of 8 and 16 query heads it did not finish on the GPU (cause not found yet).
-PP_MAX_GROUP = 8
+    # 256: two 128-row tiles per CTA whose softmax and tensor-core work overlap; 128: one tile
+    return int(os.environ.get("OMNI_FA_TILE_ROWS", "256"))
 
 
 def prefill_tiles(q_lens: list[int], group: int, rows: int = 64) -> tuple[list[int], list[int]]:
@@ -122,8 +115,6 @@ def prefill_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Ten
                                   k_cache, v_cache, block_table, cu_q, kv_lens, scale, causal)
         out.copy_(ref.reshape(out.shape))
         return out
-    if tile_rows == 256 and num_heads // num_kv_heads > PP_MAX_GROUP:
-        raise ValueError(f"256-row tiles serve GQA groups of at most {PP_MAX_GROUP} heads")
     if _check.enabled():
         _check.check_paged("attention_prefill", block_table, kv_lens, k_cache.shape[0], cu_q, q.shape[0])
         _check.check_tiles("attention_prefill", tile_req, tile_tok0, cu_q)

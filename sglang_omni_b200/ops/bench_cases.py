@@ -67,7 +67,7 @@ def run(case: str) -> None:
         bt = torch.arange(1, R * pages + 1, dtype=torch.int32, device="cuda").view(R, pages)
         kl = torch.full((R,), P, dtype=torch.int32, device="cuda")
         cu = torch.arange(0, R * P + 1, P, dtype=torch.int32, device="cuda")
-        rows = int(os.environ.get("OMNI_BENCH_TILE_ROWS", "128"))   # 128: tcgen05 kernel, 64: mma.sync
+        rows = int(os.environ.get("OMNI_BENCH_TILE_ROWS", "256"))   # 256 / 128: tcgen05 kernels, 64: mma.sync
         tr, t0 = prefill_tiles([P] * R, hq // hkv, rows)
         tr = torch.tensor(tr, dtype=torch.int32, device="cuda")
         t0 = torch.tensor(t0, dtype=torch.int32, device="cuda")
@@ -205,7 +205,7 @@ def _time_cases() -> None:
     cu = torch.arange(0, R * P + 1, P, dtype=torch.int32, device="cuda")
     q = torch.randn(R * P, hq * d, device="cuda").bfloat16()
     f_attn = 4.0 * R * (P * (P + 1) / 2) * hq * d   # causal: QK^T + PV over the visible keys
-    for rows, tag in ((64, "mma.sync"), (128, "tcgen05")):
+    for rows, tag in ((64, "mma.sync"), (128, "tcgen05"), (256, "tcgen05 2-tile")):
         tr, t0 = prefill_tiles([P] * R, hq // hkv, rows)
         tr = torch.tensor(tr, dtype=torch.int32, device="cuda")
         t0 = torch.tensor(t0, dtype=torch.int32, device="cuda")

@@ -16,6 +16,7 @@ import time
 ENABLED = os.environ.get("OMNI_TRACE", "0") not in ("", "0")
 _lock = threading.Lock()
 _events: dict[str, dict[str, float]] = {}
+_batches: list[tuple[str, int, float]] = []
 
 
 def mark(rid: str, event: str) -> None:
@@ -31,6 +32,7 @@ def mark(rid: str, event: str) -> None:
 def clear() -> None:
     with _lock:
         _events.clear()
+        _batches.clear()
 
 
 def summary(prefix: str = "") -> dict[str, float]:
@@ -43,9 +45,6 @@ def summary(prefix: str = "") -> dict[str, float]:
         for k, v in ev.items():
             out.setdefault(k, []).append(1e3 * (v - t0))
     return {k: round(statistics.median(v), 2) for k, v in sorted(out.items(), key=lambda kv: statistics.median(kv[1]))}
-
-
-_batches: list[tuple[str, int, float]] = []
 
 
 def batch(stage: str, size: int, seconds: float) -> None:

@@ -79,3 +79,22 @@ def test_vision_video_matches_hf_cpu():
         out, ds = ours(px, [grid])
     ref_main = ref.pooler_output if getattr(ref, "pooler_output", None) is not None else ref.last_hidden_state
     assert (out - ref_main).abs().max() / ref_main.abs().max() < 1e-3
+
+
+@pytest.mark.gpu
+def test_device_patch_extraction_matches_host():
+    """Images patchified on the GPU (batched per shape, nearest resize included) equal the host
+    path, in input order."""
+    import numpy as np
+
+    from sglang_omni_b200.models.qwen3_omni.vision_encoder import (VisionConfig, image_to_patches,
+                                                                    images_to_patches_device)
+
+    cfg = VisionConfig()
+    rng = np.random.default_rng(0)
+    imgs = [rng.integers(0, 256, s, dtype=np.uint8) for s in [(448, 448, 3), (300, 500, 3), (448, 448, 3), (64, 96, 3)]]
+    got, grids = images_to_patches_device(imgs, cfg, torch.device("cuda", 0))
+    refs = [image_to_patches(im, cfg) for im in imgs]
+    assert grids == [g for _, g in refs]
+    ref = torch.cat([p for p, _ in refs], 0)
+    torch.testing.assert_close(got.cpu(), ref, atol=1e-6, rtol=1e-6)
