@@ -194,7 +194,7 @@ __global__ void __launch_bounds__(256) qkv_rope_store_kernel(RopeStoreArgs a) {
 // e +- rot/2 sits in the same register of lane l +- rot/8 (a shuffle), the interleaved partner
 // e ^ 1 in the lane's own registers.  Every head's row load of the warp is issued before the
 // first use.
-constexpr int kRopeHeadsPerWarp = 4;
+constexpr int kRopeHeadsPerWarp = 8;
 
 __device__ __forceinline__ void load4_bf16(const __nv_bfloat16* p, float (&v)[4]) {
   const uint2 u = *reinterpret_cast<const uint2*>(p);
@@ -212,7 +212,7 @@ __device__ __forceinline__ void store4_bf16(__nv_bfloat16* p, const float (&v)[4
   *reinterpret_cast<uint2*>(p) = u;
 }
 
-__global__ void __launch_bounds__(256) qkv_rope_store_d128_kernel(RopeStoreArgs a) {
+__global__ void __launch_bounds__(128) qkv_rope_store_d128_kernel(RopeStoreArgs a) {
   grid_dep_launch();  // a dependent GEMM may start its prologue now
   constexpr int D = 128;
   const int heads = a.hq + 2 * a.hkv;
@@ -956,7 +956,9 @@ cudaError_t qkv_rope_store(const RopeStoreArgs& a, cudaStream_t stream) {
   if (a.head_dim == 128 && a.rot_dim % 8 == 0 && a.rot_dim <= 128 && vec_ok) {
     const int chunks = (a.hq + 2 * a.hkv + kRopeHeadsPerWarp - 1) / kRopeHeadsPerWarp;
     const long warps = static_cast<long>(a.tokens) * chunks;
-    qkv_rope_store_d128_kernel<<<(warps + 7) / 8, threads, 0, stream>>>(a);
+    // 128-thread blocks: at 90 registers a thread, five resident blocks keep more rows in flight
+    // per SM than two 256-thread blocks would
+    qkv_rope_store_d128_kernel<<<(warps + 3) / 4, 128, 0, stream>>>(a);
     return cudaGetLastError();
   }
   const long warps = static_cast<long>(a.tokens) * (a.hq + 2 * a.hkv);

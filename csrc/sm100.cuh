@@ -231,9 +231,16 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16_f32(int m, int n) {
 // small numeric helpers
 // ----------------------------------------------------------------------------
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+// tanh on the SFU (tanh.approx.f32, one instruction; relative error ~2^-11, below the bf16
+// rounding of the GEMM output this feeds).
+__device__ __forceinline__ float tanh_sfu(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ float gelu_tanh_f(float x) {
   const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
-  return 0.5f * x * (1.0f + tanhf(k0 * (x + 0.044715f * x * x * x)));
+  return 0.5f * x * (1.0f + tanh_sfu(k0 * (x + 0.044715f * x * x * x)));
 }
 __device__ __forceinline__ float gelu_erf_f(float x) { return 0.5f * x * (1.0f + erff(x * 0.7071067811865476f)); }
 

@@ -214,7 +214,8 @@ def create_image_encoder_executor(model_path: str = "", device: str = "cuda:0", 
         t0 = time.perf_counter()
         out = encode_images(model_path, dev, flat, overrides) if flat else None
         if trace.ENABLED and flat:
-            torch.cuda.synchronize(dev) if dev.type == "cuda" else None
+            if dev.type == "cuda":   # this stream only: another stage may be capturing a graph
+                torch.cuda.current_stream(dev).synchronize()
             trace.batch("image_encode", len(flat), time.perf_counter() - t0)
         res, i = [], 0
         for ims in per_req:
