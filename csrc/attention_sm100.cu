@@ -83,6 +83,8 @@ struct FaParams {
   int64_t out_stride;
   int num_pages;
   int* status;
+  const int* cu_kv;   // contiguous mode: first key row of each request (nullptr: paged)
+  int d_head;         // head dim of q / k / v / out rows (<= 128; columns past it load as zeros)
 };
 
 __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
@@ -135,6 +137,29 @@ constexpr uint32_t umma_idesc_bf16_f32_bmn(int m, int n) { return umma_idesc_bf1
 __device__ __forceinline__ int fa_page(const FaParams& p, int req, int idx) {
   const int page = p.block_table[static_cast<int64_t>(req) * p.bt_stride + idx];
   return (p.num_pages > 0 && static_cast<unsigned>(page) >= static_cast<unsigned>(p.num_pages)) ? 0 : page;
+}
+
+// Issues the TMA loads of one 64-key half block: paged (one page of the block table) or
+// contiguous (64 consecutive key rows of head h starting at the request's first key + key0).
+__device__ __forceinline__ void load_kv_half(const FaParams& p, const CUtensorMap* tmap_k, const CUtensorMap* tmap_v,
+                                             uint64_t* bar, uint8_t* dk, uint8_t* dv, int region_bytes, int req,
+                                             int h, int key0, int pages) {
+  if (p.cu_kv == nullptr) {
+    const int idx = key0 >> 6;
+    // a page past the context reads page 0 (masked): constant byte count
+    const int page = idx < pages ? fa_page(p, req, idx) : 0;
+    const int row = (page * p.hkv + h) * 64;
+    for (int r = 0; r < 2; ++r) {
+      tma_load_2d(dk + r * region_bytes, tmap_k, bar, r * 64, row);
+      tma_load_2d(dv + r * region_bytes, tmap_v, bar, r * 64, row);
+    }
+  } else {
+    const int row = p.cu_kv[req] + key0;   // rows past the tensor read zeros, other requests' are masked
+    for (int r = 0; r < 2; ++r) {
+      tma_load_3d(dk + r * region_bytes, tmap_k, bar, r * 64, h, row);
+      tma_load_3d(dv + r * region_bytes, tmap_v, bar, r * 64, h, row);
+    }
+  }
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
@@ -243,16 +268,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         issued = j + 1;
         mbar_arrive_expect_tx(&kv_full[s], 2 * kTileBytes);
         const int pages = (kv_len + 63) / 64;
-        for (int pg = 0; pg < 2; ++pg) {
-          const int idx = 2 * j + pg;
-          // a block's second page past the context reads page 0 (masked): constant byte count
-          const int page = idx < pages ? fa_page(p, req, idx) : 0;
-          const int row = (page * p.hkv + h) * 64;
-          for (int r = 0; r < 2; ++r) {
-            tma_load_2d(sK + s * kTileBytes + r * kRegion + pg * (kRegion / 2), &tmap_k, &kv_full[s], r * 64, row);
-            tma_load_2d(sV + s * kTileBytes + r * kRegion + pg * (kRegion / 2), &tmap_v, &kv_full[s], r * 64, row);
-          }
-        }
+        for (int pg = 0; pg < 2; ++pg)
+          load_kv_half(p, &tmap_k, &tmap_v, &kv_full[s], sK + s * kTileBytes + pg * (kRegion / 2),
+                       sV + s * kTileBytes + pg * (kRegion / 2), kRegion, req, h, j * kBN + pg * 64, pages);
       }
       // drain: every issued load has landed before the CTA's shared memory goes away (also
       // after an aborted wait, so no late copy writes into the next CTA on this SM)
@@ -395,8 +413,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok && nb > 0 && warp_wait(&pv_done[(nb - 1) & 1], ((nb - 1) >> 1) & 1, abort_flag, p.status, 4)) {
       tc_fence_after();
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      __nv_bfloat16* orow =
-          p.out + static_cast<int64_t>(q_begin + tok) * p.out_stride + static_cast<int64_t>(h * p.G + r % p.G) * kD;
+      __nv_bfloat16* orow = p.out + static_cast<int64_t>(q_begin + tok) * p.out_stride +
+                            static_cast<int64_t>(h * p.G + r % p.G) * p.d_head;
 #pragma unroll 1
       for (int c = 0; c < kD; c += 32) {
         uint32_t v[32];
@@ -405,6 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (row_ok) {
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
+            if (c + i >= p.d_head) break;
             uint4 o;
             o.x = pack_bf16x2(__uint_as_float(v[i]) * inv, __uint_as_float(v[i + 1]) * inv);
             o.y = pack_bf16x2(__uint_as_float(v[i + 2]) * inv, __uint_as_float(v[i + 3]) * inv);
@@ -415,9 +434,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     } else if (nb == 0 && row_ok) {
-      __nv_bfloat16* orow =
-          p.out + static_cast<int64_t>(q_begin + tok) * p.out_stride + static_cast<int64_t>(h * p.G + r % p.G) * kD;
-      for (int c = 0; c < kD; c += 8) *reinterpret_cast<uint4*>(orow + c) = make_uint4(0u, 0u, 0u, 0u);
+      __nv_bfloat16* orow = p.out + static_cast<int64_t>(q_begin + tok) * p.out_stride +
+                            static_cast<int64_t>(h * p.G + r % p.G) * p.d_head;
+      for (int c = 0; c < p.d_head; c += 8) *reinterpret_cast<uint4*>(orow + c) = make_uint4(0u, 0u, 0u, 0u);
     }
   }
 
@@ -526,12 +545,8 @@ __global__ void __launch_bounds__(pp::kThreads, 1)
           break;
         issued = j + 1;
         mbar_arrive_expect_tx(&kv_full[s], 2 * kKVBytes);
-        const int page = j < pages ? fa_page(p, req, j) : 0;
-        const int row = (page * p.hkv + h) * 64;
-        for (int r = 0; r < 2; ++r) {
-          tma_load_2d(smem + kK + s * kKVBytes + r * (kKVBytes / 2), &tmap_k, &kv_full[s], r * 64, row);
-          tma_load_2d(smem + kV + s * kKVBytes + r * (kKVBytes / 2), &tmap_v, &kv_full[s], r * 64, row);
-        }
+        load_kv_half(p, &tmap_k, &tmap_v, &kv_full[s], smem + kK + s * kKVBytes, smem + kV + s * kKVBytes,
+                     kKVBytes / 2, req, h, j * kPBN, pages);
       }
       mbar_wait(q_full, 0, nullptr, p.status);
       for (int j = max(0, issued - kStages); j < issued; ++j)
@@ -666,8 +681,8 @@ __global__ void __launch_bounds__(pp::kThreads, 1)
       tc_fence_before();
       mbar_arrive(&p_full[t]);
     }
-    __nv_bfloat16* orow =
-        p.out + static_cast<int64_t>(q_begin + tok) * p.out_stride + static_cast<int64_t>(h * p.G + r % p.G) * kD;
+    __nv_bfloat16* orow = p.out + static_cast<int64_t>(q_begin + tok) * p.out_stride +
+                          static_cast<int64_t>(h * p.G + r % p.G) * p.d_head;
     if (ok && nb > 0 && warp_wait(&pv_done[t], (nb - 1) & 1, abort_flag, p.status, 13)) {
       tc_fence_after();
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
@@ -679,6 +694,7 @@ __global__ void __launch_bounds__(pp::kThreads, 1)
         if (row_ok) {
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
+            if (c + i >= p.d_head) break;
             uint4 o;
             o.x = pack_bf16x2(__uint_as_float(v[i]) * inv, __uint_as_float(v[i + 1]) * inv);
             o.y = pack_bf16x2(__uint_as_float(v[i + 2]) * inv, __uint_as_float(v[i + 3]) * inv);
@@ -689,7 +705,7 @@ __global__ void __launch_bounds__(pp::kThreads, 1)
         }
       }
     } else if (nb == 0 && row_ok) {
-      for (int c = 0; c < kD; c += 8) *reinterpret_cast<uint4*>(orow + c) = make_uint4(0u, 0u, 0u, 0u);
+      for (int c = 0; c < p.d_head; c += 8) *reinterpret_cast<uint4*>(orow + c) = make_uint4(0u, 0u, 0u, 0u);
     }
   }
 
@@ -728,34 +744,53 @@ bool encode(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims
 
 }  // namespace
 
-// Paged mode, head_dim 128, G = Hq / Hkv in {1, 2, 4, 8, 16}, no sliding window; tiles of 128 packed rows.
+// Paged mode: head_dim 128.  Contiguous mode (ragged encoder batches, K/V rows [tokens, hkv, D]):
+// head_dim 64..128 in steps of 16, the columns past it loaded as zeros.  G = Hq / Hkv dividing 128,
+// no sliding window.
 bool attention_prefill_sm100_supported(const AttnPrefillArgs& a) {
-  if (a.block_table == nullptr || a.head_dim != kD || a.window > 0 || a.hkv <= 0 || a.hq % a.hkv != 0) return false;
+  if (a.window > 0 || a.hkv <= 0 || a.hq % a.hkv != 0) return false;
+  const bool paged = a.block_table != nullptr;
+  if (paged ? a.head_dim != kD : (a.cu_kv == nullptr || a.head_dim < 64 || a.head_dim > kD || a.head_dim % 16 != 0))
+    return false;
+  if (!paged && ((a.kv_stride * 2) % 16 != 0 || a.kv_stride < static_cast<int64_t>(a.hkv) * a.head_dim)) return false;
   const int G = a.hq / a.hkv;
   return G >= 1 && G <= 16 && kRows % G == 0 && (a.q_stride * 2) % 16 == 0 &&
          (reinterpret_cast<uintptr_t>(a.q) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.k) & 15) == 0 &&
-         (reinterpret_cast<uintptr_t>(a.v) & 15) == 0 && (a.out_stride % 8) == 0;
+         (reinterpret_cast<uintptr_t>(a.v) & 15) == 0 && (a.out_stride % 8) == 0 &&
+         (reinterpret_cast<uintptr_t>(a.out) & 15) == 0;
 }
 
 cudaError_t attention_prefill_sm100(const AttnPrefillArgs& a, cudaStream_t stream) {
   if (a.num_tiles == 0) return cudaSuccess;
-  if (!attention_prefill_sm100_supported(a) || a.num_pages <= 0) return cudaErrorInvalidValue;
+  const bool paged = a.block_table != nullptr;
+  if (!attention_prefill_sm100_supported(a) || (paged && a.num_pages <= 0) || (!paged && a.kv_rows <= 0))
+    return cudaErrorInvalidValue;
   const int G = a.hq / a.hkv;
+  const int D = a.head_dim;
   CUtensorMap tq, tk, tv;
   // Q [tokens, Hq, D]: the tensor spans every row the tile table can address (q rows are
-  // never written past the last request; rows past a request's end are masked)
+  // never written past the last request; rows past a request's end are masked).  With D < 128
+  // the second 64-column box reads zeros past column D.
   {
     const cuuint64_t rows = static_cast<cuuint64_t>(a.q_rows > 0 ? a.q_rows : 1);
-    cuuint64_t dims[3] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(a.hq), rows};
-    cuuint64_t strides[2] = {static_cast<cuuint64_t>(kD) * 2, static_cast<cuuint64_t>(a.q_stride) * 2};
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(a.hq), rows};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * 2, static_cast<cuuint64_t>(a.q_stride) * 2};
     cuuint32_t box[3] = {64, static_cast<cuuint32_t>(G), static_cast<cuuint32_t>(kRows / G)};
     if (!encode(&tq, a.q, 3, dims, strides, box)) return cudaErrorInvalidValue;
   }
-  {
+  if (paged) {
     cuuint64_t dims[2] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(a.num_pages) * a.hkv * 64};
     cuuint64_t strides[1] = {static_cast<cuuint64_t>(kD) * 2};
     cuuint32_t box[2] = {64, 64};
     if (!encode(&tk, a.k, 2, dims, strides, box) || !encode(&tv, a.v, 2, dims, strides, box))
+      return cudaErrorInvalidValue;
+  } else {
+    // K / V rows [kv_rows, Hkv, D] of stride kv_stride: one head's 64 consecutive key rows per box
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(a.hkv),
+                          static_cast<cuuint64_t>(a.kv_rows)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * 2, static_cast<cuuint64_t>(a.kv_stride) * 2};
+    cuuint32_t box[3] = {64, 1, 64};
+    if (!encode(&tk, a.k, 3, dims, strides, box) || !encode(&tv, a.v, 3, dims, strides, box))
       return cudaErrorInvalidValue;
   }
   FaParams p;
@@ -774,6 +809,8 @@ cudaError_t attention_prefill_sm100(const AttnPrefillArgs& a, cudaStream_t strea
   p.out_stride = a.out_stride;
   p.num_pages = a.num_pages;
   p.status = a.status;
+  p.cu_kv = paged ? nullptr : a.cu_kv;
+  p.d_head = D;
   dim3 grid(a.num_tiles, a.hkv);
   if (a.tile_rows == 256) {
     cudaError_t e = ensure_smem_attr<fa_prefill_pp_kernel>(pp::kSmem);

@@ -215,9 +215,11 @@ void attention_prefill(const torch::Tensor& q, const torch::Tensor& k, const tor
   a.tile_rows = static_cast<int>(tile_rows);
   a.q_rows = static_cast<int>(q.size(0));
   a.status = status_ptr(status);
+  a.kv_rows = block_table.has_value() ? 0 : static_cast<int>(k.size(0));
   TORCH_CHECK(tile_rows == 64 || tile_rows == 128 || tile_rows == 256, "tile_rows must be 64, 128 or 256");
   TORCH_CHECK(tile_rows == 64 || omni::attention_prefill_sm100_supported(a),
-              "128 / 256-row tiles need the paged tcgen05 kernel (head_dim 128, no window, aligned rows)");
+              "128 / 256-row tiles need the tcgen05 kernel (paged: head_dim 128; contiguous: head_dim 64..128 "
+              "in steps of 16; no window; aligned rows)");
   check_launch(omni::attention_prefill(a, at::cuda::getCurrentCUDAStream()), "attention_prefill");
 }
 

@@ -130,6 +130,7 @@ struct AttnPrefillArgs {
                           // two-tile ping-pong variant)
   int q_rows;             // rows of q (tokens of the batch)
   int* status;            // bounded-wait status word (tcgen05 kernel), may be nullptr
+  int kv_rows;            // contiguous mode: rows of k / v
 };
 cudaError_t attention_prefill(const AttnPrefillArgs& a, cudaStream_t stream);
 bool attention_prefill_sm100_supported(const AttnPrefillArgs& a);

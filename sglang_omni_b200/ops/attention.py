@@ -123,13 +123,32 @@ def prefill_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Ten
     return out
 
 
+def varlen_tile_rows(q: torch.Tensor, k: torch.Tensor, head_dim: int, group: int, window: int = 0,
+                     v: torch.Tensor | None = None, out: torch.Tensor | None = None) -> int:
+    """Query rows per tile for ragged attention: the tcgen05 kernels (256 or 128 rows) for head
+    dims 80..128 without a sliding window and 16-byte aligned rows, else the 64-row mma.sync
+    kernel (head dim 64 stays there: the tensor-core kernels would pad it to 128)."""
+    if os.environ.get("OMNI_FA_SM100", "1") == "0" or window > 0 or not (80 <= head_dim <= 128) or head_dim % 16:
+        return 64
+    if 128 % max(1, group) or (q.stride(0) * 2) % 16 or (k.stride(0) * 2) % 16 or q.data_ptr() % 16 or \
+            k.data_ptr() % 16:
+        return 64
+    if v is not None and (v.stride(0) != k.stride(0) or v.data_ptr() % 16):
+        return 64
+    if out is not None and (out.stride(0) % 8 or out.data_ptr() % 16):
+        return 64
+    return int(os.environ.get("OMNI_FA_TILE_ROWS", "256"))
+
+
 def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens: torch.Tensor,
                      num_heads: int, num_kv_heads: int, head_dim: int, scale: float | None = None,
                      causal: bool = False, out: torch.Tensor | None = None, q_lens: list[int] | None = None,
                      tiles: tuple[torch.Tensor, torch.Tensor] | None = None, window: int = 0) -> torch.Tensor:
     """Ragged (block-diagonal) attention over contiguous q/k/v rows (encoders, vocoder transformers).
 
-    ``window`` > 0 (with causal) limits every query to its last ``window`` keys."""
+    ``window`` > 0 (with causal) limits every query to its last ``window`` keys.  ``tiles``: a
+    precomputed 64-row tile table (the mma.sync kernel); without it the tile size is chosen by
+    ``varlen_tile_rows`` and the table is built once per layout."""
     scale = scale if scale is not None else 1.0 / math.sqrt(head_dim)
     T = q.shape[0]
     if out is None:
@@ -140,11 +159,13 @@ def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqle
         out.copy_(ref.reshape(out.shape))
         return out
     lens = None
+    rows = 64
     if tiles is None:
         if q_lens is None:
             cu = cu_seqlens.tolist()
             q_lens = [cu[i + 1] - cu[i] for i in range(len(cu) - 1)]
-        tiles_req, tiles_tok0, lens = varlen_plan(q_lens, num_heads // num_kv_heads, q.device)
+        rows = varlen_tile_rows(q, k, head_dim, num_heads // num_kv_heads, window, v, out)
+        tiles_req, tiles_tok0, lens = varlen_plan(q_lens, num_heads // num_kv_heads, q.device, rows)
         tiles = (tiles_req, tiles_tok0)
     if lens is None:
         lens = (cu_seqlens[1:] - cu_seqlens[:-1]).to(torch.int32)
@@ -154,7 +175,7 @@ def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqle
             raise _check.LaunchCheckError("varlen_attention: cu_seqlens not monotone")
         _check.check_tiles("varlen_attention", tiles[0], tiles[1], cu_seqlens)
     ext().attention_prefill(q, k, v, out, None, cu_seqlens, lens, cu_seqlens, tiles[0], tiles[1],
-                            num_heads, num_kv_heads, head_dim, scale, causal, window)
+                            num_heads, num_kv_heads, head_dim, scale, causal, window, rows, status_word(q.device))
     return out
 
 
@@ -163,18 +184,19 @@ _PLANS_LOCK = threading.Lock()
 _PLANS_MAX = 64
 
 
-def varlen_plan(q_lens: list[int], group: int, device) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+def varlen_plan(q_lens: list[int], group: int, device, rows: int = 64) -> tuple[torch.Tensor, torch.Tensor,
+                                                                                torch.Tensor]:
     """Device tile table (request, first token) and lengths of a ragged batch, built once per
     (lengths, group, device) and reused: an encoder calls the attention once per layer with the
     same layout, and a fresh host-to-device upload per layer would stall the host on the stream."""
     device = torch.device(device)
-    key = (tuple(int(n) for n in q_lens), int(group), device.index)
+    key = (tuple(int(n) for n in q_lens), int(group), device.index, int(rows))
     with _PLANS_LOCK:
         hit = _PLANS.get(key)
         if hit is not None:
             _PLANS.move_to_end(key)
             return hit[:3]
-    req, tok0 = prefill_tiles(list(key[0]), group)
+    req, tok0 = prefill_tiles(list(key[0]), group, rows)
     n = len(req)
     host = torch.tensor(req + tok0 + list(key[0]), dtype=torch.int32)
     if device.type == "cuda":

@@ -134,3 +134,37 @@ def test_varlen_noncausal(h, d):
     out = A.varlen_attention(q.contiguous(), k.contiguous(), v.contiguous(), cu, h, h, d)
     ref = A.varlen_attention_ref(qkv[:, 0], qkv[:, 1], qkv[:, 2], cu, 1 / math.sqrt(d), False)
     torch.testing.assert_close(out.float().view(T, h, d), ref, atol=2e-2, rtol=2e-2)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("rows", [128, 256])
+@pytest.mark.parametrize("h,hkv,d,causal", [(16, 16, 80, False), (16, 16, 128, False), (32, 4, 128, True),
+                                             (16, 2, 96, True)])
+def test_varlen_tcgen05_strided_views(rows, h, hkv, d, causal):
+    """The tcgen05 kernels over ragged contiguous K/V: q / k / v are strided views of fused QKV
+    rows (head dims below 128 load zeros past the head), long and short sequences, GQA groups."""
+    import os
+
+    lens = [5, 100, 333, 64, 700]
+    T = sum(lens)
+    cu = torch.tensor([0] + torch.tensor(lens).cumsum(0).tolist(), dtype=torch.int32, device="cuda")
+    width = (h + 2 * hkv) * d
+    qkv = (torch.randn(T, width, device="cuda") * 0.5).bfloat16()
+    q, k, v = qkv[:, :h * d], qkv[:, h * d:(h + hkv) * d], qkv[:, (h + hkv) * d:]
+    old = os.environ.get("OMNI_FA_TILE_ROWS")
+    os.environ["OMNI_FA_TILE_ROWS"] = str(rows)
+    try:
+        assert A.varlen_tile_rows(q, k, d, h // hkv, 0, v) == rows
+        out = A.varlen_attention(q, k, v, cu, h, hkv, d, causal=causal, q_lens=lens)
+    finally:
+        if old is None:
+            os.environ.pop("OMNI_FA_TILE_ROWS")
+        else:
+            os.environ["OMNI_FA_TILE_ROWS"] = old
+    torch.cuda.synchronize()
+    from sglang_omni_b200.ops._ext import check_status
+
+    check_status(torch.device("cuda", 0))
+    ref = A.varlen_attention_ref(q.reshape(T, h, d), k.reshape(T, hkv, d), v.reshape(T, hkv, d), cu,
+                                 1 / math.sqrt(d), causal)
+    torch.testing.assert_close(out.float().view(T, h, d), ref, atol=2e-2, rtol=2e-2)
