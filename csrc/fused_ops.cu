@@ -1032,12 +1032,47 @@ __global__ void __launch_bounds__(256) rope_half_inplace_kernel(__nv_bfloat16* _
     p[i + half] = __float2bfloat16(b * c[i + half] + a * s[i + half]);
   }
 }
+// Two adjacent pairs per thread with 4-byte bf16x2 accesses (half, strides even, 4-byte base).
+__global__ void __launch_bounds__(256) rope_half_inplace_x2_kernel(__nv_bfloat16* __restrict__ x, int64_t row_stride,
+                                                                   int rows, int heads, int head_stride, int half,
+                                                                   const float* __restrict__ cs,
+                                                                   const float* __restrict__ sn, int64_t cs_stride) {
+  const int q = half >> 1;   // pairs of pairs per head
+  const int64_t total = static_cast<int64_t>(rows) * heads * q;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int i = 2 * static_cast<int>(idx % q);
+    const int64_t th = idx / q;
+    const int h = static_cast<int>(th % heads);
+    const int64_t t = th / heads;
+    __nv_bfloat16* p = x + t * row_stride + static_cast<int64_t>(h) * head_stride;
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p + i));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p + i + half));
+    const float2 c0 = *reinterpret_cast<const float2*>(cs + t * cs_stride + i);
+    const float2 s0 = *reinterpret_cast<const float2*>(sn + t * cs_stride + i);
+    const float2 c1 = *reinterpret_cast<const float2*>(cs + t * cs_stride + i + half);
+    const float2 s1 = *reinterpret_cast<const float2*>(sn + t * cs_stride + i + half);
+    *reinterpret_cast<__nv_bfloat162*>(p + i) = __floats2bfloat162_rn(a.x * c0.x - b.x * s0.x, a.y * c0.y - b.y * s0.y);
+    *reinterpret_cast<__nv_bfloat162*>(p + i + half) =
+        __floats2bfloat162_rn(b.x * c1.x + a.x * s1.x, b.y * c1.y + a.y * s1.y);
+  }
+}
 }  // namespace
 
 cudaError_t rope_half_inplace(void* x, int64_t row_stride, int rows, int heads, int head_stride, int rot,
                               const float* cos, const float* sin, int64_t cs_stride, cudaStream_t stream) {
   if (rows == 0 || heads == 0) return cudaSuccess;
   if (rot <= 0 || rot % 2 != 0 || rot > head_stride) return cudaErrorInvalidValue;
+  const int half = rot / 2;
+  if (half % 2 == 0 && row_stride % 2 == 0 && head_stride % 2 == 0 && cs_stride % 2 == 0 &&
+      (reinterpret_cast<uintptr_t>(x) & 3) == 0 && (reinterpret_cast<uintptr_t>(cos) & 7) == 0 &&
+      (reinterpret_cast<uintptr_t>(sin) & 7) == 0) {
+    const int64_t total = static_cast<int64_t>(rows) * heads * (half / 2);
+    const int64_t grid = std::min<int64_t>((total + 255) / 256, 148 * 16);
+    rope_half_inplace_x2_kernel<<<static_cast<int>(grid), 256, 0, stream>>>(
+        static_cast<__nv_bfloat16*>(x), row_stride, rows, heads, head_stride, half, cos, sin, cs_stride);
+    return cudaGetLastError();
+  }
   const int64_t total = static_cast<int64_t>(rows) * heads * (rot / 2);
   const int64_t grid = std::min<int64_t>((total + 255) / 256, 148 * 16);
   rope_half_inplace_kernel<<<static_cast<int>(grid), 256, 0, stream>>>(

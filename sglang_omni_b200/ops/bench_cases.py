@@ -225,6 +225,14 @@ def _time_cases() -> None:
         ws = A.DecodeWorkspace(nb, hq, d, ctx, "cuda")
         res[f"decode_attn B{nb} ctx1152"] = (t(lambda: A.decode_attention(q[:nb], k, v, bt[:nb], kl[:nb], hq, hkv, d,
                                                                           ws)), 2 * nb * ctx * hkv * d * 2)
+    # split sizes of the GPU-filling batch (the rule's FILL_SPLIT_KEYS), B=64 ctx 1152
+    fill = A.FILL_SPLIT_KEYS
+    for kps in (256, 384, 576):
+        A.FILL_SPLIT_KEYS = kps
+        ws = A.DecodeWorkspace(B, hq, d, ctx, "cuda", keys_per_split=kps)
+        res[f"decode_attn B64 ctx1152 split {kps}"] = (
+            t(lambda: A.decode_attention(q, k, v, bt, kl, hq, hkv, d, ws)), 2 * B * ctx * hkv * d * 2)
+    A.FILL_SPLIT_KEYS = fill
     # skewed batch: 63 requests at 1152 keys and one at 8192 (its pages follow the others')
     long_pages = 8192 // 64
     ks = torch.randn(B * pages + long_pages + 1, hkv, 64, d, device="cuda").bfloat16()
