@@ -53,9 +53,9 @@ def parse():
     ap.add_argument("--thinker", type=int, default=1, help="run the thinker serving phase (headline value)")
     ap.add_argument("--vision", type=int, default=1, help="also measure image+text -> text serving")
     ap.add_argument("--vision-requests", type=int, default=64)
-    ap.add_argument("--vision-group", type=int, default=1,
+    ap.add_argument("--vision-group", type=int, default=0,
                     help="N > 1: also serve image+text with one pipeline whose thinker is a TP x EP rank group "
-                         "over all GPUs")
+                         "over all GPUs (the per-rank phases' models are released first)")
     ap.add_argument("--vision-tokens", type=int, default=128)
     ap.add_argument("--ep", type=int, default=1,
                     help="N>1: experts sharded over the GPUs (expert parallel MoE over NVLink, data-parallel "
@@ -561,6 +561,14 @@ def main():
                "timing": "host wall clock through Client.generate (stream=True), whole job; TTFT max over ranks"}
     vis_group = None
     if args.vision and args.vision_group and world > 1 and args.layers == 48:
+        # the group's followers need the memory the per-rank phases' models hold on every GPU
+        import gc
+
+        eng = pool = None
+        loader._CACHE.clear()
+        gc.collect()
+        torch.cuda.empty_cache()
+        dist.barrier()
         if rank == 0:
             try:
                 vis_group = vision_group_phase(args, world)

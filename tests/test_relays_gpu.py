@@ -30,10 +30,12 @@ def _payload(i, n, device):
 
 def _nccl_worker(rank, port, q, meta_q):
     import asyncio
+    import faulthandler
     from datetime import timedelta
 
     import torch.distributed as dist
 
+    faulthandler.dump_traceback_later(150, exit=True)   # a stuck worker prints where it is and ends
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     try:
         torch.cuda.set_device(rank)
@@ -60,9 +62,12 @@ def _nccl_worker(rank, port, q, meta_q):
             return ok
 
         res = asyncio.run(main())
+        torch.cuda.synchronize()
+        q.put((rank, res, None))          # reported before the shutdown collectives
+        for i in range(len(SIZES)):
+            relay.cleanup(f"r{i}")
         dist.barrier()
         dist.destroy_process_group()
-        q.put((rank, res, None))
     except Exception:
         import traceback
 
