@@ -60,6 +60,7 @@ setup(
     name="sglang_omni_b200",
     version="0.1.0",
     packages=["sglang_omni_b200"],
+    package_data={"sglang_omni_b200": ["serve/playground.html"]},
     ext_modules=ext_modules,
     # the reference's command name (pyproject.toml:68 there): sgl-omni serve | config view | config export
     entry_points={"console_scripts": ["sgl-omni=sglang_omni_b200.cli.cli:main"]},

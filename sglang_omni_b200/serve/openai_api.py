@@ -102,6 +102,15 @@ def create_app(client: Client, model_name: str = "model") -> FastAPI:
     async def models():
         return ModelList(data=[ModelCard(id=model_name, root=model_name)]).model_dump()
 
+    @app.get("/playground")
+    async def playground():
+        """A single-page browser client of the chat endpoint (text / image / audio / video in,
+        streamed text and speech out, the speech chunks played as they arrive)."""
+        import pathlib
+
+        html = (pathlib.Path(__file__).parent / "playground.html").read_text()
+        return Response(content=html, media_type="text/html")
+
     @app.post("/v1/chat/completions")
     async def chat_completions(req: ChatCompletionRequest):
         greq = build_chat_generate_request(req)

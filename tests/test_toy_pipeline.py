@@ -64,6 +64,8 @@ def test_toy_pipeline_openai_server_sse():
                 assert r.status_code == 200
                 r = await http.get("/v1/models")
                 assert r.json()["data"][0]["id"] == "toy"
+                r = await http.get("/playground")
+                assert r.status_code == 200 and "/v1/chat/completions" in r.text
                 prompts = _prompts()
 
                 async def chat(i, stream):
@@ -110,3 +112,53 @@ def test_toy_pipeline_abort():
             assert len(res.token_ids) == 4
 
     asyncio.run(main())
+
+
+def test_toy_pipeline_under_asyncio_debug_mode():
+    """The event-loop side of the runtime under asyncio's debug mode: no coroutine is left
+    un-awaited, no callback is scheduled from a foreign thread without the thread-safe entry
+    point (debug mode raises for that), no task dies with an unretrieved exception, and the
+    pipeline still completes every request."""
+    import gc
+    import logging
+    import warnings
+
+    records = []
+
+    class _Grab(logging.Handler):
+        def emit(self, rec):
+            records.append(rec.getMessage())
+
+    h = _Grab(level=logging.ERROR)
+    logging.getLogger("asyncio").addHandler(h)
+
+    async def main():
+        loop = asyncio.get_running_loop()
+        loop.slow_callback_duration = 10.0   # timing is not under test here
+        cfg = ToyPipelineConfig()
+        coord, stages = compile_pipeline(cfg)
+        async with PipelineRunner(coord, stages):
+            client = Client(coord)
+            prompts = _prompts(4)
+
+            async def one(i):
+                req = GenerateRequest(prompt_token_ids=prompts[i], sampling=SamplingParams(temperature=0.0),
+                                      max_tokens=8, stream=True)
+                n = 0
+                async for ch in client.generate(req):
+                    n += len(ch.token_ids) if ch.finish_reason is None else 0
+                return n
+
+            assert await asyncio.gather(*[one(i) for i in range(4)]) == [8] * 4
+
+    try:
+        with warnings.catch_warnings(record=True) as w:
+            warnings.simplefilter("always")
+            asyncio.run(main(), debug=True)
+            gc.collect()
+        never = [str(x.message) for x in w if "was never awaited" in str(x.message)]
+        assert not never, never
+        bad = [m for m in records if "exception was never retrieved" in m or "non-thread-safe" in m]
+        assert not bad, bad
+    finally:
+        logging.getLogger("asyncio").removeHandler(h)
