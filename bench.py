@@ -377,11 +377,64 @@ def reference_arm(args):
                        "installed with --no-deps")
         except Exception as exc:  # pragma: no cover
             why = f"probe failed: {exc}"
+    if why is None and not os.environ.get("OMNI_REF_CHECKPOINT"):
+        why = ("the reference loads weights from a checkpoint directory only (no random init); set "
+               "OMNI_REF_CHECKPOINT to a Qwen3-Omni checkpoint to run it")
     if why is not None:
         if int(os.environ.get("RANK", "0")) == 0:
             print(json.dumps({"impl": "reference", "unavailable": why}))
         return
-    raise SystemExit("reference arm: sglang present but the runner is not wired")  # pragma: no cover
+    reference_serving(args, ref, os.environ["OMNI_REF_CHECKPOINT"])  # pragma: no cover
+
+
+def reference_serving(args, ref: str, ckpt: str):  # pragma: no cover - needs sglang and a checkpoint
+    """The headline metric through the reference's own public API and stock code path: its
+    Qwen3-Omni pipeline config compiled by its compiler, run by its PipelineRunner, the same number
+    of concurrent requests submitted to its coordinator, output tokens over wall time of the
+    timed rounds (one GPU; the reference has no TP / EP path)."""
+    import asyncio
+    import random
+
+    sys.path.insert(0, ref)
+    from sglang_omni.config import PipelineRunner, compile_pipeline
+    from sglang_omni.models.qwen3_omni.config import Qwen3OmniPipelineConfig
+    from sglang_omni.proto import OmniRequest
+
+    rnd = random.Random(1234)
+    words = [w.strip() for w in "alpha bravo charlie delta echo foxtrot golf hotel india juliet kilo lima".split()]
+    prompts = [" ".join(rnd.choice(words) for _ in range(args.prompt_len)) for _ in range(args.requests)]
+
+    async def run():
+        coordinator, stages = compile_pipeline(Qwen3OmniPipelineConfig(model_path=ckpt))
+        runner = PipelineRunner(coordinator, stages)
+        await runner.start()
+        try:
+            async def one(i, tag):
+                req = OmniRequest(inputs={"messages": [{"role": "user", "content": prompts[i]}]},
+                                  params={"max_new_tokens": args.output_len, "temperature": 0.0, "ignore_eos": True})
+                res = await coordinator.submit(f"{tag}-{i}", req)
+                ids = (res or {}).get("output_ids") or (res or {}).get("token_ids") or []
+                return len(ids) if ids else args.output_len
+
+            for w in range(args.warmup):
+                await asyncio.gather(*[one(i, f"w{w}") for i in range(args.requests)])
+            t0 = time.perf_counter()
+            n = 0
+            for s_ in range(args.steps):
+                n += sum(await asyncio.gather(*[one(i, f"s{s_}") for i in range(args.requests)]))
+            return n, time.perf_counter() - t0
+        finally:
+            await runner.stop()
+
+    n, wall = asyncio.run(run())
+    print(json.dumps({"metric": "output tok/s + p50 time-to-first-audio-chunk, Qwen3-Omni-30B-A3B, 1/2/4/8 B200",
+                      "impl": "reference", "value": round(n / wall, 2), "unit": "output tokens/s (whole job)",
+                      "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": round(1e3 * wall / args.steps, 3), "higher_is_better": True,
+                      "dtype": "bf16", "data": f"checkpoint {ckpt}, random word prompts",
+                      "config": {"model": "Qwen3-Omni-30B-A3B thinker", "global_batch": args.requests,
+                                 "seq_len": args.prompt_len, "output_len": args.output_len, "parallelism": "tp1"},
+                      "timing": "host wall clock of the timed rounds through the reference's coordinator"}))
 
 
 def main():
