@@ -66,6 +66,11 @@ def _stage_process_entry(cfg_dict: dict, cfg_cls_path: str | None, stage_index: 
             dist.init_process_group("nccl", rank=stage_index, world_size=len(stages_cfg),
                                     timeout=timedelta(seconds=120))
             relay_ranks = {st.name: i for i, st in enumerate(stages_cfg)}
+            # every pair of stage processes connects once, in one global order, before any stage
+            # sends (a first send would otherwise block its host thread until the peer receives)
+            from ..relay.nccl import NcclRelay
+
+            NcclRelay(rank=stage_index, world_size=len(stages_cfg), device=f"cuda:{local_gpu or 0}").warmup_all()
         endpoints = allocate_endpoints(cfg, [st.name for st in stages_cfg], run_id)
         receivers = {name_map.get(t.to_stage, t.to_stage) for st in stages_cfg for t in st.stream_to}
         stage = build_stage(cfg, s, endpoints, name_map, receivers, stage_index, multiprocess=True,

@@ -29,6 +29,33 @@ class NcclRelay(Relay):
         self._stream = None
         self._inflight: dict[str, list] = {}
 
+    def warmup(self, peers) -> None:
+        """Establishes the point-to-point connections with ``peers`` before the first transfer.
+        NCCL sets a connection up on its first send / receive between two ranks, and the sender's
+        host call blocks until the receiver has posted its side; a receiver that posts only after
+        the sender's metadata arrives (which the sender publishes after its send call returns)
+        would wait forever.  Collective over each pair: both ranks of every pair call this, with
+        the pairs in one global order (``warmup_all``) so no rank waits on a pair its peer has not
+        reached."""
+        self._ensure()
+        for peer in peers:
+            if peer == self.rank:
+                continue
+            tx = torch.zeros(1, dtype=torch.uint8, device=self.device)
+            rx = torch.empty(1, dtype=torch.uint8, device=self.device)
+            ops = [dist.P2POp(dist.isend, tx, peer, group=self.group),
+                   dist.P2POp(dist.irecv, rx, peer, group=self.group)]
+            for w in dist.batch_isend_irecv(ops):
+                w.wait()
+        torch.cuda.synchronize(self.device)
+
+    def warmup_all(self) -> None:
+        """``warmup`` with every other rank of the group, pairs in ascending (low, high) order."""
+        for a in range(self.world_size):
+            for b in range(a + 1, self.world_size):
+                if self.rank in (a, b):
+                    self.warmup([b if self.rank == a else a])
+
     def _ensure(self):
         if not dist.is_initialized():
             raise RuntimeError("NcclRelay needs torch.distributed initialised (init_process_group('nccl'))")

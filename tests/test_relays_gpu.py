@@ -44,6 +44,7 @@ def _nccl_worker(rank, port, q, meta_q):
         from sglang_omni_b200.relay.nccl import NcclRelay
 
         relay = NcclRelay(rank=rank, world_size=2, device=f"cuda:{rank}")
+        relay.warmup_all()   # connections first: a first send blocks its host thread until the peer receives
 
         async def main():
             if rank == 0:
