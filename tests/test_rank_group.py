@@ -126,3 +126,39 @@ def test_rank_group_follower_death_fails_requests():
             ex.engine.stop()
 
     asyncio.run(main())
+
+
+def test_host_subgroups_share_one_store():
+    """Data-parallel TP subgroups of a 4-rank host group (ranks {0, 1} and {2, 3}) over the same
+    TCP store: each subgroup's all-gather / barrier sees only its members, concurrently."""
+    import socket
+    import threading
+
+    from sglang_omni_b200.parallel.hostgroup import HostGroup
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    out, errs = {}, []
+
+    def rank(r):
+        try:
+            g = HostGroup("127.0.0.1", port, r, 4, timeout_s=30)
+            members = [0, 1] if r < 2 else [2, 3]
+            sub = g.subgroup(members, f"tp{r // 2}")
+            got = sub.all_gather_object(f"r{r}")
+            sub.barrier()
+            everyone = g.all_gather_object(r * 10)
+            out[r] = (sub.rank, sub.world, got, everyone)
+        except Exception as exc:   # reported to the test thread
+            errs.append(repr(exc))
+
+    ts = [threading.Thread(target=rank, args=(r,)) for r in range(4)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join(60)
+    assert not errs, errs
+    assert out[0][:3] == (0, 2, ["r0", "r1"]) and out[1][:3] == (1, 2, ["r0", "r1"])
+    assert out[2][:3] == (0, 2, ["r2", "r3"]) and out[3][:3] == (1, 2, ["r2", "r3"])
+    assert all(v[3] == [0, 10, 20, 30] for v in out.values())
