@@ -95,7 +95,9 @@ def create_app(client: Client, model_name: str = "model") -> FastAPI:
         return {"status": "ok", **client.get_status()}
 
     @app.get("/metrics")
-    async def get_metrics():
+    async def get_metrics(format: str = "json"):
+        if format == "prometheus":
+            return Response(content=metrics.prometheus(), media_type="text/plain; version=0.0.4")
         return metrics.snapshot()
 
     @app.get("/v1/models")
@@ -120,6 +122,7 @@ def create_app(client: Client, model_name: str = "model") -> FastAPI:
         if req.stream:
             return StreamingResponse(_chat_stream(client, greq, rid, model, metrics), media_type="text/event-stream")
         t0 = time.perf_counter()
+        metrics.started()
         try:
             res = await client.completion(greq)
         except Exception as exc:
@@ -142,6 +145,7 @@ def create_app(client: Client, model_name: str = "model") -> FastAPI:
             return StreamingResponse(_speech_stream(client, greq, req.response_format, metrics),
                                      media_type="text/event-stream")
         t0 = time.perf_counter()
+        metrics.started()
         try:
             res = await client.speech(greq, req.response_format)
         except Exception as exc:
@@ -160,8 +164,10 @@ def create_app(client: Client, model_name: str = "model") -> FastAPI:
 
 async def _chat_stream(client: Client, greq: GenerateRequest, rid: str, model: str, metrics: ServerMetrics):
     t0 = time.perf_counter()
-    first_audio = None
+    first_audio = first_text = last_text = None
+    gaps: list[float] = []
     n_tokens = 0
+    metrics.started()
     yield _sse(ChatCompletionStreamResponse(id=rid, model=model, choices=[
         ChatCompletionStreamChoice(delta=ChatCompletionStreamDelta(role="assistant", content=""))]))
     try:
@@ -178,6 +184,12 @@ async def _chat_stream(client: Client, greq: GenerateRequest, rid: str, model: s
                     first_audio = time.perf_counter() - t0
                 delta = ChatCompletionStreamDelta(audio=ChatCompletionAudio(id=f"audio-{rid}", data=ch.audio_b64))
             else:
+                now = time.perf_counter()
+                if first_text is None:
+                    first_text = now - t0
+                elif last_text is not None:
+                    gaps.append(now - last_text)
+                last_text = now
                 delta = ChatCompletionStreamDelta(content=ch.text)
             yield _sse(ChatCompletionStreamResponse(id=rid, model=model,
                                                     choices=[ChatCompletionStreamChoice(delta=delta)]))
@@ -185,7 +197,8 @@ async def _chat_stream(client: Client, greq: GenerateRequest, rid: str, model: s
         metrics.failed()
         yield _sse({"error": {"message": str(exc), "type": "server_error"}})
     else:
-        metrics.finished(time.perf_counter() - t0, first_audio, n_tokens)
+        metrics.finished(time.perf_counter() - t0, first_audio, n_tokens, ttft_s=first_text,
+                         itl_s=sum(gaps) / len(gaps) if gaps else None)
     yield "data: [DONE]\n\n"
 
 
@@ -193,6 +206,7 @@ async def _speech_stream(client: Client, greq: GenerateRequest, fmt: str, metric
     t0 = time.perf_counter()
     first = None
     idx = 0
+    metrics.started()
     async for ch in client.generate(greq):
         if ch.finish_reason is not None:
             yield _sse({"type": "audio.speech.done", "usage": ch.usage.to_dict() if ch.usage else None})

@@ -88,6 +88,12 @@ def test_toy_pipeline_openai_server_sse():
                 full = await chat(0, False)
                 assert full["usage"]["completion_tokens"] == 16
                 assert full["choices"][0]["message"]["role"] == "assistant"
+                m = (await http.get("/metrics")).json()
+                assert m["requests_ok"] == 9 and m["requests_in_flight"] == 0 and m["completion_tokens"] == 144
+                assert m["ttft_p50_s"] is not None and m["itl_p50_s"] is not None
+                prom = (await http.get("/metrics", params={"format": "prometheus"})).text
+                assert 'omni_requests_total{status="ok"} 9' in prom
+                assert 'omni_time_to_first_token_seconds{quantile="0.5"}' in prom
 
     asyncio.run(main())
 
