@@ -167,8 +167,7 @@ class DecoderLM(nn.Module):
             L = nn.Module()
             L.ln1 = P(H)
             L.qkv = P(cfg.q_size + 2 * cfg.kv_size, H)
-            if cfg.attention_bias:
-                assert tp is None, "q/k/v biases are not sharded for tensor parallelism"
+            if cfg.attention_bias:   # under TP: the local heads' rows, as the QKV weight
                 L.qkv_bias = P(cfg.q_size + 2 * cfg.kv_size)
             L.o = P(H, cfg.q_size)
             L.ln2 = P(H)
@@ -246,7 +245,7 @@ class DecoderLM(nn.Module):
         return self
 
     # ------------------------------------------------------------------ tensor-parallel slices
-    _TP_KINDS = ("qkv", "o", "s13", "s2", "mlp13", "mlp2", "lm_head")
+    _TP_KINDS = ("qkv", "qkv_bias", "o", "s13", "s2", "mlp13", "mlp2", "lm_head")
 
     def full_shape(self, kind: str, p: torch.Tensor):
         """Unsharded shape of a tensor-parallel parameter (None if not sharded)."""
@@ -255,7 +254,7 @@ class DecoderLM(nn.Module):
         f, H, D = self.full_cfg, self.full_cfg.hidden_size, self.full_cfg.head_dim
         if kind == "lm_head":
             return None if self._vslice[2] == f.vocab_size else (f.vocab_size, H)
-        return {"qkv": (f.q_size + 2 * f.kv_size, H), "o": (H, f.q_size),
+        return {"qkv": (f.q_size + 2 * f.kv_size, H), "qkv_bias": (f.q_size + 2 * f.kv_size,), "o": (H, f.q_size),
                 "s13": (2 * f.shared_expert_intermediate_size, H), "s2": (H, f.shared_expert_intermediate_size),
                 "mlp13": (2 * f.intermediate_size, H), "mlp2": (H, f.intermediate_size)}[kind]
 
@@ -274,7 +273,7 @@ class DecoderLM(nn.Module):
             out = full.new_zeros(width, full.shape[1])
             out[:vl] = full[v0:v0 + vl]
             return out
-        if kind == "qkv":
+        if kind in ("qkv", "qkv_bias"):
             q = full[qh.start * D:qh.stop * D]
             k = full[f.q_size + kvh.start * D:f.q_size + kvh.stop * D]
             v = full[f.q_size + f.kv_size + kvh.start * D:f.q_size + f.kv_size + kvh.stop * D]
@@ -420,7 +419,7 @@ class DecoderLM(nn.Module):
 
     def _attention(self, L, i, normed, fb, kv_cache, wait=None):
         cfg = self.cfg
-        qkv = ops.linear(normed, L.qkv, wait=wait)
+        qkv = ops.linear(normed, L.qkv, bias=getattr(L, "qkv_bias", None), wait=wait)
         ops.qkv_rope_store(qkv, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, fb.positions, self.cos_tab,
                            self.sin_tab, cfg.rotary_dim or cfg.head_dim, getattr(L, "q_norm", None),
                            getattr(L, "k_norm", None), cfg.rms_norm_eps, cfg.rope_neox, cfg.mrope_section,

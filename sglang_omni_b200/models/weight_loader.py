@@ -74,7 +74,7 @@ def load_decoder_from_hf(model: DecoderLM, sd: dict[str, torch.Tensor], model_pr
             cp(L.qkv, sh("qkv", torch.cat([g(p + f"self_attn.{n}_proj.weight") for n in "qkv"], 0)))
         cp(L.o, sh("o", g(p + "self_attn.o_proj.weight")))
         if getattr(cfg, "attention_bias", False):
-            cp(L.qkv_bias, torch.cat([g(p + f"self_attn.{n}_proj.bias") for n in "qkv"], 0))
+            cp(L.qkv_bias, sh("qkv_bias", torch.cat([g(p + f"self_attn.{n}_proj.bias") for n in "qkv"], 0)))
         if cfg.qk_norm:
             cp(L.q_norm, g(p + "self_attn.q_norm.weight"))
             cp(L.k_norm, g(p + "self_attn.k_norm.weight"))

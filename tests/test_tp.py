@@ -320,3 +320,29 @@ def test_tp_matches_unsharded():
                 assert v < 0.2, (rank, k, v)
             else:
                 assert v == 0, (rank, k, v)
+
+
+def test_qkv_bias_shards_through_the_loader_cpu():
+    """Q / K / V biases (Qwen2-style layers, e.g. the Ming talker's LM) load into each TP rank as
+    the rows of its heads, the same slices as the QKV weight."""
+    from sglang_omni_b200.models.weight_loader import export_decoder_to_hf, load_decoder_from_hf
+    from sglang_omni_b200.parallel.tp import head_split
+
+    cfg = _cfg(False, dtype=torch.float32, attention_bias=True)
+    full = DecoderLM(cfg).random_init_(seed=5)
+    with torch.no_grad():
+        for L in full.layers:
+            L.qkv_bias.normal_(0.0, 0.1)
+    sd = export_decoder_to_hf(full)
+    world = 2
+    D = cfg.head_dim
+    for r in range(world):
+        m = DecoderLM(cfg, tp=_FakeTP(r, world))
+        load_decoder_from_hf(m, sd, "model.", "lm_head.weight")
+        q, kv = head_split(cfg.num_heads, cfg.num_kv_heads, r, world)
+        for L0, L in zip(full.layers, m.layers):
+            b = L0.qkv_bias
+            want = torch.cat([b[q.start * D:q.stop * D], b[cfg.q_size + kv.start * D:cfg.q_size + kv.stop * D],
+                              b[cfg.q_size + cfg.kv_size + kv.start * D:cfg.q_size + cfg.kv_size + kv.stop * D]])
+            assert torch.equal(L.qkv_bias, want)
+            assert torch.equal(L.qkv, m.shard("qkv", L0.qkv))
