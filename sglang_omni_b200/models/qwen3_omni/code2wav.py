@@ -361,6 +361,10 @@ class StreamingCode2Wav:
     def windows(self) -> list[int]:
         return chunk_windows(self.chunk, self.left_context, self.first_chunk)
 
+    def capture_graphs(self) -> None:
+        if self.graphs is not None:
+            self.graphs.capture_windows(self.windows())
+
     def add_codes(self, rid: str, codes: torch.Tensor) -> None:
         """codes: [Q] or [T, Q] frames for stream rid."""
         st = self.streams.setdefault(rid, _StreamState())

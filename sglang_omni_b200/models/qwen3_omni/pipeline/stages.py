@@ -49,6 +49,7 @@ from ..engine_io import build_prompt, mrope_positions
 from ..hf_config import THINKER_EOS_IDS
 from ..talker import SpeechGenerator, build_talker_prefill
 from ..code2wav import Code2WavGraphs, StreamingCode2Wav
+from ..code2wav_stateful import StatefulStreamingCode2Wav
 
 log = logging.getLogger(__name__)
 SAMPLE_RATE_IN = 16000
@@ -650,17 +651,33 @@ class Code2WavStreamingExecutor(ResultQueueMixin, Executor):
     (12.5 Hz frames -> 24 kHz) to the client as they are produced.
 
     One decoder loop serves all streams: whenever frames arrive it decodes every
-    stream that has a chunk ready in one batched forward per window length
-    (instead of one forward per stream), off the event loop."""
+    stream that has a chunk ready in one batched forward per step shape
+    (instead of one forward per stream), off the event loop.
+
+    ``mode``: "stateful" (default) keeps each stream's transformer keys / values
+    and convolution history, so a chunk runs only its new frames and the stream's
+    chunks add up to the full-sequence waveform (``code2wav_stateful``), for up to
+    ``max_open_streams`` concurrent streams; "window" re-runs ``left_context``
+    frames before every chunk, as the reference executor does.  ``max_streams``:
+    largest batch captured as one CUDA graph."""
 
     def __init__(self, model_path: str, device: str, chunk: int = 10, left_context: int = 25,
                  first_chunk: int | None = None, overrides: dict | None = None, use_graphs: bool = True,
-                 max_streams: int = 32):
+                 max_streams: int = 32, mode: str = "stateful", max_open_streams: int = 128,
+                 max_frames: int = 16384):
         super().__init__()
         dev = torch.device(device)
         self.model = loader.get_code2wav(model_path, dev, overrides)
-        graphs = Code2WavGraphs(self.model, max_streams) if use_graphs and dev.type == "cuda" else None
-        self.sc = StreamingCode2Wav(self.model, chunk, left_context, first_chunk, graphs=graphs)
+        if mode == "stateful":
+            self.sc = StatefulStreamingCode2Wav(self.model, chunk, first_chunk, max(max_open_streams, max_streams),
+                                                max_frames, use_graphs=use_graphs)
+            if self.sc.graphs is not None:
+                self.sc.graphs.max_batch = max_streams
+        elif mode == "window":
+            graphs = Code2WavGraphs(self.model, max_streams) if use_graphs and dev.type == "cuda" else None
+            self.sc = StreamingCode2Wav(self.model, chunk, left_context, first_chunk, graphs=graphs)
+        else:
+            raise ValueError(f"code2wav mode {mode!r}: expected 'stateful' or 'window'")
         # its own high-priority stream: a chunk's kernels and its host copy wait for nothing
         # the thinker / talker threads queued
         self._stream = torch.cuda.Stream(device=dev, priority=-1) if dev.type == "cuda" else None
@@ -684,7 +701,7 @@ class Code2WavStreamingExecutor(ResultQueueMixin, Executor):
 
     def _capture(self):
         with torch.cuda.stream(self._stream), torch.inference_mode():
-            self.sc.graphs.capture_windows(self.sc.windows())
+            self.sc.capture_graphs()
 
     def _decode(self, ready, finals):
         """One batched decode of the ready streams on this stage's stream; host arrays."""
@@ -832,6 +849,8 @@ class Code2WavStreamingExecutor(ResultQueueMixin, Executor):
 
 def create_code2wav_executor(model_path: str = "", device: str = "cuda:0", chunk: int = 10,
                              left_context: int = 25, first_chunk: int | None = None, overrides: dict | None = None,
-                             use_graphs: bool = True, max_streams: int = 32):
+                             use_graphs: bool = True, max_streams: int = 32, mode: str = "stateful",
+                             max_open_streams: int = 128, max_frames: int = 16384):
     return Code2WavStreamingExecutor(model_path, device, chunk, left_context, first_chunk, overrides,
-                                     use_graphs=use_graphs, max_streams=max_streams)
+                                     use_graphs=use_graphs, max_streams=max_streams, mode=mode,
+                                     max_open_streams=max_open_streams, max_frames=max_frames)

@@ -74,7 +74,7 @@ def gather_kv_ref(cache: torch.Tensor, pages: list[int] | torch.Tensor, n: int) 
     return blk.permute(0, 2, 1, 3).reshape(need * PAGE, cache.shape[1], cache.shape[3])[:n]
 
 
-def paged_attention_ref(q, k_cache, v_cache, block_table, cu_q, kv_lens, scale, causal=True):
+def paged_attention_ref(q, k_cache, v_cache, block_table, cu_q, kv_lens, scale, causal=True, window=0):
     cu = cu_q.tolist()
     kl = kv_lens.tolist()
     out = torch.empty(q.shape, dtype=torch.float32, device=q.device)
@@ -84,7 +84,7 @@ def paged_attention_ref(q, k_cache, v_cache, block_table, cu_q, kv_lens, scale, 
             continue
         k = gather_kv_ref(k_cache, block_table[b], kl[b])
         v = gather_kv_ref(v_cache, block_table[b], kl[b])
-        out[a:e] = _sdpa_ref(q[a:e], k, v, causal, kl[b] - (e - a), scale)
+        out[a:e] = _sdpa_ref(q[a:e], k, v, causal, kl[b] - (e - a), scale, window)
     return out
 
 
@@ -101,25 +101,30 @@ def varlen_attention_ref(q, k, v, cu_seqlens, scale, causal=False, window=0):
 def prefill_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table: torch.Tensor,
                       cu_q: torch.Tensor, kv_lens: torch.Tensor, tile_req: torch.Tensor, tile_tok0: torch.Tensor,
                       num_heads: int, num_kv_heads: int, head_dim: int, scale: float | None = None,
-                      out: torch.Tensor | None = None, causal: bool = True, tile_rows: int = 64) -> torch.Tensor:
+                      out: torch.Tensor | None = None, causal: bool = True, tile_rows: int = 64,
+                      window: int = 0) -> torch.Tensor:
     """Causal prefill over the paged cache. q: [T, Hq * D] rows (any row stride).
 
     ``tile_rows``: rows of the tiles in tile_req / tile_tok0 (``prefill_tile_rows``): 128 runs
-    the tcgen05 kernel, 64 the mma.sync kernel."""
+    the tcgen05 kernel, 64 the mma.sync kernel.  ``window`` > 0 (64-row tiles only) limits
+    every query to its last ``window`` keys; pages wholly below a tile's first visible key are
+    never read, so a request's block-table row may reuse pages as a ring."""
     scale = scale if scale is not None else 1.0 / math.sqrt(head_dim)
     q3 = q.view(q.shape[0], -1) if q.dim() == 2 else q
     if out is None:
         out = torch.empty(q.shape[0], num_heads * head_dim, dtype=q.dtype, device=q.device)
     if not q.is_cuda:
         ref = paged_attention_ref(q3.reshape(q.shape[0], -1)[:, : num_heads * head_dim].view(-1, num_heads, head_dim),
-                                  k_cache, v_cache, block_table, cu_q, kv_lens, scale, causal)
+                                  k_cache, v_cache, block_table, cu_q, kv_lens, scale, causal, window)
         out.copy_(ref.reshape(out.shape))
         return out
+    if window > 0 and tile_rows != 64:
+        raise ValueError("prefill_attention: a sliding window needs the 64-row (mma.sync) tiles")
     if _check.enabled():
         _check.check_paged("attention_prefill", block_table, kv_lens, k_cache.shape[0], cu_q, q.shape[0])
         _check.check_tiles("attention_prefill", tile_req, tile_tok0, cu_q)
     ext().attention_prefill(q3, k_cache, v_cache, out, block_table, cu_q, kv_lens, None, tile_req, tile_tok0,
-                            num_heads, num_kv_heads, head_dim, scale, causal, 0, tile_rows, status_word(q.device))
+                            num_heads, num_kv_heads, head_dim, scale, causal, window, tile_rows, status_word(q.device))
     return out
 
 

@@ -2,7 +2,8 @@
 three launches, a few GB on the device at most):
 
     python -m sglang_omni_b200.ops.bench_cases {moe_w13|dense_prefill|decode_attn|decode_dense|
-                                                prefill_attn|rmsnorm|rope_store|moe_route|sample|time}
+                                                prefill_attn|rmsnorm|rope_store|moe_route|sample|time|
+                                                code2wav}
 
 Used to produce the ncu summaries of the hot kernels.
 """
@@ -131,6 +132,9 @@ def run(case: str) -> None:
             sample(logits.clone(), st)
     elif case == "time":
         _time_cases()
+        return
+    elif case == "code2wav":
+        _code2wav_chunk()
         return
     else:
         raise SystemExit(f"unknown case {case!r}")
@@ -270,6 +274,52 @@ def _time_cases() -> None:
         qkv.numel() * 2 + T * (hq + 2 * hkv) * d * 2)   # read q, k, v rows; write q in place, k / v pages
     for name, (us, nbytes) in res.items():
         print(f"{name:36s} {us:8.2f} us  {nbytes / us / 1e3:7.1f} GB/s")
+
+
+
+def _code2wav_chunk(streams: int = 32, chunk: int = 10, context: int = 25) -> None:
+    """Released-size Code2Wav (random bf16 weights), one steady streaming chunk of every stream:
+    the windowed decode (context + chunk frames per stream, one graph) against the stateful one
+    (the chunk's frames only, one graph).  CUDA events, L2 flushed, the GPU kept busy while the
+    host enqueues."""
+    from ..models.qwen3_omni.code2wav import Code2Wav, Code2WavConfig, Code2WavGraphs
+    from ..models.qwen3_omni.code2wav_stateful import StatefulGraphs, Code2WavStreamState
+
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+    m = Code2Wav(Code2WavConfig(), device="cuda").random_init_(seed=0)
+    Q = m.cfg.num_quantizers
+    codes = torch.randint(0, m.cfg.codebook_size, (streams, Q, context + chunk), device="cuda")
+    win = Code2WavGraphs(m, streams)
+    win.capture(streams, context + chunk)
+    state = Code2WavStreamState(m, streams, 4096, chunk)
+    sg = StatefulGraphs(state, streams)
+    sg.capture(streams, chunk, False)
+    slots = torch.arange(streams, device="cuda")
+    with torch.no_grad():   # three chunks of history per stream
+        state.step(codes[:, :, :chunk], slots, True)
+        for _ in range(2):
+            state.step(codes[:, :, :chunk], slots, False)
+
+    def t(fn, n=20):
+        for _ in range(3):
+            fn()
+        tot = 0.0
+        for _ in range(n):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda._sleep(200_000)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            tot += a.elapsed_time(b)
+        return tot / n * 1e3
+
+    with torch.no_grad():
+        tw = t(lambda: win(codes))
+        ts = t(lambda: sg(codes[:, :, :chunk], slots, False))
+    print(f"code2wav chunk, {streams} streams: windowed ({context}+{chunk} frames) {tw:9.1f} us   "
+          f"stateful ({chunk} frames) {ts:9.1f} us   ratio {tw / ts:5.2f}   state {state.state_bytes() / 2**20:.0f} MiB")
 
 
 if __name__ == "__main__":
