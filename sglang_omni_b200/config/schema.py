@@ -79,8 +79,9 @@ class PipelineConfig(BaseModel):
     request_timeout_s: float | None = None
 
     def model_post_init(self, __context: Any = None) -> None:
-        self._validate_general()
-        self._validate_fusion()
+        problems = self.problems()
+        if problems:
+            raise ValueError(f"invalid pipeline config {self.name!r}: " + "; ".join(problems))
         if self.config_cls is None or self.config_cls == "PipelineConfig":
             self.config_cls = self.__class__.__name__
 
@@ -94,53 +95,51 @@ class PipelineConfig(BaseModel):
                 return s
         raise KeyError(name)
 
-    def _validate_general(self) -> None:
-        if not self.model_path:
-            raise ValueError("model_path is required")
-        names = [s.name for s in self.stages]
-        if not names:
-            raise ValueError("pipeline must define at least one stage")
-        if len(names) != len(set(names)):
-            raise ValueError("stage names must be unique")
-        if self.entry_stage not in names:
-            raise ValueError(f"entry_stage {self.entry_stage!r} is not defined")
-        for s in self.stages:
-            if s.num_workers < 1:
-                raise ValueError(f"stage {s.name!r} needs at least one worker")
-            if not s.executor.factory:
-                raise ValueError(f"stage {s.name!r} missing executor factory")
-            if not s.get_next:
-                raise ValueError(f"stage {s.name!r} missing get_next")
-            if s.input_handler.type == "aggregated":
-                unknown = set(s.input_handler.sources or []) - set(names)
-                if unknown:
-                    raise ValueError(f"stage {s.name!r} has unknown sources: {sorted(unknown)}")
-            for st in s.stream_to:
-                if st.to_stage not in names:
-                    raise ValueError(f"stage {s.name!r} stream_to references unknown stage {st.to_stage!r}")
-        for t in self.terminal_stages:
-            if t not in names:
-                raise ValueError(f"terminal stage {t!r} is not defined")
+    def problems(self) -> list[str]:
+        """Every inconsistency of the config, in one pass (empty when it is usable).
 
-    def _validate_fusion(self) -> None:
-        if not self.fused_stages:
-            return
-        idx = {s.name: i for i, s in enumerate(self.stages)}
-        seen: set[str] = set()
-        for group in self.fused_stages:
+        The same conditions make a config unusable as in the reference's schema
+        (sglang_omni/config/schema.py:105-175): names referenced by the entry, routing,
+        aggregation, streaming, terminal and fusion fields must be stages; stage names are
+        unique; every stage has a factory, a routing function and a worker; a fused group
+        lists two or more adjacent stages in pipeline order, each stage in one group."""
+        out: list[str] = []
+        order = {}
+        for i, s in enumerate(self.stages):
+            if s.name in order:
+                out.append(f"two stages are named {s.name!r}")
+            order.setdefault(s.name, i)
+        if not self.model_path:
+            out.append("no model_path")
+        if not self.stages:
+            out.append("no stages")
+        elif self.entry_stage not in order:
+            out.append(f"entry stage {self.entry_stage!r} is not one of the stages {list(order)}")
+        for s in self.stages:
+            lacks = [what for what, ok in (("an executor factory", s.executor.factory), ("get_next", s.get_next),
+                                           ("a worker", s.num_workers >= 1)) if not ok]
+            if lacks:
+                out.append(f"stage {s.name!r} lacks " + ", ".join(lacks))
+            refs = [("stream target", st.to_stage) for st in s.stream_to]
+            if s.input_handler.type == "aggregated":
+                refs += [("aggregation source", src) for src in s.input_handler.sources or []]
+            out += [f"stage {s.name!r}: {what} {ref!r} is not a stage" for what, ref in refs if ref not in order]
+        out += [f"terminal stage {t!r} is not a stage" for t in self.terminal_stages if t not in order]
+        grouped: set[str] = set()
+        for group in self.fused_stages or []:
+            where = [order.get(n) for n in group]
             if len(group) < 2:
-                raise ValueError("fused_stages groups need at least 2 stage names")
-            for n in group:
-                if n not in idx:
-                    raise ValueError(f"fused stage {n!r} is not defined")
-                if n in seen:
-                    raise ValueError(f"stage {n!r} appears in multiple fused groups")
-                seen.add(n)
-            ii = [idx[n] for n in group]
-            if ii != sorted(ii):
-                raise ValueError(f"fused group is out of order: {group}")
-            if ii != list(range(ii[0], ii[0] + len(ii))):
-                raise ValueError(f"stages in the fused group are not adjacent: {group}")
+                out.append(f"fused group {group} has fewer than two stages")
+            if None in where:
+                out.append(f"fused group {group} names a stage that does not exist")
+                continue
+            if where != list(range(where[0], where[0] + len(where))):
+                out.append(f"fused group {group} is not a run of neighbouring stages in pipeline order")
+            again = grouped.intersection(group)
+            if again:
+                out.append(f"stages {sorted(again)} are in more than one fused group")
+            grouped.update(group)
+        return out
 
     def apply_fusion(self) -> tuple[list[StageConfig], dict[str, str], str]:
         """Collapses each fused group into one stage named after its last member."""

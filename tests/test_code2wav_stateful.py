@@ -11,9 +11,10 @@ from sglang_omni_b200.models.qwen3_omni.code2wav_stateful import (StatefulStream
                                                                   first_chunk_samples)
 
 
-def tiny(dtype=torch.float32, device="cpu", seed=3):
-    cfg = Code2WavConfig(codebook_size=32, hidden_size=64, num_heads=4, num_kv_heads=4, sliding_window=8,
-                         intermediate_size=128, num_layers=2, num_quantizers=4, upsample_rates=(2, 3),
+def tiny(dtype=torch.float32, device="cpu", seed=3, hidden=64):
+    """head_dim = hidden / 4 (the GPU kernels take head dims 32, 64, 96 and 128)."""
+    cfg = Code2WavConfig(codebook_size=32, hidden_size=hidden, num_heads=4, num_kv_heads=4, sliding_window=8,
+                         intermediate_size=2 * hidden, num_layers=2, num_quantizers=4, upsample_rates=(2, 3),
                          upsampling_ratios=(2,), decoder_dim=32, dtype=dtype)
     m = Code2Wav(cfg, device=device).random_init_(seed=seed, std=0.05)
     g = torch.Generator().manual_seed(seed)
@@ -113,7 +114,7 @@ def test_stateful_capacity_errors():
 def test_stateful_gpu_matches_cpu_oracle_and_graphs():
     """bf16 kernels (paged sliding-window attention over the KV ring, RoPE + KV store, conv
     GEMMs) against the fp32 full-sequence oracle, eager and through captured graphs."""
-    cpu = tiny(seed=11)
+    cpu = tiny(seed=11, hidden=256)     # head_dim 64, as in the released model
     cfg = Code2WavConfig(**{**cpu.cfg.__dict__, "dtype": torch.bfloat16})
     gpu = Code2Wav(cfg, device="cuda")
     with torch.no_grad():

@@ -4,7 +4,7 @@ import sys
 
 import pytest
 
-from sglang_omni_b200.config import ConfigManager, ExecutorConfig, PipelineConfig, StageConfig
+from sglang_omni_b200.config import ConfigManager, ExecutorConfig, PipelineConfig, StageConfig, StreamTargetConfig
 from sglang_omni_b200.models.registry import PIPELINE_CONFIG_REGISTRY
 from sglang_omni_b200.models.toy.config import ToyPipelineConfig
 from sglang_omni_b200.utils.misc import import_string
@@ -77,3 +77,17 @@ def test_console_script_declared():
     with pytest.raises(SystemExit) as e:
         main(["--help"])
     assert e.value.code == 0
+
+
+def test_validation_reports_every_problem_at_once():
+    bad = _stage("b")
+    bad.stream_to = [StreamTargetConfig(to_stage="nowhere")]
+    with pytest.raises(ValueError) as e:
+        PipelineConfig(model_path="", entry_stage="zz", stages=[_stage("a"), bad, _stage("a")],
+                       terminal_stages=["gone"], fused_stages=[["a", "missing"]])
+    msg = str(e.value)
+    for part in ("two stages are named 'a'", "no model_path", "entry stage 'zz'", "'nowhere' is not a stage",
+                 "terminal stage 'gone'", "names a stage that does not exist"):
+        assert part in msg, (part, msg)
+    ok = PipelineConfig(model_path="m", entry_stage="a", stages=[_stage("a"), _stage("b")])
+    assert ok.problems() == []
