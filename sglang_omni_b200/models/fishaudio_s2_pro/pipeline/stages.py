@@ -11,11 +11,12 @@ create_vocoder_executor and the incremental stream builder
 Streaming differs in where the work runs: the reference re-decodes every code
 so far on the CPU after 5 and then every 100 tokens; here a vocoder thread
 decodes on the GPU after ``stream_stride`` frames and then every
-``stream_followup_stride`` frames, over a window of at most
-``stream_context`` earlier frames (the decoder is causal; its convolutions
-see a few frames back and its transformer up to 128 frames per layer, so a
-48-frame context reproduces the full decode closely at a fraction of the cost).
-Ready windows of all streams are decoded together, one forward per window shape.
+``stream_followup_stride`` frames.  ``stream_mode="stateful"`` (default) keeps
+each stream's decoder state (``codec_stateful``): a chunk decodes only its new
+frames and the chunks add up to the full decode exactly.  ``"window"`` re-decodes
+a window of at most ``stream_context`` earlier frames before each chunk (the
+decoder is causal, so a 48-frame context reproduces the full decode closely).
+Ready streams are decoded together, one batched step per shape.
 """
 from __future__ import annotations
 
@@ -131,7 +132,7 @@ class S2ProTTSExecutor(ResultQueueMixin, Executor):
     def __init__(self, model_path: str = "", device: str = "cuda:0", max_streams: int = 64, max_context: int = 4096,
                  max_new_tokens: int = 2048, overrides: dict | None = None, use_graphs: bool = True,
                  stream_stride: int = 5, stream_followup_stride: int = 20, stream_context: int = 48,
-                 max_prefill_tokens: int = 8192):
+                 max_prefill_tokens: int = 8192, stream_mode: str = "stateful"):
         super().__init__()
         dev = torch.device(device)
         self.device = dev
@@ -144,6 +145,11 @@ class S2ProTTSExecutor(ResultQueueMixin, Executor):
         self.stream_stride = stream_stride
         self.stream_followup = stream_followup_stride
         self.stream_context = stream_context
+        if stream_mode not in ("stateful", "window"):
+            raise ValueError(f"stream_mode {stream_mode!r}: expected 'stateful' or 'window'")
+        self.stream_mode = stream_mode
+        self.max_streams = max_streams
+        self._stateful = None    # StatefulStreamingDAC, built by _prepare_vocoder
         self._cv = threading.Condition()
         self._new: deque = deque()
         self._aborted: set[str] = set()
@@ -159,6 +165,9 @@ class S2ProTTSExecutor(ResultQueueMixin, Executor):
 
     async def start(self):
         self._loop = asyncio.get_running_loop()
+        if self.stream_mode == "stateful" and self.device.type == "cuda":
+            # decoder weights, per-stream state and step graphs before the first request
+            await asyncio.to_thread(self._prepare_vocoder)
         if self._thread is None:
             self._thread = threading.Thread(target=self._run, name="s2pro-tts", daemon=True)
             self._thread.start()
@@ -229,6 +238,8 @@ class S2ProTTSExecutor(ResultQueueMixin, Executor):
         q = self._streams.pop(rid, None)
         if q is not None:
             self._post(q.put_nowait, None)
+        if self._stateful is not None:
+            self._voc_q.put((rid, None, None, True))   # frees the stream's decoder slot
 
     def _run(self):
         stream = own_stream(self.device)
@@ -306,6 +317,8 @@ class S2ProTTSExecutor(ResultQueueMixin, Executor):
                 gen.remove(rid)
                 self._pending.pop(rid, None)
                 self._codes.pop(rid, None)
+                if self._stateful is not None:
+                    self._voc_q.put((rid, None, None, True))
             new = [r for r in new if r not in aborted]
             streams = self._admit(new)
             # ragged prefill in groups that fit the prefill budget
@@ -338,22 +351,67 @@ class S2ProTTSExecutor(ResultQueueMixin, Executor):
             stop = any(j is None for j in jobs)
             latest: dict[str, tuple] = {}
             finals: set[str] = set()
+            closed: set[str] = set()
             for j in jobs:
                 if j is None:
                     continue
                 rid, codes, info, final = j
+                if codes is None:          # the stream ended or was aborted: release its state
+                    closed.add(rid)
+                    continue
                 if rid not in latest or len(codes) >= len(latest[rid][0]):
                     latest[rid] = (codes, info)
                 if final:
                     finals.add(rid)
             try:
-                self._decode_batch(latest)
+                if self.stream_mode == "stateful":
+                    self._decode_stateful(latest, finals)
+                else:
+                    self._decode_batch(latest)
             except Exception:
                 log.exception("stream vocoding failed")
             for rid in finals:
                 self._close_stream(rid)
+            if self._stateful is not None:
+                for rid in closed:
+                    self._stateful.close(rid)
             if stop:
                 return
+
+    def _prepare_vocoder(self):
+        """The stateful stream decoder: DAC weights, one state slot per generator stream, and
+        (on a GPU) the step graphs of the first chunk and the follow-up chunks."""
+        if self._stateful is not None:
+            return
+        from ..codec_stateful import StatefulStreamingDAC
+
+        if self._decoder is None:
+            self._decoder = loader.get_decoder(self.model_path, self.device, self.overrides)
+        sd = StatefulStreamingDAC(self._decoder, chunk=self.stream_followup, first_chunk=self.stream_stride,
+                                  max_streams=self.max_streams)
+        with torch.inference_mode():
+            sd.capture_graphs()
+        self._stateful = sd
+
+    def _decode_stateful(self, latest: dict[str, tuple], finals: set[str]):
+        if not latest:
+            return
+        self._prepare_vocoder()
+        sd = self._stateful
+        for rid, (codes, _) in latest.items():
+            have = sd.frames(rid)
+            if len(codes) > have:
+                sd.add_codes(rid, torch.tensor(codes[have:], dtype=torch.long)[:, 1:])
+        with torch.inference_mode():
+            out = sd.decode_ready(list(latest), finals=finals, to_host=True)
+        now = time.perf_counter()
+        rate = self._decoder.cfg.sample_rate
+        for rid, a in out.items():
+            info = latest[rid][1]
+            info["emitted"] += a.size
+            q = self._streams.get(rid)
+            if q is not None and a.size:
+                self._post(q.put_nowait, {"modality": "audio", "audio_waveform": a, "sample_rate": rate, "t": now})
 
     def _decode_batch(self, latest: dict[str, tuple]):
         if not latest:
@@ -387,10 +445,11 @@ class S2ProTTSExecutor(ResultQueueMixin, Executor):
 def create_tts_engine_executor(model_path: str = "", device: str = "cuda:0", max_new_tokens: int = 2048,
                                max_streams: int = 64, max_context: int = 4096, overrides: dict | None = None,
                                use_graphs: bool = True, stream_stride: int = 5, stream_followup_stride: int = 20,
-                               stream_context: int = 48, top_k: int | None = None):
-    """Same factory arguments as the reference (device, max_new_tokens, stream strides)."""
+                               stream_context: int = 48, top_k: int | None = None, stream_mode: str = "stateful"):
+    """Same factory arguments as the reference (device, max_new_tokens, stream strides);
+    ``stream_mode``: "stateful" (kept decoder state per stream) or "window"."""
     return S2ProTTSExecutor(model_path, device, max_streams, max_context, max_new_tokens, overrides, use_graphs,
-                            stream_stride, stream_followup_stride, stream_context)
+                            stream_stride, stream_followup_stride, stream_context, stream_mode=stream_mode)
 
 
 # alias of the reference's factory name, so configs written for it resolve

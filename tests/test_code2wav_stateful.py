@@ -74,7 +74,7 @@ def test_stateful_long_stream_ring_and_slot_reuse():
     b = torch.randint(0, 32, (4, 40), generator=g)
     c = torch.randint(0, 32, (4, 30), generator=g)
     outs = {"a": [], "b": [], "c": []}
-    assert sc.state.ring * 64 < 300
+    assert sc.state.kv.ring * 64 < 300
     for t in range(300):
         sc.add_codes("a", a[:, t])
         if t < 40:

@@ -168,6 +168,10 @@ def test_s2pro_pipeline_cpu_end_to_end():
             assert final.sample_rate == 44100
             if stream:
                 assert chunks and sum(c.size for c in chunks) == n
+                # the stateful stream decoder's chunks add up to the vocoder stage's full decode
+                np.testing.assert_allclose(np.concatenate(chunks).reshape(-1),
+                                           np.asarray(final.audio_data, dtype=np.float32).reshape(-1),
+                                           atol=1e-4, rtol=1e-3)
 
 
 @pytest.mark.gpu
