@@ -63,6 +63,8 @@ setup(
     package_data={"sglang_omni_b200": ["serve/playground.html"]},
     ext_modules=ext_modules,
     # the reference's command name (pyproject.toml:68 there): sgl-omni serve | config view | config export
-    entry_points={"console_scripts": ["sgl-omni=sglang_omni_b200.cli.cli:main"]},
+    # sgl-omni-bench: the online serving benchmarks (tts-speed | omni-speed | tts-wer)
+    entry_points={"console_scripts": ["sgl-omni=sglang_omni_b200.cli.cli:main",
+                                      "sgl-omni-bench=sglang_omni_b200.benchmarks.__main__:main"]},
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
 )

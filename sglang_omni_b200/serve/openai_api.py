@@ -5,7 +5,8 @@ Routes (same contract as sglang_omni/serve/openai_api.py:57-632):
                               deltas, a finish chunk with usage, ``[DONE]``
   POST /v1/audio/speech       raw audio bytes with X-Prompt-Tokens /
                               X-Completion-Tokens / X-Engine-Time headers, or
-                              SSE ``audio.speech.chunk`` events
+                              SSE ``audio.speech.chunk`` objects (``audio.data``
+                              base64), a closing one with usage, ``[DONE]``
   GET  /v1/models, GET /health (503 when the coordinator is not running)
   GET  /metrics               request counters and latency percentiles
 """
@@ -203,24 +204,44 @@ async def _chat_stream(client: Client, greq: GenerateRequest, rid: str, model: s
 
 
 async def _speech_stream(client: Client, greq: GenerateRequest, fmt: str, metrics: ServerMetrics):
+    """SSE of ``/v1/audio/speech``: one ``audio.speech.chunk`` object per audio delta (its
+    ``audio`` holds base64 data, format, mime type and sample rate), then a closing object
+    with ``audio: null``, the finish reason and usage, then ``[DONE]``.  The terminal result
+    carries the whole waveform: only its samples past those already streamed are sent."""
     t0 = time.perf_counter()
     first = None
     idx = 0
+    sent = 0          # samples streamed so far
+    finish, usage = None, None
+    kind = "pcm" if fmt == "pcm" else "wav"
+    sid = greq.request_id or f"speech-{uuid.uuid4().hex[:20]}"
     metrics.started()
     async for ch in client.generate(greq):
-        if ch.finish_reason is not None:
-            yield _sse({"type": "audio.speech.done", "usage": ch.usage.to_dict() if ch.usage else None})
+        terminal = ch.finish_reason is not None
+        if terminal:
+            finish = ch.finish_reason
+            usage = ch.usage.to_dict() if ch.usage else None
+        if ch.audio_data is not None:
+            data = ch.audio_data
+            if isinstance(data, (bytes, bytearray)):
+                data = np.frombuffer(data, dtype=np.float32)
+            data = np.asarray(data, dtype=np.float32).reshape(-1)
+            if terminal:
+                data = data[sent:]
+            if data.size:
+                if first is None:
+                    first = time.perf_counter() - t0
+                sent += data.size
+                rate = ch.sample_rate or 24000
+                audio = encode_audio(data, rate, kind)
+                yield _sse({"id": sid, "object": "audio.speech.chunk", "index": idx,
+                            "audio": {"data": base64.b64encode(audio).decode(), "format": kind,
+                                      "mime_type": f"audio/{kind}", "sample_rate": rate},
+                            "finish_reason": None})
+                idx += 1
+        if terminal:
             break
-        if ch.audio_data is None:
-            continue
-        if first is None:
-            first = time.perf_counter() - t0
-        data = ch.audio_data
-        if isinstance(data, (bytes, bytearray)):
-            data = np.frombuffer(data, dtype=np.float32)
-        audio = encode_audio(np.asarray(data, dtype=np.float32), ch.sample_rate or 24000, "pcm" if fmt == "pcm" else "wav")
-        yield _sse({"type": "audio.speech.chunk", "index": idx, "audio": base64.b64encode(audio).decode(),
-                    "format": "pcm" if fmt == "pcm" else "wav", "sample_rate": ch.sample_rate or 24000})
-        idx += 1
     metrics.finished(time.perf_counter() - t0, first, 0)
+    yield _sse({"id": sid, "object": "audio.speech.chunk", "index": idx, "audio": None,
+                "finish_reason": finish or "stop", "usage": usage})
     yield "data: [DONE]\n\n"
