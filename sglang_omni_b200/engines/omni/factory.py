@@ -27,10 +27,24 @@ def create_encoder_engine(encode_fn, max_batch_size: int = 32, device="cpu", cac
                       stream_priority=prio, poll_s=0.001)
 
 
-def create_ar_engine(model, **kw):
+def create_ar_engine(model, tokenizer=None, max_seq_len: int | None = None, device=None, **kw):
+    """AR engine over the paged engine.  ``model``: a ``DecoderLM``, or a transformers causal LM
+    (Llama / Mistral / Qwen2 / Qwen3 / Qwen3-MoE), converted first (``models.hf_text``), as the
+    reference's factory takes any HF model; ``max_seq_len`` bounds a request's context;
+    ``tokenizer`` is accepted for the reference's signature (detokenising happens in the stage)."""
+    from ...models.decoder import DecoderLM
     from ..ar import AREngine, KVPool
     from ..ar.adapter import PagedAREngineAdapter
 
+    if max_seq_len is not None:
+        kw.setdefault("max_context", int(max_seq_len))
+    if not isinstance(model, DecoderLM):
+        from ...models.hf_text import decoder_from_hf
+
+        from ...models.hf_text.convert import eos_token_ids
+
+        kw.setdefault("eos_token_ids", eos_token_ids(model))
+        model = decoder_from_hf(model, device or "cpu", max_position=kw.get("max_context"))
     cfg = model.cfg
     pages = kw.pop("kv_pages", None) or (kw.get("max_batch", 64) * ((kw.get("max_context", 4096) + 63) // 64) + 8)
     pool = KVPool(cfg.num_layers, cfg.num_kv_heads, cfg.head_dim, pages, model.embed.device, cfg.dtype)

@@ -57,6 +57,7 @@ class DecoderConfig:
     mlp_only_layers: tuple = ()
     rms_norm_eps: float = 1e-6
     rope_theta: float = 1e6
+    rope_scaling: dict | None = None    # HF rope_scaling: linear / llama3 frequency rescaling
     rope_neox: bool = True
     rotary_dim: int | None = None
     mrope_section: list | None = None   # e.g. [24, 20, 20]
@@ -205,7 +206,8 @@ class DecoderLM(nn.Module):
         head_rows = self._vslice[2] if tp is not None and vocab_parallel else cfg.vocab_size
         self.lm_head = None if cfg.tie_word_embeddings else P(head_rows, H)
         rot = cfg.rotary_dim or cfg.head_dim
-        cos, sin = ops.rope_tables(rot, cfg.rope_theta, cfg.max_position, device, round_bf16=cfg.dtype == torch.bfloat16)
+        cos, sin = ops.rope_tables(rot, cfg.rope_theta, cfg.max_position, device, round_bf16=cfg.dtype == torch.bfloat16,
+                                   scaling=cfg.rope_scaling)
         self.register_buffer("cos_tab", cos, persistent=False)
         self.register_buffer("sin_tab", sin, persistent=False)
         self._moe_ws: MoEWorkspace | None = None

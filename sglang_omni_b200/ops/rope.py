@@ -14,8 +14,37 @@ from . import _check
 from ._ext import ext
 
 
-def rope_tables(rot_dim: int, theta: float, max_pos: int, device=None, round_bf16: bool = True):
-    inv_freq = 1.0 / (theta ** (torch.arange(0, rot_dim, 2, dtype=torch.int64).float() / rot_dim))
+def rope_inv_freq(rot_dim: int, theta: float, scaling: dict | None = None) -> torch.Tensor:
+    """Rotation frequencies of the ``rot_dim / 2`` pairs: theta^(-2i / rot_dim), optionally
+    rescaled for a longer context than the model was trained at.
+
+    ``scaling`` (the ``rope_scaling`` / ``rope_parameters`` dict of an HF config):
+      * ``linear``: every frequency divided by ``factor`` (position interpolation);
+      * ``llama3``: the frequency-dependent rule published with Llama 3.1 -- pairs whose
+        wavelength (2 pi / f) is shorter than original_context / high_freq_factor keep f,
+        those longer than original_context / low_freq_factor get f / factor, and in between
+        f is blended between the two with weight s = (original_context / wavelength -
+        low_freq_factor) / (high_freq_factor - low_freq_factor) on the unscaled frequency.
+    Other kinds (dynamic NTK, YaRN, LongRoPE) are refused."""
+    f = 1.0 / (theta ** (torch.arange(0, rot_dim, 2, dtype=torch.int64).float() / rot_dim))
+    kind = (scaling or {}).get("rope_type", (scaling or {}).get("type", "default")) if scaling else "default"
+    if kind in (None, "default"):
+        return f
+    factor = float(scaling["factor"])
+    if kind == "linear":
+        return f / factor
+    if kind == "llama3":
+        ctx = float(scaling["original_max_position_embeddings"])
+        lo, hi = float(scaling.get("low_freq_factor", 1.0)), float(scaling.get("high_freq_factor", 4.0))
+        wavelength = 2 * torch.pi / f
+        w = ((ctx / wavelength - lo) / (hi - lo)).clamp(0.0, 1.0)   # 0: long wavelength, 1: short
+        return w * f + (1.0 - w) * (f / factor)
+    raise NotImplementedError(f"RoPE scaling {kind!r} is not supported (default, linear and llama3 are)")
+
+
+def rope_tables(rot_dim: int, theta: float, max_pos: int, device=None, round_bf16: bool = True,
+                scaling: dict | None = None):
+    inv_freq = rope_inv_freq(rot_dim, theta, scaling)
     pos = torch.arange(max_pos, dtype=torch.float32)
     freqs = pos[:, None] * inv_freq[None, :]
     cos, sin = freqs.cos(), freqs.sin()
