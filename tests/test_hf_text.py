@@ -175,6 +175,7 @@ def test_converted_llama_on_gpu_kernels_matches_transformers():
     fb = ForwardBatch(is_decode=False, positions=t.to(torch.int32).cuda(), slot_mapping=slots.cuda(),
                       kv_lens=i32([T]), block_table=i32([pages]), input_ids=i32(tokens), cu_q=i32([0, T]),
                       tile_req=i32(req), tile_tok0=i32(tok0))
+    ours.ensure_workspaces(T, 1, 256)
     with torch.no_grad():
         got = ours.logits(ours(fb, pool.kv)).float().cpu()
     rel = float((got - ref).norm() / ref.norm())
