@@ -13,17 +13,20 @@ from .scheduler import Scheduler
 
 
 def create_encoder_engine(encode_fn, max_batch_size: int = 32, device="cpu", cache_size: int = 64,
-                          gather_window_s: float = 0.008, high_priority: bool = True) -> OmniEngine:
+                          gather_window_s: float = 0.008, high_priority: bool = True,
+                          explicit_keys: bool = False) -> OmniEngine:
     """Encoders sit on the time-to-first-token/audio path: a short gathering window
     batches a burst of arrivals, and their steps run on a high-priority stream so
-    they are not queued behind other stages' decode work on the same GPU."""
+    they are not queued behind other stages' decode work on the same GPU.
+    ``cache_size`` > 0 keeps that many outputs by request key (``explicit_keys``: only
+    requests whose data carries a ``cache_key``; otherwise a hash of their inputs)."""
     sched = Scheduler(EncoderBatchPlanner(max_batch_size, gather_window_s), SimpleResourceManager(max_batch_size * 4),
                       SinglePassIterationController())
     runner = ModelRunner(EncoderModelWrapper(encode_fn), EncoderInputPreparer(), EncoderOutputProcessor(), device)
     prio = None
     if high_priority and torch.device(device).type == "cuda" and torch.cuda.is_available():
         prio = -1   # lower = higher priority; clamped by PyTorch to the device's range
-    return OmniEngine(sched, runner, SimpleCacheManager(cache_size) if cache_size else None,
+    return OmniEngine(sched, runner, SimpleCacheManager(cache_size, explicit_keys) if cache_size else None,
                       stream_priority=prio, poll_s=0.001)
 
 

@@ -22,6 +22,7 @@ class EncoderRequestData:
     inputs: dict[str, Any]
     skip: bool = False
     counts: dict[str, int] = field(default_factory=dict)
+    cache_key: str | None = None      # media key from preprocessing: equal keys reuse one output
 
 
 class EncoderBatchPlanner:

@@ -24,23 +24,26 @@ _N = "sglang_omni_b200.models.qwen3_omni.pipeline.next_stage"
 
 
 def text_stages(overrides=None, device="cuda:0", max_batch=64, max_context=4096, speech=False, tail_frames=50,
-                first_chunk=4, thinker_parallel: dict | None = None):
+                first_chunk=4, thinker_parallel: dict | None = None, encoder_cache: int = 64):
     """``first_chunk``: frames of the first Code2Wav chunk (later chunks are 10 frames of 80 ms);
-    ``thinker_parallel``: ``tp_size`` / ``ep_size`` / ``gpus`` of a thinker rank group."""
+    ``thinker_parallel``: ``tp_size`` / ``ep_size`` / ``gpus`` of a thinker rank group;
+    ``encoder_cache``: encoder outputs each tower keeps by media content key (0: every request's
+    media is encoded and preprocessing computes no keys)."""
     ov = {"overrides": overrides} if overrides else {}
+    cache = {"cache_size": int(encoder_cache)}
     thinker_args = {"device": device, "max_batch": max_batch, "max_context": max_context, **ov,
                     **(thinker_parallel or {})}
     if speech:
         thinker_args["speech_target"] = "talker_ar"
     stages = [
         StageConfig(name="preprocessing", executor=ExecutorConfig(factory=f"{_S}.create_preprocessing_executor",
-                                                                   args=dict(ov)),
+                                                                   args={**ov, "cache_keys": encoder_cache > 0}),
                     get_next=f"{_N}.preprocessing_next"),
         StageConfig(name="image_encoder", executor=ExecutorConfig(factory=f"{_S}.create_image_encoder_executor",
-                                                                   args={"device": device, **ov}),
+                                                                   args={"device": device, **ov, **cache}),
                     get_next=f"{_N}.encoder_next"),
         StageConfig(name="audio_encoder", executor=ExecutorConfig(factory=f"{_S}.create_audio_encoder_executor",
-                                                                   args={"device": device, **ov}),
+                                                                   args={"device": device, **ov, **cache}),
                     get_next=f"{_N}.encoder_next"),
         StageConfig(name="mm_aggregate", executor=ExecutorConfig(factory=f"{_S}.create_aggregate_executor"),
                     get_next=f"{_N}.aggregate_next",

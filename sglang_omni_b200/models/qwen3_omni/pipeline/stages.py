@@ -94,7 +94,12 @@ def _load_audio(item: Any) -> torch.Tensor:
     return torch.from_numpy(load_audio(item, SAMPLE_RATE_IN))
 
 
-def create_preprocessing_executor(model_path: str = "", overrides: dict | None = None):
+def create_preprocessing_executor(model_path: str = "", overrides: dict | None = None, cache_keys: bool = True):
+    """``cache_keys``: attach content keys of the request's audio and of its images + videos
+    (``preprocessing.cache_key``), so the encoder stages reuse outputs of media they encoded
+    before."""
+    from ....preprocessing.cache_key import media_cache_key
+
     tok = load_tokenizer(model_path)
     n_window = 50
 
@@ -114,6 +119,9 @@ def create_preprocessing_executor(model_path: str = "", overrides: dict | None =
     def preprocess(payload: StagePayload) -> StagePayload:
         trace.mark(payload.request_id, "0_preprocess_start")
         inp = payload.request.inputs if isinstance(payload.request.inputs, dict) else {}
+        raw_audios, raw_visual = list(inp.get("audios") or []), list(inp.get("images") or [])
+        n_raw_images = len(raw_visual)
+        raw_visual += list(inp.get("videos") or [])
         waves = [_load_audio(a) for a in (inp.get("audios") or [])]
         counts = [audio_tokens(w.numel()) for w in waves]
         images = [_load_image(im) for im in (inp.get("images") or [])]
@@ -146,6 +154,9 @@ def create_preprocessing_executor(model_path: str = "", overrides: dict | None =
                 "images": images, "image_spans": image_spans,
                 "mrope_positions": pos, "mrope_delta": delta,
                 "speech": _speech_requested(payload.request.params or {})}
+        if cache_keys:
+            data["audio_cache_key"] = media_cache_key("audio", raw_audios, sample_rate=16000, n_window=n_window)
+            data["image_cache_key"] = media_cache_key("vision", raw_visual, unit=unit, images=n_raw_images)
         return StagePayload(payload.request_id, payload.request, data)
 
     return PreprocessingExecutor(preprocess)
@@ -158,8 +169,9 @@ def _device(device: str) -> str:
 
 
 def create_audio_encoder_executor(model_path: str = "", device: str = "cuda:0", max_batch_size: int = 32,
-                                  overrides: dict | None = None, dtype=None):
-    """``dtype``: accepted for reference configs; the tower runs in its configured dtype."""
+                                  overrides: dict | None = None, dtype=None, cache_size: int = 64):
+    """``dtype``: accepted for reference configs; the tower runs in its configured dtype.
+    ``cache_size``: outputs kept by the media key preprocessing attached (0: no cache)."""
     dev = torch.device(_device(device))
     enc = loader.get_audio_encoder(model_path, dev, overrides)
     mel = LogMel(enc.cfg.num_mel_bins, dev)
@@ -182,12 +194,14 @@ def create_audio_encoder_executor(model_path: str = "", device: str = "cuda:0", 
             i += len(ws)
         return res
 
-    engine = create_encoder_engine(encode, max_batch_size=max_batch_size, device=dev, cache_size=0)
+    engine = create_encoder_engine(encode, max_batch_size=max_batch_size, device=dev, cache_size=cache_size,
+                                   explicit_keys=True)
 
     def request_builder(payload: StagePayload):
         trace.mark(payload.request_id, "0b_audio_encoder_queued")
         waves = (payload.data or {}).get("audio_waveforms") or []
-        return EncoderRequestData(inputs={"waves": waves}, skip=not waves)
+        return EncoderRequestData(inputs={"waves": waves}, skip=not waves,
+                                  cache_key=(payload.data or {}).get("audio_cache_key") if waves else None)
 
     def result_builder(payload: StagePayload, out):
         if not isinstance(out, dict):  # skipped request (no audio)
@@ -199,9 +213,10 @@ def create_audio_encoder_executor(model_path: str = "", device: str = "cuda:0", 
 
 
 def create_image_encoder_executor(model_path: str = "", device: str = "cuda:0", max_batch_size: int = 32,
-                                  overrides: dict | None = None, dtype=None):
+                                  overrides: dict | None = None, dtype=None, cache_size: int = 64):
     """The vision tower over a gathered burst of requests: one forward for every image of
-    the batch (ragged attention keeps images apart), split back per request."""
+    the batch (ragged attention keeps images apart), split back per request.  ``cache_size``:
+    outputs kept by the media key preprocessing attached (0: no cache)."""
     from ..vision_encoder import encode_images
 
     dev = torch.device(_device(device))
@@ -227,13 +242,15 @@ def create_image_encoder_executor(model_path: str = "", device: str = "cuda:0", 
             i += n
         return res
 
-    engine = create_encoder_engine(encode, max_batch_size=max_batch_size, device=dev, cache_size=0)
+    engine = create_encoder_engine(encode, max_batch_size=max_batch_size, device=dev, cache_size=cache_size,
+                                   explicit_keys=True)
 
     def request_builder(payload: StagePayload):
         images = (payload.data or {}).get("images") or []
         if images:
             trace.mark(payload.request_id, "0c_image_encoder_queued")
-        return EncoderRequestData(inputs={"images": images}, skip=not images)
+        return EncoderRequestData(inputs={"images": images}, skip=not images,
+                                  cache_key=(payload.data or {}).get("image_cache_key") if images else None)
 
     def result_builder(payload: StagePayload, out):
         if not isinstance(out, dict):  # skipped request (no image)
