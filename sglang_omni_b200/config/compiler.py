@@ -69,7 +69,9 @@ def _call_factory(factory_path: str, args: dict, model_path: str, gpu_id: int | 
     except (TypeError, ValueError):
         params = {}
     if "model_path" in params and "model_path" not in kwargs:
-        kwargs["model_path"] = model_path
+        from ..models.model_path import resolve_model_path
+
+        kwargs["model_path"] = resolve_model_path(model_path)
     if gpu_id is not None:
         if "gpu_id" in params and "gpu_id" not in kwargs:
             kwargs["gpu_id"] = gpu_id

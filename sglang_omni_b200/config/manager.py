@@ -79,8 +79,12 @@ class ConfigManager:
 
     @staticmethod
     def from_model_path(model_path: str, variant: str | None = None, **kw) -> PipelineConfig:
+        """``model_path``: a checkpoint directory or a Hugging Face Hub repository id (resolved to
+        its local snapshot, downloaded unless offline); the config keeps the path as given."""
+        from ..models.model_path import resolve_model_path
+
         arch = None
-        cfg_file = os.path.join(model_path, "config.json")
+        cfg_file = os.path.join(resolve_model_path(model_path), "config.json")
         if os.path.exists(cfg_file):
             with open(cfg_file) as f:
                 d = json.load(f)
