@@ -178,16 +178,28 @@ def get_audio_encoder(model_path: str, device, overrides: dict | None = None) ->
         return m
 
 
+def vision_config(model_path: str, overrides: dict | None = None):
+    """The vision tower's config: defaults, the checkpoint processors' resize bounds, then the
+    ``vision`` overrides (preprocessing builds the same one, so token grids agree)."""
+    from ...preprocessing.vision_grid import checkpoint_bounds
+    from .vision_encoder import VisionConfig
+
+    b = checkpoint_bounds(model_path)
+    cfg = VisionConfig(min_pixels=b.image_min, max_pixels=b.image_max, video_min_pixels=b.video_min,
+                       video_max_pixels=b.video_max)
+    return _apply(cfg, (overrides or {}).get("vision"))
+
+
 def get_vision_encoder(model_path: str, device, overrides: dict | None = None):
-    from .vision_encoder import Qwen3OmniVisionEncoder, VisionConfig
+    from .vision_encoder import Qwen3OmniVisionEncoder
 
     k = _key(model_path, "vision", device, overrides)
     with _LOCK:
         if k in _CACHE:
             return _CACHE[k]
-        cfg = VisionConfig()
-        cfg.out_hidden_size = _apply(_cfgs(model_path)["thinker"], (overrides or {}).get("thinker")).hidden_size
-        _apply(cfg, (overrides or {}).get("vision"))
+        cfg = vision_config(model_path, overrides)
+        if "out_hidden_size" not in ((overrides or {}).get("vision") or {}):
+            cfg.out_hidden_size = _apply(_cfgs(model_path)["thinker"], (overrides or {}).get("thinker")).hidden_size
         m = Qwen3OmniVisionEncoder(cfg, device)
         if has_checkpoint(model_path):
             m.load_hf_state_dict(load_by_prefix(model_path, "thinker.visual."))

@@ -111,9 +111,9 @@ def create_preprocessing_executor(model_path: str = "", overrides: dict | None =
         full, rem = divmod(frames, cs)
         return full * cnn_out_len(cs) + (cnn_out_len(rem) if rem else 0)
 
-    from ..vision_encoder import VisionConfig
+    from ....preprocessing.vision_grid import resize_grid
 
-    vcfg = VisionConfig()
+    vcfg = loader.vision_config(model_path, overrides)
     unit = vcfg.patch_size * vcfg.spatial_merge_size
 
     def preprocess(payload: StagePayload) -> StagePayload:
@@ -127,15 +127,14 @@ def create_preprocessing_executor(model_path: str = "", overrides: dict | None =
         images = [_load_image(im) for im in (inp.get("images") or [])]
         grids = []
         for im in images:
-            th = max(unit, round(im.shape[0] / unit) * unit)
-            tw = max(unit, round(im.shape[1] / unit) * unit)
+            th, tw = resize_grid(im.shape[0], im.shape[1], unit, vcfg.min_pixels, vcfg.max_pixels)
             grids.append((1, th // unit, tw // unit))
         from ....preprocessing.media import load_video, video_grid
 
         if (payload.request.params or {}).get("use_audio_in_video"):
             raise ValueError("use_audio_in_video is not supported: pass the video's audio track in 'audios'")
         videos = [load_video(v) for v in (inp.get("videos") or [])]
-        vgrids = [video_grid(v["frames"], unit) for v in videos]
+        vgrids = [video_grid(v["frames"], unit, vcfg.video_max_pixels, vcfg.video_min_pixels) for v in videos]
         if inp.get("prompt_token_ids") is not None and not waves and not images and not videos:
             ids = list(inp["prompt_token_ids"])
             p = torch.arange(len(ids), dtype=torch.int32)

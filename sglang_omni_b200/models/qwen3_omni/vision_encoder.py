@@ -24,6 +24,8 @@ import numpy as np
 import torch
 from torch import nn
 
+from ...preprocessing.vision_grid import (IMAGE_MAX_PIXELS, IMAGE_MIN_PIXELS, VIDEO_MAX_PIXELS, VIDEO_MIN_PIXELS,
+                                          resize_grid)
 from ... import ops
 
 IMAGE_MEAN = (0.5, 0.5, 0.5)
@@ -44,6 +46,11 @@ class VisionConfig:
     num_position_embeddings: int = 2304
     deepstack_visual_indexes: list = field(default_factory=lambda: [8, 16, 24])
     dtype: torch.dtype = torch.bfloat16
+    # target-size bounds of the checkpoint's image / video processors (preprocessing.vision_grid)
+    min_pixels: int = IMAGE_MIN_PIXELS
+    max_pixels: int = IMAGE_MAX_PIXELS
+    video_min_pixels: int = VIDEO_MIN_PIXELS
+    video_max_pixels: int = VIDEO_MAX_PIXELS
 
     @property
     def head_dim(self):
@@ -259,14 +266,13 @@ class Qwen3OmniVisionEncoder(nn.Module):
 def image_to_patches(img: np.ndarray, cfg: VisionConfig, size: int | None = None):
     """uint8 RGB [H, W, 3] -> (patches [N, patch_dim] float32, grid (t, h, w)).
 
-    The image is resized (nearest) to a multiple of patch*merge, normalised,
-    repeated to the temporal patch size, and cut into patches in the merge-
-    block order the encoder expects."""
+    The image is resized (nearest) to the processor's target size (a multiple of patch*merge
+    within the config's pixel bounds, ``vision_grid.resize_grid``), normalised, repeated to the
+    temporal patch size, and cut into patches in the merge-block order the encoder expects."""
     p, ms, tp = cfg.patch_size, cfg.spatial_merge_size, cfg.temporal_patch_size
     H, W = img.shape[:2]
     unit = p * ms
-    th = size or max(unit, round(H / unit) * unit)
-    tw = size or max(unit, round(W / unit) * unit)
+    th, tw = (size, size) if size else resize_grid(H, W, unit, cfg.min_pixels, cfg.max_pixels)
     if (th, tw) != (H, W):
         yi = (np.arange(th) * H / th).astype(int)
         xi = (np.arange(tw) * W / tw).astype(int)
@@ -294,8 +300,7 @@ def images_to_patches_device(images: list[np.ndarray], cfg: VisionConfig, device
     grids: list = [None] * len(images)
     for shape, idxs in by_shape.items():
         H, W = shape[:2]
-        th = max(unit, round(H / unit) * unit)
-        tw = max(unit, round(W / unit) * unit)
+        th, tw = resize_grid(H, W, unit, cfg.min_pixels, cfg.max_pixels)
         host = torch.from_numpy(np.ascontiguousarray(np.stack([images[i] for i in idxs]))).pin_memory()
         x = host.to(device, non_blocking=True)                                # [b, H, W, 3] uint8
         if (th, tw) != (H, W):
@@ -314,16 +319,19 @@ def images_to_patches_device(images: list[np.ndarray], cfg: VisionConfig, device
     return torch.cat(parts, 0), grids
 
 
-def video_to_patches(frames: np.ndarray, cfg: VisionConfig, max_pixels: int = 448 * 448):
+def video_to_patches(frames: np.ndarray, cfg: VisionConfig, max_pixels: int | None = None,
+                     min_pixels: int | None = None):
     """uint8 RGB frames [N, H, W, 3] (N a multiple of the temporal patch) -> (patches
     [t * gh * gw, patch_dim] float32, grid (t, gh, gw)): every frame resized (nearest) to the
-    grid of ``media.video_grid``, normalised, consecutive frame pairs forming one temporal
-    patch, cut in the merge-block order of the encoder (the image path with t > 1)."""
+    grid of ``media.video_grid`` (the config's video pixel bounds unless given), normalised,
+    consecutive frame pairs forming one temporal patch, cut in the merge-block order of the
+    encoder (the image path with t > 1)."""
     from ...preprocessing.media import video_grid
 
     p, ms, tp = cfg.patch_size, cfg.spatial_merge_size, cfg.temporal_patch_size
     n, H, W = frames.shape[:3]
-    t, mh, mw = video_grid(frames, p * ms, max_pixels)
+    t, mh, mw = video_grid(frames, p * ms, cfg.video_max_pixels if max_pixels is None else max_pixels,
+                           cfg.video_min_pixels if min_pixels is None else min_pixels)
     th, tw = mh * p * ms, mw * p * ms
     if (th, tw) != (H, W):
         yi = (np.arange(th) * H / th).astype(int)

@@ -201,11 +201,14 @@ def load_audio(item: Any, target_sr: int = SAMPLE_RATE) -> np.ndarray:
     return resample(x, int(sr), target_sr)
 
 
-def video_grid(frames: np.ndarray, unit: int, max_pixels: int = 448 * 448) -> tuple[int, int, int]:
-    """Merged (t, h, w) token grid of sampled frames: each frame resized to a multiple of
-    `unit` (patch x merge) within max_pixels."""
+def video_grid(frames: np.ndarray, unit: int, max_pixels: int | None = None,
+               min_pixels: int | None = None) -> tuple[int, int, int]:
+    """Merged (t, h, w) token grid of sampled frames: each frame resized to the video
+    processor's target size (a multiple of `unit` = patch x merge within the pixel bounds,
+    ``vision_grid.resize_grid``)."""
+    from .vision_grid import VIDEO_MAX_PIXELS, VIDEO_MIN_PIXELS, resize_grid
+
     n, H, W = frames.shape[:3]
-    scale = min(1.0, math.sqrt(max_pixels / float(H * W)))
-    th = max(unit, int(round(H * scale / unit)) * unit)
-    tw = max(unit, int(round(W * scale / unit)) * unit)
+    th, tw = resize_grid(H, W, unit, VIDEO_MIN_PIXELS if min_pixels is None else min_pixels,
+                         VIDEO_MAX_PIXELS if max_pixels is None else max_pixels)
     return n // TEMPORAL_PATCH, th // unit, tw // unit

@@ -72,7 +72,7 @@ def test_vision_video_matches_hf_cpu():
     m, ours = tiny()
     rng = np.random.default_rng(3)
     frames = rng.integers(0, 256, (4, 16, 24, 3), dtype=np.uint8)
-    px, grid = video_to_patches(frames, ours.cfg, max_pixels=16 * 24)
+    px, grid = video_to_patches(frames, ours.cfg, max_pixels=16 * 24, min_pixels=16)
     assert grid == (2, 4, 6)
     with torch.no_grad():
         ref = m(px, grid_thw=torch.tensor([grid]))
@@ -98,3 +98,31 @@ def test_device_patch_extraction_matches_host():
     assert grids == [g for _, g in refs]
     ref = torch.cat([p for p, _ in refs], 0)
     torch.testing.assert_close(got.cpu(), ref, atol=1e-6, rtol=1e-6)
+
+
+def test_resize_grid_matches_the_hf_processor_rule():
+    """Target sizes of images / video frames equal transformers' Qwen2-VL-family smart_resize
+    (token counts match the processor the checkpoint was trained with), and the checkpoint's
+    processor configs set the bounds."""
+    import json
+    import random
+
+    from transformers.models.qwen2_vl.image_processing_qwen2_vl import smart_resize
+
+    from sglang_omni_b200.preprocessing.vision_grid import checkpoint_bounds, resize_grid
+
+    rnd = random.Random(0)
+    for _ in range(3000):
+        h, w = rnd.randint(16, 5000), rnd.randint(16, 5000)
+        if max(h, w) > 200 * min(h, w):
+            continue
+        f, lo, hi = rnd.choice([28, 32]), rnd.choice([3136, 131072]), rnd.choice([786432, 12845056])
+        assert tuple(smart_resize(h, w, f, lo, hi)) == resize_grid(h, w, f, lo, hi), (h, w, f, lo, hi)
+    import tempfile
+    with tempfile.TemporaryDirectory() as d:
+        with open(f"{d}/preprocessor_config.json", "w") as fh:
+            json.dump({"min_pixels": 1000, "max_pixels": 2000000}, fh)
+        with open(f"{d}/video_preprocessor_config.json", "w") as fh:
+            json.dump({"size": {"shortest_edge": 4096, "longest_edge": 90000}}, fh)
+        b = checkpoint_bounds(d)
+        assert (b.image_min, b.image_max, b.video_min, b.video_max) == (1000, 2000000, 4096, 90000)
