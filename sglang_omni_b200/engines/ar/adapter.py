@@ -30,6 +30,16 @@ class PagedAREngineAdapter:
             self.threaded.stop()
             self._started = False
 
+    def stats(self) -> dict:
+        """Scheduler queues and KV-cache occupancy of the paged engine (read without locking:
+        a snapshot for monitoring)."""
+        e = self.engine
+        pool = e.pool
+        used = pool.num_pages - pool.free_pages
+        return {"requests_running": len(e.running), "requests_waiting": len(e.waiting),
+                "kv_pages_used": used, "kv_pages_total": pool.num_pages,
+                "kv_usage": round(used / pool.num_pages, 4) if pool.num_pages else 0.0}
+
     async def generate(self, rid: str, req: ARRequest, on_chunk=None, stream_fn=None) -> ARRequest:
         self.start()
         if self.threaded.error is not None:

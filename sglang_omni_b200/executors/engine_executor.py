@@ -28,6 +28,14 @@ class EngineExecutor(ResultQueueMixin, Executor):
         self._tasks: dict[str, asyncio.Task] = {}
         self._streams: dict[str, asyncio.Queue] = {}
 
+
+    def stats(self) -> dict:
+        """Requests in this executor, plus the engine's own counters when it reports any."""
+        out = {"requests_active": len(self._tasks)}
+        fn = getattr(self.engine, "stats", None)
+        if fn is not None:
+            out.update(fn())
+        return out
     async def start(self):
         if hasattr(self.engine, "start"):
             r = self.engine.start()

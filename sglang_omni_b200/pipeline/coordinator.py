@@ -18,7 +18,8 @@ from dataclasses import dataclass, field
 from typing import Any, AsyncIterator
 
 from ..proto import (AbortMessage, CompleteMessage, OmniRequest, ProfilerStartMessage, ProfilerStopMessage,
-                     RequestInfo, RequestState, ShutdownMessage, StagePayload, StreamMessage, SubmitMessage)
+                     RequestInfo, RequestState, ShutdownMessage, StagePayload, StageStatsMessage, StreamMessage,
+                     SubmitMessage)
 from .control_plane import CoordinatorControlPlane
 
 log = logging.getLogger(__name__)
@@ -47,6 +48,7 @@ class Coordinator:
         self.entry_stage = entry_stage
         self.terminal_stages = list(terminal_stages or [])
         self.stage_endpoints: dict[str, str] = {}
+        self.stage_stats: dict[str, dict] = {}    # last load report of each stage
         self._reqs: dict[str, _Req] = {}
         self._done_states: dict[str, RequestState] = {}
         self.max_retained = max_retained
@@ -136,6 +138,8 @@ class Coordinator:
             try:
                 if isinstance(msg, CompleteMessage):
                     await self._handle_completion(msg)
+                elif isinstance(msg, StageStatsMessage):
+                    self.stage_stats[msg.stage] = {**msg.stats, "_t": time.monotonic()}
                 elif isinstance(msg, StreamMessage):
                     r = self._reqs.get(msg.request_id)
                     if r is not None and r.stream is not None:
@@ -195,4 +199,11 @@ class Coordinator:
         counts[RequestState.RUNNING.value] = len(self._reqs)
         for st in self._done_states.values():
             counts[st.value] += 1
-        return {"running": self.running, "requests": counts, "stages": list(self.stage_endpoints)}
+        return {"running": self.running, "requests": counts, "stages": list(self.stage_endpoints),
+                "stage_stats": self.latest_stage_stats()}
+
+    def latest_stage_stats(self) -> dict:
+        """Each stage's last load report, with its age in seconds."""
+        now = time.monotonic()
+        return {n: {**{k: v for k, v in st.items() if k != "_t"}, "age_s": round(now - st["_t"], 3)}
+                for n, st in self.stage_stats.items()}

@@ -19,7 +19,7 @@ import logging
 import os
 
 from ...proto import (AbortMessage, CompleteMessage, DataReadyMessage, ProfilerStartMessage, ProfilerStopMessage,
-                      ShutdownMessage, SubmitMessage)
+                      ShutdownMessage, StageStatsMessage, SubmitMessage)
 from ..control_plane import StageControlPlane
 from ..worker.data_plane import DataPlaneAdapter
 from .input import DirectInput, InputHandler
@@ -44,6 +44,8 @@ class Stage:
         self._tasks: list[asyncio.Task] = []
         self._profiler = None
         self.messages_received = 0
+        # seconds between load reports to the coordinator (0: none)
+        self.stats_interval_s = float(os.environ.get("OMNI_STAGE_STATS_S", "1.0"))
 
     def add_worker(self, worker) -> None:
         self.workers.append(worker)
@@ -69,6 +71,8 @@ class Stage:
     async def run(self):
         self._tasks = [asyncio.ensure_future(w.run()) for w in self.workers]
         self._tasks.append(asyncio.ensure_future(self._abort_loop()))
+        if self.stats_interval_s > 0:
+            self._tasks.append(asyncio.ensure_future(self._stats_loop()))
         try:
             while self._running:
                 msg = await self.cp.recv()
@@ -155,6 +159,31 @@ class Stage:
         if self._profiler is not None:
             self._profiler.stop()
             self._profiler = None
+
+    def stats(self) -> dict:
+        """Queue depth over the workers, messages received, and what the executors report
+        (an engine's running / waiting requests, KV-cache pages in use)."""
+        out = {"queue_depth": sum(w.queue.qsize() for w in self.workers if hasattr(w, "queue")),
+               "messages": self.messages_received}
+        for w in self.workers:
+            fn = getattr(w.executor, "stats", None)
+            if fn is None:
+                continue
+            try:
+                for k, v in (fn() or {}).items():
+                    if isinstance(v, (int, float)) and not isinstance(v, bool):
+                        out[k] = out.get(k, 0) + v
+            except Exception:
+                log.debug("stats of %s failed", self.name, exc_info=True)
+        return out
+
+    async def _stats_loop(self):
+        while self._running:
+            await asyncio.sleep(self.stats_interval_s)
+            try:
+                await self.cp.send_to_coordinator(StageStatsMessage(self.name, self.stats()))
+            except Exception:
+                log.debug("stats report of %s failed", self.name, exc_info=True)
 
     def health(self) -> dict:
         return {"stage": self.name, "running": self._running, "workers": len(self.workers),

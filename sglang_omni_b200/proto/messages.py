@@ -162,10 +162,24 @@ class ProfilerStopMessage:
         return cls(d["run_id"])
 
 
+@dataclass
+class StageStatsMessage:
+    """Periodic load report of a stage to the coordinator (queue depth, engine state)."""
+    stage: str
+    stats: dict
+
+    def to_dict(self):
+        return {"type": "stage_stats", "stage": self.stage, "stats": self.stats}
+
+    @classmethod
+    def from_dict(cls, d):
+        return cls(d["stage"], dict(d.get("stats") or {}))
+
+
 _TYPES = {
     "data_ready": DataReadyMessage, "abort": AbortMessage, "complete": CompleteMessage, "stream": StreamMessage,
     "submit": SubmitMessage, "shutdown": ShutdownMessage, "profiler_start": ProfilerStartMessage,
-    "profiler_stop": ProfilerStopMessage,
+    "profiler_stop": ProfilerStopMessage, "stage_stats": StageStatsMessage,
 }
 
 

@@ -83,6 +83,20 @@ def build_speech_generate_request(req: CreateSpeechRequest) -> GenerateRequest:
                                      "instructions": req.instructions, "response_format": req.response_format})
 
 
+def stage_prometheus(stages: dict, prefix: str = "omni_stage") -> str:
+    """Gauges ``omni_stage_<field>{stage="<name>"}`` of the numeric fields of the stage reports."""
+    fields: dict[str, list[str]] = {}
+    for name, st in sorted(stages.items()):
+        for k, v in sorted(st.items()):
+            if isinstance(v, (int, float)) and not isinstance(v, bool) and k.replace("_", "").isalnum():
+                fields.setdefault(k, []).append(f'{prefix}_{k}{{stage="{name}"}} {v}')
+    out = []
+    for k, lines in fields.items():
+        out.append(f"# TYPE {prefix}_{k} gauge")
+        out += lines
+    return "\n".join(out) + ("\n" if out else "")
+
+
 def create_app(client: Client, model_name: str = "model") -> FastAPI:
     app = FastAPI(title="sglang-omni-b200")
     metrics = ServerMetrics()
@@ -97,9 +111,14 @@ def create_app(client: Client, model_name: str = "model") -> FastAPI:
 
     @app.get("/metrics")
     async def get_metrics(format: str = "json"):
+        """Request counters and latency percentiles of this server, and every stage's last load
+        report (queue depth, requests in its engine, KV-cache pages in use)."""
+        coord = getattr(client, "coordinator", None)
+        stages = coord.latest_stage_stats() if coord is not None and hasattr(coord, "latest_stage_stats") else {}
         if format == "prometheus":
-            return Response(content=metrics.prometheus(), media_type="text/plain; version=0.0.4")
-        return metrics.snapshot()
+            return Response(content=metrics.prometheus() + stage_prometheus(stages),
+                            media_type="text/plain; version=0.0.4")
+        return {**metrics.snapshot(), "stages": stages}
 
     @app.get("/v1/models")
     async def models():
