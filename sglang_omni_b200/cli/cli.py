@@ -29,7 +29,9 @@ def cmd_serve(args, extra):
     from ..serve import launch_server
 
     cfg = _load(args, extra)
-    launch_server(cfg, host=args.host, port=args.port, model_name=args.model_name, log_level=args.log_level)
+    restart = [s for s in (args.restart_stages or "").split(",") if s]
+    launch_server(cfg, host=args.host, port=args.port, model_name=args.model_name, log_level=args.log_level,
+                  restart_stages=restart)
 
 
 def cmd_config(args, extra):
@@ -56,6 +58,8 @@ def main(argv=None):
     s.add_argument("--port", type=int, default=8000)
     s.add_argument("--model-name")
     s.add_argument("--log-level", default="info")
+    s.add_argument("--restart-stages", default="",
+                   help="comma-separated stages whose process is restarted when it dies (multi-GPU placements)")
     c = sub.add_parser("config")
     c.add_argument("action", choices=["view", "export"])
     c.add_argument("--model-path")

@@ -5,7 +5,9 @@ its stage from the (picklable) config, binds its control socket, signals
 readiness and runs until shutdown.  The parent hosts the coordinator, waits
 for every child with a bounded startup timeout (rolling back on failure),
 and monitors liveness: a dead stage fails the pipeline instead of leaving
-requests hanging.  With ``relay_backend: nccl`` the stage processes form one
+requests hanging -- or, with ``restart``, the runner fails the requests in
+flight, starts a new process for that stage on the same endpoints and keeps
+serving (the reference has no recovery; this is the optional one of the plan).  With ``relay_backend: nccl`` the stage processes form one
 torch.distributed NCCL group (rank = stage index) for point-to-point relays.
 
 Reference counterpart: sglang_omni/pipeline/mp_runner.py:203-486.
@@ -90,8 +92,19 @@ def _stage_process_entry(cfg_dict: dict, cfg_cls_path: str | None, stage_index: 
 
 
 class MultiProcessPipelineRunner:
-    def __init__(self, cfg: PipelineConfig, startup_timeout: float | None = None, monitor_interval: float = 5.0):
+    def __init__(self, cfg: PipelineConfig, startup_timeout: float | None = None, monitor_interval: float = 5.0,
+                 restart: bool | list[str] = False, max_restarts: int = 3):
+        """``restart``: True (every stage that can be restarted) or the names of such stages.
+        A stage can be restarted unless the pipeline relays over NCCL (a new process cannot
+        join the stage processes' group) or a rank group serves it (tp_size / ep_size > 1).
+        A restart fails every request in flight: the runner does not know which of them held
+        state in the dead stage.  After ``max_restarts`` restarts of one stage its next death
+        stops the pipeline."""
         self.cfg = cfg
+        self.restart = restart
+        self.max_restarts = max_restarts
+        self.restarts: dict[str, int] = {}
+        self._spawn_args: dict[str, tuple] = {}
         self.startup_timeout = startup_timeout or float(os.environ.get("SGLANG_OMNI_STARTUP_TIMEOUT", "600"))
         self.monitor_interval = monitor_interval
         self.run_id = uuid.uuid4().hex[:10]
@@ -118,12 +131,10 @@ class MultiProcessPipelineRunner:
         cls = type(self.cfg)
         cls_path = None if cls is PipelineConfig else f"{cls.__module__}.{cls.__qualname__}"
         events = []
+        self._ctx, self._dist = ctx, dist_env
         for i, n in enumerate(names):
-            ready, failed = ctx.Event(), ctx.Event()
-            p = ctx.Process(target=_stage_process_entry, name=f"stage-{n}",
-                            args=(self.cfg.model_dump(), cls_path, i, self.run_id, ready, failed, dist_env),
-                            daemon=True)
-            p.start()
+            self._spawn_args[n] = (i, cls_path)
+            p, ready, failed = self._spawn(n)
             self.procs.append(p)
             events.append((n, p, ready, failed))
         deadline = time.monotonic() + self.startup_timeout
@@ -140,11 +151,51 @@ class MultiProcessPipelineRunner:
         self._loop_task = self.coordinator.start_completion_loop()
         self._monitor = asyncio.ensure_future(self._monitor_children(names))
 
+    def _spawn(self, name: str):
+        i, cls_path = self._spawn_args[name]
+        ready, failed = self._ctx.Event(), self._ctx.Event()
+        p = self._ctx.Process(target=_stage_process_entry, name=f"stage-{name}",
+                              args=(self.cfg.model_dump(), cls_path, i, self.run_id, ready, failed, self._dist),
+                              daemon=True)
+        p.start()
+        return p, ready, failed
+
+    def restartable(self, name: str) -> bool:
+        if not self.restart or self._dist is not None:
+            return False
+        if isinstance(self.restart, (list, tuple, set)) and name not in self.restart:
+            return False
+        st = next(s for s in self.cfg.apply_fusion()[0] if s.name == name)
+        return not any(int(st.executor.args.get(k, 1) or 1) > 1 for k in ("tp_size", "ep_size"))
+
+    def _fail_in_flight(self, why: str):
+        for rid in list(self.coordinator._reqs):
+            self.coordinator._finish(rid, self.coordinator._reqs[rid].info.state.__class__.FAILED,
+                                     exc=RuntimeError(why))
+
+    async def _restart(self, idx: int, name: str, exitcode) -> bool:
+        """Replaces a dead stage process; False if the new one did not come up in time."""
+        self.restarts[name] = self.restarts.get(name, 0) + 1
+        log.error("stage process %s exited with %s; failing requests in flight and restarting it (%d of %d)",
+                  name, exitcode, self.restarts[name], self.max_restarts)
+        self._fail_in_flight(f"stage {name} died and was restarted")
+        p, ready, failed = self._spawn(name)
+        self.procs[idx] = p
+        deadline = time.monotonic() + self.startup_timeout
+        while not ready.is_set():
+            if failed.is_set() or not p.is_alive() or time.monotonic() > deadline:
+                return False
+            await asyncio.sleep(0.05)
+        return True
+
     async def _monitor_children(self, names):
         while True:
             await asyncio.sleep(self.monitor_interval)
-            for n, p in zip(names, self.procs):
+            for idx, (n, p) in enumerate(zip(names, list(self.procs))):
                 if not p.is_alive():
+                    if self.restartable(n) and self.restarts.get(n, 0) < self.max_restarts:
+                        if await self._restart(idx, n, p.exitcode):
+                            continue
                     self.failed_stage = n
                     log.error("stage process %s exited with %s; stopping the pipeline", n, p.exitcode)
                     self.coordinator.running = False

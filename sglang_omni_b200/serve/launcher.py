@@ -43,13 +43,16 @@ def _mount_profiler_routes(app, coordinator):
         return {"ok": True}
 
 
-async def build_server(cfg: PipelineConfig, model_name: str | None = None, tokenizer=None):
-    """Returns (app, runner) with the pipeline started."""
+async def build_server(cfg: PipelineConfig, model_name: str | None = None, tokenizer=None,
+                       restart_stages: list[str] | None = None):
+    """Returns (app, runner) with the pipeline started.  ``restart_stages`` (multi-process
+    pipelines: stages placed on more than one GPU): stages whose process is replaced when it
+    dies, instead of stopping the server."""
     gpus = set(cfg.gpu_placement.values())
     if len(gpus) > 1:
         from ..pipeline.mp_runner import MultiProcessPipelineRunner
 
-        runner = MultiProcessPipelineRunner(cfg)
+        runner = MultiProcessPipelineRunner(cfg, restart=list(restart_stages or []))
         await runner.start()
         coordinator = runner.coordinator
     else:
@@ -63,11 +66,11 @@ async def build_server(cfg: PipelineConfig, model_name: str | None = None, token
 
 
 def launch_server(cfg: PipelineConfig, host: str = "0.0.0.0", port: int = 8000, model_name: str | None = None,
-                  log_level: str = "info") -> None:
+                  log_level: str = "info", restart_stages: list[str] | None = None) -> None:
     import uvicorn
 
     async def main():
-        app, runner = await build_server(cfg, model_name)
+        app, runner = await build_server(cfg, model_name, restart_stages=restart_stages)
         server = uvicorn.Server(uvicorn.Config(app, host=host, port=port, log_level=log_level))
         try:
             await server.serve()
