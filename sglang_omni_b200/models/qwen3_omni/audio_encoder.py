@@ -14,7 +14,6 @@ sglang_omni/models/qwen3_omni/components/audio_encoder.py:37-89): chunk
 """
 from __future__ import annotations
 
-import math
 from dataclasses import dataclass
 
 import numpy as np

@@ -25,7 +25,6 @@ code_predictor_executor.py).
 """
 from __future__ import annotations
 
-import math
 from dataclasses import dataclass, field
 
 import numpy as np

@@ -16,7 +16,6 @@ from __future__ import annotations
 
 import asyncio
 import logging
-import threading
 from typing import Any, Callable
 
 from ...proto import CompleteMessage, DataReadyMessage, StagePayload, StreamMessage

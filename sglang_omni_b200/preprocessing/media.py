@@ -20,7 +20,6 @@ and frame sampling, audio decoding and resampling.
 from __future__ import annotations
 
 import base64
-import math
 import os
 import tempfile
 import threading
