@@ -38,7 +38,9 @@ class PagedAREngineAdapter:
         used = pool.num_pages - pool.free_pages
         return {"requests_running": len(e.running), "requests_waiting": len(e.waiting),
                 "kv_pages_used": used, "kv_pages_total": pool.num_pages,
-                "kv_usage": round(used / pool.num_pages, 4) if pool.num_pages else 0.0}
+                "kv_usage": round(used / pool.num_pages, 4) if pool.num_pages else 0.0,
+                "steps": getattr(self.threaded, "steps", 0),
+                "step_ms": round(getattr(self.threaded, "step_ms_ema", 0.0), 3)}
 
     async def generate(self, rid: str, req: ARRequest, on_chunk=None, stream_fn=None) -> ARRequest:
         self.start()

@@ -298,6 +298,8 @@ class ThreadedAREngine:
 
     def __init__(self, engine: AREngine):
         self.engine = engine
+        self.steps = 0            # engine steps run by this thread
+        self.step_ms_ema = 0.0    # host time of a step (moving average over ~10 steps)
         self._cv = threading.Condition()
         self._inbox: deque = deque()
         self._stop = False
@@ -380,7 +382,12 @@ class ThreadedAREngine:
                         if r is not None and eng.abort(x):
                             self._deliver(r)
                 if eng.has_work():
-                    for r in eng.step():
+                    t0 = time.perf_counter()
+                    done = eng.step()
+                    ms = (time.perf_counter() - t0) * 1e3
+                    self.steps += 1
+                    self.step_ms_ema = ms if self.steps == 1 else 0.9 * self.step_ms_ema + 0.1 * ms
+                    for r in done:
                         self._deliver(r)
         except BaseException as exc:  # engine failure fails every in-flight request
             log.exception("AR engine loop failed")

@@ -40,5 +40,6 @@ def test_stage_reports_reach_metrics(monkeypatch):
     dec = st["decoder"]
     assert dec["queue_depth"] == 0 and dec["messages"] >= 1 and dec["age_s"] < 5
     assert dec["kv_pages_total"] > 0 and 0 <= dec["kv_usage"] <= 1 and dec["requests_running"] == 0
+    assert dec["steps"] >= 6 and dec["step_ms"] > 0           # prefill + decode steps of the request
     assert 'omni_stage_kv_pages_total{stage="decoder"}' in prom and "# TYPE omni_stage_queue_depth gauge" in prom
     assert health["stage_stats"]["decoder"]["kv_pages_total"] == dec["kv_pages_total"]
