@@ -29,3 +29,11 @@ def test_two_gpu_speech_config_validates():
     assert cfg.gpu_placement["thinker"] == 0 and cfg.gpu_placement["talker_ar"] == 1
     assert cfg.relay_backend == "nccl"
     assert [s.name for s in cfg.stages][-2:] == ["talker_ar", "code2wav"]
+
+
+def test_hf_llm_engine_example_runs():
+    r = subprocess.run([sys.executable, os.path.join(EX, "hf_llm_engine.py"), "--tiny", "--device", "cpu",
+                        "--max-new-tokens", "5"], capture_output=True, text=True, timeout=600, cwd=ROOT,
+                       env=dict(os.environ, PYTHONPATH=ROOT))
+    assert r.returncode == 0, r.stderr[-3000:]
+    assert len(r.stdout.split()) == 5
